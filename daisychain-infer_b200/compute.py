@@ -1,0 +1,183 @@
+"""The compute core: the object ``Compute.initCompute`` returns in the reference.
+
+Mirrors public/webgpu.js: ``init_compute`` (initCompute :284-648),
+``load_luts`` (loadLUTs :247-257), ``kernel_probe`` (:1047-1060) and the
+compute object's ``bgemm`` (gpuBgemmDP4 / gpuBgemmLUT :819-857), so that the
+reference's vgemmBlock contract (public/verified_core.js:425-449) is met:
+
+    out = compute.bgemm(Xq, Wq, rs, cs, dict(m=.., k=.., n=.., batch=1, relu=False, acc=False))
+
+with host int8/f32 arrays in the reference's layouts; ``out`` is a fresh
+int32 array (acc) or f32 array owned by the caller.  Errors carry the
+reference's names: ``AccumulatorBoundError`` before any launch for
+k > 131071, ``NonFiniteError`` for a non-finite quantiser input.
+
+Device-resident entry points take torch CUDA tensors (torch is used only as
+the device-memory allocator and for its current stream).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import DC_ACC, DC_RELU, DC_REQUANT, AccumulatorBoundError, NonFiniteError, raise_for  # noqa: F401
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data_as(C.c_void_p)
+    return C.c_void_p(a.data_ptr())  # torch tensor
+
+
+def flags_of(d: dict) -> int:
+    f = 0
+    if d.get("relu"):
+        f |= DC_RELU
+    if d.get("acc"):
+        f |= DC_ACC
+    if d.get("requant"):
+        f |= DC_REQUANT
+    return f
+
+
+class Compute:
+    """One B200 bound to one stream: ``backend``, ``label``, ``bgemm``."""
+
+    backend = "cuda-sm100a"
+
+    def __init__(self, device: int = 0, stream=None):
+        self.L = _lib.load()
+        self.device = device
+        h = C.c_void_p()
+        rc = self.L.dc_init(device, C.byref(h))
+        if rc:
+            raise_for(rc, "dc_init: " + (self.L.dc_init_error() or b"").decode())
+        self.h = h
+        if stream is not None:
+            self.set_stream(stream)
+        self.label = self.L.dc_backend_label(self.h).decode()
+
+    # ---- plumbing -------------------------------------------------------------
+    def _check(self, rc: int, where: str) -> None:
+        if rc:
+            raise_for(rc, f"{where}: " + (self.L.dc_last_error(self.h) or b"").decode())
+
+    def set_stream(self, stream) -> None:
+        """Launch on an existing stream (a torch.cuda.Stream or a raw handle)."""
+        handle = getattr(stream, "cuda_stream", stream)
+        self._check(self.L.dc_set_stream(self.h, C.c_void_p(handle) if handle else None), "dc_set_stream")
+
+    def sync(self) -> None:
+        self._check(self.L.dc_sync(self.h), "dc_sync")
+
+    @property
+    def tc_enabled(self) -> bool:
+        return bool(self.L.dc_tc_enabled(self.h))
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.L.dc_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- the LUT units ----------------------------------------------------------
+    def luts(self) -> dict:
+        """loadLUTs: {mul int16[65536], requant int8[65536], relu int8[256], shift 8},
+        rebuilt by the library and checked against the reference's sha256 ids."""
+        mul = np.empty(65536, np.int16)
+        req = np.empty(65536, np.int8)
+        relu = np.empty(256, np.int8)
+        self._check(self.L.dc_luts(self.h, _ptr(mul), _ptr(req), _ptr(relu)), "dc_luts")
+        return dict(mul=mul, requant=req, relu=relu, shift=8)
+
+    # ---- compute.bgemm (host buffers) -------------------------------------------
+    def bgemm(self, Xq, Wq, rs, cs, d: dict) -> np.ndarray:
+        m, k, n = int(d["m"]), int(d["k"]), int(d["n"])
+        batch = int(d.get("batch") or 1)
+        flags = flags_of(d)
+        if k > _lib.MAX_INT32_K:
+            raise AccumulatorBoundError(f"bgemm: contraction length {k} exceeds the int32 accumulator headroom "
+                                        f"{_lib.MAX_INT32_K} (the sum would wrap)")
+        Xq = np.ascontiguousarray(Xq, np.int8).reshape(-1)
+        Wq = np.ascontiguousarray(Wq, np.int8).reshape(-1)
+        rs = np.ascontiguousarray(rs, np.float32).reshape(-1)
+        cs = np.ascontiguousarray(cs, np.float32).reshape(-1)
+        if Xq.size != batch * m * k or Wq.size != batch * k * n or rs.size != batch * m or cs.size != batch * n:
+            raise ValueError("bgemm: buffer sizes do not match d")
+        dt = np.int32 if flags & DC_ACC else (np.int8 if flags & DC_REQUANT else np.float32)
+        out = np.empty(batch * m * n, dt)
+        self._check(self.L.dc_bgemm(self.h, _ptr(Xq), _ptr(Wq), _ptr(rs), _ptr(cs), m, k, n, batch, flags,
+                                    _ptr(out)), "bgemm")
+        return out
+
+    # ---- device-resident entry points (torch CUDA tensors) ---------------------
+    def bgemm_dev(self, xq, ldx, wt, ldw, rs, cs, m, k, n, batch, flags, out, kind: int = 0) -> None:
+        if kind:
+            rc = self.L.dc_bgemm_dev_kind(self.h, _ptr(xq), ldx, _ptr(wt), ldw, _ptr(rs), _ptr(cs), m, k, n, batch,
+                                          flags, _ptr(out), kind)
+        else:
+            rc = self.L.dc_bgemm_dev(self.h, _ptr(xq), ldx, _ptr(wt), ldw, _ptr(rs), _ptr(cs), m, k, n, batch, flags,
+                                     _ptr(out))
+        self._check(rc, "bgemm_dev")
+
+    def bgemm_lut_dev(self, xq, wq, rs, cs, m, k, n, batch, flags, out) -> None:
+        self._check(self.L.dc_bgemm_lut_dev(self.h, _ptr(xq), _ptr(wq), _ptr(rs), _ptr(cs), m, k, n, batch, flags,
+                                            _ptr(out)), "bgemm_lut_dev")
+
+    def quantize_rows_dev(self, X, rows, cols, q, ldq, s) -> None:
+        self._check(self.L.dc_quantize_rows(self.h, _ptr(X), rows, cols, _ptr(q), ldq, _ptr(s)), "quantize_rows")
+
+    def quantize_cols_t_dev(self, W, rows, cols, qt, ldq, s) -> None:
+        self._check(self.L.dc_quantize_cols_t(self.h, _ptr(W), rows, cols, _ptr(qt), ldq, _ptr(s)),
+                    "quantize_cols_t")
+
+    def register_weight(self, W: np.ndarray, k: int, n: int) -> "Weight":
+        return Weight(self, W, k, n)
+
+    def vgemm_dev(self, X, m, w: "Weight", flags, out) -> None:
+        self._check(self.L.dc_vgemm(self.h, _ptr(X), m, w.h, flags, _ptr(out)), "vgemm")
+
+    def kernel_probe(self) -> int:
+        """kernelProbe's int32 hash (webgpu.js:1047-1055, before the math fold)."""
+        h = C.c_uint32()
+        self._check(self.L.dc_kernel_probe(self.h, C.byref(h)), "kernel_probe")
+        return h.value
+
+
+class Weight:
+    """A weight quantised once and resident in HBM (dc_weight_register)."""
+
+    def __init__(self, comp: Compute, W: np.ndarray, k: int, n: int):
+        self.comp = comp
+        W = np.ascontiguousarray(W, np.float32).reshape(-1)
+        if W.size != k * n:
+            raise ValueError("weight: size does not match k x n")
+        h = C.c_void_p()
+        comp._check(comp.L.dc_weight_register(comp.h, _ptr(W), k, n, C.byref(h)), "weight_register")
+        self.h = h
+        self.k, self.n = k, n
+        qt, ld, cs = C.c_void_p(), C.c_int(), C.c_void_p()
+        comp.L.dc_weight_info(self.h, C.byref(qt), C.byref(ld), C.byref(cs), None, None)
+        self.qt_ptr, self.ldw, self.cs_ptr = qt.value, ld.value, cs.value
+
+    def __del__(self):
+        try:
+            if self.h:
+                self.comp.L.dc_weight_free(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+
+def init_compute(device: int = 0, stream=None) -> Compute:
+    """initCompute (webgpu.js:284): a gated compute object, or an exception."""
+    return Compute(device, stream)

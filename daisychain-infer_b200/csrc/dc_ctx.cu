@@ -1,0 +1,351 @@
+// dc_ctx.cu -- context, LUT units, init gates and the kernel probe.
+//
+// Replaces Compute.loadLUTs / initCompute / kernelProbe (public/webgpu.js:247,
+// 284-648, 998-1060) and the boot self-test (public/app.js:1072-1076):
+//  * the three LUT units are rebuilt from their definitions and pinned by the
+//    sha256 of the reference's LFS objects (public/*_lut.bin pointer files);
+//  * mul[7, -3] must be -21;
+//  * every GEMM kernel is gated against the LUT kernel (every product looked
+//    up in the mul unit) at the reference's gate shapes plus tensor-core
+//    shapes, in int32-accumulator mode with exact comparison and in f32 mode
+//    with bitwise comparison, first on clean and then on poisoned output
+//    buffers (webgpu.js:470-516).  A failing tensor-core gate turns that path
+//    off (the SIMT kernel takes its shapes); any other failure fails dc_init.
+#include <math.h>
+
+#include <vector>
+
+#include "dc_internal.cuh"
+
+namespace {
+
+// ---- SHA-256 (FIPS 180-4) --------------------------------------------------
+// Round constants are the first 32 fraction bits of the cube roots of the
+// first 64 primes, initial hash the square roots of the first 8; both are
+// derived here and the implementation is checked on the FIPS "abc" vector.
+struct Sha256 {
+  uint32_t K[64], H0[8];
+  Sha256() {
+    int primes[64], np = 0;
+    for (int c = 2; np < 64; c++) {
+      bool p = true;
+      for (int d = 2; d * d <= c; d++)
+        if (c % d == 0) { p = false; break; }
+      if (p) primes[np++] = c;
+    }
+    for (int i = 0; i < 64; i++) {
+      long double r = cbrtl((long double)primes[i]);
+      K[i] = (uint32_t)(uint64_t)floorl((r - floorl(r)) * 4294967296.0L);
+    }
+    for (int i = 0; i < 8; i++) {
+      long double r = sqrtl((long double)primes[i]);
+      H0[i] = (uint32_t)(uint64_t)floorl((r - floorl(r)) * 4294967296.0L);
+    }
+  }
+  static uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
+  void digest(const uint8_t* msg, size_t len, uint8_t out[32]) const {
+    uint32_t h[8];
+    memcpy(h, H0, sizeof h);
+    uint64_t bits = (uint64_t)len * 8;
+    size_t total = ((len + 9 + 63) / 64) * 64;
+    std::vector<uint8_t> buf(total, 0);
+    memcpy(buf.data(), msg, len);
+    buf[len] = 0x80;
+    for (int i = 0; i < 8; i++) buf[total - 1 - i] = (uint8_t)(bits >> (8 * i));
+    for (size_t off = 0; off < total; off += 64) {
+      uint32_t w[64];
+      for (int i = 0; i < 16; i++)
+        w[i] = ((uint32_t)buf[off + 4 * i] << 24) | ((uint32_t)buf[off + 4 * i + 1] << 16) |
+               ((uint32_t)buf[off + 4 * i + 2] << 8) | buf[off + 4 * i + 3];
+      for (int i = 16; i < 64; i++) {
+        uint32_t s0 = rotr(w[i - 15], 7) ^ rotr(w[i - 15], 18) ^ (w[i - 15] >> 3);
+        uint32_t s1 = rotr(w[i - 2], 17) ^ rotr(w[i - 2], 19) ^ (w[i - 2] >> 10);
+        w[i] = w[i - 16] + s0 + w[i - 7] + s1;
+      }
+      uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], hh = h[7];
+      for (int i = 0; i < 64; i++) {
+        uint32_t S1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
+        uint32_t ch = (e & f) ^ (~e & g);
+        uint32_t t1 = hh + S1 + ch + K[i] + w[i];
+        uint32_t S0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
+        uint32_t mj = (a & b) ^ (a & c) ^ (b & c);
+        uint32_t t2 = S0 + mj;
+        hh = g; g = f; f = e; e = d + t1; d = c; c = b; b = a; a = t1 + t2;
+      }
+      h[0] += a; h[1] += b; h[2] += c; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
+    }
+    for (int i = 0; i < 8; i++)
+      for (int j = 0; j < 4; j++) out[4 * i + j] = (uint8_t)(h[i] >> (24 - 8 * j));
+  }
+};
+
+bool hex_eq(const uint8_t d[32], const char* hex) {
+  char buf[65];
+  for (int i = 0; i < 32; i++) snprintf(buf + 2 * i, 3, "%02x", d[i]);
+  return strcmp(buf, hex) == 0;
+}
+
+// LFS object ids of public/mul_lut.bin, requant_lut.bin, relu_lut.bin.
+const char* kMulOid = "5cecff7e22049d0083ad9ee36dcf0695222c61621bacfd5a401c7b133abe892d";
+const char* kRequantOid = "173444ecfa293433329a333289983a665c481d913e9fd1c2778b55380ca4dd31";
+const char* kReluOid = "2acb03ba7520467636273208563f8e733494748f4aa5ac2dba89d9560050da79";
+
+void build_luts(dc_ctx* c) {
+  for (int a = 0; a < 256; a++)
+    for (int b = 0; b < 256; b++) c->h_mul[a * 256 + b] = (int16_t)((a > 127 ? a - 256 : a) * (b > 127 ? b - 256 : b));
+  for (int u = 0; u < 65536; u++) c->h_requant[u] = (int8_t)((u > 32767 ? u - 65536 : u) >> 8);
+  for (int u = 0; u < 256; u++) {
+    int s = u > 127 ? u - 256 : u;
+    c->h_relu[u] = (int8_t)(s > 0 ? s : 0);
+  }
+}
+
+int check_luts(dc_ctx* c) {
+  Sha256 sh;
+  uint8_t d[32];
+  sh.digest((const uint8_t*)"abc", 3, d);
+  if (!hex_eq(d, "ba7816bf8f01cfea414140de5dae2223b00361a396177a9cb410ff61f20015ad"))
+    return dc_fail(c, DC_E_LUT, "sha256 self-test failed");
+  sh.digest((const uint8_t*)c->h_mul, sizeof c->h_mul, d);
+  if (!hex_eq(d, kMulOid)) return dc_fail(c, DC_E_LUT, "mul8 LUT does not match its LFS object id");
+  sh.digest((const uint8_t*)c->h_requant, sizeof c->h_requant, d);
+  if (!hex_eq(d, kRequantOid)) return dc_fail(c, DC_E_LUT, "requant LUT does not match its LFS object id");
+  sh.digest((const uint8_t*)c->h_relu, sizeof c->h_relu, d);
+  if (!hex_eq(d, kReluOid)) return dc_fail(c, DC_E_LUT, "relu LUT does not match its LFS object id");
+  if (c->h_mul[(7 & 0xFF) * 256 + (-3 & 0xFF)] != -21)
+    return dc_fail(c, DC_E_LUT, "mul8 LUT self-test failed (7 x -3 != -21)");
+  return DC_OK;
+}
+
+// ---- init gates ---------------------------------------------------------
+struct GateShape { int m, k, n, batch; bool relu; };
+
+uint32_t lcg_next(uint32_t& s) { s = s * 1664525u + 1013904223u; return s; }
+
+// Run one gate shape through `kind` and the LUT kernel; 0 when identical.
+int gate_one(dc_ctx* c, const GateShape& g, int kind, bool poison, uint32_t seed, std::string& why) {
+  const int m = g.m, k = g.k, n = g.n, B = g.batch;
+  const int ld = round_up(k, 16);
+  std::vector<int8_t> X((size_t)B * m * k), W((size_t)B * k * n);
+  std::vector<float> rs((size_t)B * m), cs((size_t)B * n);
+  uint32_t s = seed;
+  for (auto& v : X) v = (int8_t)(lcg_next(s) >> 24);
+  for (auto& v : W) v = (int8_t)(lcg_next(s) >> 24);
+  for (auto& v : rs) v = 0.5f + (float)(lcg_next(s) >> 8) / 16777216.0f;
+  for (auto& v : cs) v = 0.5f + (float)(lcg_next(s) >> 8) / 16777216.0f;
+  const size_t nx = X.size(), nw = W.size(), nxp = (size_t)B * m * ld, nwt = (size_t)B * n * ld,
+               no = (size_t)B * m * n;
+  char* base = nullptr;
+  size_t bytes = nx + nw + nxp + nwt + 4 * (rs.size() + cs.size()) + 8 * no + 2048;
+  if (cudaMalloc(&base, bytes) != cudaSuccess) { cudaGetLastError(); why = "gate allocation failed"; return DC_E_NOMEM; }
+  char* p = base;
+  auto take = [&](size_t b) { char* r = p; p += (b + 255) & ~(size_t)255; return r; };
+  int8_t* dX = (int8_t*)take(nx);
+  int8_t* dW = (int8_t*)take(nw);
+  int8_t* dXp = (int8_t*)take(nxp);
+  int8_t* dWt = (int8_t*)take(nwt);
+  float* drs = (float*)take(4 * rs.size());
+  float* dcs = (float*)take(4 * cs.size());
+  void* o1 = take(4 * no);
+  void* o2 = take(4 * no);
+  cudaStream_t st = c->stream;
+  int rc = DC_OK;
+  std::vector<int32_t> h1(no), h2(no);
+  cudaMemcpyAsync(dX, X.data(), nx, cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(dW, W.data(), nw, cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(drs, rs.data(), 4 * rs.size(), cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(dcs, cs.data(), 4 * cs.size(), cudaMemcpyHostToDevice, st);
+  cudaMemsetAsync(dXp, 0, nxp, st);
+  cudaMemcpy2DAsync(dXp, ld, dX, k, k, (size_t)B * m, cudaMemcpyDeviceToDevice, st);
+  rc = dc_launch_transpose_i8(c, dW, k, n, dWt, ld, B, st);
+  const unsigned modes[2] = {DC_ACC, (unsigned)(g.relu ? DC_RELU : 0)};
+  for (int mi = 0; mi < 2 && rc == DC_OK; mi++) {
+    cudaMemsetAsync(o1, poison ? 0x7F : 0, 4 * no, st);
+    cudaMemsetAsync(o2, poison ? 0x7F : 0, 4 * no, st);
+    rc = dc_gemm_lut(c, dX, dW, drs, dcs, m, k, n, B, modes[mi], o1, st);
+    if (!rc) {
+      if (kind == 3)
+        rc = dc_gemm_tc(c, dXp, ld, dWt, ld, drs, dcs, m, k, n, B, modes[mi], o2, st);
+      else
+        rc = dc_gemm_dispatch(c, dXp, ld, dWt, ld, drs, dcs, m, k, n, B, modes[mi], o2, st, kind);
+    }
+    if (!rc) {
+      cudaMemcpyAsync(h1.data(), o1, 4 * no, cudaMemcpyDeviceToHost, st);
+      cudaMemcpyAsync(h2.data(), o2, 4 * no, cudaMemcpyDeviceToHost, st);
+      cudaError_t e = cudaStreamSynchronize(st);
+      if (e != cudaSuccess) { rc = dc_cuda_fail(c, e, "gate"); break; }
+      for (size_t i = 0; i < no; i++)
+        if (h1[i] != h2[i]) {
+          char b[256];
+          snprintf(b, sizeof b, "%s mismatch @%zu (%dx%dx%d b%d, kernel %d%s): 0x%08x vs LUT 0x%08x",
+                   mi == 0 ? "accumulator" : "epilogue", i, m, k, n, B, kind, poison ? ", poisoned" : "",
+                   (unsigned)h2[i], (unsigned)h1[i]);
+          why = b;
+          rc = DC_E_GATE;
+          break;
+        }
+    }
+  }
+  cudaStreamSynchronize(st);
+  cudaFree(base);
+  return rc;
+}
+
+int run_gates(dc_ctx* c) {
+  // webgpu.js:471-475, then shapes that reach the GEMV and tensor-core kernels.
+  const GateShape ref[] = {{5, 9, 6, 3, true}, {32, 64, 32, 1, false}, {7, 253, 5, 2, true}, {1, 4, 1, 1, false},
+                           {17, 33, 9, 1, true}};
+  const GateShape tc[] = {{16, 576, 160, 1, false}, {64, 256, 200, 1, true}, {130, 320, 300, 2, false},
+                          {256, 1024, 256, 1, false}, {24, 96, 24, 2, false}};
+  std::string why;
+  uint32_t seed = 12345;
+  for (int poison = 0; poison < 2; poison++) {
+    for (const auto& g : ref) {
+      int kinds[2] = {g.m <= 8 ? 1 : 2, 2};
+      for (int kind : kinds) {
+        int rc = gate_one(c, g, kind, poison, seed++, why);
+        if (rc) return rc == DC_E_GATE ? dc_fail(c, DC_E_GATE, "init gate: %s", why.c_str()) : rc;
+      }
+    }
+    for (const auto& g : tc) {
+      int rc = gate_one(c, g, 2, poison, seed++, why);
+      if (rc) return rc == DC_E_GATE ? dc_fail(c, DC_E_GATE, "init gate: %s", why.c_str()) : rc;
+      if (c->tc_enabled) {
+        rc = gate_one(c, g, 3, poison, seed++, why);
+        if (rc == DC_E_GATE || rc == DC_E_INVAL) {
+          c->tc_enabled = false;  // tensor-core path off; SIMT kernel takes its shapes
+          fprintf(stderr, "dcinfer: tcgen05 GEMM gate failed, path disabled: %s\n", why.c_str());
+        } else if (rc) {
+          return rc;
+        }
+      }
+    }
+  }
+  return DC_OK;
+}
+
+thread_local std::string g_init_error;
+
+}  // namespace
+
+extern "C" const char* dc_init_error(void) { return g_init_error.c_str(); }
+
+extern "C" int dc_set_stream(dc_ctx* c, void* stream) {
+  if (!c) return DC_E_INVAL;
+  DC_CUDA(c, cudaStreamSynchronize(c->stream));
+  c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+  return DC_OK;
+}
+
+extern "C" int dc_sync(dc_ctx* ctx) {
+  if (!ctx) return DC_E_INVAL;
+  DC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  int st = 0;
+  DC_CUDA(ctx, cudaMemcpy(&st, ctx->d_status, 4, cudaMemcpyDeviceToHost));
+  if (st) {
+    DC_CUDA(ctx, cudaMemset(ctx->d_status, 0, 4));
+    if (st & DC_ST_NONFINITE)
+      return dc_fail(ctx, DC_E_NONFINITE, "non-finite input to a quantiser: the int8 quantize would turn it into 0");
+    if (st & DC_ST_TIMEOUT) return dc_fail(ctx, DC_E_TIMEOUT, "a bounded device wait gave up");
+    return dc_fail(ctx, DC_E_CUDA, "device bounds check failed (status 0x%x)", st);
+  }
+  return DC_OK;
+}
+
+extern "C" int dc_init(int device, dc_ctx** out) {
+  if (!out) return DC_E_INVAL;
+  *out = nullptr;
+  dc_ctx* c = new dc_ctx();
+  c->device = device;
+  int rc = DC_OK;
+  cudaDeviceProp prop;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    rc = dc_cuda_fail(c, e, "cudaSetDevice");
+  } else if (prop.major != 10) {
+    rc = dc_fail(c, DC_E_CUDA, "device %d is sm_%d%d; this library is built for sm_100a only", device, prop.major,
+                 prop.minor);
+  }
+  if (!rc) {
+    c->sm_count = prop.multiProcessorCount;
+    snprintf(c->label, sizeof c->label, "%s (sm_100a): tcgen05 i8 GEMM + dp4a GEMV, verified", prop.name);
+    build_luts(c);
+    rc = check_luts(c);
+  }
+  if (!rc) {
+    e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+    c->stream = c->own_stream;
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_mul, sizeof c->h_mul);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_requant, sizeof c->h_requant);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_relu, sizeof c->h_relu);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_status, 16);
+    if (e == cudaSuccess) e = cudaMemcpy(c->d_mul, c->h_mul, sizeof c->h_mul, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->d_requant, c->h_requant, sizeof c->h_requant, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->d_relu, c->h_relu, sizeof c->h_relu, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(c->d_status, 0, 16);
+    if (e != cudaSuccess) rc = dc_cuda_fail(c, e, "context setup");
+  }
+  if (!rc) rc = run_gates(c);
+  if (!rc && !c->tc_enabled)
+    snprintf(c->label, sizeof c->label, "%s (sm_100a): dp4a GEMM + GEMV, verified (tcgen05 gate failed)", prop.name);
+  if (rc) {
+    g_init_error = c->err;
+    fprintf(stderr, "dc_init failed: %s\n", c->err.c_str());
+    dc_destroy(c);
+    return rc;
+  }
+  *out = c;
+  return DC_OK;
+}
+
+extern "C" void dc_destroy(dc_ctx* c) {
+  if (!c) return;
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->own_stream && c->own_stream != c->stream) cudaStreamSynchronize(c->own_stream);
+  cudaFree(c->d_mul);
+  cudaFree(c->d_requant);
+  cudaFree(c->d_relu);
+  cudaFree(c->d_status);
+  cudaFree(c->scratch);
+  if (c->own_stream) cudaStreamDestroy(c->own_stream);
+  delete c;
+}
+
+extern "C" const char* dc_backend_label(const dc_ctx* c) { return c ? c->label : "none"; }
+extern "C" const char* dc_last_error(const dc_ctx* c) { return c ? c->err.c_str() : "no context"; }
+extern "C" void* dc_stream(const dc_ctx* c) { return c ? (void*)c->stream : nullptr; }
+extern "C" int dc_tc_enabled(const dc_ctx* c) { return c && c->tc_enabled ? 1 : 0; }
+
+extern "C" int dc_luts(const dc_ctx* c, int16_t* mul, int8_t* requant, int8_t* relu) {
+  if (!c) return DC_E_INVAL;
+  if (mul) memcpy(mul, c->h_mul, sizeof c->h_mul);
+  if (requant) memcpy(requant, c->h_requant, sizeof c->h_requant);
+  if (relu) memcpy(relu, c->h_relu, sizeof c->h_relu);
+  return DC_OK;
+}
+
+// webgpu.js:998-1009: LCG seed 0x5EED, x = Math.round(r*254 - 127).
+extern "C" int dc_kernel_probe(dc_ctx* c, uint32_t* hash) {
+  if (!c || !hash) return DC_E_INVAL;
+  const int m = 24, k = 96, n = 24, B = 2;
+  std::vector<int8_t> X(B * m * k), W(B * k * n);
+  uint32_t seed = 0x5EED;
+  for (int i = 0; i < B * m * k + B * k * n; i++) {
+    seed = (seed * 1103515245u + 12345u) & 0x7fffffffu;
+    double v = (double)seed / (double)0x7fffffff * 254.0 - 127.0;
+    double r = floor(v);
+    if (v - r >= 0.5) r += 1.0;
+    if (i < B * m * k) X[i] = (int8_t)r; else W[i - B * m * k] = (int8_t)r;
+  }
+  std::vector<float> rs(B * m, 1.0f), cs(B * n, 1.0f);
+  std::vector<int32_t> acc(B * m * n);
+  int rc = dc_bgemm(c, X.data(), W.data(), rs.data(), cs.data(), m, k, n, B, DC_ACC, acc.data());
+  if (rc) return rc;
+  uint32_t h = 0x811c9dc5u;
+  const uint8_t* b = (const uint8_t*)acc.data();
+  for (size_t i = 0; i < acc.size() * 4; i++) { h ^= b[i]; h *= 0x01000193u; }
+  *hash = h;
+  return DC_OK;
+}

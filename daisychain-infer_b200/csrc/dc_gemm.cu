@@ -1,0 +1,397 @@
+// dc_gemm.cu -- the verified W8A8 GEMM unit (compute.bgemm, public/webgpu.js:836-857).
+//
+// out[bz, i, j] = epilogue( sum_p X[bz, i, p] * W[bz, p, j] )  (int8 x int8 -> int32)
+//
+// The mul LUT is the exact product table s8(a)*s8(b) (its sha256 equals the
+// reference's LFS object), so an integer dot product IS the LUT GEMM; the
+// int32 sum is exact because k <= 131071 keeps |sum| < 2^31
+// (verified_core.js:41-49).  Kernels here:
+//   k_lut_gemm   every product looked up in the mul unit (the reference's
+//                WGSL_BG_LUT twin, webgpu.js:108-133); the init gate's yardstick
+//   k_gemv       M <= 8 rows: HBM-streaming, 128-bit weight loads, dp4a,
+//                warp-shuffle reduction (decode, lm_head, lookahead rows)
+//   k_gemm_simt  dp4a register-tiled GEMM for shapes the tensor-core path
+//                does not take
+// and the tcgen05 tensor-core kernel in dc_gemm_tc.cu.
+#include <stdarg.h>
+
+#include "dc_internal.cuh"
+
+namespace {
+
+// ---- the LUT twin: one thread per output, reference layouts ----------------
+__global__ void k_lut_gemm(const int8_t* __restrict__ X, const int8_t* __restrict__ W, const float* __restrict__ rs,
+                           const float* __restrict__ cs, int m, int k, int n, unsigned flags,
+                           const int16_t* __restrict__ mul, const int8_t* __restrict__ requant,
+                           const int8_t* __restrict__ relu, void* out) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  const int col = blockIdx.y * blockDim.y + threadIdx.y;
+  const int bz = blockIdx.z;
+  if (row >= m || col >= n) return;
+  const int8_t* xr = X + ((int64_t)bz * m + row) * k;
+  const int8_t* wc = W + (int64_t)bz * k * n + col;
+  uint32_t s = 0;
+  for (int p = 0; p < k; p++) s += (uint32_t)(int32_t)__ldg(mul + ((uint8_t)xr[p]) * 256 + (uint8_t)wc[(int64_t)p * n]);
+  dc_store_out(out, ((int64_t)bz * m + row) * n + col, (int32_t)s, rs[bz * m + row], cs[bz * n + col], flags, requant,
+               relu);
+}
+
+__device__ __forceinline__ int4 ld_stream(const int4* p) {
+  int4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// ---- GEMV: M <= MR rows ---------------------------------------------------
+// One warp per output column j at a time (grid-stride over columns).  The
+// weight row Wᵀ[j] (k bytes, K-major) is streamed once with 16-byte
+// non-allocating loads, 4 in flight per lane; the MR activation rows sit in
+// shared memory.  Lanes own 16-byte chunks c = lane + 32 t, so a warp reads
+// 512 contiguous bytes per step.  The int32 partial sums are combined by a
+// butterfly shuffle (integer addition: exact in any order).
+template <int MR>
+__global__ void __launch_bounds__(256) k_gemv(const int8_t* __restrict__ X, int ldx, const int8_t* __restrict__ Wt,
+                                              int ldw, const float* __restrict__ rs, const float* __restrict__ cs,
+                                              int m, int k, int n, unsigned flags, const int8_t* __restrict__ requant,
+                                              const int8_t* __restrict__ relu, void* out) {
+  extern __shared__ int4 xs[];
+  const int bz = blockIdx.y;
+  const int nch = (k + 15) >> 4;  // 16-byte chunks per row (<= ldx/16, ldw/16)
+  const int8_t* Xb = X + (int64_t)bz * m * ldx;
+  for (int idx = threadIdx.x; idx < MR * nch; idx += blockDim.x) {
+    int r = idx / nch, c = idx - r * nch;
+    xs[idx] = (r < m) ? *((const int4*)(Xb + (int64_t)r * ldx) + c) : make_int4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int8_t* Wb = Wt + (int64_t)bz * n * ldw;
+  for (int j = blockIdx.x * wpb + warp; j < n; j += gridDim.x * wpb) {
+    const int4* wrow = (const int4*)(Wb + (int64_t)j * ldw);
+    int acc[MR];
+#pragma unroll
+    for (int r = 0; r < MR; r++) acc[r] = 0;
+    int c = lane;
+    for (; c + 96 < nch; c += 128) {
+      int4 w0 = ld_stream(wrow + c), w1 = ld_stream(wrow + c + 32), w2 = ld_stream(wrow + c + 64),
+           w3 = ld_stream(wrow + c + 96);
+#pragma unroll
+      for (int r = 0; r < MR; r++) {
+        const int4* xr = xs + r * nch + c;
+        int4 a0 = xr[0], a1 = xr[32], a2 = xr[64], a3 = xr[96];
+        int t = acc[r];
+        t = __dp4a(w0.x, a0.x, t); t = __dp4a(w0.y, a0.y, t); t = __dp4a(w0.z, a0.z, t); t = __dp4a(w0.w, a0.w, t);
+        t = __dp4a(w1.x, a1.x, t); t = __dp4a(w1.y, a1.y, t); t = __dp4a(w1.z, a1.z, t); t = __dp4a(w1.w, a1.w, t);
+        t = __dp4a(w2.x, a2.x, t); t = __dp4a(w2.y, a2.y, t); t = __dp4a(w2.z, a2.z, t); t = __dp4a(w2.w, a2.w, t);
+        t = __dp4a(w3.x, a3.x, t); t = __dp4a(w3.y, a3.y, t); t = __dp4a(w3.z, a3.z, t); t = __dp4a(w3.w, a3.w, t);
+        acc[r] = t;
+      }
+    }
+    for (; c < nch; c += 32) {
+      int4 w0 = ld_stream(wrow + c);
+#pragma unroll
+      for (int r = 0; r < MR; r++) {
+        int4 a0 = xs[r * nch + c];
+        int t = acc[r];
+        t = __dp4a(w0.x, a0.x, t); t = __dp4a(w0.y, a0.y, t); t = __dp4a(w0.z, a0.z, t); t = __dp4a(w0.w, a0.w, t);
+        acc[r] = t;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < MR; r++)
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    int mine = 0;
+#pragma unroll
+    for (int r = 0; r < MR; r++)
+      if (r == lane) mine = acc[r];
+    if (lane < MR && lane < m)
+      dc_store_out(out, ((int64_t)bz * m + lane) * n + j, mine, rs[bz * m + lane], cs[bz * n + j], flags, requant,
+                   relu);
+  }
+}
+
+// ---- SIMT dp4a GEMM: 64 x 64 output tile, 256 threads, 4 x 4 per thread ---
+__global__ void __launch_bounds__(256) k_gemm_simt(const int8_t* __restrict__ X, int ldx,
+                                                   const int8_t* __restrict__ Wt, int ldw,
+                                                   const float* __restrict__ rs, const float* __restrict__ cs, int m,
+                                                   int k, int n, unsigned flags, const int8_t* __restrict__ requant,
+                                                   const int8_t* __restrict__ relu, void* out) {
+  __shared__ int xs[64][17];
+  __shared__ int ws[64][17];
+  const int bz = blockIdx.z;
+  const int row0 = blockIdx.y * 64, col0 = blockIdx.x * 64;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int8_t* Xb = X + (int64_t)bz * m * ldx;
+  const int8_t* Wb = Wt + (int64_t)bz * n * ldw;
+  int acc[4][4] = {};
+  for (int k0 = 0; k0 < k; k0 += 64) {
+    for (int idx = threadIdx.x; idx < 64 * 16; idx += 256) {
+      int r = idx >> 4, c = idx & 15;
+      int kk = k0 + 4 * c;
+      int xv = 0, wv = 0;
+      if (row0 + r < m && kk < ldx) xv = *(const int*)(Xb + (int64_t)(row0 + r) * ldx + kk);
+      if (col0 + r < n && kk < ldw) wv = *(const int*)(Wb + (int64_t)(col0 + r) * ldw + kk);
+      xs[r][c] = xv;
+      ws[r][c] = wv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < 16; c++) {
+      int a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) a[i] = xs[ty + 16 * i][c];
+#pragma unroll
+      for (int j = 0; j < 4; j++) b[j] = ws[tx + 16 * j][c];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = __dp4a(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    int row = row0 + ty + 16 * i;
+    if (row >= m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      int col = col0 + tx + 16 * j;
+      if (col < n)
+        dc_store_out(out, ((int64_t)bz * m + row) * n + col, acc[i][j], rs[bz * m + row], cs[bz * n + col], flags,
+                     requant, relu);
+    }
+  }
+}
+
+template <int MR>
+int launch_gemv(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+                int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st) {
+  const int nch = (k + 15) >> 4;
+  size_t smem = (size_t)MR * nch * 16;
+  if (smem > 200 * 1024) return dc_fail(ctx, DC_E_INVAL, "gemv: k=%d too long for %d rows in shared memory", k, MR);
+  if (smem > 48 * 1024) DC_CUDA(ctx, cudaFuncSetAttribute(k_gemv<MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                          (int)smem));
+  // 8 warps per block; enough blocks to cover every column once or fill the SMs.
+  int blocks = (n + 7) / 8;
+  int cap = ctx->sm_count * (smem > 64 * 1024 ? 1 : 4);
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  dim3 grid(blocks, batch);
+  k_gemv<MR><<<grid, 256, smem, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant, ctx->d_relu, out);
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+}  // namespace
+
+int dc_fail(dc_ctx* ctx, int code, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->err = buf;
+  }
+  return code;
+}
+
+int dc_cuda_fail(dc_ctx* ctx, cudaError_t e, const char* what) {
+  return dc_fail(ctx, DC_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int dc_gemm_lut(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs, int m, int k,
+                int n, int batch, unsigned flags, void* out, cudaStream_t st) {
+  if (m == 0 || n == 0) return DC_OK;
+  dim3 blk(8, 8);
+  dim3 grid((m + 7) / 8, (n + 7) / 8, batch);
+  k_lut_gemm<<<grid, blk, 0, st>>>(Xq, Wq, rs, cs, m, k, n, flags, ctx->d_mul, ctx->d_requant, ctx->d_relu, out);
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                     const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                     int kind) {
+  if (m == 0 || n == 0 || batch == 0) return DC_OK;
+  if (kind == 0) kind = (m <= 8) ? 1 : 3;
+  if (kind == 3) {
+    if (ctx->tc_enabled) {
+      int rc = dc_gemm_tc(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
+      if (rc != DC_E_INVAL) return rc;
+    }
+    kind = 2;  // shape the tensor-core kernel does not take: the SIMT kernel
+  }
+  if (kind == 1) {
+    if (m <= 1) return launch_gemv<1>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
+    if (m <= 2) return launch_gemv<2>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
+    if (m <= 4) return launch_gemv<4>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
+    if (m <= 8) return launch_gemv<8>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
+    kind = 2;
+  }
+  dim3 grid((n + 63) / 64, (m + 63) / 64, batch);
+  k_gemm_simt<<<grid, 256, 0, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant, ctx->d_relu, out);
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+int dc_scratch(dc_ctx* ctx, size_t bytes, void** p) {
+  if (bytes > ctx->scratch_bytes) {
+    DC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+    size_t want = bytes + (bytes >> 2) + 4096;
+    if (cudaMalloc(&ctx->scratch, want) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(ctx, DC_E_NOMEM, "scratch allocation of %zu bytes failed", want);
+    }
+    ctx->scratch_bytes = want;
+  }
+  *p = ctx->scratch;
+  return DC_OK;
+}
+
+static size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static int out_elem_bytes(unsigned flags) { return (flags & DC_ACC) ? 4 : (flags & DC_REQUANT) ? 1 : 4; }
+
+extern "C" int dc_bgemm(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs, int m,
+                        int k, int n, int batch, unsigned flags, void* out) {
+  if (!ctx) return DC_E_INVAL;
+  if (m < 0 || k < 0 || n < 0 || batch < 1) return dc_fail(ctx, DC_E_INVAL, "bgemm: bad shape");
+  if (k > DC_MAX_INT32_K)
+    return dc_fail(ctx, DC_E_ACCBOUND,
+                   "bgemm: contraction length %d exceeds the int32 accumulator headroom %d (the sum would wrap)", k,
+                   DC_MAX_INT32_K);
+  if ((int64_t)m * n * batch == 0) return DC_OK;
+  if (!Xq || !Wq || !rs || !cs || !out) return dc_fail(ctx, DC_E_INVAL, "bgemm: null buffer");
+  const int ld = round_up(k > 0 ? k : 1, 16);
+  const size_t bx = al256((size_t)batch * m * ld), bw = al256((size_t)batch * k * n),
+               bwt = al256((size_t)batch * n * ld), brs = al256(4 * (size_t)batch * m),
+               bcs = al256(4 * (size_t)batch * n),
+               bo = al256((size_t)out_elem_bytes(flags) * batch * m * n);
+  void* base;
+  int rc = dc_scratch(ctx, bx + bw + bwt + brs + bcs + bo, &base);
+  if (rc) return rc;
+  char* p = (char*)base;
+  int8_t* dx = (int8_t*)p; p += bx;
+  int8_t* dw = (int8_t*)p; p += bw;
+  int8_t* dwt = (int8_t*)p; p += bwt;
+  float* drs = (float*)p; p += brs;
+  float* dcs = (float*)p; p += bcs;
+  void* dout = p;
+  cudaStream_t st = ctx->stream;
+  DC_CUDA(ctx, cudaMemsetAsync(dx, 0, bx, st));
+  if (k > 0) {
+    DC_CUDA(ctx, cudaMemcpy2DAsync(dx, ld, Xq, k, k, (size_t)batch * m, cudaMemcpyHostToDevice, st));
+    DC_CUDA(ctx, cudaMemcpyAsync(dw, Wq, (size_t)batch * k * n, cudaMemcpyHostToDevice, st));
+  }
+  DC_CUDA(ctx, cudaMemcpyAsync(drs, rs, 4 * (size_t)batch * m, cudaMemcpyHostToDevice, st));
+  DC_CUDA(ctx, cudaMemcpyAsync(dcs, cs, 4 * (size_t)batch * n, cudaMemcpyHostToDevice, st));
+  if ((rc = dc_launch_transpose_i8(ctx, dw, k, n, dwt, ld, batch, st))) return rc;
+  if ((rc = dc_gemm_dispatch(ctx, dx, ld, dwt, ld, drs, dcs, m, k, n, batch, flags, dout, st, 0))) return rc;
+  DC_CUDA(ctx, cudaMemcpyAsync(out, dout, (size_t)out_elem_bytes(flags) * batch * m * n, cudaMemcpyDeviceToHost, st));
+  return dc_sync(ctx);
+}
+
+extern "C" int dc_bgemm_dev(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                            const float* cs, int m, int k, int n, int batch, unsigned flags, void* out) {
+  if (!ctx) return DC_E_INVAL;
+  if (m < 0 || k < 0 || n < 0 || batch < 1 || ldx < k || ldw < k || (ldx & 15) || (ldw & 15))
+    return dc_fail(ctx, DC_E_INVAL, "bgemm_dev: bad shape or leading dimension");
+  if (k > DC_MAX_INT32_K)
+    return dc_fail(ctx, DC_E_ACCBOUND, "bgemm_dev: contraction length %d exceeds %d", k, DC_MAX_INT32_K);
+  return dc_gemm_dispatch(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, ctx->stream, 0);
+}
+
+// Internal entry for tests: force one kernel (1 GEMV, 2 SIMT, 3 tcgen05).
+extern "C" int dc_bgemm_dev_kind(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                                 const float* cs, int m, int k, int n, int batch, unsigned flags, void* out,
+                                 int kind) {
+  if (!ctx) return DC_E_INVAL;
+  if (m < 0 || k < 0 || n < 0 || batch < 1 || ldx < k || ldw < k || (ldx & 15) || (ldw & 15))
+    return dc_fail(ctx, DC_E_INVAL, "bgemm_dev: bad shape or leading dimension");
+  if (k > DC_MAX_INT32_K) return dc_fail(ctx, DC_E_ACCBOUND, "bgemm_dev: k=%d too long", k);
+  if (kind == 3) {
+    if (m == 0 || n == 0) return DC_OK;
+    return dc_gemm_tc(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, ctx->stream);
+  }
+  return dc_gemm_dispatch(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, ctx->stream, kind);
+}
+
+extern "C" int dc_bgemm_lut_dev(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs,
+                                int m, int k, int n, int batch, unsigned flags, void* out) {
+  if (!ctx) return DC_E_INVAL;
+  if (m < 0 || k < 0 || n < 0 || batch < 1) return dc_fail(ctx, DC_E_INVAL, "bgemm_lut: bad shape");
+  if (k > DC_MAX_INT32_K) return dc_fail(ctx, DC_E_ACCBOUND, "bgemm_lut: k=%d too long", k);
+  return dc_gemm_lut(ctx, Xq, Wq, rs, cs, m, k, n, batch, flags, out, ctx->stream);
+}
+
+// ---- resident weights -------------------------------------------------------
+extern "C" int dc_weight_register(dc_ctx* ctx, const float* W, int k, int n, dc_weight** out) {
+  if (!ctx || !W || !out || k <= 0 || n <= 0) return dc_fail(ctx, DC_E_INVAL, "weight_register: bad arguments");
+  if (k > DC_MAX_INT32_K) return dc_fail(ctx, DC_E_ACCBOUND, "weight_register: k=%d exceeds %d", k, DC_MAX_INT32_K);
+  dc_weight* w = new dc_weight();
+  w->ctx = ctx;
+  w->k = k;
+  w->n = n;
+  w->ldw = round_up(k, 16);
+  float* dW = nullptr;
+  cudaError_t e = cudaMalloc(&w->qt, (size_t)n * w->ldw);
+  if (e == cudaSuccess) e = cudaMalloc(&w->cs, 4 * (size_t)n);
+  if (e == cudaSuccess) e = cudaMalloc(&dW, 4 * (size_t)k * n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(dW);
+    dc_weight_free(w);
+    return dc_fail(ctx, DC_E_NOMEM, "weight_register: device allocation failed");
+  }
+  int rc = DC_OK;
+  e = cudaMemcpyAsync(dW, W, 4 * (size_t)k * n, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) rc = dc_cuda_fail(ctx, e, "weight upload");
+  if (!rc) rc = dc_launch_quant_cols_t(ctx, dW, k, n, w->qt, w->ldw, w->cs, ctx->stream);
+  if (!rc) rc = dc_sync(ctx);
+  cudaFree(dW);
+  if (rc) {
+    dc_weight_free(w);
+    return rc;
+  }
+  *out = w;
+  return DC_OK;
+}
+
+extern "C" void dc_weight_free(dc_weight* w) {
+  if (!w) return;
+  if (w->owns) {
+    cudaFree(w->qt);
+    cudaFree(w->cs);
+  }
+  delete w;
+}
+
+extern "C" int dc_weight_info(const dc_weight* w, const int8_t** qt, int* ldw, const float** cs, int* k, int* n) {
+  if (!w) return DC_E_INVAL;
+  if (qt) *qt = w->qt;
+  if (ldw) *ldw = w->ldw;
+  if (cs) *cs = w->cs;
+  if (k) *k = w->k;
+  if (n) *n = w->n;
+  return DC_OK;
+}
+
+extern "C" int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned flags, void* out) {
+  if (!ctx || !w || m < 0 || (m && (!X || !out))) return dc_fail(ctx, DC_E_INVAL, "vgemm: bad arguments");
+  if (m == 0) return DC_OK;
+  const size_t bx = al256((size_t)m * w->ldw), brs = al256(4 * (size_t)m);
+  void* base;
+  int rc = dc_scratch(ctx, bx + brs, &base);
+  if (rc) return rc;
+  int8_t* xq = (int8_t*)base;
+  float* rs = (float*)((char*)base + bx);
+  if ((rc = dc_launch_quant_rows(ctx, X, m, w->k, xq, w->ldw, rs, ctx->stream))) return rc;
+  return dc_gemm_dispatch(ctx, xq, w->ldw, w->qt, w->ldw, rs, w->cs, m, w->k, w->n, 1, flags, out, ctx->stream, 0);
+}

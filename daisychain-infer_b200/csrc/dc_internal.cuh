@@ -1,0 +1,107 @@
+// dc_internal.cuh -- shared definitions of libdcinfer (not part of the C ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "../../include/dcinfer.h"
+
+// Device status word bits (atomicOr'd by kernels, read and cleared by dc_sync).
+#define DC_ST_NONFINITE 1
+#define DC_ST_TIMEOUT 2
+#define DC_ST_BOUNDS 4
+
+struct dc_ctx {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t stream = nullptr;      // where work is launched
+  cudaStream_t own_stream = nullptr;  // created by dc_init
+  std::string err;
+  char label[160] = {0};
+  // LUT units: host copies (checked by sha256) and device copies.
+  int16_t h_mul[65536];
+  int8_t h_requant[65536];
+  int8_t h_relu[256];
+  int16_t* d_mul = nullptr;
+  int8_t* d_requant = nullptr;
+  int8_t* d_relu = nullptr;
+  int* d_status = nullptr;
+  // grow-only scratch for the host-buffer entry points
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  bool tc_enabled = true;  // tcgen05 GEMM passed its gate
+};
+
+struct dc_weight {
+  dc_ctx* ctx = nullptr;
+  int k = 0, n = 0, ldw = 0;
+  int8_t* qt = nullptr;  // n x ldw int8, quantised Wᵀ, zero past k
+  float* cs = nullptr;   // n column scales
+  bool owns = true;
+};
+
+static inline int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+// Record an error message on the context and return the code.
+int dc_fail(dc_ctx* ctx, int code, const char* fmt, ...);
+// Map a CUDA error to DC_E_CUDA with a message.
+int dc_cuda_fail(dc_ctx* ctx, cudaError_t e, const char* what);
+#define DC_CUDA(ctx, call)                                      \
+  do {                                                          \
+    cudaError_t _e = (call);                                    \
+    if (_e != cudaSuccess) return dc_cuda_fail((ctx), _e, #call); \
+  } while (0)
+
+int dc_scratch(dc_ctx* ctx, size_t bytes, void** p);
+
+// ---- launchers shared between translation units ----------------------------
+int dc_launch_quant_rows(dc_ctx* ctx, const float* X, int rows, int cols, int8_t* q, int ldq, float* s,
+                         cudaStream_t st);
+int dc_launch_quant_cols_t(dc_ctx* ctx, const float* W, int rows, int cols, int8_t* qt, int ldq, float* s,
+                           cudaStream_t st);
+int dc_launch_transpose_i8(dc_ctx* ctx, const int8_t* W, int k, int n, int8_t* Wt, int ldw, int batch,
+                           cudaStream_t st);
+
+// GEMM dispatch on device buffers.  kind: 0 auto, 1 GEMV, 2 SIMT, 3 tcgen05.
+int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                     const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                     int kind);
+int dc_gemm_lut(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs, int m, int k,
+                int n, int batch, unsigned flags, void* out, cudaStream_t st);
+// tcgen05 path (dc_gemm_tc.cu): returns DC_E_INVAL when the shape is not supported.
+int dc_gemm_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+               int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st);
+
+// ---- device helpers ---------------------------------------------------------
+// ECMAScript Math.round on a double: nearest, ties toward +infinity.
+__device__ __forceinline__ double dc_js_round(double v) {
+  double r = floor(v);
+  if (__dsub_rn(v, r) >= 0.5) r = __dadd_rn(r, 1.0);
+  return r;
+}
+__device__ __forceinline__ int8_t dc_clamp8(double v) {
+  return v < -128.0 ? (int8_t)-128 : v > 127.0 ? (int8_t)127 : (int8_t)(int)v;
+}
+// verified_core.js:227-228: f32(f32(f32(s) * a) * b), each step rounded.
+__device__ __forceinline__ float dc_epi(int32_t s, float a, float b) {
+  return __fmul_rn(__fmul_rn(__int2float_rn(s), a), b);
+}
+// Store one output element in the mode selected by flags.
+__device__ __forceinline__ void dc_store_out(void* out, int64_t idx, int32_t acc, float rsv, float csv, unsigned flags,
+                                             const int8_t* __restrict__ requant, const int8_t* __restrict__ relu) {
+  if (flags & DC_ACC) {
+    ((int32_t*)out)[idx] = acc;
+  } else if (flags & DC_REQUANT) {
+    int32_t a = acc < -32768 ? -32768 : (acc > 32767 ? 32767 : acc);
+    int8_t v = __ldg(requant + (uint16_t)(int16_t)a);
+    if (flags & DC_RELU) v = __ldg(relu + (uint8_t)v);
+    ((int8_t*)out)[idx] = v;
+  } else {
+    float v = dc_epi(acc, rsv, csv);
+    if ((flags & DC_RELU) && v < 0.0f) v = 0.0f;
+    ((float*)out)[idx] = v;
+  }
+}

@@ -1,0 +1,136 @@
+/*
+ * dcinfer.h -- C ABI of the B200 verified INT8 W8A8 library (libdcinfer.so).
+ *
+ * The library replaces the WebGPU dispatch layer of DaisyChain-Infer
+ * (public/webgpu.js) behind the same compute-core contract that
+ * public/verified_core.js and public/infer.js call.  Plain C types only:
+ * pointers, sizes and integer status codes.  Every pointer argument says
+ * whether it is host or device memory.  A dc_ctx is bound to one CUDA device
+ * and one stream and is not thread safe (the reference runs on one JS thread).
+ *
+ * Arithmetic contract (bit-exact with the reference CPU mirror):
+ *   rows:    s[r] = f32(max(absmax/127, 1e-8)) computed in double; q uses the
+ *            double scale and ECMAScript Math.round (verified_core.js:108-121)
+ *   columns: s[c] = f32(max(absmax/127, 1e-8)); q uses the f32-rounded scale
+ *            (verified_core.js:122-136)
+ *   GEMM:    int32 sum of exact int8 products (= the mul LUT), k <= 131071,
+ *            epilogue f32(f32(f32(acc) * rs[row]) * cs[col]), ReLU keeps -0
+ *            (verified_core.js:227-228, 241-266)
+ *   requant: out8 = requant_lut[(uint16)sat16(acc)], then relu_lut when DC_RELU
+ *            (a rule this library declares; the reference defines none)
+ */
+#ifndef DCINFER_H
+#define DCINFER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------- */
+#define DC_OK 0
+#define DC_E_ACCBOUND 1    /* AccumulatorBoundError, verified_core.js:41-49 */
+#define DC_E_NONFINITE 2   /* NonFiniteError, verified_core.js:16-27 */
+#define DC_E_INVAL 3       /* bad argument (shape, null pointer, range) */
+#define DC_E_NOMEM 4       /* device or host allocation failed */
+#define DC_E_CUDA 5        /* a CUDA runtime call failed; see dc_last_error */
+#define DC_E_TIMEOUT 6     /* a bounded device wait gave up */
+#define DC_E_LUT 7         /* LUT self-test or sha256 check failed (app.js:1074-1075) */
+#define DC_E_GATE 8        /* init gate: a kernel disagreed with the LUT kernel (webgpu.js:470-492) */
+
+/* ---- GEMM flags (the reference's d.relu / d.acc, plus the requant unit) ---- */
+#define DC_RELU 1u         /* d.relu: v < 0 ? 0 : v after the epilogue */
+#define DC_ACC 2u          /* d.acc: return the raw int32 accumulator */
+#define DC_REQUANT 4u      /* int8 output through requant_lut (and relu_lut) */
+
+#define DC_MAX_INT32_K 131071 /* floor((2^31-1)/(128*128)), verified_core.js:41 */
+
+typedef struct dc_ctx dc_ctx;
+typedef struct dc_weight dc_weight;
+
+/* ---- context (replaces Compute.initCompute / loadLUTs, webgpu.js:247-648) --- */
+/* Binds to `device`, creates a stream, builds the three LUT units, checks their
+ * sha256 against the reference's LFS object ids and the mul[7,-3] == -21
+ * self-test (app.js:1074-1075), uploads them, and gates every GEMM kernel
+ * against the LUT kernel at the reference's gate shapes, clean and on poisoned
+ * buffers (webgpu.js:470-516).  Returns DC_E_LUT / DC_E_GATE on failure. */
+int dc_init(int device, dc_ctx** out);
+void dc_destroy(dc_ctx* ctx);
+/* compute.label (webgpu.js:616-618). */
+const char* dc_backend_label(const dc_ctx* ctx);
+/* Message of the last failing call on this context. */
+const char* dc_last_error(const dc_ctx* ctx);
+/* The context's cudaStream_t, as an opaque pointer. */
+void* dc_stream(const dc_ctx* ctx);
+/* Message of the last dc_init that failed on this thread (no context exists). */
+const char* dc_init_error(void);
+/* Run the context's work on an existing cudaStream_t (NULL = the context's own
+ * stream).  Lets a caller order the library's launches with its own work. */
+int dc_set_stream(dc_ctx* ctx, void* stream);
+/* 1 when the tcgen05 tensor-core GEMM passed its init gate and is in use. */
+int dc_tc_enabled(const dc_ctx* ctx);
+/* Copy the LUT units out (host buffers of 65536 int16, 65536 int8, 256 int8). */
+int dc_luts(const dc_ctx* ctx, int16_t* mul, int8_t* requant, int8_t* relu);
+/* Wait for the context's stream; report (and clear) a device-side status such
+ * as a non-finite input seen by a quantiser. */
+int dc_sync(dc_ctx* ctx);
+
+/* ---- the GEMM unit (compute.bgemm, webgpu.js:836-857) ------------------------
+ * Host buffers, exactly the reference's argument meaning:
+ *   Xq (batch*m) x k int8 row-major, Wq batch x (k x n) int8 row-major,
+ *   rs[batch*m], cs[batch*n] f32.  out is int32 (DC_ACC), int8 (DC_REQUANT) or
+ *   f32, (batch*m) x n row-major, owned by the caller.
+ * Refuses k > 131071 with DC_E_ACCBOUND before any launch (webgpu.js:838). */
+int dc_bgemm(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs, int m, int k, int n,
+             int batch, unsigned flags, void* out);
+
+/* Device-resident variant.  Wt is the weight in the library's layout: per batch
+ * n rows of ldw bytes (K-major, i.e. Wᵀ), zero past k; Xq is (batch*m) rows of
+ * ldx bytes, zero past k.  ldw and ldx are multiples of 16.  Asynchronous on the
+ * context's stream. */
+int dc_bgemm_dev(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+                 int m, int k, int n, int batch, unsigned flags, void* out);
+
+/* dc_bgemm_dev with one kernel forced (1 GEMV, 2 SIMT dp4a, 3 tcgen05), for the
+ * init gates and the parity tests; DC_E_INVAL when that kernel cannot take the
+ * shape. */
+int dc_bgemm_dev_kind(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                      const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, int kind);
+
+/* Same contraction through the LUT kernel (every product looked up in the mul
+ * unit, the reference's WGSL_BG_LUT twin).  Reference-layout device buffers. */
+int dc_bgemm_lut_dev(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs, int m, int k,
+                     int n, int batch, unsigned flags, void* out);
+
+/* ---- quantisers (verified_core.js:108-136), device buffers ----------------- */
+/* X rows x cols f32 -> q rows x ldq int8 (zero past cols), s[rows] f32. */
+int dc_quantize_rows(dc_ctx* ctx, const float* X, int rows, int cols, int8_t* q, int ldq, float* s);
+/* W rows x cols f32 (k x n) -> qt cols x ldq int8 = quantised Wᵀ (zero past
+ * rows), s[cols] f32.  Asynchronous; a non-finite input is reported by dc_sync. */
+int dc_quantize_cols_t(dc_ctx* ctx, const float* W, int rows, int cols, int8_t* qt, int ldq, float* s);
+
+/* ---- resident weights (vgemmBlock's per-call quantizeCols, done once) ------- */
+/* W is k x n f32 row-major in HOST memory (the reference's layout after
+ * toKN, shard.js:70-76).  Quantised once on the device: bit-identical to the
+ * reference re-quantising it on every call (verified_core.js:430). */
+int dc_weight_register(dc_ctx* ctx, const float* W, int k, int n, dc_weight** out);
+void dc_weight_free(dc_weight* w);
+/* Device pointers and leading dimension of a registered weight. */
+int dc_weight_info(const dc_weight* w, const int8_t** qt, int* ldw, const float** cs, int* k, int* n);
+
+/* vgemmBlock (verified_core.js:425-449) with a registered weight, device
+ * buffers: out (m x n f32) = epilogue(quantizeRows(X) x W).  Asynchronous. */
+int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned flags, void* out);
+
+/* ---- kernel probe (webgpu.js:998-1060) --------------------------------------
+ * Runs the seeded probe GEMM (m=24 k=96 n=24 batch=2, acc) through the live
+ * kernels; returns the FNV-1a of the int32 result (before the reference folds in
+ * its transcendental hash, which needs V8). */
+int dc_kernel_probe(dc_ctx* ctx, uint32_t* hash);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

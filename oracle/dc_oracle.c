@@ -1,0 +1,712 @@
+/*
+ * dc_oracle.c -- CPU oracle for DaisyChain-Infer's verified INT8 W8A8 path.
+ *
+ * TEST INFRASTRUCTURE, NOT PRODUCT CODE.  This file restates in plain C the
+ * arithmetic of the reference's JavaScript CPU path so that the CUDA product
+ * can be checked against it bit for bit.  Only tests/, __graft_entry__.smoke()
+ * and bench.py's CPU-baseline legs load it; the product library never links,
+ * loads or calls it, and it is never a fallback.
+ *
+ * What it restates (reference paths are relative to the reference project):
+ *   public/verified_core.js  assertFinite :16-27, accBound/MAX_INT32_K :41-49,
+ *                            quantizeRows :108-121, quantizeCols :122-136,
+ *                            epi :227-228, bgemmJS :241-266, vgemmBlock :425-449
+ *   public/infer.js          rmsNorm :30-39, silu :59, ropeTables :71-81,
+ *                            applyRope :83-97, layerForward :114-221,
+ *                            embedRows :298-310, logitsAt :324-334,
+ *                            pickToken (greedy) :390-396
+ *   public/webgpu.js         probeInputs :998-1009, kernelProbe's FNV :1053-1055
+ *   public/shard.js          fnv1a :195-200
+ *   test_pipeline.js         mulberry32 :32, rnd :33-37 (weight fixtures)
+ *
+ * Parity status.  The LUT contents are pinned by the sha256 of the reference's
+ * LFS objects.  Integer work (quantisation, int32 accumulation, LUT outputs)
+ * and every f32/f64 step built from + - * / sqrt are pinned by IEEE-754
+ * (correct rounding) and by the reference's known-answer tests.  Values
+ * downstream of a transcendental (softmax exp, SiLU exp, RoPE pow/cos/sin)
+ * are PARITY UNPINNED against V8: no JavaScript runtime exists on either
+ * machine, and the reference stores no golden vectors.  exp() here follows
+ * the fdlibm 5.3 method (Sun Microsystems, 1993), the method V8's Math.exp is
+ * ported from; pow/cos/sin for the RoPE tables come from the C library.
+ *
+ * The requant-LUT output rule is not defined anywhere in the reference (it
+ * belonged to a Python kernel that is not in the repository).  This build
+ * declares it: out8 = requant[(uint16)sat16(acc)], then relu[(uint8)out8]
+ * when the ReLU flag is set.  That output is bit-exact against this declared
+ * rule, not against reference code.
+ *
+ * Build: oracle/Makefile (gcc -O2 -ffp-contract=off, no -march, so no FMA
+ * contraction and every double/float operation rounds exactly once).
+ */
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ORC_OK 0
+#define ORC_E_ACCBOUND 1
+#define ORC_E_NONFINITE 2
+#define ORC_E_INVAL 3
+#define ORC_E_NOMEM 4
+
+#define ORC_RELU 1u
+#define ORC_ACC 2u
+#define ORC_REQUANT 4u
+
+/* floor((2^31 - 1) / (128 * 128)) -- verified_core.js:41 */
+#define ORC_MAX_INT32_K 131071
+
+static double bits2d(uint64_t u) { double d; memcpy(&d, &u, 8); return d; }
+static uint64_t d2bits(double d) { uint64_t u; memcpy(&u, &d, 8); return u; }
+
+int orc_max_int32_k(void) { return (int)floor(2147483647.0 / (128.0 * 128.0)); }
+
+/* verified_core.js:42-49: refuse a contraction that could wrap int32. */
+int orc_acc_bound(int64_t k) { return k > ORC_MAX_INT32_K ? ORC_E_ACCBOUND : ORC_OK; }
+
+/* verified_core.js:16-27: index of the first non-finite value, or -1. */
+int64_t orc_first_nonfinite(const float* x, int64_t n) {
+  for (int64_t i = 0; i < n; i++)
+    if (!isfinite(x[i])) return i;
+  return -1;
+}
+
+/* ECMAScript Math.round: nearest integer, ties toward +infinity.
+ * floor(v + 0.5) is wrong at 0.49999999999999994, so compare the remainder. */
+static double js_round(double v) {
+  double r = floor(v);
+  if (v - r >= 0.5) r += 1.0;
+  return r;
+}
+static int8_t clamp8(double v) { return v < -128.0 ? (int8_t)-128 : v > 127.0 ? (int8_t)127 : (int8_t)v; }
+
+double orc_js_round(double v) { return js_round(v); }
+
+/* ---- lookup-table units: public/{mul,requant,relu}_lut.bin, reconstructed */
+void orc_make_luts(int16_t* mul, int8_t* requant, int8_t* relu) {
+  for (int a = 0; a < 256; a++)
+    for (int b = 0; b < 256; b++)
+      mul[a * 256 + b] = (int16_t)((a > 127 ? a - 256 : a) * (b > 127 ? b - 256 : b));
+  for (int u = 0; u < 65536; u++) {
+    int s = u > 32767 ? u - 65536 : u;
+    requant[u] = (int8_t)(s >> 8); /* arithmetic shift by luts_meta.json "shift": 8 */
+  }
+  for (int u = 0; u < 256; u++) {
+    int s = u > 127 ? u - 256 : u;
+    relu[u] = (int8_t)(s > 0 ? s : 0);
+  }
+}
+
+/* ---- quantisers ------------------------------------------------------------ */
+/* verified_core.js:108-121.  The scale is computed in DOUBLE and the quotient
+ * uses that double; only the stored copy s[r] is rounded to f32. */
+int orc_quantize_rows(const float* X, int64_t rows, int64_t cols, int8_t* q, float* s) {
+  if (orc_first_nonfinite(X, rows * cols) >= 0) return ORC_E_NONFINITE;
+  for (int64_t r = 0; r < rows; r++) {
+    const float* x = X + r * cols;
+    double mx = 0.0;
+    for (int64_t c = 0; c < cols; c++) {
+      double a = fabs((double)x[c]);
+      if (a > mx) mx = a;
+    }
+    double sc = mx / 127.0;
+    if (!(sc > 1e-8)) sc = 1e-8;
+    s[r] = (float)sc;
+    for (int64_t c = 0; c < cols; c++) q[r * cols + c] = clamp8(js_round((double)x[c] / sc));
+  }
+  return ORC_OK;
+}
+
+/* verified_core.js:122-136.  The scale is stored as f32 and the quotient uses
+ * the f32-ROUNDED scale (the asymmetry with quantizeRows is real). */
+int orc_quantize_cols(const float* W, int64_t rows, int64_t cols, int8_t* q, float* s) {
+  if (orc_first_nonfinite(W, rows * cols) >= 0) return ORC_E_NONFINITE;
+  for (int64_t c = 0; c < cols; c++) {
+    double mx = 0.0;
+    for (int64_t r = 0; r < rows; r++) {
+      double a = fabs((double)W[r * cols + c]);
+      if (a > mx) mx = a;
+    }
+    double sc = mx / 127.0;
+    if (!(sc > 1e-8)) sc = 1e-8;
+    s[c] = (float)sc;
+  }
+  for (int64_t r = 0; r < rows; r++)
+    for (int64_t c = 0; c < cols; c++)
+      q[r * cols + c] = clamp8(js_round((double)W[r * cols + c] / (double)s[c]));
+  return ORC_OK;
+}
+
+/* ---- epilogue and GEMM ---------------------------------------------------- */
+/* verified_core.js:227-228: f32(f32(f32(s) * a) * b), no fused multiply-add. */
+float orc_epi(int32_t s, float a, float b) {
+  volatile float t = (float)s;
+  t = t * a;
+  t = t * b;
+  return t;
+}
+
+/* verified_core.js:241-266 (bgemmJS), extended with the declared requant rule.
+ * X is (batch*m) x k int8, W is batch x (k x n) int8 row-major, rs[batch*m],
+ * cs[batch*n].  out is int32 (ACC), int8 (REQUANT) or f32 (default). */
+int orc_bgemm(const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs, int m, int k, int n,
+              int batch, unsigned flags, const int16_t* mul, const int8_t* requant, const int8_t* relu,
+              void* out) {
+  if (m < 0 || k < 0 || n < 0 || batch < 1) return ORC_E_INVAL;
+  if (orc_acc_bound(k)) return ORC_E_ACCBOUND;
+  int32_t* acc = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n > 0 ? n : 1));
+  if (!acc) return ORC_E_NOMEM;
+  for (int bz = 0; bz < batch; bz++) {
+    const int8_t* xb = Xq + (int64_t)bz * m * k;
+    const int8_t* wb = Wq + (int64_t)bz * k * n;
+    for (int i = 0; i < m; i++) {
+      memset(acc, 0, sizeof(int32_t) * (size_t)n);
+      const int8_t* xr = xb + (int64_t)i * k;
+      for (int p = 0; p < k; p++) {
+        const int16_t* row = mul + ((uint8_t)xr[p]) * 256;
+        const int8_t* wr = wb + (int64_t)p * n;
+        for (int j = 0; j < n; j++) acc[j] = (int32_t)((uint32_t)acc[j] + (uint32_t)(int32_t)row[(uint8_t)wr[j]]);
+      }
+      int64_t orow = ((int64_t)bz * m + i) * n;
+      if (flags & ORC_ACC) {
+        memcpy((int32_t*)out + orow, acc, sizeof(int32_t) * (size_t)n);
+      } else if (flags & ORC_REQUANT) {
+        int8_t* o = (int8_t*)out + orow;
+        for (int j = 0; j < n; j++) {
+          int32_t a = acc[j] < -32768 ? -32768 : acc[j] > 32767 ? 32767 : acc[j];
+          int8_t v = requant[(uint16_t)(int16_t)a];
+          if (flags & ORC_RELU) v = relu[(uint8_t)v];
+          o[j] = v;
+        }
+      } else {
+        float* o = (float*)out + orow;
+        float rsc = rs[(int64_t)bz * m + i];
+        for (int j = 0; j < n; j++) {
+          float v = orc_epi(acc[j], rsc, cs[(int64_t)bz * n + j]);
+          o[j] = ((flags & ORC_RELU) && v < 0.0f) ? 0.0f : v;
+        }
+      }
+    }
+  }
+  free(acc);
+  return ORC_OK;
+}
+
+/* ---- exp: fdlibm 5.3 method (Sun Microsystems, 1993) ------------------------
+ * Reduce x = k*ln2 + r with |r| <= ln2/2 (r kept as hi - lo), approximate
+ * R(r^2) = r*(e^r + 1)/(e^r - 1) by a degree-5 Remez polynomial, rebuild
+ * e^r = 1 - ((lo - r*c/(2 - c)) - hi) and scale by 2^k. */
+double orc_exp(double x) {
+  const double one = 1.0, huge = 1.0e+300;
+  const double halF[2] = {0.5, -0.5};
+  const double twom1000 = bits2d(0x0170000000000000ULL);
+  const double o_threshold = bits2d(0x40862E42FEFA39EFULL);
+  const double u_threshold = bits2d(0xC0874910D52D3051ULL);
+  const double ln2HI[2] = {bits2d(0x3FE62E42FEE00000ULL), bits2d(0xBFE62E42FEE00000ULL)};
+  const double ln2LO[2] = {bits2d(0x3DEA39EF35793C76ULL), bits2d(0xBDEA39EF35793C76ULL)};
+  const double invln2 = bits2d(0x3FF71547652B82FEULL);
+  const double P1 = bits2d(0x3FC555555555553EULL), P2 = bits2d(0xBF66C16C16BEBD93ULL),
+               P3 = bits2d(0x3F11566AAF25DE2CULL), P4 = bits2d(0xBEBBBD41C5D26BF1ULL),
+               P5 = bits2d(0x3E66376972BEA4D0ULL);
+  double y, hi = 0.0, lo = 0.0, c, t;
+  int k = 0;
+  uint64_t bx = d2bits(x);
+  uint32_t hx = (uint32_t)(bx >> 32);
+  int xsb = (int)((hx >> 31) & 1);
+  hx &= 0x7fffffffu;
+  if (hx >= 0x40862E42u) { /* |x| >= 709.78... */
+    if (hx >= 0x7ff00000u) {
+      if (((hx & 0xfffffu) | (uint32_t)bx) != 0) return x + x; /* NaN */
+      return xsb == 0 ? x : 0.0;                               /* exp(+-inf) */
+    }
+    if (x > o_threshold) return huge * huge;
+    if (x < u_threshold) return twom1000 * twom1000;
+  }
+  if (hx > 0x3fd62e42u) {   /* |x| > 0.5 ln2 */
+    if (hx < 0x3FF0A2B2u) { /* and |x| < 1.5 ln2 */
+      hi = x - ln2HI[xsb];
+      lo = ln2LO[xsb];
+      k = 1 - xsb - xsb;
+    } else {
+      k = (int)(invln2 * x + halF[xsb]);
+      t = k;
+      hi = x - t * ln2HI[0];
+      lo = t * ln2LO[0];
+    }
+    x = hi - lo;
+  } else if (hx < 0x3e300000u) { /* |x| < 2^-28 */
+    if (huge + x > one) return one + x;
+  } else {
+    k = 0;
+  }
+  t = x * x;
+  c = x - t * (P1 + t * (P2 + t * (P3 + t * (P4 + t * P5))));
+  if (k == 0) return one - ((x * c) / (c - 2.0) - x);
+  y = one - ((lo - (x * c) / (2.0 - c)) - hi);
+  uint64_t by = d2bits(y);
+  /* add k (or k + 1000) to the exponent field of y */
+  if (k >= -1021) return bits2d((uint64_t)((int64_t)by + (int64_t)k * 4503599627370496LL));
+  return bits2d((uint64_t)((int64_t)by + (int64_t)(k + 1000) * 4503599627370496LL)) * twom1000;
+}
+
+/* ---- elementwise pieces of layerForward ----------------------------------- */
+/* infer.js:30-39: s accumulates v*v in double, sequentially from j = 0. */
+void orc_rmsnorm(const float* x, int rows, int C, const float* w, double eps, float* y) {
+  for (int r = 0; r < rows; r++) {
+    const float* xr = x + (int64_t)r * C;
+    double s = 0.0;
+    for (int j = 0; j < C; j++) {
+      double v = xr[j];
+      s += v * v;
+    }
+    double inv = 1.0 / sqrt(s / (double)C + eps);
+    for (int j = 0; j < C; j++) y[(int64_t)r * C + j] = (float)((double)xr[j] * inv * (double)w[j]);
+  }
+}
+
+/* infer.js:71-81: f = p / theta^(2i/hd), tables stored f32. */
+void orc_rope_tables(int hd, double theta, int maxT, float* cos_t, float* sin_t) {
+  int half = hd >> 1;
+  for (int p = 0; p < maxT; p++)
+    for (int i = 0; i < half; i++) {
+      double f = (double)p / pow(theta, (2.0 * i) / (double)hd);
+      cos_t[(int64_t)p * half + i] = (float)cos(f);
+      sin_t[(int64_t)p * half + i] = (float)sin(f);
+    }
+}
+
+/* infer.js:83-97: half-split rotation, products and sum in double, stored f32. */
+void orc_apply_rope(float* x, int T, int nHeads, int hd, const float* cos_t, const float* sin_t, int pos0) {
+  int half = hd >> 1, stride = nHeads * hd;
+  for (int t = 0; t < T; t++) {
+    int p = pos0 + t;
+    for (int h = 0; h < nHeads; h++) {
+      float* o = x + (int64_t)t * stride + h * hd;
+      for (int i = 0; i < half; i++) {
+        double c = cos_t[(int64_t)p * half + i], s = sin_t[(int64_t)p * half + i];
+        double a = o[i], b = o[half + i];
+        o[i] = (float)(a * c - b * s);
+        o[half + i] = (float)(b * c + a * s);
+      }
+    }
+  }
+}
+
+/* infer.js:182-194 for one head: causal softmax over columns oldest..see of
+ * each row (oldest = 0, no sliding window); masked entries stay 0. */
+void orc_softmax_causal(const float* scores, int T, int N, int n0, double scale, float* a) {
+  for (int64_t i = 0; i < (int64_t)T * N; i++) a[i] = 0.0f;
+  for (int i = 0; i < T; i++) {
+    int see = n0 + i;
+    double mx = -INFINITY;
+    for (int j = 0; j <= see; j++) {
+      double v = (double)scores[(int64_t)i * N + j] * scale;
+      if (v > mx) mx = v;
+    }
+    double z = 0.0;
+    for (int j = 0; j <= see; j++) {
+      double e = orc_exp((double)scores[(int64_t)i * N + j] * scale - mx);
+      a[(int64_t)i * N + j] = (float)e;
+      z += e;
+    }
+    for (int j = 0; j <= see; j++) a[(int64_t)i * N + j] = (float)((double)a[(int64_t)i * N + j] / z);
+  }
+}
+
+/* infer.js:59 + :212: f32(silu(g) * u), silu(v) = v / (1 + exp(-v)) in double. */
+void orc_swiglu(const float* g, const float* u, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; i++) {
+    double v = g[i];
+    double s = v / (1.0 + orc_exp(-v));
+    out[i] = (float)(s * (double)u[i]);
+  }
+}
+
+/* ---- vgemmBlock (verified_core.js:425-449), batch 1 ------------------------ */
+typedef struct {
+  int k, n;
+  int8_t* q; /* k x n row-major, as quantizeCols returns it */
+  float* s;  /* n */
+} orc_wq;
+
+static int wq_build(orc_wq* w, const float* Wf, int k, int n) {
+  w->k = k;
+  w->n = n;
+  w->q = (int8_t*)malloc((size_t)k * n + 1);
+  w->s = (float*)malloc(sizeof(float) * (size_t)n + 4);
+  if (!w->q || !w->s) return ORC_E_NOMEM;
+  return orc_quantize_cols(Wf, k, n, w->q, w->s);
+}
+static void wq_free(orc_wq* w) {
+  free(w->q);
+  free(w->s);
+  w->q = NULL;
+  w->s = NULL;
+}
+
+static int16_t g_mul[65536];
+static int8_t g_requant[65536], g_relu[256];
+static int g_luts_ready = 0;
+static void luts_init(void) {
+  if (!g_luts_ready) {
+    orc_make_luts(g_mul, g_requant, g_relu);
+    g_luts_ready = 1;
+  }
+}
+
+/* X (m x k f32) times a quantised weight -> out (m x n f32). */
+static int vgemm_wq(const float* X, int m, const orc_wq* w, float* out) {
+  luts_init();
+  int k = w->k, n = w->n;
+  int8_t* xq = (int8_t*)malloc((size_t)m * k + 1);
+  float* rs = (float*)malloc(sizeof(float) * (size_t)m + 4);
+  if (!xq || !rs) { free(xq); free(rs); return ORC_E_NOMEM; }
+  int rc = orc_quantize_rows(X, m, k, xq, rs);
+  if (rc == ORC_OK) rc = orc_bgemm(xq, w->q, rs, w->s, m, k, n, 1, 0, g_mul, g_requant, g_relu, out);
+  free(xq);
+  free(rs);
+  return rc;
+}
+/* The full per-call vgemmBlock: both operands quantised on every call. */
+int orc_vgemm(const float* X, const float* Wf, int m, int k, int n, float* out) {
+  orc_wq w;
+  int rc = wq_build(&w, Wf, k, n);
+  if (rc == ORC_OK) rc = vgemm_wq(X, m, &w, out);
+  wq_free(&w);
+  return rc;
+}
+
+/* ---- model ------------------------------------------------------------------ */
+typedef struct {
+  const float *nrm1, *nrm2, *Wq, *Wk, *Wv, *Wo, *Wgate, *Wup, *Wdown; /* k x n f32 */
+  orc_wq q, k, v, o, gate, up, down;
+  int quantized;
+} orc_layer;
+
+typedef struct orc_model {
+  int hidden, layers, heads, kv_heads, head_dim, inter, vocab;
+  double eps, theta;
+  const float* emb;  /* vocab x hidden */
+  const float* nrmF; /* hidden */
+  float* lm_kn;      /* hidden x vocab f32 (own copy; embᵀ when tied) */
+  orc_wq lm;
+  int lm_quantized;
+  orc_layer* L;
+  int per_call_quant; /* 1: re-quantise weights on every GEMM, as vgemmBlock does */
+  float *rope_cos, *rope_sin;
+  int rope_max;
+} orc_model;
+
+typedef struct {
+  int n, max_pos, kv_dim;
+  float *k, *v;
+} orc_kv_layer;
+typedef struct orc_kv {
+  int lo, hi;
+  orc_kv_layer* L;
+} orc_kv;
+
+orc_model* orc_model_new(int hidden, int layers, int heads, int kv_heads, int head_dim, int inter, int vocab,
+                         double eps, double theta) {
+  if (hidden <= 0 || layers < 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || head_dim <= 0 ||
+      (head_dim & 1) || inter <= 0 || vocab <= 0)
+    return NULL;
+  orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
+  if (!m) return NULL;
+  m->hidden = hidden; m->layers = layers; m->heads = heads; m->kv_heads = kv_heads;
+  m->head_dim = head_dim; m->inter = inter; m->vocab = vocab; m->eps = eps; m->theta = theta;
+  m->L = (orc_layer*)calloc((size_t)(layers > 0 ? layers : 1), sizeof(orc_layer));
+  return m;
+}
+
+void orc_model_free(orc_model* m) {
+  if (!m) return;
+  for (int l = 0; l < m->layers; l++) {
+    orc_layer* y = &m->L[l];
+    if (y->quantized) {
+      wq_free(&y->q); wq_free(&y->k); wq_free(&y->v); wq_free(&y->o);
+      wq_free(&y->gate); wq_free(&y->up); wq_free(&y->down);
+    }
+  }
+  if (m->lm_quantized) wq_free(&m->lm);
+  free(m->lm_kn);
+  free(m->L);
+  free(m->rope_cos);
+  free(m->rope_sin);
+  free(m);
+}
+
+void orc_model_set_per_call_quant(orc_model* m, int on) { m->per_call_quant = on; }
+
+/* Head tensors.  lm_kn == NULL means tied: lm_head = embᵀ (shard.js:92, 123-128). */
+int orc_model_set_head(orc_model* m, const float* emb, const float* nrmF, const float* lm_kn) {
+  int C = m->hidden, V = m->vocab;
+  m->emb = emb;
+  m->nrmF = nrmF;
+  free(m->lm_kn);
+  m->lm_kn = (float*)malloc(sizeof(float) * (size_t)C * V);
+  if (!m->lm_kn) return ORC_E_NOMEM;
+  if (lm_kn) memcpy(m->lm_kn, lm_kn, sizeof(float) * (size_t)C * V);
+  else
+    for (int v = 0; v < V; v++)
+      for (int c = 0; c < C; c++) m->lm_kn[(int64_t)c * V + v] = emb[(int64_t)v * C + c];
+  if (m->lm_quantized) wq_free(&m->lm);
+  m->lm_quantized = 0;
+  return ORC_OK;
+}
+
+int orc_model_set_layer(orc_model* m, int l, const float* nrm1, const float* nrm2, const float* Wq, const float* Wk,
+                        const float* Wv, const float* Wo, const float* Wgate, const float* Wup, const float* Wdown) {
+  if (l < 0 || l >= m->layers) return ORC_E_INVAL;
+  orc_layer* y = &m->L[l];
+  y->nrm1 = nrm1; y->nrm2 = nrm2; y->Wq = Wq; y->Wk = Wk; y->Wv = Wv; y->Wo = Wo;
+  y->Wgate = Wgate; y->Wup = Wup; y->Wdown = Wdown;
+  return ORC_OK;
+}
+
+/* Weight quantisation is deterministic, so quantising once and reusing the
+ * result is bit-identical to vgemmBlock's per-call quantizeCols. */
+static int layer_quantize(orc_model* m, orc_layer* y) {
+  if (y->quantized) return ORC_OK;
+  int C = m->hidden, q = m->heads * m->head_dim, kv = m->kv_heads * m->head_dim, I = m->inter;
+  int rc = ORC_OK;
+  rc |= wq_build(&y->q, y->Wq, C, q);
+  rc |= wq_build(&y->k, y->Wk, C, kv);
+  rc |= wq_build(&y->v, y->Wv, C, kv);
+  rc |= wq_build(&y->o, y->Wo, q, C);
+  rc |= wq_build(&y->gate, y->Wgate, C, I);
+  rc |= wq_build(&y->up, y->Wup, C, I);
+  rc |= wq_build(&y->down, y->Wdown, I, C);
+  y->quantized = 1;
+  return rc ? ORC_E_NONFINITE : ORC_OK;
+}
+
+static int proj(orc_model* m, const float* X, int T, const float* Wf, const orc_wq* w, int k, int n, float* out) {
+  if (m->per_call_quant) return orc_vgemm(X, Wf, T, k, n, out);
+  (void)k; (void)n;
+  return vgemm_wq(X, T, w, out);
+}
+
+static int rope_ensure(orc_model* m, int need) {
+  if (m->rope_max >= need) return ORC_OK;
+  int half = m->head_dim >> 1;
+  free(m->rope_cos);
+  free(m->rope_sin);
+  m->rope_cos = (float*)malloc(sizeof(float) * (size_t)need * half + 4);
+  m->rope_sin = (float*)malloc(sizeof(float) * (size_t)need * half + 4);
+  if (!m->rope_cos || !m->rope_sin) return ORC_E_NOMEM;
+  orc_rope_tables(m->head_dim, m->theta, need, m->rope_cos, m->rope_sin);
+  m->rope_max = need;
+  return ORC_OK;
+}
+
+orc_kv* orc_kv_new(orc_model* m, int lo, int hi, int max_pos) {
+  if (lo < 0 || hi > m->layers || hi < lo || max_pos < 1) return NULL;
+  orc_kv* c = (orc_kv*)calloc(1, sizeof(orc_kv));
+  if (!c) return NULL;
+  c->lo = lo; c->hi = hi;
+  c->L = (orc_kv_layer*)calloc((size_t)(hi - lo + 1), sizeof(orc_kv_layer));
+  int kvd = m->kv_heads * m->head_dim;
+  for (int l = 0; l < hi - lo; l++) {
+    c->L[l].max_pos = max_pos;
+    c->L[l].kv_dim = kvd;
+    c->L[l].k = (float*)malloc(sizeof(float) * (size_t)max_pos * kvd);
+    c->L[l].v = (float*)malloc(sizeof(float) * (size_t)max_pos * kvd);
+  }
+  return c;
+}
+void orc_kv_free(orc_kv* c) {
+  if (!c) return;
+  for (int l = 0; l < c->hi - c->lo; l++) { free(c->L[l].k); free(c->L[l].v); }
+  free(c->L);
+  free(c);
+}
+int orc_kv_len(const orc_kv* c, int layer) { return c->L[layer - c->lo].n; }
+void orc_kv_read(const orc_kv* c, int layer, float* k, float* v) {
+  const orc_kv_layer* y = &c->L[layer - c->lo];
+  memcpy(k, y->k, sizeof(float) * (size_t)y->n * y->kv_dim);
+  memcpy(v, y->v, sizeof(float) * (size_t)y->n * y->kv_dim);
+}
+
+/* infer.js:114-221, Llama block.  kvl == NULL is the full-window path. */
+static int layer_forward(orc_model* m, int li, float* x, int T, orc_kv_layer* kvl, int pos0) {
+  orc_layer* y = &m->L[li];
+  int rc = ORC_OK;
+  if (!m->per_call_quant && (rc = layer_quantize(m, y))) return rc;
+  const int C = m->hidden, hd = m->head_dim, nH = m->heads, nKV = m->kv_heads;
+  const int qDim = nH * hd, kvDim = nKV * hd, I = m->inter;
+  float* h1 = (float*)malloc(sizeof(float) * (size_t)T * C);
+  float* q = (float*)malloc(sizeof(float) * (size_t)T * qDim);
+  float* k = (float*)malloc(sizeof(float) * (size_t)T * kvDim);
+  float* v = (float*)malloc(sizeof(float) * (size_t)T * kvDim);
+  float* ctxOut = (float*)calloc((size_t)T * qDim, sizeof(float));
+  float* x2 = (float*)malloc(sizeof(float) * (size_t)T * C);
+  float* g = (float*)malloc(sizeof(float) * (size_t)T * I);
+  float* u = (float*)malloc(sizeof(float) * (size_t)T * I);
+  float* tmpC = (float*)malloc(sizeof(float) * (size_t)T * C);
+  float *qh = NULL, *khT = NULL, *vh = NULL, *scores = NULL, *a = NULL, *oh = NULL;
+  if (!h1 || !q || !k || !v || !ctxOut || !x2 || !g || !u || !tmpC) { rc = ORC_E_NOMEM; goto done; }
+
+  orc_rmsnorm(x, T, C, y->nrm1, m->eps, h1);
+  if ((rc = proj(m, h1, T, y->Wq, &y->q, C, qDim, q))) goto done;
+  if ((rc = proj(m, h1, T, y->Wk, &y->k, C, kvDim, k))) goto done;
+  if ((rc = proj(m, h1, T, y->Wv, &y->v, C, kvDim, v))) goto done;
+  if ((rc = rope_ensure(m, pos0 + T + 1))) goto done;
+  orc_apply_rope(q, T, nH, hd, m->rope_cos, m->rope_sin, pos0);
+  orc_apply_rope(k, T, nKV, hd, m->rope_cos, m->rope_sin, pos0);
+
+  int n0 = 0, N = T;
+  const float *K = k, *Vv = v;
+  if (kvl) {
+    n0 = kvl->n;
+    N = n0 + T;
+    if (N > kvl->max_pos) { rc = ORC_E_INVAL; goto done; }
+    memcpy(kvl->k + (int64_t)n0 * kvDim, k, sizeof(float) * (size_t)T * kvDim);
+    memcpy(kvl->v + (int64_t)n0 * kvDim, v, sizeof(float) * (size_t)T * kvDim);
+    kvl->n = N;
+    K = kvl->k;
+    Vv = kvl->v;
+  }
+  const int group = nH / nKV;
+  const double scale = 1.0 / sqrt((double)hd);
+  qh = (float*)malloc(sizeof(float) * (size_t)T * hd);
+  khT = (float*)malloc(sizeof(float) * (size_t)hd * N);
+  vh = (float*)malloc(sizeof(float) * (size_t)N * hd);
+  scores = (float*)malloc(sizeof(float) * (size_t)T * N);
+  a = (float*)malloc(sizeof(float) * (size_t)T * N);
+  oh = (float*)malloc(sizeof(float) * (size_t)T * hd);
+  if (!qh || !khT || !vh || !scores || !a || !oh) { rc = ORC_E_NOMEM; goto done; }
+  for (int h = 0; h < nH; h++) {
+    int kvh = h / group;
+    for (int t = 0; t < T; t++) memcpy(qh + (int64_t)t * hd, q + (int64_t)t * qDim + h * hd, sizeof(float) * hd);
+    for (int t = 0; t < N; t++)
+      for (int c = 0; c < hd; c++) {
+        khT[(int64_t)c * N + t] = K[(int64_t)t * kvDim + kvh * hd + c];
+        vh[(int64_t)t * hd + c] = Vv[(int64_t)t * kvDim + kvh * hd + c];
+      }
+    if ((rc = orc_vgemm(qh, khT, T, hd, N, scores))) goto done;
+    orc_softmax_causal(scores, T, N, n0, scale, a);
+    if ((rc = orc_vgemm(a, vh, T, N, hd, oh))) goto done;
+    for (int t = 0; t < T; t++) memcpy(ctxOut + (int64_t)t * qDim + h * hd, oh + (int64_t)t * hd, sizeof(float) * hd);
+  }
+  if ((rc = proj(m, ctxOut, T, y->Wo, &y->o, qDim, C, tmpC))) goto done;
+  for (int64_t i = 0; i < (int64_t)T * C; i++) x2[i] = x[i] + tmpC[i];
+  orc_rmsnorm(x2, T, C, y->nrm2, m->eps, h1);
+  if ((rc = proj(m, h1, T, y->Wgate, &y->gate, C, I, g))) goto done;
+  if ((rc = proj(m, h1, T, y->Wup, &y->up, C, I, u))) goto done;
+  orc_swiglu(g, u, (int64_t)T * I, g);
+  if ((rc = proj(m, g, T, y->Wdown, &y->down, I, C, tmpC))) goto done;
+  for (int64_t i = 0; i < (int64_t)T * C; i++) x[i] = x2[i] + tmpC[i];
+done:
+  free(h1); free(q); free(k); free(v); free(ctxOut); free(x2); free(g); free(u); free(tmpC);
+  free(qh); free(khT); free(vh); free(scores); free(a); free(oh);
+  return rc;
+}
+
+/* runLayers / runLayersChunk (infer.js:275-296): layers [lo, hi) in place on x
+ * (T x hidden).  kv == NULL runs the full-window path. */
+int orc_run_layers(orc_model* m, int lo, int hi, float* x, int T, orc_kv* kv, int pos0) {
+  if (lo < 0 || hi > m->layers || hi < lo || T < 1) return ORC_E_INVAL;
+  if (orc_first_nonfinite(x, (int64_t)T * m->hidden) >= 0) return ORC_E_NONFINITE;
+  for (int l = lo; l < hi; l++) {
+    orc_kv_layer* kvl = NULL;
+    if (kv) {
+      if (l < kv->lo || l >= kv->hi) return ORC_E_INVAL;
+      kvl = &kv->L[l - kv->lo];
+    }
+    int rc = layer_forward(m, l, x, T, kvl, pos0);
+    if (rc) return rc;
+  }
+  if (orc_first_nonfinite(x, (int64_t)T * m->hidden) >= 0) return ORC_E_NONFINITE;
+  return ORC_OK;
+}
+
+/* embedRows (infer.js:298-310), Llama family (no learned positions). */
+void orc_embed_rows(const orc_model* m, const int32_t* ids, int T, float* x) {
+  for (int i = 0; i < T; i++)
+    memcpy(x + (int64_t)i * m->hidden, m->emb + (int64_t)ids[i] * m->hidden, sizeof(float) * m->hidden);
+}
+
+/* logitsAt (infer.js:324-334): final RMSNorm over all T rows, then one M=1
+ * verified GEMM per requested row against lm_head. */
+int orc_logits_rows(orc_model* m, const float* x, int T, const int32_t* rows, int nrows, float* out) {
+  int C = m->hidden, V = m->vocab;
+  if (!m->lm_kn) return ORC_E_INVAL;
+  if (!m->per_call_quant && !m->lm_quantized) {
+    if (wq_build(&m->lm, m->lm_kn, C, V)) return ORC_E_NONFINITE;
+    m->lm_quantized = 1;
+  }
+  float* y = (float*)malloc(sizeof(float) * (size_t)T * C);
+  if (!y) return ORC_E_NOMEM;
+  orc_rmsnorm(x, T, C, m->nrmF, m->eps, y);
+  int rc = ORC_OK;
+  for (int r = 0; r < nrows && rc == ORC_OK; r++) {
+    if (rows[r] < 0 || rows[r] >= T) { rc = ORC_E_INVAL; break; }
+    rc = proj(m, y + (int64_t)rows[r] * C, 1, m->lm_kn, &m->lm, C, V, out + (int64_t)r * V);
+  }
+  free(y);
+  return rc;
+}
+
+/* pickToken greedy (infer.js:393-395): strict '>' so the first maximum wins. */
+int orc_argmax(const float* logits, int n) {
+  int best = 0;
+  float bv = -INFINITY;
+  for (int j = 0; j < n; j++)
+    if (logits[j] > bv) { bv = logits[j]; best = j; }
+  return best;
+}
+
+/* ---- hashes, probes and fixtures ------------------------------------------ */
+/* shard.js:195-200 */
+uint32_t orc_fnv1a(const uint8_t* b, int64_t n) {
+  uint32_t h = 0x811c9dc5u;
+  for (int64_t i = 0; i < n; i++) { h ^= b[i]; h *= 0x01000193u; }
+  return h;
+}
+
+/* webgpu.js:998-1009: LCG seeded 0x5EED, m=24 k=96 n=24 batch=2, rs = cs = 1. */
+void orc_probe_inputs(int8_t* Xq, int8_t* Wq) {
+  uint32_t seed = 0x5EED;
+  const int nx = 2 * 24 * 96, nw = 2 * 96 * 24;
+  for (int i = 0; i < nx + nw; i++) {
+    seed = (seed * 1103515245u + 12345u) & 0x7fffffffu;
+    double r = (double)seed / (double)0x7fffffff;
+    int8_t v = (int8_t)js_round(r * 254.0 - 127.0);
+    if (i < nx) Xq[i] = v; else Wq[i - nx] = v;
+  }
+}
+
+/* test_pipeline.js:32-37: mulberry32(seed), o[i] = f32((r*2 - 1) * scale). */
+void orc_mulberry_fill(uint32_t seed, int64_t n, double scale, float* out) {
+  uint32_t a = seed;
+  for (int64_t i = 0; i < n; i++) {
+    a = a + 0x6D2B79F5u;
+    uint32_t t = (a ^ (a >> 15)) * (1u | a);
+    t = (t + ((t ^ (t >> 7)) * (61u | t))) ^ t;
+    double r = (double)(t ^ (t >> 14)) / 4294967296.0;
+    out[i] = (float)((r * 2.0 - 1.0) * scale);
+  }
+}
+
+/* Synthetic random-init weights for the benchmark-size models.  Counter based,
+ * so any element can be produced independently (the CUDA model builder uses
+ * the same formula): four splitmix64 outputs are summed as 32-bit integers
+ * (Irwin-Hall, an approximately normal variable), centred exactly in int64
+ * and scaled once in double, then rounded to f32.  Every step is exact or
+ * correctly rounded, so CPU and GPU agree bit for bit. */
+static uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+void orc_synth_fill(uint64_t seed, int64_t start, int64_t n, double factor, float* out) {
+  for (int64_t i = 0; i < n; i++) {
+    uint64_t base = (seed * 0x9E3779B97F4A7C15ULL) + (uint64_t)(start + i) * 4u;
+    int64_t s = 0;
+    for (int j = 0; j < 4; j++) s += (int64_t)(mix64(base + (uint64_t)j) >> 32);
+    s -= (int64_t)2 * 4294967295LL;
+    out[i] = (float)((double)s * factor);
+  }
+}

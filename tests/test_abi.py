@@ -1,0 +1,36 @@
+"""The C ABI: the library loads without a GPU and exports every declared entry point."""
+import ctypes
+import os
+import re
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for fn in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if fn.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names += re.findall(r"\b(dc_\w+)\s*\(", src)
+    return sorted(set(names))
+
+
+def test_every_declared_symbol_is_exported(P):
+    from importlib import import_module
+    lib = ctypes.CDLL(P._lib.LIB_PATH)
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol(P):
+    bound = {n for n, _, _ in P._lib.SIGNATURES}
+    assert set(declared_functions()) <= bound
+
+
+def test_library_is_built_for_sm100a(P):
+    # nvcc embeds the target architecture in the fatbin section name table.
+    data = open(P._lib.LIB_PATH, "rb").read()
+    assert b"sm_100a" in data
