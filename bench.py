@@ -61,14 +61,27 @@ class Clocks:
         self.path = None
 
     def start(self):
+        """Start sampling and wait (up to 10 s) for the first sample, so the
+        timed region that follows is covered."""
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 10 and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
+        self.t_start = time.time()
+
+    def mark_end(self):
+        """Keep sampling until at least 0.3 s passed since the timed region began."""
+        if self.proc is not None:
+            while time.time() - self.t_start < 0.3:
+                time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -210,6 +223,7 @@ def bench_gemm_sweep(args, rank, world, peaks):
         launches += run_sweep_step(comp, data, args.warmup + s, evs, dom)
     t1.record()
     torch.cuda.synchronize()
+    clocks.mark_end()
     barrier(world)
     clk = clocks.stop()
     comp.sync()
@@ -374,7 +388,7 @@ def traffic_for(key):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="gemm-sweep", choices=["gemm-sweep"])

@@ -70,7 +70,25 @@ SIGNATURES = [
     ("dc_weight_info", _i, [_p, C.POINTER(_p), C.POINTER(_i), C.POINTER(_p), C.POINTER(_i), C.POINTER(_i)]),
     ("dc_vgemm", _i, [_p, _p, _i, _p, _u, _p]),
     ("dc_kernel_probe", _i, [_p, C.POINTER(_u32)]),
+    ("dc_stage_create", _i, [_p, _p, _i, _i, _i, _i, _i, C.POINTER(_p)]),
+    ("dc_stage_free", None, [_p]),
+    ("dc_stage_set_layer", _i, [_p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    ("dc_stage_set_head", _i, [_p, _p, _p, _p]),
+    ("dc_stage_synth", _i, [_p, _u64, _d]),
+    ("dc_stage_embed", _i, [_p, _p, _i, _p]),
+    ("dc_stage_forward", _i, [_p, _p, _i, _i, _i]),
+    ("dc_stage_logits", _i, [_p, _p, _i, _p, _i, _p, _p]),
+    ("dc_stage_kv_reset", _i, [_p]),
+    ("dc_stage_kv_len", _i, [_p]),
+    ("dc_stage_kv_read", _i, [_p, _i, _p, _p, _p]),
 ]
+
+
+class DcSpec(C.Structure):
+    """dc_spec of include/dcinfer.h."""
+    _fields_ = [("hidden", C.c_int), ("layers", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("inter", C.c_int), ("vocab", C.c_int), ("norm_eps", C.c_double),
+                ("rope_theta", C.c_double), ("tie", C.c_int)]
 
 
 def load(path: str | None = None):

@@ -69,7 +69,8 @@ class Compute:
     def set_stream(self, stream) -> None:
         """Launch on an existing stream (a torch.cuda.Stream or a raw handle)."""
         handle = getattr(stream, "cuda_stream", stream)
-        self._check(self.L.dc_set_stream(self.h, C.c_void_p(handle) if handle else None), "dc_set_stream")
+        # torch reports the legacy default stream as handle 0; CUDA names it cudaStreamLegacy (0x1)
+        self._check(self.L.dc_set_stream(self.h, C.c_void_p(handle if handle else 1)), "dc_set_stream")
 
     def sync(self) -> None:
         self._check(self.L.dc_sync(self.h), "dc_sync")

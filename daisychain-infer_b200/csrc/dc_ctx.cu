@@ -309,6 +309,8 @@ extern "C" void dc_destroy(dc_ctx* c) {
   cudaFree(c->d_relu);
   cudaFree(c->d_status);
   cudaFree(c->scratch);
+  cudaFree(c->tc_partial);
+  cudaFree(c->tc_counters);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
 }

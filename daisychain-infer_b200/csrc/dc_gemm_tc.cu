@@ -1,7 +1,428 @@
-// dc_gemm_tc.cu -- tcgen05 tensor-core path (placeholder until the kernel lands).
+// dc_gemm_tc.cu -- tcgen05 tensor-core path of the verified W8A8 GEMM (sm_100a).
+//
+// out[bz, i, j] = epilogue( sum_p X[bz, i, p] * Wt[bz, j, p] )
+//
+// Swap-AB: the MMA's 128-row "M" side is 128 weight rows (= 128 output
+// columns j), its "N" side is BN activation rows i (BN in {16..256}), so the
+// small-M shapes of chunked prefill (M = 16) and lookahead waste no tensor
+// work on padding rows of the weight.  Operands are K-major int8 tiles of
+// 128 bytes of K, brought into shared memory by TMA with the 128-byte swizzle
+// (no multicast), consumed by tcgen05.mma.cta_group::1.kind::i8 with int32
+// accumulators in TMEM; the epilogue reads TMEM with tcgen05.ld and applies
+// the verified epilogue f32(f32(f32(acc)*rs[i])*cs[j]) / ReLU / requant LUT
+// (public/verified_core.js:227-228, 241-266).
+//
+// Roles (128 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues MMAs,
+// warp 1 owns the TMEM allocation, all four warps run the epilogue (warp w
+// reads TMEM lanes 32w..32w+31).  A STAGES-deep ring of full/empty mbarriers
+// pipelines the loads against the MMAs.
+//
+// Split-K: when the output tiles do not fill the GPU, K is split across CTAs.
+// Each split adds its int32 partial sums into a zeroed int32 scratch buffer
+// with atomicAdd (integer addition is exact in any order); the last split to
+// finish a tile (an atomic tile counter) applies the epilogue and resets the
+// scratch and the counter to zero for the next call.
+//
+// Every wait on an mbarrier is bounded (%globaltimer, 2 s); a wait that gives
+// up sets DC_ST_TIMEOUT in the context status word and the CTA winds down.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "dc_internal.cuh"
 
-int dc_gemm_tc(dc_ctx* ctx, const int8_t*, int, const int8_t*, int, const float*, const float*, int, int, int, int,
-               unsigned, void*, cudaStream_t) {
-  return dc_fail(ctx, DC_E_INVAL, "tcgen05 path not built");
+namespace {
+
+constexpr int TILE_N = 128;   // weight rows (output columns) per CTA = MMA M
+constexpr int TILE_K = 128;   // bytes of K per stage = one 128B swizzle row
+constexpr int MMA_K = 32;     // K per tcgen05.mma of kind::i8
+constexpr uint64_t WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  while (!mbar_try(bar, parity)) {
+    if (gtimer() - t0 > WAIT_NS) {
+      atomicOr(status, DC_ST_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// UMMA shared-memory descriptor: K-major, 128B swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t umma_desc(const void* p) {
+  uint64_t d = (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;           // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32; // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;           // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;           // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor of kind::i8: s8 x s8 -> s32, both K-major, M = 128, N = BN.
+template <int BN>
+__device__ __forceinline__ uint32_t idesc_i8() {
+  return (2u << 4)                       // D format: s32
+         | (1u << 7) | (1u << 10)         // A, B: signed 8-bit
+         | ((uint32_t)(BN >> 3) << 17)    // N >> 3
+         | ((uint32_t)(TILE_N >> 4) << 24);  // M >> 4
+}
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN>
+struct TcCfg {
+  static constexpr int STAGES = BN <= 32 ? 8 : (BN <= 64 ? 7 : (BN <= 128 ? 5 : 4));
+  static constexpr int A_BYTES = TILE_N * TILE_K;
+  static constexpr int B_BYTES = BN * TILE_K;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct TcArgs {
+  const float* rs;
+  const float* cs;
+  int m, k, n;
+  int kb_total, kb_per_split, splits, m_tiles, n_tiles;
+  unsigned flags;
+  const int8_t* requant;
+  const int8_t* relu;
+  void* out;
+  int32_t* partial;   // split-K int32 scratch (zero between calls), or null
+  int* counters;      // split-K tile counters (zero between calls), or null
+  int* status;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(128, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
+  using C = TcCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accum = empty + C::STAGES;
+  uint32_t* tmem_slot = (uint32_t*)(accum + 1);
+  int* flag = (int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_n = blockIdx.x, tile_m = blockIdx.y;
+  const int bz = blockIdx.z / a.splits, split = blockIdx.z - bz * a.splits;
+  const int j0 = tile_n * TILE_N, i0 = tile_m * BN;
+  const int kb0 = split * a.kb_per_split;
+  const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    *flag = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer
+    int issued = 0;
+    bool ok = true;
+    for (int it = 0; it < nkb && ok; it++) {
+      const int s = it % C::STAGES;
+      const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+      if (it >= C::STAGES) ok = mbar_wait(&empty[s], ph ^ 1u, a.status);
+      if (!ok) break;
+      mbar_expect_tx(&full[s], C::STAGE_BYTES);
+      const int kx = (kb0 + it) * TILE_K;
+      tma_load_2d(sA + s * C::A_BYTES, &tmW, kx, bz * a.n + j0, &full[s]);
+      tma_load_2d(sB + s * C::B_BYTES, &tmX, kx, bz * a.m + i0, &full[s]);
+      issued++;
+    }
+    if (!ok) {
+      // wind down: let every issued load land before the CTA's memory goes away
+      atomicExch(flag, 1);
+      for (int it = max(0, issued - C::STAGES); it < issued; it++)
+        mbar_wait(&full[it % C::STAGES], (uint32_t)(it / C::STAGES) & 1u, a.status);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer
+    const uint32_t idesc = idesc_i8<BN>();
+    for (int it = 0; it < nkb; it++) {
+      const int s = it % C::STAGES;
+      const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+      if (!mbar_wait(&full[s], ph, a.status)) { atomicExch(flag, 1); break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint8_t* ta = sA + s * C::A_BYTES;
+      const uint8_t* tb = sB + s * C::B_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < TILE_K / MMA_K; kk++)
+        mma_i8(tmem, umma_desc(ta + kk * MMA_K), umma_desc(tb + kk * MMA_K), idesc, (it > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&empty[s]);  // the slot is free once these MMAs have read it
+    }
+    mma_commit(accum);  // all MMAs issued by this thread are complete
+  }
+  __syncwarp();
+
+  // ---- epilogue (all four warps)
+  const bool have = mbar_wait(accum, 0, a.status);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const bool good = have && (*(volatile int*)flag == 0) && nkb > 0;
+  const int j = j0 + warp * 32 + lane;
+  const bool jv = j < a.n;
+  const float csv = jv ? a.cs[bz * a.n + j] : 0.0f;
+  if (a.splits == 1) {
+    if (good) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+#pragma unroll
+        for (int c = 0; c < 16; c++) {
+          const int i = i0 + c0 + c;
+          if (jv && i < a.m)
+            dc_store_out(a.out, ((int64_t)bz * a.m + i) * a.n + j, (int32_t)r[c], a.rs[bz * a.m + i], csv, a.flags,
+                         a.requant, a.relu);
+        }
+      }
+    }
+  } else {
+    if (good) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+#pragma unroll
+        for (int c = 0; c < 16; c++) {
+          const int i = i0 + c0 + c;
+          if (jv && i < a.m) atomicAdd(a.partial + ((int64_t)bz * a.m + i) * a.n + j, (int32_t)r[c]);
+        }
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int last;
+    const int tile = (bz * a.m_tiles + tile_m) * a.n_tiles + tile_n;
+    if (threadIdx.x == 0) last = (atomicAdd(a.counters + tile, 1) == a.splits - 1);
+    __syncthreads();
+    if (last) {
+      __threadfence();
+      if (jv) {
+        for (int c = 0; c < BN; c++) {
+          const int i = i0 + c;
+          if (i >= a.m) break;
+          int32_t* p = a.partial + ((int64_t)bz * a.m + i) * a.n + j;
+          const int32_t v = __ldcg(p);
+          dc_store_out(a.out, ((int64_t)bz * a.m + i) * a.n + j, v, a.rs[bz * a.m + i], csv, a.flags, a.requant,
+                       a.relu);
+          *p = 0;
+        }
+      }
+      if (threadIdx.x == 0) a.counters[tile] = 0;
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// 2-D int8 map over `rows` rows of `ld` bytes, box = 128 bytes x box_rows, 128B swizzle.
+bool make_map(CUtensorMap* map, const void* base, int ld, long rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {(cuuint32_t)TILE_K, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN>
+int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+              int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st, int32_t* partial,
+              int* counters, size_t partial_cap, size_t counter_cap) {
+  using C = TcCfg<BN>;
+  CUtensorMap mW, mX;
+  if (!make_map(&mW, Wt, ldw, (long)batch * n, TILE_N) || !make_map(&mX, Xq, ldx, (long)batch * m, BN))
+    return dc_fail(ctx, DC_E_INVAL, "tcgen05: tensor map encode failed");
+  TcArgs a;
+  a.rs = rs;
+  a.cs = cs;
+  a.m = m;
+  a.k = k;
+  a.n = n;
+  a.kb_total = (k + TILE_K - 1) / TILE_K;
+  a.n_tiles = (n + TILE_N - 1) / TILE_N;
+  a.m_tiles = (m + BN - 1) / BN;
+  const int tiles = a.n_tiles * a.m_tiles * batch;
+  int splits = 1;
+  if (tiles < ctx->sm_count && a.kb_total > 1) {
+    splits = (ctx->sm_count + tiles - 1) / tiles;
+    if (splits > a.kb_total) splits = a.kb_total;
+  }
+  a.kb_per_split = (a.kb_total + splits - 1) / splits;
+  splits = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  if (splits > 1 && (!partial || (size_t)batch * m * n > partial_cap || (size_t)tiles > counter_cap)) {
+    splits = 1;
+    a.kb_per_split = a.kb_total;
+  }
+  a.splits = splits;
+  a.flags = flags;
+  a.requant = ctx->d_requant;
+  a.relu = ctx->d_relu;
+  a.out = out;
+  a.partial = partial;
+  a.counters = counters;
+  a.status = ctx->d_status;
+  DC_CUDA(ctx, cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+  dim3 grid(a.n_tiles, a.m_tiles, batch * splits);
+  k_gemm_tc<BN><<<grid, 128, C::SMEM, st>>>(mW, mX, a);
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+}  // namespace
+
+// Split-K scratch of a context: int32 partial sums and tile counters, both kept
+// at zero between calls by the kernel itself.
+static int tc_scratch(dc_ctx* ctx, size_t partial_elems, size_t counters, int32_t** p, int** c) {
+  if (partial_elems > ctx->tc_partial_cap || counters > ctx->tc_counter_cap) {
+    DC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(ctx->tc_partial);
+    cudaFree(ctx->tc_counters);
+    ctx->tc_partial = nullptr;
+    ctx->tc_counters = nullptr;
+    ctx->tc_partial_cap = ctx->tc_counter_cap = 0;
+    size_t pe = partial_elems > (1u << 20) ? partial_elems : (1u << 20);
+    size_t ce = counters > 4096 ? counters : 4096;
+    if (cudaMalloc(&ctx->tc_partial, pe * 4) != cudaSuccess || cudaMalloc(&ctx->tc_counters, ce * 4) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(ctx, DC_E_NOMEM, "split-K scratch allocation failed");
+    }
+    DC_CUDA(ctx, cudaMemset(ctx->tc_partial, 0, pe * 4));
+    DC_CUDA(ctx, cudaMemset(ctx->tc_counters, 0, ce * 4));
+    ctx->tc_partial_cap = pe;
+    ctx->tc_counter_cap = ce;
+  }
+  *p = ctx->tc_partial;
+  *c = ctx->tc_counters;
+  return DC_OK;
+}
+
+int dc_gemm_tc_with(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                    const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                    int32_t* partial, int* counters, size_t partial_cap, size_t counter_cap) {
+  if (((uintptr_t)Xq & 15) || ((uintptr_t)Wt & 15) || (ldx & 15) || (ldw & 15) || k <= 0 || m <= 0 || n <= 0)
+    return dc_fail(ctx, DC_E_INVAL, "tcgen05: operands must be 16-byte aligned with ld a multiple of 16");
+  if (m <= 16)
+    return launch_tc<16>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
+                         partial_cap, counter_cap);
+  if (m <= 32)
+    return launch_tc<32>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
+                         partial_cap, counter_cap);
+  if (m <= 64)
+    return launch_tc<64>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
+                         partial_cap, counter_cap);
+  if (m <= 128)
+    return launch_tc<128>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
+                          partial_cap, counter_cap);
+  return launch_tc<256>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
+                        partial_cap, counter_cap);
+}
+
+int dc_gemm_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+               int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st) {
+  int32_t* partial = nullptr;
+  int* counters = nullptr;
+  // worst case over the BN choices: tiles = ceil(n/128) * ceil(m/16) * batch
+  size_t tiles = (size_t)((n + 127) / 128) * ((m + 15) / 16) * batch;
+  int rc = tc_scratch(ctx, (size_t)batch * m * n, tiles, &partial, &counters);
+  if (rc) return rc;
+  return dc_gemm_tc_with(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
+                         ctx->tc_partial_cap, ctx->tc_counter_cap);
 }

@@ -33,6 +33,10 @@ struct dc_ctx {
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   bool tc_enabled = true;  // tcgen05 GEMM passed its gate
+  // split-K scratch of the tcgen05 GEMM (kept zero between calls by the kernel)
+  int32_t* tc_partial = nullptr;
+  int* tc_counters = nullptr;
+  size_t tc_partial_cap = 0, tc_counter_cap = 0;
 };
 
 struct dc_weight {

@@ -1,0 +1,78 @@
+// dc_math.cuh -- double-precision exp for the verified elementwise steps.
+//
+// The reference computes softmax and SiLU with JavaScript's Math.exp
+// (public/infer.js:59, :192), which V8 implements by porting the fdlibm 5.3
+// method (Sun Microsystems, 1993).  This is an independent restatement of that
+// published method, written with explicitly rounded double operations so no
+// multiply-add contraction can change a bit:
+//   1. reduce x = k*ln2 + r, |r| <= ln2/2, with r carried as hi - lo;
+//   2. approximate R(r^2) = r*(e^r + 1)/(e^r - 1) by a degree-5 Remez
+//      polynomial in r^2 and rebuild e^r = 1 - ((lo - r*c/(2 - c)) - hi);
+//   3. scale by 2^k through the exponent field.
+// The coefficients are fdlibm's published Remez values (given as IEEE bit
+// patterns).  Its error is below 1 ulp; it is checked against the CPU
+// oracle's separate restatement and against CUDA's exp error bound.
+#pragma once
+#include <stdint.h>
+
+namespace dcm {
+
+__device__ __forceinline__ double b2d(uint64_t u) { return __longlong_as_double((long long)u); }
+
+__device__ inline double fdlibm_exp(double x) {
+  const double one = 1.0, huge = 1.0e+300;
+  const double twom1000 = b2d(0x0170000000000000ULL);
+  const double o_threshold = b2d(0x40862E42FEFA39EFULL);
+  const double u_threshold = b2d(0xC0874910D52D3051ULL);
+  const double ln2HI0 = b2d(0x3FE62E42FEE00000ULL);
+  const double ln2LO0 = b2d(0x3DEA39EF35793C76ULL);
+  const double invln2 = b2d(0x3FF71547652B82FEULL);
+  const double P1 = b2d(0x3FC555555555553EULL), P2 = b2d(0xBF66C16C16BEBD93ULL),
+               P3 = b2d(0x3F11566AAF25DE2CULL), P4 = b2d(0xBEBBBD41C5D26BF1ULL),
+               P5 = b2d(0x3E66376972BEA4D0ULL);
+  const uint64_t bx = (uint64_t)__double_as_longlong(x);
+  uint32_t hx = (uint32_t)(bx >> 32);
+  const int xsb = (int)((hx >> 31) & 1u);
+  hx &= 0x7fffffffu;
+  double hi = 0.0, lo = 0.0;
+  int k = 0;
+  if (hx >= 0x40862E42u) {
+    if (hx >= 0x7ff00000u) {
+      if (((hx & 0xfffffu) | (uint32_t)bx) != 0) return __dadd_rn(x, x);
+      return xsb == 0 ? x : 0.0;
+    }
+    if (x > o_threshold) return __dmul_rn(huge, huge);
+    if (x < u_threshold) return __dmul_rn(twom1000, twom1000);
+  }
+  if (hx > 0x3fd62e42u) {
+    if (hx < 0x3FF0A2B2u) {
+      const double l2h = xsb ? -ln2HI0 : ln2HI0;
+      hi = __dsub_rn(x, l2h);
+      lo = xsb ? -ln2LO0 : ln2LO0;
+      k = 1 - xsb - xsb;
+    } else {
+      k = (int)__dadd_rn(__dmul_rn(invln2, x), xsb ? -0.5 : 0.5);  // truncation toward zero, as (int) in C
+      const double t = (double)k;
+      hi = __dsub_rn(x, __dmul_rn(t, ln2HI0));
+      lo = __dmul_rn(t, ln2LO0);
+    }
+    x = __dsub_rn(hi, lo);
+  } else if (hx < 0x3e300000u) {
+    if (__dadd_rn(huge, x) > one) return __dadd_rn(one, x);
+  } else {
+    k = 0;
+  }
+  const double t = __dmul_rn(x, x);
+  double p = __dadd_rn(P4, __dmul_rn(t, P5));
+  p = __dadd_rn(P3, __dmul_rn(t, p));
+  p = __dadd_rn(P2, __dmul_rn(t, p));
+  p = __dadd_rn(P1, __dmul_rn(t, p));
+  const double c = __dsub_rn(x, __dmul_rn(t, p));
+  if (k == 0) return __dsub_rn(one, __dsub_rn(__ddiv_rn(__dmul_rn(x, c), __dsub_rn(c, 2.0)), x));
+  const double y = __dsub_rn(one, __dsub_rn(__dsub_rn(lo, __ddiv_rn(__dmul_rn(x, c), __dsub_rn(2.0, c))), hi));
+  const long long by = __double_as_longlong(y);
+  if (k >= -1021) return __longlong_as_double(by + (long long)k * 4503599627370496LL);
+  return __dmul_rn(__longlong_as_double(by + (long long)(k + 1000) * 4503599627370496LL), twom1000);
+}
+
+}  // namespace dcm

@@ -1,0 +1,884 @@
+// dc_stage.cu -- one pipeline stage of the verified forward pass, resident on one B200.
+//
+// Restates public/infer.js for the Llama family (RMSNorm, RoPE, GQA, SwiGLU):
+// layerForward :114-221, runLayers :275-283, runLayersChunk :288-296,
+// embedRows :298-310, logitsAt :324-334, greedy pickToken :390-396.  A stage
+// owns a contiguous layer range [lo, hi) (shard.js planStages :32-52); the
+// head stage also owns the embedding, the final norm and lm_head.
+//
+// Bit-exactness rules kept here (every f32/f64 step is an explicitly rounded
+// operation; the library is built with --fmad=false):
+//  * RMSNorm: s += v*v in double, sequentially from j = 0 (one thread walks
+//    the row), inv = 1/sqrt(s/C + eps), y = f32((x*inv)*w)           (:30-39)
+//  * every GEMM input is quantised per row (double scale) and every weight per
+//    column (f32 scale), as vgemmBlock does (verified_core.js:425-449); the
+//    weights are quantised once at load, which is bit-identical;
+//  * Q/K/V share the row quantisation of h1, so their weights are concatenated
+//    column-wise into one GEMM; gate/up likewise (exact: column scales are
+//    per column, row scales are shared);
+//  * RoPE: f32(a*c - b*s) with the products and the difference in double
+//    (:83-97); tables f = p / theta^(2i/hd) built on the host once;
+//  * attention per head (:171-197): scores = vgemm(q_h, k_hᵀ) with the row
+//    scale per (query token, head) and the column scale per (key token, kv
+//    head) -- stable as the cache grows, so int8 K and its scale are cached
+//    at append; causal softmax: mx = max(s*scale) in double, e = exp(s*scale -
+//    mx) (fdlibm method), a = f32(e), z += e sequentially in key order,
+//    a = f32(a / z); ctx = vgemm(a, v_h) with the row scale per query row and
+//    the column scale per (kv head, channel) over all N cached tokens -- the
+//    V cache stays f32 and its int8 copy is re-quantised whenever a channel's
+//    scale moves (the running absmax only grows, so unchanged channels keep
+//    their int8 values);
+//  * SwiGLU: f32(silu(g) * u) with silu(v) = v / (1 + exp(-v)) in double;
+//  * residuals: f32 adds.
+#include <math.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "dc_internal.cuh"
+#include "dc_math.cuh"
+
+struct dc_mat {
+  int k = 0, n = 0, ldk = 0;
+  int8_t* qt = nullptr;  // n x ldk, quantised Wᵀ (zero past k)
+  float* cs = nullptr;   // n column scales
+};
+
+struct dc_kv {
+  int8_t* k8 = nullptr;   // [kvh][max_pos][hd] int8 keys (rotated)
+  float* ks = nullptr;    // [kvh][max_pos] key scales (f32, quantizeCols rule)
+  float* v = nullptr;     // [max_pos][kvDim] f32 values
+  int8_t* v8 = nullptr;   // [kvh][max_pos][hd] int8 values under the current channel scales
+  float* vs = nullptr;    // [kvDim] channel scales
+  uint32_t* vmax = nullptr;  // [kvDim] running |v| maximum (float bits)
+  int* vchg = nullptr;    // [kvDim] channel scale changed on this step
+};
+
+struct dc_layer {
+  float* nrm1 = nullptr;
+  float* nrm2 = nullptr;
+  dc_mat qkv, o, gu, down;
+  dc_kv kv;
+};
+
+struct dc_stage {
+  dc_ctx* ctx = nullptr;
+  dc_spec spec;
+  int lo = 0, hi = 0, head = 0, max_rows = 0, max_pos = 0;
+  int C = 0, hd = 0, nH = 0, nKV = 0, qDim = 0, kvDim = 0, I = 0, V = 0, nqkv = 0;
+  int ldC = 0, ldQ = 0, ldI = 0;
+  std::vector<dc_layer> L;
+  float* emb = nullptr;  // V x C
+  float* nrmF = nullptr;
+  dc_mat lm;
+  float* rope_cos = nullptr;  // max_pos x hd/2
+  float* rope_sin = nullptr;
+  int kv_len = 0;  // tokens in the KV cache (chunk path)
+  // activation scratch
+  float* hbuf = nullptr;   // max_rows x max(nqkv, 2I, C)
+  float* ctxo = nullptr;   // max_rows x qDim
+  int8_t* xq = nullptr;    // max_rows x max(ldC, ldQ, ldI)
+  float* rs = nullptr;     // max_rows
+  float* lx = nullptr;     // logits rows x C gathered
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+constexpr int NORM_THREADS = 256;
+constexpr int ATT_THREADS = 128;
+
+__device__ __forceinline__ float block_max_f(float v, float* red) {
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float w = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    for (int o = 16; o; o >>= 1) w = fmaxf(w, __shfl_xor_sync(0xffffffffu, w, o));
+    if (threadIdx.x == 0) red[0] = w;
+  }
+  __syncthreads();
+  float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ double block_max_d(double v, double* red) {
+  for (int o = 16; o; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double w = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : -INFINITY;
+    for (int o = 16; o; o >>= 1) w = fmax(w, __shfl_xor_sync(0xffffffffu, w, o));
+    if (threadIdx.x == 0) red[0] = w;
+  }
+  __syncthreads();
+  double r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// max(mx/127, 1e-8) in double (verified_core.js:114, :128).
+__device__ __forceinline__ double quant_scale(float mx) {
+  double sc = __ddiv_rn((double)mx, 127.0);
+  return sc > 1e-8 ? sc : 1e-8;
+}
+
+// RMSNorm of one row fused with quantizeRows of its output.
+// x rows x C f32 -> q rows x ldq int8 (+ s[row]); the f32 norm output is not kept.
+__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __restrict__ x, int C,
+                                                               const float* __restrict__ w, double eps,
+                                                               int8_t* __restrict__ q, int ldq,
+                                                               float* __restrict__ s, int* status) {
+  extern __shared__ float ys[];  // C floats
+  __shared__ float red[32];
+  __shared__ double inv_s;
+  const int row = blockIdx.x;
+  const float* xr = x + (int64_t)row * C;
+  bool bad = false;
+  for (int j = threadIdx.x; j < C; j += blockDim.x) {
+    float v = xr[j];
+    bad |= !isfinite(v);
+    ys[j] = v;
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(status, DC_ST_NONFINITE);
+  if (threadIdx.x == 0) {
+    // the reference's order: s += v*v for j = 0 .. C-1, each step rounded
+    double acc = 0.0;
+    int j = 0;
+    for (; j + 4 <= C; j += 4) {
+      double v0 = ys[j], v1 = ys[j + 1], v2 = ys[j + 2], v3 = ys[j + 3];
+      double p0 = __dmul_rn(v0, v0), p1 = __dmul_rn(v1, v1), p2 = __dmul_rn(v2, v2), p3 = __dmul_rn(v3, v3);
+      acc = __dadd_rn(acc, p0);
+      acc = __dadd_rn(acc, p1);
+      acc = __dadd_rn(acc, p2);
+      acc = __dadd_rn(acc, p3);
+    }
+    for (; j < C; j++) {
+      double v = ys[j];
+      acc = __dadd_rn(acc, __dmul_rn(v, v));
+    }
+    inv_s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(acc, (double)C), eps)));
+  }
+  __syncthreads();
+  const double inv = inv_s;
+  float mx = 0.0f;
+  for (int j = threadIdx.x; j < C; j += blockDim.x) {
+    float y = __double2float_rn(__dmul_rn(__dmul_rn((double)ys[j], inv), (double)w[j]));
+    ys[j] = y;
+    mx = fmaxf(mx, fabsf(y));
+  }
+  mx = block_max_f(mx, red);
+  const double sc = quant_scale(mx);
+  if (threadIdx.x == 0) s[row] = __double2float_rn(sc);
+  int8_t* qr = q + (int64_t)row * ldq;
+  for (int j = threadIdx.x; j < ldq; j += blockDim.x)
+    qr[j] = j < C ? dc_clamp8(dc_js_round(__ddiv_rn((double)ys[j], sc))) : (int8_t)0;
+}
+
+// RoPE on the q and k parts of the fused QKV output row, quantisation of each
+// rotated key (per kv head, quantizeCols rule), append of keys and values to
+// the cache at row n0 + t, and the running per-channel |v| maximum.
+__global__ void __launch_bounds__(128) k_rope_append(float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
+                                                     const float* __restrict__ rc, const float* __restrict__ rsn,
+                                                     int pos0, int n0, int max_pos, int8_t* __restrict__ k8,
+                                                     float* __restrict__ ks, float* __restrict__ vcache,
+                                                     uint32_t* __restrict__ vmax, int* status) {
+  extern __shared__ float kr[];  // nKV * hd rotated keys
+  const int t = blockIdx.x;
+  const int p = pos0 + t;
+  const int half = hd >> 1, qDim = nH * hd, kvDim = nKV * hd;
+  float* row = h + (int64_t)t * nqkv;
+  for (int idx = threadIdx.x; idx < (nH + nKV) * half; idx += blockDim.x) {
+    const int hh = idx / half, i = idx - hh * half;
+    const double c = rc[(int64_t)p * half + i], s = rsn[(int64_t)p * half + i];
+    const bool isq = hh < nH;
+    float* o = isq ? row + hh * hd : row + qDim + (hh - nH) * hd;
+    const double a = o[i], b = o[half + i];
+    const float na = __double2float_rn(__dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s)));
+    const float nb = __double2float_rn(__dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s)));
+    if (isq) {
+      o[i] = na;
+      o[half + i] = nb;
+    } else {
+      kr[(hh - nH) * hd + i] = na;
+      kr[(hh - nH) * hd + half + i] = nb;
+    }
+  }
+  // values: copy and fold into the running channel maximum
+  bool bad = false;
+  for (int c = threadIdx.x; c < kvDim; c += blockDim.x) {
+    const float v = row[qDim + kvDim + c];
+    bad |= !isfinite(v);
+    vcache[(int64_t)(n0 + t) * kvDim + c] = v;
+    atomicMax(vmax + c, __float_as_uint(fabsf(v)));
+  }
+  __syncthreads();
+  // one warp per kv head: absmax over hd, f32 scale, int8 keys
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int g = warp; g < nKV; g += blockDim.x >> 5) {
+    float mx = 0.0f;
+    for (int c = lane; c < hd; c += 32) {
+      const float v = kr[g * hd + c];
+      bad |= !isfinite(v);
+      mx = fmaxf(mx, fabsf(v));
+    }
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float sc = __double2float_rn(quant_scale(mx));
+    const int64_t slot = (int64_t)g * max_pos + n0 + t;
+    if (lane == 0) ks[slot] = sc;
+    for (int c = lane; c < hd; c += 32)
+      k8[slot * hd + c] = dc_clamp8(dc_js_round(__ddiv_rn((double)kr[g * hd + c], (double)sc)));
+  }
+  if (bad) atomicOr(status, DC_ST_NONFINITE);
+}
+
+// Channel scales of V over all cached tokens; flags the channels whose scale moved.
+__global__ void k_vscale(const uint32_t* __restrict__ vmax, float* __restrict__ vs, int* __restrict__ vchg,
+                         int kvDim, int fresh) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= kvDim) return;
+  const float ns = __double2float_rn(quant_scale(__uint_as_float(vmax[c])));
+  vchg[c] = fresh || ns != vs[c];
+  vs[c] = ns;
+}
+
+// int8 V under the channel scales: rows >= n0 always, older rows only in
+// channels whose scale moved.  grid (ceil(N/64), kvDim/32), block 32 x 8.
+__global__ void __launch_bounds__(256) k_vquant(const float* __restrict__ vcache, const float* __restrict__ vs,
+                                                const int* __restrict__ vchg, int8_t* __restrict__ v8, int N, int n0,
+                                                int kvDim, int hd, int max_pos) {
+  const int c = blockIdx.y * 32 + (threadIdx.x & 31);
+  if (c >= kvDim) return;
+  const bool chg = vchg[c] != 0;
+  const double sc = (double)vs[c];
+  const int g = c / hd, cc = c - g * hd;
+  const int jb = blockIdx.x * 64;
+  for (int j = jb + (threadIdx.x >> 5); j < min(N, jb + 64); j += 8) {
+    if (j < n0 && !chg) continue;
+    v8[((int64_t)g * max_pos + j) * hd + cc] =
+        dc_clamp8(dc_js_round(__ddiv_rn((double)vcache[(int64_t)j * kvDim + c], sc)));
+  }
+}
+
+// One (query head, query row): scores, causal softmax, context.  N = n0 + T.
+__global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ h, int nqkv, int nH, int nKV,
+                                                           int hd, const int8_t* __restrict__ k8,
+                                                           const float* __restrict__ ks,
+                                                           const int8_t* __restrict__ v8,
+                                                           const float* __restrict__ vs, int N, int n0, int max_pos,
+                                                           double scale, float* __restrict__ out, int qDim,
+                                                           int* status) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  double* ed = (double*)sm;                 // N doubles: e_j
+  float* af = (float*)(ed + max_pos);       // N floats: scores, then a_j
+  int8_t* a8 = (int8_t*)(af + max_pos);     // N int8
+  __shared__ __align__(16) int8_t q8[256];
+  __shared__ float red[32];
+  __shared__ double redd[32];
+  __shared__ double zsum;
+  __shared__ int ctxacc[ATT_THREADS / 16][128];
+  const int hq = blockIdx.x, i = blockIdx.y;
+  const int group = nH / nKV, g = hq / group;
+  const int see = n0 + i;
+  // 1. quantise the query row of this head (row scale per (token, head), double)
+  const float* qrow = h + (int64_t)i * nqkv + hq * hd;
+  float mx = 0.0f;
+  bool bad = false;
+  for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+    float v = qrow[c];
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = block_max_f(mx, red);
+  const double qsc = quant_scale(mx);
+  const float qs = __double2float_rn(qsc);
+  for (int c = threadIdx.x; c < hd; c += blockDim.x) q8[c] = dc_clamp8(dc_js_round(__ddiv_rn((double)qrow[c], qsc)));
+  __syncthreads();
+  // 2. scores for keys 0..see: int32 dot over hd, verified epilogue
+  const int8_t* kb = k8 + (int64_t)g * max_pos * hd;
+  const float* ksg = ks + (int64_t)g * max_pos;
+  for (int j = threadIdx.x; j <= see; j += blockDim.x) {
+    const int* kj = (const int*)(kb + (int64_t)j * hd);
+    const int* qq = (const int*)q8;
+    int acc = 0;
+    for (int c = 0; c < hd / 4; c++) acc = __dp4a(kj[c], qq[c], acc);
+    af[j] = dc_epi(acc, qs, ksg[j]);
+  }
+  __syncthreads();
+  // 3. row maximum of s*scale (double, exact)
+  double m = -INFINITY;
+  for (int j = threadIdx.x; j <= see; j += blockDim.x) m = fmax(m, __dmul_rn((double)af[j], scale));
+  m = block_max_d(m, redd);
+  // 4. e_j and its f32 copy
+  for (int j = threadIdx.x; j <= see; j += blockDim.x) {
+    const double e = dcm::fdlibm_exp(__dsub_rn(__dmul_rn((double)af[j], scale), m));
+    ed[j] = e;
+    af[j] = __double2float_rn(e);
+  }
+  __syncthreads();
+  // 5. z = sum of e_j in key order (one thread: the reference's rounding sequence)
+  if (threadIdx.x == 0) {
+    double z = 0.0;
+    for (int j = 0; j <= see; j++) z = __dadd_rn(z, ed[j]);
+    zsum = z;
+  }
+  __syncthreads();
+  const double z = zsum;
+  // 6. a_j = f32(a_j / z); 7. quantise the probability row over all N columns
+  float amx = 0.0f;
+  for (int j = threadIdx.x; j <= see; j += blockDim.x) {
+    const float a = __double2float_rn(__ddiv_rn((double)af[j], z));
+    af[j] = a;
+    amx = fmaxf(amx, fabsf(a));
+  }
+  amx = block_max_f(amx, red);
+  const double asc = quant_scale(amx);
+  const float as = __double2float_rn(asc);
+  for (int j = threadIdx.x; j <= see; j += blockDim.x) a8[j] = dc_clamp8(dc_js_round(__ddiv_rn((double)af[j], asc)));
+  __syncthreads();
+  // 8. ctx[c] = sum_j a8[j] * v8[j][c] over j <= see (columns past `see` hold 0)
+  const int8_t* vb = v8 + (int64_t)g * max_pos * hd;
+  const int groups = blockDim.x / hd;  // ATT_THREADS / hd: 8 groups at hd 16 .. 1 at hd 128
+  const int c = threadIdx.x % hd, grp = threadIdx.x / hd;
+  if (grp < groups) {
+    int acc = 0;
+    for (int j = grp; j <= see; j += groups) acc += (int)a8[j] * (int)vb[(int64_t)j * hd + c];
+    ctxacc[grp][c] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x < hd) {
+    int acc = 0;
+    for (int gg = 0; gg < groups; gg++) acc += ctxacc[gg][threadIdx.x];
+    out[(int64_t)i * qDim + hq * hd + threadIdx.x] = dc_epi(acc, as, vs[g * hd + threadIdx.x]);
+  }
+  if (bad && threadIdx.x == 0) atomicOr(status, DC_ST_NONFINITE);
+}
+
+// SwiGLU of one row fused with quantizeRows of the product.
+__global__ void __launch_bounds__(NORM_THREADS) k_swiglu_quant(const float* __restrict__ h, int I,
+                                                              int8_t* __restrict__ q, int ldq,
+                                                              float* __restrict__ s, int* status) {
+  extern __shared__ float ys[];
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const float* g = h + (int64_t)row * 2 * I;
+  const float* u = g + I;
+  float mx = 0.0f;
+  bool bad = false;
+  for (int j = threadIdx.x; j < I; j += blockDim.x) {
+    const double v = g[j];
+    const double sl = __ddiv_rn(v, __dadd_rn(1.0, dcm::fdlibm_exp(-v)));
+    const float y = __double2float_rn(__dmul_rn(sl, (double)u[j]));
+    bad |= !isfinite(y);
+    ys[j] = y;
+    mx = fmaxf(mx, fabsf(y));
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(status, DC_ST_NONFINITE);
+  mx = block_max_f(mx, red);
+  const double sc = quant_scale(mx);
+  if (threadIdx.x == 0) s[row] = __double2float_rn(sc);
+  int8_t* qr = q + (int64_t)row * ldq;
+  for (int j = threadIdx.x; j < ldq; j += blockDim.x)
+    qr[j] = j < I ? dc_clamp8(dc_js_round(__ddiv_rn((double)ys[j], sc))) : (int8_t)0;
+}
+
+__global__ void k_add_inplace(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    x[i] = __fadd_rn(x[i], y[i]);
+}
+
+__global__ void k_embed(const int32_t* __restrict__ ids, int T, const float* __restrict__ emb, int C, int V,
+                        float* __restrict__ x, int* status) {
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) atomicOr(status, DC_ST_BOUNDS);
+    return;
+  }
+  for (int j = threadIdx.x; j < C; j += blockDim.x) x[(int64_t)t * C + j] = emb[(int64_t)id * C + j];
+}
+
+__global__ void k_gather_rows(const float* __restrict__ x, int C, const int32_t* __restrict__ rows, int nrows,
+                              float* __restrict__ y) {
+  const int r = blockIdx.x;
+  for (int j = threadIdx.x; j < C; j += blockDim.x) y[(int64_t)r * C + j] = x[(int64_t)rows[r] * C + j];
+}
+
+// Greedy pick per row (infer.js:393-395): the first index holding the maximum
+// ('>' in index order), i.e. the largest value and, among equal values
+// (-0 == +0), the smallest index.
+__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, int V, int32_t* __restrict__ out) {
+  const float* l = logits + (int64_t)blockIdx.x * V;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    const float v = l[j];
+    if (v > bv || (v == bv && j < bi)) { bv = v; bi = j; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = sv[0];
+    int ix = si[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+      if (sv[w] > b || (sv[w] == b && si[w] < ix)) { b = sv[w]; ix = si[w]; }
+    out[blockIdx.x] = ix == 0x7fffffff ? 0 : ix;
+  }
+}
+
+// ---- weight loading ----------------------------------------------------------
+// Element (r, c) of a k x n weight, from an f32 buffer or from the synthetic
+// random-init generator (counter based; the CPU oracle restates it).
+struct WSrc {
+  const float* W = nullptr;  // k x n f32 row-major, or null for synthetic
+  uint64_t seed = 0;
+  int64_t n = 0;             // columns of the source matrix
+  int transposed = 0;        // synthetic only: element (r, c) is index c * k + r (embᵀ)
+  int64_t k = 0;
+  double factor = 0.0;
+};
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float wsrc_at(const WSrc& s, int64_t r, int64_t c) {
+  if (s.W) return s.W[r * s.n + c];
+  const int64_t idx = s.transposed ? c * s.k + r : r * s.n + c;
+  const uint64_t base = s.seed * 0x9E3779B97F4A7C15ULL + (uint64_t)idx * 4u;
+  int64_t acc = 0;
+  for (int j = 0; j < 4; j++) acc += (int64_t)(mix64(base + (uint64_t)j) >> 32);
+  acc -= (int64_t)2 * 4294967295LL;
+  return __double2float_rn(__dmul_rn((double)acc, s.factor));
+}
+
+__global__ void __launch_bounds__(256) k_wscale(WSrc src, int k, int n, float* __restrict__ s, int* status) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  float mx = 0.0f;
+  bool bad = false;
+  for (int r = 0; r < k; r++) {
+    const float v = wsrc_at(src, r, c);
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+  }
+  if (bad) atomicOr(status, DC_ST_NONFINITE);
+  s[c] = __double2float_rn(quant_scale(mx));
+}
+
+__global__ void __launch_bounds__(256) k_wquant_t(WSrc src, int k, int n, const float* __restrict__ s,
+                                                  int8_t* __restrict__ qt, int ldq) {
+  __shared__ int8_t tile[32][33];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    int8_t v = 0;
+    if (r < k && c < n) v = dc_clamp8(dc_js_round(__ddiv_rn((double)wsrc_at(src, r, c), (double)s[c])));
+    tile[i][tx] = v;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + tx;
+    if (c < n && r < ldq) qt[(int64_t)c * ldq + r] = r < k ? tile[tx][i] : (int8_t)0;
+  }
+}
+
+__global__ void k_synth_f32(WSrc src, int64_t rows, int64_t cols, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * cols;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = wsrc_at(src, i / cols, i % cols);
+}
+
+__global__ void k_fill_f32(float* p, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+}  // namespace
+
+// ---- host side ------------------------------------------------------------------
+static int st_alloc(dc_stage* S, void** p, size_t bytes) {
+  if (cudaMalloc(p, bytes ? bytes : 16) != cudaSuccess) {
+    cudaGetLastError();
+    return dc_fail(S->ctx, DC_E_NOMEM, "stage: device allocation of %zu bytes failed", bytes);
+  }
+  S->allocs.push_back(*p);
+  return DC_OK;
+}
+#define ST_ALLOC(S, ptr, bytes)                               \
+  do {                                                        \
+    int _rc = st_alloc((S), (void**)&(ptr), (size_t)(bytes)); \
+    if (_rc) return _rc;                                      \
+  } while (0)
+
+static int mat_alloc(dc_stage* S, dc_mat& m, int k, int n) {
+  m.k = k;
+  m.n = n;
+  m.ldk = round_up(k, 16);
+  ST_ALLOC(S, m.qt, (size_t)n * m.ldk);
+  ST_ALLOC(S, m.cs, 4 * (size_t)n);
+  return DC_OK;
+}
+
+// Quantise one source matrix (k x n_src) into columns [col0, col0 + n_src) of m.
+static int mat_load(dc_stage* S, dc_mat& m, int col0, const WSrc& src, int n_src) {
+  cudaStream_t st = S->ctx->stream;
+  float* s = m.cs + col0;
+  int8_t* qt = m.qt + (int64_t)col0 * m.ldk;
+  k_wscale<<<(n_src + 255) / 256, 256, 0, st>>>(src, m.k, n_src, s, S->ctx->d_status);
+  DC_CUDA(S->ctx, cudaGetLastError());
+  dim3 grid((n_src + 31) / 32, (m.ldk + 31) / 32);
+  k_wquant_t<<<grid, 256, 0, st>>>(src, m.k, n_src, s, qt, m.ldk);
+  DC_CUDA(S->ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+static int upload(dc_stage* S, const float* h, size_t n, float** d) {
+  ST_ALLOC(S, *d, 4 * n);
+  DC_CUDA(S->ctx, cudaMemcpyAsync(*d, h, 4 * n, cudaMemcpyHostToDevice, S->ctx->stream));
+  return DC_OK;
+}
+
+extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi, int head, int max_rows,
+                               int max_pos, dc_stage** out) {
+  if (!ctx || !spec || !out) return DC_E_INVAL;
+  const dc_spec& s = *spec;
+  if (s.hidden <= 0 || s.heads <= 0 || s.kv_heads <= 0 || s.heads % s.kv_heads || s.head_dim <= 0 ||
+      (s.head_dim % 16) || s.head_dim > 128 || s.inter <= 0 || s.vocab <= 0 || lo < 0 || hi > s.layers || hi < lo ||
+      max_rows < 1 || max_pos < 1 || s.hidden > 16384 || s.inter > 32768)
+    return dc_fail(ctx, DC_E_INVAL, "stage: unsupported spec (head_dim must be a multiple of 16, at most 128)");
+  if (s.hidden > DC_MAX_INT32_K || s.inter > DC_MAX_INT32_K || s.heads * s.head_dim > DC_MAX_INT32_K ||
+      max_pos > DC_MAX_INT32_K)
+    return dc_fail(ctx, DC_E_ACCBOUND, "stage: a contraction would exceed %d", DC_MAX_INT32_K);
+  dc_stage* S = new dc_stage();
+  S->ctx = ctx;
+  S->spec = s;
+  S->lo = lo;
+  S->hi = hi;
+  S->head = head;
+  S->max_rows = max_rows;
+  S->max_pos = max_pos;
+  S->C = s.hidden;
+  S->hd = s.head_dim;
+  S->nH = s.heads;
+  S->nKV = s.kv_heads;
+  S->qDim = s.heads * s.head_dim;
+  S->kvDim = s.kv_heads * s.head_dim;
+  S->I = s.inter;
+  S->V = s.vocab;
+  S->nqkv = S->qDim + 2 * S->kvDim;
+  S->ldC = round_up(S->C, 16);
+  S->ldQ = round_up(S->qDim, 16);
+  S->ldI = round_up(S->I, 16);
+  int rc = DC_OK;
+  auto fail = [&](int r) {
+    dc_stage_free(S);
+    return r;
+  };
+  S->L.resize(hi - lo);
+  for (auto& ly : S->L) {
+    if ((rc = st_alloc(S, (void**)&ly.nrm1, 4 * (size_t)S->C)) || (rc = st_alloc(S, (void**)&ly.nrm2, 4 * (size_t)S->C)))
+      return fail(rc);
+    if ((rc = mat_alloc(S, ly.qkv, S->C, S->nqkv)) || (rc = mat_alloc(S, ly.o, S->qDim, S->C)) ||
+        (rc = mat_alloc(S, ly.gu, S->C, 2 * S->I)) || (rc = mat_alloc(S, ly.down, S->I, S->C)))
+      return fail(rc);
+    dc_kv& kv = ly.kv;
+    if ((rc = st_alloc(S, (void**)&kv.k8, (size_t)S->nKV * max_pos * S->hd)) ||
+        (rc = st_alloc(S, (void**)&kv.ks, 4 * (size_t)S->nKV * max_pos)) ||
+        (rc = st_alloc(S, (void**)&kv.v, 4 * (size_t)max_pos * S->kvDim)) ||
+        (rc = st_alloc(S, (void**)&kv.v8, (size_t)S->nKV * max_pos * S->hd)) ||
+        (rc = st_alloc(S, (void**)&kv.vs, 4 * (size_t)S->kvDim)) ||
+        (rc = st_alloc(S, (void**)&kv.vmax, 4 * (size_t)S->kvDim)) ||
+        (rc = st_alloc(S, (void**)&kv.vchg, 4 * (size_t)S->kvDim)))
+      return fail(rc);
+  }
+  if (head) {
+    if ((rc = st_alloc(S, (void**)&S->emb, 4 * (size_t)S->V * S->C)) ||
+        (rc = st_alloc(S, (void**)&S->nrmF, 4 * (size_t)S->C)) || (rc = mat_alloc(S, S->lm, S->C, S->V)))
+      return fail(rc);
+  }
+  const int wide = std::max(std::max(S->nqkv, 2 * S->I), S->C);
+  if ((rc = st_alloc(S, (void**)&S->hbuf, 4 * (size_t)max_rows * wide)) ||
+      (rc = st_alloc(S, (void**)&S->ctxo, 4 * (size_t)max_rows * S->qDim)) ||
+      (rc = st_alloc(S, (void**)&S->xq, (size_t)max_rows * std::max(std::max(S->ldC, S->ldQ), S->ldI))) ||
+      (rc = st_alloc(S, (void**)&S->rs, 4 * (size_t)max_rows)) ||
+      (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
+    return fail(rc);
+  // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1
+  const int half = S->hd / 2;
+  std::vector<float> c((size_t)max_pos * half), sn((size_t)max_pos * half);
+  for (int p = 0; p < max_pos; p++)
+    for (int i = 0; i < half; i++) {
+      const double f = (double)p / pow(s.rope_theta, (2.0 * i) / (double)S->hd);
+      c[(size_t)p * half + i] = (float)cos(f);
+      sn[(size_t)p * half + i] = (float)sin(f);
+    }
+  if ((rc = upload(S, c.data(), c.size(), &S->rope_cos)) || (rc = upload(S, sn.data(), sn.size(), &S->rope_sin)))
+    return fail(rc);
+  if ((rc = dc_stage_kv_reset(S)) || (rc = dc_sync(ctx))) return fail(rc);
+  *out = S;
+  return DC_OK;
+}
+
+extern "C" void dc_stage_free(dc_stage* S) {
+  if (!S) return;
+  if (S->ctx) cudaStreamSynchronize(S->ctx->stream);
+  for (void* p : S->allocs) cudaFree(p);
+  delete S;
+}
+
+static WSrc f32src(const float* dW, int k, int n) {
+  WSrc s;
+  s.W = dW;
+  s.n = n;
+  s.k = k;
+  return s;
+}
+
+// Upload one host k x n matrix and quantise it into columns [col0, col0+n) of m.
+static int load_host(dc_stage* S, dc_mat& m, int col0, const float* W, int k, int n, float* tmp) {
+  DC_CUDA(S->ctx, cudaMemcpyAsync(tmp, W, 4 * (size_t)k * n, cudaMemcpyHostToDevice, S->ctx->stream));
+  return mat_load(S, m, col0, f32src(tmp, k, n), n);
+}
+
+extern "C" int dc_stage_set_layer(dc_stage* S, int layer, const float* nrm1, const float* nrm2, const float* Wq,
+                                  const float* Wk, const float* Wv, const float* Wo, const float* Wgate,
+                                  const float* Wup, const float* Wdown) {
+  if (!S || layer < S->lo || layer >= S->hi || !nrm1 || !nrm2 || !Wq || !Wk || !Wv || !Wo || !Wgate || !Wup ||
+      !Wdown)
+    return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_set_layer: bad arguments");
+  dc_layer& ly = S->L[layer - S->lo];
+  dc_ctx* ctx = S->ctx;
+  float* tmp = nullptr;
+  const size_t big = std::max((size_t)S->C * std::max(S->qDim, S->I), (size_t)S->I * S->C);
+  if (cudaMalloc(&tmp, 4 * big) != cudaSuccess) {
+    cudaGetLastError();
+    return dc_fail(ctx, DC_E_NOMEM, "stage_set_layer: staging allocation failed");
+  }
+  int rc = DC_OK;
+  cudaError_t e = cudaMemcpyAsync(ly.nrm1, nrm1, 4 * (size_t)S->C, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ly.nrm2, nrm2, 4 * (size_t)S->C, cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) rc = dc_cuda_fail(ctx, e, "norm upload");
+  if (!rc) rc = load_host(S, ly.qkv, 0, Wq, S->C, S->qDim, tmp);
+  if (!rc) rc = dc_sync(ctx);
+  if (!rc) rc = load_host(S, ly.qkv, S->qDim, Wk, S->C, S->kvDim, tmp);
+  if (!rc) rc = dc_sync(ctx);
+  if (!rc) rc = load_host(S, ly.qkv, S->qDim + S->kvDim, Wv, S->C, S->kvDim, tmp);
+  if (!rc) rc = dc_sync(ctx);
+  if (!rc) rc = load_host(S, ly.o, 0, Wo, S->qDim, S->C, tmp);
+  if (!rc) rc = dc_sync(ctx);
+  if (!rc) rc = load_host(S, ly.gu, 0, Wgate, S->C, S->I, tmp);
+  if (!rc) rc = dc_sync(ctx);
+  if (!rc) rc = load_host(S, ly.gu, S->I, Wup, S->C, S->I, tmp);
+  if (!rc) rc = dc_sync(ctx);
+  if (!rc) rc = load_host(S, ly.down, 0, Wdown, S->I, S->C, tmp);
+  if (!rc) rc = dc_sync(ctx);
+  cudaFree(tmp);
+  return rc;
+}
+
+extern "C" int dc_stage_set_head(dc_stage* S, const float* emb, const float* nrmF, const float* lm_kn) {
+  if (!S || !S->head || !emb || !nrmF) return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_set_head: bad arguments");
+  dc_ctx* ctx = S->ctx;
+  DC_CUDA(ctx, cudaMemcpyAsync(S->emb, emb, 4 * (size_t)S->V * S->C, cudaMemcpyHostToDevice, ctx->stream));
+  DC_CUDA(ctx, cudaMemcpyAsync(S->nrmF, nrmF, 4 * (size_t)S->C, cudaMemcpyHostToDevice, ctx->stream));
+  int rc;
+  if (lm_kn) {
+    float* tmp = nullptr;
+    if (cudaMalloc(&tmp, 4 * (size_t)S->C * S->V) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(ctx, DC_E_NOMEM, "stage_set_head: staging allocation failed");
+    }
+    rc = load_host(S, S->lm, 0, lm_kn, S->C, S->V, tmp);
+    if (!rc) rc = dc_sync(ctx);
+    cudaFree(tmp);
+  } else {
+    // tied: lm_head = embᵀ (shard.js:92, 123-128): element (c, v) = emb[v][c]
+    float* tmp = nullptr;
+    if (cudaMalloc(&tmp, 4 * (size_t)S->C * S->V) != cudaSuccess) {
+      cudaGetLastError();
+      return dc_fail(ctx, DC_E_NOMEM, "stage_set_head: staging allocation failed");
+    }
+    std::vector<float> t((size_t)S->C * S->V);
+    for (int v = 0; v < S->V; v++)
+      for (int c = 0; c < S->C; c++) t[(size_t)c * S->V + v] = emb[(size_t)v * S->C + c];
+    rc = load_host(S, S->lm, 0, t.data(), S->C, S->V, tmp);
+    if (!rc) rc = dc_sync(ctx);
+    cudaFree(tmp);
+  }
+  return rc;
+}
+
+// Synthetic random-init weights, generated on the device from the counter-based
+// formula (norm weights 1).  Tensor seed = model_seed * 1000003 + (layer+1)*64 + role
+// with roles emb 1, lm 2, Wq 3, Wk 4, Wv 5, Wo 6, Wgate 7, Wup 8, Wdown 9.
+extern "C" int dc_stage_synth(dc_stage* S, uint64_t model_seed, double factor) {
+  if (!S) return DC_E_INVAL;
+  dc_ctx* ctx = S->ctx;
+  auto seed_of = [&](int layer, int role) { return model_seed * 1000003ull + (uint64_t)(layer + 1) * 64u + role; };
+  auto src = [&](int layer, int role, int k, int n) {
+    WSrc s;
+    s.seed = seed_of(layer, role);
+    s.n = n;
+    s.k = k;
+    s.factor = factor;
+    return s;
+  };
+  int rc = DC_OK;
+  for (int l = S->lo; l < S->hi && !rc; l++) {
+    dc_layer& ly = S->L[l - S->lo];
+    k_fill_f32<<<8, 256, 0, ctx->stream>>>(ly.nrm1, S->C, 1.0f);
+    k_fill_f32<<<8, 256, 0, ctx->stream>>>(ly.nrm2, S->C, 1.0f);
+    rc = mat_load(S, ly.qkv, 0, src(l, 3, S->C, S->qDim), S->qDim);
+    if (!rc) rc = mat_load(S, ly.qkv, S->qDim, src(l, 4, S->C, S->kvDim), S->kvDim);
+    if (!rc) rc = mat_load(S, ly.qkv, S->qDim + S->kvDim, src(l, 5, S->C, S->kvDim), S->kvDim);
+    if (!rc) rc = mat_load(S, ly.o, 0, src(l, 6, S->qDim, S->C), S->C);
+    if (!rc) rc = mat_load(S, ly.gu, 0, src(l, 7, S->C, S->I), S->I);
+    if (!rc) rc = mat_load(S, ly.gu, S->I, src(l, 8, S->C, S->I), S->I);
+    if (!rc) rc = mat_load(S, ly.down, 0, src(l, 9, S->I, S->C), S->C);
+  }
+  if (!rc && S->head) {
+    WSrc e = src(-1, 1, S->V, S->C);
+    k_synth_f32<<<1024, 256, 0, ctx->stream>>>(e, S->V, S->C, S->emb);
+    k_fill_f32<<<8, 256, 0, ctx->stream>>>(S->nrmF, S->C, 1.0f);
+    if (S->spec.tie) {
+      WSrc t = e;  // embᵀ: element (c, v) = emb index v*C + c
+      t.transposed = 1;
+      t.k = S->C;
+      t.n = S->V;
+      rc = mat_load(S, S->lm, 0, t, S->V);
+    } else {
+      rc = mat_load(S, S->lm, 0, src(-1, 2, S->C, S->V), S->V);
+    }
+  }
+  if (!rc) rc = dc_sync(ctx);
+  return rc;
+}
+
+extern "C" int dc_stage_kv_reset(dc_stage* S) {
+  if (!S) return DC_E_INVAL;
+  S->kv_len = 0;
+  for (auto& ly : S->L) DC_CUDA(S->ctx, cudaMemsetAsync(ly.kv.vmax, 0, 4 * (size_t)S->kvDim, S->ctx->stream));
+  return DC_OK;
+}
+
+extern "C" int dc_stage_kv_len(const dc_stage* S) { return S ? S->kv_len : -1; }
+
+extern "C" int dc_stage_embed(dc_stage* S, const int32_t* ids, int T, float* x) {
+  if (!S || !S->head || T < 1 || T > S->max_rows || !ids || !x)
+    return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_embed: bad arguments");
+  k_embed<<<T, 256, 0, S->ctx->stream>>>(ids, T, S->emb, S->C, S->V, x, S->ctx->d_status);
+  DC_CUDA(S->ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+static int gemm(dc_stage* S, const dc_mat& m, int T, const int8_t* xq, int ldx, float* out) {
+  return dc_gemm_dispatch(S->ctx, xq, ldx, m.qt, m.ldk, S->rs, m.cs, T, m.k, m.n, 1, 0, out, S->ctx->stream, 0);
+}
+
+// runLayers (use_kv = 0: full window, positions 0..T-1) or runLayersChunk
+// (use_kv = 1: positions pos0.., keys/values appended to this stage's cache).
+extern "C" int dc_stage_forward(dc_stage* S, float* x, int T, int pos0, int use_kv) {
+  if (!S || !x || T < 1 || T > S->max_rows) return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_forward: bad T");
+  dc_ctx* ctx = S->ctx;
+  cudaStream_t st = ctx->stream;
+  const int n0 = use_kv ? S->kv_len : 0;
+  const int N = n0 + T;
+  if (use_kv && pos0 != n0)
+    return dc_fail(ctx, DC_E_INVAL, "stage_forward: chunk position %d does not follow the cached %d tokens", pos0, n0);
+  if (N > S->max_pos || pos0 + T > S->max_pos)
+    return dc_fail(ctx, DC_E_INVAL, "stage_forward: %d positions exceed max_pos %d", N, S->max_pos);
+  const double scale = 1.0 / sqrt((double)S->hd);
+  const size_t att_smem = (size_t)S->max_pos * (8 + 4 + 1) + 64;
+  if (att_smem > 48 * 1024)
+    DC_CUDA(ctx, cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)att_smem));
+  const size_t swi_smem = 4 * (size_t)S->I;
+  if (swi_smem > 48 * 1024)
+    DC_CUDA(ctx, cudaFuncSetAttribute(k_swiglu_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)swi_smem));
+  const size_t nrm_smem = 4 * (size_t)S->C;
+  if (nrm_smem > 48 * 1024)
+    DC_CUDA(ctx, cudaFuncSetAttribute(k_rmsnorm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nrm_smem));
+  int rc;
+  for (auto& ly : S->L) {
+    dc_kv& kv = ly.kv;
+    // attention block
+    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm1, S->spec.norm_eps, S->xq, S->ldC, S->rs,
+                                                         ctx->d_status);
+    if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf))) return rc;
+    if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
+    k_rope_append<<<T, 128, 4 * (size_t)S->kvDim, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos,
+                                                          S->rope_sin, pos0, n0, S->max_pos, kv.k8, kv.ks, kv.v,
+                                                          kv.vmax, ctx->d_status);
+    k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0 == 0 ? 1 : 0);
+    dim3 vq((N + 63) / 64, (S->kvDim + 31) / 32);
+    k_vquant<<<vq, 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8, N, n0, S->kvDim, S->hd, S->max_pos);
+    dim3 ag(S->nH, T);
+    k_attention<<<ag, ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8, kv.vs,
+                                                   N, n0, S->max_pos, scale, S->ctxo, S->qDim, ctx->d_status);
+    if ((rc = dc_launch_quant_rows(ctx, S->ctxo, T, S->qDim, S->xq, S->ldQ, S->rs, st))) return rc;
+    if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, S->hbuf))) return rc;
+    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C);
+    // MLP block
+    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm2, S->spec.norm_eps, S->xq, S->ldC, S->rs,
+                                                         ctx->d_status);
+    if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf))) return rc;
+    k_swiglu_quant<<<T, NORM_THREADS, swi_smem, st>>>(S->hbuf, S->I, S->xq, S->ldI, S->rs, ctx->d_status);
+    if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, S->hbuf))) return rc;
+    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C);
+    DC_CUDA(ctx, cudaGetLastError());
+  }
+  if (use_kv) S->kv_len = N;
+  return DC_OK;
+}
+
+// logitsAt (infer.js:324-334): final RMSNorm of the requested rows, lm_head
+// GEMV (one row of M per requested row; rows are independent), greedy pick.
+extern "C" int dc_stage_logits(dc_stage* S, const float* x, int T, const int32_t* rows, int nrows, float* logits,
+                               int32_t* picks) {
+  if (!S || !S->head || !x || !rows || nrows < 1 || nrows > 8 || T < 1)
+    return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_logits: bad arguments");
+  dc_ctx* ctx = S->ctx;
+  cudaStream_t st = ctx->stream;
+  for (int r = 0; r < nrows; r++)
+    if (rows[r] < 0 || rows[r] >= T) return dc_fail(ctx, DC_E_INVAL, "readout row outside the window");
+  for (int r = 0; r < nrows; r++)
+    DC_CUDA(ctx, cudaMemcpyAsync(S->lx + (size_t)r * S->C, x + (size_t)rows[r] * S->C, 4 * (size_t)S->C,
+                                 cudaMemcpyDeviceToDevice, st));
+  const size_t nrm_smem = 4 * (size_t)S->C;
+  k_rmsnorm_quant<<<nrows, NORM_THREADS, nrm_smem, st>>>(S->lx, S->C, S->nrmF, S->spec.norm_eps, S->xq, S->ldC, S->rs,
+                                                          ctx->d_status);
+  int rc = dc_gemm_dispatch(ctx, S->xq, S->ldC, S->lm.qt, S->lm.ldk, S->rs, S->lm.cs, nrows, S->C, S->V, 1, 0,
+                            logits, st, 0);
+  if (rc) return rc;
+  if (picks) k_argmax<<<nrows, 1024, 0, st>>>(logits, S->V, picks);
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+// Test access to one layer's cache: keys as int8 + scales and values as f32.
+extern "C" int dc_stage_kv_read(dc_stage* S, int layer, int8_t* k8, float* ks, float* v) {
+  if (!S || layer < S->lo || layer >= S->hi) return DC_E_INVAL;
+  const dc_kv& kv = S->L[layer - S->lo].kv;
+  const int n = S->kv_len;
+  for (int g = 0; g < S->nKV; g++) {
+    if (k8)
+      DC_CUDA(S->ctx, cudaMemcpy(k8 + (size_t)g * n * S->hd, kv.k8 + (size_t)g * S->max_pos * S->hd, (size_t)n * S->hd,
+                                 cudaMemcpyDeviceToHost));
+    if (ks)
+      DC_CUDA(S->ctx, cudaMemcpy(ks + (size_t)g * n, kv.ks + (size_t)g * S->max_pos, 4 * (size_t)n,
+                                 cudaMemcpyDeviceToHost));
+  }
+  if (v) DC_CUDA(S->ctx, cudaMemcpy(v, kv.v, 4 * (size_t)n * S->kvDim, cudaMemcpyDeviceToHost));
+  return DC_OK;
+}

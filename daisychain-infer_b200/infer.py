@@ -1,0 +1,248 @@
+"""The forward pass split at layer boundaries: public/infer.js on the B200.
+
+``Stage`` wraps a ``dc_stage`` (include/dcinfer.h): one contiguous layer range
+of a Llama-family model resident in HBM with its KV cache.  The functions
+mirror the reference's API and meaning:
+
+    embed_rows (infer.js:298)   run_layers (:275)    run_layers_chunk (:288)
+    logits_at (:324)            generate_local (:448)
+    generate_lookahead (:464)   generate_chunked (:339)
+
+Activations live on the device (torch tensors used as plain device buffers);
+greedy picks come back to the host as token ids.  ``NonFiniteError`` is raised
+for a non-finite activation, as runLayers does (:279-281).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib, shard
+from ._lib import DcSpec, raise_for
+
+
+@dataclass
+class Spec:
+    """The Llama-family fields of arch.js fromConfig (:50-71)."""
+    hidden: int
+    layers: int
+    heads: int
+    kvHeads: int
+    inter: int
+    vocab: int
+    headDim: int = 0
+    normEps: float = 1e-5
+    ropeTheta: float = 10000.0
+    tie: bool = True
+    maxPos: int = 2048
+
+    def __post_init__(self):
+        if not self.headDim:
+            self.headDim = self.hidden // self.heads
+        if self.heads % self.kvHeads:
+            raise ValueError(f"num_attention_heads ({self.heads}) is not a multiple of num_key_value_heads "
+                             f"({self.kvHeads})")
+
+    @classmethod
+    def from_config(cls, cfg: dict) -> "Spec":
+        """arch.js:30-81 for the Llama family; other families are refused by name."""
+        t = str(cfg.get("model_type", "")).lower()
+        if t not in {"llama", "mistral", "qwen2", "qwen3", "smollm", "tinyllama", "olmo", "phi3"}:
+            raise ValueError(f'unsupported architecture "{cfg.get("model_type", "unknown")}"')
+        need = ("hidden_size", "num_hidden_layers", "num_attention_heads", "vocab_size")
+        if any(not cfg.get(k) for k in need):
+            raise ValueError("config.json is missing hidden_size / num_hidden_layers / num_attention_heads / "
+                             "vocab_size")
+        if not cfg.get("intermediate_size"):
+            raise ValueError("a gated MLP needs intermediate_size in config.json")
+        h = cfg["hidden_size"]
+        heads = cfg["num_attention_heads"]
+        return cls(hidden=h, layers=cfg["num_hidden_layers"], heads=heads,
+                   kvHeads=cfg.get("num_key_value_heads", heads), inter=cfg["intermediate_size"],
+                   vocab=cfg["vocab_size"], headDim=cfg.get("head_dim", h // heads),
+                   normEps=cfg.get("rms_norm_eps", 1e-5), ropeTheta=cfg.get("rope_theta", 10000.0),
+                   tie=bool(cfg.get("tie_word_embeddings", False)), maxPos=cfg.get("max_position_embeddings", 2048))
+
+    def c_spec(self) -> DcSpec:
+        return DcSpec(self.hidden, self.layers, self.heads, self.kvHeads, self.headDim, self.inter, self.vocab,
+                      float(self.normEps), float(self.ropeTheta), 1 if self.tie else 0)
+
+
+def _ptr(a):
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data_as(C.c_void_p)
+    return C.c_void_p(a.data_ptr())
+
+
+class Stage:
+    """Layers [lo, hi) of one model on the compute core's device."""
+
+    def __init__(self, comp, spec: Spec, lo: int, hi: int, head: bool, max_rows: int, max_pos: int):
+        import torch
+        self.torch = torch
+        self.comp, self.spec, self.lo, self.hi, self.head = comp, spec, lo, hi, head
+        self.max_rows, self.max_pos = max_rows, max_pos
+        self.L = comp.L
+        h = C.c_void_p()
+        cs = spec.c_spec()
+        self._check(self.L.dc_stage_create(comp.h, C.byref(cs), lo, hi, 1 if head else 0, max_rows, max_pos,
+                                           C.byref(h)), "stage_create")
+        self.h = h
+        dev = torch.device("cuda", comp.device)
+        self.dev = dev
+        self._ids = torch.empty(max_rows, dtype=torch.int32, device=dev)
+        self._picks = torch.empty(8, dtype=torch.int32, device=dev)
+        self._logits = torch.empty(8 * spec.vocab, dtype=torch.float32, device=dev) if head else None
+
+    def _check(self, rc, where):
+        if rc:
+            raise_for(rc, f"{where}: " + (self.L.dc_last_error(self.comp.h) or b"").decode())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.dc_stage_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- weights ----------------------------------------------------------------
+    def set_layer(self, layer: int, ly: dict) -> None:
+        keys = ("nrm1", "nrm2", "Wq", "Wk", "Wv", "Wo", "Wgate", "Wup", "Wdown")
+        arrs = [np.ascontiguousarray(ly[k], np.float32) for k in keys]
+        self._check(self.L.dc_stage_set_layer(self.h, layer, *[_ptr(a) for a in arrs]), "stage_set_layer")
+
+    def set_head(self, emb, nrmF, lm=None) -> None:
+        e = np.ascontiguousarray(emb, np.float32)
+        n = np.ascontiguousarray(nrmF, np.float32)
+        m = None if lm is None else np.ascontiguousarray(lm, np.float32)
+        self._check(self.L.dc_stage_set_head(self.h, _ptr(e), _ptr(n), _ptr(m)), "stage_set_head")
+
+    def load(self, w: dict) -> None:
+        """Weights as the oracle's fixtures hold them (k x n f32, reference layout)."""
+        for l in range(self.lo, self.hi):
+            self.set_layer(l, w["layers"][l])
+        if self.head:
+            self.set_head(w["emb"], w["nrmF"], w.get("lm"))
+
+    def synth(self, model_seed: int, factor: float) -> None:
+        self._check(self.L.dc_stage_synth(self.h, model_seed, float(factor)), "stage_synth")
+
+    # ---- the pass -----------------------------------------------------------------
+    def embed_rows(self, ids) -> "torch.Tensor":
+        torch = self.torch
+        ids = torch.as_tensor(np.asarray(ids, np.int32)).to(self.dev, non_blocking=False)
+        T = ids.numel()
+        x = torch.empty(T * self.spec.hidden, dtype=torch.float32, device=self.dev)
+        self._check(self.L.dc_stage_embed(self.h, _ptr(ids), T, _ptr(x)), "stage_embed")
+        return x
+
+    def run_layers(self, x) -> "torch.Tensor":
+        """Full-window pass of this stage's layers, in place on x (positions 0..T-1)."""
+        T = x.numel() // self.spec.hidden
+        self._check(self.L.dc_stage_forward(self.h, _ptr(x), T, 0, 0), "runLayers")
+        return x
+
+    def run_layers_chunk(self, x, pos0: int) -> "torch.Tensor":
+        """One chunk at positions pos0.., appending to this stage's KV cache."""
+        T = x.numel() // self.spec.hidden
+        self._check(self.L.dc_stage_forward(self.h, _ptr(x), T, pos0, 1), "runLayersChunk")
+        return x
+
+    def logits_at(self, x, rows):
+        """Greedy picks (host list) and device logits of the given rows."""
+        T = x.numel() // self.spec.hidden
+        r = np.ascontiguousarray(rows, np.int32)
+        self._check(self.L.dc_stage_logits(self.h, _ptr(x), T, _ptr(r), r.size, _ptr(self._logits),
+                                           _ptr(self._picks)), "logitsAt")
+        self.comp.sync()
+        picks = self._picks[: r.size].cpu().tolist()
+        return picks, self._logits[: r.size * self.spec.vocab].view(r.size, self.spec.vocab)
+
+    def kv_reset(self) -> None:
+        self._check(self.L.dc_stage_kv_reset(self.h), "kv_reset")
+
+    def kv_len(self) -> int:
+        return self.L.dc_stage_kv_len(self.h)
+
+    def kv_read(self, layer: int):
+        n = self.kv_len()
+        s = self.spec
+        k8 = np.empty(s.kvHeads * n * s.headDim, np.int8)
+        ks = np.empty(s.kvHeads * n, np.float32)
+        v = np.empty(n * s.kvHeads * s.headDim, np.float32)
+        self._check(self.L.dc_stage_kv_read(self.h, layer, _ptr(k8), _ptr(ks), _ptr(v)), "kv_read")
+        return k8, ks, v
+
+
+def _sync_check(stages):
+    stages[0].comp.sync()
+
+
+def run_ring(stages, x, chunk_pos=None):
+    """One lap through every stage in plan order (the hop is a device buffer)."""
+    for S in stages:
+        if S.hi > S.lo:
+            x = S.run_layers(x) if chunk_pos is None else S.run_layers_chunk(x, chunk_pos)
+    return x
+
+
+def generate_local(stages, ids, n_tokens: int, T: int) -> list:
+    """infer.js:448-460, greedy."""
+    head = stages[0]
+    out = list(ids)
+    for _ in range(n_tokens):
+        tail = out[-T:]
+        win = [0] * (T - len(tail)) + tail
+        x = run_ring(stages, head.embed_rows(win))
+        picks, _ = head.logits_at(x, [T - 1])
+        out.append(picks[0])
+    return out
+
+
+def generate_lookahead(stages, ids0, n_new: int, T: int, max_draft: int = 4) -> list:
+    """infer.js:464-494, greedy: the prompt-lookup draft scored in the same lap."""
+    head = stages[0]
+    ids = list(ids0)
+    produced = 0
+    while produced < n_new:
+        frame = shard.lookahead_frame(ids, T, max_draft)
+        draft = frame["draft"]
+        win = [0] * (T - len(frame["win"])) + frame["win"]
+        x = run_ring(stages, head.embed_rows(win))
+        rows = shard.draft_rows(T, frame["shown"], len(draft))
+        picked, _ = head.logits_at(x, rows)
+        got = shard.accept_draft(picked, draft)
+        if not got:
+            break
+        for t in got:
+            ids.append(t)
+            produced += 1
+            if produced >= n_new:
+                break
+    return ids
+
+
+def generate_chunked(stages, ids0, n_new: int, chunk_size: int) -> list:
+    """infer.js:339-367, greedy: chunked prefill on per-stage KV, then one token per lap."""
+    head = stages[0]
+    ids = list(ids0)
+    for S in stages:
+        S.kv_reset()
+    last = None
+    for ch in shard.prefill_chunks(len(ids), chunk_size, 1)["chunks"]:
+        last = run_ring(stages, head.embed_rows(ids[ch["lo"]:ch["hi"]]), ch["lo"])
+    for _ in range(n_new):
+        rows = last.numel() // head.spec.hidden
+        picks, _ = head.logits_at(last, [rows - 1])
+        ids.append(picks[0])
+        pos = len(ids) - 1
+        last = run_ring(stages, head.embed_rows([picks[0]]), pos)
+    return ids

@@ -67,7 +67,8 @@ void* dc_stream(const dc_ctx* ctx);
 /* Message of the last dc_init that failed on this thread (no context exists). */
 const char* dc_init_error(void);
 /* Run the context's work on an existing cudaStream_t (NULL = the context's own
- * stream).  Lets a caller order the library's launches with its own work. */
+ * stream; (void*)1 = cudaStreamLegacy, the legacy default stream).  Lets a
+ * caller order the library's launches with its own work. */
 int dc_set_stream(dc_ctx* ctx, void* stream);
 /* 1 when the tcgen05 tensor-core GEMM passed its init gate and is in use. */
 int dc_tc_enabled(const dc_ctx* ctx);
@@ -129,6 +130,50 @@ int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned fl
  * kernels; returns the FNV-1a of the int32 result (before the reference folds in
  * its transcendental hash, which needs V8). */
 int dc_kernel_probe(dc_ctx* ctx, uint32_t* hash);
+
+/* ---- pipeline stages (public/infer.js, Llama family) -------------------------
+ * A stage owns layers [layer_lo, layer_hi) of one model (shard.js planStages
+ * :32-52) with every weight quantised once and resident in HBM, RoPE tables,
+ * and a KV cache of max_pos positions per layer; the head stage (head = 1)
+ * also owns the embedding, the final norm and lm_head.  Field names follow
+ * arch.js fromConfig (:50-71). */
+typedef struct dc_spec {
+  int hidden, layers, heads, kv_heads, head_dim, inter, vocab;
+  double norm_eps, rope_theta;
+  int tie; /* lm_head = embᵀ */
+} dc_spec;
+typedef struct dc_stage dc_stage;
+
+int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int layer_lo, int layer_hi, int head, int max_rows,
+                    int max_pos, dc_stage** out);
+void dc_stage_free(dc_stage* stage);
+/* Host f32 weights in the reference's k x n (in x out) layout (shard.js toKN :70-76). */
+int dc_stage_set_layer(dc_stage* stage, int layer, const float* nrm1, const float* nrm2, const float* Wq,
+                       const float* Wk, const float* Wv, const float* Wo, const float* Wgate, const float* Wup,
+                       const float* Wdown);
+/* emb vocab x hidden, nrmF hidden, lm_kn hidden x vocab or NULL when tied (shard.js:84-94). */
+int dc_stage_set_head(dc_stage* stage, const float* emb, const float* nrmF, const float* lm_kn);
+/* Synthetic random-init weights generated on the device: counter-based, each
+ * element the scaled, centred sum of four splitmix64 draws (norm weights 1). */
+int dc_stage_synth(dc_stage* stage, uint64_t model_seed, double factor);
+/* embedRows (infer.js:298-310): ids (device int32) -> x (device, T x hidden). */
+int dc_stage_embed(dc_stage* stage, const int32_t* ids, int T, float* x);
+/* runLayers (use_kv = 0: the full window, positions 0..T-1, infer.js:275-283) or
+ * runLayersChunk (use_kv = 1: positions pos0.., keys and values appended to the
+ * stage's cache, infer.js:288-296); x (device, T x hidden) is updated in place.
+ * Asynchronous: a non-finite activation is reported by dc_sync as DC_E_NONFINITE. */
+int dc_stage_forward(dc_stage* stage, float* x, int T, int pos0, int use_kv);
+/* logitsAt (infer.js:324-334) for rows[0..nrows) (host ints, nrows <= 8):
+ * logits (device, nrows x vocab) and the greedy pick of each row (device int32,
+ * may be NULL), first maximum wins (infer.js:393-395). */
+int dc_stage_logits(dc_stage* stage, const float* x, int T, const int32_t* rows, int nrows, float* logits,
+                    int32_t* picks);
+/* The chunk path's cache: reset, and the number of cached tokens. */
+int dc_stage_kv_reset(dc_stage* stage);
+int dc_stage_kv_len(const dc_stage* stage);
+/* Copy one layer's cache to host buffers: int8 keys [kv_heads][len][head_dim],
+ * key scales [kv_heads][len], f32 values [len][kv_heads*head_dim] (any may be NULL). */
+int dc_stage_kv_read(dc_stage* stage, int layer, int8_t* k8, float* ks, float* v);
 
 #ifdef __cplusplus
 }

@@ -7,7 +7,7 @@ pytestmark = pytest.mark.gpu
 
 def edge_rows():
     rows = []
-    r = np.zeros(64, np.float32); r[0] = 127.0; r[1:9] = [2.5, -2.5, 0.5, -0.5, 126.5, -127.5, 1.5, -1.5]
+    r = np.zeros(64, np.float32); r[0] = 127.0; r[1:9] = [2.5, -2.5, 0.5, -0.5, 126.5, -126.5, 1.5, -1.5]
     rows.append(r)                                           # scale exactly 1: ties go toward +inf
     r = np.zeros(64, np.float32); r[0] = 127.0; r[1] = np.float32(0.49999997); r[2] = np.float32(-0.49999997)
     rows.append(r)                                           # just below a tie
@@ -47,7 +47,7 @@ def test_quantize_rows_edge_values(comp, O):
     comp.sync()
     wq, ws = O.quantize_rows(X, rows, cols)
     assert q.cpu().numpy().tobytes() == wq.tobytes() and s.cpu().numpy().tobytes() == ws.tobytes()
-    assert list(wq[1:9]) == [3, -2, 1, 0, 127, -127, 2, -1]
+    assert list(wq[1:9]) == [3, -2, 1, 0, 127, -126, 2, -1]
 
 
 def test_quantize_cols_transposed_matches_oracle(comp, O):

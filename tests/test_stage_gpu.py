@@ -1,0 +1,188 @@
+"""The forward pass on the B200 against the CPU oracle, bit for bit.
+
+The reference's pipeline checks (test_pipeline.js) run on the device: the
+6-layer Llama fixture (hidden 64, 4/2 heads, inter 128, vocab 128, T = 16,
+prompt [5, 11, 42, 7]) must give the oracle's hidden-state bits and token ids,
+at every stage split, through the full-window, chunked-prefill and lookahead
+paths; plus synthetic random-init models at head_dim 64 and 128.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+T, PROMPT = 16, [5, 11, 42, 7]
+
+
+def ranges(splits):
+    out, lo = [], 0
+    for n in splits:
+        out.append((lo, lo + n))
+        lo += n
+    return out
+
+
+def make_stages(P, comp, spec, w, splits, max_rows=64, max_pos=64, synth=None):
+    I = P.infer
+    stages = []
+    for i, (lo, hi) in enumerate(ranges(splits)):
+        S = I.Stage(comp, spec, lo, hi, head=(i == 0), max_rows=max_rows, max_pos=max_pos)
+        if synth is not None:
+            S.synth(*synth)
+        else:
+            S.load(w)
+        stages.append(S)
+    return stages
+
+
+@pytest.fixture(scope="module")
+def fixture(O, P):
+    ospec = O.LLAMA_TEST
+    w = O.make_weights(ospec)
+    spec = P.infer.Spec(hidden=ospec.hidden, layers=ospec.layers, heads=ospec.heads, kvHeads=ospec.kvHeads,
+                        inter=ospec.inter, vocab=ospec.vocab, tie=True, maxPos=64)
+    return ospec, spec, w, O.Model(ospec, w)
+
+
+def win_of(ids, t=T):
+    return [0] * (t - len(ids)) + list(ids)
+
+
+def test_window_hidden_state_bits(comp, O, P, fixture):
+    ospec, spec, w, om = fixture
+    stages = make_stages(P, comp, spec, w, [6])
+    x = stages[0].embed_rows(win_of(PROMPT))
+    x = stages[0].run_layers(x)
+    comp.sync()
+    want = om.run_layers(om.embed_rows(np.array(win_of(PROMPT), np.int32)), 0, 6)
+    assert x.cpu().numpy().tobytes() == want.tobytes()
+
+
+def test_stage_boundary_changes_no_bit(comp, O, P, fixture):
+    ospec, spec, w, om = fixture
+    whole = make_stages(P, comp, spec, w, [6])
+    split = make_stages(P, comp, spec, w, [2, 2, 2])
+    a = P.infer.run_ring(whole, whole[0].embed_rows(win_of(PROMPT)))
+    b = P.infer.run_ring(split, split[0].embed_rows(win_of(PROMPT)))
+    comp.sync()
+    assert a.cpu().numpy().tobytes() == b.cpu().numpy().tobytes()
+
+
+def test_logits_bits_match_oracle(comp, O, P, fixture):
+    ospec, spec, w, om = fixture
+    stages = make_stages(P, comp, spec, w, [6])
+    x = P.infer.run_ring(stages, stages[0].embed_rows(win_of(PROMPT)))
+    picks, logits = stages[0].logits_at(x, [T - 1, 3, 0])
+    xo = om.run_layers(om.embed_rows(np.array(win_of(PROMPT), np.int32)), 0, 6)
+    want = om.logits_rows(xo, [T - 1, 3, 0])
+    assert logits.cpu().numpy().tobytes() == want.tobytes()
+    assert picks == [O.argmax(want[i]) for i in range(3)]
+
+
+@pytest.mark.parametrize("splits", [[6], [3, 3], [1, 2, 3], [0, 3, 3], [2, 1, 1, 1, 1]])
+def test_generation_matches_oracle_at_every_split(comp, O, P, fixture, splits):
+    ospec, spec, w, om = fixture
+    ref = O.generate_local(om, [(0, 6)], PROMPT, 8, T)
+    got = P.infer.generate_local(make_stages(P, comp, spec, w, splits), PROMPT, 8, T)
+    assert got == ref
+
+
+def test_mutations_are_caught_on_device(comp, O, P, fixture):
+    ospec, spec, w, om = fixture
+    ref = O.generate_local(om, [(0, 6)], PROMPT, 8, T)
+    st = make_stages(P, comp, spec, w, [2, 2, 2])
+    assert P.infer.generate_local([st[0], st[2], st[1]], PROMPT, 8, T) != ref
+    dropped = make_stages(P, comp, spec, w, [2, 1])  # layers 3..5 never run
+    assert P.infer.generate_local(dropped, PROMPT, 8, T) != ref
+
+
+def test_chunked_prefill_matches_oracle(comp, O, P, fixture):
+    ospec, spec, w, om = fixture
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8]
+    ref = O.generate_chunked(om, [(0, 6)], prompt, 3, 4)
+    for splits in ([6], [2, 2, 2]):
+        got = P.infer.generate_chunked(make_stages(P, comp, spec, w, splits), prompt, 3, 4)
+        assert got == ref
+
+
+def test_kv_cache_contents_match_oracle(comp, O, P, fixture):
+    ospec, spec, w, om = fixture
+    ids = [1, 2, 3, 4, 5]
+    st = make_stages(P, comp, spec, w, [6])
+    x = st[0].run_layers_chunk(st[0].embed_rows(ids[:3]), 0)
+    x = st[0].run_layers_chunk(st[0].embed_rows(ids[3:]), 3)
+    comp.sync()
+    kv = O.KV(om, 0, 6, 8)
+    om.run_layers(om.embed_rows(ids[:3]), 0, 6, kv, 0)
+    om.run_layers(om.embed_rows(ids[3:]), 0, 6, kv, 3)
+    hd, nkv = ospec.headDim, ospec.kvHeads
+    for layer in (0, 5):
+        k8, ks, v = st[0].kv_read(layer)
+        kf, vf = kv.read(layer)
+        assert v.tobytes() == vf.tobytes()
+        n = len(ids)
+        kf = kf.reshape(n, nkv, hd)
+        for g in range(nkv):
+            q, s = O.quantize_cols(kf[:, g, :].T.copy(), hd, n)   # khᵀ: columns are key tokens
+            assert ks.reshape(nkv, n)[g].tobytes() == s.tobytes()
+            assert k8.reshape(nkv, n, hd)[g].tobytes() == q.reshape(hd, n).T.copy().tobytes()
+
+
+def test_lookahead_matches_oracle(comp, O, P, fixture):
+    ospec, spec, w, om = fixture
+    prompt = [4, 4, 4, 7, 4, 4, 4]
+    ref = O.generate_lookahead(om, [(0, 6)], prompt, 4, 16, 4)
+    for splits in ([6], [1, 2, 3]):
+        got = P.infer.generate_lookahead(make_stages(P, comp, spec, w, splits), prompt, 4, 16, 4)
+        assert got == ref
+
+
+def test_non_finite_activation_refused(comp, P, fixture):
+    import torch
+    ospec, spec, w, om = fixture
+    st = make_stages(P, comp, spec, w, [6])
+    x = st[0].embed_rows(win_of(PROMPT))
+    x[5] = float("nan")
+    st[0].run_layers(x)
+    with pytest.raises(P.NonFiniteError):
+        comp.sync()
+
+
+def synth_model(O, P, hidden, layers, heads, kv, inter, vocab, tie, theta=10000.0, seed=77):
+    ospec = O.Spec(hidden=hidden, layers=layers, heads=heads, kvHeads=kv, inter=inter, vocab=vocab, tie=tie,
+                   ropeTheta=theta)
+    C_, q, kvd = hidden, heads * ospec.headDim, kv * ospec.headDim
+    w = {"emb": O.synth_weight(seed, -1, "emb", vocab, C_), "nrmF": np.ones(C_, np.float32),
+         "lm": None if tie else O.synth_weight(seed, -1, "lm", C_, vocab), "layers": []}
+    for l in range(layers):
+        w["layers"].append(dict(nrm1=np.ones(C_, np.float32), nrm2=np.ones(C_, np.float32),
+                                Wq=O.synth_weight(seed, l, "Wq", C_, q), Wk=O.synth_weight(seed, l, "Wk", C_, kvd),
+                                Wv=O.synth_weight(seed, l, "Wv", C_, kvd), Wo=O.synth_weight(seed, l, "Wo", q, C_),
+                                Wgate=O.synth_weight(seed, l, "Wgate", C_, inter),
+                                Wup=O.synth_weight(seed, l, "Wup", C_, inter),
+                                Wdown=O.synth_weight(seed, l, "Wdown", inter, C_)))
+    spec = P.infer.Spec(hidden=hidden, layers=layers, heads=heads, kvHeads=kv, inter=inter, vocab=vocab, tie=tie,
+                        ropeTheta=theta)
+    return ospec, spec, w
+
+
+@pytest.mark.parametrize("cfg", [dict(hidden=256, layers=2, heads=4, kv=2, inter=512, vocab=1000, tie=True),
+                                 dict(hidden=512, layers=2, heads=4, kv=1, inter=1024, vocab=777, tie=False,
+                                      theta=500000.0)],
+                         ids=["hd64-tied", "hd128-untied"])
+def test_synthetic_model_device_generator_matches_oracle(comp, O, P, cfg):
+    ospec, spec, w = synth_model(O, P, **cfg)
+    om = O.Model(ospec, w)
+    seed = 77
+    ids = list(np.random.default_rng(3).integers(0, cfg["vocab"], 40))
+    for synth in (True, False):
+        st = make_stages(P, comp, spec, w, [cfg["layers"]], max_rows=64, max_pos=96,
+                         synth=(seed, O.SYNTH_FACTOR) if synth else None)
+        x = P.infer.run_ring(st, st[0].embed_rows(ids))
+        comp.sync()
+        want = om.run_layers(om.embed_rows(np.array(ids, np.int32)), 0, cfg["layers"])
+        assert x.cpu().numpy().tobytes() == want.tobytes(), f"synth={synth}"
+        picks, logits = st[0].logits_at(x, [len(ids) - 1])
+        assert logits.cpu().numpy().tobytes() == om.logits_rows(want, [len(ids) - 1]).tobytes()
+    got = P.infer.generate_chunked(st, ids, 6, 16)
+    assert got == O.generate_chunked(om, [(0, cfg["layers"])], ids, 6, 16)
