@@ -62,6 +62,7 @@ SIGNATURES = [
     ("dc_bgemm", _i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _u, _p]),
     ("dc_bgemm_dev", _i, [_p, _p, _i, _p, _i, _p, _p, _i, _i, _i, _i, _u, _p]),
     ("dc_bgemm_dev_kind", _i, [_p, _p, _i, _p, _i, _p, _p, _i, _i, _i, _i, _u, _p, _i]),
+    ("dc_bgemm_dev_noalloc", _i, [_p, _p, _i, _p, _i, _p, _p, _i, _i, _i, _i, _u, _p]),
     ("dc_bgemm_lut_dev", _i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _u, _p]),
     ("dc_quantize_rows", _i, [_p, _p, _i, _i, _p, _i, _p]),
     ("dc_quantize_cols_t", _i, [_p, _p, _i, _i, _p, _i, _p]),
