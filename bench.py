@@ -1,23 +1,32 @@
 #!/usr/bin/env python3
-"""Benchmark of the verified INT8 W8A8 path on B200.
+"""Benchmark of DaisyChain-Infer's verified INT8 W8A8 path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-Prints one JSON line (rank 0).  Workloads:
+One JSON line (rank 0).  The metric is the reference's: INT8 decode tok/s and
+chunked-prefill tok/s at 1/2/4/8 B200 (pipeline stages), with the GEMM's
+fraction of the roofline.  Workloads (synthetic random-init models of the named
+shapes; seeded uniform token ids; no dataset is involved):
 
-* ``gemm-sweep``: the standalone INT8 GEMM sweep (seeded): A f32 ~ N(0,1)
-  quantised per row on the device, B int8 uniform in [-127, 127] with
-  per-column scales uniform in [1e-3, 1e-2], M in {1,16,128,512} x (K,N) in
-  {(576,1536), (1536,576), (2048,5632), (4096,14336)}; int32 accumulate and
-  the requant-LUT int8 output.  One step = the 16 shapes once.  Weights are
-  resident in HBM with enough copies per shape that every launch reads them
-  cold (each shape's copies total more than 3x the 126 MB L2).
+* ``llama3-8b-chunked`` (default): hidden 4096, 32 layers, 32/8 heads, inter
+  14336, vocab 128256, RoPE theta 500000; a 2048-token prompt prefilled in
+  16-token chunks with two in flight, then 256 greedy decode tokens.  At N GPUs
+  the 32 layers are split over N pipeline stages (planStages, equal capacity).
+* ``tinyllama-chunked``: hidden 2048, 22 layers, 32/4 heads, inter 5632, vocab
+  32000; 512-token prompt, chunks of 16, 128 decode tokens.
+* ``smollm-135m-window``: hidden 576, 30 layers, 9/3 heads, inter 1536, vocab
+  49152 (tied); full-window lookahead path, T = 64, 24-token prompt, 16 tokens.
+* ``smollm-360m-lookahead``: hidden 960, 32 layers, 15/5 heads, inter 2560,
+  vocab 49152 (tied); T = 512, a 256-token prompt of a seeded 8-gram repeated
+  with 20% substitutions, 128 new tokens.
+* ``gemm-sweep``: the standalone INT8 GEMM sweep (M in {1,16,128,512} x (K,N)).
 
-Timing: W untimed warm-up steps, then K steps between barrier +
-synchronize, measured with CUDA events on the launching stream, max over
-ranks.  ``--impl reference`` times the reference's CPU algorithm (the C
-restatement in oracle/, all host cores) on a bounded sample of the same
-workload.
+One step = one whole generation (prefill + decode, or the lookahead laps).
+``value`` is decode tokens/s (new tokens / decode time on the head);
+``prefill_tok_s`` is prompt tokens / prefill time.  Timing: W untimed warm-up
+steps, then K steps between barrier + synchronize, CUDA events on the launching
+stream, max over ranks.  The model's weights (~8 GB for Llama-3-8B) exceed the
+126 MB L2, so every step reads them from HBM.
 """
 from __future__ import annotations
 
@@ -35,9 +44,28 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "INT8 decode tok/s + chunked-prefill tok/s at 1/2/4/8 B200; GEMM % roofline"
+MODEL_SEED = 20261201
 SWEEP_M = [1, 16, 128, 512]
 SWEEP_KN = [(576, 1536), (1536, 576), (2048, 5632), (4096, 14336)]
 L2_BYTES = 126 * 1024 * 1024
+
+WORKLOADS = {
+    "llama3-8b-chunked": dict(spec=dict(hidden=4096, layers=32, heads=32, kvHeads=8, inter=14336, vocab=128256,
+                                        ropeTheta=500000.0, tie=False),
+                              mode="chunked", prompt=2048, new=256, chunk=16, window=2,
+                              name="Llama-3-8B-shaped decoder"),
+    "tinyllama-chunked": dict(spec=dict(hidden=2048, layers=22, heads=32, kvHeads=4, inter=5632, vocab=32000,
+                                        ropeTheta=10000.0, tie=False),
+                              mode="chunked", prompt=512, new=128, chunk=16, window=2,
+                              name="TinyLlama-1.1B-shaped decoder"),
+    "smollm-135m-window": dict(spec=dict(hidden=576, layers=30, heads=9, kvHeads=3, inter=1536, vocab=49152,
+                                         ropeTheta=10000.0, tie=True),
+                               mode="lookahead", prompt=24, new=16, T=64, name="SmolLM-135M-shaped decoder"),
+    "smollm-360m-lookahead": dict(spec=dict(hidden=960, layers=32, heads=15, kvHeads=5, inter=2560, vocab=49152,
+                                            ropeTheta=10000.0, tie=True),
+                                  mode="lookahead", prompt="ngram", new=128, T=512,
+                                  name="SmolLM-360M-shaped decoder"),
+}
 
 
 def load_peaks():
@@ -49,6 +77,13 @@ def load_peaks():
     return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0, src="fallback")
 
 
+def traffic_for(key):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(key)
+    return None
+
+
 # ---- clocks during the timed region ----------------------------------------------
 class Clocks:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -56,13 +91,10 @@ class Clocks:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
+        self.gpu, self.proc, self.path, self.t_start = gpu_index, None, None, 0.0
 
     def start(self):
-        """Start sampling and wait (up to 10 s) for the first sample, so the
-        timed region that follows is covered."""
+        """Start sampling and wait (up to 10 s) for the first sample."""
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -78,7 +110,6 @@ class Clocks:
         self.t_start = time.time()
 
     def mark_end(self):
-        """Keep sampling until at least 0.3 s passed since the timed region began."""
         if self.proc is not None:
             while time.time() - self.t_start < 0.3:
                 time.sleep(0.05)
@@ -115,13 +146,12 @@ def dist_init():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
     if world > 1:
         import datetime
         import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
     return rank, local, world
 
 
@@ -131,184 +161,311 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(v: float, world: int) -> float:
+def max_over_ranks(vals, world):
     if world == 1:
-        return v
+        return list(vals)
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    t = torch.tensor(list(vals), dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return t.tolist()
 
 
-# ---- the GEMM sweep -------------------------------------------------------------------
-def sweep_shapes():
-    return [(m, k, n) for (k, n) in SWEEP_KN for m in SWEEP_M]
+def sum_over_ranks(vals, world):
+    if world == 1:
+        return list(vals)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(list(vals), dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.tolist()
 
 
-def gemm_bytes(m, k, n, out_bytes):
-    return m * k + k * n + 4 * m + 4 * n + out_bytes * m * n
+# ---- model workloads --------------------------------------------------------------------
+def prompt_ids(w: dict, vocab: int, seed: int = 7):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    if w["prompt"] == "ngram":
+        gram = rng.integers(0, vocab, 8)
+        ids = np.resize(gram, 256)
+        sub = rng.random(256) < 0.2
+        ids[sub] = rng.integers(0, vocab, int(sub.sum()))
+        return [int(v) for v in ids]
+    return [int(v) for v in rng.integers(0, vocab, w["prompt"])]
 
 
-class SweepData:
-    """Device buffers of the sweep: A f32, its int8 rows + scales, weight copies."""
-
-    def __init__(self, torch, seed=2026):
-        g = torch.Generator(device="cuda").manual_seed(seed)
-        self.items = []
-        for (m, k, n) in sweep_shapes():
-            ld = (k + 15) // 16 * 16
-            A = torch.randn(m, k, generator=g, device="cuda", dtype=torch.float32)
-            copies = max(3, math.ceil(3 * L2_BYTES / (n * ld)))
-            W = torch.randint(-127, 128, (copies, n, ld), generator=g, device="cuda", dtype=torch.int8)
-            if ld != k:
-                W[:, :, k:] = 0
-            cs = torch.rand(copies, n, generator=g, device="cuda") * 9e-3 + 1e-3
-            self.items.append(dict(m=m, k=k, n=n, ld=ld, A=A, W=W, cs=cs, copies=copies,
-                                   xq=torch.zeros(m, ld, dtype=torch.int8, device="cuda"),
-                                   rs=torch.empty(m, device="cuda"),
-                                   out=torch.empty(m * n, dtype=torch.int8, device="cuda")))
-
-
-def run_sweep_step(comp, data, step, events=None, dom=None):
-    """One step: every shape quantises its A rows and runs the GEMM (requant out)."""
-    launches = 0
-    for i, it in enumerate(data.items):
-        c = step % it["copies"]
-        comp.quantize_rows_dev(it["A"], it["m"], it["k"], it["xq"], it["ld"], it["rs"])
-        if events is not None and i == dom:
-            events[0].record()
-        comp.bgemm_dev(it["xq"], it["ld"], it["W"][c], it["ld"], it["rs"], it["cs"][c], it["m"], it["k"], it["n"], 1,
-                       4, it["out"])
-        if events is not None and i == dom:
-            events[1].record()
-            events[2].append((events[0], events[1]))
-            events[0], events[1] = type(events[0])(enable_timing=True), type(events[1])(enable_timing=True)
-        launches += 2
-    return launches
+def build_rank(P, comp, w: dict, rank: int, world: int):
+    """This rank's stage of the plan (planStages over equal capacities)."""
+    import torch
+    spec = P.infer.Spec(**w["spec"])
+    plan = P.shard.plan_stages(spec.layers, [dict(id=f"gpu{i}", capacity=1.0) for i in range(world)])
+    assert len(plan) == world
+    st = plan[rank]
+    if w["mode"] == "chunked":
+        max_rows, max_pos = max(w["chunk"], 8), w["prompt"] + w["new"] + 1
+    else:
+        max_rows, max_pos = w["T"], w["T"]
+    S = P.infer.Stage(comp, spec, st["lo"], st["hi"], head=(rank == 0), max_rows=max_rows, max_pos=max_pos)
+    import __graft_entry__ as G
+    S.synth(MODEL_SEED, G.oracle().SYNTH_FACTOR)
+    dev = torch.device("cuda", comp.device)
+    ring = P.pipeline.Ring(S, rank, world, spec.hidden, P.pipeline.TorchP2P() if world > 1 else None,
+                           new_buffer=lambda n: torch.empty(n, dtype=torch.float32, device=dev))
+    return spec, plan, S, ring
 
 
-def bench_gemm_sweep(args, rank, world, peaks):
+def P_fnv(ids):
+    """FNV-1a of the generated ids (int32 little-endian): equal at every GPU count."""
+    h = 0x811C9DC5
+    for v in ids or []:
+        for b in int(v).to_bytes(4, "little", signed=True):
+            h = ((h ^ b) * 0x01000193) & 0xFFFFFFFF
+    return h
+
+
+def weight_bytes(spec, lo, hi, head):
+    C, q, kv, I, V = spec.hidden, spec.heads * spec.headDim, spec.kvHeads * spec.headDim, spec.inter, spec.vocab
+    per_layer = C * (q + 2 * kv) + q * C + 2 * C * I + I * C
+    return (hi - lo) * per_layer + (C * V if head else 0)
+
+
+def bench_model(args, rank, world, peaks):
     import torch
     import __graft_entry__ as G
     P = G.package()
-    comp = P.init_compute(0 if world == 1 else int(os.environ.get("LOCAL_RANK", "0")),
-                          stream=torch.cuda.current_stream())
-    data = SweepData(torch)
-    shapes = sweep_shapes()
-    # pick the dominant GEMM: time each shape's launch during a warm-up pass
-    per = []
-    for i, it in enumerate(data.items):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        comp.quantize_rows_dev(it["A"], it["m"], it["k"], it["xq"], it["ld"], it["rs"])
+    w = WORKLOADS[args.workload]
+    comp = P.init_compute(int(os.environ.get("LOCAL_RANK", "0")), stream=torch.cuda.current_stream())
+    spec, plan, S, ring = build_rank(P, comp, w, rank, world)
+    ids = prompt_ids(w, spec.vocab)
+    marks = {}
+
+    def one_step():
+        if w["mode"] == "chunked":
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            out = ring.generate_chunked(ids, w["new"], w["chunk"], w["window"], on_prefill=e1.record)
+            e2.record()
+            marks.setdefault("ev", []).append((e0, e1, e2))
+            return out
+        e0, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        comp.bgemm_dev(it["xq"], it["ld"], it["W"][0], it["ld"], it["rs"], it["cs"][0], it["m"], it["k"], it["n"], 1,
-                       4, it["out"])
-        e1.record()
-        torch.cuda.synchronize()
-        per.append(e0.elapsed_time(e1))
-    dom = max(range(len(per)), key=lambda i: per[i])
-    for s in range(args.warmup):
-        run_sweep_step(comp, data, s)
+        out = ring.generate_lookahead(ids, w["new"], w["T"], 4)
+        e2.record()
+        marks.setdefault("ev", []).append((e0, e0, e2))
+        return out
+
+    for _ in range(args.warmup):
+        one_step()
     comp.sync()
+    marks.clear()
+    l0 = comp.L.dc_launch_count()
     clocks = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
+    comp.L.dc_timing(comp.h, 1)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    evs = [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True), []]
-    launches = 0
     t0.record()
-    for s in range(args.steps):
-        launches += run_sweep_step(comp, data, args.warmup + s, evs, dom)
+    outs = [one_step() for _ in range(args.steps)]
     t1.record()
+    gen_ids = None
+    if rank == 0:
+        o = outs[-1]
+        gen_ids = [int(v) for v in (o.tolist() if hasattr(o, "tolist") else o[len(ids):])]
     torch.cuda.synchronize()
     clocks.mark_end()
     barrier(world)
     clk = clocks.stop()
     comp.sync()
-    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
-    ops_step = sum(2.0 * m * k * n for (m, k, n) in shapes)
-    value = ops_step * world / (ms / 1e3) / 1e12
-    m, k, n = shapes[dom]
-    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in evs[2])
-    ops = 2.0 * m * k * n
-    byts = gemm_bytes(m, k, n, 1)
-    i8_peak = 2.0 * peaks["bf16_tflops"]
-    ridge = i8_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
-    if ops / byts > ridge:
-        roof = dict(bound="tensor", achieved=ops / (dom_ms / 1e3) / 1e12, peak=i8_peak, unit="TOPS")
-        peak_note = f"2 x {peaks['src']} bf16 dense TFLOP/s (int8 dense rate = 2 x bf16)"
-    else:
-        roof = dict(bound="hbm", achieved=byts / (dom_ms / 1e3) / 1e9, peak=peaks["hbm_gbs"], unit="GB/s")
-        peak_note = f"{peaks['src']} HBM copy bandwidth"
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = traffic_for(f"gemm_{m}x{k}x{n}")
-    roof["kernel"] = f"{'tcgen05' if comp.tc_enabled and m > 8 else ('gemv' if m <= 8 else 'simt')} GEMM {m}x{k}x{n}"
-    roof["peak_source"] = peak_note
-    roof["algorithmic_per_launch"] = dict(ops=ops, bytes=byts)
-    line = dict(metric=METRIC, value=value, unit="TOPS (int8 ops/s, GEMM sweep)", n_gpus=world, steps=args.steps,
-                warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None,
-                dtype="int8 x int8 -> int32", data="synthetic (seeded)",
-                config=dict(workload="gemm-sweep: M{1,16,128,512} x (K,N){(576,1536),(1536,576),(2048,5632),"
-                                     "(4096,14336)}, quantise rows + GEMM + requant-LUT int8 out",
-                            cold_l2="weight copies per shape > 3x L2, rotated every step",
-                            parallelism=f"replicas x{world}"),
-                roofline=roof, gpu_launches=launches, clocks=clk,
-                per_shape_ms={f"{m}x{k}x{n}": round(t, 4) for (m, k, n), t in zip(shapes, per)},
-                backend=comp.label)
+    launches = comp.L.dc_launch_count() - l0
+    ms_step = t0.elapsed_time(t1) / args.steps
+    pre = statistics.mean(a.elapsed_time(b) for a, b, _ in marks["ev"])
+    dec = statistics.mean(b.elapsed_time(c) for _, b, c in marks["ev"])
+    # the live GEMM timing of this rank: GEMV (decode) and tcgen05 (prefill)
+    import ctypes as C
+    kinds = {}
+    for kind in (1, 3):
+        ms, n, by, op = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
+        comp.L.dc_timing_read(comp.h, kind, C.byref(ms), C.byref(n), C.byref(by), C.byref(op))
+        kinds[kind] = (ms.value, n.value, by.value, op.value)
+    comp.L.dc_timing(comp.h, 0)
+    ms_step, pre, dec = max_over_ranks([ms_step, pre, dec], world)
+    launches = int(sum_over_ranks([launches], world)[0])
+    n_new = w["new"]
+    if w["mode"] == "lookahead":
+        n_new = len(outs[-1]) - len(ids) if rank == 0 else w["new"]
+    line = None
+    if rank == 0:
+        value = n_new / (dec / 1e3)
+        dom = max(kinds, key=lambda k: kinds[k][0])
+        ms, n, by, op = kinds[dom]
+        per_launch_ms = ms / max(n, 1)
+        ach = by / (ms / 1e3) / 1e9
+        roof = dict(bound="hbm", achieved=ach, peak=peaks["hbm_gbs"], unit="GB/s", frac=ach / peaks["hbm_gbs"],
+                    traffic=traffic_for("gemv_decode" if dom == 1 else "tc_prefill"),
+                    kernel=("k_gemv (decode GEMV, M<=8)" if dom == 1 else "k_gemm_tc (tcgen05, M>8)"),
+                    launches=n, avg_launch_us=per_launch_ms * 1e3, share_of_step=ms / (ms_step * args.steps),
+                    algorithmic_bytes_per_launch=by / max(n, 1), ops_per_launch=op / max(n, 1),
+                    peak_source=f"{peaks['src']} HBM copy bandwidth (MEASURED_PEAKS.json)")
+        other = {("gemv" if k == 1 else "tcgen05"): dict(ms=kinds[k][0], launches=kinds[k][1],
+                                                          gbs=(kinds[k][2] / (kinds[k][0] / 1e3) / 1e9
+                                                               if kinds[k][0] else None),
+                                                          tops=(kinds[k][3] / (kinds[k][0] / 1e3) / 1e12
+                                                                if kinds[k][0] else None))
+                 for k in kinds}
+        stages = [f"{s['lo']}-{s['hi']}" for s in plan]
+        line = dict(metric=METRIC, value=value, unit="tok/s (decode)", n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=ms_step, higher_is_better=True, scaling="strong",
+                    vs_baseline=None, dtype="int8 x int8 -> int32 (f32 epilogue, f64 norms/softmax)",
+                    data="synthetic (random-init weights, seeded uniform token ids)",
+                    config=dict(workload=f"{args.workload}: {w['name']}, " +
+                                (f"{len(ids)}-token prompt in chunks of {w['chunk']} ({w['window']} in flight), "
+                                 f"{w['new']} greedy decode tokens" if w["mode"] == "chunked" else
+                                 f"full-window lookahead T={w['T']}, {len(ids)}-token prompt, {w['new']} new"),
+                                stages=stages, parallelism=f"pipeline x{world}",
+                                l2="weights ≫ L2: every step streams them from HBM"),
+                    prefill_tok_s=(len(ids) / (pre / 1e3)) if w["mode"] == "chunked" else None,
+                    prefill_ms=pre if w["mode"] == "chunked" else None, decode_ms=dec,
+                    roofline=roof, kernels=other, gpu_launches=launches, clocks=clk, backend=comp.label,
+                    generated_ids_fnv=P_fnv(gen_ids), generated_head=gen_ids[:8],
+                    weights_gb=weight_bytes(spec, 0, spec.layers, True) / 1e9)
     if rank == 0 and world == 1 and not args.no_e2e:
-        line["e2e"] = e2e_gemm_sweep(comp, torch, args)
+        line["e2e"] = e2e_model(comp, ring, w, ids, args)
     if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline_sweep(threads=1)
+        line["cpu_baseline"] = cpu_model_baseline(w)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    S.close()
     return line
 
 
-def e2e_gemm_sweep(comp, torch, args):
-    """Through the public API: per shape a pinned-host f32 A goes to the device,
-    vgemmBlock runs (row quantise + GEMM with a resident weight), the int8
-    output comes back to pinned host memory."""
-    import numpy as np
-    rng = np.random.default_rng(5)
-    items = []
-    h2d = d2h = 0
-    for (m, k, n) in sweep_shapes():
-        W = (rng.standard_normal((k, n), dtype=np.float32) * 0.02)
-        w = comp.register_weight(W, k, n)
-        A = torch.randn(m, k).pin_memory()
-        items.append(dict(m=m, k=k, n=n, w=w, A=A, dA=torch.empty(m, k, device="cuda"),
-                          out=torch.empty(m * n, dtype=torch.int8, device="cuda"),
-                          hout=torch.empty(m * n, dtype=torch.int8).pin_memory()))
-        h2d += 4 * m * k
-        d2h += m * n
-
-    def step():
-        for it in items:
-            it["dA"].copy_(it["A"], non_blocking=True)
-            comp.vgemm_dev(it["dA"], it["m"], it["w"], 4, it["out"])
-            it["hout"].copy_(it["out"], non_blocking=True)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
+def e2e_model(comp, ring, w, ids, args):
+    """Through the public API with host buffers: the prompt ids come from pinned
+    host memory each step, the generated ids go back to host memory."""
+    import torch
+    host_ids = torch.tensor(ids, dtype=torch.int32).pin_memory()
+    steps = max(1, min(args.steps, 3))
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = None
     t0.record()
-    for _ in range(args.steps):
-        step()
+    for _ in range(steps):
+        prompt = host_ids.tolist()
+        if w["mode"] == "chunked":
+            picks = ring.generate_chunked(prompt, w["new"], w["chunk"], w["window"])
+            out = picks.cpu()
+        else:
+            out = ring.generate_lookahead(prompt, w["new"], w["T"], 4)
     t1.record()
     torch.cuda.synchronize()
-    comp.sync()
-    ms = t0.elapsed_time(t1) / args.steps
-    ops = sum(2.0 * m * k * n for (m, k, n) in sweep_shapes())
-    return dict(value=ops / (ms / 1e3) / 1e12, unit="TOPS", h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
-                ms_per_step=ms, path="pinned H2D f32 A -> dc_vgemm (quantizeRows + GEMM, resident weight) -> D2H int8")
+    ms = t0.elapsed_time(t1) / steps
+    n_new = w["new"]
+    return dict(value=n_new / (ms / 1e3), unit="tok/s (prompt to generated ids, prefill included)",
+                h2d_bytes_per_step=4 * len(ids), d2h_bytes_per_step=4 * n_new, ms_per_step=ms,
+                path="host ids -> infer/pipeline API (embed, stages, logits, greedy) -> host ids")
 
 
-# ---- the reference's CPU path (oracle restatement) -----------------------------
+# ---- the reference's CPU path (oracle restatement), sampled ----------------------------
+def cpu_model_rates(w: dict):
+    """Time the reference's CPU algorithm on a bounded sample of the workload:
+    one layer of this model (vgemmBlock re-quantising every weight per call, as
+    verified_core.js:430 does) for one decode row, one 16-row prefill chunk (or
+    one full window), and lm_head over 1/16 of the vocabulary, then
+    extrapolate linearly to all layers and the whole vocabulary."""
+    import numpy as np
+    import __graft_entry__ as G
+    O = G.oracle()
+    sp = w["spec"]
+    spec = O.Spec(hidden=sp["hidden"], layers=1, heads=sp["heads"], kvHeads=sp["kvHeads"], inter=sp["inter"],
+                  vocab=max(16, sp["vocab"] // 16), ropeTheta=sp["ropeTheta"], tie=False)
+    C_, q, kv, I_ = spec.hidden, spec.heads * spec.headDim, spec.kvHeads * spec.headDim, spec.inter
+    s = MODEL_SEED
+    wts = {"emb": O.synth_weight(s, -1, "emb", spec.vocab, C_), "nrmF": np.ones(C_, np.float32),
+           "lm": O.synth_weight(s, -1, "lm", C_, spec.vocab),
+           "layers": [dict(nrm1=np.ones(C_, np.float32), nrm2=np.ones(C_, np.float32),
+                           Wq=O.synth_weight(s, 0, "Wq", C_, q), Wk=O.synth_weight(s, 0, "Wk", C_, kv),
+                           Wv=O.synth_weight(s, 0, "Wv", C_, kv), Wo=O.synth_weight(s, 0, "Wo", q, C_),
+                           Wgate=O.synth_weight(s, 0, "Wgate", C_, I_), Wup=O.synth_weight(s, 0, "Wup", C_, I_),
+                           Wdown=O.synth_weight(s, 0, "Wdown", I_, C_))]}
+    m = O.Model(spec, wts, per_call_quant=True)
+    rng = np.random.default_rng(1)
+    out = {}
+    if w["mode"] == "chunked":
+        kvc = O.KV(m, 0, 1, 64)
+        x = m.embed_rows(rng.integers(0, spec.vocab, 16))
+        t = time.perf_counter()
+        y = m.run_layers(x, 0, 1, kvc, 0)
+        out["chunk_layer_s"] = time.perf_counter() - t
+        t = time.perf_counter()
+        m.run_layers(m.embed_rows([3]), 0, 1, kvc, 16)
+        out["decode_layer_s"] = time.perf_counter() - t
+        t = time.perf_counter()
+        m.logits_rows(y, [15])
+        out["lm_sample_s"] = time.perf_counter() - t
+        L, V16 = sp["layers"], 16
+        out["decode_tok_s"] = 1.0 / (L * out["decode_layer_s"] + V16 * out["lm_sample_s"])
+        out["prefill_tok_s"] = 16.0 / (L * out["chunk_layer_s"])
+    else:
+        T = w["T"]
+        x = m.embed_rows(rng.integers(0, spec.vocab, T))
+        t = time.perf_counter()
+        y = m.run_layers(x, 0, 1)
+        out["window_layer_s"] = time.perf_counter() - t
+        t = time.perf_counter()
+        m.logits_rows(y, [T - 1])
+        out["lm_sample_s"] = time.perf_counter() - t
+        out["decode_tok_s"] = 1.0 / (sp["layers"] * out["window_layer_s"] + 16 * out["lm_sample_s"])
+    return out
+
+
+def cpu_model_baseline(w):
+    t = time.perf_counter()
+    r = cpu_model_rates(w)
+    wall = time.perf_counter() - t
+    return dict(value=r["decode_tok_s"], unit="tok/s (decode)", cores=1, kind="port",
+                prefill_tok_s=r.get("prefill_tok_s"),
+                sample="one layer of this model through the C restatement of verified_core.js/infer.js "
+                       "(weights re-quantised per call as vgemmBlock does) for one decode row and one 16-row chunk "
+                       "(or one full window), lm_head over 1/16 of the vocabulary; extrapolated to every layer and "
+                       f"the whole vocabulary; {wall:.1f} s of CPU work, one thread (the reference's JS path is "
+                       "single-threaded)", detail=r)
+
+
+def bench_reference(args, rank, world):
+    """The reference's CPU implementation of the path, timed on this host."""
+    if rank != 0:
+        return None
+    if args.workload == "gemm-sweep":
+        vals = [cpu_sweep_rate(1)[0] for _ in range(max(1, args.steps))]
+        v = statistics.median(vals)
+        ops_step = sum(2.0 * m * k * n for (m, k, n) in sweep_shapes())
+        ms = ops_step / (v * 1e12) * 1e3
+        unit = "TOPS (int8 ops/s, GEMM sweep)"
+        extra = {}
+    else:
+        w = WORKLOADS[args.workload]
+        rs = [cpu_model_rates(w) for _ in range(max(1, min(args.steps, 2)))]
+        v = statistics.median(r["decode_tok_s"] for r in rs)
+        ms = w["new"] / v * 1e3
+        unit = "tok/s (decode)"
+        extra = dict(prefill_tok_s=statistics.median(r["prefill_tok_s"] for r in rs) if "prefill_tok_s" in rs[0]
+                     else None)
+    sample = ("one layer + 1/16 of lm_head per sample through the C restatement (per-call weight "
+              "quantisation, LUT GEMM), extrapolated to the whole model" if args.workload != "gemm-sweep" else
+              "per (K,N): one per-call quantizeCols + 2 LUT-GEMM rows, extrapolated to the 16 shapes")
+    return dict(metric=METRIC, impl="reference", value=v, unit=unit, n_gpus=world, steps=args.steps,
+                warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="strong", vs_baseline=None,
+                dtype="int8 x int8 -> int32", data="synthetic (seeded)", config=dict(workload=args.workload),
+                cpu_baseline=dict(value=v, unit=unit, cores=1, kind="port", sample=sample),
+                e2e=dict(value=v, unit=unit, h2d_bytes_per_step=0, d2h_bytes_per_step=0), **extra)
+
+
+# ---- the GEMM sweep -----------------------------------------------------------------
+def sweep_shapes():
+    return [(m, k, n) for (k, n) in SWEEP_KN for m in SWEEP_M]
+
+
 def _cpu_shape_worker(args):
-    """Time vgemmBlock's CPU path on one (K, N): quantizeCols of the whole weight
-    (per call, as verified_core.js:430 does) and `rows` rows of quantizeRows +
-    the LUT triple loop.  Returns (t_qcols, t_per_row)."""
     k, n, rows, seed = args
     import numpy as np
     import __graft_entry__ as G
@@ -322,91 +479,129 @@ def _cpu_shape_worker(args):
     t = time.perf_counter()
     xq, xs = O.quantize_rows(A, rows, k)
     O.bgemm(xq, wq, xs, ws, rows, k, n, 1, O.REQUANT)
-    tr = (time.perf_counter() - t) / rows
-    return tq, tr
+    return tq, (time.perf_counter() - t) / rows
 
 
 def cpu_sweep_rate(threads: int, rows: int = 2):
-    """Sweep throughput of the reference CPU algorithm, extrapolated from a
-    bounded sample: per (K,N) one quantizeCols + `rows` LUT-GEMM rows."""
     jobs = [(k, n, rows, i) for i, (k, n) in enumerate(SWEEP_KN)]
     t0 = time.perf_counter()
-    if threads > 1:
-        import multiprocessing as mp
-        with mp.get_context("spawn").Pool(min(threads, len(jobs))) as pool:
-            res = pool.map(_cpu_shape_worker, jobs)
-    else:
-        res = [_cpu_shape_worker(j) for j in jobs]
+    res = [_cpu_shape_worker(j) for j in jobs]
     wall = time.perf_counter() - t0
-    total_t = 0.0
-    for (k, n), (tq, tr) in zip(SWEEP_KN, res):
-        for m in SWEEP_M:
-            total_t += tq + m * tr
+    total_t = sum(tq + m * tr for (k, n), (tq, tr) in zip(SWEEP_KN, res) for m in SWEEP_M)
     ops = sum(2.0 * m * k * n for (m, k, n) in sweep_shapes())
     return ops / total_t / 1e12, wall
 
 
-def cpu_baseline_sweep(threads=1):
-    v, wall = cpu_sweep_rate(threads)
-    return dict(value=v, unit="TOPS", cores=threads, kind="port",
-                sample=f"per (K,N): one per-call quantizeCols + 2 rows of quantizeRows + LUT GEMM "
-                       f"(C restatement of verified_core.js, single thread), extrapolated to the 16 shapes; "
-                       f"{wall:.1f} s of CPU work")
+def bench_gemm_sweep(args, rank, world, peaks):
+    import torch
+    import __graft_entry__ as G
+    P = G.package()
+    comp = P.init_compute(int(os.environ.get("LOCAL_RANK", "0")), stream=torch.cuda.current_stream())
+    g = torch.Generator(device="cuda").manual_seed(2026)
+    items = []
+    for (m, k, n) in sweep_shapes():
+        ld = (k + 15) // 16 * 16
+        copies = max(3, math.ceil(3 * L2_BYTES / (n * ld)))
+        W = torch.randint(-127, 128, (copies, n, ld), generator=g, device="cuda", dtype=torch.int8)
+        if ld != k:
+            W[:, :, k:] = 0
+        items.append(dict(m=m, k=k, n=n, ld=ld, A=torch.randn(m, k, generator=g, device="cuda"), W=W,
+                          cs=torch.rand(copies, n, generator=g, device="cuda") * 9e-3 + 1e-3, copies=copies,
+                          xq=torch.zeros(m, ld, dtype=torch.int8, device="cuda"), rs=torch.empty(m, device="cuda"),
+                          out=torch.empty(m * n, dtype=torch.int8, device="cuda")))
 
+    def step(s):
+        for it in items:
+            c = s % it["copies"]
+            comp.quantize_rows_dev(it["A"], it["m"], it["k"], it["xq"], it["ld"], it["rs"])
+            comp.bgemm_dev(it["xq"], it["ld"], it["W"][c], it["ld"], it["rs"], it["cs"][c], it["m"], it["k"],
+                           it["n"], 1, 4, it["out"])
 
-def bench_reference(args, rank, world):
-    if rank != 0:
-        return None
-    threads = os.cpu_count() or 1
-    vals = []
-    for s in range(args.warmup + args.steps):
-        # each step a bounded sample of the sweep spread over the host cores
-        v, _ = cpu_sweep_rate(min(threads, len(SWEEP_KN)), rows=1)
-        if s >= args.warmup:
-            vals.append(v)
-    v = statistics.median(vals)
+    for s in range(args.warmup):
+        step(s)
+    comp.sync()
+    l0 = comp.L.dc_launch_count()
+    clocks = Clocks(int(os.environ.get("LOCAL_RANK", "0")))
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    comp.L.dc_timing(comp.h, 1)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for s in range(args.steps):
+        step(args.warmup + s)
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.mark_end()
+    barrier(world)
+    clk = clocks.stop()
+    import ctypes as C
+    per = {}
+    for kind in (1, 3):
+        ms, n, by, op = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
+        comp.L.dc_timing_read(comp.h, kind, C.byref(ms), C.byref(n), C.byref(by), C.byref(op))
+        per[kind] = (ms.value, n.value, by.value, op.value)
+    comp.L.dc_timing(comp.h, 0)
+    ms = max_over_ranks([t0.elapsed_time(t1) / args.steps], world)[0]
     ops_step = sum(2.0 * m * k * n for (m, k, n) in sweep_shapes())
-    ms = ops_step / (v * 1e12) * 1e3
-    return dict(metric=METRIC, impl="reference", value=v, unit="TOPS (int8 ops/s, GEMM sweep)", n_gpus=world,
-                steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak",
-                vs_baseline=None, dtype="int8 x int8 -> int32", data="synthetic (seeded)",
-                config=dict(workload="gemm-sweep (same shapes)", parallelism="host cores"),
-                cpu_baseline=dict(value=v, unit="TOPS", cores=min(threads, len(SWEEP_KN)), kind="port",
-                                  sample="per (K,N): one per-call quantizeCols + 1 LUT-GEMM row per step, "
-                                         "extrapolated; one process per (K,N)"),
-                e2e=dict(value=v, unit="TOPS", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
-
-
-def traffic_for(key):
-    p = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(p):
-        d = json.load(open(p))
-        return d.get(key)
-    return None
+    dom = max(per, key=lambda k: per[k][0])
+    tms, n, by, op = per[dom]
+    i8_peak = 2.0 * peaks["bf16_tflops"]
+    roof = dict(bound="tensor" if dom == 3 else "hbm",
+                achieved=(op / (tms / 1e3) / 1e12) if dom == 3 else by / (tms / 1e3) / 1e9,
+                peak=i8_peak if dom == 3 else peaks["hbm_gbs"], unit="TOPS" if dom == 3 else "GB/s",
+                traffic=None, kernel="k_gemm_tc" if dom == 3 else "k_gemv",
+                peak_source=("2 x measured bf16 dense TFLOP/s (int8 dense = 2 x bf16)" if dom == 3
+                             else "measured HBM copy bandwidth"))
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    line = None
+    if rank == 0:
+        line = dict(metric=METRIC, value=ops_step * world / (ms / 1e3) / 1e12, unit="TOPS (int8 ops/s, GEMM sweep)",
+                    n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True,
+                    scaling="weak", vs_baseline=None, dtype="int8 x int8 -> int32", data="synthetic (seeded)",
+                    config=dict(workload="gemm-sweep", cold_l2="weight copies per shape > 3x L2, rotated",
+                                parallelism=f"replicas x{world}"),
+                    roofline=roof, gpu_launches=comp.L.dc_launch_count() - l0, clocks=clk, backend=comp.label,
+                    kernels={("gemv" if k == 1 else "tcgen05"): dict(ms=v[0], launches=v[1]) for k, v in per.items()})
+        if world == 1 and not args.no_cpu:
+            v, wall = cpu_sweep_rate(1)
+            line["cpu_baseline"] = dict(value=v, unit="TOPS", cores=1, kind="port",
+                                        sample=f"per (K,N): one per-call quantizeCols + 2 LUT-GEMM rows, "
+                                               f"extrapolated; {wall:.1f} s")
+    return line
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemm-sweep", choices=["gemm-sweep"])
+    ap.add_argument("--workload", default="llama3-8b-chunked", choices=list(WORKLOADS) + ["gemm-sweep"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--prompt-len", type=int, default=0, help="override the prompt length (profiling runs)")
+    ap.add_argument("--new-tokens", type=int, default=0, help="override the generated tokens (profiling runs)")
     args = ap.parse_args()
+    if args.workload in WORKLOADS:
+        w = WORKLOADS[args.workload]
+        if args.prompt_len and w["prompt"] != "ngram":
+            w["prompt"] = args.prompt_len
+        if args.new_tokens:
+            w["new"] = args.new_tokens
     args.warmup = max(args.warmup, 3)
     peaks = load_peaks()
     if args.impl == "reference":
-        rank = int(os.environ.get("RANK", "0"))
-        world = int(os.environ.get("WORLD_SIZE", "1"))
-        line = bench_reference(args, rank, world)
+        line = bench_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         if line is not None:
             print(json.dumps(line), flush=True)
         return
     rank, local, world = dist_init()
-    line = bench_gemm_sweep(args, rank, world, peaks)
-    if rank == 0:
+    if args.workload == "gemm-sweep":
+        line = bench_gemm_sweep(args, rank, world, peaks)
+    else:
+        line = bench_model(args, rank, world, peaks)
+    if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

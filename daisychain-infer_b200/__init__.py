@@ -8,3 +8,4 @@ public/verified_core.js's contract, public/infer.js's stage API).
 from ._lib import AccumulatorBoundError, DeviceError, NonFiniteError  # noqa: F401
 from .compute import Compute, Weight, init_compute  # noqa: F401
 from . import infer, shard  # noqa: E402,F401
+from . import pipeline  # noqa: E402,F401

@@ -57,6 +57,9 @@ SIGNATURES = [
     ("dc_stream", _p, [_p]),
     ("dc_set_stream", _i, [_p, _p]),
     ("dc_tc_enabled", _i, [_p]),
+    ("dc_launch_count", C.c_ulonglong, []),
+    ("dc_timing", _i, [_p, _i]),
+    ("dc_timing_read", _i, [_p, _i, C.POINTER(_d), C.POINTER(C.c_longlong), C.POINTER(_d), C.POINTER(_d)]),
     ("dc_luts", _i, [_p, _p, _p, _p]),
     ("dc_sync", _i, [_p]),
     ("dc_bgemm", _i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _u, _p]),

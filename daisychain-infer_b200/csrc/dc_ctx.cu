@@ -13,6 +13,7 @@
 //    off (the SIMT kernel takes its shapes); any other failure fails dc_init.
 #include <math.h>
 
+#include <atomic>
 #include <vector>
 
 #include "dc_internal.cuh"
@@ -230,6 +231,10 @@ thread_local std::string g_init_error;
 
 extern "C" const char* dc_init_error(void) { return g_init_error.c_str(); }
 
+static std::atomic<unsigned long long> g_launches{0};
+void dc_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+extern "C" unsigned long long dc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
 extern "C" int dc_set_stream(dc_ctx* c, void* stream) {
   if (!c) return DC_E_INVAL;
   DC_CUDA(c, cudaStreamSynchronize(c->stream));
@@ -311,6 +316,11 @@ extern "C" void dc_destroy(dc_ctx* c) {
   cudaFree(c->scratch);
   cudaFree(c->tc_partial);
   cudaFree(c->tc_counters);
+  for (auto& t : c->timed) {
+    cudaEventDestroy(t.a);
+    cudaEventDestroy(t.b);
+  }
+  for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
 }

@@ -180,7 +180,7 @@ int launch_gemv(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ld
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   dim3 grid(blocks, batch);
-  k_gemv<MR><<<grid, 256, smem, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant, ctx->d_relu, out);
+  k_gemv<MR><<<grid, 256, smem, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant, ctx->d_relu, out); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }
@@ -208,15 +208,84 @@ int dc_gemm_lut(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs
   if (m == 0 || n == 0) return DC_OK;
   dim3 blk(8, 8);
   dim3 grid((m + 7) / 8, (n + 7) / 8, batch);
-  k_lut_gemm<<<grid, blk, 0, st>>>(Xq, Wq, rs, cs, m, k, n, flags, ctx->d_mul, ctx->d_requant, ctx->d_relu, out);
+  k_lut_gemm<<<grid, blk, 0, st>>>(Xq, Wq, rs, cs, m, k, n, flags, ctx->d_mul, ctx->d_requant, ctx->d_relu, out); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }
 
+static int gemm_dispatch_impl(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                              const float* cs, int m, int k, int n, int batch, unsigned flags, void* out,
+                              cudaStream_t st, int kind);
+
+static cudaEvent_t timing_event(dc_ctx* ctx) {
+  cudaEvent_t e = nullptr;
+  if (!ctx->event_pool.empty()) {
+    e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+  } else if (cudaEventCreate(&e) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return e;
+}
+
+// With timing on (dc_timing), every GEMM launch is bracketed by CUDA events on
+// its own stream and its algorithmic bytes and ops are recorded.
 int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
                      const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
                      int kind) {
   if (m == 0 || n == 0 || batch == 0) return DC_OK;
+  if (!ctx->timing) return gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind);
+  dc_timed t;
+  t.a = timing_event(ctx);
+  t.b = timing_event(ctx);
+  t.kind = (kind == 0) ? (m <= 8 ? 1 : 3) : kind;
+  const double ob = (flags & DC_ACC) ? 4 : (flags & DC_REQUANT) ? 1 : 4;
+  t.bytes = (double)batch * ((double)m * k + (double)k * n + 4.0 * m + 4.0 * n + ob * m * n);
+  t.ops = 2.0 * batch * (double)m * n * k;
+  if (t.a) cudaEventRecord(t.a, st);
+  int rc = gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind);
+  if (t.b) cudaEventRecord(t.b, st);
+  if (t.a && t.b) ctx->timed.push_back(t);
+  return rc;
+}
+
+extern "C" int dc_timing(dc_ctx* ctx, int on) {
+  if (!ctx) return DC_E_INVAL;
+  for (auto& t : ctx->timed) {
+    ctx->event_pool.push_back(t.a);
+    ctx->event_pool.push_back(t.b);
+  }
+  ctx->timed.clear();
+  ctx->timing = on != 0;
+  return DC_OK;
+}
+
+extern "C" int dc_timing_read(dc_ctx* ctx, int kind, double* ms, long long* launches, double* bytes, double* ops) {
+  if (!ctx) return DC_E_INVAL;
+  DC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  double tms = 0, tb = 0, to = 0;
+  long long n = 0;
+  for (auto& t : ctx->timed) {
+    if (t.kind != kind) continue;
+    float e = 0;
+    DC_CUDA(ctx, cudaEventSynchronize(t.b));
+    DC_CUDA(ctx, cudaEventElapsedTime(&e, t.a, t.b));
+    tms += e;
+    tb += t.bytes;
+    to += t.ops;
+    n++;
+  }
+  if (ms) *ms = tms;
+  if (launches) *launches = n;
+  if (bytes) *bytes = tb;
+  if (ops) *ops = to;
+  return DC_OK;
+}
+
+static int gemm_dispatch_impl(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                              const float* cs, int m, int k, int n, int batch, unsigned flags, void* out,
+                              cudaStream_t st, int kind) {
   if (kind == 0) kind = (m <= 8) ? 1 : 3;
   if (kind == 3) {
     if (ctx->tc_enabled) {
@@ -233,7 +302,7 @@ int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, i
     kind = 2;
   }
   dim3 grid((n + 63) / 64, (m + 63) / 64, batch);
-  k_gemm_simt<<<grid, 256, 0, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant, ctx->d_relu, out);
+  k_gemm_simt<<<grid, 256, 0, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant, ctx->d_relu, out); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }

@@ -361,7 +361,7 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
   a.status = ctx->d_status;
   DC_CUDA(ctx, cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
   dim3 grid(a.n_tiles, a.m_tiles, batch * splits);
-  k_gemm_tc<BN><<<grid, 128, C::SMEM, st>>>(mW, mX, a);
+  k_gemm_tc<BN><<<grid, 128, C::SMEM, st>>>(mW, mX, a); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }

@@ -14,6 +14,14 @@
 #define DC_ST_TIMEOUT 2
 #define DC_ST_BOUNDS 4
 
+#include <vector>
+
+struct dc_timed {
+  cudaEvent_t a = nullptr, b = nullptr;
+  int kind = 0;  // 1 GEMV, 2 SIMT, 3 tcgen05
+  double bytes = 0, ops = 0;
+};
+
 struct dc_ctx {
   int device = 0;
   int sm_count = 148;
@@ -37,6 +45,10 @@ struct dc_ctx {
   int32_t* tc_partial = nullptr;
   int* tc_counters = nullptr;
   size_t tc_partial_cap = 0, tc_counter_cap = 0;
+  // live GEMM timing (dc_timing / dc_timing_read)
+  bool timing = false;
+  std::vector<dc_timed> timed;
+  std::vector<cudaEvent_t> event_pool;
 };
 
 struct dc_weight {
@@ -60,6 +72,9 @@ int dc_cuda_fail(dc_ctx* ctx, cudaError_t e, const char* what);
   } while (0)
 
 int dc_scratch(dc_ctx* ctx, size_t bytes, void** p);
+
+// Kernels launched by this library in this process (reported by dc_launch_count).
+void dc_count_launch();
 
 // ---- launchers shared between translation units ----------------------------
 int dc_launch_quant_rows(dc_ctx* ctx, const float* X, int rows, int cols, int8_t* q, int ldq, float* s,

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(256) k_transpose_i8(const int8_t* __restrict__
 int dc_launch_quant_rows(dc_ctx* ctx, const float* X, int rows, int cols, int8_t* q, int ldq, float* s,
                          cudaStream_t st) {
   if (rows <= 0) return DC_OK;
-  k_quant_rows<<<rows, 256, 0, st>>>(X, rows, cols, q, ldq, s, ctx->d_status);
+  k_quant_rows<<<rows, 256, 0, st>>>(X, rows, cols, q, ldq, s, ctx->d_status); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }
@@ -126,10 +126,10 @@ int dc_launch_quant_rows(dc_ctx* ctx, const float* X, int rows, int cols, int8_t
 int dc_launch_quant_cols_t(dc_ctx* ctx, const float* W, int rows, int cols, int8_t* qt, int ldq, float* s,
                            cudaStream_t st) {
   if (cols <= 0) return DC_OK;
-  k_col_scales<<<(cols + 255) / 256, 256, 0, st>>>(W, rows, cols, s, ctx->d_status);
+  k_col_scales<<<(cols + 255) / 256, 256, 0, st>>>(W, rows, cols, s, ctx->d_status); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   dim3 grid((cols + 31) / 32, (ldq + 31) / 32);
-  k_quant_cols_t<<<grid, 256, 0, st>>>(W, rows, cols, s, qt, ldq);
+  k_quant_cols_t<<<grid, 256, 0, st>>>(W, rows, cols, s, qt, ldq); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }
@@ -138,7 +138,7 @@ int dc_launch_transpose_i8(dc_ctx* ctx, const int8_t* W, int k, int n, int8_t* W
                            cudaStream_t st) {
   if (n <= 0 || batch <= 0) return DC_OK;
   dim3 grid((n + 31) / 32, (ldw + 31) / 32, batch);
-  k_transpose_i8<<<grid, 256, 0, st>>>(W, k, n, Wt, ldw);
+  k_transpose_i8<<<grid, 256, 0, st>>>(W, k, n, Wt, ldw); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }

@@ -536,10 +536,10 @@ static int mat_load(dc_stage* S, dc_mat& m, int col0, const WSrc& src, int n_src
   cudaStream_t st = S->ctx->stream;
   float* s = m.cs + col0;
   int8_t* qt = m.qt + (int64_t)col0 * m.ldk;
-  k_wscale<<<(n_src + 255) / 256, 256, 0, st>>>(src, m.k, n_src, s, S->ctx->d_status);
+  k_wscale<<<(n_src + 255) / 256, 256, 0, st>>>(src, m.k, n_src, s, S->ctx->d_status); dc_count_launch();
   DC_CUDA(S->ctx, cudaGetLastError());
   dim3 grid((n_src + 31) / 32, (m.ldk + 31) / 32);
-  k_wquant_t<<<grid, 256, 0, st>>>(src, m.k, n_src, s, qt, m.ldk);
+  k_wquant_t<<<grid, 256, 0, st>>>(src, m.k, n_src, s, qt, m.ldk); dc_count_launch();
   DC_CUDA(S->ctx, cudaGetLastError());
   return DC_OK;
 }
@@ -738,8 +738,8 @@ extern "C" int dc_stage_synth(dc_stage* S, uint64_t model_seed, double factor) {
   int rc = DC_OK;
   for (int l = S->lo; l < S->hi && !rc; l++) {
     dc_layer& ly = S->L[l - S->lo];
-    k_fill_f32<<<8, 256, 0, ctx->stream>>>(ly.nrm1, S->C, 1.0f);
-    k_fill_f32<<<8, 256, 0, ctx->stream>>>(ly.nrm2, S->C, 1.0f);
+    k_fill_f32<<<8, 256, 0, ctx->stream>>>(ly.nrm1, S->C, 1.0f); dc_count_launch();
+    k_fill_f32<<<8, 256, 0, ctx->stream>>>(ly.nrm2, S->C, 1.0f); dc_count_launch();
     rc = mat_load(S, ly.qkv, 0, src(l, 3, S->C, S->qDim), S->qDim);
     if (!rc) rc = mat_load(S, ly.qkv, S->qDim, src(l, 4, S->C, S->kvDim), S->kvDim);
     if (!rc) rc = mat_load(S, ly.qkv, S->qDim + S->kvDim, src(l, 5, S->C, S->kvDim), S->kvDim);
@@ -750,8 +750,8 @@ extern "C" int dc_stage_synth(dc_stage* S, uint64_t model_seed, double factor) {
   }
   if (!rc && S->head) {
     WSrc e = src(-1, 1, S->V, S->C);
-    k_synth_f32<<<1024, 256, 0, ctx->stream>>>(e, S->V, S->C, S->emb);
-    k_fill_f32<<<8, 256, 0, ctx->stream>>>(S->nrmF, S->C, 1.0f);
+    k_synth_f32<<<1024, 256, 0, ctx->stream>>>(e, S->V, S->C, S->emb); dc_count_launch();
+    k_fill_f32<<<8, 256, 0, ctx->stream>>>(S->nrmF, S->C, 1.0f); dc_count_launch();
     if (S->spec.tie) {
       WSrc t = e;  // embᵀ: element (c, v) = emb index v*C + c
       t.transposed = 1;
@@ -778,7 +778,7 @@ extern "C" int dc_stage_kv_len(const dc_stage* S) { return S ? S->kv_len : -1; }
 extern "C" int dc_stage_embed(dc_stage* S, const int32_t* ids, int T, float* x) {
   if (!S || !S->head || T < 1 || T > S->max_rows || !ids || !x)
     return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_embed: bad arguments");
-  k_embed<<<T, 256, 0, S->ctx->stream>>>(ids, T, S->emb, S->C, S->V, x, S->ctx->d_status);
+  k_embed<<<T, 256, 0, S->ctx->stream>>>(ids, T, S->emb, S->C, S->V, x, S->ctx->d_status); dc_count_launch();
   DC_CUDA(S->ctx, cudaGetLastError());
   return DC_OK;
 }
@@ -814,28 +814,28 @@ extern "C" int dc_stage_forward(dc_stage* S, float* x, int T, int pos0, int use_
     dc_kv& kv = ly.kv;
     // attention block
     k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm1, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status);
+                                                         ctx->d_status); dc_count_launch();
     if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf))) return rc;
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
     k_rope_append<<<T, 128, 4 * (size_t)S->kvDim, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos,
                                                           S->rope_sin, pos0, n0, S->max_pos, kv.k8, kv.ks, kv.v,
-                                                          kv.vmax, ctx->d_status);
-    k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0 == 0 ? 1 : 0);
+                                                          kv.vmax, ctx->d_status); dc_count_launch();
+    k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0 == 0 ? 1 : 0); dc_count_launch();
     dim3 vq((N + 63) / 64, (S->kvDim + 31) / 32);
-    k_vquant<<<vq, 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8, N, n0, S->kvDim, S->hd, S->max_pos);
+    k_vquant<<<vq, 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8, N, n0, S->kvDim, S->hd, S->max_pos); dc_count_launch();
     dim3 ag(S->nH, T);
     k_attention<<<ag, ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8, kv.vs,
-                                                   N, n0, S->max_pos, scale, S->ctxo, S->qDim, ctx->d_status);
+                                                   N, n0, S->max_pos, scale, S->ctxo, S->qDim, ctx->d_status); dc_count_launch();
     if ((rc = dc_launch_quant_rows(ctx, S->ctxo, T, S->qDim, S->xq, S->ldQ, S->rs, st))) return rc;
     if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, S->hbuf))) return rc;
-    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C);
+    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C); dc_count_launch();
     // MLP block
     k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm2, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status);
+                                                         ctx->d_status); dc_count_launch();
     if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf))) return rc;
-    k_swiglu_quant<<<T, NORM_THREADS, swi_smem, st>>>(S->hbuf, S->I, S->xq, S->ldI, S->rs, ctx->d_status);
+    k_swiglu_quant<<<T, NORM_THREADS, swi_smem, st>>>(S->hbuf, S->I, S->xq, S->ldI, S->rs, ctx->d_status); dc_count_launch();
     if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, S->hbuf))) return rc;
-    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C);
+    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C); dc_count_launch();
     DC_CUDA(ctx, cudaGetLastError());
   }
   if (use_kv) S->kv_len = N;
@@ -857,11 +857,14 @@ extern "C" int dc_stage_logits(dc_stage* S, const float* x, int T, const int32_t
                                  cudaMemcpyDeviceToDevice, st));
   const size_t nrm_smem = 4 * (size_t)S->C;
   k_rmsnorm_quant<<<nrows, NORM_THREADS, nrm_smem, st>>>(S->lx, S->C, S->nrmF, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                          ctx->d_status);
+                                                          ctx->d_status); dc_count_launch();
   int rc = dc_gemm_dispatch(ctx, S->xq, S->ldC, S->lm.qt, S->lm.ldk, S->rs, S->lm.cs, nrows, S->C, S->V, 1, 0,
                             logits, st, 0);
   if (rc) return rc;
-  if (picks) k_argmax<<<nrows, 1024, 0, st>>>(logits, S->V, picks);
+  if (picks) {
+    k_argmax<<<nrows, 1024, 0, st>>>(logits, S->V, picks);
+    dc_count_launch();
+  }
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }

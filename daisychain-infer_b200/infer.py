@@ -166,6 +166,30 @@ class Stage:
         picks = self._picks[: r.size].cpu().tolist()
         return picks, self._logits[: r.size * self.spec.vocab].view(r.size, self.spec.vocab)
 
+    # ---- device-resident token ids (no host round trip per decode lap) ------------
+    def new_ids(self, n: int):
+        return self.torch.zeros(max(n, 1), dtype=self.torch.int32, device=self.dev)
+
+    def ids_buffer(self, n: int):
+        return self.torch.zeros(n, dtype=self.torch.int32, device=self.dev)
+
+    def pick_into(self, x, row: int, picks, n: int) -> None:
+        """Greedy pick of one row of x written to picks[n] on the device."""
+        T = x.numel() // self.spec.hidden
+        r = np.array([row], np.int32)
+        self._check(self.L.dc_stage_logits(self.h, _ptr(x), T, _ptr(r), 1, _ptr(self._logits),
+                                           C.c_void_p(picks.data_ptr() + 4 * n)), "logitsAt")
+
+    def embed_device(self, picks, n: int):
+        """embedRows of the single id picks[n] (a device int32)."""
+        x = self.torch.empty(self.spec.hidden, dtype=self.torch.float32, device=self.dev)
+        self._check(self.L.dc_stage_embed(self.h, C.c_void_p(picks.data_ptr() + 4 * n), 1, _ptr(x)), "stage_embed")
+        return x
+
+    def broadcast_ids(self, buf) -> None:
+        import torch.distributed as dist
+        dist.broadcast(buf, src=0)
+
     def kv_reset(self) -> None:
         self._check(self.L.dc_stage_kv_reset(self.h), "kv_reset")
 

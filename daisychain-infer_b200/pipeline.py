@@ -1,0 +1,205 @@
+"""Pipeline stages on 1..8 GPUs of one box: the reference's ring, over NVLink.
+
+The reference hands a T x hidden f32 activation from stage to stage over
+WebRTC (public/app.js:705-765, 877-961; wire.js routing :129-138): stage 0 (the
+head) embeds, runs its layers and sends; every stage runs its layers and
+forwards; the last stage returns to the head, which reads the logits.  Here
+each stage is one process on one GPU (torch.distributed, NCCL point-to-point
+send/recv of the same f32 buffer), and the lap never leaves the devices:
+
+* chunked prefill (app.js:877-906): prompt chunks from ``prefill_chunks``;
+  the head keeps ``window`` (2) chunks in flight, so chunk c+1 runs on stage 0
+  while chunk c runs on stage 1; every stage applies its chunks in order and
+  appends to its own KV cache;
+* decode (app.js:907-921): one token per lap; the head's greedy pick stays on
+  the device and feeds the next embedding, so a lap needs no host round trip;
+* full-window / lookahead laps (app.js:925-961): the head embeds the window,
+  the lap returns the hidden state, the head scores the draft rows.
+
+``Ring`` is written against two small interfaces so its schedule can be tested
+on CPU ranks (gloo) with a stand-in stage: a stage with
+``embed_rows / run_layers / run_layers_chunk / logits_at`` and a transport
+with ``send(tensor, dst) / recv(tensor, src)``.
+"""
+from __future__ import annotations
+
+from . import shard
+
+RETURN = -1  # wire.js:29: the head's return leg is not "stage 0"
+
+
+def route_after(plan: list, my_index: int) -> dict:
+    """wire.js:129-133."""
+    is_last = my_index == len(plan) - 1
+    nxt = plan[0] if is_last else plan[my_index + 1]
+    return dict(to=nxt["id"], address=RETURN if is_last else nxt["index"], isReturn=is_last)
+
+
+def classify_act(next_index: int, my_index: int) -> str:
+    """wire.js:134-138."""
+    if next_index == RETURN:
+        return "return"
+    if next_index == my_index:
+        return "mine"
+    return "other"
+
+
+class TorchP2P:
+    """Point-to-point transport over torch.distributed (NCCL on GPUs, gloo on CPU)."""
+
+    def __init__(self):
+        import torch.distributed as dist
+        self.dist = dist
+
+    def send(self, t, dst: int):
+        return self.dist.isend(t, dst)
+
+    def recv(self, t, src: int):
+        return self.dist.irecv(t, src)
+
+
+class Ring:
+    """One rank's part of the lap.  ``stage`` holds this rank's layers; rank 0
+    is the head.  Every rank runs the same schedule (same chunk list, same
+    number of decode laps), so no control messages are needed."""
+
+    def __init__(self, stage, rank: int, world: int, hidden: int, transport=None, device=None, new_buffer=None):
+        self.stage, self.rank, self.world, self.hidden = stage, rank, world, hidden
+        self.tp = transport
+        self.nxt = (rank + 1) % world
+        self.prv = (rank - 1) % world
+        self.new_buffer = new_buffer  # new_buffer(n_floats) -> tensor on this rank's device
+
+    # ---- chunked prefill + decode --------------------------------------------------
+    def generate_chunked(self, ids0: list, n_new: int, chunk_size: int = 16, window: int = 2, on_prefill=None):
+        """Returns the device tensor of picked ids on the head (n_new int32), None elsewhere.
+        ``on_prefill`` (optional) is called on the head when the prefill lap is complete."""
+        S, H = self.stage, self.hidden
+        S.kv_reset()
+        chunks = shard.prefill_chunks(len(ids0), chunk_size, window)
+        last = None
+        if self.world == 1:
+            for ch in chunks["chunks"]:
+                last = S.run_layers_chunk(S.embed_rows(ids0[ch["lo"]:ch["hi"]]), ch["lo"])
+            if on_prefill:
+                on_prefill()
+            return self._decode_local(last, len(ids0), n_new)
+        if self.rank == 0:
+            flights = []
+            for ch in chunks["chunks"]:
+                x = S.run_layers_chunk(S.embed_rows(ids0[ch["lo"]:ch["hi"]]), ch["lo"])
+                sent = self.tp.send(x, self.nxt)  # the handle keeps the send (and x) alive
+                back = self.new_buffer((ch["hi"] - ch["lo"]) * H)
+                flights.append((sent, self.tp.recv(back, self.prv), back))
+                if len(flights) >= chunks["window"]:
+                    sent_, req, buf = flights.pop(0)
+                    sent_.wait()
+                    req.wait()
+                    last = buf
+            while flights:
+                sent_, req, buf = flights.pop(0)
+                sent_.wait()
+                req.wait()
+                last = buf
+            if on_prefill:
+                on_prefill()
+            return self._decode_head(last, len(ids0), n_new)
+        # a middle or last stage: chunks arrive in order (the inbox of app.js:719-749)
+        pending = []
+        for ch in chunks["chunks"]:
+            buf = self.new_buffer((ch["hi"] - ch["lo"]) * H)
+            self.tp.recv(buf, self.prv).wait()
+            S.run_layers_chunk(buf, ch["lo"])
+            pending.append(self.tp.send(buf, self.nxt))
+        for n in range(n_new):
+            buf = self.new_buffer(H)
+            self.tp.recv(buf, self.prv).wait()
+            S.run_layers_chunk(buf, len(ids0) + n)
+            pending.append(self.tp.send(buf, self.nxt))
+        for p in pending:
+            p.wait()
+        return None
+
+    def _decode_local(self, last, n_prompt: int, n_new: int):
+        S = self.stage
+        picks = S.new_ids(n_new)
+        for n in range(n_new):
+            rows = last.numel() // self.hidden
+            S.pick_into(last, rows - 1, picks, n)
+            last = S.run_layers_chunk(S.embed_device(picks, n), n_prompt + n)
+        return picks
+
+    def _decode_head(self, last, n_prompt: int, n_new: int):
+        S = self.stage
+        picks = S.new_ids(n_new)
+        for n in range(n_new):
+            rows = last.numel() // self.hidden
+            S.pick_into(last, rows - 1, picks, n)
+            x = S.run_layers_chunk(S.embed_device(picks, n), n_prompt + n)
+            sent = self.tp.send(x, self.nxt)
+            back = self.new_buffer(self.hidden)
+            self.tp.recv(back, self.prv).wait()
+            sent.wait()
+            last = back
+        return picks
+
+    # ---- full-window laps ------------------------------------------------------------
+    def window_lap(self, win_ids: list):
+        """One full-window lap; the head gets the returned hidden state."""
+        S, H, T = self.stage, self.hidden, len(win_ids)
+        if self.rank == 0:
+            x = S.run_layers(S.embed_rows(win_ids))
+            if self.world == 1:
+                return x
+            sent = self.tp.send(x, self.nxt)
+            back = self.new_buffer(T * H)
+            self.tp.recv(back, self.prv).wait()
+            sent.wait()
+            return back
+        buf = self.new_buffer(T * H)
+        self.tp.recv(buf, self.prv).wait()
+        S.run_layers(buf)
+        self.tp.send(buf, self.nxt).wait()
+        return None
+
+    def generate_lookahead(self, ids0: list, n_new: int, T: int, max_draft: int = 4):
+        """infer.js:464-494 across the ring.  Every rank needs the window size of
+        each lap, so the head shares the accepted count over the transport."""
+        ids = list(ids0)
+        produced = 0
+        S = self.stage
+        while produced < n_new:
+            frame = shard.lookahead_frame(ids, T, max_draft)
+            draft = frame["draft"]
+            win = [0] * (T - len(frame["win"])) + frame["win"]
+            x = self.window_lap(win)
+            got = None
+            if self.rank == 0:
+                rows = shard.draft_rows(T, frame["shown"], len(draft))
+                picked, _ = S.logits_at(x, rows)
+                got = shard.accept_draft(picked, draft)
+            got = self._share_ids(got)
+            if not got:
+                break
+            for t in got:
+                ids.append(t)
+                produced += 1
+                if produced >= n_new:
+                    break
+        return ids
+
+    def _share_ids(self, got):
+        if self.world == 1:
+            return got
+        import torch
+        buf = self.new_ids_host_buffer()
+        if self.rank == 0:
+            buf.zero_()
+            buf[0] = len(got)
+            buf[1:1 + len(got)] = torch.tensor(got, dtype=buf.dtype)
+        self.stage.broadcast_ids(buf)
+        n = int(buf[0].item())
+        return [int(v) for v in buf[1:1 + n].tolist()]
+
+    def new_ids_host_buffer(self):
+        return self.stage.ids_buffer(16)

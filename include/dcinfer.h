@@ -70,6 +70,15 @@ const char* dc_init_error(void);
  * stream; (void*)1 = cudaStreamLegacy, the legacy default stream).  Lets a
  * caller order the library's launches with its own work. */
 int dc_set_stream(dc_ctx* ctx, void* stream);
+/* Live GEMM timing: while on, every GEMM launch is bracketed by CUDA events on
+ * its stream.  dc_timing(ctx, 1) resets and starts, dc_timing(ctx, 0) stops;
+ * dc_timing_read sums the launches of one kernel kind (1 GEMV, 2 SIMT dp4a,
+ * 3 tcgen05): total device ms, launch count, algorithmic bytes
+ * (M·K + K·N + 4M + 4N + output) and ops (2·M·N·K). */
+int dc_timing(dc_ctx* ctx, int on);
+int dc_timing_read(dc_ctx* ctx, int kind, double* ms, long long* launches, double* bytes, double* ops);
+/* Number of kernels this library has launched in this process (all contexts). */
+unsigned long long dc_launch_count(void);
 /* 1 when the tcgen05 tensor-core GEMM passed its init gate and is in use. */
 int dc_tc_enabled(const dc_ctx* ctx);
 /* Copy the LUT units out (host buffers of 65536 int16, 65536 int8, 256 int8). */
