@@ -73,6 +73,8 @@ SIGNATURES = [
     ("dc_weight_free", None, [_p]),
     ("dc_weight_info", _i, [_p, C.POINTER(_p), C.POINTER(_i), C.POINTER(_p), C.POINTER(_i), C.POINTER(_i)]),
     ("dc_vgemm", _i, [_p, _p, _i, _p, _u, _p]),
+    ("dc_ordered_sum_dev", _i, [_p, _p, _i, _i, _p]),
+    ("dc_rmsnorm_dev", _i, [_p, _p, _i, _i, _p, _d, _p]),
     ("dc_kernel_probe", _i, [_p, C.POINTER(_u32)]),
     ("dc_stage_create", _i, [_p, _p, _i, _i, _i, _i, _i, C.POINTER(_p)]),
     ("dc_stage_free", None, [_p]),
@@ -82,6 +84,7 @@ SIGNATURES = [
     ("dc_stage_embed", _i, [_p, _p, _i, _p]),
     ("dc_stage_forward", _i, [_p, _p, _i, _i, _i]),
     ("dc_stage_logits", _i, [_p, _p, _i, _p, _i, _p, _p]),
+    ("dc_decode_run", _i, [C.POINTER(_p), _i, _p, _i, _p, _i]),
     ("dc_stage_kv_reset", _i, [_p]),
     ("dc_stage_kv_len", _i, [_p]),
     ("dc_stage_kv_read", _i, [_p, _i, _p, _p, _p]),

@@ -147,6 +147,14 @@ class Compute:
     def vgemm_dev(self, X, m, w: "Weight", flags, out) -> None:
         self._check(self.L.dc_vgemm(self.h, _ptr(X), m, w.h, flags, _ptr(out)), "vgemm")
 
+    def ordered_sum_dev(self, terms, rows, n, out) -> None:
+        """out[r] = serial double sum of terms[r] in index order (infer.js:73-76, :100-104)."""
+        self._check(self.L.dc_ordered_sum_dev(self.h, _ptr(terms), rows, n, _ptr(out)), "ordered_sum")
+
+    def rmsnorm_dev(self, x, rows, cols, w, eps, y) -> None:
+        """infer.js rmsnorm (:70-80) of rows x cols f32."""
+        self._check(self.L.dc_rmsnorm_dev(self.h, _ptr(x), rows, cols, _ptr(w), float(eps), _ptr(y)), "rmsnorm")
+
     def kernel_probe(self) -> int:
         """kernelProbe's int32 hash (webgpu.js:1047-1055, before the math fold)."""
         h = C.c_uint32()

@@ -14,6 +14,8 @@
 #include <math.h>
 
 #include <atomic>
+#include <map>
+#include <mutex>
 #include <vector>
 
 #include "dc_internal.cuh"
@@ -231,6 +233,17 @@ thread_local std::string g_init_error;
 
 extern "C" const char* dc_init_error(void) { return g_init_error.c_str(); }
 
+int dc_set_smem(dc_ctx* ctx, const void* func, int bytes) {
+  static std::mutex lock;
+  static std::map<std::pair<const void*, int>, int> done;
+  std::lock_guard<std::mutex> guard(lock);
+  int& have = done[{func, ctx->device}];
+  if (bytes <= have) return DC_OK;
+  DC_CUDA(ctx, cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  have = bytes;
+  return DC_OK;
+}
+
 static std::atomic<unsigned long long> g_launches{0};
 void dc_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 extern "C" unsigned long long dc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
@@ -281,6 +294,8 @@ extern "C" int dc_init(int device, dc_ctx** out) {
   }
   if (!rc) {
     e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
     c->stream = c->own_stream;
     if (e == cudaSuccess) e = cudaMalloc(&c->d_mul, sizeof c->h_mul);
     if (e == cudaSuccess) e = cudaMalloc(&c->d_requant, sizeof c->h_requant);
@@ -321,6 +336,8 @@ extern "C" void dc_destroy(dc_ctx* c) {
     cudaEventDestroy(t.b);
   }
   for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
+  if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+  if (c->ev_join) cudaEventDestroy(c->ev_join);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
 }

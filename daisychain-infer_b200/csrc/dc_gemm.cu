@@ -15,7 +15,10 @@
 // and the tcgen05 tensor-core kernel in dc_gemm_tc.cu.
 #include <stdarg.h>
 
+#include <algorithm>
+
 #include "dc_internal.cuh"
+#include "dc_ptx.cuh"
 
 namespace {
 
@@ -45,71 +48,243 @@ __device__ __forceinline__ int4 ld_stream(const int4* p) {
 }
 
 // ---- GEMV: M <= MR rows ---------------------------------------------------
-// One warp per output column j at a time (grid-stride over columns).  The
-// weight row Wᵀ[j] (k bytes, K-major) is streamed once with 16-byte
-// non-allocating loads, 4 in flight per lane; the MR activation rows sit in
-// shared memory.  Lanes own 16-byte chunks c = lane + 32 t, so a warp reads
-// 512 contiguous bytes per step.  The int32 partial sums are combined by a
-// butterfly shuffle (integer addition: exact in any order).
-template <int MR>
-__global__ void __launch_bounds__(256) k_gemv(const int8_t* __restrict__ X, int ldx, const int8_t* __restrict__ Wt,
-                                              int ldw, const float* __restrict__ rs, const float* __restrict__ cs,
-                                              int m, int k, int n, unsigned flags, const int8_t* __restrict__ requant,
-                                              const int8_t* __restrict__ relu, void* out) {
+// G warps per output column j (G = 1, 2, 4 or 8: more than one when the matrix
+// has fewer columns than the GPU has warps), each streaming a contiguous K
+// slice of the weight row Wᵀ[j] with 16-byte non-allocating loads, 8 in flight
+// per lane (one 4 KB row in a single round trip).  The MR activation rows sit in
+// shared memory.  Partial sums are int32 (exact in any order): a butterfly
+// shuffle inside the warp, then the G warps of a column add theirs in shared
+// memory.  Columns step through the grid; the block's 8 warps move together.
+__device__ __forceinline__ int dp4a16g(const int4 a, const int4 b, int acc) {
+  acc = __dp4a(a.x, b.x, acc);
+  acc = __dp4a(a.y, b.y, acc);
+  acc = __dp4a(a.z, b.z, acc);
+  return __dp4a(a.w, b.w, acc);
+}
+
+template <int MR, int G>
+__global__ void __launch_bounds__(256, 3) k_gemv(const int8_t* __restrict__ X, int ldx,
+                                                 const int8_t* __restrict__ Wt, int ldw,
+                                                 const float* __restrict__ rs, const float* __restrict__ cs, int m,
+                                                 int k, int n, unsigned flags, const int8_t* __restrict__ requant,
+                                                 const int8_t* __restrict__ relu, void* out) {
   extern __shared__ int4 xs[];
+  __shared__ int part[8][MR];
   const int bz = blockIdx.y;
   const int nch = (k + 15) >> 4;  // 16-byte chunks per row (<= ldx/16, ldw/16)
   const int8_t* Xb = X + (int64_t)bz * m * ldx;
   for (int idx = threadIdx.x; idx < MR * nch; idx += blockDim.x) {
-    int r = idx / nch, c = idx - r * nch;
+    const int r = idx / nch, c = idx - r * nch;
     xs[idx] = (r < m) ? *((const int4*)(Xb + (int64_t)r * ldx) + c) : make_int4(0, 0, 0, 0);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wpb = blockDim.x >> 5;
+  constexpr int SLOTS = 8 / G;  // columns per block step
+  const int slot = warp / G, kp = warp - slot * G;
+  const int per = (nch + G - 1) / G;
+  const int c_lo = kp * per, c_hi = min(nch, c_lo + per);
   const int8_t* Wb = Wt + (int64_t)bz * n * ldw;
-  for (int j = blockIdx.x * wpb + warp; j < n; j += gridDim.x * wpb) {
-    const int4* wrow = (const int4*)(Wb + (int64_t)j * ldw);
+  for (int jb = blockIdx.x * SLOTS; jb < n; jb += gridDim.x * SLOTS) {
+    const int j = jb + slot;
     int acc[MR];
 #pragma unroll
     for (int r = 0; r < MR; r++) acc[r] = 0;
-    int c = lane;
-    for (; c + 96 < nch; c += 128) {
-      int4 w0 = ld_stream(wrow + c), w1 = ld_stream(wrow + c + 32), w2 = ld_stream(wrow + c + 64),
-           w3 = ld_stream(wrow + c + 96);
+    if (j < n) {
+      const int4* wrow = (const int4*)(Wb + (int64_t)j * ldw);
+      for (int c = c_lo + lane; c < c_hi; c += 256) {
+        int4 w[8];
 #pragma unroll
-      for (int r = 0; r < MR; r++) {
-        const int4* xr = xs + r * nch + c;
-        int4 a0 = xr[0], a1 = xr[32], a2 = xr[64], a3 = xr[96];
-        int t = acc[r];
-        t = __dp4a(w0.x, a0.x, t); t = __dp4a(w0.y, a0.y, t); t = __dp4a(w0.z, a0.z, t); t = __dp4a(w0.w, a0.w, t);
-        t = __dp4a(w1.x, a1.x, t); t = __dp4a(w1.y, a1.y, t); t = __dp4a(w1.z, a1.z, t); t = __dp4a(w1.w, a1.w, t);
-        t = __dp4a(w2.x, a2.x, t); t = __dp4a(w2.y, a2.y, t); t = __dp4a(w2.z, a2.z, t); t = __dp4a(w2.w, a2.w, t);
-        t = __dp4a(w3.x, a3.x, t); t = __dp4a(w3.y, a3.y, t); t = __dp4a(w3.z, a3.z, t); t = __dp4a(w3.w, a3.w, t);
-        acc[r] = t;
+        for (int u = 0; u < 8; u++) w[u] = (c + 32 * u < c_hi) ? ld_stream(wrow + c + 32 * u) : make_int4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          if (c + 32 * u < c_hi) {
+#pragma unroll
+            for (int r = 0; r < MR; r++) acc[r] = dp4a16g(w[u], xs[r * nch + c + 32 * u], acc[r]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < MR; r++)
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    }
+    if (G > 1) {
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < MR; r++) part[warp][r] = acc[r];
+      __syncthreads();
+      if (kp == 0 && lane < MR && lane < m && j < n) {
+        int v = 0;
+        for (int q = 0; q < G; q++) v += part[warp + q][lane];
+        dc_store_out(out, ((int64_t)bz * m + lane) * n + j, v, rs[bz * m + lane], cs[bz * n + j], flags, requant,
+                     relu);
+      }
+      __syncthreads();
+    } else {
+      int mine = 0;
+#pragma unroll
+      for (int r = 0; r < MR; r++)
+        if (r == lane) mine = acc[r];
+      if (lane < MR && lane < m && j < n)
+        dc_store_out(out, ((int64_t)bz * m + lane) * n + j, mine, rs[bz * m + lane], cs[bz * n + j], flags, requant,
+                     relu);
+    }
+  }
+}
+
+// ---- bulk-staged GEMV: M <= MR rows, the decode path -----------------------
+// One CTA per SM streams a contiguous range of weight rows (rows_per_cta rows
+// of Wᵀ, i.e. output columns) through a ring of `stages` shared-memory stages
+// of R rows each, filled by 1-D bulk async copies (cp.async.bulk + mbarrier
+// transaction counts) issued by one producer thread: several 20-32 KB copies
+// are in flight per SM, which is what keeps HBM busy.  Eight consumer warps
+// form the dot products from shared memory (16-byte reads, dp4a, butterfly
+// shuffle).  When a stage holds fewer than 8 rows, WR = 8/R warps share a row
+// and add their int32 partials with shared-memory atomics; the last of them
+// applies the epilogue.  Waits are bounded; a timeout aborts the whole CTA.
+template <int MR>
+__global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* __restrict__ X, int ldx,
+                                                      const int8_t* __restrict__ Wt, int ldw,
+                                                      const float* __restrict__ rs, const float* __restrict__ cs,
+                                                      int m, int k, int n, unsigned flags,
+                                                      const int8_t* __restrict__ requant,
+                                                      const int8_t* __restrict__ relu, void* out, int R, int stages,
+                                                      int rows_per_cta, int* status) {
+  extern __shared__ __align__(128) uint8_t smraw[];
+  __shared__ int rowacc[8][8][MR];  // [stage % 8][row in stage][r]
+  __shared__ int rowcnt[8][8];
+  __shared__ int abort_flag;
+  const int nch = (k + 15) >> 4;
+  const int stage_bytes = R * ldw;
+  uint8_t* sW = smraw;
+  int4* xs = (int4*)(smraw + (size_t)stages * stage_bytes);
+  uint64_t* full = (uint64_t*)(xs + MR * nch);
+  uint64_t* empty = full + stages;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bz = blockIdx.y;
+  const int rb = blockIdx.x * rows_per_cta;
+  const int nrows = min(n, rb + rows_per_cta) - rb;
+  const int nst = nrows > 0 ? (nrows + R - 1) / R : 0;
+  if (tid == 0) {
+    for (int s = 0; s < stages; s++) {
+      dcp::mbar_init(&full[s], 1);
+      dcp::mbar_init(&empty[s], 8);
+    }
+    dcp::mbar_fence_init();
+    abort_flag = 0;
+  }
+  for (int i = tid; i < 8 * 8 * MR; i += blockDim.x) (&rowacc[0][0][0])[i] = 0;
+  for (int i = tid; i < 8 * 8; i += blockDim.x) (&rowcnt[0][0])[i] = 0;
+  const int8_t* Xb = X + (int64_t)bz * m * ldx;
+  for (int idx = tid; idx < MR * nch; idx += blockDim.x) {
+    const int r = idx / nch, c = idx - r * nch;
+    xs[idx] = (r < m) ? *((const int4*)(Xb + (int64_t)r * ldx) + c) : make_int4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  if (nst == 0) return;
+  if (warp == 8) {
+    // ---- producer
+    if (lane == 0) {
+      int issued = 0;
+      const int8_t* Wb = Wt + ((int64_t)bz * n + rb) * ldw;
+      for (int it = 0; it < nst; it++) {
+        const int s = it % stages;
+        if (it >= stages && !dcp::mbar_wait(&empty[s], (uint32_t)((it / stages) - 1) & 1u, status)) {
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        if (*(volatile int*)&abort_flag) break;
+        const int rows_this = min(R, nrows - it * R);
+        const uint32_t bytes = (uint32_t)rows_this * (uint32_t)ldw;
+        dcp::mbar_expect_tx(&full[s], bytes);
+        dcp::bulk_load(sW + (size_t)s * stage_bytes, Wb + (int64_t)it * R * ldw, bytes, &full[s]);
+        issued++;
+      }
+      // let every issued copy land before this CTA's shared memory can go away
+      for (int it = max(0, issued - stages); it < issued; it++)
+        dcp::mbar_wait(&full[it % stages], (uint32_t)(it / stages) & 1u, status);
+    }
+    return;
+  }
+  // ---- consumers
+  const int WR = R >= 8 ? 1 : 8 / R;
+  const int per = (nch + WR - 1) / WR;
+  for (int it = 0; it < nst; it++) {
+    const int s = it % stages;
+    if (*(volatile int*)&abort_flag) break;
+    if (!dcp::mbar_wait(&full[s], (uint32_t)(it / stages) & 1u, status)) {
+      atomicExch(&abort_flag, 1);
+      break;
+    }
+    const int rows_this = min(R, nrows - it * R);
+    const uint8_t* base = sW + (size_t)s * stage_bytes;
+    const int j0 = rb + it * R;
+    if (WR == 1) {
+      for (int rr = warp; rr < rows_this; rr += 8) {
+        const int4* wr = (const int4*)(base + (size_t)rr * ldw);
+        int acc[MR];
+#pragma unroll
+        for (int r = 0; r < MR; r++) acc[r] = 0;
+        for (int c = lane; c < nch; c += 32) {
+          const int4 w = wr[c];
+#pragma unroll
+          for (int r = 0; r < MR; r++) acc[r] = dp4a16g(w, xs[r * nch + c], acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < MR; r++)
+#pragma unroll
+          for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+        int mine = 0;
+#pragma unroll
+        for (int r = 0; r < MR; r++)
+          if (r == lane) mine = acc[r];
+        if (lane < MR && lane < m) {
+          const int j = j0 + rr;
+          dc_store_out(out, ((int64_t)bz * m + lane) * n + j, mine, rs[bz * m + lane], cs[bz * n + j], flags, requant,
+                       relu);
+        }
+      }
+    } else {
+      const int rr = warp / WR, p = warp - rr * WR;
+      if (rr < rows_this) {
+        const int4* wr = (const int4*)(base + (size_t)rr * ldw);
+        const int c1 = min(nch, (p + 1) * per);
+        int acc[MR];
+#pragma unroll
+        for (int r = 0; r < MR; r++) acc[r] = 0;
+        for (int c = p * per + lane; c < c1; c += 32) {
+          const int4 w = wr[c];
+#pragma unroll
+          for (int r = 0; r < MR; r++) acc[r] = dp4a16g(w, xs[r * nch + c], acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < MR; r++)
+#pragma unroll
+          for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+        int* ra = rowacc[s & 7][rr];
+        if (lane == 0)
+#pragma unroll
+          for (int r = 0; r < MR; r++) atomicAdd(&ra[r], acc[r]);
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = (atomicAdd(&rowcnt[s & 7][rr], 1) == WR - 1);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence_block();
+          if (lane < MR && lane < m) {
+            const int j = j0 + rr;
+            const int v = atomicExch(&ra[lane], 0);
+            dc_store_out(out, ((int64_t)bz * m + lane) * n + j, v, rs[bz * m + lane], cs[bz * n + j], flags, requant,
+                         relu);
+          }
+          if (lane == 0) rowcnt[s & 7][rr] = 0;
+          __syncwarp();
+        }
       }
     }
-    for (; c < nch; c += 32) {
-      int4 w0 = ld_stream(wrow + c);
-#pragma unroll
-      for (int r = 0; r < MR; r++) {
-        int4 a0 = xs[r * nch + c];
-        int t = acc[r];
-        t = __dp4a(w0.x, a0.x, t); t = __dp4a(w0.y, a0.y, t); t = __dp4a(w0.z, a0.z, t); t = __dp4a(w0.w, a0.w, t);
-        acc[r] = t;
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < MR; r++)
-#pragma unroll
-      for (int o = 16; o; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-    int mine = 0;
-#pragma unroll
-    for (int r = 0; r < MR; r++)
-      if (r == lane) mine = acc[r];
-    if (lane < MR && lane < m)
-      dc_store_out(out, ((int64_t)bz * m + lane) * n + j, mine, rs[bz * m + lane], cs[bz * n + j], flags, requant,
-                   relu);
+    __syncwarp();
+    if (lane == 0) dcp::mbar_arrive(&empty[s]);
   }
 }
 
@@ -166,23 +341,83 @@ __global__ void __launch_bounds__(256) k_gemm_simt(const int8_t* __restrict__ X,
   }
 }
 
+template <int MR, int G>
+int launch_gemv_g(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                  const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                  size_t smem, int blocks) {
+  if (smem > 48 * 1024)
+    if (int rc = dc_set_smem(ctx, (const void*)k_gemv<MR, G>, (int)smem)) return rc;
+  k_gemv<MR, G><<<dim3(blocks, batch), 256, smem, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant,
+                                                        ctx->d_relu, out);
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+// Bulk-staged GEMV launch: ~32 KB stages of whole weight rows, as many stages as
+// fit beside the activation rows, one CTA per SM over contiguous row ranges.
+// Returns DC_E_INVAL (nothing launched) when the operands are not 16-byte
+// aligned or a stage does not fit; the caller then uses k_gemv.
+template <int MR>
+int launch_gemv_bulk(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                     const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st) {
+  if (((uintptr_t)Wt & 15) || ((uintptr_t)Xq & 15) || (ldw & 15) || (ldx & 15)) return DC_E_INVAL;
+  const int nch = (k + 15) >> 4;
+  const size_t xbytes = (size_t)MR * nch * 16;
+  int R = 32768 / ldw;
+  if (R >= 8) R = std::min(64, R / 8 * 8);
+  else R = R >= 4 ? 4 : (R >= 2 ? 2 : 1);
+  const size_t stage_bytes = (size_t)R * ldw;
+  const size_t budget = 216 * 1024;
+  if (xbytes + 2 * stage_bytes + 256 > budget) return DC_E_INVAL;
+  const int stages = (int)std::min<size_t>(8, (budget - xbytes - 256) / stage_bytes);
+  const size_t smem = (size_t)stages * stage_bytes + xbytes + 16 * (size_t)stages + 128;
+  int gx = std::min(ctx->sm_count, n);
+  const int rows_per_cta = (n + gx - 1) / gx;
+  gx = (n + rows_per_cta - 1) / rows_per_cta;
+  if (int rc = dc_set_smem(ctx, (const void*)k_gemv_bulk<MR>, (int)smem)) return rc;
+  k_gemv_bulk<MR><<<dim3(gx, batch), 288, smem, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant,
+                                                      ctx->d_relu, out, R, stages, rows_per_cta, ctx->d_status);
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
 template <int MR>
 int launch_gemv(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
                 int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st) {
+  {
+    const int rc = launch_gemv_bulk<MR>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
+    if (rc != DC_E_INVAL) return rc;
+  }
   const int nch = (k + 15) >> 4;
-  size_t smem = (size_t)MR * nch * 16;
+  const size_t smem = (size_t)MR * nch * 16;
   if (smem > 200 * 1024) return dc_fail(ctx, DC_E_INVAL, "gemv: k=%d too long for %d rows in shared memory", k, MR);
-  if (smem > 48 * 1024) DC_CUDA(ctx, cudaFuncSetAttribute(k_gemv<MR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                          (int)smem));
-  // 8 warps per block; enough blocks to cover every column once or fill the SMs.
-  int blocks = (n + 7) / 8;
-  int cap = ctx->sm_count * (smem > 64 * 1024 ? 1 : 4);
-  if (blocks > cap) blocks = cap;
+  const int per_sm = smem > 64 * 1024 ? 1 : 3;
+  const int warps = ctx->sm_count * per_sm * 8;
+  // warps per column: split K so that the (column, K-slice) units fill whole
+  // rounds of the resident warps, keeping each slice at least 128 chunks
+  int G = 1;
+  double best = 0.0;
+  for (int g = 1; g <= 8; g *= 2) {
+    if (g > 1 && nch < 128 * g) break;
+    const long units = (long)n * batch * g;
+    const long rounds = (units + warps - 1) / warps;
+    const double eff = (double)units / ((double)rounds * warps);
+    if (eff > best + 0.02) {
+      best = eff;
+      G = g;
+    }
+  }
+  int blocks = (n + 8 / G - 1) / (8 / G);
+  if (blocks > ctx->sm_count * per_sm) blocks = ctx->sm_count * per_sm;
   if (blocks < 1) blocks = 1;
-  dim3 grid(blocks, batch);
-  k_gemv<MR><<<grid, 256, smem, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant, ctx->d_relu, out); dc_count_launch();
-  DC_CUDA(ctx, cudaGetLastError());
-  return DC_OK;
+  switch (G) {
+    case 1: return launch_gemv_g<MR, 1>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, smem, blocks);
+    case 2: return launch_gemv_g<MR, 2>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, smem, blocks);
+    case 4: return launch_gemv_g<MR, 4>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, smem, blocks);
+    default: return launch_gemv_g<MR, 8>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, smem, blocks);
+  }
 }
 
 }  // namespace

@@ -28,6 +28,9 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+#include <unordered_map>
+
 #include "dc_internal.cuh"
 
 namespace {
@@ -309,7 +312,40 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D int8 map over `rows` rows of `ld` bytes, box = 128 bytes x box_rows, 128B swizzle.
+// A map is a pure function of (address, ld, rows, box rows), so encoded maps are
+// cached under that key: the resident weights and the stage's activation
+// buffers are encoded once instead of on every GEMM call.
+struct MapKey {
+  uintptr_t base;
+  long rows;
+  int ld, box;
+  bool operator==(const MapKey& o) const { return base == o.base && rows == o.rows && ld == o.ld && box == o.box; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<uintptr_t>()(k.base) ^ (std::hash<long>()(k.rows) * 31u) ^ ((size_t)k.ld << 20) ^ (size_t)k.box;
+  }
+};
+std::mutex g_map_lock;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+bool encode_map(CUtensorMap* map, const void* base, int ld, long rows, int box_rows);
+
 bool make_map(CUtensorMap* map, const void* base, int ld, long rows, int box_rows) {
+  const MapKey key{(uintptr_t)base, rows, ld, box_rows};
+  std::lock_guard<std::mutex> guard(g_map_lock);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *map = it->second;
+    return true;
+  }
+  if (!encode_map(map, base, ld, rows, box_rows)) return false;
+  if (g_maps.size() > 65536) g_maps.clear();
+  g_maps.emplace(key, *map);
+  return true;
+}
+
+bool encode_map(CUtensorMap* map, const void* base, int ld, long rows, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)rows};
@@ -359,7 +395,7 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
   a.partial = partial;
   a.counters = counters;
   a.status = ctx->d_status;
-  DC_CUDA(ctx, cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+  if (int rc = dc_set_smem(ctx, (const void*)k_gemm_tc<BN>, C::SMEM)) return rc;
   dim3 grid(a.n_tiles, a.m_tiles, batch * splits);
   k_gemm_tc<BN><<<grid, 128, C::SMEM, st>>>(mW, mX, a); dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());

@@ -9,6 +9,10 @@
 
 #include "../../include/dcinfer.h"
 
+// Internal GEMM flag (beside the public DC_RELU / DC_ACC / DC_REQUANT): add the
+// f32 epilogue value to what `out` already holds (the residual connection).
+#define DC_F_ADDTO 0x100u
+
 // Device status word bits (atomicOr'd by kernels, read and cleared by dc_sync).
 #define DC_ST_NONFINITE 1
 #define DC_ST_TIMEOUT 2
@@ -27,6 +31,7 @@ struct dc_ctx {
   int sm_count = 148;
   cudaStream_t stream = nullptr;      // where work is launched
   cudaStream_t own_stream = nullptr;  // created by dc_init
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;  // ordering between `stream` and `own_stream`
   std::string err;
   char label[160] = {0};
   // LUT units: host copies (checked by sha256) and device copies.
@@ -72,6 +77,10 @@ int dc_cuda_fail(dc_ctx* ctx, cudaError_t e, const char* what);
   } while (0)
 
 int dc_scratch(dc_ctx* ctx, size_t bytes, void** p);
+
+// Allow `bytes` of dynamic shared memory for kernel `func` on ctx's device; the
+// attribute is set once per (kernel, device) and raised only when needed.
+int dc_set_smem(dc_ctx* ctx, const void* func, int bytes);
 
 // Kernels launched by this library in this process (reported by dc_launch_count).
 void dc_count_launch();
@@ -121,6 +130,7 @@ __device__ __forceinline__ void dc_store_out(void* out, int64_t idx, int32_t acc
   } else {
     float v = dc_epi(acc, rsv, csv);
     if ((flags & DC_RELU) && v < 0.0f) v = 0.0f;
+    if (flags & DC_F_ADDTO) v = __fadd_rn(((const float*)out)[idx], v);  // residual: out = out + v (f32 add)
     ((float*)out)[idx] = v;
   }
 }

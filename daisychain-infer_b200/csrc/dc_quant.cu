@@ -31,7 +31,8 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float* __restrict__ X,
     if (!isfinite(v)) bad = true;
     mx = fmaxf(mx, fabsf(v));
   }
-  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(status, DC_ST_NONFINITE);
+  // a warp vote, not a block vote: __syncthreads_or costs microseconds here
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(status, DC_ST_NONFINITE);
   __shared__ float red[32];
   for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;

@@ -37,6 +37,7 @@
 
 #include "dc_internal.cuh"
 #include "dc_math.cuh"
+#include "dc_osum.cuh"
 
 struct dc_mat {
   int k = 0, n = 0, ldk = 0;
@@ -48,7 +49,7 @@ struct dc_kv {
   int8_t* k8 = nullptr;   // [kvh][max_pos][hd] int8 keys (rotated)
   float* ks = nullptr;    // [kvh][max_pos] key scales (f32, quantizeCols rule)
   float* v = nullptr;     // [max_pos][kvDim] f32 values
-  int8_t* v8 = nullptr;   // [kvh][max_pos][hd] int8 values under the current channel scales
+  int8_t* v8t = nullptr;  // [kvh][hd][ldp] int8 values (channel-major) under the current channel scales
   float* vs = nullptr;    // [kvDim] channel scales
   uint32_t* vmax = nullptr;  // [kvDim] running |v| maximum (float bits)
   int* vchg = nullptr;    // [kvDim] channel scale changed on this step
@@ -66,7 +67,7 @@ struct dc_stage {
   dc_spec spec;
   int lo = 0, hi = 0, head = 0, max_rows = 0, max_pos = 0;
   int C = 0, hd = 0, nH = 0, nKV = 0, qDim = 0, kvDim = 0, I = 0, V = 0, nqkv = 0;
-  int ldC = 0, ldQ = 0, ldI = 0;
+  int ldC = 0, ldQ = 0, ldI = 0, ldp = 0;  // ldp: positions per channel row of the int8 V cache
   std::vector<dc_layer> L;
   float* emb = nullptr;  // V x C
   float* nrmF = nullptr;
@@ -80,13 +81,24 @@ struct dc_stage {
   int8_t* xq = nullptr;    // max_rows x max(ldC, ldQ, ldI)
   float* rs = nullptr;     // max_rows
   float* lx = nullptr;     // logits rows x C gathered
+  uint32_t* rowmax = nullptr;  // max_rows running row maxima (float bits)
+  // device-side positions (read by the kernels, so decode laps can be replayed as a graph)
+  int* d_pos = nullptr;     // cached tokens of this stage
+  int* d_zero = nullptr;    // constant 0 (the full window)
+  int* d_step = nullptr;    // head: decode lap counter (index into the picks buffer)
+  float* xlap = nullptr;    // head: the one hidden row a decode lap carries
+  float* logits1 = nullptr; // head: logits of the lap's row
+  unsigned long long* amax_keys = nullptr;  // head: greedy-pick keys (8 rows), kept at zero between uses
+  cudaGraphExec_t lap_exec = nullptr;
+  std::vector<dc_stage*> lap_key;
+  int32_t* lap_picks = nullptr;
   std::vector<void*> allocs;
 };
 
 namespace {
 
 constexpr int NORM_THREADS = 256;
-constexpr int ATT_THREADS = 128;
+constexpr int ATT_THREADS = 256;
 
 __device__ __forceinline__ float block_max_f(float v, float* red) {
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -131,44 +143,36 @@ __device__ __forceinline__ double quant_scale(float mx) {
 __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __restrict__ x, int C,
                                                                const float* __restrict__ w, double eps,
                                                                int8_t* __restrict__ q, int ldq,
-                                                               float* __restrict__ s, int* status) {
-  extern __shared__ float ys[];  // C floats
+                                                               float* __restrict__ s, int* status,
+                                                               float* __restrict__ yo = nullptr) {
+  extern __shared__ __align__(16) double sq[];  // C doubles (v*v), then C floats (x, then y)
+  float* ys = (float*)(sq + C);
   __shared__ float red[32];
-  __shared__ double inv_s;
+  __shared__ dco::Smem osm;
   const int row = blockIdx.x;
   const float* xr = x + (int64_t)row * C;
   bool bad = false;
   for (int j = threadIdx.x; j < C; j += blockDim.x) {
-    float v = xr[j];
+    const float v = xr[j];
     bad |= !isfinite(v);
     ys[j] = v;
+    sq[j] = __dmul_rn((double)v, (double)v);  // exact: a float square fits in a double
   }
-  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(status, DC_ST_NONFINITE);
-  if (threadIdx.x == 0) {
-    // the reference's order: s += v*v for j = 0 .. C-1, each step rounded
-    double acc = 0.0;
-    int j = 0;
-    for (; j + 4 <= C; j += 4) {
-      double v0 = ys[j], v1 = ys[j + 1], v2 = ys[j + 2], v3 = ys[j + 3];
-      double p0 = __dmul_rn(v0, v0), p1 = __dmul_rn(v1, v1), p2 = __dmul_rn(v2, v2), p3 = __dmul_rn(v3, v3);
-      acc = __dadd_rn(acc, p0);
-      acc = __dadd_rn(acc, p1);
-      acc = __dadd_rn(acc, p2);
-      acc = __dadd_rn(acc, p3);
-    }
-    for (; j < C; j++) {
-      double v = ys[j];
-      acc = __dadd_rn(acc, __dmul_rn(v, v));
-    }
-    inv_s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(acc, (double)C), eps)));
-  }
+  // warp votes and a plain barrier: a block vote (__syncthreads_or) costs microseconds here
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(status, DC_ST_NONFINITE);
   __syncthreads();
-  const double inv = inv_s;
+  // the reference's order: s += v*v for j = 0 .. C-1, each step rounded
+  const double acc = dco::ordered_sum(sq, C, osm);
+  const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(acc, (double)C), eps)));
   float mx = 0.0f;
   for (int j = threadIdx.x; j < C; j += blockDim.x) {
     float y = __double2float_rn(__dmul_rn(__dmul_rn((double)ys[j], inv), (double)w[j]));
     ys[j] = y;
     mx = fmaxf(mx, fabsf(y));
+  }
+  if (yo) {  // the normalised row itself (infer.js rmsnorm), no quantisation
+    for (int j = threadIdx.x; j < C; j += blockDim.x) yo[(int64_t)row * C + j] = ys[j];
+    return;
   }
   mx = block_max_f(mx, red);
   const double sc = quant_scale(mx);
@@ -181,21 +185,38 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
 // RoPE on the q and k parts of the fused QKV output row, quantisation of each
 // rotated key (per kv head, quantizeCols rule), append of keys and values to
 // the cache at row n0 + t, and the running per-channel |v| maximum.
-__global__ void __launch_bounds__(128) k_rope_append(float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
-                                                     const float* __restrict__ rc, const float* __restrict__ rsn,
-                                                     int pos0, int n0, int max_pos, int8_t* __restrict__ k8,
-                                                     float* __restrict__ ks, float* __restrict__ vcache,
-                                                     uint32_t* __restrict__ vmax, int* status) {
-  extern __shared__ float kr[];  // nKV * hd rotated keys
-  const int t = blockIdx.x;
-  const int p = pos0 + t;
+// grid (T, nH + nKV + 1), block 64: block y < nH rotates query head y in place;
+// nH <= y < nH + nKV rotates key head y - nH, quantises it and appends it;
+// the last block appends the value row and folds |v| into the channel maxima.
+__global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
+                                                    const float* __restrict__ rc, const float* __restrict__ rsn,
+                                                    const int* __restrict__ n0p, int max_pos,
+                                                    int8_t* __restrict__ k8, float* __restrict__ ks,
+                                                    float* __restrict__ vcache, uint32_t* __restrict__ vmax,
+                                                    int* status) {
+  __shared__ float kr[128];
+  __shared__ float red[32];
+  const int n0 = *n0p;  // cached tokens before this chunk = its first position
+  const int t = blockIdx.x, hh = blockIdx.y;
+  const int p = n0 + t;
   const int half = hd >> 1, qDim = nH * hd, kvDim = nKV * hd;
   float* row = h + (int64_t)t * nqkv;
-  for (int idx = threadIdx.x; idx < (nH + nKV) * half; idx += blockDim.x) {
-    const int hh = idx / half, i = idx - hh * half;
+  bool bad = false;
+  if (hh == nH + nKV) {
+    // values: copy and fold into the running channel maximum
+    for (int c = threadIdx.x; c < kvDim; c += blockDim.x) {
+      const float v = row[qDim + kvDim + c];
+      bad |= !isfinite(v);
+      vcache[(int64_t)(n0 + t) * kvDim + c] = v;
+      atomicMax(vmax + c, __float_as_uint(fabsf(v)));
+    }
+    if (bad) atomicOr(status, DC_ST_NONFINITE);
+    return;
+  }
+  const bool isq = hh < nH;
+  float* o = isq ? row + hh * hd : row + qDim + (hh - nH) * hd;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
     const double c = rc[(int64_t)p * half + i], s = rsn[(int64_t)p * half + i];
-    const bool isq = hh < nH;
-    float* o = isq ? row + hh * hd : row + qDim + (hh - nH) * hd;
     const double a = o[i], b = o[half + i];
     const float na = __double2float_rn(__dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s)));
     const float nb = __double2float_rn(__dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s)));
@@ -203,86 +224,145 @@ __global__ void __launch_bounds__(128) k_rope_append(float* __restrict__ h, int 
       o[i] = na;
       o[half + i] = nb;
     } else {
-      kr[(hh - nH) * hd + i] = na;
-      kr[(hh - nH) * hd + half + i] = nb;
+      kr[i] = na;
+      kr[half + i] = nb;
     }
   }
-  // values: copy and fold into the running channel maximum
-  bool bad = false;
-  for (int c = threadIdx.x; c < kvDim; c += blockDim.x) {
-    const float v = row[qDim + kvDim + c];
-    bad |= !isfinite(v);
-    vcache[(int64_t)(n0 + t) * kvDim + c] = v;
-    atomicMax(vmax + c, __float_as_uint(fabsf(v)));
-  }
+  if (isq) return;
   __syncthreads();
-  // one warp per kv head: absmax over hd, f32 scale, int8 keys
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int g = warp; g < nKV; g += blockDim.x >> 5) {
-    float mx = 0.0f;
-    for (int c = lane; c < hd; c += 32) {
-      const float v = kr[g * hd + c];
-      bad |= !isfinite(v);
-      mx = fmaxf(mx, fabsf(v));
-    }
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float sc = __double2float_rn(quant_scale(mx));
-    const int64_t slot = (int64_t)g * max_pos + n0 + t;
-    if (lane == 0) ks[slot] = sc;
-    for (int c = lane; c < hd; c += 32)
-      k8[slot * hd + c] = dc_clamp8(dc_js_round(__ddiv_rn((double)kr[g * hd + c], (double)sc)));
+  // the rotated key: absmax over hd, f32 scale (quantizeCols rule), int8 row
+  float mx = 0.0f;
+  for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+    const float v = kr[c];
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
   }
+  mx = block_max_f(mx, red);
+  const float sc = __double2float_rn(quant_scale(mx));
+  const int g = hh - nH;
+  const int64_t slot = (int64_t)g * max_pos + n0 + t;
+  if (threadIdx.x == 0) ks[slot] = sc;
+  for (int c = threadIdx.x; c < hd; c += blockDim.x)
+    k8[slot * hd + c] = dc_clamp8(dc_js_round(__ddiv_rn((double)kr[c], (double)sc)));
   if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
 
 // Channel scales of V over all cached tokens; flags the channels whose scale moved.
 __global__ void k_vscale(const uint32_t* __restrict__ vmax, float* __restrict__ vs, int* __restrict__ vchg,
-                         int kvDim, int fresh) {
+                         int kvDim, const int* __restrict__ n0p) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= kvDim) return;
+  const int fresh = *n0p == 0;
   const float ns = __double2float_rn(quant_scale(__uint_as_float(vmax[c])));
   vchg[c] = fresh || ns != vs[c];
   vs[c] = ns;
 }
 
-// int8 V under the channel scales: rows >= n0 always, older rows only in
-// channels whose scale moved.  grid (ceil(N/64), kvDim/32), block 32 x 8.
+// int8 V under the channel scales, stored channel-major ([kv head][channel][ldp]
+// so a context dot product streams contiguous bytes): rows >= n0 always, older
+// rows only in channels whose scale moved.  grid (ceil(N/64), ceil(kvDim/32)),
+// block 256 (32 channels x 8 rows); the tile is transposed through shared memory.
 __global__ void __launch_bounds__(256) k_vquant(const float* __restrict__ vcache, const float* __restrict__ vs,
-                                                const int* __restrict__ vchg, int8_t* __restrict__ v8, int N, int n0,
-                                                int kvDim, int hd, int max_pos) {
-  const int c = blockIdx.y * 32 + (threadIdx.x & 31);
-  if (c >= kvDim) return;
-  const bool chg = vchg[c] != 0;
-  const double sc = (double)vs[c];
-  const int g = c / hd, cc = c - g * hd;
-  const int jb = blockIdx.x * 64;
-  for (int j = jb + (threadIdx.x >> 5); j < min(N, jb + 64); j += 8) {
-    if (j < n0 && !chg) continue;
-    v8[((int64_t)g * max_pos + j) * hd + cc] =
-        dc_clamp8(dc_js_round(__ddiv_rn((double)vcache[(int64_t)j * kvDim + c], sc)));
+                                                const int* __restrict__ vchg, int8_t* __restrict__ v8t, int N, int n0,
+                                                int kvDim, int hd, int ldp) {
+  __shared__ int8_t tile[32][65];
+  const int cb = blockIdx.y * 32, jb = blockIdx.x * 64;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = cb + tx;
+  const bool cval = c < kvDim;
+  const bool chg = cval && vchg[c] != 0;
+  const double sc = cval ? (double)vs[c] : 1.0;
+  for (int r = ty; r < 64; r += 8) {
+    const int j = jb + r;
+    int8_t v = 0;
+    if (cval && j < N && (j >= n0 || chg))
+      v = dc_clamp8(dc_js_round(__ddiv_rn((double)vcache[(int64_t)j * kvDim + c], sc)));
+    tile[tx][r] = v;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 32 * 64; idx += blockDim.x) {
+    const int cl = idx >> 6, r = idx & 63;
+    const int cc = cb + cl, j = jb + r;
+    if (cc >= kvDim || j >= N) continue;
+    if (j < n0 && !vchg[cc]) continue;  // an unchanged channel keeps its int8 rows
+    const int g = cc / hd, ch = cc - g * hd;
+    v8t[((int64_t)g * hd + ch) * ldp + j] = tile[cl][r];
   }
 }
 
+// The tiled quantisation for a decode lap, reading the cache length from
+// device memory: grid (ceil(max_pos/64), ceil(kvDim/32)) tiles of 64 rows x 32
+// channels; a tile with no new row and no channel whose scale moved exits at
+// once, the others quantise and transpose like k_vquant.
+__global__ void __launch_bounds__(256) k_vquant_dev(const float* __restrict__ vcache, const float* __restrict__ vs,
+                                                    const int* __restrict__ vchg, int8_t* __restrict__ v8t, int T,
+                                                    const int* __restrict__ n0p, int kvDim, int hd, int ldp) {
+  __shared__ int8_t tile[32][65];
+  const int n0 = *n0p, N = n0 + T;
+  const int cb = blockIdx.y * 32, jb = blockIdx.x * 64;
+  if (jb >= N) return;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = cb + tx;
+  const bool cval = c < kvDim;
+  const bool chg = cval && vchg[c] != 0;
+  const bool fresh_rows = jb + 64 > n0;  // the tile holds rows >= n0
+  // every warp holds the same 32 channels, so this warp vote is block-uniform
+  if (!fresh_rows && !__any_sync(0xffffffffu, chg)) return;
+  const double sc = cval ? (double)vs[c] : 1.0;
+  for (int r = ty; r < 64; r += 8) {
+    const int j = jb + r;
+    int8_t v = 0;
+    if (cval && j < N && (j >= n0 || chg))
+      v = dc_clamp8(dc_js_round(__ddiv_rn((double)vcache[(int64_t)j * kvDim + c], sc)));
+    tile[tx][r] = v;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 32 * 64; idx += blockDim.x) {
+    const int cl = idx >> 6, r = idx & 63;
+    const int cc = cb + cl, j = jb + r;
+    if (cc >= kvDim || j >= N) continue;
+    if (j < n0 && !vchg[cc]) continue;
+    const int g = cc / hd, ch = cc - g * hd;
+    v8t[((int64_t)g * hd + ch) * ldp + j] = tile[cl][r];
+  }
+}
+
+__global__ void k_setpos(int* p, int v) { *p = v; }
+__global__ void k_addpos(int* p, int v) { *p += v; }
+
+__device__ __forceinline__ int dp4a16(const int4 a, const int4 b, int acc) {
+  acc = __dp4a(a.x, b.x, acc);
+  acc = __dp4a(a.y, b.y, acc);
+  acc = __dp4a(a.z, b.z, acc);
+  return __dp4a(a.w, b.w, acc);
+}
+
 // One (query head, query row): scores, causal softmax, context.  N = n0 + T.
+// Scores: hd/16 lanes per key, 16-byte loads of the int8 key row, shuffle sum.
+// Context: one warp per output channel, lanes stream 16-byte chunks of that
+// channel's int8 values (channel-major cache) against the int8 probabilities.
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ h, int nqkv, int nH, int nKV,
                                                            int hd, const int8_t* __restrict__ k8,
                                                            const float* __restrict__ ks,
-                                                           const int8_t* __restrict__ v8,
-                                                           const float* __restrict__ vs, int N, int n0, int max_pos,
-                                                           double scale, float* __restrict__ out, int qDim,
+                                                           const int8_t* __restrict__ v8t,
+                                                           const float* __restrict__ vs, int T,
+                                                           const int* __restrict__ n0p, int max_pos,
+                                                           int ldp, double scale, float* __restrict__ out,
+                                                           uint32_t* __restrict__ rowmax, int qDim,
                                                            int* status) {
   extern __shared__ __align__(16) uint8_t sm[];
-  double* ed = (double*)sm;                 // N doubles: e_j
-  float* af = (float*)(ed + max_pos);       // N floats: scores, then a_j
-  int8_t* a8 = (int8_t*)(af + max_pos);     // N int8
-  __shared__ __align__(16) int8_t q8[256];
+  double* ed = (double*)sm;                                 // max_pos doubles: e_j
+  float* af = (float*)(ed + max_pos);                       // max_pos floats: scores, then a_j
+  int8_t* a8 = (int8_t*)(sm + ((12 * (size_t)max_pos + 15) & ~(size_t)15));  // ldp int8, 16-byte aligned
+  __shared__ __align__(16) int8_t q8[128];
   __shared__ float red[32];
   __shared__ double redd[32];
-  __shared__ double zsum;
-  __shared__ int ctxacc[ATT_THREADS / 16][128];
+  __shared__ dco::Smem osm;
   const int hq = blockIdx.x, i = blockIdx.y;
   const int group = nH / nKV, g = hq / group;
-  const int see = n0 + i;
+  const int n0 = *n0p;
+  const int see = n0 + i;  // this query's own position in the cache (keys 0..see are visible)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   // 1. quantise the query row of this head (row scale per (token, head), double)
   const float* qrow = h + (int64_t)i * nqkv + hq * hd;
   float mx = 0.0f;
@@ -298,14 +378,28 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
   for (int c = threadIdx.x; c < hd; c += blockDim.x) q8[c] = dc_clamp8(dc_js_round(__ddiv_rn((double)qrow[c], qsc)));
   __syncthreads();
   // 2. scores for keys 0..see: int32 dot over hd, verified epilogue
-  const int8_t* kb = k8 + (int64_t)g * max_pos * hd;
-  const float* ksg = ks + (int64_t)g * max_pos;
-  for (int j = threadIdx.x; j <= see; j += blockDim.x) {
-    const int* kj = (const int*)(kb + (int64_t)j * hd);
-    const int* qq = (const int*)q8;
-    int acc = 0;
-    for (int c = 0; c < hd / 4; c++) acc = __dp4a(kj[c], qq[c], acc);
-    af[j] = dc_epi(acc, qs, ksg[j]);
+  {
+    const int8_t* kb = k8 + (int64_t)g * max_pos * hd;
+    const float* ksg = ks + (int64_t)g * max_pos;
+    const int lpk = hd >> 4, kpw = 32 / lpk;  // lanes per key, keys per warp step
+    const int sub = lane / lpk, part = lane - sub * lpk;
+    const int4 qv = ((const int4*)q8)[part];
+    const int step = nwarps * kpw;  // keys per block pass; 8 passes' loads are issued together
+    for (int j0 = warp * kpw; j0 <= see; j0 += 8 * step) {
+      int4 kv[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int j = j0 + u * step + sub;
+        kv[u] = j <= see ? *(const int4*)(kb + (int64_t)j * hd + part * 16) : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int j = j0 + u * step + sub;
+        int acc = dp4a16(kv[u], qv, 0);
+        for (int o = lpk >> 1; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (part == 0 && j <= see) af[j] = dc_epi(acc, qs, ksg[j]);
+      }
+    }
   }
   __syncthreads();
   // 3. row maximum of s*scale (double, exact)
@@ -319,14 +413,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
     af[j] = __double2float_rn(e);
   }
   __syncthreads();
-  // 5. z = sum of e_j in key order (one thread: the reference's rounding sequence)
-  if (threadIdx.x == 0) {
-    double z = 0.0;
-    for (int j = 0; j <= see; j++) z = __dadd_rn(z, ed[j]);
-    zsum = z;
-  }
-  __syncthreads();
-  const double z = zsum;
+  // 5. z = sum of e_j in key order, with the reference's rounding sequence
+  const double z = dco::ordered_sum(ed, see + 1, osm);
   // 6. a_j = f32(a_j / z); 7. quantise the probability row over all N columns
   float amx = 0.0f;
   for (int j = threadIdx.x; j <= see; j += blockDim.x) {
@@ -337,58 +425,92 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
   amx = block_max_f(amx, red);
   const double asc = quant_scale(amx);
   const float as = __double2float_rn(asc);
-  for (int j = threadIdx.x; j <= see; j += blockDim.x) a8[j] = dc_clamp8(dc_js_round(__ddiv_rn((double)af[j], asc)));
+  const int nchunk = (see + 16) >> 4;  // 16-byte chunks covering keys 0..see
+  for (int j = threadIdx.x; j < nchunk * 16; j += blockDim.x)
+    a8[j] = j <= see ? dc_clamp8(dc_js_round(__ddiv_rn((double)af[j], asc))) : (int8_t)0;
   __syncthreads();
-  // 8. ctx[c] = sum_j a8[j] * v8[j][c] over j <= see (columns past `see` hold 0)
-  const int8_t* vb = v8 + (int64_t)g * max_pos * hd;
-  const int groups = blockDim.x / hd;  // ATT_THREADS / hd: 8 groups at hd 16 .. 1 at hd 128
-  const int c = threadIdx.x % hd, grp = threadIdx.x / hd;
-  if (grp < groups) {
-    int acc = 0;
-    for (int j = grp; j <= see; j += groups) acc += (int)a8[j] * (int)vb[(int64_t)j * hd + c];
-    ctxacc[grp][c] = acc;
+  // 8. ctx[c] = sum_j a8[j] * v8[c][j] over j <= see (a8 is zero past `see`)
+  const int4* a4 = (const int4*)a8;
+  const int8_t* vg = v8t + (int64_t)g * hd * ldp;
+  for (int c0 = warp * 4; c0 < hd; c0 += nwarps * 4) {
+    const int4* r0 = (const int4*)(vg + (int64_t)(c0 + 0) * ldp);
+    const int4* r1 = (const int4*)(vg + (int64_t)(c0 + 1) * ldp);
+    const int4* r2 = (const int4*)(vg + (int64_t)(c0 + 2) * ldp);
+    const int4* r3 = (const int4*)(vg + (int64_t)(c0 + 3) * ldp);
+    int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    int q = lane;
+    for (; q + 32 < nchunk; q += 64) {  // two chunks of four channels: 8 loads in flight
+      const int4 a0 = a4[q], a1 = a4[q + 32];
+      const int4 v00 = r0[q], v10 = r1[q], v20 = r2[q], v30 = r3[q];
+      const int4 v01 = r0[q + 32], v11 = r1[q + 32], v21 = r2[q + 32], v31 = r3[q + 32];
+      s0 = dp4a16(v01, a1, dp4a16(v00, a0, s0));
+      s1 = dp4a16(v11, a1, dp4a16(v10, a0, s1));
+      s2 = dp4a16(v21, a1, dp4a16(v20, a0, s2));
+      s3 = dp4a16(v31, a1, dp4a16(v30, a0, s3));
+    }
+    for (; q < nchunk; q += 32) {
+      const int4 av = a4[q];
+      s0 = dp4a16(r0[q], av, s0);
+      s1 = dp4a16(r1[q], av, s1);
+      s2 = dp4a16(r2[q], av, s2);
+      s3 = dp4a16(r3[q], av, s3);
+    }
+    for (int o = 16; o; o >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      s3 += __shfl_xor_sync(0xffffffffu, s3, o);
+    }
+    if (lane < 4) {
+      const int c = c0 + lane;
+      const int acc = lane == 0 ? s0 : lane == 1 ? s1 : lane == 2 ? s2 : s3;
+      const float o = dc_epi(acc, as, vs[g * hd + c]);
+      out[(int64_t)i * qDim + hq * hd + c] = o;
+      bad |= !isfinite(o);
+      atomicMax(rowmax + i, __float_as_uint(fabsf(o)));  // for the next GEMM's row quantisation
+    }
   }
-  __syncthreads();
-  if (threadIdx.x < hd) {
-    int acc = 0;
-    for (int gg = 0; gg < groups; gg++) acc += ctxacc[gg][threadIdx.x];
-    out[(int64_t)i * qDim + hq * hd + threadIdx.x] = dc_epi(acc, as, vs[g * hd + threadIdx.x]);
-  }
-  if (bad && threadIdx.x == 0) atomicOr(status, DC_ST_NONFINITE);
+  if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
 
-// SwiGLU of one row fused with quantizeRows of the product.
-__global__ void __launch_bounds__(NORM_THREADS) k_swiglu_quant(const float* __restrict__ h, int I,
-                                                              int8_t* __restrict__ q, int ldq,
-                                                              float* __restrict__ s, int* status) {
-  extern __shared__ float ys[];
+// SwiGLU, element-parallel over grid (ceil(I/256), rows): hid = f32(silu(g)*u)
+// with silu(v) = v / (1 + exp(-v)) in double, written over g in place, and
+// |hid| folded into the row maximum (rowmax must start at 0).  The row's
+// quantisation follows in k_rowquant once every block has contributed.
+__global__ void __launch_bounds__(256) k_swiglu(float* __restrict__ h, int I, uint32_t* __restrict__ rowmax,
+                                               int* status) {
   __shared__ float red[32];
-  const int row = blockIdx.x;
-  const float* g = h + (int64_t)row * 2 * I;
-  const float* u = g + I;
+  const int row = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  float* g = h + (int64_t)row * 2 * I;
   float mx = 0.0f;
   bool bad = false;
-  for (int j = threadIdx.x; j < I; j += blockDim.x) {
+  if (j < I) {
     const double v = g[j];
     const double sl = __ddiv_rn(v, __dadd_rn(1.0, dcm::fdlibm_exp(-v)));
-    const float y = __double2float_rn(__dmul_rn(sl, (double)u[j]));
-    bad |= !isfinite(y);
-    ys[j] = y;
-    mx = fmaxf(mx, fabsf(y));
+    const float y = __double2float_rn(__dmul_rn(sl, (double)g[I + j]));
+    bad = !isfinite(y);
+    g[j] = y;
+    mx = fabsf(y);
   }
-  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(status, DC_ST_NONFINITE);
   mx = block_max_f(mx, red);
-  const double sc = quant_scale(mx);
-  if (threadIdx.x == 0) s[row] = __double2float_rn(sc);
-  int8_t* qr = q + (int64_t)row * ldq;
-  for (int j = threadIdx.x; j < ldq; j += blockDim.x)
-    qr[j] = j < I ? dc_clamp8(dc_js_round(__ddiv_rn((double)ys[j], sc))) : (int8_t)0;
+  if (threadIdx.x == 0) atomicMax(rowmax + row, __float_as_uint(mx));
+  if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(status, DC_ST_NONFINITE);
 }
 
-__global__ void k_add_inplace(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    x[i] = __fadd_rn(x[i], y[i]);
+// quantizeRows from a finished row maximum, element-parallel over grid
+// (ceil(ldq/256), rows): s[row] = f32(max(mx/127, 1e-8)) in double, q = clamp(round(x/sc)).
+__global__ void __launch_bounds__(256) k_rowquant(const float* __restrict__ x, int64_t ldx, int cols,
+                                                 const uint32_t* __restrict__ rowmax, int8_t* __restrict__ q,
+                                                 int ldq, float* __restrict__ s) {
+  const int row = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const double sc = quant_scale(__uint_as_float(rowmax[row]));
+  if (blockIdx.x == 0 && threadIdx.x == 0) s[row] = __double2float_rn(sc);
+  if (j < ldq)
+    q[(int64_t)row * ldq + j] = j < cols ? dc_clamp8(dc_js_round(__ddiv_rn((double)x[row * ldx + j], sc))) : (int8_t)0;
 }
+
 
 __global__ void k_embed(const int32_t* __restrict__ ids, int T, const float* __restrict__ emb, int C, int V,
                         float* __restrict__ x, int* status) {
@@ -401,39 +523,56 @@ __global__ void k_embed(const int32_t* __restrict__ ids, int T, const float* __r
   for (int j = threadIdx.x; j < C; j += blockDim.x) x[(int64_t)t * C + j] = emb[(int64_t)id * C + j];
 }
 
+// One id per decode lap: ids[*stepp] (the previous lap's greedy pick).
+__global__ void k_embed_at(const int32_t* __restrict__ ids, const int* __restrict__ stepp,
+                           const float* __restrict__ emb, int C, int V, float* __restrict__ x, int* status) {
+  const int id = ids[*stepp];
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) atomicOr(status, DC_ST_BOUNDS);
+    return;
+  }
+  for (int j = threadIdx.x; j < C; j += blockDim.x) x[j] = emb[(int64_t)id * C + j];
+}
+
 __global__ void k_gather_rows(const float* __restrict__ x, int C, const int32_t* __restrict__ rows, int nrows,
                               float* __restrict__ y) {
   const int r = blockIdx.x;
   for (int j = threadIdx.x; j < C; j += blockDim.x) y[(int64_t)r * C + j] = x[(int64_t)rows[r] * C + j];
 }
 
-// Greedy pick per row (infer.js:393-395): the first index holding the maximum
-// ('>' in index order), i.e. the largest value and, among equal values
-// (-0 == +0), the smallest index.
-__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, int V, int32_t* __restrict__ out) {
-  const float* l = logits + (int64_t)blockIdx.x * V;
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int j = threadIdx.x; j < V; j += blockDim.x) {
-    const float v = l[j];
-    if (v > bv || (v == bv && j < bi)) { bv = v; bi = j; }
+// Greedy pick over a grid: the key (orderable value bits, then the complement
+// of the index) is maximal for the largest value and, among equal values, the
+// smallest index -- the first maximum that pickToken's strict '>' scan keeps
+// (infer.js:393-395).  -0 is folded to +0 first, since -0 > +0 is false there.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int j) {
+  if (v == 0.0f) v = 0.0f;
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)j);
+}
+// grid (blocks, rows): each block folds a slice of its row into keys[row] (zero beforehand).
+__global__ void __launch_bounds__(256) k_argmax_part(const float* __restrict__ logits, int V,
+                                                    unsigned long long* __restrict__ keys) {
+  const float* l = logits + (int64_t)blockIdx.y * V;
+  unsigned long long best = 0;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < V; j += gridDim.x * blockDim.x) {
+    const unsigned long long kk = argmax_key(l[j], j);
+    best = kk > best ? kk : best;
   }
-  __shared__ float sv[32];
-  __shared__ int si[32];
   for (int o = 16; o; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);
+    best = ob > best ? ob : best;
   }
-  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float b = sv[0];
-    int ix = si[0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); w++)
-      if (sv[w] > b || (sv[w] == b && si[w] < ix)) { b = sv[w]; ix = si[w]; }
-    out[blockIdx.x] = ix == 0x7fffffff ? 0 : ix;
-  }
+  if ((threadIdx.x & 31) == 0 && best) atomicMax(keys + blockIdx.y, best);
+}
+// picks[(*stepp) + row] = index of keys[row]; resets the keys for the next use.
+__global__ void k_argmax_fin(unsigned long long* __restrict__ keys, int rows, int32_t* __restrict__ out,
+                             const int* __restrict__ stepp) {
+  const int r = threadIdx.x;
+  if (r >= rows) return;
+  const unsigned long long kk = keys[r];
+  out[(stepp ? *stepp : 0) + r] = (int32_t)(0xFFFFFFFFu - (uint32_t)(kk & 0xFFFFFFFFu));
+  keys[r] = 0;
 }
 
 // ---- weight loading ----------------------------------------------------------
@@ -581,6 +720,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
   S->ldC = round_up(S->C, 16);
   S->ldQ = round_up(S->qDim, 16);
   S->ldI = round_up(S->I, 16);
+  S->ldp = round_up(max_pos, 16);
   int rc = DC_OK;
   auto fail = [&](int r) {
     dc_stage_free(S);
@@ -597,7 +737,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
     if ((rc = st_alloc(S, (void**)&kv.k8, (size_t)S->nKV * max_pos * S->hd)) ||
         (rc = st_alloc(S, (void**)&kv.ks, 4 * (size_t)S->nKV * max_pos)) ||
         (rc = st_alloc(S, (void**)&kv.v, 4 * (size_t)max_pos * S->kvDim)) ||
-        (rc = st_alloc(S, (void**)&kv.v8, (size_t)S->nKV * max_pos * S->hd)) ||
+        (rc = st_alloc(S, (void**)&kv.v8t, (size_t)S->kvDim * S->ldp)) ||
         (rc = st_alloc(S, (void**)&kv.vs, 4 * (size_t)S->kvDim)) ||
         (rc = st_alloc(S, (void**)&kv.vmax, 4 * (size_t)S->kvDim)) ||
         (rc = st_alloc(S, (void**)&kv.vchg, 4 * (size_t)S->kvDim)))
@@ -613,6 +753,11 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->ctxo, 4 * (size_t)max_rows * S->qDim)) ||
       (rc = st_alloc(S, (void**)&S->xq, (size_t)max_rows * std::max(std::max(S->ldC, S->ldQ), S->ldI))) ||
       (rc = st_alloc(S, (void**)&S->rs, 4 * (size_t)max_rows)) ||
+      (rc = st_alloc(S, (void**)&S->rowmax, 4 * (size_t)max_rows)) ||
+      (rc = st_alloc(S, (void**)&S->d_pos, 16)) || (rc = st_alloc(S, (void**)&S->d_zero, 16)) ||
+      (rc = st_alloc(S, (void**)&S->d_step, 16)) || (rc = st_alloc(S, (void**)&S->xlap, 4 * (size_t)S->C)) ||
+      (rc = st_alloc(S, (void**)&S->logits1, 4 * (size_t)(head ? S->V : 1))) ||
+      (rc = st_alloc(S, (void**)&S->amax_keys, 64)) ||
       (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
     return fail(rc);
   // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1
@@ -626,6 +771,10 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
     }
   if ((rc = upload(S, c.data(), c.size(), &S->rope_cos)) || (rc = upload(S, sn.data(), sn.size(), &S->rope_sin)))
     return fail(rc);
+  if (cudaMemsetAsync(S->amax_keys, 0, 64, ctx->stream) != cudaSuccess ||
+      cudaMemsetAsync(S->d_zero, 0, 16, ctx->stream) != cudaSuccess ||
+      cudaMemsetAsync(S->d_pos, 0, 16, ctx->stream) != cudaSuccess)
+    return fail(dc_fail(ctx, DC_E_CUDA, "stage: position init failed"));
   if ((rc = dc_stage_kv_reset(S)) || (rc = dc_sync(ctx))) return fail(rc);
   *out = S;
   return DC_OK;
@@ -634,6 +783,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
 extern "C" void dc_stage_free(dc_stage* S) {
   if (!S) return;
   if (S->ctx) cudaStreamSynchronize(S->ctx->stream);
+  if (S->lap_exec) cudaGraphExecDestroy(S->lap_exec);
   for (void* p : S->allocs) cudaFree(p);
   delete S;
 }
@@ -783,8 +933,84 @@ extern "C" int dc_stage_embed(dc_stage* S, const int32_t* ids, int T, float* x) 
   return DC_OK;
 }
 
-static int gemm(dc_stage* S, const dc_mat& m, int T, const int8_t* xq, int ldx, float* out) {
-  return dc_gemm_dispatch(S->ctx, xq, ldx, m.qt, m.ldk, S->rs, m.cs, T, m.k, m.n, 1, 0, out, S->ctx->stream, 0);
+static int launch_argmax(dc_stage* S, const float* logits, int rows, int32_t* picks, const int* stepp) {
+  cudaStream_t st = S->ctx->stream;
+  const int blocks = std::max(1, std::min(2 * S->ctx->sm_count, (S->V + 255) / 256));
+  k_argmax_part<<<dim3(blocks, rows), 256, 0, st>>>(logits, S->V, S->amax_keys);
+  dc_count_launch();
+  k_argmax_fin<<<1, 32, 0, st>>>(S->amax_keys, rows, picks, stepp);
+  dc_count_launch();
+  DC_CUDA(S->ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+static int gemm(dc_stage* S, const dc_mat& m, int T, const int8_t* xq, int ldx, float* out, unsigned flags) {
+  return dc_gemm_dispatch(S->ctx, xq, ldx, m.qt, m.ldk, S->rs, m.cs, T, m.k, m.n, 1, flags, out, S->ctx->stream, 0);
+}
+
+// The layer loop of one stage on T rows of x (in place).  Every position the
+// kernels need is read from *n0p (the cached tokens before this call; 0 for the
+// full window), so the same launches can be captured once in a CUDA graph and
+// replayed lap after lap.  n0 is the host's copy, used only to size the tiled
+// V quantisation of chunk/window calls (T > 8), which are never captured.
+static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, const int* n0p) {
+  dc_ctx* ctx = S->ctx;
+  cudaStream_t st = ctx->stream;
+  const int N = n0 + T;
+  const double scale = 1.0 / sqrt((double)S->hd);
+  const size_t att_smem = ((12 * (size_t)S->max_pos + 15) & ~(size_t)15) + (size_t)S->ldp + 16;
+  if (int rc0 = dc_set_smem(ctx, (const void*)k_attention, (int)att_smem)) return rc0;
+  const size_t nrm_smem = 12 * (size_t)S->C;  // squares (double) + the row (float)
+  // always raised: the kernel's static shared memory counts against the 48 KB default too
+  if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
+  int rc;
+  for (auto& ly : S->L) {
+    dc_kv& kv = ly.kv;
+    // attention block
+    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm1, S->spec.norm_eps, S->xq, S->ldC, S->rs,
+                                                         ctx->d_status);
+    dc_count_launch();
+    if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
+    if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
+    k_rope_append<<<dim3(T, S->nH + S->nKV + 1), 64, 0, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos,
+                                                              S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
+                                                              kv.vmax, ctx->d_status);
+    dc_count_launch();
+    k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0p);
+    dc_count_launch();
+    if (T <= 8) {
+      k_vquant_dev<<<dim3((S->max_pos + 63) / 64, (S->kvDim + 31) / 32), 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8t,
+                                                                                       T, n0p, S->kvDim, S->hd,
+                                                                                       S->ldp);
+    } else {
+      k_vquant<<<dim3((N + 63) / 64, (S->kvDim + 31) / 32), 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8t, N, n0,
+                                                                        S->kvDim, S->hd, S->ldp);
+    }
+    dc_count_launch();
+    DC_CUDA(ctx, cudaMemsetAsync(S->rowmax, 0, 4 * (size_t)T, st));
+    k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
+                                                              kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
+                                                              S->ctxo, S->rowmax, S->qDim, ctx->d_status);
+    dc_count_launch();
+    k_rowquant<<<dim3((S->ldQ + 255) / 256, T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
+                                                              S->rs);
+    dc_count_launch();
+    if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, x, DC_F_ADDTO))) return rc;  // x2 = x + attn
+    // MLP block
+    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm2, S->spec.norm_eps, S->xq, S->ldC, S->rs,
+                                                         ctx->d_status);
+    dc_count_launch();
+    if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
+    DC_CUDA(ctx, cudaMemsetAsync(S->rowmax, 0, 4 * (size_t)T, st));
+    k_swiglu<<<dim3((S->I + 255) / 256, T), 256, 0, st>>>(S->hbuf, S->I, S->rowmax, ctx->d_status);
+    dc_count_launch();
+    k_rowquant<<<dim3((S->ldI + 255) / 256, T), 256, 0, st>>>(S->hbuf, 2 * (int64_t)S->I, S->I, S->rowmax, S->xq,
+                                                              S->ldI, S->rs);
+    dc_count_launch();
+    if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, x, DC_F_ADDTO))) return rc;  // out = x2 + down
+    DC_CUDA(ctx, cudaGetLastError());
+  }
+  return DC_OK;
 }
 
 // runLayers (use_kv = 0: full window, positions 0..T-1) or runLayersChunk
@@ -792,53 +1018,141 @@ static int gemm(dc_stage* S, const dc_mat& m, int T, const int8_t* xq, int ldx, 
 extern "C" int dc_stage_forward(dc_stage* S, float* x, int T, int pos0, int use_kv) {
   if (!S || !x || T < 1 || T > S->max_rows) return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_forward: bad T");
   dc_ctx* ctx = S->ctx;
-  cudaStream_t st = ctx->stream;
   const int n0 = use_kv ? S->kv_len : 0;
   const int N = n0 + T;
   if (use_kv && pos0 != n0)
     return dc_fail(ctx, DC_E_INVAL, "stage_forward: chunk position %d does not follow the cached %d tokens", pos0, n0);
   if (N > S->max_pos || pos0 + T > S->max_pos)
     return dc_fail(ctx, DC_E_INVAL, "stage_forward: %d positions exceed max_pos %d", N, S->max_pos);
-  const double scale = 1.0 / sqrt((double)S->hd);
-  const size_t att_smem = (size_t)S->max_pos * (8 + 4 + 1) + 64;
-  if (att_smem > 48 * 1024)
-    DC_CUDA(ctx, cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)att_smem));
-  const size_t swi_smem = 4 * (size_t)S->I;
-  if (swi_smem > 48 * 1024)
-    DC_CUDA(ctx, cudaFuncSetAttribute(k_swiglu_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)swi_smem));
-  const size_t nrm_smem = 4 * (size_t)S->C;
-  if (nrm_smem > 48 * 1024)
-    DC_CUDA(ctx, cudaFuncSetAttribute(k_rmsnorm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)nrm_smem));
-  int rc;
-  for (auto& ly : S->L) {
-    dc_kv& kv = ly.kv;
-    // attention block
-    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm1, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status); dc_count_launch();
-    if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf))) return rc;
-    if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
-    k_rope_append<<<T, 128, 4 * (size_t)S->kvDim, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos,
-                                                          S->rope_sin, pos0, n0, S->max_pos, kv.k8, kv.ks, kv.v,
-                                                          kv.vmax, ctx->d_status); dc_count_launch();
-    k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0 == 0 ? 1 : 0); dc_count_launch();
-    dim3 vq((N + 63) / 64, (S->kvDim + 31) / 32);
-    k_vquant<<<vq, 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8, N, n0, S->kvDim, S->hd, S->max_pos); dc_count_launch();
-    dim3 ag(S->nH, T);
-    k_attention<<<ag, ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8, kv.vs,
-                                                   N, n0, S->max_pos, scale, S->ctxo, S->qDim, ctx->d_status); dc_count_launch();
-    if ((rc = dc_launch_quant_rows(ctx, S->ctxo, T, S->qDim, S->xq, S->ldQ, S->rs, st))) return rc;
-    if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, S->hbuf))) return rc;
-    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C); dc_count_launch();
-    // MLP block
-    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm2, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status); dc_count_launch();
-    if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf))) return rc;
-    k_swiglu_quant<<<T, NORM_THREADS, swi_smem, st>>>(S->hbuf, S->I, S->xq, S->ldI, S->rs, ctx->d_status); dc_count_launch();
-    if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, S->hbuf))) return rc;
-    k_add_inplace<<<std::min(1024, (T * S->C + 255) / 256), 256, 0, st>>>(x, S->hbuf, (int64_t)T * S->C); dc_count_launch();
-    DC_CUDA(ctx, cudaGetLastError());
+  if (S->L.empty()) return DC_OK;
+  const int* n0p = S->d_zero;
+  if (use_kv) {
+    k_setpos<<<1, 1, 0, ctx->stream>>>(S->d_pos, n0);
+    dc_count_launch();
+    n0p = S->d_pos;
   }
+  int rc = forward_layers(S, x, T, n0, use_kv, n0p);
+  if (rc) return rc;
   if (use_kv) S->kv_len = N;
+  return DC_OK;
+}
+
+// One decode lap of the whole ring on one device: greedy pick from the
+// previous lap's hidden row (logitsAt, infer.js:324-334 + pickToken :393-395)
+// into picks[step], embedRows of that id (:298-310), runLayersChunk on every
+// stage (:288-296), step + 1 -- the chunked decode loop of infer.js:353-365
+// (app.js:907-921) with the token id never leaving the device.
+static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
+  dc_stage* H = st[0];
+  dc_ctx* ctx = H->ctx;
+  cudaStream_t s = ctx->stream;
+  const size_t nrm_smem = 12 * (size_t)H->C;  // squares (double) + the row (float)
+  // always raised: the kernel's static shared memory counts against the 48 KB default too
+  if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
+  k_rmsnorm_quant<<<1, NORM_THREADS, nrm_smem, s>>>(H->xlap, H->C, H->nrmF, H->spec.norm_eps, H->xq, H->ldC, H->rs,
+                                                     ctx->d_status);
+  dc_count_launch();
+  int rc = dc_gemm_dispatch(ctx, H->xq, H->ldC, H->lm.qt, H->lm.ldk, H->rs, H->lm.cs, 1, H->C, H->V, 1, 0, H->logits1,
+                            s, 0);
+  if (rc) return rc;
+  if ((rc = launch_argmax(H, H->logits1, 1, picks, H->d_step))) return rc;
+  k_embed_at<<<1, 256, 0, s>>>(picks, H->d_step, H->emb, H->C, H->V, H->xlap, ctx->d_status);
+  dc_count_launch();
+  for (int i = 0; i < ns; i++) {
+    dc_stage* S = st[i];
+    if (S->L.empty()) continue;
+    if ((rc = forward_layers(S, H->xlap, 1, S->kv_len, 1, S->d_pos))) return rc;
+    k_addpos<<<1, 1, 0, s>>>(S->d_pos, 1);
+    dc_count_launch();
+  }
+  k_addpos<<<1, 1, 0, s>>>(H->d_step, 1);
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+// n_new decode laps over stages[0..ns) (all on the context's device, stage 0
+// the head), starting from `x_last` (device, one hidden row: the last row of
+// the prefill's output).  picks (device int32, n_new) receive the greedy ids.
+// With use_graph, lap 0 runs as ordinary launches and one lap is captured as a
+// CUDA graph (cached on the head for this stage list) and replayed for the rest.
+extern "C" int dc_decode_run(dc_stage** stages, int ns, const float* x_last, int n_new, int32_t* picks,
+                             int use_graph) {
+  if (!stages || ns < 1 || !stages[0] || !stages[0]->head || !x_last || !picks || n_new < 0)
+    return dc_fail(stages && stages[0] ? stages[0]->ctx : nullptr, DC_E_INVAL, "decode_run: bad arguments");
+  dc_stage* H = stages[0];
+  dc_ctx* ctx = H->ctx;
+  cudaStream_t s = ctx->stream;
+  for (int i = 0; i < ns; i++) {
+    if (!stages[i] || stages[i]->ctx != ctx) return dc_fail(ctx, DC_E_INVAL, "decode_run: stages must share a context");
+    if (stages[i]->kv_len + n_new > stages[i]->max_pos)
+      return dc_fail(ctx, DC_E_INVAL, "decode_run: %d + %d positions exceed max_pos %d", stages[i]->kv_len, n_new,
+                     stages[i]->max_pos);
+  }
+  if (n_new == 0) return DC_OK;
+  // Work on the context's own stream (the legacy default stream cannot be
+  // captured): it waits for the caller's stream, and the caller's stream waits
+  // for it when the laps are enqueued.
+  struct StreamSwap {
+    dc_ctx* c;
+    cudaStream_t user;
+    bool on;
+    StreamSwap(dc_ctx* c_) : c(c_), user(c_->stream), on(false) {}
+    ~StreamSwap() {
+      if (on) {
+        cudaEventRecord(c->ev_join, c->own_stream);
+        cudaStreamWaitEvent(user, c->ev_join, 0);
+        c->stream = user;
+      }
+    }
+  } swap(ctx);
+  if (ctx->stream != ctx->own_stream) {
+    DC_CUDA(ctx, cudaEventRecord(ctx->ev_fork, ctx->stream));
+    DC_CUDA(ctx, cudaStreamWaitEvent(ctx->own_stream, ctx->ev_fork, 0));
+    ctx->stream = ctx->own_stream;
+    swap.on = true;
+  }
+  s = ctx->stream;
+  DC_CUDA(ctx, cudaMemcpyAsync(H->xlap, x_last, 4 * (size_t)H->C, cudaMemcpyDeviceToDevice, s));
+  k_setpos<<<1, 1, 0, s>>>(H->d_step, 0);
+  dc_count_launch();
+  for (int i = 0; i < ns; i++) {
+    k_setpos<<<1, 1, 0, s>>>(stages[i]->d_pos, stages[i]->kv_len);
+    dc_count_launch();
+  }
+  int rc = decode_lap(stages, ns, picks);
+  if (rc) return rc;
+  if (n_new > 1) {
+    if (use_graph) {
+      std::vector<dc_stage*> key(stages, stages + ns);
+      if (!H->lap_exec || H->lap_key != key || H->lap_picks != picks) {
+        if (H->lap_exec) cudaGraphExecDestroy(H->lap_exec);
+        H->lap_exec = nullptr;
+        const bool timing = ctx->timing;
+        ctx->timing = false;  // no per-GEMM timing events inside the captured lap
+        cudaGraph_t g = nullptr;
+        DC_CUDA(ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+        rc = decode_lap(stages, ns, picks);
+        cudaError_t e = cudaStreamEndCapture(s, &g);
+        ctx->timing = timing;
+        if (rc) {
+          if (g) cudaGraphDestroy(g);
+          return rc;
+        }
+        if (e != cudaSuccess) return dc_cuda_fail(ctx, e, "cudaStreamEndCapture");
+        e = cudaGraphInstantiate(&H->lap_exec, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return dc_cuda_fail(ctx, e, "cudaGraphInstantiate");
+        H->lap_key = key;
+        H->lap_picks = picks;
+      }
+      for (int n = 1; n < n_new; n++) DC_CUDA(ctx, cudaGraphLaunch(H->lap_exec, s));
+    } else {
+      for (int n = 1; n < n_new; n++)
+        if ((rc = decode_lap(stages, ns, picks))) return rc;
+    }
+  }
+  for (int i = 0; i < ns; i++) stages[i]->kv_len += n_new;
   return DC_OK;
 }
 
@@ -855,16 +1169,15 @@ extern "C" int dc_stage_logits(dc_stage* S, const float* x, int T, const int32_t
   for (int r = 0; r < nrows; r++)
     DC_CUDA(ctx, cudaMemcpyAsync(S->lx + (size_t)r * S->C, x + (size_t)rows[r] * S->C, 4 * (size_t)S->C,
                                  cudaMemcpyDeviceToDevice, st));
-  const size_t nrm_smem = 4 * (size_t)S->C;
+  const size_t nrm_smem = 12 * (size_t)S->C;  // squares (double) + the row (float)
+  // always raised: the kernel's static shared memory counts against the 48 KB default too
+  if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
   k_rmsnorm_quant<<<nrows, NORM_THREADS, nrm_smem, st>>>(S->lx, S->C, S->nrmF, S->spec.norm_eps, S->xq, S->ldC, S->rs,
                                                           ctx->d_status); dc_count_launch();
   int rc = dc_gemm_dispatch(ctx, S->xq, S->ldC, S->lm.qt, S->lm.ldk, S->rs, S->lm.cs, nrows, S->C, S->V, 1, 0,
                             logits, st, 0);
   if (rc) return rc;
-  if (picks) {
-    k_argmax<<<nrows, 1024, 0, st>>>(logits, S->V, picks);
-    dc_count_launch();
-  }
+  if (picks && (rc = launch_argmax(S, logits, nrows, picks, nullptr))) return rc;
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }
@@ -883,5 +1196,33 @@ extern "C" int dc_stage_kv_read(dc_stage* S, int layer, int8_t* k8, float* ks, f
                                  cudaMemcpyDeviceToHost));
   }
   if (v) DC_CUDA(S->ctx, cudaMemcpy(v, kv.v, 4 * (size_t)n * S->kvDim, cudaMemcpyDeviceToHost));
+  return DC_OK;
+}
+
+// ---- standalone row operations (parity access to the fused kernels' math) ----
+__global__ void __launch_bounds__(256) k_ordered_sum(const double* __restrict__ t, int n, double* __restrict__ out) {
+  __shared__ dco::Smem osm;
+  const double v = dco::ordered_sum(t + (int64_t)blockIdx.x * n, n, osm);
+  if (threadIdx.x == 0) out[blockIdx.x] = v;
+}
+
+extern "C" int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double* out) {
+  if (!ctx || rows < 0 || n < 0 || (rows && (!out || (n && !terms)))) return dc_fail(ctx, DC_E_INVAL, "ordered_sum: bad arguments");
+  if (!rows) return DC_OK;
+  k_ordered_sum<<<rows, 256, 0, ctx->stream>>>(terms, n, out);
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+extern "C" int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y) {
+  if (!ctx || rows < 0 || cols < 1 || (rows && (!x || !w || !y))) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: bad arguments");
+  if ((size_t)cols * 12 > 200 * 1024) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: row of %d does not fit on chip", cols);
+  if (!rows) return DC_OK;
+  const int smem = 12 * cols;
+  if (int rc = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, smem)) return rc;
+  k_rmsnorm_quant<<<rows, NORM_THREADS, smem, ctx->stream>>>(x, cols, w, eps, nullptr, 0, nullptr, ctx->d_status, y);
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
 }

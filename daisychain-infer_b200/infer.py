@@ -186,6 +186,16 @@ class Stage:
         self._check(self.L.dc_stage_embed(self.h, C.c_void_p(picks.data_ptr() + 4 * n), 1, _ptr(x)), "stage_embed")
         return x
 
+    def decode_many(self, stages, last, n_new: int, use_graph: bool = True):
+        """n_new chunked-decode laps over `stages` (this stage is the head, all on
+        one device) from the last hidden row of `last`; returns the device ids."""
+        picks = self.new_ids(n_new)
+        row = last[last.numel() - self.spec.hidden:]
+        arr = (C.c_void_p * len(stages))(*[s.h.value for s in stages])
+        self._check(self.L.dc_decode_run(arr, len(stages), _ptr(row), n_new, _ptr(picks), 1 if use_graph else 0),
+                    "decode_run")
+        return picks
+
     def broadcast_ids(self, buf) -> None:
         import torch.distributed as dist
         dist.broadcast(buf, src=0)
@@ -254,8 +264,11 @@ def generate_lookahead(stages, ids0, n_new: int, T: int, max_draft: int = 4) -> 
     return ids
 
 
-def generate_chunked(stages, ids0, n_new: int, chunk_size: int) -> list:
-    """infer.js:339-367, greedy: chunked prefill on per-stage KV, then one token per lap."""
+def generate_chunked(stages, ids0, n_new: int, chunk_size: int, use_device_loop: bool = True,
+                     use_graph: bool = True) -> list:
+    """infer.js:339-367, greedy: chunked prefill on per-stage KV, then one token per lap.
+    The decode laps run on the device (dc_decode_run, optionally one CUDA graph
+    replayed per lap); use_device_loop=False runs them from the host instead."""
     head = stages[0]
     ids = list(ids0)
     for S in stages:
@@ -263,6 +276,9 @@ def generate_chunked(stages, ids0, n_new: int, chunk_size: int) -> list:
     last = None
     for ch in shard.prefill_chunks(len(ids), chunk_size, 1)["chunks"]:
         last = run_ring(stages, head.embed_rows(ids[ch["lo"]:ch["hi"]]), ch["lo"])
+    if use_device_loop:
+        picks = head.decode_many(stages, last, n_new, use_graph)
+        return ids + picks[:n_new].cpu().tolist()
     for _ in range(n_new):
         rows = last.numel() // head.spec.hidden
         picks, _ = head.logits_at(last, [rows - 1])

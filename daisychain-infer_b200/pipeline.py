@@ -69,6 +69,7 @@ class Ring:
         self.nxt = (rank + 1) % world
         self.prv = (rank - 1) % world
         self.new_buffer = new_buffer  # new_buffer(n_floats) -> tensor on this rank's device
+        self.use_graph = True
 
     # ---- chunked prefill + decode --------------------------------------------------
     def generate_chunked(self, ids0: list, n_new: int, chunk_size: int = 16, window: int = 2, on_prefill=None):
@@ -122,6 +123,8 @@ class Ring:
 
     def _decode_local(self, last, n_prompt: int, n_new: int):
         S = self.stage
+        if hasattr(S, "decode_many"):  # the device loop (one CUDA graph per lap)
+            return S.decode_many([S], last, n_new, use_graph=self.use_graph)
         picks = S.new_ids(n_new)
         for n in range(n_new):
             rows = last.numel() // self.hidden

@@ -151,6 +151,19 @@ int dc_weight_info(const dc_weight* w, const int8_t** qt, int* ldw, const float*
  * buffers: out (m x n f32) = epilogue(quantizeRows(X) x W).  Asynchronous. */
 int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned flags, void* out);
 
+/* ---- row operations of the layer forward, device buffers ---------------------
+ * The stage kernels' own math, callable on its own (asynchronous; non-finite
+ * input is reported by dc_sync).
+ * dc_ordered_sum_dev: out[r] = the serial double sum of terms[r*n .. r*n+n) in
+ *   index order, each add rounded to nearest even -- the chains of infer.js
+ *   rmsnorm (:73-76) and softmax (:100-104), computed by a block in parallel
+ *   and bit-identical to the serial loop for every input.
+ * dc_rmsnorm_dev: y = infer.js rmsnorm (:70-80) of each of `rows` rows of
+ *   `cols` floats with weight w (cols * 12 bytes must fit on chip: cols <=
+ *   17066). */
+int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double* out);
+int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y);
+
 /* ---- kernel probe (webgpu.js:998-1060) --------------------------------------
  * Runs the seeded probe GEMM (m=24 k=96 n=24 batch=2, acc) through the live
  * kernels; returns the FNV-1a of the int32 result (before the reference folds in
@@ -194,6 +207,14 @@ int dc_stage_forward(dc_stage* stage, float* x, int T, int pos0, int use_kv);
  * may be NULL), first maximum wins (infer.js:393-395). */
 int dc_stage_logits(dc_stage* stage, const float* x, int T, const int32_t* rows, int nrows, float* logits,
                     int32_t* picks);
+/* The chunked-decode loop (infer.js:353-365, app.js:907-921) for stages[0..ns)
+ * sharing one context (stages[0] the head): n_new laps, each the greedy pick of
+ * the previous lap's hidden row, its embedding, and runLayersChunk on every
+ * stage.  x_last (device) is the hidden row the first pick reads (the last row
+ * of the prefill output); picks (device int32[n_new]) receive the ids, which
+ * never leave the device between laps.  use_graph = 1 captures one lap as a
+ * CUDA graph (kernel positions live in device memory) and replays it. */
+int dc_decode_run(dc_stage** stages, int ns, const float* x_last, int n_new, int32_t* picks, int use_graph);
 /* The chunk path's cache: reset, and the number of cached tokens. */
 int dc_stage_kv_reset(dc_stage* stage);
 int dc_stage_kv_len(const dc_stage* stage);

@@ -1,0 +1,102 @@
+"""Row operations of the layer forward on the B200, bit for bit.
+
+The serial double chains of infer.js (rmsnorm's sum of squares, :73-76; the
+softmax denominator, :100-104) are computed on the device by a whole block; the
+result must equal the one-add-at-a-time loop for every input -- including the
+inputs built to defeat the parallel path: ties that depend on the running
+sum's last bit, sums landing exactly on powers of two, subnormal terms, sums
+that change binade at every term, and terms that are negative or not finite.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def serial(row):
+    s = 0.0
+    for v in row:
+        s += float(v)
+    return s
+
+
+def run_sum(comp, rows):
+    import torch
+    n = len(rows[0])
+    t = torch.tensor(np.array(rows, np.float64).reshape(-1), dtype=torch.float64, device="cuda")
+    out = torch.empty(len(rows), dtype=torch.float64, device="cuda")
+    comp.ordered_sum_dev(t, len(rows), n, out)
+    comp.sync()
+    return out.cpu().numpy()
+
+
+def check(comp, rows):
+    got = run_sum(comp, rows)
+    for r, g in zip(rows, got):
+        want = serial(r)
+        if np.isnan(want):
+            assert np.isnan(g)
+        else:
+            assert np.float64(g).tobytes() == np.float64(want).tobytes(), (len(r), g, want)
+
+
+@pytest.mark.parametrize("n", [0, 1, 2, 3, 31, 32, 33, 255, 256, 257, 1000, 4096, 5000, 8192, 20000])
+def test_random_terms(comp, n):
+    rng = np.random.default_rng(n)
+    rows = [rng.random(n), rng.random(n) ** 8, rng.standard_normal(n).astype(np.float32).astype(np.float64) ** 2,
+            np.exp(-rng.random(n) * 40.0), np.exp(-rng.random(n) * 800.0)]
+    check(comp, [list(r) for r in rows])
+
+
+def test_ties_follow_the_running_sum(comp):
+    h = 2.0 ** -53
+    rows = [
+        [1.0] + [h] * 999,                                   # every add ties and rounds back to 1
+        [1.0, 2.0 ** -52] + [h] * 998,                       # odd last bit: the first tie rounds up
+        [1.0] + [h, 2.0 ** -52] * 500,
+        [1.5] + [3 * h] * 999,                               # 1.5 ulp: ties at every step
+        [4.0] + [2.0 ** -51, 2.0 ** -50, 2.0 ** -51] * 333,
+        [1.0] + ([2.0 ** -40] * 24 + [h]) * 20,              # a few ties: handled as explicit terms
+        [1.0, 2.0 ** -52] + ([2.0 ** -40] * 30 + [h, h]) * 15,
+    ]
+    n = max(len(r) for r in rows)
+    check(comp, [r + [0.0] * (n - len(r)) for r in rows])
+
+
+def test_sums_on_binade_edges(comp):
+    rows = [[1.0] * 4096, [0.5] * 4096, [0.25, 0.75] * 2048, [2.0 ** -1074] * 4096, [0.0] * 4096,
+            [2.0 ** -1022 - 2.0 ** -1074] + [2.0 ** -1074] * 4095,
+            [1.0 - 2.0 ** -53] * 4096]
+    check(comp, rows)
+
+
+def test_binade_at_every_term_falls_back_exactly(comp):
+    rows = [[2.0 ** j for j in range(300)] + [1e-3] * 212,
+            [2.0 ** (j - 800) * (1 + 2.0 ** -40) for j in range(512)],
+            list(np.random.default_rng(5).random(512) * 2.0 ** np.arange(512) / 2.0 ** 400)]
+    check(comp, rows)
+
+
+def test_negative_and_non_finite_terms_take_the_serial_loop(comp):
+    rng = np.random.default_rng(9)
+    a = list(rng.standard_normal(3000))
+    b = list(rng.random(3000)); b[1234] = float("inf")
+    c = list(rng.random(3000)); c[17] = float("nan")
+    d = list(rng.random(3000)); d[2999] = -0.0
+    check(comp, [a, b, c, d])
+
+
+@pytest.mark.parametrize("cols", [64, 1000, 4096, 5120, 8192, 14336])
+def test_rmsnorm_matches_oracle(comp, O, cols):
+    import torch
+    rng = np.random.default_rng(cols)
+    rows = 5
+    x = (rng.standard_normal((rows, cols)) * np.array([1e-3, 1.0, 30.0, 1e4, 1e-20])[:, None]).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    want = O.rmsnorm(x, rows, cols, w, 1e-5).reshape(rows, cols)
+    xd = torch.tensor(x, device="cuda")
+    wd = torch.tensor(w, device="cuda")
+    y = torch.empty_like(xd)
+    comp.rmsnorm_dev(xd, rows, cols, wd, 1e-5, y)
+    comp.sync()
+    assert y.cpu().numpy().tobytes() == want.tobytes()

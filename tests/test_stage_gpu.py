@@ -105,6 +105,18 @@ def test_chunked_prefill_matches_oracle(comp, O, P, fixture):
         assert got == ref
 
 
+def test_decode_loop_modes_agree(comp, O, P, fixture):
+    """The device decode loop, replayed as one CUDA graph per lap, equals the
+    un-captured device loop and the host-driven loop (and the oracle)."""
+    ospec, spec, w, om = fixture
+    prompt = [9, 8, 7, 6, 5, 4, 3, 2, 1, 0, 11, 12, 13]
+    ref = O.generate_chunked(om, [(0, 6)], prompt, 12, 5)
+    for kw in (dict(use_device_loop=False), dict(use_graph=False), dict(use_graph=True)):
+        for splits in ([6], [0, 3, 3]):
+            got = P.infer.generate_chunked(make_stages(P, comp, spec, w, splits), prompt, 12, 5, **kw)
+            assert got == ref, (kw, splits)
+
+
 def test_kv_cache_contents_match_oracle(comp, O, P, fixture):
     ospec, spec, w, om = fixture
     ids = [1, 2, 3, 4, 5]
@@ -168,8 +180,10 @@ def synth_model(O, P, hidden, layers, heads, kv, inter, vocab, tie, theta=10000.
 
 @pytest.mark.parametrize("cfg", [dict(hidden=256, layers=2, heads=4, kv=2, inter=512, vocab=1000, tie=True),
                                  dict(hidden=512, layers=2, heads=4, kv=1, inter=1024, vocab=777, tie=False,
+                                      theta=500000.0),
+                                 dict(hidden=4096, layers=1, heads=32, kv=8, inter=1024, vocab=512, tie=False,
                                       theta=500000.0)],
-                         ids=["hd64-tied", "hd128-untied"])
+                         ids=["hd64-tied", "hd128-untied", "hidden4096"])
 def test_synthetic_model_device_generator_matches_oracle(comp, O, P, cfg):
     ospec, spec, w = synth_model(O, P, **cfg)
     om = O.Model(ospec, w)
