@@ -265,9 +265,11 @@ def bench_model(args, rank, world, peaks):
     clocks.start()
     comp.L.dc_timing(comp.h, 1)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     t0.record()
     outs = [one_step() for _ in range(args.steps)]
     t1.record()
+    torch.cuda.nvtx.range_pop()
     gen_ids = None
     if rank == 0:
         o = outs[-1]
@@ -289,6 +291,25 @@ def bench_model(args, rank, world, peaks):
         comp.L.dc_timing_read(comp.h, kind, C.byref(ms), C.byref(n), C.byref(by), C.byref(op))
         kinds[kind] = (ms.value, n.value, by.value, op.value)
     comp.L.dc_timing(comp.h, 0)
+    # On one GPU the timed decode laps are CUDA-graph replays, which carry no
+    # per-GEMV events: the GEMV launch duration is measured right after the
+    # timed region on the same stage and shapes, in 16 un-captured laps.
+    gemv_method = "CUDA events around every GEMV launch in the timed region"
+    if world == 1 and w["mode"] == "chunked" and getattr(ring, "use_graph", False):
+        ring.use_graph = False
+        comp.L.dc_timing(comp.h, 1)
+        ring.generate_chunked(ids, 16, w["chunk"], w["window"])
+        ms_, n_, by_, op_ = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
+        comp.L.dc_timing_read(comp.h, 1, C.byref(ms_), C.byref(n_), C.byref(by_), C.byref(op_))
+        comp.L.dc_timing(comp.h, 0)
+        ring.use_graph = True
+        laps = w["new"] * args.steps
+        per_lap = n_.value / 16.0
+        scale = laps * per_lap / max(n_.value, 1)
+        kinds[1] = (ms_.value * scale, int(round(laps * per_lap)), by_.value * scale, op_.value * scale)
+        gemv_method = ("CUDA events around every GEMV launch of 16 un-captured decode laps run right after the "
+                       "timed region (same stage, same shapes; the timed laps are CUDA-graph replays), scaled to "
+                       "the timed region's laps")
     ms_step, pre, dec = max_over_ranks([ms_step, pre, dec], world)
     launches = int(sum_over_ranks([launches], world)[0])
     n_new = w["new"]
@@ -303,9 +324,11 @@ def bench_model(args, rank, world, peaks):
         ach = by / (ms / 1e3) / 1e9
         roof = dict(bound="hbm", achieved=ach, peak=peaks["hbm_gbs"], unit="GB/s", frac=ach / peaks["hbm_gbs"],
                     traffic=traffic_for("gemv_decode" if dom == 1 else "tc_prefill"),
-                    kernel=("k_gemv (decode GEMV, M<=8)" if dom == 1 else "k_gemm_tc (tcgen05, M>8)"),
+                    kernel=("k_gemv_bulk (decode GEMV, M<=8)" if dom == 1 else "k_gemm_tc (tcgen05, M>8)"),
                     launches=n, avg_launch_us=per_launch_ms * 1e3, share_of_step=ms / (ms_step * args.steps),
                     algorithmic_bytes_per_launch=by / max(n, 1), ops_per_launch=op / max(n, 1),
+                    method=(gemv_method if dom == 1 else "CUDA events around every tcgen05 GEMM launch in the "
+                            "timed region"),
                     peak_source=f"{peaks['src']} HBM copy bandwidth (MEASURED_PEAKS.json)")
         other = {("gemv" if k == 1 else "tcgen05"): dict(ms=kinds[k][0], launches=kinds[k][1],
                                                           gbs=(kinds[k][2] / (kinds[k][0] / 1e3) / 1e9
@@ -571,6 +594,48 @@ def bench_gemm_sweep(args, rank, world, peaks):
     return line
 
 
+def profile_model(args):
+    """One prefill chunk or one decode lap of the workload, inside an NVTX range
+    named "profile", for an ncu launch list of exactly that unit of work:
+
+        ncu --nvtx --nvtx-include "profile/" --metrics gpu__time_duration.sum ...
+            python bench.py --profile decode
+
+    The prompt is prefilled first (outside the range), so the profiled chunk or
+    lap sees the full-length KV cache of the benchmark.  Prints what it ran."""
+    import torch
+    import __graft_entry__ as G
+    P = G.package()
+    w = WORKLOADS[args.workload]
+    assert w["mode"] == "chunked", "--profile takes a chunked workload"
+    comp = P.init_compute(0, stream=torch.cuda.current_stream())
+    spec, plan, S, ring = build_rank(P, comp, w, 0, 1)
+    ids = prompt_ids(w, spec.vocab)
+    chunks = P.shard.prefill_chunks(len(ids), w["chunk"], w["window"])["chunks"]
+    S.kv_reset()
+    last = None
+    for i, ch in enumerate(chunks):
+        inside = args.profile == "prefill" and i == len(chunks) - 1
+        if inside:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_push("profile")
+        last = S.run_layers_chunk(S.embed_rows(ids[ch["lo"]:ch["hi"]]), ch["lo"])
+        if inside:
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
+    if args.profile == "decode":
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("profile")
+        S.decode_many([S], last, 1, use_graph=False)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    comp.sync()
+    S.close()
+    return dict(profiled=args.profile, workload=args.workload, prompt=len(ids),
+                unit=("the last prefill chunk (rows %d..%d)" % (chunks[-1]["lo"], chunks[-1]["hi"])
+                      if args.profile == "prefill" else "one decode lap at KV length %d" % len(ids)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -582,6 +647,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--prompt-len", type=int, default=0, help="override the prompt length (profiling runs)")
     ap.add_argument("--new-tokens", type=int, default=0, help="override the generated tokens (profiling runs)")
+    ap.add_argument("--profile", choices=["prefill", "decode"], default=None,
+                    help="run one prefill chunk or one decode lap inside an NVTX range 'profile' (for ncu); "
+                         "prints no benchmark line")
     args = ap.parse_args()
     if args.workload in WORKLOADS:
         w = WORKLOADS[args.workload]
@@ -591,6 +659,9 @@ def main():
             w["new"] = args.new_tokens
     args.warmup = max(args.warmup, 3)
     peaks = load_peaks()
+    if args.profile:
+        print(json.dumps(profile_model(args)), flush=True)
+        return
     if args.impl == "reference":
         line = bench_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))
         if line is not None:

@@ -246,6 +246,7 @@ int dc_set_smem(dc_ctx* ctx, const void* func, int bytes) {
 
 static std::atomic<unsigned long long> g_launches{0};
 void dc_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void dc_count_launches(long long n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 extern "C" unsigned long long dc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" int dc_set_stream(dc_ctx* c, void* stream) {

@@ -84,6 +84,7 @@ int dc_set_smem(dc_ctx* ctx, const void* func, int bytes);
 
 // Kernels launched by this library in this process (reported by dc_launch_count).
 void dc_count_launch();
+void dc_count_launches(long long n);  // e.g. the kernels of one CUDA-graph replay
 
 // ---- launchers shared between translation units ----------------------------
 int dc_launch_quant_rows(dc_ctx* ctx, const float* X, int rows, int cols, int8_t* q, int ldq, float* s,
@@ -113,6 +114,38 @@ __device__ __forceinline__ double dc_js_round(double v) {
 __device__ __forceinline__ int8_t dc_clamp8(double v) {
   return v < -128.0 ? (int8_t)-128 : v > 127.0 ? (int8_t)127 : (int8_t)(int)v;
 }
+// The correctly rounded double quotient, out of line (one copy of the
+// division's code per kernel; reached only from the checks below).
+static __device__ __noinline__ double dc_ddiv_slow(double a, double b) { return __ddiv_rn(a, b); }
+
+// clamp8(Math.round(v / s)) for s > 0 with |v / s| below a few hundred (every
+// quantiser here: s >= max|v| / 127, rounded).  rs = 1/s (any rounding).  The
+// quotient comes from v * rs, within a few ulp of the rounded v / s; only when
+// that lands within 2^-20 of a half-integer -- where Math.round's decision
+// could depend on the last bits -- is the correctly rounded quotient taken.
+__device__ __forceinline__ int8_t dc_quant_div(double v, double s, double rs) {
+  double q = __dmul_rn(v, rs);
+  const double f = __dsub_rn(q, floor(q));
+  if (fabs(__dsub_rn(f, 0.5)) < 9.5367431640625e-07) q = dc_ddiv_slow(v, s);
+  return dc_clamp8(dc_js_round(q));
+}
+
+// f32(a / z) for a >= 0, z > 0 (the double quotient rounded to float): from
+// a * rz (rz = 1/z, any rounding) unless that lies within 2^-40 (relative) of
+// a midpoint between two floats, or at a power of two or below the normal
+// range, where the correctly rounded double quotient decides.
+__device__ __forceinline__ float dc_div_to_f32(double a, double z, double rz) {
+  const double q = __dmul_rn(a, rz);
+  const float f = __double2float_rn(q);
+  const unsigned fb = __float_as_uint(f);
+  const int fe = (int)((fb >> 23) & 0xff);
+  if (fe <= 1 || fe >= 254 || (fb & 0x7fffff) == 0) return __double2float_rn(dc_ddiv_slow(a, z));
+  const double hu = __longlong_as_double((long long)(fe - 151 + 1023) << 52);  // half a float ulp at f
+  const double d = fabs(__dsub_rn(q, (double)f));
+  if (fabs(__dsub_rn(d, hu)) < q * 9.094947017729282e-13) return __double2float_rn(dc_ddiv_slow(a, z));
+  return f;
+}
+
 // verified_core.js:227-228: f32(f32(f32(s) * a) * b), each step rounded.
 __device__ __forceinline__ float dc_epi(int32_t s, float a, float b) {
   return __fmul_rn(__fmul_rn(__int2float_rn(s), a), b);

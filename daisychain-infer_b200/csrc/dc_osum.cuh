@@ -34,7 +34,7 @@
 
 namespace dco {
 
-constexpr int MAXSEG = 96;                     // explicit terms per row (else serial)
+constexpr int MAXW = 24;                       // explicit terms per warp and chunk (else serial)
 constexpr double DELTA = 1.0 / 68719476736.0;  // 2^-36 margin around binade edges
 constexpr unsigned long long CAP = 1ull << 54; // saturation of the composed constants
 
@@ -44,18 +44,21 @@ struct Fn {
   int t;
 };
 
+// Per warp: its explicit terms (value, and the map of the stretch that
+// follows each up to the next explicit term of the warp), the map of its terms
+// before the first explicit one (head) and after the last (tail), or of all
+// its terms when it has none (kept in tail).
+struct Entry {
+  double v;
+  unsigned long long c1, c2;
+  int t, emin, emax;
+};
 struct Smem {
-  unsigned long long c1[MAXSEG], c2[MAXSEG];  // composed map of stretch s (after explicit term s)
-  int ft[MAXSEG];
-  int expl[MAXSEG];                           // index of explicit term s
-  int emin[MAXSEG], emax[MAXSEG];             // binades its terms were rounded in (must agree)
-  unsigned long long wc1[32], wc2[32];
-  int wt[32], wr[32];
-  double wtot[32];
-  int wcnt[32];
-  int wbad[32];
-  int nseg;
-  double tv[MAXSEG];                           // value of explicit term s
+  Entry ent[8][MAXW];
+  Entry whead[8], wtail[8];  // v unused
+  int wn[8];                 // explicit terms of warp w
+  int wbad[8];
+  double wtot[8];
   double result;
 };
 
@@ -96,43 +99,35 @@ __device__ __forceinline__ int binade(double x) {
 // (r then holds its floor).  t/u >= 2^53 only happens for a term that moves
 // the sum out of the binade, which is explicit; r then saturates and the
 // stretch check fails.
-__device__ __forceinline__ void units(double t, int E, unsigned long long& r, bool& tie) {
-  constexpr double MAGIC = 6755399441055744.0;  // 1.5 * 2^52: MAGIC + q lands on an integer grid
-  if (E > -900) {
-    // q = t * 2^(52-E) is exact (a power-of-two scale that neither overflows
-    // nor loses bits, except for q far below 1/2 where only r = 0 matters)
-    const double q = __dmul_rn(t, __longlong_as_double((long long)(1075 - E) << 52));
-    if (q < 2251799813685248.0) {  // q < 2^51: RN-even(q) from the grid, d = q - RN-even(q)
-      const double y = __dadd_rn(q, MAGIC);
-      const double d = __dsub_rn(q, __dsub_rn(y, MAGIC));
-      const unsigned long long rne = ((unsigned long long)__double_as_longlong(y) & 0xFFFFFFFFFFFFFull) - (1ull << 51);
-      tie = d == 0.5 || d == -0.5;
-      r = rne - (d < 0.0 && tie ? 1ull : 0ull);  // a tie keeps its floor
-      return;
-    }
-    const double fl = floor(q);
-    const double fr = __dsub_rn(q, fl);
-    tie = fr == 0.5;
-    r = fl < 18014398509481984.0 ? (unsigned long long)fl + (fr > 0.5 ? 1ull : 0ull) : CAP;
-    return;
-  }
+// The general case of units(): integer arithmetic on the term's bits.
+__device__ __noinline__ unsigned long long units_bits(double t, int E, bool* tie) {
   const unsigned long long b = (unsigned long long)__double_as_longlong(t);
   const int f = (int)(b >> 52) & 0x7ff;
   const unsigned long long M = (b & 0xFFFFFFFFFFFFFull) | (f ? (1ull << 52) : 0ull);
   const int et = (f ? f : 1) - 1075;  // t = M * 2^et
   const int d = (E - 52) - et;
-  tie = false;
-  if (d < 0) {
-    r = M ? CAP : 0ull;
-  } else if (d == 0) {
-    r = M;
-  } else if (d < 64) {
-    const unsigned long long rem = M & ((1ull << d) - 1), half = 1ull << (d - 1);
-    r = (M >> d) + (rem > half ? 1ull : 0ull);
-    tie = rem == half;
-  } else {
-    r = 0;
+  *tie = false;
+  if (d < 0) return M ? CAP : 0ull;
+  if (d == 0) return M;
+  if (d >= 64) return 0ull;
+  const unsigned long long rem = M & ((1ull << d) - 1), half = 1ull << (d - 1);
+  *tie = rem == half;
+  return (M >> d) + (rem > half ? 1ull : 0ull);
+}
+__device__ __forceinline__ void units(double t, int E, unsigned long long& r, bool& tie) {
+  constexpr double MAGIC = 6755399441055744.0;  // 1.5 * 2^52: MAGIC + q lands on an integer grid
+  // q = t * 2^(52-E) is exact (a power-of-two scale that neither overflows
+  // nor loses bits, except for q far below 1/2 where only r = 0 matters)
+  const double q = __dmul_rn(t, __longlong_as_double((long long)(1075 - max(E, -900)) << 52));
+  if (E > -900 && q < 2251799813685248.0) {  // q < 2^51: RN-even(q) from the grid
+    const double y = __dadd_rn(q, MAGIC);
+    const double d = __dsub_rn(q, __dsub_rn(y, MAGIC));
+    const unsigned long long rne = ((unsigned long long)__double_as_longlong(y) & 0xFFFFFFFFFFFFFull) - (1ull << 51);
+    tie = d == 0.5 || d == -0.5;
+    r = rne - (d < 0.0 && tie ? 1ull : 0ull);  // a tie keeps its floor
+    return;
   }
+  r = units_bits(t, E, &tie);
 }
 
 template <typename T>
@@ -145,16 +140,21 @@ __device__ __forceinline__ T warp_incl(T v, int lane) {
   return v;
 }
 
-// Segmented composition: (reset, f) then (reset', g) = reset' ? (1, g) : (reset, f then g).
+// A stretch map with the binades its terms were rounded in (empty: emin > emax)
+// and whether an explicit term precedes it inside the scanned range.
 struct SegFn {
   Fn f;
+  int emin, emax;
   int reset;
 };
-__device__ __forceinline__ SegFn seg_then(const SegFn& a, const SegFn& b) {
+__device__ __forceinline__ SegFn seg_empty() { return SegFn{Fn{0ull, 0ull, 0}, INT_MAX, INT_MIN, 0}; }
+__device__ __forceinline__ SegFn seg_cat(const SegFn& a, const SegFn& b) {  // a, then b
   if (b.reset) return b;
   SegFn c;
-  c.reset = a.reset;
   c.f = then(a.f, b.f);
+  c.emin = min(a.emin, b.emin);
+  c.emax = max(a.emax, b.emax);
+  c.reset = a.reset;
   return c;
 }
 __device__ __forceinline__ SegFn shfl_up_seg(const SegFn& v, int o) {
@@ -162,50 +162,71 @@ __device__ __forceinline__ SegFn shfl_up_seg(const SegFn& v, int o) {
   r.f.c1 = __shfl_up_sync(0xffffffffu, v.f.c1, o);
   r.f.c2 = __shfl_up_sync(0xffffffffu, v.f.c2, o);
   r.f.t = __shfl_up_sync(0xffffffffu, v.f.t, o);
+  r.emin = __shfl_up_sync(0xffffffffu, v.emin, o);
+  r.emax = __shfl_up_sync(0xffffffffu, v.emax, o);
   r.reset = __shfl_up_sync(0xffffffffu, v.reset, o);
   return r;
 }
+__device__ __forceinline__ void put(Entry& e, const SegFn& s) {
+  e.c1 = sat(s.f.c1);
+  e.c2 = sat(s.f.c2);
+  e.t = s.f.t;
+  e.emin = s.emin;
+  e.emax = s.emax;
+}
+__device__ __forceinline__ SegFn get(const Entry& e) { return SegFn{Fn{e.c1, e.c2, e.t}, e.emin, e.emax, 0}; }
 
 // The reference's loop, one thread: acc = 0; acc = acc + t[j] for j < n.
 __device__ __forceinline__ double serial(const double* t, int n) {
   double a = 0.0;
+#pragma unroll 1
   for (int j = 0; j < n; j++) a = __dadd_rn(a, t[j]);
   return a;
 }
 
-// Term j is explicit when it is term 0 of a chunk, when the approximate sums
-// before and after it lie in different binades, or when one of them lies
-// within 2^-36 of a binade edge (the approximation could be on the wrong side).
-__device__ __forceinline__ bool explicit_term(double before, double after, int j, int& Eb) {
-  constexpr unsigned long long MANT = 0xFFFFFFFFFFFFFull, EDGE = 1ull << 16;
-  const unsigned long long bb = (unsigned long long)__double_as_longlong(before);
-  const unsigned long long ba = (unsigned long long)__double_as_longlong(after);
-  const int fb = (int)(bb >> 52), fa = (int)(ba >> 52);
-  Eb = (fb ? fb : 1) - 1023;
-  const int Ea = (fa ? fa : 1) - 1023;
-  return j == 0 || Eb != Ea || (fb > 1 && (bb & MANT) < EDGE) || (ba & MANT) > MANT - EDGE;
-}
-__device__ __forceinline__ Fn term_map(double v, int E) {
-  unsigned long long r;
-  bool tie;
-  units(v, E, r, tie);
-  Fn fn;
-  fn.t = tie ? 1 : 0;
-  fn.c1 = tie ? r : 0ull;
-  fn.c2 = tie ? 0ull : r;
-  return fn;
+// Binade tracking along a lane's run of approximate sums.  A term is explicit
+// when it is term 0 of the chunk, when the piece it would join started within
+// the margin above its binade's lower edge, or when the approximate sum after
+// it reaches the margin below the binade's upper edge.
+struct Track {
+  int E;
+  double top;  // 2^(E+1) * (1 - 2^-36)
+  bool low;    // the piece starts within 2^-36 above 2^E
+  __device__ __forceinline__ void start(double x) {
+    E = binade(x);
+    top = __longlong_as_double((long long)(E + 1024) << 52) * (1.0 - DELTA);
+    const int f = (int)((unsigned long long)__double_as_longlong(x) >> 52);
+    low = f > 1 && x < __longlong_as_double((long long)(E + 1023) << 52) * (1.0 + DELTA);
+  }
+};
+
+// Finish a stretch on the serial chain: apply its map to the exact running sum
+// a (checked: every term rounded in a's binade, result below 2^53 units).
+__device__ __forceinline__ bool finish(double& a, const SegFn& st) {
+  if (st.emin > st.emax) return true;  // no term
+  const int E = st.emin;
+  const unsigned long long bits = (unsigned long long)__double_as_longlong(a);
+  const int f = (int)(bits >> 52);
+  if (st.emax != E || (f ? f : 1) - 1023 != E) return false;
+  const unsigned long long A = (bits & 0xFFFFFFFFFFFFFull) | (f ? (1ull << 52) : 0ull);
+  const unsigned long long A2 = apply(st.f.t, st.f.c1, st.f.c2, A);
+  if (A2 > (1ull << 53) - 1ull) return false;
+  a = __longlong_as_double((long long)(((unsigned long long)(E + 1022) << 52) + A2));
+  return true;
 }
 
-// One chunk of at most PER * blockDim.x terms, continuing the chain from
-// acc_in (the exact running sum before the chunk).  Thread i owns terms
-// [i*PER, i*PER + PER); PER is odd, so that consecutive lanes reading shared
-// memory 8*PER bytes apart hit distinct banks.  The per-term loops stay
-// rolled: the kernel's code then fits the instruction cache.
+// One chunk of at most PER * 256 terms (blockDim.x == 256), continuing the
+// chain from acc_in (the exact running sum before the chunk).  Lane l of warp
+// w owns terms [(32w + l) * PER, ... + PER); PER is odd, so that consecutive
+// lanes reading shared memory 8*PER bytes apart hit distinct banks.  Two block
+// barriers; the rest is warp-local.  The per-term loops stay rolled: this code
+// runs once per row on one SM, where instruction fetch, not arithmetic, sets
+// the pace of long straight-line code.
 template <int PER>
 __device__ __forceinline__ double osum_chunk(const double* t, int len, double acc_in, Smem& S) {
-  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, wid = tid >> 5, nw = nt >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int lo = min(len, tid * PER), hi = min(len, lo + PER);
-  // 1. approximate sums (only used to predict binades)
+  // 1. the run's approximate sum, warp prefix sums
   double loc = 0.0;
   bool bad = !(acc_in >= 0.0) || isinf(acc_in);
 #pragma unroll 1
@@ -215,202 +236,151 @@ __device__ __forceinline__ double osum_chunk(const double* t, int len, double ac
     loc += v;
   }
   const double inc = warp_incl(loc, lane);
-  if (lane == 31) S.wtot[wid] = inc;
-  for (int i = tid; i < MAXSEG; i += nt) {
-    S.emin[i] = INT_MAX;
-    S.emax[i] = INT_MIN;
-    S.ft[i] = 0;
-    S.c1[i] = 0ull;
-    S.c2[i] = 0ull;
-  }
-  // per-warp votes read back after a plain barrier (a block vote,
-  // __syncthreads_or, takes microseconds to deliver its result)
   const bool wbad = __any_sync(0xffffffffu, bad);
-  if (lane == 0) S.wbad[wid] = wbad ? 1 : 0;
+  if (lane == 31) {
+    S.wtot[wid] = inc;
+    S.wbad[wid] = wbad ? 1 : 0;
+  }
   __syncthreads();
-  bad = false;
-  for (int w = 0; w < nw; w++) bad |= S.wbad[w] != 0;
-  bool fits = false;
-  if (!bad) {
-    if (wid == 0) {
-      const double w = lane < nw ? S.wtot[lane] : 0.0;
-      const double wi = warp_incl(w, lane);
-      double ex = __shfl_up_sync(0xffffffffu, wi, 1);
-      if (lane == 0) ex = 0.0;
-      if (lane < nw) S.wtot[lane] = ex;
-    }
-    __syncthreads();
+  bool any_bad = false;
+  double P = acc_in;
+#pragma unroll 1
+  for (int w = 0; w < 8; w++) {
+    any_bad |= S.wbad[w] != 0;
+    if (w < wid) P += S.wtot[w];
+  }
+  if (!any_bad) {
     double exl = __shfl_up_sync(0xffffffffu, inc, 1);
     if (lane == 0) exl = 0.0;
-    const double P = acc_in + (S.wtot[wid] + exl);  // ~ the sum before this run
-    // 2. explicit terms of the run (bit k of exmask: term lo + k), and their ordinals
+    P += exl;  // ~ the exact sum before this run
+    // 2a. explicit terms of the run (bit k: term lo + k)
     unsigned exmask = 0u;
     {
+      Track tr;
+      tr.start(P);
       double before = P;
 #pragma unroll 1
       for (int j = lo; j < hi; j++) {
         const double after = before + t[j];
-        int Eb;
-        if (explicit_term(before, after, j, Eb)) exmask |= 1u << (j - lo);
+        if (j == 0 || tr.low || after >= tr.top) {
+          exmask |= 1u << (j - lo);
+          tr.start(after);
+        }
         before = after;
       }
     }
     const int cnt = __popc(exmask);
     const int cinc = warp_incl(cnt, lane);
-    if (lane == 31) S.wcnt[wid] = cinc;
-    __syncthreads();
-    if (wid == 0) {
-      const int w = lane < nw ? S.wcnt[lane] : 0;
-      const int wi = warp_incl(w, lane);
-      int ex = __shfl_up_sync(0xffffffffu, wi, 1);
-      if (lane == 0) ex = 0;
-      if (lane < nw) S.wcnt[lane] = ex;
-      if (lane == 31) S.nseg = wi;  // total explicit terms
-    }
-    __syncthreads();
-    const int nseg = S.nseg;
-    const int base = S.wcnt[wid] + cinc - cnt;  // explicit terms before this run
-    fits = nseg <= MAXSEG;
-    // 3. compose the run's terms: the head piece (up to its first explicit
-    //    term), inner pieces (stored at once) and the tail piece.  Between
-    //    explicit terms the predicted binade cannot change, so a piece's
-    //    binade is read once, at its start, and recorded for the check.
-    Fn head = {0ull, 0ull, 0}, cur = {0ull, 0ull, 0};
-    if (fits && hi > lo) {
+    const int wn = __shfl_sync(0xffffffffu, cinc, 31);
+    const bool fits = wn <= MAXW;
+    // 2b. compose: head piece (before the first explicit term), inner pieces
+    //     (stored at once) and the tail piece, each with its binade
+    SegFn head = seg_empty(), cur = seg_empty();
+    if (fits) {
+      const int base = cinc - cnt;  // explicit terms of this warp before this run
       int ord = base - 1;
+      Track tr;
+      tr.start(P);
       double before = P;
-      int E = binade(P);
-      bool open = false;  // the current piece holds a term
 #pragma unroll 1
       for (int j = lo; j < hi; j++) {
-        const double v = t[j];
+        const double v = t[j], after = before + v;
         if ((exmask >> (j - lo)) & 1u) {
-          if (ord >= 0 && open) {
-            atomicMin(&S.emin[ord], E);
-            atomicMax(&S.emax[ord], E);
-          }
-          if (ord >= base) {  // an inner piece: both ends in this run
-            S.c1[ord] = cur.c1;
-            S.c2[ord] = cur.c2;
-            S.ft[ord] = cur.t;
-          } else {
-            head = cur;
-          }
+          if (ord >= base) put(S.ent[wid][ord], cur);
+          else head = cur;
           ord++;
-          S.expl[ord] = j;
-          S.tv[ord] = v;
-          cur = Fn{0ull, 0ull, 0};
-          open = false;
-          before = before + v;
-          E = binade(before);
+          S.ent[wid][ord].v = v;
+          cur = seg_empty();
+          tr.start(after);
         } else {
-          // A -> A + r, or for a tie A -> roundup_even(A + r); pieces stay
-          // below 2^59 inside a run, so no saturation is needed here
           unsigned long long r;
           bool tie;
-          units(v, E, r, tie);
+          units(v, tr.E, r, tie);
           if (!tie) {
-            cur.c2 += r;
-          } else if (!cur.t) {
-            cur.t = 1;
-            cur.c1 = cur.c2 + r;
-            cur.c2 = 0ull;
+            cur.f.c2 += r;
+          } else if (!cur.f.t) {
+            cur.f.t = 1;
+            cur.f.c1 = cur.f.c2 + r;
+            cur.f.c2 = 0ull;
           } else {
-            cur.c2 = (cur.c2 + r + 1ull) & ~1ull;
+            cur.f.c2 = (cur.f.c2 + r + 1ull) & ~1ull;
           }
-          open = true;
-          before = before + v;
+          cur.emin = min(cur.emin, tr.E);
+          cur.emax = max(cur.emax, tr.E);
         }
+        before = after;
       }
-      if (ord >= 0 && open) {
-        atomicMin(&S.emin[ord], E);
-        atomicMax(&S.emax[ord], E);
-      }
-      cur.c1 = sat(cur.c1);
-      cur.c2 = sat(cur.c2);
-      head.c1 = sat(head.c1);
-      head.c2 = sat(head.c2);
+      // a run's constants stay below 2^59 (17 terms of < 2^55): saturate once
+      cur.f.c1 = sat(cur.f.c1);
+      cur.f.c2 = sat(cur.f.c2);
+      head.f.c1 = sat(head.f.c1);
+      head.f.c2 = sat(head.f.c2);
     }
-    // 4. chain the pieces across runs: segmented scan of (has explicit, tail
-    //    or whole-run map) over the threads in order
-    const bool seen = exmask != 0u;
-    SegFn mine;
-    mine.reset = seen ? 1 : 0;
-    mine.f = cur;  // seen: the tail piece; else the whole run
-    SegFn incl = mine;
-#pragma unroll
+    // 2c. chain the runs of the warp: segmented scan of (has explicit,
+    //     tail or whole-run map)
+    SegFn incl = cur;
+    incl.reset = exmask ? 1 : 0;
+#pragma unroll 1
     for (int o = 1; o < 32; o <<= 1) {
       const SegFn y = shfl_up_seg(incl, o);
-      if (lane >= o) incl = seg_then(y, incl);
+      if (lane >= o) incl = seg_cat(y, incl);
     }
     SegFn lexc = shfl_up_seg(incl, 1);
-    if (lane == 0) lexc = SegFn{Fn{0ull, 0ull, 0}, 0};
-    if (lane == 31) {
-      S.wc1[wid] = incl.f.c1;
-      S.wc2[wid] = incl.f.c2;
-      S.wt[wid] = incl.f.t;
-      S.wr[wid] = incl.reset;
-    }
-    __syncthreads();
-    if (wid == 0) {
-      SegFn w = {Fn{0ull, 0ull, 0}, 0};
-      if (lane < nw) w = SegFn{Fn{S.wc1[lane], S.wc2[lane], S.wt[lane]}, S.wr[lane]};
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const SegFn y = shfl_up_seg(w, o);
-        if (lane >= o) w = seg_then(y, w);
-      }
-      SegFn ex = shfl_up_seg(w, 1);
-      if (lane == 0) ex = SegFn{Fn{0ull, 0ull, 0}, 0};
-      if (lane < nw) {
-        S.wc1[lane] = ex.f.c1;
-        S.wc2[lane] = ex.f.c2;
-        S.wt[lane] = ex.f.t;
-        S.wr[lane] = ex.reset;
-      }
-    }
-    __syncthreads();
+    if (lane == 0) lexc = seg_empty();
     if (fits) {
-      const SegFn wex = {Fn{S.wc1[wid], S.wc2[wid], S.wt[wid]}, S.wr[wid]};
-      const SegFn exc = seg_then(wex, lexc);  // everything before this run
-      if (seen && base >= 1) {                // the stretch ending at this run's first explicit term
-        const Fn f = then(exc.f, head);
-        S.c1[base - 1] = f.c1;
-        S.c2[base - 1] = f.c2;
-        S.ft[base - 1] = f.t;
+      if (exmask) {  // the stretch ending at this run's first explicit term
+        const SegFn h = seg_cat(lexc, head);
+        if (lexc.reset) put(S.ent[wid][cinc - cnt - 1], h);
+        else put(S.whead[wid], h);
       }
-      if (tid == nt - 1 && nseg >= 1) {  // the last stretch runs to the end
-        const SegFn all = seg_then(exc, mine);
-        S.c1[nseg - 1] = all.f.c1;
-        S.c2[nseg - 1] = all.f.c2;
-        S.ft[nseg - 1] = all.f.t;
-      }
+      if (lane == 31) put(S.wtail[wid], incl);
     }
-    __syncthreads();
+    if (lane == 31) S.wn[wid] = wn;
   }
-  // 5. the chain itself (one thread): explicit terms by __dadd_rn, stretches
-  //    by their composed maps, each checked
+  __syncthreads();
+  // 3a. the map after each warp's last explicit term runs through the
+  //     following warps up to the next explicit term (or the chunk's end):
+  //     composed by one lane per warp, in parallel
+  if (wid == 0 && !any_bad && lane < 8) {
+    const int n = S.wn[lane];
+    if (n > 0 && n <= MAXW) {
+      SegFn m = get(S.wtail[lane]);
+#pragma unroll 1
+      for (int x = lane + 1; x < 8; x++) {
+        if (S.wn[x] > 0) {
+          m = seg_cat(m, get(S.whead[x]));
+          break;
+        }
+        m = seg_cat(m, get(S.wtail[x]));
+      }
+      put(S.ent[lane][n - 1], m);
+    }
+  }
+  __syncwarp();
+  // 3b. the chain itself (one thread): explicit terms by __dadd_rn, the
+  //     stretch after each by its composed map, each checked
   if (tid == 0) {
     double a = acc_in;
-    bool ok = fits;
+    bool ok = !any_bad && (len == 0 || S.wn[0] > 0);  // term 0 is explicit
     if (ok) {
-      const int nseg = S.nseg;
 #pragma unroll 1
-      for (int s = 0; s < nseg; s++) {
-        a = __dadd_rn(a, S.tv[s]);
-        const int E = S.emin[s], E2 = S.emax[s];
-        if (E > E2) continue;  // no term between this explicit one and the next
-        const unsigned long long bits = (unsigned long long)__double_as_longlong(a);
-        const int f = (int)(bits >> 52);
-        if (E2 != E || (f ? f : 1) - 1023 != E) { ok = false; break; }
-        const unsigned long long A = (bits & 0xFFFFFFFFFFFFFull) | (f ? (1ull << 52) : 0ull);
-        const unsigned long long A2 = apply(S.ft[s], S.c1[s], S.c2[s], A);
-        if (A2 > (1ull << 53) - 1ull) { ok = false; break; }
-        a = __longlong_as_double((long long)(((unsigned long long)(E + 1022) << 52) + A2));
+      for (int w = 0; w < 8; w++) ok &= S.wn[w] <= MAXW;
+    }
+    if (ok) {
+#pragma unroll 1
+      for (int w = 0; w < 8; w++) {
+        const int n = S.wn[w];
+#pragma unroll 1
+        for (int i = 0; i < n; i++) {
+          const Entry& e = S.ent[w][i];
+          a = __dadd_rn(a, e.v);
+          ok &= finish(a, get(e));
+        }
       }
     }
     if (!ok) {
       a = acc_in;
+#pragma unroll 1
       for (int j = 0; j < len; j++) a = __dadd_rn(a, t[j]);
     }
     S.result = a;
@@ -419,15 +389,22 @@ __device__ __forceinline__ double osum_chunk(const double* t, int len, double ac
   return S.result;
 }
 
-// Same value as serial(t, n), computed by the whole block (blockDim.x a
-// multiple of 32, at most 1024) in chunks of 17 * blockDim.x terms.  Every
-// thread must call it; every thread gets the sum.  `t` may be in shared or
-// global memory.
+// Same value as serial(t, n), computed by the whole block in chunks of
+// 17 * 256 terms.  Every thread must call it; every thread gets the sum.  `t`
+// may be in shared or global memory.  Written for 256-thread blocks; any
+// other block size takes the serial loop.
 __device__ __forceinline__ double ordered_sum(const double* t, int n, Smem& S) {
   constexpr int PER = 17;
-  const int chunk = PER * (int)blockDim.x;
+  if (blockDim.x != 256) {
+    if (threadIdx.x == 0) S.result = serial(t, n);
+    __syncthreads();
+    const double r = S.result;
+    __syncthreads();
+    return r;
+  }
   double acc = 0.0;
-  for (int c0 = 0; c0 < n; c0 += chunk) acc = osum_chunk<PER>(t + c0, min(chunk, n - c0), acc, S);
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += PER * 256) acc = osum_chunk<PER>(t + c0, min(PER * 256, n - c0), acc, S);
   return acc;
 }
 

@@ -38,6 +38,7 @@
 #include "dc_internal.cuh"
 #include "dc_math.cuh"
 #include "dc_osum.cuh"
+#include "dc_ptx.cuh"
 
 struct dc_mat {
   int k = 0, n = 0, ldk = 0;
@@ -90,6 +91,7 @@ struct dc_stage {
   float* logits1 = nullptr; // head: logits of the lap's row
   unsigned long long* amax_keys = nullptr;  // head: greedy-pick keys (8 rows), kept at zero between uses
   cudaGraphExec_t lap_exec = nullptr;
+  unsigned long long lap_nk = 0;  // kernels in one replay of lap_exec
   std::vector<dc_stage*> lap_key;
   int32_t* lap_picks = nullptr;
   std::vector<void*> allocs;
@@ -134,7 +136,7 @@ __device__ __forceinline__ double block_max_d(double v, double* red) {
 
 // max(mx/127, 1e-8) in double (verified_core.js:114, :128).
 __device__ __forceinline__ double quant_scale(float mx) {
-  double sc = __ddiv_rn((double)mx, 127.0);
+  double sc = dc_ddiv_slow((double)mx, 127.0);  // out of line: once per row
   return sc > 1e-8 ? sc : 1e-8;
 }
 
@@ -151,12 +153,27 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   __shared__ dco::Smem osm;
   const int row = blockIdx.x;
   const float* xr = x + (int64_t)row * C;
+  // float4 access when the row allows it (all loads of a thread in flight at once)
+  const bool vec = (C & 3) == 0 && ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
   bool bad = false;
-  for (int j = threadIdx.x; j < C; j += blockDim.x) {
-    const float v = xr[j];
-    bad |= !isfinite(v);
-    ys[j] = v;
-    sq[j] = __dmul_rn((double)v, (double)v);  // exact: a float square fits in a double
+  if (vec) {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(xr)[i];
+      bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
+      reinterpret_cast<float4*>(ys)[i] = v;
+      sq[4 * i + 0] = __dmul_rn((double)v.x, (double)v.x);  // exact: a float square fits in a double
+      sq[4 * i + 1] = __dmul_rn((double)v.y, (double)v.y);
+      sq[4 * i + 2] = __dmul_rn((double)v.z, (double)v.z);
+      sq[4 * i + 3] = __dmul_rn((double)v.w, (double)v.w);
+    }
+  } else {
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+      const float v = xr[j];
+      bad |= !isfinite(v);
+      ys[j] = v;
+      sq[j] = __dmul_rn((double)v, (double)v);
+    }
   }
   // warp votes and a plain barrier: a block vote (__syncthreads_or) costs microseconds here
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(status, DC_ST_NONFINITE);
@@ -165,21 +182,52 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   const double acc = dco::ordered_sum(sq, C, osm);
   const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(acc, (double)C), eps)));
   float mx = 0.0f;
-  for (int j = threadIdx.x; j < C; j += blockDim.x) {
-    float y = __double2float_rn(__dmul_rn(__dmul_rn((double)ys[j], inv), (double)w[j]));
-    ys[j] = y;
-    mx = fmaxf(mx, fabsf(y));
+  if (vec) {
+#pragma unroll 2
+    for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
+      const float4 wv = reinterpret_cast<const float4*>(w)[i];
+      float4 y = reinterpret_cast<const float4*>(ys)[i];
+      y.x = __double2float_rn(__dmul_rn(__dmul_rn((double)y.x, inv), (double)wv.x));
+      y.y = __double2float_rn(__dmul_rn(__dmul_rn((double)y.y, inv), (double)wv.y));
+      y.z = __double2float_rn(__dmul_rn(__dmul_rn((double)y.z, inv), (double)wv.z));
+      y.w = __double2float_rn(__dmul_rn(__dmul_rn((double)y.w, inv), (double)wv.w));
+      reinterpret_cast<float4*>(ys)[i] = y;
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+    }
+  } else {
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+      float y = __double2float_rn(__dmul_rn(__dmul_rn((double)ys[j], inv), (double)w[j]));
+      ys[j] = y;
+      mx = fmaxf(mx, fabsf(y));
+    }
   }
   if (yo) {  // the normalised row itself (infer.js rmsnorm), no quantisation
+    __syncthreads();
     for (int j = threadIdx.x; j < C; j += blockDim.x) yo[(int64_t)row * C + j] = ys[j];
     return;
   }
   mx = block_max_f(mx, red);
-  const double sc = quant_scale(mx);
+  const double sc = quant_scale(mx), rsc = __drcp_rn(sc);
   if (threadIdx.x == 0) s[row] = __double2float_rn(sc);
   int8_t* qr = q + (int64_t)row * ldq;
-  for (int j = threadIdx.x; j < ldq; j += blockDim.x)
-    qr[j] = j < C ? dc_clamp8(dc_js_round(__ddiv_rn((double)ys[j], sc))) : (int8_t)0;
+  if (vec && (ldq & 3) == 0 && (reinterpret_cast<uintptr_t>(qr) & 3) == 0) {
+#pragma unroll 1
+    for (int i = threadIdx.x; i < (ldq >> 2); i += blockDim.x) {
+      char4 o = make_char4(0, 0, 0, 0);
+      if (4 * i < C) {
+        const float4 y = reinterpret_cast<const float4*>(ys)[i];
+        o.x = dc_quant_div((double)y.x, sc, rsc);
+        o.y = dc_quant_div((double)y.y, sc, rsc);
+        o.z = dc_quant_div((double)y.z, sc, rsc);
+        o.w = dc_quant_div((double)y.w, sc, rsc);
+      }
+      reinterpret_cast<char4*>(qr)[i] = o;
+    }
+  } else {
+#pragma unroll 1
+    for (int j = threadIdx.x; j < ldq; j += blockDim.x)
+      qr[j] = j < C ? dc_quant_div((double)ys[j], sc, rsc) : (int8_t)0;
+  }
 }
 
 // RoPE on the q and k parts of the fused QKV output row, quantisation of each
@@ -469,6 +517,174 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
       bad |= !isfinite(o);
       atomicMax(rowmax + i, __float_as_uint(fabsf(o)));  // for the next GEMM's row quantisation
     }
+  }
+  if (bad) atomicOr(status, DC_ST_NONFINITE);
+}
+
+// Attention of one decode row (T = 1) against the whole cache, split over
+// channel groups: grid (nH, hd / CH), 256 threads.  Every CTA of a head
+// computes the head's scores and probabilities (the same numbers as
+// k_attention: scores, exact max, fdlibm exp, the serial softmax sum,
+// quantizeRows of the probabilities) and then CH channels of the context.
+// The keys stream through a two-slot shared-memory ring of 256-key blocks,
+// and the CTA's CH value rows (channel-major) land in shared memory once, all
+// by 1-D bulk async copies, so the loads are in flight while the softmax runs.
+// Dynamic shared memory: 2 * 256 * hd (keys) + CH * ldp (values) + 13 * ldp.
+// hd is 32, 64, 128 or 256; CH divides hd.
+constexpr int ATTD_KB = 256;  // keys per ring slot
+__global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
+                                                       const int8_t* __restrict__ k8, const float* __restrict__ ks,
+                                                       const int8_t* __restrict__ v8t, const float* __restrict__ vs,
+                                                       const int* __restrict__ n0p, int max_pos, int ldp, int CH,
+                                                       double scale, float* __restrict__ out,
+                                                       uint32_t* __restrict__ rowmax, int* status) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int ldpv = ldp;                                        // bytes per value row in shared memory
+  int8_t* sK = (int8_t*)sm;                                    // 2 slots x ATTD_KB x hd
+  int8_t* sV = sK + 2 * ATTD_KB * hd;                          // CH x ldpv
+  double* xs = (double*)(sV + (size_t)CH * ldpv);              // ldp doubles: s*scale, then e
+  float* af = (float*)(xs + ldp);                              // ldp floats: key scales, then f32(e), then a
+  int8_t* a8 = (int8_t*)(af + ldp);                            // ldp bytes
+  __shared__ __align__(8) uint64_t full[2], vbar;
+  __shared__ __align__(16) int8_t q8[256];
+  __shared__ float red[32];
+  __shared__ double redd[32];
+  __shared__ int abort_flag;
+  __shared__ dco::Smem osm;
+  const int hq = blockIdx.x, c0 = blockIdx.y * CH;
+  const int g = hq / (nH / nKV);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = *n0p, N = n0 + 1;            // keys 0..n0 are visible
+  const int ldpN = (N + 15) & ~15;            // 16-byte chunks covering the keys
+  const int nb = (N + ATTD_KB - 1) / ATTD_KB;  // key blocks
+  const int8_t* kg = k8 + (int64_t)g * max_pos * hd;
+  if (tid == 0) {
+    dcp::mbar_init(&full[0], 1);
+    dcp::mbar_init(&full[1], 1);
+    dcp::mbar_init(&vbar, 1);
+    abort_flag = 0;
+    dcp::mbar_fence_init();
+  }
+  __syncthreads();
+  int issued[2] = {-1, -1};  // thread 0: last key block issued into each slot
+  if (warp == 0) {  // issue: the CH value rows, then the first two key blocks
+    if (lane == 0) dcp::mbar_expect_tx(&vbar, (uint32_t)(CH * ldpN));
+    __syncwarp();
+    for (int c = lane; c < CH; c += 32)
+      dcp::bulk_load(sV + (size_t)c * ldpv, v8t + ((int64_t)g * hd + c0 + c) * ldp, (uint32_t)ldpN, &vbar);
+    if (lane == 0)
+      for (int b = 0; b < 2 && b < nb; b++) {
+        issued[b] = b;
+        const int kn = min(ATTD_KB, N - b * ATTD_KB);
+        const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
+        dcp::mbar_expect_tx(&full[b], bytes);
+        dcp::bulk_load(sK + (size_t)b * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[b]);
+      }
+  }
+  // 1. the query row of this head, quantised (row scale per (token, head), double)
+  const float* qrow = h + hq * hd;
+  float mx = 0.0f;
+  bool bad = false;
+  for (int c = tid; c < hd; c += 256) {
+    const float v = qrow[c];
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+  }
+  const float* ksg = ks + (int64_t)g * max_pos;
+  for (int j = tid; j < N; j += 256) af[j] = ksg[j];  // key scales
+  mx = block_max_f(mx, red);
+  const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
+  const float qs = __double2float_rn(qsc);
+  for (int c = tid; c < hd; c += 256) q8[c] = dc_quant_div((double)qrow[c], qsc, rqsc);
+  __syncthreads();
+  // 2. scores block by block from the ring: int32 dot over hd, verified epilogue
+  const int lpk = hd >> 4, kpw = 32 / lpk;  // lanes per key, keys per warp step
+  const int sub = lane / lpk, part = lane - sub * lpk;
+  const int4 qv = ((const int4*)q8)[part];
+  double m = -INFINITY;
+  for (int b = 0; b < nb; b++) {
+    const int slot = b & 1;
+    if (!dcp::mbar_wait(&full[slot], (uint32_t)(b >> 1) & 1u, status)) abort_flag = 1;
+    __syncthreads();
+    if (abort_flag) break;
+    const int kb = b * ATTD_KB, kn = min(ATTD_KB, N - kb);
+    const int8_t* sk = sK + (size_t)slot * ATTD_KB * hd;
+    for (int k = warp * kpw + sub; k - sub < kn; k += 8 * kpw) {
+      int acc = 0;
+      if (k < kn) acc = dp4a16(*(const int4*)(sk + (size_t)k * hd + part * 16), qv, 0);
+      for (int o = lpk >> 1; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (part == 0 && k < kn) {
+        const double x = __dmul_rn((double)dc_epi(acc, qs, af[kb + k]), scale);
+        xs[kb + k] = x;
+        m = fmax(m, x);
+      }
+    }
+    __syncthreads();  // slot consumed
+    if (tid == 0 && b + 2 < nb) {
+      issued[slot] = b + 2;
+      const int kn2 = min(ATTD_KB, N - (b + 2) * ATTD_KB);
+      const uint32_t bytes = (uint32_t)(((kn2 * hd) + 15) & ~15);
+      dcp::mbar_expect_tx(&full[slot], bytes);
+      dcp::bulk_load(sK + (size_t)slot * ATTD_KB * hd, kg + (int64_t)(b + 2) * ATTD_KB * hd, bytes, &full[slot]);
+    }
+  }
+  const bool aborted = abort_flag != 0;
+  if (!aborted) {
+    // 3. row maximum (exact); 4. e_j and its f32 copy
+    m = block_max_d(m, redd);
+#pragma unroll 1
+    for (int j = tid; j < N; j += 256) {
+      const double e = dcm::fdlibm_exp(__dsub_rn(xs[j], m));
+      xs[j] = e;
+      af[j] = __double2float_rn(e);
+    }
+    __syncthreads();
+    // 5. z = sum of e_j in key order, with the reference's rounding sequence
+    const double z = dco::ordered_sum(xs, N, osm);
+    // 6. a_j = f32(f32(e_j) / z); 7. quantizeRows of the probability row
+    const double rz = __drcp_rn(z);
+    float amx = 0.0f;
+    for (int j = tid; j < N; j += 256) {
+      const float a = dc_div_to_f32((double)af[j], z, rz);
+      af[j] = a;
+      amx = fmaxf(amx, a);
+    }
+    amx = block_max_f(amx, red);
+    const double asc = quant_scale(amx), rasc = __drcp_rn(asc);
+    const float as = __double2float_rn(asc);
+    for (int j = tid; j < ldpN; j += 256) a8[j] = j < N ? dc_quant_div((double)af[j], asc, rasc) : (int8_t)0;
+    __syncthreads();
+    // 8. ctx[c] = sum_j a8[j] * v[c][j] for this CTA's CH channels
+    if (!dcp::mbar_wait(&vbar, 0, status)) abort_flag = 1;
+    __syncthreads();
+    if (!abort_flag) {
+      const int nch = ldpN >> 4;
+      const int4* a4 = (const int4*)a8;
+      for (int cl = warp * 4; cl < CH; cl += 32) {
+        int sacc[4] = {0, 0, 0, 0};
+        for (int q = lane; q < nch; q += 32) {
+          const int4 av = a4[q];
+#pragma unroll
+          for (int u = 0; u < 4; u++) sacc[u] = dp4a16(((const int4*)(sV + (size_t)(cl + u) * ldpv))[q], av, sacc[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+          for (int o = 16; o; o >>= 1) sacc[u] += __shfl_xor_sync(0xffffffffu, sacc[u], o);
+        if (lane < 4) {
+          const int c = c0 + cl + lane;
+          const int acc = lane == 0 ? sacc[0] : lane == 1 ? sacc[1] : lane == 2 ? sacc[2] : sacc[3];
+          const float o = dc_epi(acc, as, vs[g * hd + c]);
+          out[hq * hd + c] = o;
+          bad |= !isfinite(o);
+          atomicMax(rowmax, __float_as_uint(fabsf(o)));
+        }
+      }
+    }
+  }
+  if (abort_flag && tid == 0) {  // let copies still in flight land before the CTA goes away (bounded)
+    dcp::mbar_wait(&vbar, 0, status);
+    for (int sl = 0; sl < 2; sl++)
+      if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] >> 1) & 1u, status);
   }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
@@ -960,6 +1176,21 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   const double scale = 1.0 / sqrt((double)S->hd);
   const size_t att_smem = ((12 * (size_t)S->max_pos + 15) & ~(size_t)15) + (size_t)S->ldp + 16;
   if (int rc0 = dc_set_smem(ctx, (const void*)k_attention, (int)att_smem)) return rc0;
+  // the decode attention (one row): the widest channel group whose buffers fit on chip
+  int dec_ch = 0;
+  size_t dec_smem = 0;
+  if (S->hd == 32 || S->hd == 64 || S->hd == 128 || S->hd == 256) {
+    for (int ch = 32; ch >= 8 && !dec_ch; ch >>= 1) {
+      if (S->hd % ch) continue;
+      const size_t need = 2 * (size_t)ATTD_KB * S->hd + (size_t)(ch + 13) * S->ldp;
+      if (need + 12 * 1024 <= 232448) {
+        dec_ch = ch;
+        dec_smem = need;
+      }
+    }
+    if (dec_ch)
+      if (int rc0 = dc_set_smem(ctx, (const void*)k_attention_dec, (int)dec_smem)) return rc0;
+  }
   const size_t nrm_smem = 12 * (size_t)S->C;  // squares (double) + the row (float)
   // always raised: the kernel's static shared memory counts against the 48 KB default too
   if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
@@ -988,9 +1219,15 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     dc_count_launch();
     DC_CUDA(ctx, cudaMemsetAsync(S->rowmax, 0, 4 * (size_t)T, st));
-    k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
-                                                              kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
-                                                              S->ctxo, S->rowmax, S->qDim, ctx->d_status);
+    if (T == 1 && use_kv && dec_ch) {
+      k_attention_dec<<<dim3(S->nH, S->hd / dec_ch), 256, dec_smem, st>>>(
+          S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale,
+          S->ctxo, S->rowmax, ctx->d_status);
+    } else {
+      k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
+                                                                kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
+                                                                S->ctxo, S->rowmax, S->qDim, ctx->d_status);
+    }
     dc_count_launch();
     k_rowquant<<<dim3((S->ldQ + 255) / 256, T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
                                                               S->rs);
@@ -1131,9 +1368,12 @@ extern "C" int dc_decode_run(dc_stage** stages, int ns, const float* x_last, int
         const bool timing = ctx->timing;
         ctx->timing = false;  // no per-GEMM timing events inside the captured lap
         cudaGraph_t g = nullptr;
+        const unsigned long long nk0 = dc_launch_count();
         DC_CUDA(ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
         rc = decode_lap(stages, ns, picks);
         cudaError_t e = cudaStreamEndCapture(s, &g);
+        H->lap_nk = dc_launch_count() - nk0;
+        dc_count_launches(-(long long)H->lap_nk);  // captured, not launched
         ctx->timing = timing;
         if (rc) {
           if (g) cudaGraphDestroy(g);
@@ -1146,7 +1386,10 @@ extern "C" int dc_decode_run(dc_stage** stages, int ns, const float* x_last, int
         H->lap_key = key;
         H->lap_picks = picks;
       }
-      for (int n = 1; n < n_new; n++) DC_CUDA(ctx, cudaGraphLaunch(H->lap_exec, s));
+      for (int n = 1; n < n_new; n++) {
+        DC_CUDA(ctx, cudaGraphLaunch(H->lap_exec, s));
+        dc_count_launches(H->lap_nk);
+      }
     } else {
       for (int n = 1; n < n_new; n++)
         if ((rc = decode_lap(stages, ns, picks))) return rc;
