@@ -324,7 +324,7 @@ def bench_model(args, rank, world, peaks):
         ach = by / (ms / 1e3) / 1e9
         roof = dict(bound="hbm", achieved=ach, peak=peaks["hbm_gbs"], unit="GB/s", frac=ach / peaks["hbm_gbs"],
                     traffic=traffic_for("gemv_decode" if dom == 1 else "tc_prefill"),
-                    kernel=("k_gemv_bulk (decode GEMV, M<=8)" if dom == 1 else "k_gemm_tc (tcgen05, M>8)"),
+                    kernel=("k_gemv_row (decode GEMV, M=1)" if dom == 1 else "k_gemm_tc (tcgen05, M>8)"),
                     launches=n, avg_launch_us=per_launch_ms * 1e3, share_of_step=ms / (ms_step * args.steps),
                     algorithmic_bytes_per_launch=by / max(n, 1), ops_per_launch=op / max(n, 1),
                     method=(gemv_method if dom == 1 else "CUDA events around every tcgen05 GEMM launch in the "

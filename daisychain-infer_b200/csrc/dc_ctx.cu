@@ -237,7 +237,12 @@ int dc_set_smem(dc_ctx* ctx, const void* func, int bytes) {
   static std::mutex lock;
   static std::map<std::pair<const void*, int>, int> done;
   std::lock_guard<std::mutex> guard(lock);
-  int& have = done[{func, ctx->device}];
+  const auto key = std::make_pair(func, ctx->device);
+  const bool first = done.find(key) == done.end();
+  int& have = done[key];
+  if (first)  // one shared-memory carve-out for every kernel: no reconfiguration between launches
+    DC_CUDA(ctx, cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      (int)cudaSharedmemCarveoutMaxShared));
   if (bytes <= have) return DC_OK;
   DC_CUDA(ctx, cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   have = bytes;

@@ -132,6 +132,83 @@ __global__ void __launch_bounds__(256, 3) k_gemv(const int8_t* __restrict__ X, i
   }
 }
 
+// ---- L2 prefetch -------------------------------------------------------------
+// Bulk prefetches (cp.async.bulk.prefetch.L2) of [p, p + bytes) in 64 KB
+// pieces, spread over the grid: the copy engine pulls the bytes into L2 while
+// the issuing threads move on.  p and bytes are 16-byte multiples.
+__global__ void k_l2_prefetch(const int8_t* __restrict__ p, size_t bytes) {
+  constexpr size_t PIECE = 65536;
+  const size_t npiece = (bytes + PIECE - 1) / PIECE;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < npiece; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t off = i * PIECE;
+    const uint32_t len = (uint32_t)((bytes - off) < PIECE ? (bytes - off) : PIECE);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(len) : "memory");
+  }
+}
+
+// ---- one-row GEMV (M = 1), the decode path ---------------------------------
+// Each warp takes two weight rows (output columns) at a time and walks K in
+// segments of 8 x 32 16-byte chunks: the 16 streaming weight loads of a
+// segment (L1 no-allocate) and its 8 activation loads (L1-resident: every warp
+// reads the same row) are issued back to back, then consumed by dp4a.  No
+// shared memory, no prologue: a CTA starts pulling weights at its first
+// instruction, and 4-warp CTAs at 4 per SM keep ~128 KB of loads in flight on
+// each SM.  Grid-stride over row pairs; the epilogue is dc_store_out.
+constexpr int GV_SEG = 8;
+__global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* __restrict__ X, const int8_t* __restrict__ Wt,
+                                                     int ldw, const float* __restrict__ rs,
+                                                     const float* __restrict__ cs, int k, int n, unsigned flags,
+                                                     const int8_t* __restrict__ requant,
+                                                     const int8_t* __restrict__ relu, void* out) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * 4 + (threadIdx.x >> 5), nw = gridDim.x * 4;
+  const int nch = (k + 15) >> 4;
+  const int4* X4 = (const int4*)X;
+  bool waited = false;
+  for (int j0 = gw * 2; j0 < n; j0 += nw * 2) {
+    const int j1 = min(j0 + 1, n - 1);
+    const int4* w0 = (const int4*)(Wt + (int64_t)j0 * ldw);
+    const int4* w1 = (const int4*)(Wt + (int64_t)j1 * ldw);
+    const float csv = cs[lane == 1 ? j1 : j0];  // the epilogue's column scale, loaded with the weights
+    int a0 = 0, a1 = 0;
+#pragma unroll 1
+    for (int c0 = 0; c0 < nch; c0 += 32 * GV_SEG) {
+      int4 wa[GV_SEG], wb[GV_SEG], xv[GV_SEG];
+#pragma unroll
+      for (int u = 0; u < GV_SEG; u++) {
+        const int c = c0 + u * 32 + lane;
+        wa[u] = c < nch ? ld_stream(w0 + c) : make_int4(0, 0, 0, 0);
+        wb[u] = c < nch ? ld_stream(w1 + c) : make_int4(0, 0, 0, 0);
+      }
+      if (!waited) {
+        // launched as a programmatic dependent: the weights (constant) are
+        // already in flight; the activation row is read only after the
+        // kernel that writes it has completed
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        waited = true;
+      }
+#pragma unroll
+      for (int u = 0; u < GV_SEG; u++) {
+        const int c = c0 + u * 32 + lane;
+        xv[u] = c < nch ? X4[c] : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < GV_SEG; u++) {
+        a0 = dp4a16g(wa[u], xv[u], a0);
+        a1 = dp4a16g(wb[u], xv[u], a1);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+    }
+    if (lane == 0) dc_store_out(out, j0, a0, rs[0], csv, flags, requant, relu);
+    if (lane == 1 && j0 + 1 < n) dc_store_out(out, j0 + 1, a1, rs[0], csv, flags, requant, relu);
+  }
+  if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- bulk-staged GEMV: M <= MR rows, the decode path -----------------------
 // One CTA per SM streams a contiguous range of weight rows (rows_per_cta rows
 // of Wᵀ, i.e. output columns) through a ring of `stages` shared-memory stages
@@ -386,6 +463,28 @@ int launch_gemv_bulk(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, i
 template <int MR>
 int launch_gemv(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
                 int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st) {
+  if (MR == 1 && m == 1 && batch == 1 && !(((uintptr_t)Wt | (uintptr_t)Xq) & 15) && !(ldw & 15)) {
+    if (int rc = dc_set_smem(ctx, (const void*)k_gemv_row, 0)) return rc;
+    const int pairs = (n + 1) / 2;
+    const int blocks = std::max(1, std::min((pairs + 3) / 4, ctx->sm_count * 4));
+    // programmatic dependent launch: the CTAs may start (and issue their
+    // weight loads) while the previous kernel on the stream finishes
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemv_row, Xq, Wt, ldw, rs, cs, k, n, flags, (const int8_t*)ctx->d_requant,
+                                    (const int8_t*)ctx->d_relu, out));
+    dc_count_launch();
+    DC_CUDA(ctx, cudaGetLastError());
+    return DC_OK;
+  }
   {
     const int rc = launch_gemv_bulk<MR>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
     if (rc != DC_E_INVAL) return rc;
@@ -698,4 +797,21 @@ extern "C" int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, 
   float* rs = (float*)((char*)base + bx);
   if ((rc = dc_launch_quant_rows(ctx, X, m, w->k, xq, w->ldw, rs, ctx->stream))) return rc;
   return dc_gemm_dispatch(ctx, xq, w->ldw, w->qt, w->ldw, rs, w->cs, m, w->k, w->n, 1, flags, out, ctx->stream, 0);
+}
+
+// Prefetch a device range into L2 on the context's stream (asynchronous).
+int dc_l2_prefetch_on(dc_ctx* ctx, const void* p, size_t bytes, cudaStream_t st) {
+  if (!p || !bytes) return DC_OK;
+  if (((uintptr_t)p & 15) || (bytes & 15)) return dc_fail(ctx, DC_E_INVAL, "l2_prefetch: range must be 16-byte aligned");
+  const size_t npiece = (bytes + 65535) / 65536;
+  const int blocks = (int)std::min<size_t>((npiece + 127) / 128, (size_t)ctx->sm_count);
+  k_l2_prefetch<<<blocks, 128, 0, st>>>((const int8_t*)p, bytes);
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+extern "C" int dc_l2_prefetch(dc_ctx* ctx, const void* p, size_t bytes) {
+  if (!ctx) return DC_E_INVAL;
+  return dc_l2_prefetch_on(ctx, p, bytes, ctx->stream);
 }

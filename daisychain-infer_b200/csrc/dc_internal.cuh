@@ -79,7 +79,10 @@ int dc_cuda_fail(dc_ctx* ctx, cudaError_t e, const char* what);
 int dc_scratch(dc_ctx* ctx, size_t bytes, void** p);
 
 // Allow `bytes` of dynamic shared memory for kernel `func` on ctx's device; the
-// attribute is set once per (kernel, device) and raised only when needed.
+// attribute is set once per (kernel, device) and raised only when needed.  The
+// first call for a kernel also sets the maximal shared-memory carve-out, the
+// same for every kernel of the library, so that consecutive kernels never
+// make the SM repartition its L1 / shared memory.
 int dc_set_smem(dc_ctx* ctx, const void* func, int bytes);
 
 // Kernels launched by this library in this process (reported by dc_launch_count).
@@ -98,6 +101,8 @@ int dc_launch_transpose_i8(dc_ctx* ctx, const int8_t* W, int k, int n, int8_t* W
 int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
                      const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
                      int kind);
+// L2 prefetch of a device range (dc_gemm.cu).
+int dc_l2_prefetch_on(dc_ctx* ctx, const void* p, size_t bytes, cudaStream_t st);
 int dc_gemm_lut(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs, const float* cs, int m, int k,
                 int n, int batch, unsigned flags, void* out, cudaStream_t st);
 // tcgen05 path (dc_gemm_tc.cu): returns DC_E_INVAL when the shape is not supported.

@@ -151,6 +151,8 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   float* ys = (float*)(sq + C);
   __shared__ float red[32];
   __shared__ dco::Smem osm;
+  // the GEMV that consumes q may launch now: it streams its weights meanwhile
+  asm volatile("griddepcontrol.launch_dependents;");
   const int row = blockIdx.x;
   const float* xr = x + (int64_t)row * C;
   // float4 access when the row allows it (all loads of a thread in flight at once)
@@ -719,6 +721,7 @@ __global__ void __launch_bounds__(256) k_swiglu(float* __restrict__ h, int I, ui
 __global__ void __launch_bounds__(256) k_rowquant(const float* __restrict__ x, int64_t ldx, int cols,
                                                  const uint32_t* __restrict__ rowmax, int8_t* __restrict__ q,
                                                  int ldq, float* __restrict__ s) {
+  asm volatile("griddepcontrol.launch_dependents;");  // the next GEMV may start streaming weights
   const int row = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   const double sc = quant_scale(__uint_as_float(rowmax[row]));
@@ -905,9 +908,21 @@ static int upload(dc_stage* S, const float* h, size_t n, float** d) {
   return DC_OK;
 }
 
+// The shared-memory carve-out of every kernel a layer launches (dc_set_smem).
+static int stage_kernel_attrs(dc_ctx* ctx) {
+  const void* fns[] = {(const void*)k_rope_append, (const void*)k_vscale,      (const void*)k_vquant,
+                       (const void*)k_vquant_dev,  (const void*)k_setpos,      (const void*)k_addpos,
+                       (const void*)k_swiglu,      (const void*)k_rowquant,    (const void*)k_embed,
+                       (const void*)k_embed_at,    (const void*)k_argmax_part, (const void*)k_argmax_fin};
+  for (const void* f : fns)
+    if (int rc = dc_set_smem(ctx, f, 0)) return rc;
+  return DC_OK;
+}
+
 extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi, int head, int max_rows,
                                int max_pos, dc_stage** out) {
   if (!ctx || !spec || !out) return DC_E_INVAL;
+  if (int rc = stage_kernel_attrs(ctx)) return rc;
   const dc_spec& s = *spec;
   if (s.hidden <= 0 || s.heads <= 0 || s.kv_heads <= 0 || s.heads % s.kv_heads || s.head_dim <= 0 ||
       (s.head_dim % 16) || s.head_dim > 128 || s.inter <= 0 || s.vocab <= 0 || lo < 0 || hi > s.layers || hi < lo ||

@@ -164,6 +164,11 @@ int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned fl
 int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double* out);
 int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y);
 
+/* Prefetch [p, p + bytes) of device memory into L2 (16-byte aligned range),
+ * asynchronously on the context's stream.  No counterpart in the reference:
+ * the stages use it to pull the next weights while latency-bound kernels run. */
+int dc_l2_prefetch(dc_ctx* ctx, const void* p, size_t bytes);
+
 /* ---- kernel probe (webgpu.js:998-1060) --------------------------------------
  * Runs the seeded probe GEMM (m=24 k=96 n=24 batch=2, acc) through the live
  * kernels; returns the FNV-1a of the int32 result (before the reference folds in
