@@ -90,6 +90,7 @@ struct dc_stage {
   float* xlap = nullptr;    // head: the one hidden row a decode lap carries
   float* logits1 = nullptr; // head: logits of the lap's row
   unsigned long long* amax_keys = nullptr;  // head: greedy-pick keys (8 rows), kept at zero between uses
+  int* att_done = nullptr;  // decode attention: CTAs finished (kept at zero between launches)
   cudaGraphExec_t lap_exec = nullptr;
   unsigned long long lap_nk = 0;  // kernels in one replay of lap_exec
   std::vector<dc_stage*> lap_key;
@@ -146,7 +147,8 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
                                                                const float* __restrict__ w, double eps,
                                                                int8_t* __restrict__ q, int ldq,
                                                                float* __restrict__ s, int* status,
-                                                               float* __restrict__ yo = nullptr) {
+                                                               float* __restrict__ yo = nullptr,
+                                                               uint32_t* __restrict__ zrow = nullptr) {
   extern __shared__ __align__(16) double sq[];  // C doubles (v*v), then C floats (x, then y)
   float* ys = (float*)(sq + C);
   __shared__ float red[32];
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   asm volatile("griddepcontrol.launch_dependents;");
   const int row = blockIdx.x;
   const float* xr = x + (int64_t)row * C;
+  if (zrow && threadIdx.x == 0) zrow[row] = 0;  // the row maximum the next row quantisation collects
   // float4 access when the row allows it (all loads of a thread in flight at once)
   const bool vec = (C & 3) == 0 && ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
   bool bad = false;
@@ -243,7 +246,7 @@ __global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int n
                                                     const int* __restrict__ n0p, int max_pos,
                                                     int8_t* __restrict__ k8, float* __restrict__ ks,
                                                     float* __restrict__ vcache, uint32_t* __restrict__ vmax,
-                                                    int* status) {
+                                                    float* __restrict__ vs, int* __restrict__ vchg, int* status) {
   __shared__ float kr[128];
   __shared__ float red[32];
   const int n0 = *n0p;  // cached tokens before this chunk = its first position
@@ -252,13 +255,24 @@ __global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int n
   const int half = hd >> 1, qDim = nH * hd, kvDim = nKV * hd;
   float* row = h + (int64_t)t * nqkv;
   bool bad = false;
-  if (hh == nH + nKV) {
-    // values: copy and fold into the running channel maximum
-    for (int c = threadIdx.x; c < kvDim; c += blockDim.x) {
+  if (hh >= nH + nKV) {
+    // values, 64 channels per block: copy and fold into the running channel
+    // maximum; with one row (vs != null) also the channel scales and their
+    // change flags, which otherwise k_vscale computes once every row is in
+    const int c = (hh - nH - nKV) * 64 + threadIdx.x;
+    if (c < kvDim) {
       const float v = row[qDim + kvDim + c];
       bad |= !isfinite(v);
       vcache[(int64_t)(n0 + t) * kvDim + c] = v;
-      atomicMax(vmax + c, __float_as_uint(fabsf(v)));
+      if (vs) {
+        const uint32_t m = max(vmax[c], __float_as_uint(fabsf(v)));
+        vmax[c] = m;
+        const float ns = __double2float_rn(quant_scale(__uint_as_float(m)));
+        vchg[c] = n0 == 0 || ns != vs[c];
+        vs[c] = ns;
+      } else {
+        atomicMax(vmax + c, __float_as_uint(fabsf(v)));
+      }
     }
     if (bad) atomicOr(status, DC_ST_NONFINITE);
     return;
@@ -539,8 +553,11 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
                                                        const int8_t* __restrict__ v8t, const float* __restrict__ vs,
                                                        const int* __restrict__ n0p, int max_pos, int ldp, int CH,
                                                        double scale, float* __restrict__ out,
-                                                       uint32_t* __restrict__ rowmax, int* status) {
+                                                       uint32_t* __restrict__ rowmax, int* __restrict__ done,
+                                                       int8_t* __restrict__ xq, int ldq, float* __restrict__ rsq,
+                                                       int* status) {
   extern __shared__ __align__(16) uint8_t sm[];
+  asm volatile("griddepcontrol.launch_dependents;");  // the O projection may start streaming its weights
   const int ldpv = ldp;                                        // bytes per value row in shared memory
   int8_t* sK = (int8_t*)sm;                                    // 2 slots x ATTD_KB x hd
   int8_t* sV = sK + 2 * ATTD_KB * hd;                          // CH x ldpv
@@ -689,6 +706,23 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
       if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] >> 1) & 1u, status);
   }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
+  // the last CTA to finish quantises the whole context row (quantizeRows) for
+  // the O projection, then re-arms the counter
+  __shared__ int is_last;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(done, 1) == (int)(gridDim.x * gridDim.y) - 1;
+  __syncthreads();
+  if (is_last) {
+    __threadfence();
+    const double sc = quant_scale(__uint_as_float(__ldcg(rowmax))), rsc = __drcp_rn(sc);
+    const int qDim = nH * hd;
+    if (tid == 0) {
+      rsq[0] = __double2float_rn(sc);
+      *done = 0;
+    }
+    for (int j = tid; j < ldq; j += 256) xq[j] = j < qDim ? dc_quant_div((double)__ldcg(out + j), sc, rsc) : (int8_t)0;
+  }
 }
 
 // SwiGLU, element-parallel over grid (ceil(I/256), rows): hid = f32(silu(g)*u)
@@ -989,6 +1023,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->d_step, 16)) || (rc = st_alloc(S, (void**)&S->xlap, 4 * (size_t)S->C)) ||
       (rc = st_alloc(S, (void**)&S->logits1, 4 * (size_t)(head ? S->V : 1))) ||
       (rc = st_alloc(S, (void**)&S->amax_keys, 64)) ||
+      (rc = st_alloc(S, (void**)&S->att_done, 16)) ||
       (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
     return fail(rc);
   // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1
@@ -1003,6 +1038,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
   if ((rc = upload(S, c.data(), c.size(), &S->rope_cos)) || (rc = upload(S, sn.data(), sn.size(), &S->rope_sin)))
     return fail(rc);
   if (cudaMemsetAsync(S->amax_keys, 0, 64, ctx->stream) != cudaSuccess ||
+      cudaMemsetAsync(S->att_done, 0, 16, ctx->stream) != cudaSuccess ||
       cudaMemsetAsync(S->d_zero, 0, 16, ctx->stream) != cudaSuccess ||
       cudaMemsetAsync(S->d_pos, 0, 16, ctx->stream) != cudaSuccess)
     return fail(dc_fail(ctx, DC_E_CUDA, "stage: position init failed"));
@@ -1214,16 +1250,19 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     dc_kv& kv = ly.kv;
     // attention block
     k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm1, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status);
+                                                         ctx->d_status, nullptr, S->rowmax);
     dc_count_launch();
     if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
-    k_rope_append<<<dim3(T, S->nH + S->nKV + 1), 64, 0, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos,
-                                                              S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
-                                                              kv.vmax, ctx->d_status);
+    const int vblocks = (S->kvDim + 63) / 64;
+    k_rope_append<<<dim3(T, S->nH + S->nKV + vblocks), 64, 0, st>>>(
+        S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
+        kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, ctx->d_status);
     dc_count_launch();
-    k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0p);
-    dc_count_launch();
+    if (T > 1) {
+      k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0p);
+      dc_count_launch();
+    }
     if (T <= 8) {
       k_vquant_dev<<<dim3((S->max_pos + 63) / 64, (S->kvDim + 31) / 32), 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8t,
                                                                                        T, n0p, S->kvDim, S->hd,
@@ -1233,27 +1272,26 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                                                                         S->kvDim, S->hd, S->ldp);
     }
     dc_count_launch();
-    DC_CUDA(ctx, cudaMemsetAsync(S->rowmax, 0, 4 * (size_t)T, st));
     if (T == 1 && use_kv && dec_ch) {
       k_attention_dec<<<dim3(S->nH, S->hd / dec_ch), 256, dec_smem, st>>>(
           S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale,
-          S->ctxo, S->rowmax, ctx->d_status);
+          S->ctxo, S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status);
+      dc_count_launch();
     } else {
       k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
                                                                 kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
                                                                 S->ctxo, S->rowmax, S->qDim, ctx->d_status);
+      dc_count_launch();
+      k_rowquant<<<dim3((S->ldQ + 255) / 256, T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
+                                                                S->rs);
+      dc_count_launch();
     }
-    dc_count_launch();
-    k_rowquant<<<dim3((S->ldQ + 255) / 256, T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
-                                                              S->rs);
-    dc_count_launch();
     if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, x, DC_F_ADDTO))) return rc;  // x2 = x + attn
     // MLP block
     k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm2, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status);
+                                                         ctx->d_status, nullptr, S->rowmax);
     dc_count_launch();
     if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
-    DC_CUDA(ctx, cudaMemsetAsync(S->rowmax, 0, 4 * (size_t)T, st));
     k_swiglu<<<dim3((S->I + 255) / 256, T), 256, 0, st>>>(S->hbuf, S->I, S->rowmax, ctx->d_status);
     dc_count_launch();
     k_rowquant<<<dim3((S->ldI + 255) / 256, T), 256, 0, st>>>(S->hbuf, 2 * (int64_t)S->I, S->I, S->rowmax, S->xq,
