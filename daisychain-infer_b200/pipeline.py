@@ -74,7 +74,8 @@ class Ring:
     # ---- chunked prefill + decode --------------------------------------------------
     def generate_chunked(self, ids0: list, n_new: int, chunk_size: int = 16, window: int = 2, on_prefill=None):
         """Returns the device tensor of picked ids on the head (n_new int32), None elsewhere.
-        ``on_prefill`` (optional) is called on the head when the prefill lap is complete."""
+        ``on_prefill`` (optional) is called on every rank once its prefill part is issued
+        (on the head: when the prefill lap has returned)."""
         S, H = self.stage, self.hidden
         S.kv_reset()
         chunks = shard.prefill_chunks(len(ids0), chunk_size, window)
@@ -112,6 +113,8 @@ class Ring:
             self.tp.recv(buf, self.prv).wait()
             S.run_layers_chunk(buf, ch["lo"])
             pending.append(self.tp.send(buf, self.nxt))
+        if on_prefill:
+            on_prefill()
         for n in range(n_new):
             buf = self.new_buffer(H)
             self.tp.recv(buf, self.prv).wait()

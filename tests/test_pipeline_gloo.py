@@ -95,7 +95,9 @@ def run_rank(rank, world, port, prompt, q):
     st = FakeStage(lo, hi, rank == 0)
     ring = P.pipeline.Ring(st, rank, world, H, P.pipeline.TorchP2P() if world > 1 else None,
                            new_buffer=lambda n: torch.empty(n, dtype=torch.float32))
-    picks = ring.generate_chunked(prompt, 5, chunk_size=3, window=2)
+    marks = []
+    picks = ring.generate_chunked(prompt, 5, chunk_size=3, window=2, on_prefill=lambda: marks.append(rank))
+    assert marks == [rank]  # every rank marks the end of its prefill part once (the bench's timer)
     look = ring.generate_lookahead([4, 4, 4, 7, 4, 4, 4], 4, 12, 4)
     if world > 1:
         dist.destroy_process_group()
