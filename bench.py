@@ -263,7 +263,12 @@ def bench_model(args, rank, world, peaks):
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
-    comp.L.dc_timing(comp.h, 1)
+    # chunked workloads run their decode rows as CUDA graphs, which carry no
+    # per-GEMM events: their GEMMs are timed in a pass right after the timed
+    # region; the window / lookahead workloads time them live
+    live = w["mode"] != "chunked"
+    if live:
+        comp.L.dc_timing(comp.h, 1)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     t0.record()
@@ -283,33 +288,42 @@ def bench_model(args, rank, world, peaks):
     ms_step = t0.elapsed_time(t1) / args.steps
     pre = statistics.mean(a.elapsed_time(b) for a, b, _ in marks["ev"])
     dec = statistics.mean(b.elapsed_time(c) for _, b, c in marks["ev"])
-    # the live GEMM timing of this rank: GEMV (decode) and tcgen05 (prefill)
+    # the GEMM timing of this rank: GEMV (decode) and tcgen05 (prefill)
     import ctypes as C
-    kinds = {}
-    for kind in (1, 3):
-        ms, n, by, op = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
-        comp.L.dc_timing_read(comp.h, kind, C.byref(ms), C.byref(n), C.byref(by), C.byref(op))
-        kinds[kind] = (ms.value, n.value, by.value, op.value)
-    comp.L.dc_timing(comp.h, 0)
-    # On one GPU the timed decode laps are CUDA-graph replays, which carry no
-    # per-GEMV events: the GEMV launch duration is measured right after the
-    # timed region on the same stage and shapes, in 16 un-captured laps.
-    gemv_method = "CUDA events around every GEMV launch in the timed region"
-    if world == 1 and w["mode"] == "chunked" and getattr(ring, "use_graph", False):
+
+    def read_kinds():
+        out = {}
+        for kind in (1, 3):
+            ms, n, by, op = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
+            comp.L.dc_timing_read(comp.h, kind, C.byref(ms), C.byref(n), C.byref(by), C.byref(op))
+            out[kind] = (ms.value, n.value, by.value, op.value)
+        return out
+
+    if live:
+        kinds = read_kinds()
+        comp.L.dc_timing(comp.h, 0)
+        gemv_method = tc_method = "CUDA events around every launch in the timed region"
+    else:
+        # every rank: one more generation (the same prompt, 16 decode tokens)
+        # with events around each GEMM; its laps run kernel by kernel
+        use_graph = getattr(ring, "use_graph", False)
         ring.use_graph = False
         comp.L.dc_timing(comp.h, 1)
         ring.generate_chunked(ids, 16, w["chunk"], w["window"])
-        ms_, n_, by_, op_ = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
-        comp.L.dc_timing_read(comp.h, 1, C.byref(ms_), C.byref(n_), C.byref(by_), C.byref(op_))
+        got = read_kinds()
         comp.L.dc_timing(comp.h, 0)
-        ring.use_graph = True
+        ring.use_graph = use_graph
         laps = w["new"] * args.steps
-        per_lap = n_.value / 16.0
-        scale = laps * per_lap / max(n_.value, 1)
-        kinds[1] = (ms_.value * scale, int(round(laps * per_lap)), by_.value * scale, op_.value * scale)
-        gemv_method = ("CUDA events around every GEMV launch of 16 un-captured decode laps run right after the "
-                       "timed region (same stage, same shapes; the timed laps are CUDA-graph replays), scaled to "
-                       "the timed region's laps")
+        ms_, n_, by_, op_ = got[1]
+        scale = laps / 16.0
+        kinds = {1: (ms_ * scale, int(round(n_ * scale)), by_ * scale, op_ * scale),
+                 3: (got[3][0] * args.steps, int(got[3][1] * args.steps), got[3][2] * args.steps,
+                     got[3][3] * args.steps)}
+        gemv_method = ("CUDA events around every GEMV launch of 16 decode steps run kernel by kernel right after "
+                       "the timed region (same stages, same shapes; the timed decode steps are CUDA-graph "
+                       "replays), scaled to the timed region's steps")
+        tc_method = ("CUDA events around every tcgen05 launch of the same prompt's prefill, run right after the "
+                     "timed region, times the timed steps")
     ms_step, pre, dec = max_over_ranks([ms_step, pre, dec], world)
     launches = int(sum_over_ranks([launches], world)[0])
     n_new = w["new"]
@@ -327,8 +341,7 @@ def bench_model(args, rank, world, peaks):
                     kernel=("k_gemv_row (decode GEMV, M=1)" if dom == 1 else "k_gemm_tc (tcgen05, M>8)"),
                     launches=n, avg_launch_us=per_launch_ms * 1e3, share_of_step=ms / (ms_step * args.steps),
                     algorithmic_bytes_per_launch=by / max(n, 1), ops_per_launch=op / max(n, 1),
-                    method=(gemv_method if dom == 1 else "CUDA events around every tcgen05 GEMM launch in the "
-                            "timed region"),
+                    method=(gemv_method if dom == 1 else tc_method),
                     peak_source=f"{peaks['src']} HBM copy bandwidth (MEASURED_PEAKS.json)")
         other = {("gemv" if k == 1 else "tcgen05"): dict(ms=kinds[k][0], launches=kinds[k][1],
                                                           gbs=(kinds[k][2] / (kinds[k][0] / 1e3) / 1e9

@@ -93,6 +93,10 @@ struct dc_stage {
   int* att_done = nullptr;  // decode attention: CTAs finished (kept at zero between launches)
   cudaGraphExec_t lap_exec = nullptr;
   unsigned long long lap_nk = 0;  // kernels in one replay of lap_exec
+  float* xrow = nullptr;              // one-row graph: the row, in place
+  cudaGraphExec_t row_exec = nullptr;  // one-row graph of this stage's layers
+  unsigned long long row_nk = 0;
+  bool row_graph = true;
   std::vector<dc_stage*> lap_key;
   int32_t* lap_picks = nullptr;
   std::vector<void*> allocs;
@@ -548,6 +552,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
 // Dynamic shared memory: 2 * 256 * hd (keys) + CH * ldp (values) + 13 * ldp.
 // hd is 32, 64, 128 or 256; CH divides hd.
 constexpr int ATTD_KB = 256;  // keys per ring slot
+constexpr int ATTD_NS = 2;    // ring slots (one block in flight while one is consumed)
 __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
                                                        const int8_t* __restrict__ k8, const float* __restrict__ ks,
                                                        const int8_t* __restrict__ v8t, const float* __restrict__ vs,
@@ -559,12 +564,12 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
   extern __shared__ __align__(16) uint8_t sm[];
   asm volatile("griddepcontrol.launch_dependents;");  // the O projection may start streaming its weights
   const int ldpv = ldp;                                        // bytes per value row in shared memory
-  int8_t* sK = (int8_t*)sm;                                    // 2 slots x ATTD_KB x hd
-  int8_t* sV = sK + 2 * ATTD_KB * hd;                          // CH x ldpv
+  int8_t* sK = (int8_t*)sm;                                    // ATTD_NS slots x ATTD_KB x hd
+  int8_t* sV = sK + ATTD_NS * ATTD_KB * hd;                    // CH x ldpv
   double* xs = (double*)(sV + (size_t)CH * ldpv);              // ldp doubles: s*scale, then e
   float* af = (float*)(xs + ldp);                              // ldp floats: key scales, then f32(e), then a
   int8_t* a8 = (int8_t*)(af + ldp);                            // ldp bytes
-  __shared__ __align__(8) uint64_t full[2], vbar;
+  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar;
   __shared__ __align__(16) int8_t q8[256];
   __shared__ float red[32];
   __shared__ double redd[32];
@@ -578,21 +583,21 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
   const int nb = (N + ATTD_KB - 1) / ATTD_KB;  // key blocks
   const int8_t* kg = k8 + (int64_t)g * max_pos * hd;
   if (tid == 0) {
-    dcp::mbar_init(&full[0], 1);
-    dcp::mbar_init(&full[1], 1);
+    for (int i = 0; i < ATTD_NS; i++) dcp::mbar_init(&full[i], 1);
     dcp::mbar_init(&vbar, 1);
     abort_flag = 0;
     dcp::mbar_fence_init();
   }
   __syncthreads();
-  int issued[2] = {-1, -1};  // thread 0: last key block issued into each slot
-  if (warp == 0) {  // issue: the CH value rows, then the first two key blocks
+  int issued[ATTD_NS];  // thread 0: last key block issued into each slot
+  for (int i = 0; i < ATTD_NS; i++) issued[i] = -1;
+  if (warp == 0) {  // issue: the CH value rows, then the first ATTD_NS key blocks
     if (lane == 0) dcp::mbar_expect_tx(&vbar, (uint32_t)(CH * ldpN));
     __syncwarp();
     for (int c = lane; c < CH; c += 32)
       dcp::bulk_load(sV + (size_t)c * ldpv, v8t + ((int64_t)g * hd + c0 + c) * ldp, (uint32_t)ldpN, &vbar);
     if (lane == 0)
-      for (int b = 0; b < 2 && b < nb; b++) {
+      for (int b = 0; b < ATTD_NS && b < nb; b++) {
         issued[b] = b;
         const int kn = min(ATTD_KB, N - b * ATTD_KB);
         const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
@@ -610,7 +615,8 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
     mx = fmaxf(mx, fabsf(v));
   }
   const float* ksg = ks + (int64_t)g * max_pos;
-  for (int j = tid; j < N; j += 256) af[j] = ksg[j];  // key scales
+#pragma unroll 8
+  for (int j = tid; j < N; j += 256) af[j] = ksg[j];  // key scales (all loads in flight together)
   mx = block_max_f(mx, red);
   const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
   const float qs = __double2float_rn(qsc);
@@ -622,8 +628,8 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
   const int4 qv = ((const int4*)q8)[part];
   double m = -INFINITY;
   for (int b = 0; b < nb; b++) {
-    const int slot = b & 1;
-    if (!dcp::mbar_wait(&full[slot], (uint32_t)(b >> 1) & 1u, status)) abort_flag = 1;
+    const int slot = b % ATTD_NS;
+    if (!dcp::mbar_wait(&full[slot], (uint32_t)(b / ATTD_NS) & 1u, status)) abort_flag = 1;
     __syncthreads();
     if (abort_flag) break;
     const int kb = b * ATTD_KB, kn = min(ATTD_KB, N - kb);
@@ -639,12 +645,13 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
       }
     }
     __syncthreads();  // slot consumed
-    if (tid == 0 && b + 2 < nb) {
-      issued[slot] = b + 2;
-      const int kn2 = min(ATTD_KB, N - (b + 2) * ATTD_KB);
+    if (tid == 0 && b + ATTD_NS < nb) {
+      issued[slot] = b + ATTD_NS;
+      const int kn2 = min(ATTD_KB, N - (b + ATTD_NS) * ATTD_KB);
       const uint32_t bytes = (uint32_t)(((kn2 * hd) + 15) & ~15);
       dcp::mbar_expect_tx(&full[slot], bytes);
-      dcp::bulk_load(sK + (size_t)slot * ATTD_KB * hd, kg + (int64_t)(b + 2) * ATTD_KB * hd, bytes, &full[slot]);
+      dcp::bulk_load(sK + (size_t)slot * ATTD_KB * hd, kg + (int64_t)(b + ATTD_NS) * ATTD_KB * hd, bytes,
+                     &full[slot]);
     }
   }
   const bool aborted = abort_flag != 0;
@@ -702,8 +709,8 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
   }
   if (abort_flag && tid == 0) {  // let copies still in flight land before the CTA goes away (bounded)
     dcp::mbar_wait(&vbar, 0, status);
-    for (int sl = 0; sl < 2; sl++)
-      if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] >> 1) & 1u, status);
+    for (int sl = 0; sl < ATTD_NS; sl++)
+      if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] / ATTD_NS) & 1u, status);
   }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
   // the last CTA to finish quantises the whole context row (quantizeRows) for
@@ -1024,6 +1031,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->logits1, 4 * (size_t)(head ? S->V : 1))) ||
       (rc = st_alloc(S, (void**)&S->amax_keys, 64)) ||
       (rc = st_alloc(S, (void**)&S->att_done, 16)) ||
+      (rc = st_alloc(S, (void**)&S->xrow, 4 * (size_t)S->C)) ||
       (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
     return fail(rc);
   // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1
@@ -1051,6 +1059,7 @@ extern "C" void dc_stage_free(dc_stage* S) {
   if (!S) return;
   if (S->ctx) cudaStreamSynchronize(S->ctx->stream);
   if (S->lap_exec) cudaGraphExecDestroy(S->lap_exec);
+  if (S->row_exec) cudaGraphExecDestroy(S->row_exec);
   for (void* p : S->allocs) cudaFree(p);
   delete S;
 }
@@ -1233,7 +1242,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   if (S->hd == 32 || S->hd == 64 || S->hd == 128 || S->hd == 256) {
     for (int ch = 32; ch >= 8 && !dec_ch; ch >>= 1) {
       if (S->hd % ch) continue;
-      const size_t need = 2 * (size_t)ATTD_KB * S->hd + (size_t)(ch + 13) * S->ldp;
+      const size_t need = (size_t)ATTD_NS * ATTD_KB * S->hd + (size_t)(ch + 13) * S->ldp;
       if (need + 12 * 1024 <= 232448) {
         dec_ch = ch;
         dec_smem = need;
@@ -1305,6 +1314,73 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
 
 // runLayers (use_kv = 0: full window, positions 0..T-1) or runLayersChunk
 // (use_kv = 1: positions pos0.., keys/values appended to this stage's cache).
+// Moves the context onto its own (capturable) stream for the scope: the own
+// stream waits for the caller's, and the caller's waits for the own stream at
+// the end of the scope.
+struct StreamSwap {
+  dc_ctx* c;
+  cudaStream_t user;
+  bool on;
+  explicit StreamSwap(dc_ctx* c_) : c(c_), user(c_->stream), on(false) {}
+  int fork() {
+    if (c->stream == c->own_stream) return DC_OK;
+    DC_CUDA(c, cudaEventRecord(c->ev_fork, c->stream));
+    DC_CUDA(c, cudaStreamWaitEvent(c->own_stream, c->ev_fork, 0));
+    c->stream = c->own_stream;
+    on = true;
+    return DC_OK;
+  }
+  ~StreamSwap() {
+    if (on) {
+      cudaEventRecord(c->ev_join, c->own_stream);
+      cudaStreamWaitEvent(user, c->ev_join, 0);
+      c->stream = user;
+    }
+  }
+};
+
+// One cached row (T = 1) through the stage's layers as a CUDA graph: the row is
+// copied into the stage's own buffer, the graph (captured on first use; every
+// position-dependent kernel reads the position from d_pos) runs in place, and
+// the row is copied back.  Used for decode steps of a multi-GPU pipeline, where
+// each stage runs one row per token.
+static int forward_row_graph(dc_stage* S, float* x, int n0) {
+  dc_ctx* ctx = S->ctx;
+  StreamSwap swap(ctx);
+  if (int rc = swap.fork()) return rc;
+  cudaStream_t s = ctx->stream;
+  DC_CUDA(ctx, cudaMemcpyAsync(S->xrow, x, 4 * (size_t)S->C, cudaMemcpyDeviceToDevice, s));
+  k_setpos<<<1, 1, 0, s>>>(S->d_pos, n0);
+  dc_count_launch();
+  if (!S->row_exec) {
+    cudaGraph_t g = nullptr;
+    const unsigned long long nk0 = dc_launch_count();
+    DC_CUDA(ctx, cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+    int rc = forward_layers(S, S->xrow, 1, n0, 1, S->d_pos);
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    S->row_nk = dc_launch_count() - nk0;
+    dc_count_launches(-(long long)S->row_nk);  // captured, not launched
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return dc_cuda_fail(ctx, e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&S->row_exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return dc_cuda_fail(ctx, e, "cudaGraphInstantiate");
+  }
+  DC_CUDA(ctx, cudaGraphLaunch(S->row_exec, s));
+  dc_count_launches((long long)S->row_nk);
+  DC_CUDA(ctx, cudaMemcpyAsync(x, S->xrow, 4 * (size_t)S->C, cudaMemcpyDeviceToDevice, s));
+  return DC_OK;
+}
+
+extern "C" int dc_stage_set_row_graph(dc_stage* S, int on) {
+  if (!S) return DC_E_INVAL;
+  S->row_graph = on != 0;
+  return DC_OK;
+}
+
 extern "C" int dc_stage_forward(dc_stage* S, float* x, int T, int pos0, int use_kv) {
   if (!S || !x || T < 1 || T > S->max_rows) return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_forward: bad T");
   dc_ctx* ctx = S->ctx;
@@ -1315,6 +1391,11 @@ extern "C" int dc_stage_forward(dc_stage* S, float* x, int T, int pos0, int use_
   if (N > S->max_pos || pos0 + T > S->max_pos)
     return dc_fail(ctx, DC_E_INVAL, "stage_forward: %d positions exceed max_pos %d", N, S->max_pos);
   if (S->L.empty()) return DC_OK;
+  if (use_kv && T == 1 && S->row_graph && !ctx->timing) {
+    if (int rc = forward_row_graph(S, x, n0)) return rc;
+    S->kv_len = N;
+    return DC_OK;
+  }
   const int* n0p = S->d_zero;
   if (use_kv) {
     k_setpos<<<1, 1, 0, ctx->stream>>>(S->d_pos, n0);
@@ -1383,25 +1464,8 @@ extern "C" int dc_decode_run(dc_stage** stages, int ns, const float* x_last, int
   // Work on the context's own stream (the legacy default stream cannot be
   // captured): it waits for the caller's stream, and the caller's stream waits
   // for it when the laps are enqueued.
-  struct StreamSwap {
-    dc_ctx* c;
-    cudaStream_t user;
-    bool on;
-    StreamSwap(dc_ctx* c_) : c(c_), user(c_->stream), on(false) {}
-    ~StreamSwap() {
-      if (on) {
-        cudaEventRecord(c->ev_join, c->own_stream);
-        cudaStreamWaitEvent(user, c->ev_join, 0);
-        c->stream = user;
-      }
-    }
-  } swap(ctx);
-  if (ctx->stream != ctx->own_stream) {
-    DC_CUDA(ctx, cudaEventRecord(ctx->ev_fork, ctx->stream));
-    DC_CUDA(ctx, cudaStreamWaitEvent(ctx->own_stream, ctx->ev_fork, 0));
-    ctx->stream = ctx->own_stream;
-    swap.on = true;
-  }
+  StreamSwap swap(ctx);
+  if (int rc0 = swap.fork()) return rc0;
   s = ctx->stream;
   DC_CUDA(ctx, cudaMemcpyAsync(H->xlap, x_last, 4 * (size_t)H->C, cudaMemcpyDeviceToDevice, s));
   k_setpos<<<1, 1, 0, s>>>(H->d_step, 0);

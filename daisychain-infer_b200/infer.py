@@ -203,6 +203,10 @@ class Stage:
     def kv_reset(self) -> None:
         self._check(self.L.dc_stage_kv_reset(self.h), "kv_reset")
 
+    def set_row_graph(self, on: bool) -> None:
+        """One-row cached forwards (decode steps) as a CUDA graph (default) or kernel by kernel."""
+        self._check(self.L.dc_stage_set_row_graph(self.h, 1 if on else 0), "set_row_graph")
+
     def kv_len(self) -> int:
         return self.L.dc_stage_kv_len(self.h)
 

@@ -207,6 +207,11 @@ int dc_stage_embed(dc_stage* stage, const int32_t* ids, int T, float* x);
  * stage's cache, infer.js:288-296); x (device, T x hidden) is updated in place.
  * Asynchronous: a non-finite activation is reported by dc_sync as DC_E_NONFINITE. */
 int dc_stage_forward(dc_stage* stage, float* x, int T, int pos0, int use_kv);
+/* A cached one-row forward (use_kv = 1, T = 1: a decode step of a pipeline
+ * stage) runs as a CUDA graph of the stage's layers, captured on first use
+ * (the default).  on = 0 launches the kernels one by one instead; the results
+ * are identical. */
+int dc_stage_set_row_graph(dc_stage* stage, int on);
 /* logitsAt (infer.js:324-334) for rows[0..nrows) (host ints, nrows <= 8):
  * logits (device, nrows x vocab) and the greedy pick of each row (device int32,
  * may be NULL), first maximum wins (infer.js:393-395). */

@@ -115,6 +115,11 @@ def test_decode_loop_modes_agree(comp, O, P, fixture):
         for splits in ([6], [0, 3, 3]):
             got = P.infer.generate_chunked(make_stages(P, comp, spec, w, splits), prompt, 12, 5, **kw)
             assert got == ref, (kw, splits)
+    # the host-driven loop with each stage's one-row forward kernel by kernel (no row graph)
+    st = make_stages(P, comp, spec, w, [2, 4])
+    for S in st:
+        S.set_row_graph(False)
+    assert P.infer.generate_chunked(st, prompt, 12, 5, use_device_loop=False) == ref
 
 
 def test_kv_cache_contents_match_oracle(comp, O, P, fixture):
