@@ -91,6 +91,8 @@ struct dc_stage {
   float* logits1 = nullptr; // head: logits of the lap's row
   unsigned long long* amax_keys = nullptr;  // head: greedy-pick keys (8 rows), kept at zero between uses
   int* att_done = nullptr;  // decode attention: CTAs finished (kept at zero between launches)
+  int8_t* a8g = nullptr;    // chunk attention: probability rows [head][row][ldp] (rows <= 16)
+  float* asg = nullptr;     // and their scales [head][row]
   cudaGraphExec_t lap_exec = nullptr;
   unsigned long long lap_nk = 0;  // kernels in one replay of lap_exec
   float* xrow = nullptr;              // one-row graph: the row, in place
@@ -417,7 +419,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
                                                            const int* __restrict__ n0p, int max_pos,
                                                            int ldp, double scale, float* __restrict__ out,
                                                            uint32_t* __restrict__ rowmax, int qDim,
-                                                           int* status) {
+                                                           int* status, int8_t* __restrict__ a8g = nullptr,
+                                                           float* __restrict__ asg = nullptr) {
   extern __shared__ __align__(16) uint8_t sm[];
   double* ed = (double*)sm;                                 // max_pos doubles: e_j
   float* af = (float*)(ed + max_pos);                       // max_pos floats: scores, then a_j
@@ -485,17 +488,28 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
   const double z = dco::ordered_sum(ed, see + 1, osm);
   // 6. a_j = f32(a_j / z); 7. quantise the probability row over all N columns
   float amx = 0.0f;
+  const double rz = __drcp_rn(z);
   for (int j = threadIdx.x; j <= see; j += blockDim.x) {
-    const float a = __double2float_rn(__ddiv_rn((double)af[j], z));
+    const float a = dc_div_to_f32((double)af[j], z, rz);
     af[j] = a;
     amx = fmaxf(amx, fabsf(a));
   }
   amx = block_max_f(amx, red);
-  const double asc = quant_scale(amx);
+  const double asc = quant_scale(amx), rasc = __drcp_rn(asc);
   const float as = __double2float_rn(asc);
+  if (a8g) {
+    // split form: the probability row (zero past `see`, up to the chunk's last
+    // key) and its scale go to global memory; k_attn_ctx forms the context
+    const int nfill = (n0 + T + 15) & ~15;
+    int8_t* dst = a8g + ((int64_t)hq * T + i) * ldp;
+    for (int j = threadIdx.x; j < nfill; j += blockDim.x) dst[j] = j <= see ? dc_quant_div((double)af[j], asc, rasc) : (int8_t)0;
+    if (threadIdx.x == 0) asg[hq * T + i] = as;
+    if (bad) atomicOr(status, DC_ST_NONFINITE);
+    return;
+  }
   const int nchunk = (see + 16) >> 4;  // 16-byte chunks covering keys 0..see
   for (int j = threadIdx.x; j < nchunk * 16; j += blockDim.x)
-    a8[j] = j <= see ? dc_clamp8(dc_js_round(__ddiv_rn((double)af[j], asc))) : (int8_t)0;
+    a8[j] = j <= see ? dc_quant_div((double)af[j], asc, rasc) : (int8_t)0;
   __syncthreads();
   // 8. ctx[c] = sum_j a8[j] * v8[c][j] over j <= see (a8 is zero past `see`)
   const int4* a4 = (const int4*)a8;
@@ -537,6 +551,70 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restri
       bad |= !isfinite(o);
       atomicMax(rowmax + i, __float_as_uint(fabsf(o)));  // for the next GEMM's row quantisation
     }
+  }
+  if (bad) atomicOr(status, DC_ST_NONFINITE);
+}
+
+// The context of a chunk's T rows for 32 channels of one head, from the
+// probability rows k_attention wrote (split form): grid (nH, hd / 32), 256
+// threads; ctx[t][c] = sum_j a8[t][j] * v8[c][j] (exact int32), verified
+// epilogue with the row's probability scale and the channel's value scale.
+// The 32 value rows and the T probability rows land in shared memory by 1-D
+// bulk copies.  Dynamic shared memory: (32 + T) * ldp.
+__global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* __restrict__ a8g, const float* __restrict__ asg,
+                                                  const int8_t* __restrict__ v8t, const float* __restrict__ vs,
+                                                  int nH, int nKV, int hd, int T, const int* __restrict__ n0p,
+                                                  int ldp, float* __restrict__ out, int qDim,
+                                                  uint32_t* __restrict__ rowmax, int* status) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  int8_t* sV = (int8_t*)sm;              // 32 x ldp
+  int8_t* sA = sV + (size_t)32 * ldp;     // T x ldp
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float sas[16];
+  const int hq = blockIdx.x, c0 = blockIdx.y * 32;
+  const int g = hq / (nH / nKV);
+  const int tid = threadIdx.x;
+  const int nfill = (*n0p + T + 15) & ~15;  // bytes of each row in use
+  if (tid == 0) {
+    dcp::mbar_init(&bar, 1);
+    dcp::mbar_fence_init();
+  }
+  __syncthreads();
+  if (tid < 32) {
+    if (tid == 0) dcp::mbar_expect_tx(&bar, (uint32_t)((32 + T) * nfill));
+    __syncwarp();
+    dcp::bulk_load(sV + (size_t)tid * ldp, v8t + ((int64_t)g * hd + c0 + tid) * ldp, (uint32_t)nfill, &bar);
+    if (tid < T) dcp::bulk_load(sA + (size_t)tid * ldp, a8g + ((int64_t)hq * T + tid) * ldp, (uint32_t)nfill, &bar);
+  }
+  if (tid < T) sas[tid] = asg[hq * T + tid];
+  const bool ok = dcp::mbar_wait(&bar, 0, status);
+  __syncthreads();
+  if (!ok) return;
+  const int cl = tid >> 3, tg = tid & 7;  // channel c0 + cl; rows tg and tg + 8
+  const int t0 = tg, t1 = tg + 8;
+  const int4* vr = (const int4*)(sV + (size_t)cl * ldp);
+  const int4* ar0 = (const int4*)(sA + (size_t)t0 * ldp);
+  const int4* ar1 = (const int4*)(sA + (size_t)(t1 < T ? t1 : t0) * ldp);
+  int s0 = 0, s1 = 0;
+  for (int q = 0; q < (nfill >> 4); q++) {
+    const int4 v = vr[q];
+    s0 = dp4a16(v, ar0[q], s0);
+    s1 = dp4a16(v, ar1[q], s1);
+  }
+  const int c = c0 + cl;
+  const float vsc = vs[g * hd + c];
+  bool bad = false;
+  if (t0 < T) {
+    const float o = dc_epi(s0, sas[t0], vsc);
+    out[(int64_t)t0 * qDim + hq * hd + c] = o;
+    bad |= !isfinite(o);
+    atomicMax(rowmax + t0, __float_as_uint(fabsf(o)));
+  }
+  if (t1 < T) {
+    const float o = dc_epi(s1, sas[t1], vsc);
+    out[(int64_t)t1 * qDim + hq * hd + c] = o;
+    bad |= !isfinite(o);
+    atomicMax(rowmax + t1, __float_as_uint(fabsf(o)));
   }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
@@ -1032,6 +1110,8 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->amax_keys, 64)) ||
       (rc = st_alloc(S, (void**)&S->att_done, 16)) ||
       (rc = st_alloc(S, (void**)&S->xrow, 4 * (size_t)S->C)) ||
+      (rc = st_alloc(S, (void**)&S->a8g, (size_t)std::min(S->max_rows, 16) * S->nH * S->ldp)) ||
+      (rc = st_alloc(S, (void**)&S->asg, 4 * (size_t)std::min(S->max_rows, 16) * S->nH)) ||
       (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
     return fail(rc);
   // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1
@@ -1251,6 +1331,12 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     if (dec_ch)
       if (int rc0 = dc_set_smem(ctx, (const void*)k_attention_dec, (int)dec_smem)) return rc0;
   }
+  // chunk rows (T <= 16): probabilities per (head, row), then the context per
+  // (head, 32 channels) from shared-memory copies of the value and probability rows
+  const size_t ctx_smem = (size_t)(32 + 16) * S->ldp;
+  const bool split_ctx = S->a8g && S->hd % 32 == 0 && ctx_smem + 1024 <= 232448;
+  if (split_ctx)
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_attn_ctx, (int)ctx_smem)) return rc0;
   const size_t nrm_smem = 12 * (size_t)S->C;  // squares (double) + the row (float)
   // always raised: the kernel's static shared memory counts against the 48 KB default too
   if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
@@ -1285,6 +1371,19 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       k_attention_dec<<<dim3(S->nH, S->hd / dec_ch), 256, dec_smem, st>>>(
           S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale,
           S->ctxo, S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status);
+      dc_count_launch();
+    } else if (split_ctx && T <= 16) {
+      k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
+                                                                kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
+                                                                S->ctxo, S->rowmax, S->qDim, ctx->d_status, S->a8g,
+                                                                S->asg);
+      dc_count_launch();
+      k_attn_ctx<<<dim3(S->nH, S->hd / 32), 256, ctx_smem, st>>>(S->a8g, S->asg, kv.v8t, kv.vs, S->nH, S->nKV, S->hd,
+                                                                  T, n0p, S->ldp, S->ctxo, S->qDim, S->rowmax,
+                                                                  ctx->d_status);
+      dc_count_launch();
+      k_rowquant<<<dim3((S->ldQ + 255) / 256, T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
+                                                                S->rs);
       dc_count_launch();
     } else {
       k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
