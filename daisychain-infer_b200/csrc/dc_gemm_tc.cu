@@ -28,6 +28,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -191,13 +192,25 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // ---- TMA producer
+    // ---- TMA producer.  Launched as a programmatic dependent: the weight
+    // tiles of the first stages (constant data) are requested before the
+    // grid-dependency wait, the activation tiles (written by the previous
+    // kernel) after it.
     int issued = 0;
     bool ok = true;
-    for (int it = 0; it < nkb && ok; it++) {
+    const int pre = min(nkb, C::STAGES);
+    for (int it = 0; it < pre; it++) {
+      mbar_expect_tx(&full[it], C::STAGE_BYTES);
+      tma_load_2d(sA + it * C::A_BYTES, &tmW, (kb0 + it) * TILE_K, bz * a.n + j0, &full[it]);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int it = 0; it < pre; it++)
+      tma_load_2d(sB + it * C::B_BYTES, &tmX, (kb0 + it) * TILE_K, bz * a.m + i0, &full[it]);
+    issued = pre;
+    for (int it = pre; it < nkb && ok; it++) {
       const int s = it % C::STAGES;
       const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
-      if (it >= C::STAGES) ok = mbar_wait(&empty[s], ph ^ 1u, a.status);
+      ok = mbar_wait(&empty[s], ph ^ 1u, a.status);
       if (!ok) break;
       mbar_expect_tx(&full[s], C::STAGE_BYTES);
       const int kx = (kb0 + it) * TILE_K;
@@ -230,7 +243,8 @@ __global__ void __launch_bounds__(128, 1)
   }
   __syncwarp();
 
-  // ---- epilogue (all four warps)
+  // ---- epilogue (all four warps); rs and a residual `out` come from earlier kernels
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const bool have = mbar_wait(accum, 0, a.status);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const bool good = have && (*(volatile int*)flag == 0) && nkb > 0;
@@ -379,6 +393,9 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
   int splits = 1;
   if (tiles < ctx->sm_count && a.kb_total > 1) {
     splits = (ctx->sm_count + tiles - 1) / tiles;
+    // at least 4 K blocks (512 bytes of K) per split: a CTA's fixed costs
+    // (TMEM allocation, pipeline fill, the split-K fixup) need work to hide behind
+    splits = std::min(splits, std::max(1, a.kb_total / 4));
     if (splits > a.kb_total) splits = a.kb_total;
   }
   a.kb_per_split = (a.kb_total + splits - 1) / splits;
@@ -396,9 +413,18 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
   a.counters = counters;
   a.status = ctx->d_status;
   if (int rc = dc_set_smem(ctx, (const void*)k_gemm_tc<BN>, C::SMEM)) return rc;
-  dim3 grid(a.n_tiles, a.m_tiles, batch * splits);
-  k_gemm_tc<BN><<<grid, 128, C::SMEM, st>>>(mW, mX, a); dc_count_launch();
-  DC_CUDA(ctx, cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_tiles, a.m_tiles, batch * splits);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemm_tc<BN>, mW, mX, a));
+  dc_count_launch();
   return DC_OK;
 }
 
