@@ -56,10 +56,10 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
@@ -126,7 +126,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 template <int BN>
 struct TcCfg {
-  static constexpr int STAGES = BN <= 32 ? 8 : (BN <= 64 ? 7 : (BN <= 128 ? 5 : 4));
+  // BN <= 32 (chunked prefill): 5 stages (~92-102 KB), two CTAs per SM, so a
+  // layer's tiles (up to ~296 CTAs) run in one wave
+  static constexpr int STAGES = BN <= 32 ? 5 : (BN <= 64 ? 7 : (BN <= 128 ? 5 : 4));
+  static constexpr int PER_SM = BN <= 32 ? 2 : 1;
   static constexpr int A_BYTES = TILE_N * TILE_K;
   static constexpr int B_BYTES = BN * TILE_K;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -245,25 +248,52 @@ __global__ void __launch_bounds__(128, 1)
 
   // ---- epilogue (all four warps); rs and a residual `out` come from earlier kernels
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the tile's row scales, once, into shared memory (the stores below may
+  // alias them as far as the compiler knows, which would serialise every load)
+  __shared__ float rs_s[BN];
+  for (int c = threadIdx.x; c < BN; c += blockDim.x) rs_s[c] = (i0 + c < a.m) ? __ldg(a.rs + bz * a.m + i0 + c) : 0.0f;
   const bool have = mbar_wait(accum, 0, a.status);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  __syncthreads();
   const bool good = have && (*(volatile int*)flag == 0) && nkb > 0;
   const int j = j0 + warp * 32 + lane;
   const bool jv = j < a.n;
-  const float csv = jv ? a.cs[bz * a.n + j] : 0.0f;
+  const float csv = jv ? __ldg(a.cs + bz * a.n + j) : 0.0f;
+  // 16 accumulators of one column j: residual values loaded first, then stored
+  auto store16 = [&](int cbase, const int32_t (&v)[16]) {
+    float old[16];
+    if (a.flags & DC_F_ADDTO) {
+#pragma unroll
+      for (int c = 0; c < 16; c++) {
+        const int i = i0 + cbase + c;
+        old[c] = (jv && i < a.m) ? ((const float*)a.out)[((int64_t)bz * a.m + i) * a.n + j] : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 16; c++) {
+      const int i = i0 + cbase + c;
+      if (!(jv && i < a.m)) continue;
+      const int64_t idx = ((int64_t)bz * a.m + i) * a.n + j;
+      if (a.flags & (DC_ACC | DC_REQUANT)) {
+        dc_store_out(a.out, idx, v[c], rs_s[cbase + c], csv, a.flags, a.requant, a.relu);
+      } else {
+        float o = dc_epi(v[c], rs_s[cbase + c], csv);
+        if ((a.flags & DC_RELU) && o < 0.0f) o = 0.0f;
+        if (a.flags & DC_F_ADDTO) o = __fadd_rn(old[c], o);
+        ((float*)a.out)[idx] = o;
+      }
+    }
+  };
   if (a.splits == 1) {
     if (good) {
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
         tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+        int32_t v[16];
 #pragma unroll
-        for (int c = 0; c < 16; c++) {
-          const int i = i0 + c0 + c;
-          if (jv && i < a.m)
-            dc_store_out(a.out, ((int64_t)bz * a.m + i) * a.n + j, (int32_t)r[c], a.rs[bz * a.m + i], csv, a.flags,
-                         a.requant, a.relu);
-        }
+        for (int c = 0; c < 16; c++) v[c] = (int32_t)r[c];
+        store16(c0, v);
       }
     }
   } else {
@@ -287,15 +317,19 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     if (last) {
       __threadfence();
-      if (jv) {
-        for (int c = 0; c < BN; c++) {
-          const int i = i0 + c;
-          if (i >= a.m) break;
-          int32_t* p = a.partial + ((int64_t)bz * a.m + i) * a.n + j;
-          const int32_t v = __ldcg(p);
-          dc_store_out(a.out, ((int64_t)bz * a.m + i) * a.n + j, v, a.rs[bz * a.m + i], csv, a.flags, a.requant,
-                       a.relu);
-          *p = 0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        int32_t v[16];
+#pragma unroll
+        for (int c = 0; c < 16; c++) {  // all 16 partial sums in flight together
+          const int i = i0 + c0 + c;
+          v[c] = (jv && i < a.m) ? __ldcg(a.partial + ((int64_t)bz * a.m + i) * a.n + j) : 0;
+        }
+        store16(c0, v);
+#pragma unroll
+        for (int c = 0; c < 16; c++) {
+          const int i = i0 + c0 + c;
+          if (jv && i < a.m) a.partial[((int64_t)bz * a.m + i) * a.n + j] = 0;
         }
       }
       if (threadIdx.x == 0) a.counters[tile] = 0;
@@ -391,8 +425,9 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
   a.m_tiles = (m + BN - 1) / BN;
   const int tiles = a.n_tiles * a.m_tiles * batch;
   int splits = 1;
-  if (tiles < ctx->sm_count && a.kb_total > 1) {
-    splits = (ctx->sm_count + tiles - 1) / tiles;
+  const int slots = ctx->sm_count * C::PER_SM;  // CTAs resident at once
+  if (tiles < slots && a.kb_total > 1) {
+    splits = slots / tiles;  // the whole grid in one wave
     // at least 4 K blocks (512 bytes of K) per split: a CTA's fixed costs
     // (TMEM allocation, pipeline fill, the split-K fixup) need work to hide behind
     splits = std::min(splits, std::max(1, a.kb_total / 4));
