@@ -411,7 +411,7 @@ __device__ __forceinline__ int dp4a16(const int4 a, const int4 b, int acc) {
 // Scores: hd/16 lanes per key, 16-byte loads of the int8 key row, shuffle sum.
 // Context: one warp per output channel, lanes stream 16-byte chunks of that
 // channel's int8 values (channel-major cache) against the int8 probabilities.
-__global__ void __launch_bounds__(ATT_THREADS) k_attention(const float* __restrict__ h, int nqkv, int nH, int nKV,
+__global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* __restrict__ h, int nqkv, int nH, int nKV,
                                                            int hd, const int8_t* __restrict__ k8,
                                                            const float* __restrict__ ks,
                                                            const int8_t* __restrict__ v8t,
