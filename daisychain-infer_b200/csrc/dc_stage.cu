@@ -624,13 +624,13 @@ __global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* __restrict__ a8g
 // computes the head's scores and probabilities (the same numbers as
 // k_attention: scores, exact max, fdlibm exp, the serial softmax sum,
 // quantizeRows of the probabilities) and then CH channels of the context.
-// The keys stream through a two-slot shared-memory ring of 256-key blocks,
+// The keys stream through a three-slot shared-memory ring of 256-key blocks,
 // and the CTA's CH value rows (channel-major) land in shared memory once, all
 // by 1-D bulk async copies, so the loads are in flight while the softmax runs.
-// Dynamic shared memory: 2 * 256 * hd (keys) + CH * ldp (values) + 13 * ldp.
+// Dynamic shared memory: 3 * 256 * hd (keys) + CH * ldp (values) + 13 * ldp.
 // hd is 32, 64, 128 or 256; CH divides hd.
 constexpr int ATTD_KB = 256;  // keys per ring slot
-constexpr int ATTD_NS = 2;    // ring slots (one block in flight while one is consumed)
+constexpr int ATTD_NS = 3;    // ring slots (two blocks in flight while one is consumed)
 __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
                                                        const int8_t* __restrict__ k8, const float* __restrict__ ks,
                                                        const int8_t* __restrict__ v8t, const float* __restrict__ vs,
@@ -679,8 +679,11 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
         issued[b] = b;
         const int kn = min(ATTD_KB, N - b * ATTD_KB);
         const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
-        dcp::mbar_expect_tx(&full[b], bytes);
+        // the first block also brings the key scales (max_pos is a multiple of 16)
+        const uint32_t sbytes = b == 0 ? (uint32_t)(((N + 3) & ~3) * 4) : 0u;
+        dcp::mbar_expect_tx(&full[b], bytes + sbytes);
         dcp::bulk_load(sK + (size_t)b * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[b]);
+        if (sbytes) dcp::bulk_load(af, ks + (int64_t)g * max_pos, sbytes, &full[b]);
       }
   }
   // 1. the query row of this head, quantised (row scale per (token, head), double)
@@ -692,18 +695,17 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
     bad |= !isfinite(v);
     mx = fmaxf(mx, fabsf(v));
   }
-  const float* ksg = ks + (int64_t)g * max_pos;
-#pragma unroll 8
-  for (int j = tid; j < N; j += 256) af[j] = ksg[j];  // key scales (all loads in flight together)
   mx = block_max_f(mx, red);
   const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
   const float qs = __double2float_rn(qsc);
   for (int c = tid; c < hd; c += 256) q8[c] = dc_quant_div((double)qrow[c], qsc, rqsc);
   __syncthreads();
-  // 2. scores block by block from the ring: int32 dot over hd, verified epilogue
-  const int lpk = hd >> 4, kpw = 32 / lpk;  // lanes per key, keys per warp step
-  const int sub = lane / lpk, part = lane - sub * lpk;
-  const int4 qv = ((const int4*)q8)[part];
+  // 2. scores block by block from the ring: one key per thread (256 keys per
+  //    block), the int32 dot over hd from 16-byte chunks taken in a rotated
+  //    order (lanes 4l..4l+3 start at chunk l: at most 4-way bank conflicts),
+  //    then the verified epilogue; no shuffles
+  const int nchk = hd >> 4;  // a power of two: hd is 32, 64, 128 or 256
+  const int rot = lane >> 2;
   double m = -INFINITY;
   for (int b = 0; b < nb; b++) {
     const int slot = b % ATTD_NS;
@@ -711,16 +713,18 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
     __syncthreads();
     if (abort_flag) break;
     const int kb = b * ATTD_KB, kn = min(ATTD_KB, N - kb);
-    const int8_t* sk = sK + (size_t)slot * ATTD_KB * hd;
-    for (int k = warp * kpw + sub; k - sub < kn; k += 8 * kpw) {
+    const int k = tid;  // ATTD_KB == blockDim.x
+    if (k < kn) {
+      const int8_t* kr = sK + (size_t)slot * ATTD_KB * hd + (size_t)k * hd;
       int acc = 0;
-      if (k < kn) acc = dp4a16(*(const int4*)(sk + (size_t)k * hd + part * 16), qv, 0);
-      for (int o = lpk >> 1; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (part == 0 && k < kn) {
-        const double x = __dmul_rn((double)dc_epi(acc, qs, af[kb + k]), scale);
-        xs[kb + k] = x;
-        m = fmax(m, x);
+#pragma unroll 4
+      for (int c = 0; c < nchk; c++) {
+        const int cc = (c + rot) & (nchk - 1);
+        acc = dp4a16(*(const int4*)(kr + cc * 16), ((const int4*)q8)[cc], acc);
       }
+      const double x = __dmul_rn((double)dc_epi(acc, qs, af[kb + k]), scale);
+      xs[kb + k] = x;
+      m = fmax(m, x);
     }
     __syncthreads();  // slot consumed
     if (tid == 0 && b + ATTD_NS < nb) {
@@ -1042,6 +1046,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
                                int max_pos, dc_stage** out) {
   if (!ctx || !spec || !out) return DC_E_INVAL;
   if (int rc = stage_kernel_attrs(ctx)) return rc;
+  if (max_pos > 0) max_pos = round_up(max_pos, 16);  // whole 16-byte rows of key scales and int8 values
   const dc_spec& s = *spec;
   if (s.hidden <= 0 || s.heads <= 0 || s.kv_heads <= 0 || s.heads % s.kv_heads || s.head_dim <= 0 ||
       (s.head_dim % 16) || s.head_dim > 128 || s.inter <= 0 || s.vocab <= 0 || lo < 0 || hi > s.layers || hi < lo ||
