@@ -448,28 +448,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* __res
   const float qs = __double2float_rn(qsc);
   for (int c = threadIdx.x; c < hd; c += blockDim.x) q8[c] = dc_clamp8(dc_js_round(__ddiv_rn((double)qrow[c], qsc)));
   __syncthreads();
-  // 2. scores for keys 0..see: int32 dot over hd, verified epilogue
+  // 2. scores for keys 0..see: one key per thread (its 128-byte row in one
+  //    line), int32 dot over hd, verified epilogue
   {
     const int8_t* kb = k8 + (int64_t)g * max_pos * hd;
     const float* ksg = ks + (int64_t)g * max_pos;
-    const int lpk = hd >> 4, kpw = 32 / lpk;  // lanes per key, keys per warp step
-    const int sub = lane / lpk, part = lane - sub * lpk;
-    const int4 qv = ((const int4*)q8)[part];
-    const int step = nwarps * kpw;  // keys per block pass; 8 passes' loads are issued together
-    for (int j0 = warp * kpw; j0 <= see; j0 += 8 * step) {
-      int4 kv[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int j = j0 + u * step + sub;
-        kv[u] = j <= see ? *(const int4*)(kb + (int64_t)j * hd + part * 16) : make_int4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int j = j0 + u * step + sub;
-        int acc = dp4a16(kv[u], qv, 0);
-        for (int o = lpk >> 1; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (part == 0 && j <= see) af[j] = dc_epi(acc, qs, ksg[j]);
-      }
+    const int nchk = hd >> 4;
+    const int4* q4 = (const int4*)q8;
+    for (int j = threadIdx.x; j <= see; j += blockDim.x) {
+      const int4* kr = (const int4*)(kb + (int64_t)j * hd);
+      const float kscale = ksg[j];
+      int acc = 0;
+#pragma unroll 8
+      for (int c = 0; c < nchk; c++) acc = dp4a16(kr[c], q4[c], acc);
+      af[j] = dc_epi(acc, qs, kscale);
     }
   }
   __syncthreads();
