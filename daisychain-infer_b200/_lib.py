@@ -74,7 +74,7 @@ SIGNATURES = [
     ("dc_weight_info", _i, [_p, C.POINTER(_p), C.POINTER(_i), C.POINTER(_p), C.POINTER(_i), C.POINTER(_i)]),
     ("dc_vgemm", _i, [_p, _p, _i, _p, _u, _p]),
     ("dc_ordered_sum_dev", _i, [_p, _p, _i, _i, _p]),
-    ("dc_rmsnorm_dev", _i, [_p, _p, _i, _i, _p, _d, _p]),
+    ("dc_rmsnorm_dev", _i, [_p, _p, _i, _i, _p, _d, _p, _i]),
     ("dc_l2_prefetch", _i, [_p, _p, C.c_size_t]),
     ("dc_kernel_probe", _i, [_p, C.POINTER(_u32)]),
     ("dc_stage_create", _i, [_p, _p, _i, _i, _i, _i, _i, C.POINTER(_p)]),

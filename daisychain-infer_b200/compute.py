@@ -151,9 +151,10 @@ class Compute:
         """out[r] = serial double sum of terms[r] in index order (infer.js:73-76, :100-104)."""
         self._check(self.L.dc_ordered_sum_dev(self.h, _ptr(terms), rows, n, _ptr(out)), "ordered_sum")
 
-    def rmsnorm_dev(self, x, rows, cols, w, eps, y) -> None:
-        """infer.js rmsnorm (:70-80) of rows x cols f32."""
-        self._check(self.L.dc_rmsnorm_dev(self.h, _ptr(x), rows, cols, _ptr(w), float(eps), _ptr(y)), "rmsnorm")
+    def rmsnorm_dev(self, x, rows, cols, w, eps, y, exact_sum: bool = False) -> None:
+        """infer.js rmsnorm (:70-80) of rows x cols f32 (exact_sum: always the serial-order sum)."""
+        self._check(self.L.dc_rmsnorm_dev(self.h, _ptr(x), rows, cols, _ptr(w), float(eps), _ptr(y),
+                                          1 if exact_sum else 0), "rmsnorm")
 
     def kernel_probe(self) -> int:
         """kernelProbe's int32 hash (webgpu.js:1047-1055, before the math fold)."""

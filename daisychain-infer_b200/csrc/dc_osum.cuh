@@ -53,12 +53,13 @@ struct Entry {
   unsigned long long c1, c2;
   int t, emin, emax;
 };
-struct Smem {
-  Entry ent[8][MAXW];
-  Entry whead[8], wtail[8];  // v unused
-  int wn[8];                 // explicit terms of warp w
-  int wbad[8];
-  double wtot[8];
+template <int NW>  // warps of the block
+struct SmemT {
+  Entry ent[NW][MAXW];
+  Entry whead[NW], wtail[NW];  // v unused
+  int wn[NW];                  // explicit terms of warp w
+  int wbad[NW];
+  double wtot[NW];
   double result;
 };
 
@@ -215,15 +216,15 @@ __device__ __forceinline__ bool finish(double& a, const SegFn& st) {
   return true;
 }
 
-// One chunk of at most PER * 256 terms (blockDim.x == 256), continuing the
+// One chunk of at most PER * 32 * NW terms (blockDim.x == 32 * NW), continuing the
 // chain from acc_in (the exact running sum before the chunk).  Lane l of warp
 // w owns terms [(32w + l) * PER, ... + PER); PER is odd, so that consecutive
 // lanes reading shared memory 8*PER bytes apart hit distinct banks.  Two block
 // barriers; the rest is warp-local.  The per-term loops stay rolled: this code
 // runs once per row on one SM, where instruction fetch, not arithmetic, sets
 // the pace of long straight-line code.
-template <int PER>
-__device__ __forceinline__ double osum_chunk(const double* t, int len, double acc_in, Smem& S) {
+template <int PER, int NW>
+__device__ __forceinline__ double osum_chunk(const double* t, int len, double acc_in, SmemT<NW>& S) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int lo = min(len, tid * PER), hi = min(len, lo + PER);
   // 1. the run's approximate sum, warp prefix sums
@@ -245,7 +246,7 @@ __device__ __forceinline__ double osum_chunk(const double* t, int len, double ac
   bool any_bad = false;
   double P = acc_in;
 #pragma unroll 1
-  for (int w = 0; w < 8; w++) {
+  for (int w = 0; w < NW; w++) {
     any_bad |= S.wbad[w] != 0;
     if (w < wid) P += S.wtot[w];
   }
@@ -341,12 +342,12 @@ __device__ __forceinline__ double osum_chunk(const double* t, int len, double ac
   // 3a. the map after each warp's last explicit term runs through the
   //     following warps up to the next explicit term (or the chunk's end):
   //     composed by one lane per warp, in parallel
-  if (wid == 0 && !any_bad && lane < 8) {
+  if (wid == 0 && !any_bad && lane < NW) {
     const int n = S.wn[lane];
     if (n > 0 && n <= MAXW) {
       SegFn m = get(S.wtail[lane]);
 #pragma unroll 1
-      for (int x = lane + 1; x < 8; x++) {
+      for (int x = lane + 1; x < NW; x++) {
         if (S.wn[x] > 0) {
           m = seg_cat(m, get(S.whead[x]));
           break;
@@ -364,11 +365,11 @@ __device__ __forceinline__ double osum_chunk(const double* t, int len, double ac
     bool ok = !any_bad && (len == 0 || S.wn[0] > 0);  // term 0 is explicit
     if (ok) {
 #pragma unroll 1
-      for (int w = 0; w < 8; w++) ok &= S.wn[w] <= MAXW;
+      for (int w = 0; w < NW; w++) ok &= S.wn[w] <= MAXW;
     }
     if (ok) {
 #pragma unroll 1
-      for (int w = 0; w < 8; w++) {
+      for (int w = 0; w < NW; w++) {
         const int n = S.wn[w];
 #pragma unroll 1
         for (int i = 0; i < n; i++) {
@@ -389,13 +390,14 @@ __device__ __forceinline__ double osum_chunk(const double* t, int len, double ac
   return S.result;
 }
 
-// Same value as serial(t, n), computed by the whole block in chunks of
-// 17 * 256 terms.  Every thread must call it; every thread gets the sum.  `t`
-// may be in shared or global memory.  Written for 256-thread blocks; any
-// other block size takes the serial loop.
-__device__ __forceinline__ double ordered_sum(const double* t, int n, Smem& S) {
+// Same value as serial(t, n), computed by the whole block (NW warps) in
+// chunks of 17 * 32 * NW terms.  Every thread must call it; every thread gets
+// the sum.  `t` may be in shared or global memory.  A block of another size
+// than 32 * NW threads takes the serial loop.
+template <int NW>
+__device__ __forceinline__ double ordered_sum(const double* t, int n, SmemT<NW>& S) {
   constexpr int PER = 17;
-  if (blockDim.x != 256) {
+  if (blockDim.x != 32 * NW) {
     if (threadIdx.x == 0) S.result = serial(t, n);
     __syncthreads();
     const double r = S.result;
@@ -404,8 +406,11 @@ __device__ __forceinline__ double ordered_sum(const double* t, int n, Smem& S) {
   }
   double acc = 0.0;
 #pragma unroll 1
-  for (int c0 = 0; c0 < n; c0 += PER * 256) acc = osum_chunk<PER>(t + c0, min(PER * 256, n - c0), acc, S);
+  for (int c0 = 0; c0 < n; c0 += PER * 32 * NW)
+    acc = osum_chunk<PER, NW>(t + c0, min(PER * 32 * NW, n - c0), acc, S);
   return acc;
 }
+using Smem = SmemT<8>;    // 256-thread blocks
+using Smem16 = SmemT<16>; // 512-thread blocks
 
 }  // namespace dco

@@ -147,6 +147,28 @@ __device__ __forceinline__ double quant_scale(float mx) {
   return sc > 1e-8 ? sc : 1e-8;
 }
 
+// 1 / sqrt(s / C + eps) with every step correctly rounded (infer.js:77-78);
+// monotone non-increasing in s.
+__device__ __noinline__ double rms_inv(double s, int C, double eps) {
+  return __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)C), eps)));
+}
+// Block sum of doubles in any order (an approximation: only used to bracket).
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double w = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    if (threadIdx.x == 0) red[0] = w;
+  }
+  __syncthreads();
+  const double r = red[0];
+  __syncthreads();
+  return r;
+}
+
 // RMSNorm of one row fused with quantizeRows of its output.
 // x rows x C f32 -> q rows x ldq int8 (+ s[row]); the f32 norm output is not kept.
 __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __restrict__ x, int C,
@@ -154,10 +176,13 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
                                                                int8_t* __restrict__ q, int ldq,
                                                                float* __restrict__ s, int* status,
                                                                float* __restrict__ yo = nullptr,
-                                                               uint32_t* __restrict__ zrow = nullptr) {
+                                                               uint32_t* __restrict__ zrow = nullptr,
+                                                               int exact_sum = 0) {
   extern __shared__ __align__(16) double sq[];  // C doubles (v*v), then C floats (x, then y)
   float* ys = (float*)(sq + C);
   __shared__ float red[32];
+  __shared__ double redd[32];
+  __shared__ int vote[32];
   __shared__ dco::Smem osm;
   // the GEMV that consumes q may launch now: it streams its weights meanwhile
   asm volatile("griddepcontrol.launch_dependents;");
@@ -189,9 +214,35 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   // warp votes and a plain barrier: a block vote (__syncthreads_or) costs microseconds here
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(status, DC_ST_NONFINITE);
   __syncthreads();
-  // the reference's order: s += v*v for j = 0 .. C-1, each step rounded
-  const double acc = dco::ordered_sum(sq, C, osm);
-  const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(acc, (double)C), eps)));
+  // The reference sums s += v*v for j = 0 .. C-1, each step rounded.  That
+  // serial value is bracketed first: an any-order sum S' is within
+  // 2*gamma_(C-1)*S' of it (both are within gamma_(C-1) of the exact sum of
+  // these non-negative terms), inv = 1/sqrt(s/C + eps) is monotone in s, and
+  // each y_j = f32(x_j*inv*w_j) is monotone in inv.  When every y_j is the same
+  // at both ends of the bracket, it is the serial sum's y_j; otherwise (rare:
+  // some y_j within ~1e-12 of an f32 rounding boundary) the block computes the
+  // serial-order sum itself.
+  double inv;
+  {
+    double part = 0.0;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) part += sq[j];
+    const double sp = block_sum_d(part, redd);
+    const double d = (double)(C + 16) * 4.440892098500626e-16;  // 4 * (C + 4) * 2^-53
+    const double inv_hi = rms_inv(sp * (1.0 - d), C, eps), inv_lo = rms_inv(sp * (1.0 + d), C, eps);
+    bool amb = exact_sum != 0;
+    for (int j = threadIdx.x; j < C && !amb; j += blockDim.x) {
+      const double xw = (double)ys[j], wj = (double)w[j];
+      amb |= __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_lo), wj)) !=
+             __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_hi), wj));
+    }
+    const bool wamb = __any_sync(0xffffffffu, amb);
+    if ((threadIdx.x & 31) == 0) vote[threadIdx.x >> 5] = wamb ? 1 : 0;
+    __syncthreads();
+    bool any = false;
+    for (int wv = 0; wv < (int)(blockDim.x >> 5); wv++) any |= vote[wv] != 0;
+    inv = inv_lo;
+    if (any) inv = rms_inv(dco::ordered_sum(sq, C, osm), C, eps);
+  }
   float mx = 0.0f;
   if (vec) {
 #pragma unroll 2
@@ -239,6 +290,32 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
     for (int j = threadIdx.x; j < ldq; j += blockDim.x)
       qr[j] = j < C ? dc_quant_div((double)ys[j], sc, rsc) : (int8_t)0;
   }
+}
+
+// The softmax denominator z (infer.js:100-104: z += e_j in key order, each
+// add rounded) as far as the probabilities a_j = f32(f32(e_j) / z) can tell:
+// an any-order sum brackets the serial z within 2*gamma_(n-1) (non-negative
+// terms), each a_j is monotone in z, so when every a_j is the same at both
+// ends of the bracket the lower end gives the serial z's a_j; otherwise the
+// block computes the serial-order sum.  `af` holds f32(e_j).
+__device__ __forceinline__ double softmax_z(const double* e, const float* af, int n, dco::Smem& osm, double* redd,
+                                            int* vote) {
+  double part = 0.0;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) part += e[j];
+  const double zp = block_sum_d(part, redd);
+  const double d = (double)(n + 16) * 4.440892098500626e-16;  // 4 * (n + 4) * 2^-53
+  const double zlo = zp * (1.0 - d), zhi = zp * (1.0 + d);
+  const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
+  bool amb = false;
+  for (int j = threadIdx.x; j < n && !amb; j += blockDim.x)
+    amb |= dc_div_to_f32((double)af[j], zlo, rlo) != dc_div_to_f32((double)af[j], zhi, rhi);
+  const bool wamb = __any_sync(0xffffffffu, amb);
+  if ((threadIdx.x & 31) == 0) vote[threadIdx.x >> 5] = wamb ? 1 : 0;
+  __syncthreads();
+  bool any = false;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) any |= vote[w] != 0;
+  __syncthreads();
+  return any ? dco::ordered_sum(e, n, osm) : zlo;
 }
 
 // RoPE on the q and k parts of the fused QKV output row, quantisation of each
@@ -428,6 +505,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* __res
   __shared__ __align__(16) int8_t q8[128];
   __shared__ float red[32];
   __shared__ double redd[32];
+  __shared__ int vote[32];
   __shared__ dco::Smem osm;
   const int hq = blockIdx.x, i = blockIdx.y;
   const int group = nH / nKV, g = hq / group;
@@ -476,8 +554,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* __res
     af[j] = __double2float_rn(e);
   }
   __syncthreads();
-  // 5. z = sum of e_j in key order, with the reference's rounding sequence
-  const double z = dco::ordered_sum(ed, see + 1, osm);
+  // 5. z: the serial key-order sum, as far as the probabilities can tell
+  const double z = softmax_z(ed, af, see + 1, osm, redd, vote);
   // 6. a_j = f32(a_j / z); 7. quantise the probability row over all N columns
   float amx = 0.0f;
   const double rz = __drcp_rn(z);
@@ -643,6 +721,7 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
   __shared__ __align__(16) int8_t q8[256];
   __shared__ float red[32];
   __shared__ double redd[32];
+  __shared__ int vote[32];
   __shared__ int abort_flag;
   __shared__ dco::Smem osm;
   const int hq = blockIdx.x, c0 = blockIdx.y * CH;
@@ -739,8 +818,8 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
       af[j] = __double2float_rn(e);
     }
     __syncthreads();
-    // 5. z = sum of e_j in key order, with the reference's rounding sequence
-    const double z = dco::ordered_sum(xs, N, osm);
+    // 5. z: the serial key-order sum, as far as the probabilities can tell
+    const double z = softmax_z(xs, af, N, osm, redd, vote);
     // 6. a_j = f32(f32(e_j) / z); 7. quantizeRows of the probability row
     const double rz = __drcp_rn(z);
     float amx = 0.0f;
@@ -1671,13 +1750,15 @@ extern "C" int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, in
   return DC_OK;
 }
 
-extern "C" int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y) {
+extern "C" int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y,
+                              int exact_sum) {
   if (!ctx || rows < 0 || cols < 1 || (rows && (!x || !w || !y))) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: bad arguments");
   if ((size_t)cols * 12 > 200 * 1024) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: row of %d does not fit on chip", cols);
   if (!rows) return DC_OK;
   const int smem = 12 * cols;
   if (int rc = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, smem)) return rc;
-  k_rmsnorm_quant<<<rows, NORM_THREADS, smem, ctx->stream>>>(x, cols, w, eps, nullptr, 0, nullptr, ctx->d_status, y);
+  k_rmsnorm_quant<<<rows, NORM_THREADS, smem, ctx->stream>>>(x, cols, w, eps, nullptr, 0, nullptr, ctx->d_status, y,
+                                                           nullptr, exact_sum);
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;

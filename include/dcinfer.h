@@ -160,9 +160,12 @@ int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned fl
  *   and bit-identical to the serial loop for every input.
  * dc_rmsnorm_dev: y = infer.js rmsnorm (:70-80) of each of `rows` rows of
  *   `cols` floats with weight w (cols * 12 bytes must fit on chip: cols <=
- *   17066). */
+ *   17066).  The serial sum of squares is first bracketed (any-order sum and
+ *   its error bound); exact_sum = 1 always computes the serial-order sum
+ *   instead -- both give the same bits. */
 int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double* out);
-int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y);
+int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y,
+                   int exact_sum);
 
 /* Prefetch [p, p + bytes) of device memory into L2 (16-byte aligned range),
  * asynchronously on the context's stream.  No counterpart in the reference:

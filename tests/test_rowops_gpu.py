@@ -96,7 +96,25 @@ def test_rmsnorm_matches_oracle(comp, O, cols):
     want = O.rmsnorm(x, rows, cols, w, 1e-5).reshape(rows, cols)
     xd = torch.tensor(x, device="cuda")
     wd = torch.tensor(w, device="cuda")
+    for exact_sum in (False, True):  # bracketed sum, and the serial-order sum on the device
+        y = torch.empty_like(xd)
+        comp.rmsnorm_dev(xd, rows, cols, wd, 1e-5, y, exact_sum=exact_sum)
+        comp.sync()
+        assert y.cpu().numpy().tobytes() == want.tobytes(), exact_sum
+
+
+def test_rmsnorm_many_rows_matches_oracle(comp, O):
+    """Many rows, so that the bracket of the serial sum is ambiguous for some
+    (an output within ~1e-12 of an f32 rounding boundary) and those rows take
+    the serial-order sum: every row must still equal the oracle's."""
+    import torch
+    rng = np.random.default_rng(11)
+    rows, cols = 4096, 256
+    x = (rng.standard_normal((rows, cols)) * rng.random((rows, 1)) * 10).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    want = O.rmsnorm(x, rows, cols, w, 1e-6).reshape(rows, cols)
+    xd, wd = torch.tensor(x, device="cuda"), torch.tensor(w, device="cuda")
     y = torch.empty_like(xd)
-    comp.rmsnorm_dev(xd, rows, cols, wd, 1e-5, y)
+    comp.rmsnorm_dev(xd, rows, cols, wd, 1e-6, y)
     comp.sync()
     assert y.cpu().numpy().tobytes() == want.tobytes()
