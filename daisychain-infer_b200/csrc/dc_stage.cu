@@ -147,6 +147,12 @@ __device__ __forceinline__ double quant_scale(float mx) {
   return sc > 1e-8 ? sc : 1e-8;
 }
 
+// Dynamic shared memory of k_rmsnorm_quant: squares (double) and the row
+// (float), plus the weight row (float) when that still fits.
+static size_t rms_smem(int C) {
+  return 16 * (size_t)C + 20 * 1024 <= 232448 ? 16 * (size_t)C : 12 * (size_t)C;
+}
+
 // 1 / sqrt(s / C + eps) with every step correctly rounded (infer.js:77-78);
 // monotone non-increasing in s.
 __device__ __noinline__ double rms_inv(double s, int C, double eps) {
@@ -178,8 +184,11 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
                                                                float* __restrict__ yo = nullptr,
                                                                uint32_t* __restrict__ zrow = nullptr,
                                                                int exact_sum = 0) {
-  extern __shared__ __align__(16) double sq[];  // C doubles (v*v), then C floats (x, then y)
+  extern __shared__ __align__(16) double sq[];  // C doubles (v*v), C floats (x, then y), C floats (w)
   float* ys = (float*)(sq + C);
+  // the weight row rides along in shared memory when it fits (16 bytes per column)
+  float* wsm = 16 * (size_t)C + 20 * 1024 <= 232448 ? ys + C : nullptr;
+  const float* wr = wsm ? wsm : w;
   __shared__ float red[32];
   __shared__ double redd[32];
   __shared__ int vote[32];
@@ -196,6 +205,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
 #pragma unroll 4
     for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
       const float4 v = reinterpret_cast<const float4*>(xr)[i];
+      if (wsm) reinterpret_cast<float4*>(wsm)[i] = reinterpret_cast<const float4*>(w)[i];  // in flight with x
       bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
       reinterpret_cast<float4*>(ys)[i] = v;
       sq[4 * i + 0] = __dmul_rn((double)v.x, (double)v.x);  // exact: a float square fits in a double
@@ -206,6 +216,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   } else {
     for (int j = threadIdx.x; j < C; j += blockDim.x) {
       const float v = xr[j];
+      if (wsm) wsm[j] = w[j];
       bad |= !isfinite(v);
       ys[j] = v;
       sq[j] = __dmul_rn((double)v, (double)v);
@@ -231,7 +242,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
     const double inv_hi = rms_inv(sp * (1.0 - d), C, eps), inv_lo = rms_inv(sp * (1.0 + d), C, eps);
     bool amb = exact_sum != 0;
     for (int j = threadIdx.x; j < C && !amb; j += blockDim.x) {
-      const double xw = (double)ys[j], wj = (double)w[j];
+      const double xw = (double)ys[j], wj = (double)wr[j];
       amb |= __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_lo), wj)) !=
              __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_hi), wj));
     }
@@ -247,7 +258,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   if (vec) {
 #pragma unroll 2
     for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
-      const float4 wv = reinterpret_cast<const float4*>(w)[i];
+      const float4 wv = reinterpret_cast<const float4*>(wr)[i];
       float4 y = reinterpret_cast<const float4*>(ys)[i];
       y.x = __double2float_rn(__dmul_rn(__dmul_rn((double)y.x, inv), (double)wv.x));
       y.y = __double2float_rn(__dmul_rn(__dmul_rn((double)y.y, inv), (double)wv.y));
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
     }
   } else {
     for (int j = threadIdx.x; j < C; j += blockDim.x) {
-      float y = __double2float_rn(__dmul_rn(__dmul_rn((double)ys[j], inv), (double)w[j]));
+      float y = __double2float_rn(__dmul_rn(__dmul_rn((double)ys[j], inv), (double)wr[j]));
       ys[j] = y;
       mx = fmaxf(mx, fabsf(y));
     }
@@ -1413,7 +1424,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   const bool split_ctx = S->a8g && S->hd % 32 == 0 && ctx_smem + 1024 <= 232448;
   if (split_ctx)
     if (int rc0 = dc_set_smem(ctx, (const void*)k_attn_ctx, (int)ctx_smem)) return rc0;
-  const size_t nrm_smem = 12 * (size_t)S->C;  // squares (double) + the row (float)
+  const size_t nrm_smem = rms_smem(S->C);
   // always raised: the kernel's static shared memory counts against the 48 KB default too
   if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
   int rc;
@@ -1592,7 +1603,7 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
   dc_stage* H = st[0];
   dc_ctx* ctx = H->ctx;
   cudaStream_t s = ctx->stream;
-  const size_t nrm_smem = 12 * (size_t)H->C;  // squares (double) + the row (float)
+  const size_t nrm_smem = rms_smem(H->C);
   // always raised: the kernel's static shared memory counts against the 48 KB default too
   if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
   k_rmsnorm_quant<<<1, NORM_THREADS, nrm_smem, s>>>(H->xlap, H->C, H->nrmF, H->spec.norm_eps, H->xq, H->ldC, H->rs,
@@ -1704,7 +1715,7 @@ extern "C" int dc_stage_logits(dc_stage* S, const float* x, int T, const int32_t
   for (int r = 0; r < nrows; r++)
     DC_CUDA(ctx, cudaMemcpyAsync(S->lx + (size_t)r * S->C, x + (size_t)rows[r] * S->C, 4 * (size_t)S->C,
                                  cudaMemcpyDeviceToDevice, st));
-  const size_t nrm_smem = 12 * (size_t)S->C;  // squares (double) + the row (float)
+  const size_t nrm_smem = rms_smem(S->C);
   // always raised: the kernel's static shared memory counts against the 48 KB default too
   if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
   k_rmsnorm_quant<<<nrows, NORM_THREADS, nrm_smem, st>>>(S->lx, S->C, S->nrmF, S->spec.norm_eps, S->xq, S->ldC, S->rs,
@@ -1755,7 +1766,7 @@ extern "C" int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, c
   if (!ctx || rows < 0 || cols < 1 || (rows && (!x || !w || !y))) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: bad arguments");
   if ((size_t)cols * 12 > 200 * 1024) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: row of %d does not fit on chip", cols);
   if (!rows) return DC_OK;
-  const int smem = 12 * cols;
+  const int smem = (int)rms_smem(cols);
   if (int rc = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, smem)) return rc;
   k_rmsnorm_quant<<<rows, NORM_THREADS, smem, ctx->stream>>>(x, cols, w, eps, nullptr, 0, nullptr, ctx->d_status, y,
                                                            nullptr, exact_sum);
