@@ -40,6 +40,8 @@
 #include "dc_osum.cuh"
 #include "dc_ptx.cuh"
 
+#include <cooperative_groups.h>
+
 struct dc_mat {
   int k = 0, n = 0, ldk = 0;
   int8_t* qt = nullptr;  // n x ldk, quantised Wᵀ (zero past k)
@@ -896,6 +898,268 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
   }
 }
 
+// The decode attention of k_attention_dec with the head's S = hd / CH CTAs
+// forming a thread-block cluster: CTA r computes the scores, exps and
+// probabilities of key blocks r, r + S, r + 2S, ... only, and the CTAs
+// exchange through distributed shared memory what the softmax needs across
+// blocks (the maximum, the partial sums of e, the probability maximum, and
+// finally the int8 probability rows for the context).  Each CTA then forms the
+// context of its CH channels over all keys.  The numbers are k_attention_dec's.
+// Every CTA takes every cluster barrier on every path.
+__global__ void __launch_bounds__(256) k_attention_dcl(const float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
+                                                       const int8_t* __restrict__ k8, const float* __restrict__ ks,
+                                                       const int8_t* __restrict__ v8t, const float* __restrict__ vs,
+                                                       const int* __restrict__ n0p, int max_pos, int ldp, int CH,
+                                                       double scale, float* __restrict__ out,
+                                                       uint32_t* __restrict__ rowmax, int* __restrict__ done,
+                                                       int8_t* __restrict__ xq, int ldq, float* __restrict__ rsq,
+                                                       int* status) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  extern __shared__ __align__(16) uint8_t sm[];
+  asm volatile("griddepcontrol.launch_dependents;");  // the O projection may start streaming its weights
+  const int ldpv = ldp;
+  int8_t* sK = (int8_t*)sm;                                    // ATTD_NS slots x ATTD_KB x hd
+  int8_t* sV = sK + ATTD_NS * ATTD_KB * hd;                    // CH x ldpv
+  double* xs = (double*)(sV + (size_t)CH * ldpv);              // ldp doubles: s*scale, then e
+  float* af = (float*)(xs + ldp);                              // ldp floats: key scales, then f32(e), then a
+  int8_t* a8 = (int8_t*)(af + ldp);                            // ldp bytes
+  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar;
+  __shared__ __align__(16) int8_t q8[256];
+  __shared__ float red[32];
+  __shared__ double redd[32];
+  __shared__ int vote[32];
+  __shared__ int abort_flag;
+  __shared__ double xd[2];  // published to the cluster: score maximum, sum of e
+  __shared__ float xf;      // probability maximum
+  __shared__ int xi;        // 1: some probability is ambiguous under the bracket of z
+  __shared__ dco::Smem osm;
+  const int S = (int)gridDim.y, r = (int)blockIdx.y;
+  const int hq = blockIdx.x, c0 = r * CH;
+  const int g = hq / (nH / nKV);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = *n0p, N = n0 + 1;
+  const int ldpN = (N + 15) & ~15;
+  const int nb = (N + ATTD_KB - 1) / ATTD_KB;
+  const int nmine = r < nb ? (nb - r + S - 1) / S : 0;  // this CTA's key blocks: r, r + S, ...
+  const int8_t* kg = k8 + (int64_t)g * max_pos * hd;
+  if (tid == 0) {
+    for (int i = 0; i < ATTD_NS; i++) dcp::mbar_init(&full[i], 1);
+    dcp::mbar_init(&vbar, 1);
+    abort_flag = 0;
+    dcp::mbar_fence_init();
+  }
+  __syncthreads();
+  int issued[ATTD_NS];
+  for (int i = 0; i < ATTD_NS; i++) issued[i] = -1;
+  if (warp == 0) {
+    if (lane == 0) dcp::mbar_expect_tx(&vbar, (uint32_t)(CH * ldpN));
+    __syncwarp();
+    for (int c = lane; c < CH; c += 32)
+      dcp::bulk_load(sV + (size_t)c * ldpv, v8t + ((int64_t)g * hd + c0 + c) * ldp, (uint32_t)ldpN, &vbar);
+    if (lane == 0)
+      for (int i = 0; i < ATTD_NS && i < nmine; i++) {
+        issued[i] = i;
+        const int b = r + i * S;
+        const int kn = min(ATTD_KB, N - b * ATTD_KB);
+        const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
+        const uint32_t sbytes = i == 0 ? (uint32_t)(((N + 3) & ~3) * 4) : 0u;  // key scales with the first block
+        dcp::mbar_expect_tx(&full[i], bytes + sbytes);
+        dcp::bulk_load(sK + (size_t)i * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[i]);
+        if (sbytes) dcp::bulk_load(af, ks + (int64_t)g * max_pos, sbytes, &full[i]);
+      }
+  }
+  // 1. the query row, quantised
+  const float* qrow = h + hq * hd;
+  float mx = 0.0f;
+  bool bad = false;
+  for (int c = tid; c < hd; c += 256) {
+    const float v = qrow[c];
+    bad |= !isfinite(v);
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = block_max_f(mx, red);
+  const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
+  const float qs = __double2float_rn(qsc);
+  for (int c = tid; c < hd; c += 256) q8[c] = dc_quant_div((double)qrow[c], qsc, rqsc);
+  __syncthreads();
+  // 2. scores of this CTA's key blocks (one key per thread)
+  const int nchk = hd >> 4;
+  const int rot = lane >> 2;
+  double m = -INFINITY;
+  for (int i = 0; i < nmine; i++) {
+    const int slot = i % ATTD_NS, b = r + i * S;
+    if (!dcp::mbar_wait(&full[slot], (uint32_t)(i / ATTD_NS) & 1u, status)) abort_flag = 1;
+    __syncthreads();
+    if (abort_flag) break;
+    const int kb = b * ATTD_KB, kn = min(ATTD_KB, N - kb);
+    const int k = tid;
+    if (k < kn) {
+      const int8_t* kr = sK + (size_t)slot * ATTD_KB * hd + (size_t)k * hd;
+      int acc = 0;
+#pragma unroll 4
+      for (int c = 0; c < nchk; c++) {
+        const int cc = (c + rot) & (nchk - 1);
+        acc = dp4a16(*(const int4*)(kr + cc * 16), ((const int4*)q8)[cc], acc);
+      }
+      const double x = __dmul_rn((double)dc_epi(acc, qs, af[kb + k]), scale);
+      xs[kb + k] = x;
+      m = fmax(m, x);
+    }
+    __syncthreads();
+    if (tid == 0 && i + ATTD_NS < nmine) {
+      issued[slot] = i + ATTD_NS;
+      const int b2 = r + (i + ATTD_NS) * S;
+      const int kn2 = min(ATTD_KB, N - b2 * ATTD_KB);
+      const uint32_t bytes = (uint32_t)(((kn2 * hd) + 15) & ~15);
+      dcp::mbar_expect_tx(&full[slot], bytes);
+      dcp::bulk_load(sK + (size_t)slot * ATTD_KB * hd, kg + (int64_t)b2 * ATTD_KB * hd, bytes, &full[slot]);
+    }
+  }
+  // 3. the exact maximum over the cluster
+  m = block_max_d(m, redd);
+  if (tid == 0) xd[0] = m;
+  cl.sync();
+  m = -INFINITY;
+  for (int q = 0; q < S; q++) m = fmax(m, *cl.map_shared_rank(&xd[0], q));
+  // 4. e_j of this CTA's keys; the cluster's any-order sum brackets z
+  double part = 0.0;
+  for (int i = 0; i < nmine; i++) {
+    const int j = (r + i * S) * ATTD_KB + tid;
+    if (j < N) {
+      const double e = dcm::fdlibm_exp(__dsub_rn(xs[j], m));
+      xs[j] = e;
+      af[j] = __double2float_rn(e);
+      part += e;
+    }
+  }
+  part = block_sum_d(part, redd);
+  if (tid == 0) xd[1] = part;
+  cl.sync();
+  double zp = 0.0;
+  for (int q = 0; q < S; q++) zp += *cl.map_shared_rank(&xd[1], q);
+  const double d = (double)(N + 16) * 4.440892098500626e-16;  // 4 * (N + 4) * 2^-53
+  const double zlo = zp * (1.0 - d), zhi = zp * (1.0 + d);
+  const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
+  bool amb = false;
+  float amx = 0.0f;
+  for (int i = 0; i < nmine; i++) {
+    const int j = (r + i * S) * ATTD_KB + tid;
+    if (j < N) {
+      const float alo = dc_div_to_f32((double)af[j], zhi, rhi), ahi = dc_div_to_f32((double)af[j], zlo, rlo);
+      amb |= alo != ahi;
+      amx = fmaxf(amx, ahi);
+    }
+  }
+  {
+    const bool wamb = __any_sync(0xffffffffu, amb);
+    if (lane == 0) vote[warp] = wamb ? 1 : 0;
+    amx = block_max_f(amx, red);  // (its barriers also publish the votes)
+    int any = 0;
+    for (int w = 0; w < 8; w++) any |= vote[w];
+    if (tid == 0) {
+      xi = any;
+      xf = amx;
+    }
+  }
+  cl.sync();
+  int any_amb = 0;
+  for (int q = 0; q < S; q++) any_amb |= *cl.map_shared_rank(&xi, q);
+  double z = zlo;
+  if (any_amb) {
+    // rare: the serial key-order z itself.  Every CTA gathers all e_j from
+    // their owners and sums them (the same value in each).
+    for (int j = tid; j < N; j += 256) {
+      const int owner = (j / ATTD_KB) % S;
+      if (owner != r) {
+        xs[j] = *cl.map_shared_rank(&xs[j], owner);
+        af[j] = *cl.map_shared_rank(&af[j], owner);
+      }
+    }
+    __syncthreads();
+    z = dco::ordered_sum(xs, N, osm);
+    const double rz = __drcp_rn(z);
+    float a2 = 0.0f;
+    for (int i = 0; i < nmine; i++) {
+      const int j = (r + i * S) * ATTD_KB + tid;
+      if (j < N) a2 = fmaxf(a2, dc_div_to_f32((double)af[j], z, rz));
+    }
+    a2 = block_max_f(a2, red);
+    cl.sync();  // everyone has read the published values before they change
+    if (tid == 0) xf = a2;
+  }
+  cl.sync();
+  amx = 0.0f;
+  for (int q = 0; q < S; q++) amx = fmaxf(amx, *cl.map_shared_rank(&xf, q));
+  // 6-7. a_j = f32(f32(e_j) / z) of this CTA's keys, quantised with the row's scale
+  const double asc = quant_scale(amx), rasc = __drcp_rn(asc);
+  const float as = __double2float_rn(asc);
+  {
+    const double rz = __drcp_rn(z);
+    for (int i = 0; i < nmine; i++) {
+      const int kb = (r + i * S) * ATTD_KB;
+      const int j = kb + tid;
+      if (j < ldpN) a8[j] = j < N ? dc_quant_div((double)dc_div_to_f32((double)af[j], z, rz), asc, rasc) : (int8_t)0;
+    }
+  }
+  cl.sync();
+  // the other CTAs' probability bytes, 16 at a time
+  for (int q16 = tid; q16 < (ldpN >> 4); q16 += 256) {
+    const int owner = ((q16 << 4) / ATTD_KB) % S;
+    if (owner != r) ((int4*)a8)[q16] = *cl.map_shared_rank(&((int4*)a8)[q16], owner);
+  }
+  __syncthreads();
+  // 8. the context of this CTA's CH channels over all keys
+  const bool vok = dcp::mbar_wait(&vbar, 0, status);
+  if (!vok) abort_flag = 1;
+  __syncthreads();
+  if (!abort_flag) {
+    const int nch = ldpN >> 4;
+    const int4* a4 = (const int4*)a8;
+    for (int cl4 = warp * 4; cl4 < CH; cl4 += 32) {
+      int sacc[4] = {0, 0, 0, 0};
+      for (int q = lane; q < nch; q += 32) {
+        const int4 av = a4[q];
+#pragma unroll
+        for (int u = 0; u < 4; u++) sacc[u] = dp4a16(((const int4*)(sV + (size_t)(cl4 + u) * ldpv))[q], av, sacc[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        for (int o = 16; o; o >>= 1) sacc[u] += __shfl_xor_sync(0xffffffffu, sacc[u], o);
+      if (lane < 4) {
+        const int c = c0 + cl4 + lane;
+        const int acc = lane == 0 ? sacc[0] : lane == 1 ? sacc[1] : lane == 2 ? sacc[2] : sacc[3];
+        const float o = dc_epi(acc, as, vs[g * hd + c]);
+        out[hq * hd + c] = o;
+        bad |= !isfinite(o);
+        atomicMax(rowmax, __float_as_uint(fabsf(o)));
+      }
+    }
+  }
+  if (abort_flag && tid == 0) {
+    dcp::mbar_wait(&vbar, 0, status);
+    for (int sl = 0; sl < ATTD_NS; sl++)
+      if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] / ATTD_NS) & 1u, status);
+  }
+  if (bad) atomicOr(status, DC_ST_NONFINITE);
+  cl.sync();  // no CTA leaves while another may still read its shared memory
+  __shared__ int is_last;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(done, 1) == (int)(gridDim.x * gridDim.y) - 1;
+  __syncthreads();
+  if (is_last) {
+    __threadfence();
+    const double sc = quant_scale(__uint_as_float(__ldcg(rowmax))), rsc = __drcp_rn(sc);
+    const int qDim = nH * hd;
+    if (tid == 0) {
+      rsq[0] = __double2float_rn(sc);
+      *done = 0;
+    }
+    for (int j = tid; j < ldq; j += 256) xq[j] = j < qDim ? dc_quant_div((double)__ldcg(out + j), sc, rsc) : (int8_t)0;
+  }
+}
+
 // SwiGLU, element-parallel over grid (ceil(I/256), rows): hid = f32(silu(g)*u)
 // with silu(v) = v / (1 + exp(-v)) in double, written over g in place, and
 // |hid| folded into the row maximum (rowmax must start at 0).  The row's
@@ -1415,8 +1679,10 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
         dec_smem = need;
       }
     }
-    if (dec_ch)
+    if (dec_ch) {
       if (int rc0 = dc_set_smem(ctx, (const void*)k_attention_dec, (int)dec_smem)) return rc0;
+      if (int rc0 = dc_set_smem(ctx, (const void*)k_attention_dcl, (int)dec_smem)) return rc0;
+    }
   }
   // chunk rows (T <= 16): probabilities per (head, row), then the context per
   // (head, 32 channels) from shared-memory copies of the value and probability rows
@@ -1454,7 +1720,26 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                                                                         S->kvDim, S->hd, S->ldp);
     }
     dc_count_launch();
-    if (T == 1 && use_kv && dec_ch) {
+    if (T == 1 && use_kv && dec_ch && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8) {
+      // the channel-group CTAs of a head as one cluster: the key work is split among them
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(S->nH, S->hd / dec_ch);
+      cfg.blockDim = dim3(256);
+      cfg.dynamicSmemBytes = dec_smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = S->hd / dec_ch;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_attention_dcl, (const float*)S->hbuf, S->nqkv, S->nH, S->nKV, S->hd,
+                                      (const int8_t*)kv.k8, (const float*)kv.ks, (const int8_t*)kv.v8t,
+                                      (const float*)kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale, S->ctxo,
+                                      S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status));
+      dc_count_launch();
+    } else if (T == 1 && use_kv && dec_ch) {
       k_attention_dec<<<dim3(S->nH, S->hd / dec_ch), 256, dec_smem, st>>>(
           S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale,
           S->ctxo, S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status);
