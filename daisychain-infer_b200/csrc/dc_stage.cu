@@ -342,7 +342,8 @@ __global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int n
                                                     const int* __restrict__ n0p, int max_pos,
                                                     int8_t* __restrict__ k8, float* __restrict__ ks,
                                                     float* __restrict__ vcache, uint32_t* __restrict__ vmax,
-                                                    float* __restrict__ vs, int* __restrict__ vchg, int* status) {
+                                                    float* __restrict__ vs, int* __restrict__ vchg,
+                                                    int8_t* __restrict__ v8t, int ldp, int* status) {
   __shared__ float kr[128];
   __shared__ float red[32];
   const int n0 = *n0p;  // cached tokens before this chunk = its first position
@@ -353,8 +354,9 @@ __global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int n
   bool bad = false;
   if (hh >= nH + nKV) {
     // values, 64 channels per block: copy and fold into the running channel
-    // maximum; with one row (vs != null) also the channel scales and their
-    // change flags, which otherwise k_vscale computes once every row is in
+    // maximum; with one row (vs != null) also the channel scales, their change
+    // flags and the row's int8 values, which otherwise k_vscale and k_vquant*
+    // compute once every row is in
     const int c = (hh - nH - nKV) * 64 + threadIdx.x;
     if (c < kvDim) {
       const float v = row[qDim + kvDim + c];
@@ -366,6 +368,9 @@ __global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int n
         const float ns = __double2float_rn(quant_scale(__uint_as_float(m)));
         vchg[c] = n0 == 0 || ns != vs[c];
         vs[c] = ns;
+        // the new row's int8 value (channel-major); older rows move only when
+        // the channel's scale did (k_vquant_dev)
+        v8t[(int64_t)c * ldp + n0] = dc_clamp8(dc_js_round(dc_ddiv_slow((double)v, (double)ns)));
       } else {
         atomicMax(vmax + c, __float_as_uint(fabsf(v)));
       }
@@ -450,40 +455,43 @@ __global__ void __launch_bounds__(256) k_vquant(const float* __restrict__ vcache
   }
 }
 
-// The tiled quantisation for a decode lap, reading the cache length from
-// device memory: grid (ceil(max_pos/64), ceil(kvDim/32)) tiles of 64 rows x 32
-// channels; a tile with no new row and no channel whose scale moved exits at
-// once, the others quantise and transpose like k_vquant.
+// The tiled quantisation for short chunks and decode steps, reading the cache
+// length from device memory: grid (ceil(max_pos/128), ceil(kvDim/32)) tiles of
+// 128 rows x 32 channels.  A tile with no channel whose scale moved and no new
+// row to write exits at once (for one-row steps, fresh_done = 1, the append
+// already wrote the new row); the others quantise and transpose like k_vquant.
 __global__ void __launch_bounds__(256) k_vquant_dev(const float* __restrict__ vcache, const float* __restrict__ vs,
                                                     const int* __restrict__ vchg, int8_t* __restrict__ v8t, int T,
-                                                    const int* __restrict__ n0p, int kvDim, int hd, int ldp) {
-  __shared__ int8_t tile[32][65];
+                                                    const int* __restrict__ n0p, int kvDim, int hd, int ldp,
+                                                    int fresh_done) {
+  __shared__ int8_t tile[32][129];
   const int n0 = *n0p, N = n0 + T;
-  const int cb = blockIdx.y * 32, jb = blockIdx.x * 64;
+  const int cb = blockIdx.y * 32, jb = blockIdx.x * 128;
   if (jb >= N) return;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = cb + tx;
   const bool cval = c < kvDim;
   const bool chg = cval && vchg[c] != 0;
-  const bool fresh_rows = jb + 64 > n0;  // the tile holds rows >= n0
+  // rows >= n0 still to write in this tile (unless the one-row append wrote them)
+  const bool fresh_rows = !fresh_done && jb + 128 > n0;
   // every warp holds the same 32 channels, so this warp vote is block-uniform
   if (!fresh_rows && !__any_sync(0xffffffffu, chg)) return;
   const double sc = cval ? (double)vs[c] : 1.0;
-  for (int r = ty; r < 64; r += 8) {
+#pragma unroll
+  for (int r = ty; r < 128; r += 8) {  // 16 rows per thread, loads in flight together
     const int j = jb + r;
     int8_t v = 0;
-    if (cval && j < N && (j >= n0 || chg))
+    if (cval && j < N && (chg || (!fresh_done && j >= n0)))
       v = dc_clamp8(dc_js_round(__ddiv_rn((double)vcache[(int64_t)j * kvDim + c], sc)));
     tile[tx][r] = v;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < 32 * 64; idx += blockDim.x) {
-    const int cl = idx >> 6, r = idx & 63;
+  for (int idx = threadIdx.x; idx < 32 * 128; idx += blockDim.x) {
+    const int cl = idx >> 7, r = idx & 127;
     const int cc = cb + cl, j = jb + r;
     if (cc >= kvDim || j >= N) continue;
-    if (j < n0 && !vchg[cc]) continue;
-    const int g = cc / hd, ch = cc - g * hd;
-    v8t[((int64_t)g * hd + ch) * ldp + j] = tile[cl][r];
+    if (!vchg[cc] && (fresh_done || j < n0)) continue;
+    v8t[(int64_t)cc * ldp + j] = tile[cl][r];
   }
 }
 
@@ -1705,16 +1713,15 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     const int vblocks = (S->kvDim + 63) / 64;
     k_rope_append<<<dim3(T, S->nH + S->nKV + vblocks), 64, 0, st>>>(
         S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
-        kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, ctx->d_status);
+        kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status);
     dc_count_launch();
     if (T > 1) {
       k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0p);
       dc_count_launch();
     }
     if (T <= 8) {
-      k_vquant_dev<<<dim3((S->max_pos + 63) / 64, (S->kvDim + 31) / 32), 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8t,
-                                                                                       T, n0p, S->kvDim, S->hd,
-                                                                                       S->ldp);
+      k_vquant_dev<<<dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), 256, 0, st>>>(
+          kv.v, kv.vs, kv.vchg, kv.v8t, T, n0p, S->kvDim, S->hd, S->ldp, T == 1 ? 1 : 0);
     } else {
       k_vquant<<<dim3((N + 63) / 64, (S->kvDim + 31) / 32), 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8t, N, n0,
                                                                         S->kvDim, S->hd, S->ldp);
