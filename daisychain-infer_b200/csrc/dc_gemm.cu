@@ -39,11 +39,13 @@ __global__ void k_lut_gemm(const int8_t* __restrict__ X, const int8_t* __restric
                relu);
 }
 
-__device__ __forceinline__ int4 ld_stream(const int4* p) {
+// A weight load: read once, so it bypasses L1 and is first out of L2 (`pol`
+// from dcp::l2_evict_first()).
+__device__ __forceinline__ int4 ld_stream(const int4* p, uint64_t pol) {
   int4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.s32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+               : "l"(p), "l"(pol));
   return v;
 }
 
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(256, 3) k_gemv(const int8_t* __restrict__ X, i
   const int per = (nch + G - 1) / G;
   const int c_lo = kp * per, c_hi = min(nch, c_lo + per);
   const int8_t* Wb = Wt + (int64_t)bz * n * ldw;
+  const uint64_t pol = dcp::l2_evict_first();
   for (int jb = blockIdx.x * SLOTS; jb < n; jb += gridDim.x * SLOTS) {
     const int j = jb + slot;
     int acc[MR];
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(256, 3) k_gemv(const int8_t* __restrict__ X, i
       for (int c = c_lo + lane; c < c_hi; c += 256) {
         int4 w[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) w[u] = (c + 32 * u < c_hi) ? ld_stream(wrow + c + 32 * u) : make_int4(0, 0, 0, 0);
+        for (int u = 0; u < 8; u++) w[u] = (c + 32 * u < c_hi) ? ld_stream(wrow + c + 32 * u, pol) : make_int4(0, 0, 0, 0);
 #pragma unroll
         for (int u = 0; u < 8; u++) {
           if (c + 32 * u < c_hi) {
@@ -155,15 +158,21 @@ __global__ void k_l2_prefetch(const int8_t* __restrict__ p, size_t bytes) {
 // instruction, and 4-warp CTAs at 4 per SM keep ~128 KB of loads in flight on
 // each SM.  Grid-stride over row pairs; the epilogue is dc_store_out.
 constexpr int GV_SEG = 8;
-__global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* __restrict__ X, const int8_t* __restrict__ Wt,
-                                                     int ldw, const float* __restrict__ rs,
+// X and rs are written by the kernel before this one on the stream: they carry
+// no __restrict__, so that no load of them is moved above griddepcontrol.wait.
+__global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8_t* __restrict__ Wt,
+                                                     int ldw, const float* rs,
                                                      const float* __restrict__ cs, int k, int n, unsigned flags,
                                                      const int8_t* __restrict__ requant,
                                                      const int8_t* __restrict__ relu, void* out) {
+  // the next kernel (launched as a programmatic dependent) may be scheduled
+  // now; it waits for this grid's completion before reading its output
+  asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * 4 + (threadIdx.x >> 5), nw = gridDim.x * 4;
   const int nch = (k + 15) >> 4;
   const int4* X4 = (const int4*)X;
+  const uint64_t pol = dcp::l2_evict_first();
   bool waited = false;
   for (int j0 = gw * 2; j0 < n; j0 += nw * 2) {
     const int j1 = min(j0 + 1, n - 1);
@@ -177,8 +186,8 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* __restrict__ 
 #pragma unroll
       for (int u = 0; u < GV_SEG; u++) {
         const int c = c0 + u * 32 + lane;
-        wa[u] = c < nch ? ld_stream(w0 + c) : make_int4(0, 0, 0, 0);
-        wb[u] = c < nch ? ld_stream(w1 + c) : make_int4(0, 0, 0, 0);
+        wa[u] = c < nch ? ld_stream(w0 + c, pol) : make_int4(0, 0, 0, 0);
+        wb[u] = c < nch ? ld_stream(w1 + c, pol) : make_int4(0, 0, 0, 0);
       }
       if (!waited) {
         // launched as a programmatic dependent: the weights (constant) are
@@ -264,6 +273,7 @@ __global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* __restrict__
     if (lane == 0) {
       int issued = 0;
       const int8_t* Wb = Wt + ((int64_t)bz * n + rb) * ldw;
+      const uint64_t pol = dcp::l2_evict_first();
       for (int it = 0; it < nst; it++) {
         const int s = it % stages;
         if (it >= stages && !dcp::mbar_wait(&empty[s], (uint32_t)((it / stages) - 1) & 1u, status)) {
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* __restrict__
         const int rows_this = min(R, nrows - it * R);
         const uint32_t bytes = (uint32_t)rows_this * (uint32_t)ldw;
         dcp::mbar_expect_tx(&full[s], bytes);
-        dcp::bulk_load(sW + (size_t)s * stage_bytes, Wb + (int64_t)it * R * ldw, bytes, &full[s]);
+        dcp::bulk_load_hint(sW + (size_t)s * stage_bytes, Wb + (int64_t)it * R * ldw, bytes, &full[s], pol);
         issued++;
       }
       // let every issued copy land before this CTA's shared memory can go away
@@ -460,31 +470,36 @@ int launch_gemv_bulk(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, i
   return DC_OK;
 }
 
+// k_gemv_row on one activation row (16-byte aligned operands), launched as a
+// programmatic dependent: the CTAs may start, and issue their weight loads,
+// while the previous kernel on the stream finishes.
+static int launch_gemv_row(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wt, int ldw, const float* rs,
+                           const float* cs, int k, int n, unsigned flags, void* out, cudaStream_t st) {
+  if (int rc = dc_set_smem(ctx, (const void*)k_gemv_row, 0)) return rc;
+  const int pairs = (n + 1) / 2;
+  const int blocks = std::max(1, std::min((pairs + 3) / 4, ctx->sm_count * 4));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemv_row, Xq, Wt, ldw, rs, cs, k, n, flags, (const int8_t*)ctx->d_requant,
+                                  (const int8_t*)ctx->d_relu, out));
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
 template <int MR>
 int launch_gemv(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
                 int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st) {
-  if (MR == 1 && m == 1 && batch == 1 && !(((uintptr_t)Wt | (uintptr_t)Xq) & 15) && !(ldw & 15)) {
-    if (int rc = dc_set_smem(ctx, (const void*)k_gemv_row, 0)) return rc;
-    const int pairs = (n + 1) / 2;
-    const int blocks = std::max(1, std::min((pairs + 3) / 4, ctx->sm_count * 4));
-    // programmatic dependent launch: the CTAs may start (and issue their
-    // weight loads) while the previous kernel on the stream finishes
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemv_row, Xq, Wt, ldw, rs, cs, k, n, flags, (const int8_t*)ctx->d_requant,
-                                    (const int8_t*)ctx->d_relu, out));
-    dc_count_launch();
-    DC_CUDA(ctx, cudaGetLastError());
-    return DC_OK;
-  }
+  if (MR == 1 && m == 1 && batch == 1 && !(((uintptr_t)Wt | (uintptr_t)Xq) & 15) && !(ldw & 15))
+    return launch_gemv_row(ctx, Xq, Wt, ldw, rs, cs, k, n, flags, out, st);
   {
     const int rc = launch_gemv_bulk<MR>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
     if (rc != DC_E_INVAL) return rc;

@@ -86,6 +86,22 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// tma_load_2d with an L2 cache policy (evict-first for tiles no other CTA reads).
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_w(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                           bool once, uint64_t policy) {
+  if (once)
+    tma_load_2d_hint(dst, map, x, y, bar, policy);
+  else
+    tma_load_2d(dst, map, x, y, bar);
+}
 // UMMA shared-memory descriptor: K-major, 128B swizzle, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t umma_desc(const void* p) {
   uint64_t d = (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu);
@@ -201,10 +217,14 @@ __global__ void __launch_bounds__(128, 1)
     // kernel) after it.
     int issued = 0;
     bool ok = true;
+    // with a single row tile every weight tile is read by exactly one CTA
+    const bool once = gridDim.y == 1;
+    uint64_t pol = 0;
+    if (once) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
     const int pre = min(nkb, C::STAGES);
     for (int it = 0; it < pre; it++) {
       mbar_expect_tx(&full[it], C::STAGE_BYTES);
-      tma_load_2d(sA + it * C::A_BYTES, &tmW, (kb0 + it) * TILE_K, bz * a.n + j0, &full[it]);
+      tma_load_w(sA + it * C::A_BYTES, &tmW, (kb0 + it) * TILE_K, bz * a.n + j0, &full[it], once, pol);
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int it = 0; it < pre; it++)
@@ -217,7 +237,7 @@ __global__ void __launch_bounds__(128, 1)
       if (!ok) break;
       mbar_expect_tx(&full[s], C::STAGE_BYTES);
       const int kx = (kb0 + it) * TILE_K;
-      tma_load_2d(sA + s * C::A_BYTES, &tmW, kx, bz * a.n + j0, &full[s]);
+      tma_load_w(sA + s * C::A_BYTES, &tmW, kx, bz * a.n + j0, &full[s], once, pol);
       tma_load_2d(sB + s * C::B_BYTES, &tmX, kx, bz * a.m + i0, &full[s]);
       issued++;
     }

@@ -149,6 +149,13 @@ __device__ __forceinline__ double quant_scale(float mx) {
   return sc > 1e-8 ? sc : 1e-8;
 }
 
+// The serial-order sum of dc_osum.cuh, out of line: only ambiguous rows reach
+// it, so its code stays out of the callers' instruction stream.  Every thread
+// of the block calls it.
+__device__ __noinline__ double ordered_sum_cold(const double* t, int n, dco::Smem& osm) {
+  return dco::ordered_sum(t, n, osm);
+}
+
 // Dynamic shared memory of k_rmsnorm_quant: squares (double) and the row
 // (float), plus the weight row (float) when that still fits.
 static size_t rms_smem(int C) {
@@ -179,12 +186,12 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
 
 // RMSNorm of one row fused with quantizeRows of its output.
 // x rows x C f32 -> q rows x ldq int8 (+ s[row]); the f32 norm output is not kept.
-__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __restrict__ x, int C,
-                                                               const float* __restrict__ w, double eps,
-                                                               int8_t* __restrict__ q, int ldq,
-                                                               float* __restrict__ s, int* status,
-                                                               float* __restrict__ yo = nullptr,
-                                                               uint32_t* __restrict__ zrow = nullptr,
+__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, int C,
+                                                               const float* w, double eps,
+                                                               int8_t* q, int ldq,
+                                                               float* s, int* status,
+                                                               float* yo = nullptr,
+                                                               uint32_t* zrow = nullptr,
                                                                int exact_sum = 0) {
   extern __shared__ __align__(16) double sq[];  // C doubles (v*v), C floats (x, then y), C floats (w)
   float* ys = (float*)(sq + C);
@@ -199,15 +206,24 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
   asm volatile("griddepcontrol.launch_dependents;");
   const int row = blockIdx.x;
   const float* xr = x + (int64_t)row * C;
-  if (zrow && threadIdx.x == 0) zrow[row] = 0;  // the row maximum the next row quantisation collects
   // float4 access when the row allows it (all loads of a thread in flight at once)
   const bool vec = (C & 3) == 0 && ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  // The weight row is constant: its copy into shared memory (asynchronous,
+  // awaited after the input row's loads) starts before the grid-dependency
+  // wait.  Everything else this kernel reads or writes comes after it.
+  if (vec && wsm) {
+    for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dcp::smem_u32(wsm + 4 * i)), "l"(w + 4 * i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (zrow && threadIdx.x == 0) zrow[row] = 0;  // the row maximum the next row quantisation collects
   bool bad = false;
   if (vec) {
 #pragma unroll 4
     for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
       const float4 v = reinterpret_cast<const float4*>(xr)[i];
-      if (wsm) reinterpret_cast<float4*>(wsm)[i] = reinterpret_cast<const float4*>(w)[i];  // in flight with x
       bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
       reinterpret_cast<float4*>(ys)[i] = v;
       sq[4 * i + 0] = __dmul_rn((double)v.x, (double)v.x);  // exact: a float square fits in a double
@@ -215,6 +231,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
       sq[4 * i + 2] = __dmul_rn((double)v.z, (double)v.z);
       sq[4 * i + 3] = __dmul_rn((double)v.w, (double)v.w);
     }
+    if (wsm) asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's copies (the barrier below publishes them)
   } else {
     for (int j = threadIdx.x; j < C; j += blockDim.x) {
       const float v = xr[j];
@@ -254,7 +271,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* __r
     bool any = false;
     for (int wv = 0; wv < (int)(blockDim.x >> 5); wv++) any |= vote[wv] != 0;
     inv = inv_lo;
-    if (any) inv = rms_inv(dco::ordered_sum(sq, C, osm), C, eps);
+    if (any) inv = rms_inv(ordered_sum_cold(sq, C, osm), C, eps);
   }
   float mx = 0.0f;
   if (vec) {
@@ -328,7 +345,7 @@ __device__ __forceinline__ double softmax_z(const double* e, const float* af, in
   bool any = false;
   for (int w = 0; w < (int)(blockDim.x >> 5); w++) any |= vote[w] != 0;
   __syncthreads();
-  return any ? dco::ordered_sum(e, n, osm) : zlo;
+  return any ? ordered_sum_cold(e, n, osm) : zlo;
 }
 
 // RoPE on the q and k parts of the fused QKV output row, quantisation of each
@@ -337,13 +354,15 @@ __device__ __forceinline__ double softmax_z(const double* e, const float* af, in
 // grid (T, nH + nKV + 1), block 64: block y < nH rotates query head y in place;
 // nH <= y < nH + nKV rotates key head y - nH, quantises it and appends it;
 // the last block appends the value row and folds |v| into the channel maxima.
-__global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
-                                                    const float* __restrict__ rc, const float* __restrict__ rsn,
-                                                    const int* __restrict__ n0p, int max_pos,
-                                                    int8_t* __restrict__ k8, float* __restrict__ ks,
-                                                    float* __restrict__ vcache, uint32_t* __restrict__ vmax,
-                                                    float* __restrict__ vs, int* __restrict__ vchg,
-                                                    int8_t* __restrict__ v8t, int ldp, int* status) {
+__global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, int nKV, int hd,
+                                                    const float* rc, const float* rsn,
+                                                    const int* n0p, int max_pos,
+                                                    int8_t* k8, float* ks,
+                                                    float* vcache, uint32_t* vmax,
+                                                    float* vs, int* vchg,
+                                                    int8_t* v8t, int ldp, int* status) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   __shared__ float kr[128];
   __shared__ float red[32];
   const int n0 = *n0p;  // cached tokens before this chunk = its first position
@@ -407,14 +426,16 @@ __global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ h, int n
   const int g = hh - nH;
   const int64_t slot = (int64_t)g * max_pos + n0 + t;
   if (threadIdx.x == 0) ks[slot] = sc;
-  for (int c = threadIdx.x; c < hd; c += blockDim.x)
-    k8[slot * hd + c] = dc_clamp8(dc_js_round(__ddiv_rn((double)kr[c], (double)sc)));
+  const double rsc = __drcp_rn((double)sc);
+  for (int c = threadIdx.x; c < hd; c += blockDim.x) k8[slot * hd + c] = dc_quant_div((double)kr[c], (double)sc, rsc);
   if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
 
 // Channel scales of V over all cached tokens; flags the channels whose scale moved.
-__global__ void k_vscale(const uint32_t* __restrict__ vmax, float* __restrict__ vs, int* __restrict__ vchg,
-                         int kvDim, const int* __restrict__ n0p) {
+__global__ void k_vscale(const uint32_t* vmax, float* vs, int* vchg,
+                         int kvDim, const int* n0p) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= kvDim) return;
   const int fresh = *n0p == 0;
@@ -427,21 +448,22 @@ __global__ void k_vscale(const uint32_t* __restrict__ vmax, float* __restrict__ 
 // so a context dot product streams contiguous bytes): rows >= n0 always, older
 // rows only in channels whose scale moved.  grid (ceil(N/64), ceil(kvDim/32)),
 // block 256 (32 channels x 8 rows); the tile is transposed through shared memory.
-__global__ void __launch_bounds__(256) k_vquant(const float* __restrict__ vcache, const float* __restrict__ vs,
-                                                const int* __restrict__ vchg, int8_t* __restrict__ v8t, int N, int n0,
+__global__ void __launch_bounds__(256) k_vquant(const float* vcache, const float* vs,
+                                                const int* vchg, int8_t* v8t, int N, int n0,
                                                 int kvDim, int hd, int ldp) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   __shared__ int8_t tile[32][65];
   const int cb = blockIdx.y * 32, jb = blockIdx.x * 64;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = cb + tx;
   const bool cval = c < kvDim;
   const bool chg = cval && vchg[c] != 0;
-  const double sc = cval ? (double)vs[c] : 1.0;
+  const double sc = cval ? (double)vs[c] : 1.0, rsc = __drcp_rn(sc);
   for (int r = ty; r < 64; r += 8) {
     const int j = jb + r;
     int8_t v = 0;
-    if (cval && j < N && (j >= n0 || chg))
-      v = dc_clamp8(dc_js_round(__ddiv_rn((double)vcache[(int64_t)j * kvDim + c], sc)));
+    if (cval && j < N && (j >= n0 || chg)) v = dc_quant_div((double)vcache[(int64_t)j * kvDim + c], sc, rsc);
     tile[tx][r] = v;
   }
   __syncthreads();
@@ -460,10 +482,12 @@ __global__ void __launch_bounds__(256) k_vquant(const float* __restrict__ vcache
 // 128 rows x 32 channels.  A tile with no channel whose scale moved and no new
 // row to write exits at once (for one-row steps, fresh_done = 1, the append
 // already wrote the new row); the others quantise and transpose like k_vquant.
-__global__ void __launch_bounds__(256) k_vquant_dev(const float* __restrict__ vcache, const float* __restrict__ vs,
-                                                    const int* __restrict__ vchg, int8_t* __restrict__ v8t, int T,
-                                                    const int* __restrict__ n0p, int kvDim, int hd, int ldp,
+__global__ void __launch_bounds__(256) k_vquant_dev(const float* vcache, const float* vs,
+                                                    const int* vchg, int8_t* v8t, int T,
+                                                    const int* n0p, int kvDim, int hd, int ldp,
                                                     int fresh_done) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   __shared__ int8_t tile[32][129];
   const int n0 = *n0p, N = n0 + T;
   const int cb = blockIdx.y * 32, jb = blockIdx.x * 128;
@@ -476,13 +500,13 @@ __global__ void __launch_bounds__(256) k_vquant_dev(const float* __restrict__ vc
   const bool fresh_rows = !fresh_done && jb + 128 > n0;
   // every warp holds the same 32 channels, so this warp vote is block-uniform
   if (!fresh_rows && !__any_sync(0xffffffffu, chg)) return;
-  const double sc = cval ? (double)vs[c] : 1.0;
+  const double sc = cval ? (double)vs[c] : 1.0, rsc = __drcp_rn(sc);
 #pragma unroll
   for (int r = ty; r < 128; r += 8) {  // 16 rows per thread, loads in flight together
     const int j = jb + r;
     int8_t v = 0;
     if (cval && j < N && (chg || (!fresh_done && j >= n0)))
-      v = dc_clamp8(dc_js_round(__ddiv_rn((double)vcache[(int64_t)j * kvDim + c], sc)));
+      v = dc_quant_div((double)vcache[(int64_t)j * kvDim + c], sc, rsc);
     tile[tx][r] = v;
   }
   __syncthreads();
@@ -509,16 +533,18 @@ __device__ __forceinline__ int dp4a16(const int4 a, const int4 b, int acc) {
 // Scores: hd/16 lanes per key, 16-byte loads of the int8 key row, shuffle sum.
 // Context: one warp per output channel, lanes stream 16-byte chunks of that
 // channel's int8 values (channel-major cache) against the int8 probabilities.
-__global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* __restrict__ h, int nqkv, int nH, int nKV,
-                                                           int hd, const int8_t* __restrict__ k8,
-                                                           const float* __restrict__ ks,
-                                                           const int8_t* __restrict__ v8t,
-                                                           const float* __restrict__ vs, int T,
-                                                           const int* __restrict__ n0p, int max_pos,
-                                                           int ldp, double scale, float* __restrict__ out,
-                                                           uint32_t* __restrict__ rowmax, int qDim,
-                                                           int* status, int8_t* __restrict__ a8g = nullptr,
-                                                           float* __restrict__ asg = nullptr) {
+__global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* h, int nqkv, int nH, int nKV,
+                                                           int hd, const int8_t* k8,
+                                                           const float* ks,
+                                                           const int8_t* v8t,
+                                                           const float* vs, int T,
+                                                           const int* n0p, int max_pos,
+                                                           int ldp, double scale, float* out,
+                                                           uint32_t* rowmax, int qDim,
+                                                           int* status, int8_t* a8g = nullptr,
+                                                           float* asg = nullptr) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   extern __shared__ __align__(16) uint8_t sm[];
   double* ed = (double*)sm;                                 // max_pos doubles: e_j
   float* af = (float*)(ed + max_pos);                       // max_pos floats: scores, then a_j
@@ -545,7 +571,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* __res
   mx = block_max_f(mx, red);
   const double qsc = quant_scale(mx);
   const float qs = __double2float_rn(qsc);
-  for (int c = threadIdx.x; c < hd; c += blockDim.x) q8[c] = dc_clamp8(dc_js_round(__ddiv_rn((double)qrow[c], qsc)));
+  const double rqsc = __drcp_rn(qsc);
+  for (int c = threadIdx.x; c < hd; c += blockDim.x) q8[c] = dc_quant_div((double)qrow[c], qsc, rqsc);
   __syncthreads();
   // 2. scores for keys 0..see: one key per thread (its 128-byte row in one
   //    line), int32 dot over hd, verified epilogue
@@ -652,11 +679,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* __res
 // epilogue with the row's probability scale and the channel's value scale.
 // The 32 value rows and the T probability rows land in shared memory by 1-D
 // bulk copies.  Dynamic shared memory: (32 + T) * ldp.
-__global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* __restrict__ a8g, const float* __restrict__ asg,
-                                                  const int8_t* __restrict__ v8t, const float* __restrict__ vs,
-                                                  int nH, int nKV, int hd, int T, const int* __restrict__ n0p,
-                                                  int ldp, float* __restrict__ out, int qDim,
-                                                  uint32_t* __restrict__ rowmax, int* status) {
+__global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* a8g, const float* asg,
+                                                  const int8_t* v8t, const float* vs,
+                                                  int nH, int nKV, int hd, int T, const int* n0p,
+                                                  int ldp, float* out, int qDim,
+                                                  uint32_t* rowmax, int* status) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   extern __shared__ __align__(16) uint8_t sm[];
   int8_t* sV = (int8_t*)sm;              // 32 x ldp
   int8_t* sA = sV + (size_t)32 * ldp;     // T x ldp
@@ -722,16 +751,17 @@ __global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* __restrict__ a8g
 // hd is 32, 64, 128 or 256; CH divides hd.
 constexpr int ATTD_KB = 256;  // keys per ring slot
 constexpr int ATTD_NS = 3;    // ring slots (two blocks in flight while one is consumed)
-__global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
-                                                       const int8_t* __restrict__ k8, const float* __restrict__ ks,
-                                                       const int8_t* __restrict__ v8t, const float* __restrict__ vs,
-                                                       const int* __restrict__ n0p, int max_pos, int ldp, int CH,
-                                                       double scale, float* __restrict__ out,
-                                                       uint32_t* __restrict__ rowmax, int* __restrict__ done,
-                                                       int8_t* __restrict__ xq, int ldq, float* __restrict__ rsq,
+__global__ void __launch_bounds__(256) k_attention_dec(const float* h, int nqkv, int nH, int nKV, int hd,
+                                                       const int8_t* k8, const float* ks,
+                                                       const int8_t* v8t, const float* vs,
+                                                       const int* n0p, int max_pos, int ldp, int CH,
+                                                       double scale, float* out,
+                                                       uint32_t* rowmax, int* done,
+                                                       int8_t* xq, int ldq, float* rsq,
                                                        int* status) {
   extern __shared__ __align__(16) uint8_t sm[];
   asm volatile("griddepcontrol.launch_dependents;");  // the O projection may start streaming its weights
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int ldpv = ldp;                                        // bytes per value row in shared memory
   int8_t* sK = (int8_t*)sm;                                    // ATTD_NS slots x ATTD_KB x hd
   int8_t* sV = sK + ATTD_NS * ATTD_KB * hd;                    // CH x ldpv
@@ -914,18 +944,19 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* __restrict__
 // finally the int8 probability rows for the context).  Each CTA then forms the
 // context of its CH channels over all keys.  The numbers are k_attention_dec's.
 // Every CTA takes every cluster barrier on every path.
-__global__ void __launch_bounds__(256) k_attention_dcl(const float* __restrict__ h, int nqkv, int nH, int nKV, int hd,
-                                                       const int8_t* __restrict__ k8, const float* __restrict__ ks,
-                                                       const int8_t* __restrict__ v8t, const float* __restrict__ vs,
-                                                       const int* __restrict__ n0p, int max_pos, int ldp, int CH,
-                                                       double scale, float* __restrict__ out,
-                                                       uint32_t* __restrict__ rowmax, int* __restrict__ done,
-                                                       int8_t* __restrict__ xq, int ldq, float* __restrict__ rsq,
+__global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv, int nH, int nKV, int hd,
+                                                       const int8_t* k8, const float* ks,
+                                                       const int8_t* v8t, const float* vs,
+                                                       const int* n0p, int max_pos, int ldp, int CH,
+                                                       double scale, float* out,
+                                                       uint32_t* rowmax, int* done,
+                                                       int8_t* xq, int ldq, float* rsq,
                                                        int* status) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   extern __shared__ __align__(16) uint8_t sm[];
   asm volatile("griddepcontrol.launch_dependents;");  // the O projection may start streaming its weights
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int ldpv = ldp;
   int8_t* sK = (int8_t*)sm;                                    // ATTD_NS slots x ATTD_KB x hd
   int8_t* sV = sK + ATTD_NS * ATTD_KB * hd;                    // CH x ldpv
@@ -1085,7 +1116,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* __restrict__
       }
     }
     __syncthreads();
-    z = dco::ordered_sum(xs, N, osm);
+    z = ordered_sum_cold(xs, N, osm);
     const double rz = __drcp_rn(z);
     float a2 = 0.0f;
     for (int i = 0; i < nmine; i++) {
@@ -1172,8 +1203,10 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* __restrict__
 // with silu(v) = v / (1 + exp(-v)) in double, written over g in place, and
 // |hid| folded into the row maximum (rowmax must start at 0).  The row's
 // quantisation follows in k_rowquant once every block has contributed.
-__global__ void __launch_bounds__(256) k_swiglu(float* __restrict__ h, int I, uint32_t* __restrict__ rowmax,
+__global__ void __launch_bounds__(256) k_swiglu(float* h, int I, uint32_t* rowmax,
                                                int* status) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   __shared__ float red[32];
   const int row = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1195,16 +1228,16 @@ __global__ void __launch_bounds__(256) k_swiglu(float* __restrict__ h, int I, ui
 
 // quantizeRows from a finished row maximum, element-parallel over grid
 // (ceil(ldq/256), rows): s[row] = f32(max(mx/127, 1e-8)) in double, q = clamp(round(x/sc)).
-__global__ void __launch_bounds__(256) k_rowquant(const float* __restrict__ x, int64_t ldx, int cols,
-                                                 const uint32_t* __restrict__ rowmax, int8_t* __restrict__ q,
-                                                 int ldq, float* __restrict__ s) {
+__global__ void __launch_bounds__(256) k_rowquant(const float* x, int64_t ldx, int cols,
+                                                 const uint32_t* rowmax, int8_t* q,
+                                                 int ldq, float* s) {
   asm volatile("griddepcontrol.launch_dependents;");  // the next GEMV may start streaming weights
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int row = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   const double sc = quant_scale(__uint_as_float(rowmax[row]));
   if (blockIdx.x == 0 && threadIdx.x == 0) s[row] = __double2float_rn(sc);
-  if (j < ldq)
-    q[(int64_t)row * ldq + j] = j < cols ? dc_clamp8(dc_js_round(__ddiv_rn((double)x[row * ldx + j], sc))) : (int8_t)0;
+  if (j < ldq) q[(int64_t)row * ldq + j] = j < cols ? dc_quant_div((double)x[row * ldx + j], sc, __drcp_rn(sc)) : (int8_t)0;
 }
 
 
@@ -1663,6 +1696,29 @@ static int gemm(dc_stage* S, const dc_mat& m, int T, const int8_t* xq, int ldx, 
   return dc_gemm_dispatch(S->ctx, xq, ldx, m.qt, m.ldk, S->rs, m.cs, T, m.k, m.n, 1, flags, out, S->ctx->stream, 0);
 }
 
+// Launch as a programmatic dependent of the previous kernel on the stream: the
+// CTAs may be scheduled while that kernel finishes.  Every kernel launched so
+// executes griddepcontrol.wait before it touches memory that earlier work on
+// the stream writes or reads (only constant data may be read before it), and
+// none of their pointer parameters to such memory is __restrict__: the
+// compiler may move a load through a restrict pointer above the wait's inline
+// assembly (a loop-invariant load hoisted out of a loop did exactly that).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // The layer loop of one stage on T rows of x (in place).  Every position the
 // kernels need is read from *n0p (the cached tokens before this call; 0 for the
 // full window), so the same launches can be captured once in a CUDA graph and
@@ -1705,26 +1761,27 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   for (auto& ly : S->L) {
     dc_kv& kv = ly.kv;
     // attention block
-    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm1, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status, nullptr, S->rowmax);
+    DC_CUDA(ctx, launch_dep(k_rmsnorm_quant, dim3(T), dim3(NORM_THREADS), nrm_smem, st, x, S->C, ly.nrm1,
+                            S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
     dc_count_launch();
     if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
     const int vblocks = (S->kvDim + 63) / 64;
-    k_rope_append<<<dim3(T, S->nH + S->nKV + vblocks), 64, 0, st>>>(
-        S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
-        kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status);
+    DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
+                            S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
+                            kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status));
     dc_count_launch();
     if (T > 1) {
-      k_vscale<<<(S->kvDim + 127) / 128, 128, 0, st>>>(kv.vmax, kv.vs, kv.vchg, S->kvDim, n0p);
+      DC_CUDA(ctx, launch_dep(k_vscale, dim3((S->kvDim + 127) / 128), dim3(128), 0, st, kv.vmax, kv.vs, kv.vchg,
+                              S->kvDim, n0p));
       dc_count_launch();
     }
     if (T <= 8) {
-      k_vquant_dev<<<dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), 256, 0, st>>>(
-          kv.v, kv.vs, kv.vchg, kv.v8t, T, n0p, S->kvDim, S->hd, S->ldp, T == 1 ? 1 : 0);
+      DC_CUDA(ctx, launch_dep(k_vquant_dev, dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), dim3(256), 0, st,
+                              kv.v, kv.vs, kv.vchg, kv.v8t, T, n0p, S->kvDim, S->hd, S->ldp, T == 1 ? 1 : 0));
     } else {
-      k_vquant<<<dim3((N + 63) / 64, (S->kvDim + 31) / 32), 256, 0, st>>>(kv.v, kv.vs, kv.vchg, kv.v8t, N, n0,
-                                                                        S->kvDim, S->hd, S->ldp);
+      DC_CUDA(ctx, launch_dep(k_vquant, dim3((N + 63) / 64, (S->kvDim + 31) / 32), dim3(256), 0, st, kv.v, kv.vs,
+                              kv.vchg, kv.v8t, N, n0, S->kvDim, S->hd, S->ldp));
     }
     dc_count_launch();
     if (T == 1 && use_kv && dec_ch && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8) {
@@ -1734,35 +1791,36 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       cfg.blockDim = dim3(256);
       cfg.dynamicSmemBytes = dec_smem;
       cfg.stream = st;
-      cudaLaunchAttribute attr[1];
+      cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 1;
       attr[0].val.clusterDim.y = S->hd / dec_ch;
       attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // a programmatic dependent too
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
-      cfg.numAttrs = 1;
+      cfg.numAttrs = 2;
       DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_attention_dcl, (const float*)S->hbuf, S->nqkv, S->nH, S->nKV, S->hd,
                                       (const int8_t*)kv.k8, (const float*)kv.ks, (const int8_t*)kv.v8t,
                                       (const float*)kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale, S->ctxo,
                                       S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status));
       dc_count_launch();
     } else if (T == 1 && use_kv && dec_ch) {
-      k_attention_dec<<<dim3(S->nH, S->hd / dec_ch), 256, dec_smem, st>>>(
-          S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale,
-          S->ctxo, S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status);
+      DC_CUDA(ctx, launch_dep(k_attention_dec, dim3(S->nH, S->hd / dec_ch), dim3(256), dec_smem, st, S->hbuf, S->nqkv,
+                              S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch,
+                              scale, S->ctxo, S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status));
       dc_count_launch();
     } else if (split_ctx && T <= 16) {
-      k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
-                                                                kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
-                                                                S->ctxo, S->rowmax, S->qDim, ctx->d_status, S->a8g,
-                                                                S->asg);
+      DC_CUDA(ctx, launch_dep(k_attention, dim3(S->nH, T), dim3(ATT_THREADS), att_smem, st, S->hbuf, S->nqkv, S->nH,
+                              S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale, S->ctxo,
+                              S->rowmax, S->qDim, ctx->d_status, S->a8g, S->asg));
       dc_count_launch();
-      k_attn_ctx<<<dim3(S->nH, S->hd / 32), 256, ctx_smem, st>>>(S->a8g, S->asg, kv.v8t, kv.vs, S->nH, S->nKV, S->hd,
-                                                                  T, n0p, S->ldp, S->ctxo, S->qDim, S->rowmax,
-                                                                  ctx->d_status);
+      DC_CUDA(ctx, launch_dep(k_attn_ctx, dim3(S->nH, S->hd / 32), dim3(256), ctx_smem, st, S->a8g, S->asg, kv.v8t,
+                              kv.vs, S->nH, S->nKV, S->hd, T, n0p, S->ldp, S->ctxo, S->qDim, S->rowmax,
+                              ctx->d_status));
       dc_count_launch();
-      k_rowquant<<<dim3((S->ldQ + 255) / 256, T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
-                                                                S->rs);
+      DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldQ + 255) / 256, T), dim3(256), 0, st, S->ctxo,
+                              (int64_t)S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ, S->rs));
       dc_count_launch();
     } else {
       k_attention<<<dim3(S->nH, T), ATT_THREADS, att_smem, st>>>(S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, kv.k8, kv.ks,
@@ -1775,14 +1833,15 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, x, DC_F_ADDTO))) return rc;  // x2 = x + attn
     // MLP block
-    k_rmsnorm_quant<<<T, NORM_THREADS, nrm_smem, st>>>(x, S->C, ly.nrm2, S->spec.norm_eps, S->xq, S->ldC, S->rs,
-                                                         ctx->d_status, nullptr, S->rowmax);
+    DC_CUDA(ctx, launch_dep(k_rmsnorm_quant, dim3(T), dim3(NORM_THREADS), nrm_smem, st, x, S->C, ly.nrm2,
+                            S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
     dc_count_launch();
     if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
-    k_swiglu<<<dim3((S->I + 255) / 256, T), 256, 0, st>>>(S->hbuf, S->I, S->rowmax, ctx->d_status);
+    DC_CUDA(ctx, launch_dep(k_swiglu, dim3((S->I + 255) / 256, T), dim3(256), 0, st, S->hbuf, S->I, S->rowmax,
+                            ctx->d_status));
     dc_count_launch();
-    k_rowquant<<<dim3((S->ldI + 255) / 256, T), 256, 0, st>>>(S->hbuf, 2 * (int64_t)S->I, S->I, S->rowmax, S->xq,
-                                                              S->ldI, S->rs);
+    DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldI + 255) / 256, T), dim3(256), 0, st, S->hbuf, 2 * (int64_t)S->I,
+                            S->I, S->rowmax, S->xq, S->ldI, S->rs));
     dc_count_launch();
     if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, x, DC_F_ADDTO))) return rc;  // out = x2 + down
     DC_CUDA(ctx, cudaGetLastError());
