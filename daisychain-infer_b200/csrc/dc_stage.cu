@@ -167,21 +167,40 @@ static size_t rms_smem(int C) {
 __device__ __noinline__ double rms_inv(double s, int C, double eps) {
   return __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)C), eps)));
 }
-// Block sum of doubles in any order (an approximation: only used to bracket).
-__device__ __forceinline__ double block_sum_d(double v, double* red) {
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+// Block sums of two doubles in any order (used only to bracket serial sums).
+__device__ __forceinline__ double2 block_sum_d2(double a, double b, double2* red) {
+  for (int o = 16; o; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
   __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_double2(a, b);
   __syncthreads();
   if (threadIdx.x < 32) {
-    double w = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
-    for (int o = 16; o; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+    double2 w = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : make_double2(0.0, 0.0);
+    for (int o = 16; o; o >>= 1) {
+      w.x += __shfl_xor_sync(0xffffffffu, w.x, o);
+      w.y += __shfl_xor_sync(0xffffffffu, w.y, o);
+    }
     if (threadIdx.x == 0) red[0] = w;
   }
   __syncthreads();
-  const double r = red[0];
+  const double2 r = red[0];
   __syncthreads();
   return r;
+}
+
+// Radius of an interval around s that holds the serial sum t_0 + t_1 + ... +
+// t_(n-1) of non-negative doubles (each add rounded to nearest), where s is
+// the same terms summed in any order with every term passing through at most
+// `depth` rounded adds, and w is the sum of (n - j) * t_j (any order).  The
+// serial sum errs by at most u times the sum of its exact prefix sums, i.e.
+// u * sum (n - j) t_j (each add errs by at most u times its result, and the
+// running sum stays within a factor 1 + gamma_n of the exact prefix); s errs
+// by at most gamma_depth times the total.  u = 2^-53; the constants absorb
+// the rounding of w, of this radius and of s -/+ radius.
+__device__ __forceinline__ double serial_sum_radius(double s, double w, int depth) {
+  return 1.1102230246251565e-16 * (1.001 * w + (double)(depth + 8) * s);
 }
 
 // RMSNorm of one row fused with quantizeRows of its output.
@@ -199,7 +218,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
   float* wsm = 16 * (size_t)C + 20 * 1024 <= 232448 ? ys + C : nullptr;
   const float* wr = wsm ? wsm : w;
   __shared__ float red[32];
-  __shared__ double redd[32];
+  __shared__ double2 redd2[32];
   __shared__ int vote[32];
   __shared__ dco::Smem osm;
   // the GEMV that consumes q may launch now: it streams its weights meanwhile
@@ -245,20 +264,22 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
   if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(status, DC_ST_NONFINITE);
   __syncthreads();
   // The reference sums s += v*v for j = 0 .. C-1, each step rounded.  That
-  // serial value is bracketed first: an any-order sum S' is within
-  // 2*gamma_(C-1)*S' of it (both are within gamma_(C-1) of the exact sum of
-  // these non-negative terms), inv = 1/sqrt(s/C + eps) is monotone in s, and
-  // each y_j = f32(x_j*inv*w_j) is monotone in inv.  When every y_j is the same
-  // at both ends of the bracket, it is the serial sum's y_j; otherwise (rare:
-  // some y_j within ~1e-12 of an f32 rounding boundary) the block computes the
-  // serial-order sum itself.
+  // serial value is bracketed first: an any-order sum S' and the error bound
+  // of serial_sum_radius give an interval that holds it, inv = 1/sqrt(s/C +
+  // eps) is monotone in s, and each y_j = f32(x_j*inv*w_j) is monotone in inv.
+  // When every y_j is the same at both ends of the bracket, it is the serial
+  // sum's y_j; otherwise (rare: some y_j within ~1e-13 of an f32 rounding
+  // boundary) the block computes the serial-order sum itself.
   double inv;
   {
-    double part = 0.0;
-    for (int j = threadIdx.x; j < C; j += blockDim.x) part += sq[j];
-    const double sp = block_sum_d(part, redd);
-    const double d = (double)(C + 16) * 4.440892098500626e-16;  // 4 * (C + 4) * 2^-53
-    const double inv_hi = rms_inv(sp * (1.0 - d), C, eps), inv_lo = rms_inv(sp * (1.0 + d), C, eps);
+    double part = 0.0, wpart = 0.0;
+    for (int j = threadIdx.x; j < C; j += blockDim.x) {
+      part += sq[j];
+      wpart += (double)(C - j) * sq[j];
+    }
+    const double2 sw = block_sum_d2(part, wpart, redd2);
+    const double h = serial_sum_radius(sw.x, sw.y, (C + (int)blockDim.x - 1) / (int)blockDim.x + 10);
+    const double inv_hi = rms_inv(sw.x - h, C, eps), inv_lo = rms_inv(sw.x + h, C, eps);
     bool amb = exact_sum != 0;
     for (int j = threadIdx.x; j < C && !amb; j += blockDim.x) {
       const double xw = (double)ys[j], wj = (double)wr[j];
@@ -324,17 +345,20 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
 
 // The softmax denominator z (infer.js:100-104: z += e_j in key order, each
 // add rounded) as far as the probabilities a_j = f32(f32(e_j) / z) can tell:
-// an any-order sum brackets the serial z within 2*gamma_(n-1) (non-negative
+// an any-order sum and serial_sum_radius bracket the serial z (non-negative
 // terms), each a_j is monotone in z, so when every a_j is the same at both
 // ends of the bracket the lower end gives the serial z's a_j; otherwise the
 // block computes the serial-order sum.  `af` holds f32(e_j).
-__device__ __forceinline__ double softmax_z(const double* e, const float* af, int n, dco::Smem& osm, double* redd,
+__device__ __forceinline__ double softmax_z(const double* e, const float* af, int n, dco::Smem& osm, double2* redd2,
                                             int* vote) {
-  double part = 0.0;
-  for (int j = threadIdx.x; j < n; j += blockDim.x) part += e[j];
-  const double zp = block_sum_d(part, redd);
-  const double d = (double)(n + 16) * 4.440892098500626e-16;  // 4 * (n + 4) * 2^-53
-  const double zlo = zp * (1.0 - d), zhi = zp * (1.0 + d);
+  double part = 0.0, wpart = 0.0;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    part += e[j];
+    wpart += (double)(n - j) * e[j];
+  }
+  const double2 zw = block_sum_d2(part, wpart, redd2);
+  const double h = serial_sum_radius(zw.x, zw.y, (n + (int)blockDim.x - 1) / (int)blockDim.x + 10);
+  const double zp = zw.x, zlo = zp - h, zhi = zp + h;
   const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
   bool amb = false;
   for (int j = threadIdx.x; j < n && !amb; j += blockDim.x)
@@ -551,7 +575,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* h, in
   int8_t* a8 = (int8_t*)(sm + ((12 * (size_t)max_pos + 15) & ~(size_t)15));  // ldp int8, 16-byte aligned
   __shared__ __align__(16) int8_t q8[128];
   __shared__ float red[32];
-  __shared__ double redd[32];
+  __shared__ double2 redd2[32];  // also the 32 doubles of block_max_d / block_sum_d
+  double* redd = reinterpret_cast<double*>(redd2);
   __shared__ int vote[32];
   __shared__ dco::Smem osm;
   const int hq = blockIdx.x, i = blockIdx.y;
@@ -603,7 +628,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* h, in
   }
   __syncthreads();
   // 5. z: the serial key-order sum, as far as the probabilities can tell
-  const double z = softmax_z(ed, af, see + 1, osm, redd, vote);
+  const double z = softmax_z(ed, af, see + 1, osm, redd2, vote);
   // 6. a_j = f32(a_j / z); 7. quantise the probability row over all N columns
   float amx = 0.0f;
   const double rz = __drcp_rn(z);
@@ -771,7 +796,8 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* h, int nqkv,
   __shared__ __align__(8) uint64_t full[ATTD_NS], vbar;
   __shared__ __align__(16) int8_t q8[256];
   __shared__ float red[32];
-  __shared__ double redd[32];
+  __shared__ double2 redd2[32];  // also the 32 doubles of block_max_d / block_sum_d
+  double* redd = reinterpret_cast<double*>(redd2);
   __shared__ int vote[32];
   __shared__ int abort_flag;
   __shared__ dco::Smem osm;
@@ -870,7 +896,7 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* h, int nqkv,
     }
     __syncthreads();
     // 5. z: the serial key-order sum, as far as the probabilities can tell
-    const double z = softmax_z(xs, af, N, osm, redd, vote);
+    const double z = softmax_z(xs, af, N, osm, redd2, vote);
     // 6. a_j = f32(f32(e_j) / z); 7. quantizeRows of the probability row
     const double rz = __drcp_rn(z);
     float amx = 0.0f;
@@ -966,10 +992,11 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   __shared__ __align__(8) uint64_t full[ATTD_NS], vbar;
   __shared__ __align__(16) int8_t q8[256];
   __shared__ float red[32];
-  __shared__ double redd[32];
+  __shared__ double2 redd2[32];  // also the 32 doubles of block_max_d / block_sum_d
+  double* redd = reinterpret_cast<double*>(redd2);
   __shared__ int vote[32];
   __shared__ int abort_flag;
-  __shared__ double xd[2];  // published to the cluster: score maximum, sum of e
+  __shared__ double xd[3];  // published to the cluster: score maximum, sum of e, sum of (N - j) e_j
   __shared__ float xf;      // probability maximum
   __shared__ int xi;        // 1: some probability is ambiguous under the bracket of z
   __shared__ dco::Smem osm;
@@ -1062,7 +1089,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   m = -INFINITY;
   for (int q = 0; q < S; q++) m = fmax(m, *cl.map_shared_rank(&xd[0], q));
   // 4. e_j of this CTA's keys; the cluster's any-order sum brackets z
-  double part = 0.0;
+  double part = 0.0, wpart = 0.0;
   for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < N) {
@@ -1070,15 +1097,25 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       xs[j] = e;
       af[j] = __double2float_rn(e);
       part += e;
+      wpart += (double)(N - j) * e;
     }
   }
-  part = block_sum_d(part, redd);
-  if (tid == 0) xd[1] = part;
+  {
+    const double2 pw = block_sum_d2(part, wpart, redd2);
+    if (tid == 0) {
+      xd[1] = pw.x;
+      xd[2] = pw.y;
+    }
+  }
   cl.sync();
-  double zp = 0.0;
-  for (int q = 0; q < S; q++) zp += *cl.map_shared_rank(&xd[1], q);
-  const double d = (double)(N + 16) * 4.440892098500626e-16;  // 4 * (N + 4) * 2^-53
-  const double zlo = zp * (1.0 - d), zhi = zp * (1.0 + d);
+  double zp = 0.0, zw = 0.0;
+  for (int q = 0; q < S; q++) {
+    zp += *cl.map_shared_rank(&xd[1], q);
+    zw += *cl.map_shared_rank(&xd[2], q);
+  }
+  // a term passes through at most nmine + 10 adds in its CTA and S - 1 across the cluster
+  const double zr = serial_sum_radius(zp, zw, (N + ATTD_KB - 1) / ATTD_KB + 24);
+  const double zlo = zp - zr, zhi = zp + zr;
   const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
   bool amb = false;
   float amx = 0.0f;
