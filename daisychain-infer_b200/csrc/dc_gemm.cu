@@ -228,10 +228,15 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
 // shuffle).  When a stage holds fewer than 8 rows, WR = 8/R warps share a row
 // and add their int32 partials with shared-memory atomics; the last of them
 // applies the epilogue.  Waits are bounded; a timeout aborts the whole CTA.
+//
+// Launched as a programmatic dependent: the producer starts streaming weights
+// (constant) at once; the consumer warps read the activation rows (written by
+// the previous kernel: X and rs carry no __restrict__) after
+// griddepcontrol.wait and meet on a named barrier.
 template <int MR>
-__global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* __restrict__ X, int ldx,
+__global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* X, int ldx,
                                                       const int8_t* __restrict__ Wt, int ldw,
-                                                      const float* __restrict__ rs, const float* __restrict__ cs,
+                                                      const float* rs, const float* __restrict__ cs,
                                                       int m, int k, int n, unsigned flags,
                                                       const int8_t* __restrict__ requant,
                                                       const int8_t* __restrict__ relu, void* out, int R, int stages,
@@ -246,6 +251,7 @@ __global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* __restrict__
   int4* xs = (int4*)(smraw + (size_t)stages * stage_bytes);
   uint64_t* full = (uint64_t*)(xs + MR * nch);
   uint64_t* empty = full + stages;
+  asm volatile("griddepcontrol.launch_dependents;");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bz = blockIdx.y;
   const int rb = blockIdx.x * rows_per_cta;
@@ -261,13 +267,21 @@ __global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* __restrict__
   }
   for (int i = tid; i < 8 * 8 * MR; i += blockDim.x) (&rowacc[0][0][0])[i] = 0;
   for (int i = tid; i < 8 * 8; i += blockDim.x) (&rowcnt[0][0])[i] = 0;
-  const int8_t* Xb = X + (int64_t)bz * m * ldx;
-  for (int idx = tid; idx < MR * nch; idx += blockDim.x) {
-    const int r = idx / nch, c = idx - r * nch;
-    xs[idx] = (r < m) ? *((const int4*)(Xb + (int64_t)r * ldx) + c) : make_int4(0, 0, 0, 0);
-  }
   __syncthreads();
-  if (nst == 0) return;
+  if (nst == 0) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    return;
+  }
+  if (warp < 8) {
+    // consumers: the activation rows, once the kernel that writes them is done
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int8_t* Xb = X + (int64_t)bz * m * ldx;
+    for (int idx = tid; idx < MR * nch; idx += 256) {
+      const int r = idx / nch, c = idx - r * nch;
+      xs[idx] = (r < m) ? *((const int4*)(Xb + (int64_t)r * ldx) + c) : make_int4(0, 0, 0, 0);
+    }
+    dcp::named_sync(1, 256);
+  }
   if (warp == 8) {
     // ---- producer
     if (lane == 0) {
@@ -463,8 +477,20 @@ int launch_gemv_bulk(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, i
   const int rows_per_cta = (n + gx - 1) / gx;
   gx = (n + rows_per_cta - 1) / rows_per_cta;
   if (int rc = dc_set_smem(ctx, (const void*)k_gemv_bulk<MR>, (int)smem)) return rc;
-  k_gemv_bulk<MR><<<dim3(gx, batch), 288, smem, st>>>(Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags, ctx->d_requant,
-                                                      ctx->d_relu, out, R, stages, rows_per_cta, ctx->d_status);
+  // a programmatic dependent: the weight stream starts while the previous kernel finishes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(gx, batch);
+  cfg.blockDim = dim3(288);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemv_bulk<MR>, Xq, ldx, Wt, ldw, rs, cs, m, k, n, flags,
+                                  (const int8_t*)ctx->d_requant, (const int8_t*)ctx->d_relu, out, R, stages,
+                                  rows_per_cta, ctx->d_status));
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
