@@ -962,6 +962,37 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* h, int nqkv,
   }
 }
 
+// The rare path of k_attention_dcl, out of line: the serial key-order z
+// itself.  Every CTA of the cluster gathers all e_j (and f32(e_j)) from their
+// owners, sums them in key order (the same value in each), and publishes in
+// *xf the largest probability of its own keys under that z.  Every thread of
+// every CTA of the cluster calls it.
+__device__ __noinline__ double dcl_exact_z(double* xs, float* af, int N, int S, int r, int nmine, dco::Smem& osm,
+                                           float* red, float* xf) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int tid = threadIdx.x;
+  for (int j = tid; j < N; j += 256) {
+    const int owner = (j / ATTD_KB) % S;
+    if (owner != r) {
+      xs[j] = *cl.map_shared_rank(&xs[j], owner);
+      af[j] = *cl.map_shared_rank(&af[j], owner);
+    }
+  }
+  __syncthreads();
+  const double z = dco::ordered_sum(xs, N, osm);
+  const double rz = __drcp_rn(z);
+  float a2 = 0.0f;
+  for (int i = 0; i < nmine; i++) {
+    const int j = (r + i * S) * ATTD_KB + tid;
+    if (j < N) a2 = fmaxf(a2, dc_div_to_f32((double)af[j], z, rz));
+  }
+  a2 = block_max_f(a2, red);
+  cl.sync();  // everyone has read the published values before they change
+  if (tid == 0) *xf = a2;
+  return z;
+}
+
 // The decode attention of k_attention_dec with the head's S = hd / CH CTAs
 // forming a thread-block cluster: CTA r computes the scores, exps and
 // probabilities of key blocks r, r + S, r + 2S, ... only, and the CTAs
@@ -1021,9 +1052,11 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   if (warp == 0) {
     if (lane == 0) dcp::mbar_expect_tx(&vbar, (uint32_t)(CH * ldpN));
     __syncwarp();
+    #pragma unroll 1
     for (int c = lane; c < CH; c += 32)
       dcp::bulk_load(sV + (size_t)c * ldpv, v8t + ((int64_t)g * hd + c0 + c) * ldp, (uint32_t)ldpN, &vbar);
     if (lane == 0)
+      #pragma unroll 1
       for (int i = 0; i < ATTD_NS && i < nmine; i++) {
         issued[i] = i;
         const int b = r + i * S;
@@ -1039,6 +1072,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const float* qrow = h + hq * hd;
   float mx = 0.0f;
   bool bad = false;
+  #pragma unroll 1
   for (int c = tid; c < hd; c += 256) {
     const float v = qrow[c];
     bad |= !isfinite(v);
@@ -1047,13 +1081,14 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   mx = block_max_f(mx, red);
   const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
   const float qs = __double2float_rn(qsc);
+  #pragma unroll 1
   for (int c = tid; c < hd; c += 256) q8[c] = dc_quant_div((double)qrow[c], qsc, rqsc);
   __syncthreads();
   // 2. scores of this CTA's key blocks (one key per thread)
   const int nchk = hd >> 4;
   const int rot = lane >> 2;
   double m = -INFINITY;
-  for (int i = 0; i < nmine; i++) {
+  _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
     const int slot = i % ATTD_NS, b = r + i * S;
     if (!dcp::mbar_wait(&full[slot], (uint32_t)(i / ATTD_NS) & 1u, status)) abort_flag = 1;
     __syncthreads();
@@ -1087,10 +1122,12 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   if (tid == 0) xd[0] = m;
   cl.sync();
   m = -INFINITY;
-  for (int q = 0; q < S; q++) m = fmax(m, *cl.map_shared_rank(&xd[0], q));
+#pragma unroll
+  for (int q = 0; q < 8; q++)  // S <= 8: every remote load in flight at once
+    if (q < S) m = fmax(m, *cl.map_shared_rank(&xd[0], q));
   // 4. e_j of this CTA's keys; the cluster's any-order sum brackets z
   double part = 0.0, wpart = 0.0;
-  for (int i = 0; i < nmine; i++) {
+  _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < N) {
       const double e = dcm::fdlibm_exp(__dsub_rn(xs[j], m));
@@ -1109,9 +1146,12 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   }
   cl.sync();
   double zp = 0.0, zw = 0.0;
-  for (int q = 0; q < S; q++) {
-    zp += *cl.map_shared_rank(&xd[1], q);
-    zw += *cl.map_shared_rank(&xd[2], q);
+#pragma unroll
+  for (int q = 0; q < 8; q++) {
+    if (q < S) {
+      zp += *cl.map_shared_rank(&xd[1], q);
+      zw += *cl.map_shared_rank(&xd[2], q);
+    }
   }
   // a term passes through at most nmine + 10 adds in its CTA and S - 1 across the cluster
   const double zr = serial_sum_radius(zp, zw, (N + ATTD_KB - 1) / ATTD_KB + 24);
@@ -1119,7 +1159,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
   bool amb = false;
   float amx = 0.0f;
-  for (int i = 0; i < nmine; i++) {
+  _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < N) {
       const float alo = dc_div_to_f32((double)af[j], zhi, rhi), ahi = dc_div_to_f32((double)af[j], zlo, rlo);
@@ -1140,39 +1180,21 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   }
   cl.sync();
   int any_amb = 0;
-  for (int q = 0; q < S; q++) any_amb |= *cl.map_shared_rank(&xi, q);
-  double z = zlo;
-  if (any_amb) {
-    // rare: the serial key-order z itself.  Every CTA gathers all e_j from
-    // their owners and sums them (the same value in each).
-    for (int j = tid; j < N; j += 256) {
-      const int owner = (j / ATTD_KB) % S;
-      if (owner != r) {
-        xs[j] = *cl.map_shared_rank(&xs[j], owner);
-        af[j] = *cl.map_shared_rank(&af[j], owner);
-      }
-    }
-    __syncthreads();
-    z = ordered_sum_cold(xs, N, osm);
-    const double rz = __drcp_rn(z);
-    float a2 = 0.0f;
-    for (int i = 0; i < nmine; i++) {
-      const int j = (r + i * S) * ATTD_KB + tid;
-      if (j < N) a2 = fmaxf(a2, dc_div_to_f32((double)af[j], z, rz));
-    }
-    a2 = block_max_f(a2, red);
-    cl.sync();  // everyone has read the published values before they change
-    if (tid == 0) xf = a2;
-  }
+#pragma unroll
+  for (int q = 0; q < 8; q++)
+    if (q < S) any_amb |= *cl.map_shared_rank(&xi, q);
+  const double z = any_amb ? dcl_exact_z(xs, af, N, S, r, nmine, osm, red, &xf) : zlo;
   cl.sync();
   amx = 0.0f;
-  for (int q = 0; q < S; q++) amx = fmaxf(amx, *cl.map_shared_rank(&xf, q));
+#pragma unroll
+  for (int q = 0; q < 8; q++)
+    if (q < S) amx = fmaxf(amx, *cl.map_shared_rank(&xf, q));
   // 6-7. a_j = f32(f32(e_j) / z) of this CTA's keys, quantised with the row's scale
   const double asc = quant_scale(amx), rasc = __drcp_rn(asc);
   const float as = __double2float_rn(asc);
   {
     const double rz = __drcp_rn(z);
-    for (int i = 0; i < nmine; i++) {
+    _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
       const int kb = (r + i * S) * ATTD_KB;
       const int j = kb + tid;
       if (j < ldpN) a8[j] = j < N ? dc_quant_div((double)dc_div_to_f32((double)af[j], z, rz), asc, rasc) : (int8_t)0;
@@ -1180,6 +1202,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   }
   cl.sync();
   // the other CTAs' probability bytes, 16 at a time
+  #pragma unroll 1
   for (int q16 = tid; q16 < (ldpN >> 4); q16 += 256) {
     const int owner = ((q16 << 4) / ATTD_KB) % S;
     if (owner != r) ((int4*)a8)[q16] = *cl.map_shared_rank(&((int4*)a8)[q16], owner);
@@ -1192,8 +1215,10 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   if (!abort_flag) {
     const int nch = ldpN >> 4;
     const int4* a4 = (const int4*)a8;
+    #pragma unroll 1
     for (int cl4 = warp * 4; cl4 < CH; cl4 += 32) {
       int sacc[4] = {0, 0, 0, 0};
+      #pragma unroll 1
       for (int q = lane; q < nch; q += 32) {
         const int4 av = a4[q];
 #pragma unroll
