@@ -168,8 +168,9 @@ int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float*
                    int exact_sum);
 
 /* Prefetch [p, p + bytes) of device memory into L2 (16-byte aligned range),
- * asynchronously on the context's stream.  No counterpart in the reference:
- * the stages use it to pull the next weights while latency-bound kernels run. */
+ * asynchronously on the context's stream.  No counterpart in the reference; a
+ * host may warm a buffer it is about to use (the stage forward does not call
+ * it: issuing the prefetch cost more than it saved on the layer loop). */
 int dc_l2_prefetch(dc_ctx* ctx, const void* p, size_t bytes);
 
 /* ---- kernel probe (webgpu.js:998-1060) --------------------------------------
