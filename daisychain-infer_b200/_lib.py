@@ -77,6 +77,7 @@ SIGNATURES = [
     ("dc_rmsnorm_dev", _i, [_p, _p, _i, _i, _p, _d, _p, _i]),
     ("dc_l2_prefetch", _i, [_p, _p, C.c_size_t]),
     ("dc_kernel_probe", _i, [_p, C.POINTER(_u32)]),
+    ("dc_fnv1a", _u32, [_p, C.c_size_t]),
     ("dc_stage_create", _i, [_p, _p, _i, _i, _i, _i, _i, C.POINTER(_p)]),
     ("dc_stage_free", None, [_p]),
     ("dc_stage_set_layer", _i, [_p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p]),

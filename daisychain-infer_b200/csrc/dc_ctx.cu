@@ -348,6 +348,16 @@ extern "C" void dc_destroy(dc_ctx* c) {
   delete c;
 }
 
+// FNV-1a over raw bytes (shard.js:195-200): h = (h ^ b) * 16777619 mod 2^32
+// from 2166136261.  Host code: the hash is byte-serial (each step depends on
+// the last), and it is only needed where an activation leaves the GPU.
+extern "C" uint32_t dc_fnv1a(const void* p, size_t n) {
+  const unsigned char* b = static_cast<const unsigned char*>(p);
+  uint32_t h = 2166136261u;
+  for (size_t i = 0; i < n; i++) h = (h ^ b[i]) * 16777619u;
+  return h;
+}
+
 extern "C" const char* dc_backend_label(const dc_ctx* c) { return c ? c->label : "none"; }
 extern "C" const char* dc_last_error(const dc_ctx* c) { return c ? c->err.c_str() : "no context"; }
 extern "C" void* dc_stream(const dc_ctx* c) { return c ? (void*)c->stream : nullptr; }

@@ -19,7 +19,9 @@ send/recv of the same f32 buffer), and the lap never leaves the devices:
 ``Ring`` is written against two small interfaces so its schedule can be tested
 on CPU ranks (gloo) with a stand-in stage: a stage with
 ``embed_rows / run_layers / run_layers_chunk / logits_at`` and a transport
-with ``send(tensor, dst) / recv(tensor, src)``.
+with ``send(tensor, dst, token_idx) / recv(tensor, src, token_idx)`` (the
+token index of the hop's first row, which ``wire.WireTransport`` writes into
+and checks against the reference's activation frame; ``TorchP2P`` ignores it).
 """
 from __future__ import annotations
 
@@ -51,10 +53,10 @@ class TorchP2P:
         import torch.distributed as dist
         self.dist = dist
 
-    def send(self, t, dst: int):
+    def send(self, t, dst: int, token_idx: int = 0):
         return self.dist.isend(t, dst)
 
-    def recv(self, t, src: int):
+    def recv(self, t, src: int, token_idx: int | None = None):
         return self.dist.irecv(t, src)
 
 
@@ -90,9 +92,9 @@ class Ring:
             flights = []
             for ch in chunks["chunks"]:
                 x = S.run_layers_chunk(S.embed_rows(ids0[ch["lo"]:ch["hi"]]), ch["lo"])
-                sent = self.tp.send(x, self.nxt)  # the handle keeps the send (and x) alive
+                sent = self.tp.send(x, self.nxt, token_idx=ch["lo"])  # the handle keeps the send (and x) alive
                 back = self.new_buffer((ch["hi"] - ch["lo"]) * H)
-                flights.append((sent, self.tp.recv(back, self.prv), back))
+                flights.append((sent, self.tp.recv(back, self.prv, token_idx=ch["lo"]), back))
                 if len(flights) >= chunks["window"]:
                     sent_, req, buf = flights.pop(0)
                     sent_.wait()
@@ -110,16 +112,16 @@ class Ring:
         pending = []
         for ch in chunks["chunks"]:
             buf = self.new_buffer((ch["hi"] - ch["lo"]) * H)
-            self.tp.recv(buf, self.prv).wait()
+            self.tp.recv(buf, self.prv, token_idx=ch["lo"]).wait()
             S.run_layers_chunk(buf, ch["lo"])
-            pending.append(self.tp.send(buf, self.nxt))
+            pending.append(self.tp.send(buf, self.nxt, token_idx=ch["lo"]))
         if on_prefill:
             on_prefill()
         for n in range(n_new):
             buf = self.new_buffer(H)
-            self.tp.recv(buf, self.prv).wait()
+            self.tp.recv(buf, self.prv, token_idx=len(ids0) + n).wait()
             S.run_layers_chunk(buf, len(ids0) + n)
-            pending.append(self.tp.send(buf, self.nxt))
+            pending.append(self.tp.send(buf, self.nxt, token_idx=len(ids0) + n))
         for p in pending:
             p.wait()
         return None
@@ -142,9 +144,9 @@ class Ring:
             rows = last.numel() // self.hidden
             S.pick_into(last, rows - 1, picks, n)
             x = S.run_layers_chunk(S.embed_device(picks, n), n_prompt + n)
-            sent = self.tp.send(x, self.nxt)
+            sent = self.tp.send(x, self.nxt, token_idx=n_prompt + n)
             back = self.new_buffer(self.hidden)
-            self.tp.recv(back, self.prv).wait()
+            self.tp.recv(back, self.prv, token_idx=n_prompt + n).wait()
             sent.wait()
             last = back
         return picks

@@ -179,6 +179,12 @@ int dc_l2_prefetch(dc_ctx* ctx, const void* p, size_t bytes);
  * its transcendental hash, which needs V8). */
 int dc_kernel_probe(dc_ctx* ctx, uint32_t* hash);
 
+/* FNV-1a (32-bit) of n bytes of host memory: shard.js fnv1a (:195-200), the
+ * actHash of an activation frame (wire.js packAct :106-112, over the f32
+ * payload's bytes) and the model fingerprint (shard.js:206-213).  Host-only;
+ * needs no context. */
+uint32_t dc_fnv1a(const void* p, size_t n);
+
 /* ---- pipeline stages (public/infer.js, Llama family) -------------------------
  * A stage owns layers [layer_lo, layer_hi) of one model (shard.js planStages
  * :32-52) with every weight quantised once and resident in HBM, RoPE tables,

@@ -83,7 +83,7 @@ def plan_for(world):
     return {1: [(0, 6)], 2: [(0, 2), (2, 6)], 3: [(0, 1), (1, 4), (4, 6)]}[world]
 
 
-def run_rank(rank, world, port, prompt, q):
+def run_rank(rank, world, port, prompt, q, wire=False):
     import torch.distributed as dist
     import __graft_entry__ as G
     P = G.package()
@@ -93,8 +93,12 @@ def run_rank(rank, world, port, prompt, q):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     lo, hi = plan_for(world)[rank]
     st = FakeStage(lo, hi, rank == 0)
-    ring = P.pipeline.Ring(st, rank, world, H, P.pipeline.TorchP2P() if world > 1 else None,
-                           new_buffer=lambda n: torch.empty(n, dtype=torch.float32))
+    tp = P.pipeline.TorchP2P() if world > 1 else None
+    if tp is not None and wire:
+        # every hop as a wire.js activation frame, checked on arrival
+        plan = [dict(id=f"rank{i}", index=i) for i in range(world)]
+        tp = P.wire.WireTransport(tp, plan, rank, model_hash=0x5EED1234, seq=7)
+    ring = P.pipeline.Ring(st, rank, world, H, tp, new_buffer=lambda n: torch.empty(n, dtype=torch.float32))
     marks = []
     picks = ring.generate_chunked(prompt, 5, chunk_size=3, window=2, on_prefill=lambda: marks.append(rank))
     assert marks == [rank]  # every rank marks the end of its prefill part once (the bench's timer)
@@ -113,11 +117,11 @@ def _free_port():
     return p
 
 
-def run_world(world, prompt):
+def run_world(world, prompt, wire=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=run_rank, args=(r, world, port, prompt, q)) for r in range(world)]
+    procs = [ctx.Process(target=run_rank, args=(r, world, port, prompt, q, wire)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -139,6 +143,14 @@ def test_ring_matches_single_rank(P, world):
     assert run_world(world, prompt) == ref
     assert len(ref[0]) == 5 and len(ref[1]) == 7 + 4
     assert len(set(ref[0])) > 1  # the stand-in model is not degenerate
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_ring_over_wire_frames_matches_single_rank(P, world):
+    """The same schedule with every hop framed, hashed and checked as the
+    reference's activation messages (wire.js:100-121) picks the same ids."""
+    prompt = [2, 7, 1, 8, 2, 8, 1, 8, 2, 8]
+    assert run_world(world, prompt, wire=True) == run_world(1, prompt)
 
 
 def walk_lap(P, plan):
