@@ -10,3 +10,4 @@ from .compute import Compute, Weight, init_compute  # noqa: F401
 from . import infer, shard  # noqa: E402,F401
 from . import pipeline  # noqa: E402,F401
 from . import wire  # noqa: E402,F401
+from . import safetensors  # noqa: E402,F401

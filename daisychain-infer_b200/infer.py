@@ -132,6 +132,12 @@ class Stage:
         if self.head:
             self.set_head(w["emb"], w["nrmF"], w.get("lm"))
 
+    def load_safetensors(self, path: str) -> None:
+        """This stage's tensors of a safetensors model file: only their byte
+        ranges are read (shard.js stageWeights :78-121), then quantised on the GPU."""
+        from . import safetensors
+        self.load(safetensors.read_stage_weights(path, self.spec, self.lo, self.hi, self.head))
+
     def synth(self, model_seed: int, factor: float) -> None:
         self._check(self.L.dc_stage_synth(self.h, model_seed, float(factor)), "stage_synth")
 

@@ -87,6 +87,22 @@ def test_generation_matches_oracle_at_every_split(comp, O, P, fixture, splits):
     assert got == ref
 
 
+def test_stages_load_their_slice_of_a_safetensors_file(comp, O, P, fixture, tmp_path):
+    """The fixture model written as a safetensors file; every stage reads only
+    its own tensors from it and the generation equals the oracle's."""
+    ospec, spec, w, om = fixture
+    path = str(tmp_path / "fixture.safetensors")
+    P.safetensors.save_weights(path, w, spec)
+    ref = O.generate_local(om, [(0, 6)], PROMPT, 8, T)
+    for splits in ([6], [2, 4]):
+        stages = []
+        for i, (lo, hi) in enumerate(ranges(splits)):
+            S = P.infer.Stage(comp, spec, lo, hi, head=(i == 0), max_rows=64, max_pos=64)
+            S.load_safetensors(path)
+            stages.append(S)
+        assert P.infer.generate_local(stages, PROMPT, 8, T) == ref
+
+
 def test_mutations_are_caught_on_device(comp, O, P, fixture):
     ospec, spec, w, om = fixture
     ref = O.generate_local(om, [(0, 6)], PROMPT, 8, T)
