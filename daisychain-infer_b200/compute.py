@@ -156,6 +156,65 @@ class Compute:
         self._check(self.L.dc_rmsnorm_dev(self.h, _ptr(x), rows, cols, _ptr(w), float(eps), _ptr(y),
                                           1 if exact_sum else 0), "rmsnorm")
 
+    def measure_capacity(self, spec=None, T: int = 16, seconds: float = 0.3) -> float:
+        """The capacity the ring's planner apportions layers by, in the
+        reference's unit: verified 32x64x64 GEMMs per second (app.js
+        measureCapacity, :508-519).  Without ``spec`` it is that probe itself
+        (vgemmBlock of the same X = sin(i)/2, W = cos(i)/2, each call waited
+        for).  With a model ``spec`` it is measured at the real shapes: the
+        four projection GEMMs of a T-row chunk (QKV, O, gate/up, down) on
+        device-resident int8 weights, back to back, as MACs per second over the
+        probe's 32*64*64 MACs -- the unit shard.estimate_lap_ms divides by."""
+        import time
+
+        import torch
+        from .shard import UNIT_MACS
+        dev = torch.device("cuda", self.device)
+        if spec is None:
+            m, k, n = 32, 64, 64
+            X = torch.from_numpy((np.sin(np.arange(m * k)) * 0.5).astype(np.float32)).to(dev)
+            w = self.register_weight((np.cos(np.arange(k * n)) * 0.5).astype(np.float32), k, n)
+            out = torch.empty(m * n, dtype=torch.float32, device=dev)
+            self.vgemm_dev(X, m, w, 0, out)
+            self.sync()
+            t0, it = time.perf_counter(), 0
+            while time.perf_counter() - t0 < seconds:
+                self.vgemm_dev(X, m, w, 0, out)
+                self.sync()
+                it += 1
+            return it / (time.perf_counter() - t0)
+        C_, hd = spec.hidden, spec.headDim or spec.hidden // spec.heads
+        q, kv, I_ = spec.heads * hd, spec.kvHeads * hd, spec.inter
+        g = torch.Generator(device=dev)
+        g.manual_seed(0x5EED)
+        ops = []
+        for k, n in ((C_, q + 2 * kv), (q, C_), (C_, 2 * I_), (I_, C_)):
+            ld = (k + 15) // 16 * 16
+            wt = torch.randint(-127, 128, (n, ld), dtype=torch.int8, device=dev, generator=g)
+            xq = torch.randint(-127, 128, (T, ld), dtype=torch.int8, device=dev, generator=g)
+            cs = torch.rand(n, device=dev, generator=g) * 1e-3
+            rs = torch.rand(T, device=dev, generator=g)
+            out = torch.empty(T * n, dtype=torch.float32, device=dev)
+            ops.append((xq, ld, wt, rs, cs, k, n, out))
+
+        def one_pass():
+            for xq, ld, wt, rs, cs, k, n, out in ops:
+                self.bgemm_dev(xq, ld, wt, ld, rs, cs, T, k, n, 1, 0, out)
+
+        one_pass()
+        self.sync()
+        t0, passes = time.perf_counter(), 0
+        while True:
+            for _ in range(8):
+                one_pass()
+            passes += 8
+            self.sync()
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        macs = T * sum(k * n for _, _, _, _, _, k, n, _ in ops)
+        return macs * passes / UNIT_MACS / el
+
     def kernel_probe(self) -> int:
         """kernelProbe's int32 hash (webgpu.js:1047-1055, before the math fold)."""
         h = C.c_uint32()

@@ -7,7 +7,10 @@ pipeline calls around its compute core:
   by measured capacity; stage 0 is the head; empty non-head stages dropped;
 * ``prefill_chunks`` (shard.js:345-361): even prompt chunks, ``window`` in flight;
 * ``prompt_lookup_draft`` (:366-385), ``lookahead_frame`` (:391-398),
-  ``accept_draft`` (:530-536) and ``draft_rows`` (infer.js:371-380).
+  ``accept_draft`` (:530-536) and ``draft_rows`` (infer.js:371-380);
+* ``ring_members`` (:215-222), ``estimate_lap_ms`` / ``estimate_plan_ms``
+  (:224-256), ``head_can_hold`` / ``prefer_local`` (:258-272): who joins the
+  ring, the lap-time budget check, and whether the head runs alone.
 """
 from __future__ import annotations
 
@@ -100,3 +103,55 @@ def draft_rows(T: int, seq_len: int, draft_len: int) -> list:
             break
         rows.append(T - seq_len + tok)
     return rows
+
+
+def ring_members(caps: list, probe_hash=None) -> list:
+    """shard.js ringMembers: peers whose kernel probe disagrees with the head's
+    are left out; the head (first) is always kept; a peer without a probe yet
+    is not a disagreement."""
+    if not caps:
+        return []
+    head, rest = caps[0], caps[1:]
+    return [head] + [d for d in rest if not probe_hash or not d.get("probe") or d["probe"] == probe_hash]
+
+
+UNIT_MACS = 32 * 64 * 64  # the capacity probe's verified GEMM (app.js:508-519)
+
+
+def estimate_lap_ms(spec, T: int, gemm_per_sec: float) -> float:
+    """shard.js estimateLapMs: the MACs of one T-row window through every
+    layer, in capacity-probe units, at ``gemm_per_sec`` units per second."""
+    C = spec.hidden
+    inter = spec.inter or C * 4
+    hd = spec.headDim or C // spec.heads
+    q = spec.heads * hd
+    kv = (spec.kvHeads or spec.heads) * hd
+    mac_per_layer = (T * C * q + 2 * T * C * kv + T * q * C + 3 * T * C * inter
+                     + spec.heads * (T * hd * T + T * T * hd))
+    gemms = mac_per_layer * spec.layers / UNIT_MACS
+    return gemms / max(gemm_per_sec, 1e-6) * 1000.0
+
+
+def estimate_plan_ms(spec, T: int, stages: list) -> float:
+    """shard.js estimatePlanMs: each stage pays for the layers it holds at its
+    own capacity; a head without layers pays 5 % for embedding and readout."""
+    layers = max(spec.layers, 1)
+    ms = 0.0
+    for s in stages:
+        owned = max(0, int(s.get("hi", 0)) - int(s.get("lo", 0)))
+        share = owned / layers if owned > 0 else (0.05 if s.get("head") else 0.0)
+        ms += estimate_lap_ms(spec, T, s.get("capacity") or 0) * share
+    return ms
+
+
+def head_can_hold(tensors, device_gb: float) -> bool:
+    """shard.js headCanHold: the whole model as f32 under a quarter of the
+    device's memory; unknown memory says no (the ring is used)."""
+    if not device_gb or device_gb <= 0:
+        return False
+    return sum(t["elems"] * 4 for t in tensors) < device_gb * 0.25 * 1073741824
+
+
+def prefer_local(prompt_tokens: int, peer_count: int, fits: bool) -> bool:
+    """shard.js preferLocal: run on the head alone when it can hold the model."""
+    return bool(fits and peer_count > 0 and prompt_tokens > 0)

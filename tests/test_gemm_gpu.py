@@ -125,3 +125,14 @@ def test_gemm_sweep_full_size(comp, O, P, M, K, N):
         Xs = X.reshape(M, K)[rows].reshape(-1)
         want = O.bgemm(Xs, W, rs[rows], cs, len(rows), K, N, 1, f).reshape(len(rows), N)
         assert got[rows].tobytes() == want.tobytes(), (M, K, N, f)
+
+
+def test_capacity_probe_and_real_shapes(comp, P):
+    """measureCapacity (app.js:508-519) in the reference's unit, and at a model's
+    real shapes; the planner apportions layers by these numbers."""
+    unit = comp.measure_capacity(seconds=0.05)
+    spec = P.infer.Spec(hidden=512, layers=4, heads=8, kvHeads=4, inter=1536, vocab=1000)
+    real = comp.measure_capacity(spec, T=16, seconds=0.05)
+    assert unit > 100 and real > unit  # a waited-for 32x64x64 call vs streamed layer GEMMs
+    plan = P.shard.plan_stages(spec.layers, [dict(id="gpu", capacity=real), dict(id="peer", capacity=unit)])
+    assert plan[0]["hi"] - plan[0]["lo"] >= plan[-1]["hi"] - plan[-1]["lo"]
