@@ -206,8 +206,7 @@ def build_rank(P, comp, w: dict, rank: int, world: int):
     else:
         max_rows, max_pos = w["T"], w["T"]
     S = P.infer.Stage(comp, spec, st["lo"], st["hi"], head=(rank == 0), max_rows=max_rows, max_pos=max_pos)
-    import __graft_entry__ as G
-    S.synth(MODEL_SEED, G.oracle().SYNTH_FACTOR)
+    S.synth(MODEL_SEED, P.infer.SYNTH_FACTOR)
     dev = torch.device("cuda", comp.device)
     ring = P.pipeline.Ring(S, rank, world, spec.hidden, P.pipeline.TorchP2P() if world > 1 else None,
                            new_buffer=lambda n: torch.empty(n, dtype=torch.float32, device=dev))

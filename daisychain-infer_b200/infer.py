@@ -15,12 +15,19 @@ for a non-finite activation, as runLayers does (:279-281).
 from __future__ import annotations
 
 import ctypes as C
+import math
 from dataclasses import dataclass
 
 import numpy as np
 
 from . import _lib, shard
 from ._lib import DcSpec, raise_for
+
+
+# Synthetic benchmark weights: a sum of four uniform 32-bit draws (variance
+# 4 * 2^64 / 12), centred, scaled once to standard deviation 0.02.
+SYNTH_STD = 0.02
+SYNTH_FACTOR = SYNTH_STD / (math.sqrt(4.0 / 12.0) * 4294967296.0)
 
 
 @dataclass
@@ -138,7 +145,11 @@ class Stage:
         from . import safetensors
         self.load(safetensors.read_stage_weights(path, self.spec, self.lo, self.hi, self.head))
 
-    def synth(self, model_seed: int, factor: float) -> None:
+    def synth(self, model_seed: int, factor: float | None = None) -> None:
+        """Random-init weights of the synthetic benchmark models, generated on
+        the GPU (``dc_stage_synth``); ``factor`` defaults to SYNTH_FACTOR."""
+        if factor is None:
+            factor = SYNTH_FACTOR
         self._check(self.L.dc_stage_synth(self.h, model_seed, float(factor)), "stage_synth")
 
     # ---- the pass -----------------------------------------------------------------

@@ -49,3 +49,9 @@ def test_head_holds_the_model_under_a_quarter_of_its_memory(S):
 def test_plan_follows_measured_capacity(S):
     plan = S.plan_stages(32, [dict(id="b200", capacity=3.0e6), dict(id="laptop", capacity=1.0e6)])
     assert [(p["lo"], p["hi"]) for p in plan] == [(0, 24), (24, 32)]
+
+
+def test_synthetic_weight_scale_matches_the_oracle(P, O):
+    """The benchmark models' weight scale is the package's own constant; the
+    oracle's restatement of the generator uses the same one."""
+    assert P.infer.SYNTH_FACTOR == O.SYNTH_FACTOR and P.infer.SYNTH_STD == O.SYNTH_STD
