@@ -38,6 +38,9 @@
  * Build: oracle/Makefile (gcc -O2 -ffp-contract=off, no -march, so no FMA
  * contraction and every double/float operation rounds exactly once).
  */
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 #include <math.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -56,6 +59,10 @@
 
 /* floor((2^31 - 1) / (128 * 128)) -- verified_core.js:41 */
 #define ORC_MAX_INT32_K 131071
+
+/* Parallel loops (OpenMP) only above this much work; smaller calls stay serial. */
+#define PAR_MIN (1 << 16)
+#define BGEMM_JB 512
 
 static double bits2d(uint64_t u) { double d; memcpy(&d, &u, 8); return d; }
 static uint64_t d2bits(double d) { uint64_t u; memcpy(&u, &d, 8); return u; }
@@ -103,6 +110,7 @@ void orc_make_luts(int16_t* mul, int8_t* requant, int8_t* relu) {
  * uses that double; only the stored copy s[r] is rounded to f32. */
 int orc_quantize_rows(const float* X, int64_t rows, int64_t cols, int8_t* q, float* s) {
   if (orc_first_nonfinite(X, rows * cols) >= 0) return ORC_E_NONFINITE;
+#pragma omp parallel for schedule(static) if (rows * cols >= PAR_MIN)
   for (int64_t r = 0; r < rows; r++) {
     const float* x = X + r * cols;
     double mx = 0.0;
@@ -122,6 +130,7 @@ int orc_quantize_rows(const float* X, int64_t rows, int64_t cols, int8_t* q, flo
  * the f32-ROUNDED scale (the asymmetry with quantizeRows is real). */
 int orc_quantize_cols(const float* W, int64_t rows, int64_t cols, int8_t* q, float* s) {
   if (orc_first_nonfinite(W, rows * cols) >= 0) return ORC_E_NONFINITE;
+#pragma omp parallel for schedule(static) if (rows * cols >= PAR_MIN)
   for (int64_t c = 0; c < cols; c++) {
     double mx = 0.0;
     for (int64_t r = 0; r < rows; r++) {
@@ -132,6 +141,7 @@ int orc_quantize_cols(const float* W, int64_t rows, int64_t cols, int8_t* q, flo
     if (!(sc > 1e-8)) sc = 1e-8;
     s[c] = (float)sc;
   }
+#pragma omp parallel for schedule(static) if (rows * cols >= PAR_MIN)
   for (int64_t r = 0; r < rows; r++)
     for (int64_t c = 0; c < cols; c++)
       q[r * cols + c] = clamp8(js_round((double)W[r * cols + c] / (double)s[c]));
@@ -155,42 +165,59 @@ int orc_bgemm(const int8_t* Xq, const int8_t* Wq, const float* rs, const float* 
               void* out) {
   if (m < 0 || k < 0 || n < 0 || batch < 1) return ORC_E_INVAL;
   if (orc_acc_bound(k)) return ORC_E_ACCBOUND;
-  int32_t* acc = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n > 0 ? n : 1));
-  if (!acc) return ORC_E_NOMEM;
+  /* Each (row, block of BGEMM_JB columns) is one task: its int32 sums run over
+   * p in order (each output element is computed by one thread, so the result
+   * does not depend on the thread count). */
+  const int nb = (n + BGEMM_JB - 1) / BGEMM_JB;
+  const int64_t work = (int64_t)batch * m * k * n;
   for (int bz = 0; bz < batch; bz++) {
     const int8_t* xb = Xq + (int64_t)bz * m * k;
     const int8_t* wb = Wq + (int64_t)bz * k * n;
+#pragma omp parallel for collapse(2) schedule(static) if (work >= PAR_MIN)
     for (int i = 0; i < m; i++) {
-      memset(acc, 0, sizeof(int32_t) * (size_t)n);
-      const int8_t* xr = xb + (int64_t)i * k;
-      for (int p = 0; p < k; p++) {
-        const int16_t* row = mul + ((uint8_t)xr[p]) * 256;
-        const int8_t* wr = wb + (int64_t)p * n;
-        for (int j = 0; j < n; j++) acc[j] = (int32_t)((uint32_t)acc[j] + (uint32_t)(int32_t)row[(uint8_t)wr[j]]);
-      }
-      int64_t orow = ((int64_t)bz * m + i) * n;
-      if (flags & ORC_ACC) {
-        memcpy((int32_t*)out + orow, acc, sizeof(int32_t) * (size_t)n);
-      } else if (flags & ORC_REQUANT) {
-        int8_t* o = (int8_t*)out + orow;
-        for (int j = 0; j < n; j++) {
-          int32_t a = acc[j] < -32768 ? -32768 : acc[j] > 32767 ? 32767 : acc[j];
-          int8_t v = requant[(uint16_t)(int16_t)a];
-          if (flags & ORC_RELU) v = relu[(uint8_t)v];
-          o[j] = v;
+      for (int jbk = 0; jbk < nb; jbk++) {
+        const int j0 = jbk * BGEMM_JB, j1 = j0 + BGEMM_JB < n ? j0 + BGEMM_JB : n;
+        int32_t acc[BGEMM_JB];
+        memset(acc, 0, sizeof(acc));
+        const int8_t* xr = xb + (int64_t)i * k;
+        for (int p = 0; p < k; p++) {
+          const int16_t* row = mul + ((uint8_t)xr[p]) * 256;
+          const int8_t* wr = wb + (int64_t)p * n;
+          for (int j = j0; j < j1; j++)
+            acc[j - j0] = (int32_t)((uint32_t)acc[j - j0] + (uint32_t)(int32_t)row[(uint8_t)wr[j]]);
         }
-      } else {
-        float* o = (float*)out + orow;
-        float rsc = rs[(int64_t)bz * m + i];
-        for (int j = 0; j < n; j++) {
-          float v = orc_epi(acc[j], rsc, cs[(int64_t)bz * n + j]);
-          o[j] = ((flags & ORC_RELU) && v < 0.0f) ? 0.0f : v;
+        int64_t orow = ((int64_t)bz * m + i) * n;
+        if (flags & ORC_ACC) {
+          memcpy((int32_t*)out + orow + j0, acc, sizeof(int32_t) * (size_t)(j1 - j0));
+        } else if (flags & ORC_REQUANT) {
+          int8_t* o = (int8_t*)out + orow;
+          for (int j = j0; j < j1; j++) {
+            int32_t a = acc[j - j0] < -32768 ? -32768 : acc[j - j0] > 32767 ? 32767 : acc[j - j0];
+            int8_t v = requant[(uint16_t)(int16_t)a];
+            if (flags & ORC_RELU) v = relu[(uint8_t)v];
+            o[j] = v;
+          }
+        } else {
+          float* o = (float*)out + orow;
+          float rsc = rs[(int64_t)bz * m + i];
+          for (int j = j0; j < j1; j++) {
+            float v = orc_epi(acc[j - j0], rsc, cs[(int64_t)bz * n + j]);
+            o[j] = ((flags & ORC_RELU) && v < 0.0f) ? 0.0f : v;
+          }
         }
       }
     }
   }
-  free(acc);
   return ORC_OK;
+}
+
+/* Threads the parallel loops above may use (1 without OpenMP). */
+int orc_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
 }
 
 /* ---- exp: fdlibm 5.3 method (Sun Microsystems, 1993) ------------------------

@@ -104,6 +104,7 @@ def lib():
         "orc_logits_rows": (i32, [p, p, i32, p, i32, p]),
         "orc_argmax": (i32, [p, i32]),
         "orc_fnv1a": (u32, [p, i64]),
+        "orc_threads": (i32, []),
         "orc_probe_inputs": (None, [p, p]),
         "orc_mulberry_fill": (None, [u32, i64, d, p]),
         "orc_synth_fill": (None, [C.c_uint64, i64, i64, d, p]),
@@ -219,6 +220,11 @@ def swiglu(g, u):
     out = np.empty_like(g)
     lib().orc_swiglu(_p(g), _p(u), g.size, _p(out))
     return out
+
+
+def threads() -> int:
+    """Threads the C restatement's parallel loops use (OpenMP; 1 without it)."""
+    return int(lib().orc_threads())
 
 
 def fnv1a(b: bytes | np.ndarray) -> int:
