@@ -151,7 +151,11 @@ def resolver(available):
 def stage_tensors(header: dict, spec, lo: int, hi: int, head: bool) -> dict:
     """Role -> tensor entry for one stage (arch.js tensorsFor, :141-157)."""
     resolve = resolver(header["tensors"])
-    pick = lambda n, opt=False: (lambda r: header["tensors"][r] if r else None)(resolve(n, opt))
+
+    def pick(name, optional=False):
+        r = resolve(name, optional)
+        return header["tensors"][r] if r else None
+
     out = {}
     if head:
         h = head_tensors(spec.tie)
