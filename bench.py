@@ -364,8 +364,10 @@ def bench_model(args, rank, world, peaks):
                     roofline=roof, kernels=other, gpu_launches=launches, clocks=clk, backend=comp.label,
                     generated_ids_fnv=P_fnv(gen_ids), generated_head=gen_ids[:8],
                     weights_gb=weight_bytes(spec, 0, spec.layers, True) / 1e9)
-    if rank == 0 and world == 1 and not args.no_e2e:
-        line["e2e"] = e2e_model(comp, ring, w, ids, args)
+    if not args.no_e2e:  # every rank takes part in the ring; rank 0 reports
+        e2e = e2e_model(comp, ring, w, ids, args, world)
+        if rank == 0:
+            line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_model_baseline(w)
     if world > 1:
@@ -375,25 +377,29 @@ def bench_model(args, rank, world, peaks):
     return line
 
 
-def e2e_model(comp, ring, w, ids, args):
+def e2e_model(comp, ring, w, ids, args, world=1):
     """Through the public API with host buffers: the prompt ids come from pinned
-    host memory each step, the generated ids go back to host memory."""
+    host memory each step, the generated ids go back to host memory (on the
+    head).  Every rank runs its part of the ring; the time is the max over
+    ranks (the head's lap spans the others')."""
     import torch
     host_ids = torch.tensor(ids, dtype=torch.int32).pin_memory()
     steps = max(1, min(args.steps, 3))
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     out = None
+    barrier(world)
+    torch.cuda.synchronize()
     t0.record()
     for _ in range(steps):
         prompt = host_ids.tolist()
         if w["mode"] == "chunked":
             picks = ring.generate_chunked(prompt, w["new"], w["chunk"], w["window"])
-            out = picks.cpu()
+            out = picks.cpu() if picks is not None else None
         else:
             out = ring.generate_lookahead(prompt, w["new"], w["T"], 4)
     t1.record()
     torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1) / steps
+    ms = max_over_ranks([t0.elapsed_time(t1) / steps], world)[0]
     n_new = w["new"]
     return dict(value=n_new / (ms / 1e3), unit="tok/s (prompt to generated ids, prefill included)",
                 h2d_bytes_per_step=4 * len(ids), d2h_bytes_per_step=4 * n_new, ms_per_step=ms,
