@@ -20,7 +20,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import _lib, shard
+from . import shard
 from ._lib import DcSpec, raise_for
 
 

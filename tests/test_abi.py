@@ -17,7 +17,6 @@ def declared_functions():
 
 
 def test_every_declared_symbol_is_exported(P):
-    from importlib import import_module
     lib = ctypes.CDLL(P._lib.LIB_PATH)
     names = declared_functions()
     assert len(names) >= 20

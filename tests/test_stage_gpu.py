@@ -171,7 +171,6 @@ def test_lookahead_matches_oracle(comp, O, P, fixture):
 
 
 def test_non_finite_activation_refused(comp, P, fixture):
-    import torch
     ospec, spec, w, om = fixture
     st = make_stages(P, comp, spec, w, [6])
     x = st[0].embed_rows(win_of(PROMPT))
