@@ -6,22 +6,27 @@ LUT content = the LFS object ids of public/*_lut.bin; mul[7,-3] = -21
 (test_pipeline.js:405-429); bgemm exactness (webgpu.js:470-492 gates).
 """
 import hashlib
+import json
 import math
+import os
 
 import numpy as np
 import pytest
 
-MUL_OID = "5cecff7e22049d0083ad9ee36dcf0695222c61621bacfd5a401c7b133abe892d"
-REQUANT_OID = "173444ecfa293433329a333289983a665c481d913e9fd1c2778b55380ca4dd31"
-RELU_OID = "2acb03ba7520467636273208563f8e733494748f4aa5ac2dba89d9560050da79"
+# the reference's LFS object ids and sizes of public/*_lut.bin and its
+# luts_meta.json, as tests/golden/make_golden.py read them
+GOLDEN = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "luts.json")))
 
 
 def test_luts_match_lfs_object_ids(O):
     mul, req, relu = O.make_luts()
-    assert mul.nbytes == 131072 and req.nbytes == 65536 and relu.nbytes == 256
-    assert hashlib.sha256(mul.astype("<i2").tobytes()).hexdigest() == MUL_OID
-    assert hashlib.sha256(req.tobytes()).hexdigest() == REQUANT_OID
-    assert hashlib.sha256(relu.tobytes()).hexdigest() == RELU_OID
+    tables = {"mul": mul.astype("<i2").tobytes(), "requant": req.tobytes(), "relu": relu.tobytes()}
+    for name, raw in tables.items():
+        assert len(raw) == GOLDEN[name]["size"], name
+        assert hashlib.sha256(raw).hexdigest() == GOLDEN[name]["oid"], name
+    meta = GOLDEN["meta"]
+    assert list(mul.shape) in ([meta["mul"][0] * meta["mul"][1]], meta["mul"])
+    assert req.size == meta["requant"] and relu.size == meta["relu"] and meta["shift"] == 8
     assert mul[(7 & 0xFF) * 256 + (-3 & 0xFF)] == -21
 
 
