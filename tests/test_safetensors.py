@@ -1,7 +1,8 @@
 """safetensors model files for the stages (public/safetensors.js, arch.js
 names, shard.js toKN), checked on CPU: a written model reads back bit for bit
 at every stage split, only a stage's byte ranges are read, the widenings are
-exact, and malformed headers are refused as test_loader.js expects."""
+exact, malformed headers are refused, and the known answers of the
+reference's own loader tests (test_loader.js:24-126) hold."""
 import dataclasses
 import json
 import struct
@@ -130,3 +131,83 @@ def test_fingerprint_of_a_file(P, O, ST, tmp_path):
     t2 = dict(t)
     t2.pop("model.norm.weight")
     assert P.wire.model_fingerprint("test/llama", "main", t2) != a
+
+
+# ---- the reference's loader tests (test_loader.js:24-126), restated --------------------
+def build_file(entries):
+    """test_loader.js buildFile: [(name, dtype, shape, bytes)] -> a safetensors buffer."""
+    header, chunks, off = {}, [], 0
+    for name, dtype, shape, raw in entries:
+        header[name] = {"dtype": dtype, "shape": shape, "data_offsets": [off, off + len(raw)]}
+        chunks.append(raw)
+        off += len(raw)
+    hj = json.dumps(header).encode()
+    return struct.pack("<II", len(hj), 0) + hj + b"".join(chunks)
+
+
+def test_loader_parses_and_locates_every_tensor(ST):
+    buf = build_file([("w.a", "F32", [2, 2], np.array([1, 2, 3, 4], "<f4").tobytes()),
+                      ("w.b", "F32", [2], np.array([5, 6], "<f4").tobytes())])
+    t = ST.parse_header(buf)["tensors"]
+    assert len(t) == 2 and t["w.a"]["shape"] == [2, 2] and t["w.a"]["elems"] == 4
+    a, b = t["w.a"], t["w.b"]
+    assert list(ST.to_f32("F32", buf[a["start"]:a["end"]])) == [1, 2, 3, 4]
+    assert list(ST.to_f32("F32", buf[b["start"]:b["end"]])) == [5, 6]
+
+
+def test_loader_refuses_contradictions_and_junk(ST):
+    with pytest.raises(ValueError, match="expected"):
+        ST.parse_header(build_file([("w", "F32", [9, 9], np.arange(4, dtype="<f4").tobytes())]))
+    junk = bytearray(64)
+    junk[0:4] = struct.pack("<I", 16)
+    with pytest.raises(ValueError, match="not valid JSON|not a safetensors"):
+        ST.parse_header(bytes(junk))
+    big = bytearray(16)
+    big[4:8] = struct.pack("<I", 7)
+    with pytest.raises(ValueError, match="implausibly large"):
+        ST.parse_header(bytes(big))
+
+
+def test_loader_known_widenings(ST):
+    vals = np.array([1, -1, 0.5, -0.5, 2, 100, -0.0078125, 0], np.float32)
+    bf = (vals.view(np.uint32) >> 16).astype("<u2")
+    assert ST.to_f32("BF16", bf.tobytes()).tobytes() == vals.tobytes()
+    cases = [(0x3C00, 1.0), (0xBC00, -1.0), (0x3800, 0.5), (0x0000, 0.0), (0x8000, -0.0),
+             (0x0001, 2.0 ** -24), (0x7BFF, 65504.0)]
+    out = ST.to_f32("F16", np.array([c[0] for c in cases], "<u2").tobytes())
+    for (bits, want), got in zip(cases, out):
+        assert got == want and np.signbit(got) == np.signbit(want), hex(bits)
+
+
+def test_loader_coalescing_keeps_offsets(ST):
+    mk = lambda s, e: dict(start=s, end=e, bytes=e - s, elems=(e - s) // 4, dtype="F32", name=f"t{s}")
+    runs = ST.coalesce([mk(0, 100), mk(100, 200), mk(10_000_000, 10_000_100)], 1024)
+    assert len(runs) == 2 and (runs[0]["start"], runs[0]["end"]) == (0, 200) and len(runs[0]["tensors"]) == 2
+    assert (runs[1]["start"], runs[1]["end"]) == (10_000_000, 10_000_100)
+    assert runs[0]["tensors"][1]["start"] - runs[0]["start"] == 100
+
+
+def test_stage_byte_cost_from_the_header_alone(P, ST):
+    spec = P.infer.Spec(hidden=64, layers=4, heads=4, kvHeads=4, inter=128, vocab=100)
+    tensors = {}
+
+    def add(name, elems):
+        tensors[name] = dict(name=name, elems=elems, bytes=elems * 2, dtype="BF16", shape=[elems], start=0, end=0)
+
+    h = ST.head_tensors(True)
+    add(h["emb"], 100 * 64)
+    add(h["nrmF"], 64)
+    for l in range(4):
+        lt = ST.layer_tensors(l)
+        add(lt["nrm1"], 64)
+        add(lt["nrm2"], 64)
+        for r in ("Wq", "Wk", "Wv", "Wo"):
+            add(lt[r], 64 * 64)
+        add(lt["Wgate"], 128 * 64)
+        add(lt["Wup"], 128 * 64)
+        add(lt["Wdown"], 64 * 128)
+    header = {"tensors": tensors}
+    mid = ST.f32_bytes(t for t in ST.stage_tensors(header, spec, 1, 2, False).values() if t)
+    head = ST.f32_bytes(t for t in ST.stage_tensors(header, spec, 0, 1, True).values() if t)
+    assert mid == (4 * 64 * 64 + 3 * 128 * 64 + 2 * 64) * 4
+    assert head > mid
