@@ -117,3 +117,12 @@ def test_transport_refuses_bad_frames(W):
         hop(W, 0, 2, x)                         # a frame for stage 1 arriving at stage 2
     with pytest.raises(ValueError, match="token index"):
         hop(W, 0, 1, x, tok=16, tok_due=32)
+
+
+def test_sentinels_and_the_solo_ring(W, P):
+    """test_wire.js:192-205: the activation tag is negative and outside the
+    -2..-8 range of DaisyChain-Web; RETURN is not a stage index; a one-stage
+    ring returns to itself at once."""
+    assert W.ACT == -23 and W.ACT <= -20 and W.RETURN == -1
+    hop = P.pipeline.route_after([dict(id="p0", index=0)], 0)
+    assert hop["isReturn"] and hop["to"] == "p0" and hop["address"] == W.RETURN
