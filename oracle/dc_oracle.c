@@ -41,6 +41,10 @@
 #ifdef _OPENMP
 #include <omp.h>
 #endif
+#if defined(__x86_64__) && defined(__GNUC__)
+#include <immintrin.h>
+#define ORC_X86 1
+#endif
 #include <math.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -278,8 +282,10 @@ double orc_exp(double x) {
 }
 
 /* ---- elementwise pieces of layerForward ----------------------------------- */
-/* infer.js:30-39: s accumulates v*v in double, sequentially from j = 0. */
+/* infer.js:30-39: s accumulates v*v in double, sequentially from j = 0.  Rows
+ * are independent; each row's sum runs serially on one thread. */
 void orc_rmsnorm(const float* x, int rows, int C, const float* w, double eps, float* y) {
+#pragma omp parallel for schedule(static) if ((int64_t)rows * C >= PAR_MIN)
   for (int r = 0; r < rows; r++) {
     const float* xr = x + (int64_t)r * C;
     double s = 0.0;
@@ -343,6 +349,7 @@ void orc_softmax_causal(const float* scores, int T, int N, int n0, double scale,
 
 /* infer.js:59 + :212: f32(silu(g) * u), silu(v) = v / (1 + exp(-v)) in double. */
 void orc_swiglu(const float* g, const float* u, int64_t n, float* out) {
+#pragma omp parallel for schedule(static) if (n >= PAR_MIN)
   for (int64_t i = 0; i < n; i++) {
     double v = g[i];
     double s = v / (1.0 + orc_exp(-v));
@@ -351,27 +358,6 @@ void orc_swiglu(const float* g, const float* u, int64_t n, float* out) {
 }
 
 /* ---- vgemmBlock (verified_core.js:425-449), batch 1 ------------------------ */
-typedef struct {
-  int k, n;
-  int8_t* q; /* k x n row-major, as quantizeCols returns it */
-  float* s;  /* n */
-} orc_wq;
-
-static int wq_build(orc_wq* w, const float* Wf, int k, int n) {
-  w->k = k;
-  w->n = n;
-  w->q = (int8_t*)malloc((size_t)k * n + 1);
-  w->s = (float*)malloc(sizeof(float) * (size_t)n + 4);
-  if (!w->q || !w->s) return ORC_E_NOMEM;
-  return orc_quantize_cols(Wf, k, n, w->q, w->s);
-}
-static void wq_free(orc_wq* w) {
-  free(w->q);
-  free(w->s);
-  w->q = NULL;
-  w->s = NULL;
-}
-
 static int16_t g_mul[65536];
 static int8_t g_requant[65536], g_relu[256];
 static int g_luts_ready = 0;
@@ -382,6 +368,233 @@ static void luts_init(void) {
   }
 }
 
+typedef struct {
+  int k, n;
+  int8_t* q;  /* k x n row-major, as quantizeCols returns it (LUT path) */
+  int8_t* qt; /* n x k: the same values transposed (exact-product path) */
+  float* s;   /* n */
+} orc_wq;
+
+static int wq_build(orc_wq* w, const float* Wf, int k, int n) {
+  w->k = k;
+  w->n = n;
+  w->qt = NULL;
+  w->q = (int8_t*)malloc((size_t)k * n + 1);
+  w->s = (float*)malloc(sizeof(float) * (size_t)n + 4);
+  if (!w->q || !w->s) return ORC_E_NOMEM;
+  return orc_quantize_cols(Wf, k, n, w->q, w->s);
+}
+static void wq_free(orc_wq* w) {
+  free(w->q);
+  free(w->qt);
+  free(w->s);
+  w->q = NULL;
+  w->qt = NULL;
+  w->s = NULL;
+}
+
+/* ---- the exact-product path (golden fixtures at full model size) ------------
+ * bgemmJS adds mul-LUT entries in int32.  The mul unit is the exact product of
+ * its two int8 indices (its sha256 equals the reference's LFS object id), and
+ * k <= 131071 keeps every partial sum inside int32, so the accumulator is the
+ * exact integer dot product whatever the order of its terms.  This path forms
+ * that dot product directly, over a weight held transposed (n x k), with
+ * AVX-512 where the CPU has it.  The quantisers and the epilogue are the
+ * functions above, unchanged; tests check this path against the LUT path. */
+
+/* quantizeCols (verified_core.js:122-136) writing qt = the quantised Wᵀ (cols x
+ * rows).  Same arithmetic as orc_quantize_cols: absmax in double, f32 scale,
+ * quotient by the f32-rounded scale. */
+int orc_quantize_cols_t(const float* W, int64_t rows, int64_t cols, int8_t* qt, float* s) {
+  if (orc_first_nonfinite(W, rows * cols) >= 0) return ORC_E_NONFINITE;
+#pragma omp parallel for schedule(static) if (rows * cols >= PAR_MIN)
+  for (int64_t cb = 0; cb < cols; cb += 256) {
+    const int64_t ce = cb + 256 < cols ? cb + 256 : cols;
+    double mx[256];
+    for (int64_t c = cb; c < ce; c++) mx[c - cb] = 0.0;
+    for (int64_t r = 0; r < rows; r++) {
+      const float* wr = W + r * cols;
+      for (int64_t c = cb; c < ce; c++) {
+        double a = fabs((double)wr[c]);
+        if (a > mx[c - cb]) mx[c - cb] = a;
+      }
+    }
+    for (int64_t c = cb; c < ce; c++) {
+      double sc = mx[c - cb] / 127.0;
+      if (!(sc > 1e-8)) sc = 1e-8;
+      s[c] = (float)sc;
+    }
+  }
+  const int64_t nrb = (rows + 63) / 64, ncb = (cols + 63) / 64;
+#pragma omp parallel for schedule(static) if (rows * cols >= PAR_MIN)
+  for (int64_t t = 0; t < nrb * ncb; t++) {
+    const int64_t r0 = (t % nrb) * 64, c0 = (t / nrb) * 64;
+    const int64_t r1 = r0 + 64 < rows ? r0 + 64 : rows, c1 = c0 + 64 < cols ? c0 + 64 : cols;
+    for (int64_t c = c0; c < c1; c++) {
+      const double sc = (double)s[c];
+      for (int64_t r = r0; r < r1; r++) qt[c * rows + r] = clamp8(js_round((double)W[r * cols + c] / sc));
+    }
+  }
+  return ORC_OK;
+}
+
+static int cpu_avx512(void) {
+#ifdef ORC_X86
+  static int v = -1;
+  if (v < 0) {
+    __builtin_cpu_init();
+    v = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+        __builtin_cpu_supports("avx512vl");
+  }
+  return v;
+#else
+  return 0;
+#endif
+}
+
+/* acc[i*n + j] = sum_p X16[i*kp + p] * Wt[j*k + p] for columns [j0, j1).  X16
+ * is the activation widened to int16 and zero-padded to kp (a multiple of 32). */
+static void idot_cols_generic(const int16_t* X16, int m, int kp, int k, const int8_t* Wt, int j0, int j1,
+                              int32_t* acc, int n) {
+  (void)kp;
+  for (int j = j0; j < j1; j++) {
+    const int8_t* w = Wt + (int64_t)j * k;
+    for (int i = 0; i < m; i++) {
+      const int16_t* x = X16 + (int64_t)i * kp;
+      int32_t t = 0;
+      for (int p = 0; p < k; p++) t += (int32_t)x[p] * (int32_t)w[p];
+      acc[(int64_t)i * n + j] = t;
+    }
+  }
+}
+
+#ifdef ORC_X86
+#define ORC_AVX512 __attribute__((target("avx512f,avx512bw,avx512vl")))
+ORC_AVX512 static inline __m512i wload(const int8_t* p, int left) {
+  const __mmask32 mk = left >= 32 ? (__mmask32)0xFFFFFFFFu : (__mmask32)((1u << left) - 1u);
+  return _mm512_cvtepi8_epi16(_mm256_maskz_loadu_epi8(mk, p));
+}
+#define MADD(a, x, w) a = _mm512_add_epi32(a, _mm512_madd_epi16(x, w))
+ORC_AVX512 static void idot_cols_avx512(const int16_t* X16, int m, int kp, int k, const int8_t* Wt, int j0, int j1,
+                                        int32_t* acc, int n) {
+  int j = j0;
+  for (; j + 4 <= j1; j += 4) {
+    const int8_t* w0 = Wt + (int64_t)j * k;
+    const int8_t *w1 = w0 + k, *w2 = w1 + k, *w3 = w2 + k;
+    int i = 0;
+    for (; i + 4 <= m; i += 4) {
+      const int16_t* x0 = X16 + (int64_t)i * kp;
+      const int16_t *x1 = x0 + kp, *x2 = x1 + kp, *x3 = x2 + kp;
+      __m512i a00 = _mm512_setzero_si512(), a01 = a00, a02 = a00, a03 = a00, a10 = a00, a11 = a00, a12 = a00,
+              a13 = a00, a20 = a00, a21 = a00, a22 = a00, a23 = a00, a30 = a00, a31 = a00, a32 = a00, a33 = a00;
+      for (int p = 0; p < k; p += 32) {
+        const __m512i b0 = wload(w0 + p, k - p), b1 = wload(w1 + p, k - p), b2 = wload(w2 + p, k - p),
+                      b3 = wload(w3 + p, k - p);
+        __m512i x = _mm512_loadu_si512((const void*)(x0 + p));
+        MADD(a00, x, b0); MADD(a01, x, b1); MADD(a02, x, b2); MADD(a03, x, b3);
+        x = _mm512_loadu_si512((const void*)(x1 + p));
+        MADD(a10, x, b0); MADD(a11, x, b1); MADD(a12, x, b2); MADD(a13, x, b3);
+        x = _mm512_loadu_si512((const void*)(x2 + p));
+        MADD(a20, x, b0); MADD(a21, x, b1); MADD(a22, x, b2); MADD(a23, x, b3);
+        x = _mm512_loadu_si512((const void*)(x3 + p));
+        MADD(a30, x, b0); MADD(a31, x, b1); MADD(a32, x, b2); MADD(a33, x, b3);
+      }
+      int32_t* o = acc + (int64_t)i * n + j;
+      o[0] = _mm512_reduce_add_epi32(a00); o[1] = _mm512_reduce_add_epi32(a01);
+      o[2] = _mm512_reduce_add_epi32(a02); o[3] = _mm512_reduce_add_epi32(a03);
+      o += n;
+      o[0] = _mm512_reduce_add_epi32(a10); o[1] = _mm512_reduce_add_epi32(a11);
+      o[2] = _mm512_reduce_add_epi32(a12); o[3] = _mm512_reduce_add_epi32(a13);
+      o += n;
+      o[0] = _mm512_reduce_add_epi32(a20); o[1] = _mm512_reduce_add_epi32(a21);
+      o[2] = _mm512_reduce_add_epi32(a22); o[3] = _mm512_reduce_add_epi32(a23);
+      o += n;
+      o[0] = _mm512_reduce_add_epi32(a30); o[1] = _mm512_reduce_add_epi32(a31);
+      o[2] = _mm512_reduce_add_epi32(a32); o[3] = _mm512_reduce_add_epi32(a33);
+    }
+    for (; i < m; i++) {
+      const int16_t* x0 = X16 + (int64_t)i * kp;
+      __m512i a0 = _mm512_setzero_si512(), a1 = a0, a2 = a0, a3 = a0;
+      for (int p = 0; p < k; p += 32) {
+        const __m512i x = _mm512_loadu_si512((const void*)(x0 + p));
+        MADD(a0, x, wload(w0 + p, k - p)); MADD(a1, x, wload(w1 + p, k - p));
+        MADD(a2, x, wload(w2 + p, k - p)); MADD(a3, x, wload(w3 + p, k - p));
+      }
+      int32_t* o = acc + (int64_t)i * n + j;
+      o[0] = _mm512_reduce_add_epi32(a0); o[1] = _mm512_reduce_add_epi32(a1);
+      o[2] = _mm512_reduce_add_epi32(a2); o[3] = _mm512_reduce_add_epi32(a3);
+    }
+  }
+  for (; j < j1; j++) {
+    const int8_t* w0 = Wt + (int64_t)j * k;
+    for (int i = 0; i < m; i++) {
+      const int16_t* x0 = X16 + (int64_t)i * kp;
+      __m512i a0 = _mm512_setzero_si512();
+      for (int p = 0; p < k; p += 32) MADD(a0, _mm512_loadu_si512((const void*)(x0 + p)), wload(w0 + p, k - p));
+      acc[(int64_t)i * n + j] = _mm512_reduce_add_epi32(a0);
+    }
+  }
+}
+#undef MADD
+#endif
+
+/* bgemmJS (batch 1) over a transposed weight Wt (n x k), exact products; the
+ * output rules (f32 epilogue, ReLU, int32, declared requant) are orc_bgemm's. */
+int orc_bgemm_t(const int8_t* Xq, const int8_t* Wt, const float* rs, const float* cs, int m, int k, int n,
+                unsigned flags, void* out) {
+  if (m < 0 || k < 0 || n < 0) return ORC_E_INVAL;
+  if (orc_acc_bound(k)) return ORC_E_ACCBOUND;
+  const int kp = ((k + 31) / 32) * 32;
+  int16_t* X16 = (int16_t*)calloc((size_t)m * kp + 32, sizeof(int16_t));
+  int32_t* acc = (flags & ORC_ACC) ? (int32_t*)out : (int32_t*)malloc(sizeof(int32_t) * ((size_t)m * n + 1));
+  if (!X16 || !acc) { free(X16); if (!(flags & ORC_ACC)) free(acc); return ORC_E_NOMEM; }
+  for (int64_t i = 0; i < m; i++)
+    for (int64_t p = 0; p < k; p++) X16[i * kp + p] = Xq[i * k + p];
+  const int simd = cpu_avx512();
+  const int JB = 64;
+  const int nb = (n + JB - 1) / JB;
+  const int64_t work = (int64_t)m * k * n;
+#pragma omp parallel for schedule(dynamic, 1) if (work >= PAR_MIN)
+  for (int b = 0; b < nb; b++) {
+    const int j0 = b * JB, j1 = j0 + JB < n ? j0 + JB : n;
+#ifdef ORC_X86
+    if (simd) { idot_cols_avx512(X16, m, kp, k, Wt, j0, j1, acc, n); continue; }
+#endif
+    idot_cols_generic(X16, m, kp, k, Wt, j0, j1, acc, n);
+  }
+  (void)simd;
+  if (!(flags & ORC_ACC)) {
+    luts_init();
+    for (int64_t i = 0; i < m; i++)
+      for (int64_t j = 0; j < n; j++) {
+        const int32_t a = acc[i * n + j];
+        if (flags & ORC_REQUANT) {
+          const int32_t c = a < -32768 ? -32768 : a > 32767 ? 32767 : a;
+          int8_t v = g_requant[(uint16_t)(int16_t)c];
+          if (flags & ORC_RELU) v = g_relu[(uint8_t)v];
+          ((int8_t*)out)[i * n + j] = v;
+        } else {
+          const float v = orc_epi(a, rs[i], cs[j]);
+          ((float*)out)[i * n + j] = ((flags & ORC_RELU) && v < 0.0f) ? 0.0f : v;
+        }
+      }
+    free(acc);
+  }
+  free(X16);
+  return ORC_OK;
+}
+
+/* qt built directly (the model's exact-product path keeps no k x n copy). */
+static int wq_build_t(orc_wq* w, const float* Wf, int k, int n) {
+  w->k = k;
+  w->n = n;
+  w->q = NULL;
+  w->qt = (int8_t*)malloc((size_t)k * n + 1);
+  w->s = (float*)malloc(sizeof(float) * (size_t)n + 4);
+  if (!w->qt || !w->s) return ORC_E_NOMEM;
+  return orc_quantize_cols_t(Wf, k, n, w->qt, w->s);
+}
+
 /* X (m x k f32) times a quantised weight -> out (m x n f32). */
 static int vgemm_wq(const float* X, int m, const orc_wq* w, float* out) {
   luts_init();
@@ -390,7 +603,9 @@ static int vgemm_wq(const float* X, int m, const orc_wq* w, float* out) {
   float* rs = (float*)malloc(sizeof(float) * (size_t)m + 4);
   if (!xq || !rs) { free(xq); free(rs); return ORC_E_NOMEM; }
   int rc = orc_quantize_rows(X, m, k, xq, rs);
-  if (rc == ORC_OK) rc = orc_bgemm(xq, w->q, rs, w->s, m, k, n, 1, 0, g_mul, g_requant, g_relu, out);
+  if (rc == ORC_OK)
+    rc = w->qt ? orc_bgemm_t(xq, w->qt, rs, w->s, m, k, n, 0, out)
+               : orc_bgemm(xq, w->q, rs, w->s, m, k, n, 1, 0, g_mul, g_requant, g_relu, out);
   free(xq);
   free(rs);
   return rc;
@@ -399,6 +614,14 @@ static int vgemm_wq(const float* X, int m, const orc_wq* w, float* out) {
 int orc_vgemm(const float* X, const float* Wf, int m, int k, int n, float* out) {
   orc_wq w;
   int rc = wq_build(&w, Wf, k, n);
+  if (rc == ORC_OK) rc = vgemm_wq(X, m, &w, out);
+  wq_free(&w);
+  return rc;
+}
+/* The same per-call vgemmBlock through the exact-product path. */
+static int vgemm_fast(const float* X, const float* Wf, int m, int k, int n, float* out) {
+  orc_wq w;
+  int rc = wq_build_t(&w, Wf, k, n);
   if (rc == ORC_OK) rc = vgemm_wq(X, m, &w, out);
   wq_free(&w);
   return rc;
@@ -421,8 +644,11 @@ typedef struct orc_model {
   int lm_quantized;
   orc_layer* L;
   int per_call_quant; /* 1: re-quantise weights on every GEMM, as vgemmBlock does */
+  int fast;           /* 1: the exact-product path, weights held transposed */
   float *rope_cos, *rope_sin;
   int rope_max;
+  float* own_ones;    /* synthetic models: the norm weights (all 1) */
+  float* own_emb;     /* synthetic models: the embedding */
 } orc_model;
 
 typedef struct {
@@ -461,10 +687,14 @@ void orc_model_free(orc_model* m) {
   free(m->L);
   free(m->rope_cos);
   free(m->rope_sin);
+  free(m->own_ones);
+  free(m->own_emb);
   free(m);
 }
 
 void orc_model_set_per_call_quant(orc_model* m, int on) { m->per_call_quant = on; }
+/* Weights quantised from now on go through the exact-product path. */
+void orc_model_set_fast(orc_model* m, int on) { m->fast = on; }
 
 /* Head tensors.  lm_kn == NULL means tied: lm_head = embᵀ (shard.js:92, 123-128). */
 int orc_model_set_head(orc_model* m, const float* emb, const float* nrmF, const float* lm_kn) {
@@ -498,13 +728,14 @@ static int layer_quantize(orc_model* m, orc_layer* y) {
   if (y->quantized) return ORC_OK;
   int C = m->hidden, q = m->heads * m->head_dim, kv = m->kv_heads * m->head_dim, I = m->inter;
   int rc = ORC_OK;
-  rc |= wq_build(&y->q, y->Wq, C, q);
-  rc |= wq_build(&y->k, y->Wk, C, kv);
-  rc |= wq_build(&y->v, y->Wv, C, kv);
-  rc |= wq_build(&y->o, y->Wo, q, C);
-  rc |= wq_build(&y->gate, y->Wgate, C, I);
-  rc |= wq_build(&y->up, y->Wup, C, I);
-  rc |= wq_build(&y->down, y->Wdown, I, C);
+  int (*build)(orc_wq*, const float*, int, int) = m->fast ? wq_build_t : wq_build;
+  rc |= build(&y->q, y->Wq, C, q);
+  rc |= build(&y->k, y->Wk, C, kv);
+  rc |= build(&y->v, y->Wv, C, kv);
+  rc |= build(&y->o, y->Wo, q, C);
+  rc |= build(&y->gate, y->Wgate, C, I);
+  rc |= build(&y->up, y->Wup, C, I);
+  rc |= build(&y->down, y->Wdown, I, C);
   y->quantized = 1;
   return rc ? ORC_E_NONFINITE : ORC_OK;
 }
@@ -556,6 +787,37 @@ void orc_kv_read(const orc_kv* c, int layer, float* k, float* v) {
   memcpy(v, y->v, sizeof(float) * (size_t)y->n * y->kv_dim);
 }
 
+/* One head of infer.js:171-197: the scores vgemmBlock (q_h x k_hᵀ), the causal
+ * softmax and the context vgemmBlock (a x v_h), written into the head's
+ * columns of ctxOut.  The buffers are the head's own, so heads may run on
+ * separate threads. */
+static int attn_head(int fast, int h, int group, const float* q, int qDim, const float* K, const float* Vv,
+                     int kvDim, int T, int N, int n0, int hd, double scale, float* ctxOut) {
+  int rc = ORC_OK;
+  const int kvh = h / group;
+  float* qh = (float*)malloc(sizeof(float) * (size_t)T * hd);
+  float* khT = (float*)malloc(sizeof(float) * (size_t)hd * N);
+  float* vh = (float*)malloc(sizeof(float) * (size_t)N * hd);
+  float* scores = (float*)malloc(sizeof(float) * (size_t)T * N);
+  float* a = (float*)malloc(sizeof(float) * (size_t)T * N);
+  float* oh = (float*)malloc(sizeof(float) * (size_t)T * hd);
+  int (*vg)(const float*, const float*, int, int, int, float*) = fast ? vgemm_fast : orc_vgemm;
+  if (!qh || !khT || !vh || !scores || !a || !oh) { rc = ORC_E_NOMEM; goto out; }
+  for (int t = 0; t < T; t++) memcpy(qh + (int64_t)t * hd, q + (int64_t)t * qDim + h * hd, sizeof(float) * hd);
+  for (int t = 0; t < N; t++)
+    for (int c = 0; c < hd; c++) {
+      khT[(int64_t)c * N + t] = K[(int64_t)t * kvDim + kvh * hd + c];
+      vh[(int64_t)t * hd + c] = Vv[(int64_t)t * kvDim + kvh * hd + c];
+    }
+  if ((rc = vg(qh, khT, T, hd, N, scores))) goto out;
+  orc_softmax_causal(scores, T, N, n0, scale, a);
+  if ((rc = vg(a, vh, T, N, hd, oh))) goto out;
+  for (int t = 0; t < T; t++) memcpy(ctxOut + (int64_t)t * qDim + h * hd, oh + (int64_t)t * hd, sizeof(float) * hd);
+out:
+  free(qh); free(khT); free(vh); free(scores); free(a); free(oh);
+  return rc;
+}
+
 /* infer.js:114-221, Llama block.  kvl == NULL is the full-window path. */
 static int layer_forward(orc_model* m, int li, float* x, int T, orc_kv_layer* kvl, int pos0) {
   orc_layer* y = &m->L[li];
@@ -572,7 +834,6 @@ static int layer_forward(orc_model* m, int li, float* x, int T, orc_kv_layer* kv
   float* g = (float*)malloc(sizeof(float) * (size_t)T * I);
   float* u = (float*)malloc(sizeof(float) * (size_t)T * I);
   float* tmpC = (float*)malloc(sizeof(float) * (size_t)T * C);
-  float *qh = NULL, *khT = NULL, *vh = NULL, *scores = NULL, *a = NULL, *oh = NULL;
   if (!h1 || !q || !k || !v || !ctxOut || !x2 || !g || !u || !tmpC) { rc = ORC_E_NOMEM; goto done; }
 
   orc_rmsnorm(x, T, C, y->nrm1, m->eps, h1);
@@ -597,25 +858,19 @@ static int layer_forward(orc_model* m, int li, float* x, int T, orc_kv_layer* kv
   }
   const int group = nH / nKV;
   const double scale = 1.0 / sqrt((double)hd);
-  qh = (float*)malloc(sizeof(float) * (size_t)T * hd);
-  khT = (float*)malloc(sizeof(float) * (size_t)hd * N);
-  vh = (float*)malloc(sizeof(float) * (size_t)N * hd);
-  scores = (float*)malloc(sizeof(float) * (size_t)T * N);
-  a = (float*)malloc(sizeof(float) * (size_t)T * N);
-  oh = (float*)malloc(sizeof(float) * (size_t)T * hd);
-  if (!qh || !khT || !vh || !scores || !a || !oh) { rc = ORC_E_NOMEM; goto done; }
-  for (int h = 0; h < nH; h++) {
-    int kvh = h / group;
-    for (int t = 0; t < T; t++) memcpy(qh + (int64_t)t * hd, q + (int64_t)t * qDim + h * hd, sizeof(float) * hd);
-    for (int t = 0; t < N; t++)
-      for (int c = 0; c < hd; c++) {
-        khT[(int64_t)c * N + t] = K[(int64_t)t * kvDim + kvh * hd + c];
-        vh[(int64_t)t * hd + c] = Vv[(int64_t)t * kvDim + kvh * hd + c];
-      }
-    if ((rc = orc_vgemm(qh, khT, T, hd, N, scores))) goto done;
-    orc_softmax_causal(scores, T, N, n0, scale, a);
-    if ((rc = orc_vgemm(a, vh, T, N, hd, oh))) goto done;
-    for (int t = 0; t < T; t++) memcpy(ctxOut + (int64_t)t * qDim + h * hd, oh + (int64_t)t * hd, sizeof(float) * hd);
+  if (m->fast) {
+    /* heads are independent: one head per task, each with its own buffers */
+    int* hrc = (int*)calloc((size_t)nH, sizeof(int));
+    if (!hrc) { rc = ORC_E_NOMEM; goto done; }
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int h = 0; h < nH; h++)
+      hrc[h] = attn_head(1, h, group, q, qDim, K, Vv, kvDim, T, N, n0, hd, scale, ctxOut);
+    for (int h = 0; h < nH && !rc; h++) rc = hrc[h];
+    free(hrc);
+    if (rc) goto done;
+  } else {
+    for (int h = 0; h < nH; h++)
+      if ((rc = attn_head(0, h, group, q, qDim, K, Vv, kvDim, T, N, n0, hd, scale, ctxOut))) goto done;
   }
   if ((rc = proj(m, ctxOut, T, y->Wo, &y->o, qDim, C, tmpC))) goto done;
   for (int64_t i = 0; i < (int64_t)T * C; i++) x2[i] = x[i] + tmpC[i];
@@ -627,7 +882,6 @@ static int layer_forward(orc_model* m, int li, float* x, int T, orc_kv_layer* kv
   for (int64_t i = 0; i < (int64_t)T * C; i++) x[i] = x2[i] + tmpC[i];
 done:
   free(h1); free(q); free(k); free(v); free(ctxOut); free(x2); free(g); free(u); free(tmpC);
-  free(qh); free(khT); free(vh); free(scores); free(a); free(oh);
   return rc;
 }
 
@@ -659,9 +913,9 @@ void orc_embed_rows(const orc_model* m, const int32_t* ids, int T, float* x) {
  * verified GEMM per requested row against lm_head. */
 int orc_logits_rows(orc_model* m, const float* x, int T, const int32_t* rows, int nrows, float* out) {
   int C = m->hidden, V = m->vocab;
-  if (!m->lm_kn) return ORC_E_INVAL;
+  if (!m->lm_kn && !m->lm_quantized) return ORC_E_INVAL;
   if (!m->per_call_quant && !m->lm_quantized) {
-    if (wq_build(&m->lm, m->lm_kn, C, V)) return ORC_E_NONFINITE;
+    if ((m->fast ? wq_build_t : wq_build)(&m->lm, m->lm_kn, C, V)) return ORC_E_NONFINITE;
     m->lm_quantized = 1;
   }
   float* y = (float*)malloc(sizeof(float) * (size_t)T * C);
@@ -729,6 +983,7 @@ static uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 void orc_synth_fill(uint64_t seed, int64_t start, int64_t n, double factor, float* out) {
+#pragma omp parallel for schedule(static) if (n >= PAR_MIN)
   for (int64_t i = 0; i < n; i++) {
     uint64_t base = (seed * 0x9E3779B97F4A7C15ULL) + (uint64_t)(start + i) * 4u;
     int64_t s = 0;
@@ -736,4 +991,73 @@ void orc_synth_fill(uint64_t seed, int64_t start, int64_t n, double factor, floa
     s -= (int64_t)2 * 4294967295LL;
     out[i] = (float)((double)s * factor);
   }
+}
+
+/* A synthetic benchmark model built in place, through the exact-product path:
+ * every weight of layers [lo, hi) (and, with head, the embedding and lm_head)
+ * is generated by orc_synth_fill, quantised once (quantizeCols, kept
+ * transposed) and its f32 copy dropped, so a Llama-3-8B-sized model needs
+ * ~8 GB here instead of ~32 GB.  Tensor seed = model_seed * 1000003 +
+ * (layer + 1) * 64 + role; roles emb 1, lm 2, Wq 3, Wk 4, Wv 5, Wo 6,
+ * Wgate 7, Wup 8, Wdown 9; norm weights are 1.  tie: lm_head = embᵀ. */
+static int synth_wq(uint64_t model_seed, int layer, int role, int k, int n, double factor, orc_wq* w) {
+  float* f = (float*)malloc(sizeof(float) * (size_t)k * n + 4);
+  if (!f) return ORC_E_NOMEM;
+  orc_synth_fill(model_seed * 1000003ULL + (uint64_t)(layer + 1) * 64u + (uint64_t)role, 0, (int64_t)k * n, factor,
+                 f);
+  int rc = wq_build_t(w, f, k, n);
+  free(f);
+  return rc;
+}
+
+int orc_model_synth(orc_model* m, uint64_t model_seed, double factor, int tie, int lo, int hi, int head) {
+  if (lo < 0 || hi > m->layers || hi < lo) return ORC_E_INVAL;
+  const int C = m->hidden, q = m->heads * m->head_dim, kv = m->kv_heads * m->head_dim, I = m->inter, V = m->vocab;
+  m->fast = 1;
+  m->per_call_quant = 0;
+  if (!m->own_ones) {
+    m->own_ones = (float*)malloc(sizeof(float) * (size_t)C);
+    if (!m->own_ones) return ORC_E_NOMEM;
+    for (int i = 0; i < C; i++) m->own_ones[i] = 1.0f;
+  }
+  int rc = ORC_OK;
+  for (int l = lo; l < hi && !rc; l++) {
+    orc_layer* y = &m->L[l];
+    if (y->quantized) continue;
+    y->nrm1 = y->nrm2 = m->own_ones;
+    y->Wq = y->Wk = y->Wv = y->Wo = y->Wgate = y->Wup = y->Wdown = NULL;
+    rc |= synth_wq(model_seed, l, 3, C, q, factor, &y->q);
+    rc |= synth_wq(model_seed, l, 4, C, kv, factor, &y->k);
+    rc |= synth_wq(model_seed, l, 5, C, kv, factor, &y->v);
+    rc |= synth_wq(model_seed, l, 6, q, C, factor, &y->o);
+    rc |= synth_wq(model_seed, l, 7, C, I, factor, &y->gate);
+    rc |= synth_wq(model_seed, l, 8, C, I, factor, &y->up);
+    rc |= synth_wq(model_seed, l, 9, I, C, factor, &y->down);
+    y->quantized = 1;
+  }
+  if (rc || !head) return rc ? ORC_E_NOMEM : ORC_OK;
+  free(m->own_emb);
+  m->own_emb = (float*)malloc(sizeof(float) * (size_t)V * C);
+  if (!m->own_emb) return ORC_E_NOMEM;
+  orc_synth_fill(model_seed * 1000003ULL + 1u, 0, (int64_t)V * C, factor, m->own_emb);
+  m->emb = m->own_emb;
+  m->nrmF = m->own_ones;
+  free(m->lm_kn);
+  m->lm_kn = NULL;
+  if (m->lm_quantized) wq_free(&m->lm);
+  m->lm_quantized = 0;
+  if (tie) {
+    float* t = (float*)malloc(sizeof(float) * (size_t)C * V);
+    if (!t) return ORC_E_NOMEM;
+#pragma omp parallel for schedule(static)
+    for (int64_t c = 0; c < C; c++)
+      for (int64_t v = 0; v < V; v++) t[c * V + v] = m->own_emb[v * C + c];
+    rc = wq_build_t(&m->lm, t, C, V);
+    free(t);
+  } else {
+    rc = synth_wq(model_seed, -1, 2, C, V, factor, &m->lm);
+  }
+  if (rc) return rc;
+  m->lm_quantized = 1;
+  return ORC_OK;
 }

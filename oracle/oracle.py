@@ -81,6 +81,10 @@ def lib():
         "orc_make_luts": (None, [p, p, p]),
         "orc_quantize_rows": (i32, [p, i64, i64, p, p]),
         "orc_quantize_cols": (i32, [p, i64, i64, p, p]),
+        "orc_quantize_cols_t": (i32, [p, i64, i64, p, p]),
+        "orc_bgemm_t": (i32, [p, p, p, p, i32, i32, i32, C.c_uint, p]),
+        "orc_model_set_fast": (None, [p, i32]),
+        "orc_model_synth": (i32, [p, C.c_uint64, d, i32, i32, i32, i32]),
         "orc_epi": (f, [i32, f, f]),
         "orc_bgemm": (i32, [p, p, p, p, i32, i32, i32, i32, C.c_uint, p, p, p, p]),
         "orc_exp": (d, [d]),
@@ -148,6 +152,28 @@ def quantize_cols(W: np.ndarray, rows: int, cols: int):
     s = np.empty(cols, np.float32)
     _check(lib().orc_quantize_cols(_p(W), rows, cols, _p(q), _p(s)), "quantizeCols")
     return q, s
+
+
+def quantize_cols_t(W: np.ndarray, rows: int, cols: int):
+    """quantizeCols with the values returned transposed (cols x rows)."""
+    W = np.ascontiguousarray(W, np.float32).reshape(-1)
+    qt = np.empty(rows * cols, np.int8)
+    s = np.empty(cols, np.float32)
+    _check(lib().orc_quantize_cols_t(_p(W), rows, cols, _p(qt), _p(s)), "quantizeCols")
+    return qt, s
+
+
+def bgemm_t(Xq, Wt, rs, cs, m, k, n, flags=0):
+    """bgemmJS (batch 1) over a transposed weight (n x k) by exact products:
+    the path the full-size golden fixtures use; equal to ``bgemm``."""
+    Xq = np.ascontiguousarray(Xq, np.int8).reshape(-1)
+    Wt = np.ascontiguousarray(Wt, np.int8).reshape(-1)
+    rs = np.ascontiguousarray(rs, np.float32).reshape(-1)
+    cs = np.ascontiguousarray(cs, np.float32).reshape(-1)
+    dt = np.int32 if flags & ACC else (np.int8 if flags & REQUANT else np.float32)
+    out = np.empty(m * n, dt)
+    _check(lib().orc_bgemm_t(_p(Xq), _p(Wt), _p(rs), _p(cs), m, k, n, flags, _p(out)), "bgemmJS")
+    return out
 
 
 _LUTS = None
@@ -348,7 +374,7 @@ def synth_weight(model_seed: int, layer: int, role: str, k: int, n: int) -> np.n
 class Model:
     """A whole Llama-family model held by the C oracle (weights k x n f32)."""
 
-    def __init__(self, spec: Spec, w: dict, per_call_quant: bool = False):
+    def __init__(self, spec: Spec, w: dict, per_call_quant: bool = False, fast: bool = False):
         self.spec = spec
         self._keep = []
         L = lib()
@@ -357,6 +383,9 @@ class Model:
         if not self.h:
             raise ValueError("bad spec")
         L.orc_model_set_per_call_quant(self.h, 1 if per_call_quant else 0)
+        L.orc_model_set_fast(self.h, 1 if fast else 0)
+        if w is None:
+            return
 
         def keep(a):
             if a is None:
@@ -398,6 +427,20 @@ class Model:
         out = np.empty(rows.size * self.spec.vocab, np.float32)
         _check(lib().orc_logits_rows(self.h, _p(x), T, _p(rows), rows.size, _p(out)), "logitsAt")
         return out.reshape(rows.size, self.spec.vocab)
+
+
+class SynthModel(Model):
+    """A synthetic benchmark model (the weights ``synth_weight`` gives) built
+    inside the C oracle on the exact-product path: each weight is generated,
+    quantised once and its f32 copy dropped, so full-size models fit in RAM."""
+
+    def __init__(self, spec: Spec, model_seed: int, factor: float = None, lo: int = 0, hi: int | None = None,
+                 head: bool = True):
+        super().__init__(spec, None, fast=True)
+        hi = spec.layers if hi is None else hi
+        _check(lib().orc_model_synth(self.h, model_seed & 0xFFFFFFFFFFFFFFFF,
+                                     float(SYNTH_FACTOR if factor is None else factor), 1 if spec.tie else 0, lo, hi,
+                                     1 if head else 0), "synth model")
 
 
 class KV:
@@ -548,10 +591,15 @@ def generate_local(model: Model, stages, ids, n_tokens, T):
     return out
 
 
-def generate_lookahead(model: Model, stages, ids0, n_new, T, max_draft=4):
-    """infer.js:464-494 (greedy)."""
+def generate_lookahead(model: Model, stages, ids0, n_new, T, max_draft=4, trace=None):
+    """infer.js:464-494 (greedy).  ``trace`` (a dict), when given, receives the
+    first lap's hidden state (``first_hidden``), scored rows (``first_rows``)
+    and their logits (``first_logits``), the same of the last lap (``last_win``
+    its window ids, ``last_hidden``, ``last_rows``, ``last_logits``), and the
+    number of laps (``laps``)."""
     ids = list(ids0)
     produced = 0
+    laps = 0
     while produced < n_new:
         frame = lookahead_frame(ids, T, max_draft)
         draft = frame["draft"]
@@ -562,6 +610,12 @@ def generate_lookahead(model: Model, stages, ids0, n_new, T, max_draft=4):
             x = model.run_layers(x, lo, hi)
         rows = draft_rows(T, frame["shown"], len(draft))
         logits = model.logits_rows(x, rows)
+        if trace is not None:
+            if laps == 0:
+                trace.update(first_hidden=x.copy(), first_rows=list(rows), first_logits=logits.copy())
+            trace.update(last_win=[int(v) for v in win], last_hidden=x.copy(), last_rows=list(rows),
+                         last_logits=logits.copy())
+        laps += 1
         picked = [argmax(logits[i]) for i in range(len(rows))]
         got = accept_draft(picked, draft)
         if not got:
@@ -571,11 +625,16 @@ def generate_lookahead(model: Model, stages, ids0, n_new, T, max_draft=4):
             produced += 1
             if produced >= n_new:
                 break
+    if trace is not None:
+        trace["laps"] = laps
     return ids
 
 
-def generate_chunked(model: Model, stages, ids0, n_new, chunk_size, max_pos=None):
-    """infer.js:339-367 (greedy); per-stage KV caches."""
+def generate_chunked(model: Model, stages, ids0, n_new, chunk_size, max_pos=None, trace=None):
+    """infer.js:339-367 (greedy); per-stage KV caches.  ``trace`` (a dict), when
+    given, receives the prefill's last hidden row (``prefill_last``), the
+    logits row of the first pick (``first_logits``) and the stages' caches
+    after the last lap (``caches``, one ``KV`` per stage)."""
     ids = list(ids0)
     max_pos = max_pos or (len(ids0) + n_new + 1)
     caches = [KV(model, lo, hi, max_pos) if hi > lo else None for lo, hi in stages]
@@ -586,9 +645,12 @@ def generate_chunked(model: Model, stages, ids0, n_new, chunk_size, max_pos=None
             if hi > lo:
                 x = model.run_layers(x, lo, hi, kv, ch["lo"])
         last = x
-    for _ in range(n_new):
+    for n in range(n_new):
         rows = last.size // model.spec.hidden
-        t = argmax(model.logits_rows(last, [rows - 1])[0])
+        lg = model.logits_rows(last, [rows - 1])[0]
+        if trace is not None and n == 0:
+            trace.update(prefill_last=last[(rows - 1) * model.spec.hidden:].copy(), first_logits=lg.copy())
+        t = argmax(lg)
         ids.append(t)
         pos = len(ids) - 1
         x = model.embed_rows([t])
@@ -596,6 +658,8 @@ def generate_chunked(model: Model, stages, ids0, n_new, chunk_size, max_pos=None
             if hi > lo:
                 x = model.run_layers(x, lo, hi, kv, pos)
         last = x
+    if trace is not None:
+        trace["caches"] = caches
     return ids
 
 
