@@ -194,6 +194,27 @@ def prompt_ids(w: dict, vocab: int, seed: int = 7):
     return [int(v) for v in rng.integers(0, vocab, w["prompt"])]
 
 
+E2E_UNIT = "tok/s (prompt ids on the host to generated ids on the host, prefill included)"
+
+
+def workload_config(name: str, world: int) -> dict:
+    """The ``config`` object of both arms' lines (identical for the same
+    workload and GPU count): the model shape, the schedule and the stages."""
+    import __graft_entry__ as G
+    shard = G.package().shard  # host logic only: no device call
+    w = WORKLOADS[name]
+    sp = w["spec"]
+    n_prompt = 256 if w["prompt"] == "ngram" else w["prompt"]
+    plan = shard.plan_stages(sp["layers"], [dict(id=f"gpu{i}", capacity=1.0) for i in range(world)])
+    sched = (f"{n_prompt}-token prompt in chunks of {w['chunk']} ({w['window']} in flight), {w['new']} greedy decode "
+             f"tokens" if w["mode"] == "chunked" else
+             f"full-window lookahead T={w['T']}, {n_prompt}-token prompt, {w['new']} new tokens")
+    return dict(workload=name, model=(f"{w['name']}: hidden {sp['hidden']}, {sp['layers']} layers, "
+                                      f"{sp['heads']}/{sp['kvHeads']} heads, inter {sp['inter']}, vocab {sp['vocab']}"),
+                schedule=sched, stages=[f"{s['lo']}-{s['hi']}" for s in plan], parallelism=f"pipeline x{world}",
+                l2="weights >> L2: every step streams them from HBM")
+
+
 def build_rank(P, comp, w: dict, rank: int, world: int):
     """This rank's stage of the plan (planStages over equal capacities)."""
     import torch
@@ -348,17 +369,11 @@ def bench_model(args, rank, world, peaks):
                                                           tops=(kinds[k][3] / (kinds[k][0] / 1e3) / 1e12
                                                                 if kinds[k][0] else None))
                  for k in kinds}
-        stages = [f"{s['lo']}-{s['hi']}" for s in plan]
         line = dict(metric=METRIC, value=value, unit="tok/s (decode)", n_gpus=world, steps=args.steps,
                     warmup=args.warmup, ms_per_step=ms_step, higher_is_better=True, scaling="strong",
                     vs_baseline=None, dtype="int8 x int8 -> int32 (f32 epilogue, f64 norms/softmax)",
                     data="synthetic (random-init weights, seeded uniform token ids)",
-                    config=dict(workload=f"{args.workload}: {w['name']}, " +
-                                (f"{len(ids)}-token prompt in chunks of {w['chunk']} ({w['window']} in flight), "
-                                 f"{w['new']} greedy decode tokens" if w["mode"] == "chunked" else
-                                 f"full-window lookahead T={w['T']}, {len(ids)}-token prompt, {w['new']} new"),
-                                stages=stages, parallelism=f"pipeline x{world}",
-                                l2="weights ≫ L2: every step streams them from HBM"),
+                    config=workload_config(args.workload, world),
                     prefill_tok_s=(len(ids) / (pre / 1e3)) if w["mode"] == "chunked" else None,
                     prefill_ms=pre if w["mode"] == "chunked" else None, decode_ms=dec,
                     roofline=roof, kernels=other, gpu_launches=launches, clocks=clk, backend=comp.label,
@@ -401,7 +416,7 @@ def e2e_model(comp, ring, w, ids, args, world=1):
     torch.cuda.synchronize()
     ms = max_over_ranks([t0.elapsed_time(t1) / steps], world)[0]
     n_new = w["new"]
-    return dict(value=n_new / (ms / 1e3), unit="tok/s (prompt to generated ids, prefill included)",
+    return dict(value=n_new / (ms / 1e3), unit=E2E_UNIT,
                 h2d_bytes_per_step=4 * len(ids), d2h_bytes_per_step=4 * n_new, ms_per_step=ms,
                 path="host ids -> infer/pipeline API (embed, stages, logits, greedy) -> host ids")
 
@@ -464,18 +479,30 @@ def cpu_threads():
     return G.oracle().threads()
 
 
-def cpu_model_baseline(w):
+def cpu_e2e_rate(w: dict, r: dict):
+    """Whole-generation rate (prefill included) of the sampled CPU rates."""
+    n_prompt = 256 if w["prompt"] == "ngram" else w["prompt"]
+    if "prefill_tok_s" not in r:  # the full-window path: every token is one lap
+        return r["decode_tok_s"]
+    return w["new"] / (n_prompt / r["prefill_tok_s"] + w["new"] / r["decode_tok_s"])
+
+
+SAMPLE_DESC = ("one layer of this model through the C restatement of verified_core.js/infer.js (weights re-quantised "
+               "per call as vgemmBlock does, LUT GEMM) for one decode row and one 16-row chunk (or one full window), "
+               "plus lm_head over 1/16 of the vocabulary; extrapolated to every layer and the whole vocabulary")
+
+
+def cpu_model_baseline(w, samples: int = 3):
     t = time.perf_counter()
-    r = cpu_model_rates(w)
+    rs = [cpu_model_rates(w) for _ in range(samples)]
     wall = time.perf_counter() - t
     cores = cpu_threads()
-    return dict(value=r["decode_tok_s"], unit="tok/s (decode)", cores=cores, kind="port",
-                prefill_tok_s=r.get("prefill_tok_s"),
-                sample="one layer of this model through the C restatement of verified_core.js/infer.js "
-                       "(weights re-quantised per call as vgemmBlock does) for one decode row and one 16-row chunk "
-                       "(or one full window), lm_head over 1/16 of the vocabulary; extrapolated to every layer and "
-                       f"the whole vocabulary; {wall:.1f} s of CPU work on {cores} threads (its GEMMs and "
-                       "quantisers split by output element; the reference's own JS path uses one)", detail=r)
+    med = {k: statistics.median(r[k] for r in rs) for k in rs[0]}
+    return dict(value=med["decode_tok_s"], unit="tok/s (decode)", cores=cores, kind="port",
+                prefill_tok_s=med.get("prefill_tok_s"), e2e_tok_s=cpu_e2e_rate(w, med),
+                sample=f"{SAMPLE_DESC}; median of {samples} samples, {wall:.1f} s of CPU work on {cores} threads "
+                       "(GEMMs and quantisers split by output element; the reference's own JS path uses one)",
+                detail=med)
 
 
 def bench_reference(args, rank, world):
@@ -483,31 +510,58 @@ def bench_reference(args, rank, world):
     if rank != 0:
         return None
     if args.workload == "gemm-sweep":
-        vals = [cpu_sweep_rate(1)[0] for _ in range(max(1, args.steps))]
-        v = statistics.median(vals)
-        ops_step = sum(2.0 * m * k * n for (m, k, n) in sweep_shapes())
-        ms = ops_step / (v * 1e12) * 1e3
+        for _ in range(args.warmup):
+            cpu_sweep_rate()
+        res = [cpu_sweep_rate() for _ in range(max(1, args.steps))]
+        v = statistics.median(r[0] for r in res)
+        ms = statistics.mean(r[1] for r in res) * 1e3
         unit = "TOPS (int8 ops/s, GEMM sweep)"
         extra = {}
     else:
+        # one step = one bounded sample of the workload (one layer, one decode
+        # row, one chunk or window, 1/16 of lm_head); the model-level rates are
+        # the median of the steps' extrapolations
         w = WORKLOADS[args.workload]
-        rs = [cpu_model_rates(w) for _ in range(max(1, min(args.steps, 2)))]
-        v = statistics.median(r["decode_tok_s"] for r in rs)
-        ms = w["new"] / v * 1e3
+        for _ in range(args.warmup):
+            cpu_model_rates(w)
+        walls, rs = [], []
+        for _ in range(args.steps):
+            t = time.perf_counter()
+            rs.append(cpu_model_rates(w))
+            walls.append((time.perf_counter() - t) * 1e3)
+        med = {k: statistics.median(r[k] for r in rs) for k in rs[0]}
+        v = med["decode_tok_s"]
+        ms = statistics.mean(walls)
         unit = "tok/s (decode)"
-        extra = dict(prefill_tok_s=statistics.median(r["prefill_tok_s"] for r in rs) if "prefill_tok_s" in rs[0]
-                     else None)
-    sample = ("one layer + 1/16 of lm_head per sample through the C restatement (per-call weight "
-              "quantisation, LUT GEMM), extrapolated to the whole model" if args.workload != "gemm-sweep" else
-              "per (K,N): one per-call quantizeCols + 2 LUT-GEMM rows, extrapolated to the 16 shapes")
+        e2e_v = cpu_e2e_rate(w, med)
+        extra = dict(prefill_tok_s=med.get("prefill_tok_s"),
+                     extrapolated=dict(decode_tok_s=v, prefill_tok_s=med.get("prefill_tok_s"), e2e_tok_s=e2e_v,
+                                       method="each step times the sample; its rates are extrapolated to every layer "
+                                              "and the whole vocabulary; value is the median over the steps"),
+                     config=workload_config(args.workload, world))
+        sample = SAMPLE_DESC
+        return dict(metric=METRIC, impl="reference", value=v, unit=unit, n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="strong", vs_baseline=None,
+                    dtype="int8 x int8 -> int32 (f32 epilogue, f64 norms/softmax)",
+                    data="synthetic (random-init weights, seeded uniform token ids)",
+                    cpu_baseline=dict(value=v, unit=unit, cores=cpu_threads(), kind="port", sample=sample),
+                    e2e=dict(value=e2e_v, unit=E2E_UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0,
+                             path="the sampled CPU rates combined over the whole generation (prefill included)"),
+                    **extra)
+    sample = "per (K,N): one per-call quantizeCols + 2 LUT-GEMM rows, extrapolated to the 16 shapes"
     return dict(metric=METRIC, impl="reference", value=v, unit=unit, n_gpus=world, steps=args.steps,
-                warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="strong", vs_baseline=None,
-                dtype="int8 x int8 -> int32", data="synthetic (seeded)", config=dict(workload=args.workload),
+                warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None,
+                dtype="int8 x int8 -> int32", data="synthetic (seeded)", config=sweep_config(world),
                 cpu_baseline=dict(value=v, unit=unit, cores=cpu_threads(), kind="port", sample=sample),
                 e2e=dict(value=v, unit=unit, h2d_bytes_per_step=0, d2h_bytes_per_step=0), **extra)
 
 
 # ---- the GEMM sweep -----------------------------------------------------------------
+def sweep_config(world: int) -> dict:
+    return dict(workload="gemm-sweep", shapes="M in {1,16,128,512} x (K,N) in {(576,1536),(1536,576),(2048,5632),"
+                "(4096,14336)}", cold_l2="weight copies per shape > 3x L2, rotated", parallelism=f"replicas x{world}")
+
+
 def sweep_shapes():
     return [(m, k, n) for (k, n) in SWEEP_KN for m in SWEEP_M]
 
@@ -529,7 +583,7 @@ def _cpu_shape_worker(args):
     return tq, (time.perf_counter() - t) / rows
 
 
-def cpu_sweep_rate(threads: int, rows: int = 2):
+def cpu_sweep_rate(rows: int = 2):
     jobs = [(k, n, rows, i) for i, (k, n) in enumerate(SWEEP_KN)]
     t0 = time.perf_counter()
     res = [_cpu_shape_worker(j) for j in jobs]
@@ -606,13 +660,12 @@ def bench_gemm_sweep(args, rank, world, peaks):
         line = dict(metric=METRIC, value=ops_step * world / (ms / 1e3) / 1e12, unit="TOPS (int8 ops/s, GEMM sweep)",
                     n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True,
                     scaling="weak", vs_baseline=None, dtype="int8 x int8 -> int32", data="synthetic (seeded)",
-                    config=dict(workload="gemm-sweep", cold_l2="weight copies per shape > 3x L2, rotated",
-                                parallelism=f"replicas x{world}"),
+                    config=sweep_config(world),
                     roofline=roof, gpu_launches=comp.L.dc_launch_count() - l0, clocks=clk, backend=comp.label,
                     kernels={("gemv" if k == 1 else "tcgen05"): dict(ms=v[0], launches=v[1]) for k, v in per.items()})
         if world == 1 and not args.no_cpu:
-            v, wall = cpu_sweep_rate(1)
-            line["cpu_baseline"] = dict(value=v, unit="TOPS", cores=1, kind="port",
+            v, wall = cpu_sweep_rate()
+            line["cpu_baseline"] = dict(value=v, unit="TOPS", cores=cpu_threads(), kind="port",
                                         sample=f"per (K,N): one per-call quantizeCols + 2 LUT-GEMM rows, "
                                                f"extrapolated; {wall:.1f} s")
     return line
