@@ -682,6 +682,13 @@ static int gemm_dispatch_impl(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8
   return DC_OK;
 }
 
+int dc_gemm_untimed(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                    const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                    int kind) {
+  if (m == 0 || n == 0 || batch == 0) return DC_OK;
+  return gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind);
+}
+
 int dc_scratch(dc_ctx* ctx, size_t bytes, void** p) {
   if (bytes > ctx->scratch_bytes) {
     DC_CUDA(ctx, cudaStreamSynchronize(ctx->stream));

@@ -429,7 +429,7 @@ bool encode_map(CUtensorMap* map, const void* base, int ld, long rows, int box_r
 template <int BN>
 int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
               int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st, int32_t* partial,
-              int* counters, size_t partial_cap, size_t counter_cap) {
+              int* counters, size_t partial_cap, size_t counter_cap, int clear) {
   using C = TcCfg<BN>;
   CUtensorMap mW, mX;
   if (!make_map(&mW, Wt, ldw, (long)batch * n, TILE_N) || !make_map(&mX, Xq, ldx, (long)batch * m, BN))
@@ -460,6 +460,10 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
     a.kb_per_split = a.kb_total;
   }
   a.splits = splits;
+  if (splits > 1 && clear) {  // caller-owned scratch of unknown contents: zero what the split-K fixup reads
+    DC_CUDA(ctx, cudaMemsetAsync(partial, 0, 4 * (size_t)batch * m * n, st));
+    DC_CUDA(ctx, cudaMemsetAsync(counters, 0, 4 * (size_t)tiles, st));
+  }
   a.flags = flags;
   a.requant = ctx->d_requant;
   a.relu = ctx->d_relu;
@@ -513,23 +517,23 @@ static int tc_scratch(dc_ctx* ctx, size_t partial_elems, size_t counters, int32_
 
 int dc_gemm_tc_with(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
                     const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
-                    int32_t* partial, int* counters, size_t partial_cap, size_t counter_cap) {
+                    int32_t* partial, int* counters, size_t partial_cap, size_t counter_cap, int clear) {
   if (((uintptr_t)Xq & 15) || ((uintptr_t)Wt & 15) || (ldx & 15) || (ldw & 15) || k <= 0 || m <= 0 || n <= 0)
     return dc_fail(ctx, DC_E_INVAL, "tcgen05: operands must be 16-byte aligned with ld a multiple of 16");
   if (m <= 16)
     return launch_tc<16>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
-                         partial_cap, counter_cap);
+                         partial_cap, counter_cap, clear);
   if (m <= 32)
     return launch_tc<32>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
-                         partial_cap, counter_cap);
+                         partial_cap, counter_cap, clear);
   if (m <= 64)
     return launch_tc<64>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
-                         partial_cap, counter_cap);
+                         partial_cap, counter_cap, clear);
   if (m <= 128)
     return launch_tc<128>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
-                          partial_cap, counter_cap);
+                          partial_cap, counter_cap, clear);
   return launch_tc<256>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
-                        partial_cap, counter_cap);
+                        partial_cap, counter_cap, clear);
 }
 
 int dc_gemm_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
@@ -541,5 +545,5 @@ int dc_gemm_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw
   int rc = tc_scratch(ctx, (size_t)batch * m * n, tiles, &partial, &counters);
   if (rc) return rc;
   return dc_gemm_tc_with(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
-                         ctx->tc_partial_cap, ctx->tc_counter_cap);
+                         ctx->tc_partial_cap, ctx->tc_counter_cap, 0);
 }

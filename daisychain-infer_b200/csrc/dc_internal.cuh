@@ -50,6 +50,9 @@ struct dc_ctx {
   int32_t* tc_partial = nullptr;
   int* tc_counters = nullptr;
   size_t tc_partial_cap = 0, tc_counter_cap = 0;
+  // dc_bgemm_dev_noalloc: device address of the library's fixed scratch array,
+  // looked up by the first call on this context
+  int32_t* noalloc_scratch = nullptr;
   // live GEMM timing (dc_timing / dc_timing_read)
   bool timing = false;
   std::vector<dc_timed> timed;
@@ -108,6 +111,16 @@ int dc_gemm_lut(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wq, const float* rs
 // tcgen05 path (dc_gemm_tc.cu): returns DC_E_INVAL when the shape is not supported.
 int dc_gemm_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
                int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st);
+// The same with caller-provided split-K scratch of the given capacities; clear = 1
+// zeroes the part a split-K launch uses first (scratch of unknown contents).
+int dc_gemm_tc_with(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                    const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                    int32_t* partial, int* counters, size_t partial_cap, size_t counter_cap, int clear);
+// dc_gemm_dispatch without the timing events: kind 1 GEMV (m <= 8), 2 SIMT dp4a,
+// 3 tcgen05 (falls back to 2 for shapes it does not take), 0 by m.
+int dc_gemm_untimed(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                    const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                    int kind);
 
 // ---- device helpers ---------------------------------------------------------
 // ECMAScript Math.round on a double: nearest, ties toward +infinity.

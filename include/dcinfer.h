@@ -113,14 +113,16 @@ int dc_bgemm_dev_kind(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, 
  * For callers that cannot let the library call cudaMalloc/cudaFree behind their
  * back: a host that sizes all of HBM up front, a runtime that owns device
  * allocation, or a process whose other streams must not be stalled by the device
- * synchronisation cudaFree implies.  Runs the tcgen05 kernel with its split-K
- * scratch in a fixed array inside the library (DC_NOALLOC_MAX_OUT int32 +
- * DC_NOALLOC_MAX_TILES counters, about 4.2 MB held on every GPU that loads the
- * library); outputs of more than DC_NOALLOC_MAX_OUT elements (batch*m*n) are
- * refused with DC_E_INVAL.  Each call clears the scratch it uses first; calls
- * that overlap on one GPU race on the shared array.  The first call on a device
- * looks up the array's address with that device current: make it before any
- * stream capture on that device. */
+ * synchronisation cudaFree implies.  Same arguments, kernels and results as
+ * dc_bgemm_dev (k == 0 gives zero accumulators; the SIMT kernel runs when the
+ * tcgen05 kernel failed its init gate or cannot take the operands), but the
+ * tcgen05 kernel's split-K scratch is a fixed array inside the library
+ * (DC_NOALLOC_MAX_OUT int32 + DC_NOALLOC_MAX_TILES counters, about 4.2 MB held
+ * on every GPU that loads the library); outputs of more than DC_NOALLOC_MAX_OUT
+ * elements (batch*m*n) are refused with DC_E_INVAL.  A call that splits K
+ * clears the scratch it uses first; calls that overlap on one GPU race on the
+ * shared array.  The first call on a context looks up the array's address with
+ * the context's device current: make it before any stream capture. */
 #define DC_NOALLOC_MAX_OUT (1 << 20)
 #define DC_NOALLOC_MAX_TILES 4096
 int dc_bgemm_dev_noalloc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
