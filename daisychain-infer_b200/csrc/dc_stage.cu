@@ -35,6 +35,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "dc_fdlibm.cuh"
 #include "dc_internal.cuh"
 #include "dc_math.cuh"
 #include "dc_osum.cuh"
@@ -1568,15 +1569,28 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->asg, 4 * (size_t)std::min(S->max_rows, 16) * S->nH)) ||
       (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
     return fail(rc);
-  // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1
+  // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1, with the fdlibm
+  // method of Math.pow / Math.cos / Math.sin (dc_fdlibm.cuh)
   const int half = S->hd / 2;
   std::vector<float> c((size_t)max_pos * half), sn((size_t)max_pos * half);
-  for (int p = 0; p < max_pos; p++)
-    for (int i = 0; i < half; i++) {
-      const double f = (double)p / pow(s.rope_theta, (2.0 * i) / (double)S->hd);
-      c[(size_t)p * half + i] = (float)cos(f);
-      sn[(size_t)p * half + i] = (float)sin(f);
+  bool ok = true;
+  for (int i = 0; i < half && ok; i++) {
+    bool okp = true;
+    const double den = dcf::pow(s.rope_theta, (2.0 * i) / (double)S->hd, &okp);
+    ok = okp;
+    for (int p = 0; p < max_pos && ok; p++) {
+      const double f = (double)p / den;
+      bool okc = true, oks = true;
+      c[(size_t)p * half + i] = (float)dcf::cos(f, &okc);
+      sn[(size_t)p * half + i] = (float)dcf::sin(f, &oks);
+      ok = okc && oks;
     }
+  }
+  if (!ok) {
+    dc_fail(ctx, DC_E_INVAL, "stage_create: rope_theta %g gives RoPE angles outside the table builder's range",
+            s.rope_theta);
+    return fail(DC_E_INVAL);
+  }
   if ((rc = upload(S, c.data(), c.size(), &S->rope_cos)) || (rc = upload(S, sn.data(), sn.size(), &S->rope_sin)))
     return fail(rc);
   if (cudaMemsetAsync(S->amax_keys, 0, 64, ctx->stream) != cudaSuccess ||

@@ -27,7 +27,7 @@
  * are PARITY UNPINNED against V8: no JavaScript runtime exists on either
  * machine, and the reference stores no golden vectors.  exp() here follows
  * the fdlibm 5.3 method (Sun Microsystems, 1993), the method V8's Math.exp is
- * ported from; pow/cos/sin for the RoPE tables come from the C library.
+ * ported from, and so do pow/cos/sin for the RoPE tables.
  *
  * The requant-LUT output rule is not defined anywhere in the reference (it
  * belonged to a Python kernel that is not in the repository).  This build
@@ -281,6 +281,211 @@ double orc_exp(double x) {
   return bits2d((uint64_t)((int64_t)by + (int64_t)(k + 1000) * 4503599627370496LL)) * twom1000;
 }
 
+/* ---- pow / sin / cos: the fdlibm 5.3 method (Sun Microsystems, 1993) -------
+ * The RoPE tables of infer.js:71-81 come from Math.pow, Math.cos and Math.sin,
+ * which V8 implements with its fdlibm-derived ieee754 routines; these are a
+ * restatement of the same published method (not the C library's):
+ * sin/cos reduce x = n*pi/2 + (y0 + y1) with pi/2 in 33-bit pieces (three
+ * Cody-Waite stages as cancellation requires; |x| <= 2^19*pi/2, NaN beyond),
+ * then minimax polynomials on [-pi/4, pi/4]; pow (x > 0 finite, y finite)
+ * forms log2(x) in extra precision, multiplies by y split in two, and
+ * evaluates 2^z by range reduction and the exp polynomial.  Within 1 ulp of
+ * the C library's results (tests/test_rope_tables.py). */
+static double with_lo(double d, uint32_t lo) { return bits2d((d2bits(d) & 0xFFFFFFFF00000000ULL) | lo); }
+static double with_hi(double d, uint32_t hi) { return bits2d((d2bits(d) & 0xFFFFFFFFULL) | ((uint64_t)hi << 32)); }
+static uint32_t lo32(double d) { return (uint32_t)d2bits(d); }
+static int32_t hi32(double d) { return (int32_t)(d2bits(d) >> 32); }
+
+static double fdl_ksin(double x, double y, int iy) {
+  const double S1 = bits2d(0xBFC5555555555549ULL), S2 = bits2d(0x3F8111111110F8A6ULL),
+               S3 = bits2d(0xBF2A01A019C161D5ULL), S4 = bits2d(0x3EC71DE357B1FE7DULL),
+               S5 = bits2d(0xBE5AE5E68A2B9CEBULL), S6 = bits2d(0x3DE5D93A5ACFD57CULL);
+  int32_t ix = hi32(x) & 0x7fffffff;
+  if (ix < 0x3e400000 && (int)x == 0) return x;
+  double z = x * x, v = z * x;
+  double r = S2 + z * (S3 + z * (S4 + z * (S5 + z * S6)));
+  if (iy == 0) return x + v * (S1 + z * r);
+  return x - ((z * (0.5 * y - v * r) - y) - v * S1);
+}
+static double fdl_kcos(double x, double y) {
+  const double C1 = bits2d(0x3FA555555555554CULL), C2 = bits2d(0xBF56C16C16C15177ULL),
+               C3 = bits2d(0x3EFA01A019CB1590ULL), C4 = bits2d(0xBE927E4F809C52ADULL),
+               C5 = bits2d(0x3E21EE9EBDB4B1C4ULL), C6 = bits2d(0xBDA8FAE9BE8838D4ULL);
+  int32_t ix = hi32(x) & 0x7fffffff;
+  if (ix < 0x3e400000 && (int)x == 0) return 1.0;
+  double z = x * x;
+  double r = z * (C1 + z * (C2 + z * (C3 + z * (C4 + z * (C5 + z * C6)))));
+  if (ix < 0x3FD33333) return 1.0 - (0.5 * z - (z * r - x * y));
+  double qx = ix > 0x3fe90000 ? 0.28125 : bits2d((uint64_t)(uint32_t)(ix - 0x00200000) << 32);
+  double hz = 0.5 * z - qx, a = 1.0 - qx;
+  return a - (hz - (z * r - x * y));
+}
+static const int32_t npio2_hw[32] = {
+  0x3FF921FB, 0x400921FB, 0x4012D97C, 0x401921FB, 0x401F6A7A, 0x4022D97C, 0x4025FDBB, 0x402921FB,
+  0x402C463A, 0x402F6A7A, 0x4031475C, 0x4032D97C, 0x40346B9C, 0x4035FDBB, 0x40378FDB, 0x403921FB,
+  0x403AB41B, 0x403C463A, 0x403DD85A, 0x403F6A7A, 0x40407E4C, 0x4041475C, 0x4042106C, 0x4042D97C,
+  0x4043A28C, 0x40446B9C, 0x404534AC, 0x4045FDBB, 0x4046C6CB, 0x40478FDB, 0x404858EB, 0x404921FB};
+/* |x| <= 2^19 pi/2 only; returns n, y[0]+y[1] = x - n pi/2 */
+static int fdl_rem_pio2(double x, double* y) {
+  const double invpio2 = bits2d(0x3FE45F306DC9C883ULL), pio2_1 = bits2d(0x3FF921FB54400000ULL),
+               pio2_1t = bits2d(0x3DD0B4611A626331ULL), pio2_2 = bits2d(0x3DD0B4611A600000ULL),
+               pio2_2t = bits2d(0x3BA3198A2E037073ULL), pio2_3 = bits2d(0x3BA3198A2E000000ULL),
+               pio2_3t = bits2d(0x397B839A252049C1ULL);
+  int32_t hx = hi32(x), ix = hx & 0x7fffffff;
+  if (ix <= 0x3fe921fb) { y[0] = x; y[1] = 0; return 0; }
+  if (ix < 0x4002d97c) {
+    if (hx > 0) {
+      double z = x - pio2_1;
+      if (ix != 0x3ff921fb) { y[0] = z - pio2_1t; y[1] = (z - y[0]) - pio2_1t; }
+      else { z -= pio2_2; y[0] = z - pio2_2t; y[1] = (z - y[0]) - pio2_2t; }
+      return 1;
+    } else {
+      double z = x + pio2_1;
+      if (ix != 0x3ff921fb) { y[0] = z + pio2_1t; y[1] = (z - y[0]) + pio2_1t; }
+      else { z += pio2_2; y[0] = z + pio2_2t; y[1] = (z - y[0]) + pio2_2t; }
+      return -1;
+    }
+  }
+  if (ix <= 0x413921fb) {
+    double t = fabs(x);
+    int n = (int)(t * invpio2 + 0.5);
+    double fn = (double)n, r = t - fn * pio2_1, w = fn * pio2_1t;
+    if (n < 32 && ix != npio2_hw[n - 1]) {
+      y[0] = r - w;
+    } else {
+      int32_t j = ix >> 20;
+      y[0] = r - w;
+      int32_t i = j - ((hi32(y[0]) >> 20) & 0x7ff);
+      if (i > 16) {
+        t = r; w = fn * pio2_2; r = t - w; w = fn * pio2_2t - ((t - r) - w); y[0] = r - w;
+        i = j - ((hi32(y[0]) >> 20) & 0x7ff);
+        if (i > 49) { t = r; w = fn * pio2_3; r = t - w; w = fn * pio2_3t - ((t - r) - w); y[0] = r - w; }
+      }
+    }
+    y[1] = (r - y[0]) - w;
+    if (hx < 0) { y[0] = -y[0]; y[1] = -y[1]; return -n; }
+    return n;
+  }
+  y[0] = y[1] = NAN; /* beyond 2^19 pi/2: not needed by the RoPE tables */
+  return 0;
+}
+double orc_fdl_sin(double x) {
+  int32_t ix = hi32(x) & 0x7fffffff; double y[2];
+  if (ix <= 0x3fe921fb) return fdl_ksin(x, 0.0, 0);
+  if (ix >= 0x7ff00000) return x - x;
+  int n = fdl_rem_pio2(x, y);
+  if (isnan(y[0])) return NAN;
+  switch (n & 3) { case 0: return fdl_ksin(y[0], y[1], 1); case 1: return fdl_kcos(y[0], y[1]);
+    case 2: return -fdl_ksin(y[0], y[1], 1); default: return -fdl_kcos(y[0], y[1]); }
+}
+double orc_fdl_cos(double x) {
+  int32_t ix = hi32(x) & 0x7fffffff; double y[2];
+  if (ix <= 0x3fe921fb) return fdl_kcos(x, 0.0);
+  if (ix >= 0x7ff00000) return x - x;
+  int n = fdl_rem_pio2(x, y);
+  if (isnan(y[0])) return NAN;
+  switch (n & 3) { case 0: return fdl_kcos(y[0], y[1]); case 1: return -fdl_ksin(y[0], y[1], 1);
+    case 2: return -fdl_kcos(y[0], y[1]); default: return fdl_ksin(y[0], y[1], 1); }
+}
+/* x > 0 finite, y finite */
+double orc_fdl_pow(double x, double y) {
+  const double bp[2] = {1.0, 1.5}, dp_h[2] = {0.0, bits2d(0x3FE2B80340000000ULL)},
+               dp_l[2] = {0.0, bits2d(0x3E4CFDEB43CFD006ULL)}, two53 = bits2d(0x4340000000000000ULL),
+               huge = 1.0e300, tiny = 1.0e-300,
+               L1 = bits2d(0x3FE3333333333303ULL), L2 = bits2d(0x3FDB6DB6DB6FABFFULL), L3 = bits2d(0x3FD55555518F264DULL),
+               L4 = bits2d(0x3FD17460A91D4101ULL), L5 = bits2d(0x3FCD864A93C9DB65ULL), L6 = bits2d(0x3FCA7E284A454EEFULL),
+               P1 = bits2d(0x3FC555555555553EULL), P2 = bits2d(0xBF66C16C16BEBD93ULL), P3 = bits2d(0x3F11566AAF25DE2CULL),
+               P4 = bits2d(0xBEBBBD41C5D26BF1ULL), P5 = bits2d(0x3E66376972BEA4D0ULL),
+               lg2 = bits2d(0x3FE62E42FEFA39EFULL), lg2_h = bits2d(0x3FE62E4300000000ULL),
+               lg2_l = bits2d(0xBE205C610CA86C39ULL), ovt = 8.0085662595372944372e-17,
+               cp = bits2d(0x3FEEC709DC3A03FDULL), cp_h = bits2d(0x3FEEC709E0000000ULL), cp_l = bits2d(0xBE3E2FE0145B01F5ULL),
+               ivln2 = bits2d(0x3FF71547652B82FEULL), ivln2_h = bits2d(0x3FF7154760000000ULL),
+               ivln2_l = bits2d(0x3E54AE0BF85DDF44ULL);
+  int32_t hx = hi32(x), hy = hi32(y), ix = hx & 0x7fffffff, iy = hy & 0x7fffffff;
+  uint32_t lx = lo32(x), ly = lo32(y);
+  if ((iy | ly) == 0) return 1.0;
+  double ax = fabs(x);
+  if (lx == 0 && (ix == 0x7ff00000 || ix == 0 || ix == 0x3ff00000)) {
+    double z = ax; if (hy < 0) z = 1.0 / z; return z;
+  }
+  double t1, t2;
+  if (iy > 0x41e00000) {
+    if (iy > 0x43f00000) {
+      if (ix <= 0x3fefffff) return hy < 0 ? huge * huge : tiny * tiny;
+      if (ix >= 0x3ff00000) return hy > 0 ? huge * huge : tiny * tiny;
+    }
+    if (ix < 0x3fefffff) return hy < 0 ? huge * huge : tiny * tiny;
+    if (ix > 0x3ff00000) return hy > 0 ? huge * huge : tiny * tiny;
+    double t = ax - 1.0;
+    double w = (t * t) * (0.5 - t * (0.3333333333333333333333 - t * 0.25));
+    double u = ivln2_h * t, v = t * ivln2_l - w * ivln2;
+    t1 = with_lo(u + v, 0);
+    t2 = v - (t1 - u);
+  } else {
+    int32_t n = 0, k;
+    if (ix < 0x00100000) { ax *= two53; n -= 53; ix = hi32(ax); }
+    n += (ix >> 20) - 0x3ff;
+    int32_t j = ix & 0x000fffff;
+    ix = j | 0x3ff00000;
+    if (j <= 0x3988E) k = 0;
+    else if (j < 0xBB67A) k = 1;
+    else { k = 0; n += 1; ix -= 0x00100000; }
+    ax = with_hi(ax, (uint32_t)ix);
+    double u = ax - bp[k], v = 1.0 / (ax + bp[k]);
+    double ss = u * v, s_h = with_lo(ss, 0);
+    double t_h = bits2d((uint64_t)(uint32_t)(((ix >> 1) | 0x20000000) + 0x00080000 + (k << 18)) << 32);
+    double t_l = ax - (t_h - bp[k]);
+    double s_l = v * ((u - s_h * t_h) - s_h * t_l);
+    double s2 = ss * ss;
+    double r = s2 * s2 * (L1 + s2 * (L2 + s2 * (L3 + s2 * (L4 + s2 * (L5 + s2 * L6)))));
+    r += s_l * (s_h + ss);
+    s2 = s_h * s_h;
+    t_h = with_lo(3.0 + s2 + r, 0);
+    t_l = r - ((t_h - 3.0) - s2);
+    u = s_h * t_h;
+    v = s_l * t_h + t_l * ss;
+    double p_h = with_lo(u + v, 0), p_l = v - (p_h - u);
+    double z_h = cp_h * p_h, z_l = cp_l * p_h + p_l * cp + dp_l[k];
+    double t = (double)n;
+    t1 = with_lo(((z_h + z_l) + dp_h[k]) + t, 0);
+    t2 = z_l - (((t1 - t) - dp_h[k]) - z_h);
+  }
+  double s = 1.0;
+  double y1 = with_lo(y, 0);
+  double p_l = (y - y1) * t1 + y * t2, p_h = y1 * t1, z = p_l + p_h;
+  int32_t j = hi32(z), i = (int32_t)lo32(z);
+  if (j >= 0x40900000) {
+    if (((j - 0x40900000) | i) != 0) return s * huge * huge;
+    if (p_l + ovt > z - p_h) return s * huge * huge;
+  } else if ((j & 0x7fffffff) >= 0x4090cc00) {
+    if (((j - (int32_t)0xc090cc00) | i) != 0) return s * tiny * tiny;
+    if (p_l <= z - p_h) return s * tiny * tiny;
+  }
+  i = j & 0x7fffffff;
+  int32_t k = (i >> 20) - 0x3ff, n = 0;
+  if (i > 0x3fe00000) {
+    n = j + (0x00100000 >> (k + 1));
+    k = ((n & 0x7fffffff) >> 20) - 0x3ff;
+    double t = bits2d((uint64_t)(uint32_t)(n & ~(0x000fffff >> k)) << 32);
+    n = ((n & 0x000fffff) | 0x00100000) >> (20 - k);
+    if (j < 0) n = -n;
+    p_h -= t;
+  }
+  double t = with_lo(p_l + p_h, 0);
+  double u = t * lg2_h, v = (p_l - (t - p_h)) * lg2 + t * lg2_l;
+  z = u + v;
+  double w = v - (z - u);
+  t = z * z;
+  t1 = z - t * (P1 + t * (P2 + t * (P3 + t * (P4 + t * P5))));
+  double r = (z * t1) / (t1 - 2.0) - (w + z * w);
+  z = 1.0 - (r - z);
+  j = hi32(z);
+  j += (n << 20);
+  if ((j >> 20) <= 0) z = scalbn(z, n);
+  else z = with_hi(z, (uint32_t)j);
+  return s * z;
+}
+
 /* ---- elementwise pieces of layerForward ----------------------------------- */
 /* infer.js:30-39: s accumulates v*v in double, sequentially from j = 0.  Rows
  * are independent; each row's sum runs serially on one thread. */
@@ -298,14 +503,15 @@ void orc_rmsnorm(const float* x, int rows, int C, const float* w, double eps, fl
   }
 }
 
-/* infer.js:71-81: f = p / theta^(2i/hd), tables stored f32. */
+/* infer.js:71-81: f = p / theta^(2i/hd), tables stored f32; Math.pow, cos and
+ * sin by the fdlibm method above. */
 void orc_rope_tables(int hd, double theta, int maxT, float* cos_t, float* sin_t) {
   int half = hd >> 1;
   for (int p = 0; p < maxT; p++)
     for (int i = 0; i < half; i++) {
-      double f = (double)p / pow(theta, (2.0 * i) / (double)hd);
-      cos_t[(int64_t)p * half + i] = (float)cos(f);
-      sin_t[(int64_t)p * half + i] = (float)sin(f);
+      double f = (double)p / orc_fdl_pow(theta, (2.0 * i) / (double)hd);
+      cos_t[(int64_t)p * half + i] = (float)orc_fdl_cos(f);
+      sin_t[(int64_t)p * half + i] = (float)orc_fdl_sin(f);
     }
 }
 

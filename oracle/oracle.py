@@ -88,6 +88,9 @@ def lib():
         "orc_epi": (f, [i32, f, f]),
         "orc_bgemm": (i32, [p, p, p, p, i32, i32, i32, i32, C.c_uint, p, p, p, p]),
         "orc_exp": (d, [d]),
+        "orc_fdl_sin": (d, [d]),
+        "orc_fdl_cos": (d, [d]),
+        "orc_fdl_pow": (d, [d, d]),
         "orc_rmsnorm": (None, [p, i32, i32, p, d, p]),
         "orc_rope_tables": (None, [i32, d, i32, p, p]),
         "orc_apply_rope": (None, [p, i32, i32, i32, p, p, i32]),
@@ -206,6 +209,21 @@ def epi(s: int, a: float, b: float) -> float:
 
 def exp(x: float) -> float:
     return lib().orc_exp(float(x))
+
+
+def fdl_sin(x: float) -> float:
+    """Math.sin by the fdlibm method (|x| <= 2^19 pi/2)."""
+    return lib().orc_fdl_sin(float(x))
+
+
+def fdl_cos(x: float) -> float:
+    """Math.cos by the fdlibm method (|x| <= 2^19 pi/2)."""
+    return lib().orc_fdl_cos(float(x))
+
+
+def fdl_pow(x: float, y: float) -> float:
+    """Math.pow by the fdlibm method (x > 0 finite, y finite)."""
+    return lib().orc_fdl_pow(float(x), float(y))
 
 
 def vgemm(X, W, m, k, n):
