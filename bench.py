@@ -654,8 +654,8 @@ def bench_gemm_sweep(args, rank, world, peaks):
     cap = torch.cuda.Stream()
     for it in items:
         graph = torch.cuda.CUDAGraph()
+        comp.set_stream(cap)  # outside the capture: switching streams synchronises the old one
         with torch.cuda.graph(graph, stream=cap):
-            comp.set_stream(cap)
             for c in range(it["copies"]):
                 launch(it, c)
         comp.set_stream(torch.cuda.current_stream())
@@ -728,6 +728,35 @@ def bench_gemm_sweep(args, rank, world, peaks):
     return line
 
 
+def profile_gemm(args):
+    """One GEMM of the sweep inside an NVTX range "profile", for an ncu capture
+    of exactly that launch (M = --gemm-m, K = 4096, N = 14336, requant int8
+    out), after three warm-up calls of the same shape:
+
+        ncu --set full --nvtx --nvtx-include "profile/" -k regex:k_gemm ... python bench.py --profile gemm"""
+    import torch
+    import __graft_entry__ as G
+    P = G.package()
+    comp = P.init_compute(0, stream=torch.cuda.current_stream())
+    m, k, n = args.gemm_m, 4096, 14336
+    g = torch.Generator(device="cuda").manual_seed(1)
+    W = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
+    cs = torch.rand(n, generator=g, device="cuda") * 9e-3 + 1e-3
+    xq = torch.zeros(m, k, dtype=torch.int8, device="cuda")
+    rs = torch.empty(m, device="cuda")
+    comp.quantize_rows_dev(torch.randn(m, k, generator=g, device="cuda"), m, k, xq, k, rs)
+    out = torch.empty(m * n, dtype=torch.int8, device="cuda")
+    for _ in range(3):
+        comp.bgemm_dev(xq, k, W, k, rs, cs, m, k, n, 1, 4, out)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("profile")
+    comp.bgemm_dev(xq, k, W, k, rs, cs, m, k, n, 1, 4, out)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    comp.sync()
+    return dict(profiled="gemm", m=m, k=k, n=n, flags="requant int8")
+
+
 def profile_model(args):
     """One prefill chunk or one decode lap of the workload, inside an NVTX range
     named "profile", for an ncu launch list of exactly that unit of work:
@@ -781,9 +810,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--prompt-len", type=int, default=0, help="override the prompt length (profiling runs)")
     ap.add_argument("--new-tokens", type=int, default=0, help="override the generated tokens (profiling runs)")
-    ap.add_argument("--profile", choices=["prefill", "decode"], default=None,
-                    help="run one prefill chunk or one decode lap inside an NVTX range 'profile' (for ncu); "
-                         "prints no benchmark line")
+    ap.add_argument("--profile", choices=["prefill", "decode", "gemm"], default=None,
+                    help="run one prefill chunk, one decode lap or one sweep GEMM inside an NVTX range 'profile' "
+                         "(for ncu); prints no benchmark line")
+    ap.add_argument("--gemm-m", type=int, default=512, help="M of the --profile gemm launch (K 4096, N 14336)")
     args = ap.parse_args()
     if args.workload in WORKLOADS:
         w = WORKLOADS[args.workload]
@@ -794,7 +824,7 @@ def main():
     args.warmup = max(args.warmup, 3)
     peaks = load_peaks()
     if args.profile:
-        print(json.dumps(profile_model(args)), flush=True)
+        print(json.dumps(profile_gemm(args) if args.profile == "gemm" else profile_model(args)), flush=True)
         return
     if args.impl == "reference":
         line = bench_reference(args, int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")))

@@ -12,9 +12,12 @@
 // the verified epilogue f32(f32(f32(acc)*rs[i])*cs[j]) / ReLU / requant LUT
 // (public/verified_core.js:227-228, 241-266).
 //
-// Roles (128 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues MMAs,
-// warp 1 owns the TMEM allocation, all four warps run the epilogue (warp w
-// reads TMEM lanes 32w..32w+31).  A STAGES-deep ring of full/empty mbarriers
+// Roles: warp 0 lane 0 issues TMA, warp 1 lane 0 issues MMAs, warp 1 owns
+// the TMEM allocation, and every warp runs the epilogue: warp w reads TMEM
+// lanes 32(w%4)..32(w%4)+31 (its 32 output columns j) and, with more than four
+// warps, one slice of the BN activation rows (128 threads for BN <= 16, 256 for
+// BN = 32, 512 above: the epilogue of a 128 x 256 tile is 32K outputs, too much
+// latency for four warps).  A STAGES-deep ring of full/empty mbarriers
 // pipelines the loads against the MMAs.
 //
 // Split-K: when the output tiles do not fill the GPU, K is split across CTAs.
@@ -150,6 +153,8 @@ struct TcCfg {
   static constexpr int B_BYTES = BN * TILE_K;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int THREADS = BN <= 16 ? 128 : (BN == 32 ? 256 : 512);
+  static constexpr int COLS_PER_WARP = BN / (THREADS / 128);  // activation rows each epilogue warp covers
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -168,7 +173,7 @@ struct TcArgs {
 };
 
 template <int BN>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -276,7 +281,10 @@ __global__ void __launch_bounds__(128, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();
   const bool good = have && (*(volatile int*)flag == 0) && nkb > 0;
-  const int j = j0 + warp * 32 + lane;
+  const int quarter = warp & 3;                          // TMEM lanes 32*quarter .. +31
+  const int cb0 = (warp >> 2) * C::COLS_PER_WARP;        // this warp's activation rows
+  const int cb1 = cb0 + C::COLS_PER_WARP;
+  const int j = j0 + quarter * 32 + lane;
   const bool jv = j < a.n;
   const float csv = jv ? __ldg(a.cs + bz * a.n + j) : 0.0f;
   // 16 accumulators of one column j: residual values loaded first, then stored
@@ -307,9 +315,9 @@ __global__ void __launch_bounds__(128, 1)
   if (a.splits == 1) {
     if (good) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = cb0; c0 < cb1; c0 += 16) {
         uint32_t r[16];
-        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, r);
         int32_t v[16];
 #pragma unroll
         for (int c = 0; c < 16; c++) v[c] = (int32_t)r[c];
@@ -319,9 +327,9 @@ __global__ void __launch_bounds__(128, 1)
   } else {
     if (good) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = cb0; c0 < cb1; c0 += 16) {
         uint32_t r[16];
-        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, r);
 #pragma unroll
         for (int c = 0; c < 16; c++) {
           const int i = i0 + c0 + c;
@@ -338,7 +346,7 @@ __global__ void __launch_bounds__(128, 1)
     if (last) {
       __threadfence();
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = cb0; c0 < cb1; c0 += 16) {
         int32_t v[16];
 #pragma unroll
         for (int c = 0; c < 16; c++) {  // all 16 partial sums in flight together
@@ -474,7 +482,7 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
   if (int rc = dc_set_smem(ctx, (const void*)k_gemm_tc<BN>, C::SMEM)) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_tiles, a.m_tiles, batch * splits);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

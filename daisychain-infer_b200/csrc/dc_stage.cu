@@ -81,6 +81,7 @@ struct dc_stage {
   int kv_len = 0;  // tokens in the KV cache (chunk path)
   // activation scratch
   float* hbuf = nullptr;   // max_rows x max(nqkv, 2I, C)
+  float* hmid = nullptr;   // max_rows x I: the SwiGLU output (the down projection's input)
   float* ctxo = nullptr;   // max_rows x qDim
   int8_t* xq = nullptr;    // max_rows x max(ldC, ldQ, ldI)
   float* rs = nullptr;     // max_rows
@@ -102,6 +103,7 @@ struct dc_stage {
   cudaGraphExec_t row_exec = nullptr;  // one-row graph of this stage's layers
   unsigned long long row_nk = 0;
   bool row_graph = true;
+  bool row_fused = false;  // decode rows: GEMVs with the norm / SwiGLU / row quantisation fused
   std::vector<dc_stage*> lap_key;
   int32_t* lap_picks = nullptr;
   std::vector<void*> allocs;
@@ -156,6 +158,18 @@ __device__ __forceinline__ double quant_scale(float mx) {
 __device__ __noinline__ double ordered_sum_cold(const double* t, int n, dco::Smem& osm) {
   return dco::ordered_sum(t, n, osm);
 }
+__device__ __noinline__ double ordered_sum_cold16(const double* t, int n, dco::Smem16& osm) {
+  return dco::ordered_sum(t, n, osm);
+}
+template <int NW> struct OsumCold;
+template <> struct OsumCold<8> {
+  static __device__ __forceinline__ double sum(const double* t, int n, dco::SmemT<8>& s) { return ordered_sum_cold(t, n, s); }
+};
+template <> struct OsumCold<16> {
+  static __device__ __forceinline__ double sum(const double* t, int n, dco::SmemT<16>& s) {
+    return ordered_sum_cold16(t, n, s);
+  }
+};
 
 // Dynamic shared memory of k_rmsnorm_quant: squares (double) and the row
 // (float), plus the weight row (float) when that still fits.
@@ -204,41 +218,19 @@ __device__ __forceinline__ double serial_sum_radius(double s, double w, int dept
   return 1.1102230246251565e-16 * (1.001 * w + (double)(depth + 8) * s);
 }
 
-// RMSNorm of one row fused with quantizeRows of its output.
-// x rows x C f32 -> q rows x ldq int8 (+ s[row]); the f32 norm output is not kept.
-__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, int C,
-                                                               const float* w, double eps,
-                                                               int8_t* q, int ldq,
-                                                               float* s, int* status,
-                                                               float* yo = nullptr,
-                                                               uint32_t* zrow = nullptr,
-                                                               int exact_sum = 0) {
-  extern __shared__ __align__(16) double sq[];  // C doubles (v*v), C floats (x, then y), C floats (w)
-  float* ys = (float*)(sq + C);
-  // the weight row rides along in shared memory when it fits (16 bytes per column)
-  float* wsm = 16 * (size_t)C + 20 * 1024 <= 232448 ? ys + C : nullptr;
-  const float* wr = wsm ? wsm : w;
-  __shared__ float red[32];
-  __shared__ double2 redd2[32];
-  __shared__ int vote[32];
-  __shared__ dco::Smem osm;
-  // the GEMV that consumes q may launch now: it streams its weights meanwhile
-  asm volatile("griddepcontrol.launch_dependents;");
-  const int row = blockIdx.x;
-  const float* xr = x + (int64_t)row * C;
-  // float4 access when the row allows it (all loads of a thread in flight at once)
-  const bool vec = (C & 3) == 0 && ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
-  // The weight row is constant: its copy into shared memory (asynchronous,
-  // awaited after the input row's loads) starts before the grid-dependency
-  // wait.  Everything else this kernel reads or writes comes after it.
-  if (vec && wsm) {
-    for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x)
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dcp::smem_u32(wsm + 4 * i)), "l"(w + 4 * i)
-                   : "memory");
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  }
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (zrow && threadIdx.x == 0) zrow[row] = 0;  // the row maximum the next row quantisation collects
+// RMSNorm of one row (infer.js:30-39) fused with quantizeRows of its output,
+// computed by the whole block (NW warps); every thread calls it after
+// griddepcontrol.wait.  xr: the row (C floats; float4 access when `vec`),
+// wr: the weight row (in shared memory when the caller copied it there with
+// cp.async, `wpend` then says the copies are still in flight).  Shared
+// scratch: sq (C doubles), ys (C floats).  Output: yo (the normalised f32 row,
+// no quantisation) when not null, else q (ldq bytes, zero past C) and *s
+// (thread 0).  A non-finite input sets DC_ST_NONFINITE in *status.
+template <int NW>
+__device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, const float* wr, bool wpend, bool vec,
+                                                    double eps, double* sq, float* ys, int8_t* q, int ldq,
+                                                    float* s, int* status, float* yo, int exact_sum,
+                                                    dco::SmemT<NW>& osm, float* red, double2* redd2, int* vote) {
   bool bad = false;
   if (vec) {
 #pragma unroll 4
@@ -251,11 +243,10 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
       sq[4 * i + 2] = __dmul_rn((double)v.z, (double)v.z);
       sq[4 * i + 3] = __dmul_rn((double)v.w, (double)v.w);
     }
-    if (wsm) asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's copies (the barrier below publishes them)
+    if (wpend) asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's copies (the barrier below publishes them)
   } else {
     for (int j = threadIdx.x; j < C; j += blockDim.x) {
       const float v = xr[j];
-      if (wsm) wsm[j] = w[j];
       bad |= !isfinite(v);
       ys[j] = v;
       sq[j] = __dmul_rn((double)v, (double)v);
@@ -293,7 +284,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
     bool any = false;
     for (int wv = 0; wv < (int)(blockDim.x >> 5); wv++) any |= vote[wv] != 0;
     inv = inv_lo;
-    if (any) inv = rms_inv(ordered_sum_cold(sq, C, osm), C, eps);
+    if (any) inv = rms_inv(OsumCold<NW>::sum(sq, C, osm), C, eps);
   }
   float mx = 0.0f;
   if (vec) {
@@ -317,14 +308,13 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
   }
   if (yo) {  // the normalised row itself (infer.js rmsnorm), no quantisation
     __syncthreads();
-    for (int j = threadIdx.x; j < C; j += blockDim.x) yo[(int64_t)row * C + j] = ys[j];
+    for (int j = threadIdx.x; j < C; j += blockDim.x) yo[j] = ys[j];
     return;
   }
   mx = block_max_f(mx, red);
   const double sc = quant_scale(mx), rsc = __drcp_rn(sc);
-  if (threadIdx.x == 0) s[row] = __double2float_rn(sc);
-  int8_t* qr = q + (int64_t)row * ldq;
-  if (vec && (ldq & 3) == 0 && (reinterpret_cast<uintptr_t>(qr) & 3) == 0) {
+  if (threadIdx.x == 0) s[0] = __double2float_rn(sc);
+  if (vec && (ldq & 3) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
 #pragma unroll 1
     for (int i = threadIdx.x; i < (ldq >> 2); i += blockDim.x) {
       char4 o = make_char4(0, 0, 0, 0);
@@ -335,13 +325,55 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
         o.z = dc_quant_div((double)y.z, sc, rsc);
         o.w = dc_quant_div((double)y.w, sc, rsc);
       }
-      reinterpret_cast<char4*>(qr)[i] = o;
+      reinterpret_cast<char4*>(q)[i] = o;
     }
   } else {
 #pragma unroll 1
-    for (int j = threadIdx.x; j < ldq; j += blockDim.x)
-      qr[j] = j < C ? dc_quant_div((double)ys[j], sc, rsc) : (int8_t)0;
+    for (int j = threadIdx.x; j < ldq; j += blockDim.x) q[j] = j < C ? dc_quant_div((double)ys[j], sc, rsc) : (int8_t)0;
   }
+}
+
+// RMSNorm of one row fused with quantizeRows of its output, one block per row.
+// x rows x C f32 -> q rows x ldq int8 (+ s[row]); the f32 norm output is not kept.
+__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, int C,
+                                                               const float* w, double eps,
+                                                               int8_t* q, int ldq,
+                                                               float* s, int* status,
+                                                               float* yo = nullptr,
+                                                               uint32_t* zrow = nullptr,
+                                                               int exact_sum = 0) {
+  extern __shared__ __align__(16) double sq[];  // C doubles (v*v), C floats (x, then y), C floats (w)
+  float* ys = (float*)(sq + C);
+  // the weight row rides along in shared memory when it fits (16 bytes per column)
+  float* wsm = 16 * (size_t)C + 20 * 1024 <= 232448 ? ys + C : nullptr;
+  __shared__ float red[32];
+  __shared__ double2 redd2[32];
+  __shared__ int vote[32];
+  __shared__ dco::Smem osm;
+  // the GEMV that consumes q may launch now: it streams its weights meanwhile
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int row = blockIdx.x;
+  const float* xr = x + (int64_t)row * C;
+  // float4 access when the row allows it (all loads of a thread in flight at once)
+  const bool vec = (C & 3) == 0 && ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  // The weight row is constant: its copy into shared memory (asynchronous,
+  // awaited after the input row's loads) starts before the grid-dependency
+  // wait.  Everything else this kernel reads or writes comes after it.
+  bool wpend = false;
+  if (vec && wsm) {
+    for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dcp::smem_u32(wsm + 4 * i)), "l"(w + 4 * i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    wpend = true;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (zrow && threadIdx.x == 0) zrow[row] = 0;  // the row maximum the next row quantisation collects
+  if (!vec && wsm)
+    for (int j = threadIdx.x; j < C; j += blockDim.x) wsm[j] = w[j];  // published by the block's first barrier
+  rmsnorm_quant_block<NORM_THREADS / 32>(xr, C, wsm ? wsm : w, wpend, vec, eps, sq, ys, q + (int64_t)row * ldq, ldq,
+                                          s + row, status, yo ? yo + (int64_t)row * C : nullptr, exact_sum, osm, red,
+                                          redd2, vote);
 }
 
 // The softmax denominator z (infer.js:100-104: z += e_j in key order, each
@@ -1262,26 +1294,33 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   }
 }
 
+// infer.js:59 + :212: f32(silu(g) * u), silu(v) = v / (1 + exp(-v)) in double
+// with the fdlibm exp.
+__device__ __forceinline__ float swiglu_f32(float gf, float uf) {
+  const double v = gf;
+  const double sl = __ddiv_rn(v, __dadd_rn(1.0, dcm::fdlibm_exp(-v)));
+  return __double2float_rn(__dmul_rn(sl, (double)uf));
+}
+
 // SwiGLU, element-parallel over grid (ceil(I/256), rows): hid = f32(silu(g)*u)
-// with silu(v) = v / (1 + exp(-v)) in double, written over g in place, and
+// with silu(v) = v / (1 + exp(-v)) in double, from the fused gate/up GEMM's
+// interleaved output row (g_j at 2j, u_j at 2j + 1) into hout (I per row), and
 // |hid| folded into the row maximum (rowmax must start at 0).  The row's
 // quantisation follows in k_rowquant once every block has contributed.
-__global__ void __launch_bounds__(256) k_swiglu(float* h, int I, uint32_t* rowmax,
+__global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* hout, uint32_t* rowmax,
                                                int* status) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   __shared__ float red[32];
   const int row = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  float* g = h + (int64_t)row * 2 * I;
+  const float* g = h + (int64_t)row * 2 * I;
   float mx = 0.0f;
   bool bad = false;
   if (j < I) {
-    const double v = g[j];
-    const double sl = __ddiv_rn(v, __dadd_rn(1.0, dcm::fdlibm_exp(-v)));
-    const float y = __double2float_rn(__dmul_rn(sl, (double)g[I + j]));
+    const float y = swiglu_f32(g[2 * j], g[2 * j + 1]);
     bad = !isfinite(y);
-    g[j] = y;
+    hout[(int64_t)row * I + j] = y;
     mx = fabsf(y);
   }
   mx = block_max_f(mx, red);
@@ -1303,6 +1342,152 @@ __global__ void __launch_bounds__(256) k_rowquant(const float* x, int64_t ldx, i
   if (j < ldq) q[(int64_t)row * ldq + j] = j < cols ? dc_quant_div((double)x[row * ldx + j], sc, __drcp_rn(sc)) : (int8_t)0;
 }
 
+
+// ---- the decode row's GEMVs with their neighbours fused ---------------------
+// A one-row GEMV (M = 1: the decode step of infer.js:353-365) whose int8
+// activation row each block forms on chip from the previous kernel's f32
+// output, so that no normalisation or quantisation kernel runs between two
+// GEMVs of a decode layer:
+//   FG_NORM   x (K floats) -> RMSNorm with weight nw (infer.js:30-39) ->
+//             quantizeRows (rmsnorm_quant_block: k_rmsnorm_quant's arithmetic);
+//   FG_ROWQ   x (K floats) whose |x| maximum the previous kernel folded into
+//             *rmax -> quantizeRows (k_rowquant's arithmetic);
+// and whose epilogue is the verified store (f32 epilogue, added to `out` with
+// DC_F_ADDTO: the residual) or
+//   FG_SWIGLU the weight rows interleaved (gate_j, up_j), so the warp holding
+//             both accumulators forms h_j = f32(silu(g_j) * u_j) (infer.js:59,
+//             212), writes it to out[j] and folds |h_j| into *rmax_out (zeroed
+//             by an earlier kernel of the step).
+// zero2, when not null, is set to {0, 0} by one thread after the wait (the row
+// maxima the step's later kernels collect).  512 threads, one block per SM;
+// each warp streams two weight rows at a time (16-byte non-allocating loads, 8
+// per lane in flight per row).  Before griddepcontrol.wait every warp asks L2
+// for its first two rows, so the weight stream is under way while the prologue
+// runs.  Dynamic shared memory: FG_NORM: 16*K bytes (squares, row, weight) +
+// ldK; FG_ROWQ: ldK (the int8 row).
+constexpr int FG_THREADS = 512;
+constexpr int FG_SEG = 8;
+enum { FG_NORM = 1, FG_ROWQ = 2, FG_SWIGLU = 4 };
+static size_t fg_smem(int mode, int K) {
+  return ((mode & FG_NORM) ? 16 * (size_t)K : 0) + (size_t)round_up(K, 16) + 16;
+}
+__device__ __forceinline__ int4 ld_weights16(const int4* p, uint64_t pol) {
+  int4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.s32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+template <int MODE>
+__global__ void __launch_bounds__(FG_THREADS, 1) k_gemv_fused(const float* x, int K, const float* nw, double eps,
+                                                              const uint32_t* rmax, const int8_t* __restrict__ Wt,
+                                                              int ldw, const float* __restrict__ cs, int n,
+                                                              unsigned flags, float* out, uint32_t* rmax_out,
+                                                              uint32_t* zero2, int* status) {
+  extern __shared__ __align__(16) uint8_t fsm[];
+  __shared__ float red[32];
+  __shared__ double2 redd2[32];
+  __shared__ int vote[32];
+  __shared__ float s_row;
+  __shared__ dco::Smem16 osm;
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gw = blockIdx.x * (FG_THREADS / 32) + warp, nwarps = gridDim.x * (FG_THREADS / 32);
+  const int ldK = (K + 15) & ~15;
+  double* sq = (double*)fsm;
+  float* ys = (float*)(fsm + 8 * (size_t)K);
+  float* wsm = ys + K;
+  int8_t* x8 = (int8_t*)(fsm + ((MODE & FG_NORM) ? 16 * (size_t)K : 0));
+  // constant data first: L2 requests for this warp's first two weight rows,
+  // and (FG_NORM) the norm weight into shared memory
+  if (gw * 2 < n) {
+    const char* r0 = (const char*)(Wt + (int64_t)(gw * 2) * ldw);
+    const char* r1 = (const char*)(Wt + (int64_t)min(gw * 2 + 1, n - 1) * ldw);
+    for (int c = lane * 128; c < K; c += 32 * 128) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(r0 + c));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(r1 + c));
+    }
+  }
+  const bool vec = (K & 3) == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(nw)) & 15) == 0;
+  bool wpend = false;
+  if ((MODE & FG_NORM) && vec) {
+    for (int i = threadIdx.x; i < (K >> 2); i += blockDim.x)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dcp::smem_u32(wsm + 4 * i)), "l"(nw + 4 * i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    wpend = true;
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (zero2 && blockIdx.x == 0 && threadIdx.x == 0) {
+    zero2[0] = 0;
+    zero2[1] = 0;
+  }
+  // ---- prologue: the int8 activation row in shared memory
+  if (MODE & FG_NORM) {
+    if (!vec)
+      for (int j = threadIdx.x; j < K; j += blockDim.x) wsm[j] = nw[j];  // published by the block's first barrier
+    rmsnorm_quant_block<FG_THREADS / 32>(x, K, wsm, wpend, vec, eps, sq, ys, x8, ldK, &s_row, status, nullptr, 0, osm,
+                                         red, redd2, vote);
+  } else {
+    const double sc = quant_scale(__uint_as_float(*rmax)), rsc = __drcp_rn(sc);
+    if (threadIdx.x == 0) s_row = __double2float_rn(sc);
+    for (int j = threadIdx.x; j < ldK; j += blockDim.x)
+      x8[j] = j < K ? dc_quant_div((double)x[j], sc, rsc) : (int8_t)0;
+  }
+  __syncthreads();
+  const float rsv = s_row;
+  // ---- the GEMV: two weight rows per warp at a time
+  const int nch = ldK >> 4;
+  const int4* X4 = (const int4*)x8;
+  const uint64_t pol = dcp::l2_evict_first();
+  bool bad = false;
+  float hmax = 0.0f;
+  for (int j0 = gw * 2; j0 < n; j0 += nwarps * 2) {
+    const int j1 = min(j0 + 1, n - 1);
+    const int4* w0 = (const int4*)(Wt + (int64_t)j0 * ldw);
+    const int4* w1 = (const int4*)(Wt + (int64_t)j1 * ldw);
+    int a0 = 0, a1 = 0;
+#pragma unroll 1
+    for (int c0 = 0; c0 < nch; c0 += 32 * FG_SEG) {
+      int4 wa[FG_SEG], wb[FG_SEG];
+#pragma unroll
+      for (int u = 0; u < FG_SEG; u++) {
+        const int c = c0 + u * 32 + lane;
+        wa[u] = c < nch ? ld_weights16(w0 + c, pol) : make_int4(0, 0, 0, 0);
+        wb[u] = c < nch ? ld_weights16(w1 + c, pol) : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < FG_SEG; u++) {
+        const int c = c0 + u * 32 + lane;
+        const int4 xv = c < nch ? X4[c] : make_int4(0, 0, 0, 0);
+        a0 = dp4a16(wa[u], xv, a0);
+        a1 = dp4a16(wb[u], xv, a1);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+    }
+    if (MODE & FG_SWIGLU) {
+      if (lane == 0) {
+        const float h = swiglu_f32(dc_epi(a0, rsv, cs[j0]), dc_epi(a1, rsv, cs[j1]));
+        bad |= !isfinite(h);
+        out[j0 >> 1] = h;
+        hmax = fmaxf(hmax, fabsf(h));
+      }
+    } else if (lane < 2 && (lane == 0 || j0 + 1 < n)) {
+      const int j = lane == 0 ? j0 : j1;
+      float v = dc_epi(lane == 0 ? a0 : a1, rsv, cs[j]);
+      if (flags & DC_F_ADDTO) v = __fadd_rn(out[j], v);  // residual: out = out + v (f32 add)
+      out[j] = v;
+    }
+  }
+  if (MODE & FG_SWIGLU) {
+    if (lane == 0 && hmax > 0.0f) atomicMax(rmax_out, __float_as_uint(hmax));
+    if (bad) atomicOr(status, DC_ST_NONFINITE);
+  }
+}
 
 __global__ void k_embed(const int32_t* __restrict__ ids, int T, const float* __restrict__ emb, int C, int V,
                         float* __restrict__ x, int* status) {
@@ -1393,7 +1578,10 @@ __device__ __forceinline__ float wsrc_at(const WSrc& s, int64_t r, int64_t c) {
   return __double2float_rn(__dmul_rn((double)acc, s.factor));
 }
 
-__global__ void __launch_bounds__(256) k_wscale(WSrc src, int k, int n, float* __restrict__ s, int* status) {
+// Source column c lands in destination column c * cstride (cstride 2
+// interleaves the gate and up projections: gate_j, up_j, gate_j+1, ...).
+__global__ void __launch_bounds__(256) k_wscale(WSrc src, int k, int n, int cstride, float* __restrict__ s,
+                                                int* status) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= n) return;
   float mx = 0.0f;
@@ -1404,10 +1592,10 @@ __global__ void __launch_bounds__(256) k_wscale(WSrc src, int k, int n, float* _
     mx = fmaxf(mx, fabsf(v));
   }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
-  s[c] = __double2float_rn(quant_scale(mx));
+  s[(int64_t)c * cstride] = __double2float_rn(quant_scale(mx));
 }
 
-__global__ void __launch_bounds__(256) k_wquant_t(WSrc src, int k, int n, const float* __restrict__ s,
+__global__ void __launch_bounds__(256) k_wquant_t(WSrc src, int k, int n, int cstride, const float* __restrict__ s,
                                                   int8_t* __restrict__ qt, int ldq) {
   __shared__ int8_t tile[32][33];
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
@@ -1415,13 +1603,14 @@ __global__ void __launch_bounds__(256) k_wquant_t(WSrc src, int k, int n, const 
   for (int i = ty; i < 32; i += 8) {
     const int r = r0 + i, c = c0 + tx;
     int8_t v = 0;
-    if (r < k && c < n) v = dc_clamp8(dc_js_round(__ddiv_rn((double)wsrc_at(src, r, c), (double)s[c])));
+    if (r < k && c < n)
+      v = dc_clamp8(dc_js_round(__ddiv_rn((double)wsrc_at(src, r, c), (double)s[(int64_t)c * cstride])));
     tile[i][tx] = v;
   }
   __syncthreads();
   for (int i = ty; i < 32; i += 8) {
     const int c = c0 + i, r = r0 + tx;
-    if (c < n && r < ldq) qt[(int64_t)c * ldq + r] = r < k ? tile[tx][i] : (int8_t)0;
+    if (c < n && r < ldq) qt[(int64_t)c * cstride * ldq + r] = r < k ? tile[tx][i] : (int8_t)0;
   }
 }
 
@@ -1463,14 +1652,15 @@ static int mat_alloc(dc_stage* S, dc_mat& m, int k, int n) {
 }
 
 // Quantise one source matrix (k x n_src) into columns [col0, col0 + n_src) of m.
-static int mat_load(dc_stage* S, dc_mat& m, int col0, const WSrc& src, int n_src) {
+// Quantise a k x n_src source into columns col0, col0 + cstride, ... of m.
+static int mat_load(dc_stage* S, dc_mat& m, int col0, const WSrc& src, int n_src, int cstride = 1) {
   cudaStream_t st = S->ctx->stream;
   float* s = m.cs + col0;
   int8_t* qt = m.qt + (int64_t)col0 * m.ldk;
-  k_wscale<<<(n_src + 255) / 256, 256, 0, st>>>(src, m.k, n_src, s, S->ctx->d_status); dc_count_launch();
+  k_wscale<<<(n_src + 255) / 256, 256, 0, st>>>(src, m.k, n_src, cstride, s, S->ctx->d_status); dc_count_launch();
   DC_CUDA(S->ctx, cudaGetLastError());
   dim3 grid((n_src + 31) / 32, (m.ldk + 31) / 32);
-  k_wquant_t<<<grid, 256, 0, st>>>(src, m.k, n_src, s, qt, m.ldk); dc_count_launch();
+  k_wquant_t<<<grid, 256, 0, st>>>(src, m.k, n_src, cstride, s, qt, m.ldk); dc_count_launch();
   DC_CUDA(S->ctx, cudaGetLastError());
   return DC_OK;
 }
@@ -1555,10 +1745,11 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
   }
   const int wide = std::max(std::max(S->nqkv, 2 * S->I), S->C);
   if ((rc = st_alloc(S, (void**)&S->hbuf, 4 * (size_t)max_rows * wide)) ||
+      (rc = st_alloc(S, (void**)&S->hmid, 4 * (size_t)max_rows * S->I)) ||
       (rc = st_alloc(S, (void**)&S->ctxo, 4 * (size_t)max_rows * S->qDim)) ||
       (rc = st_alloc(S, (void**)&S->xq, (size_t)max_rows * std::max(std::max(S->ldC, S->ldQ), S->ldI))) ||
       (rc = st_alloc(S, (void**)&S->rs, 4 * (size_t)max_rows)) ||
-      (rc = st_alloc(S, (void**)&S->rowmax, 4 * (size_t)max_rows)) ||
+      (rc = st_alloc(S, (void**)&S->rowmax, 4 * (size_t)std::max(max_rows, 2))) ||
       (rc = st_alloc(S, (void**)&S->d_pos, 16)) || (rc = st_alloc(S, (void**)&S->d_zero, 16)) ||
       (rc = st_alloc(S, (void**)&S->d_step, 16)) || (rc = st_alloc(S, (void**)&S->xlap, 4 * (size_t)S->C)) ||
       (rc = st_alloc(S, (void**)&S->logits1, 4 * (size_t)(head ? S->V : 1))) ||
@@ -1620,10 +1811,10 @@ static WSrc f32src(const float* dW, int k, int n) {
   return s;
 }
 
-// Upload one host k x n matrix and quantise it into columns [col0, col0+n) of m.
-static int load_host(dc_stage* S, dc_mat& m, int col0, const float* W, int k, int n, float* tmp) {
+// Upload one host k x n matrix and quantise it into columns col0, col0 + cstride, ... of m.
+static int load_host(dc_stage* S, dc_mat& m, int col0, const float* W, int k, int n, float* tmp, int cstride = 1) {
   DC_CUDA(S->ctx, cudaMemcpyAsync(tmp, W, 4 * (size_t)k * n, cudaMemcpyHostToDevice, S->ctx->stream));
-  return mat_load(S, m, col0, f32src(tmp, k, n), n);
+  return mat_load(S, m, col0, f32src(tmp, k, n), n, cstride);
 }
 
 extern "C" int dc_stage_set_layer(dc_stage* S, int layer, const float* nrm1, const float* nrm2, const float* Wq,
@@ -1652,9 +1843,9 @@ extern "C" int dc_stage_set_layer(dc_stage* S, int layer, const float* nrm1, con
   if (!rc) rc = dc_sync(ctx);
   if (!rc) rc = load_host(S, ly.o, 0, Wo, S->qDim, S->C, tmp);
   if (!rc) rc = dc_sync(ctx);
-  if (!rc) rc = load_host(S, ly.gu, 0, Wgate, S->C, S->I, tmp);
+  if (!rc) rc = load_host(S, ly.gu, 0, Wgate, S->C, S->I, tmp, 2);  // gate_j in column 2j
   if (!rc) rc = dc_sync(ctx);
-  if (!rc) rc = load_host(S, ly.gu, S->I, Wup, S->C, S->I, tmp);
+  if (!rc) rc = load_host(S, ly.gu, 1, Wup, S->C, S->I, tmp, 2);    // up_j in column 2j + 1
   if (!rc) rc = dc_sync(ctx);
   if (!rc) rc = load_host(S, ly.down, 0, Wdown, S->I, S->C, tmp);
   if (!rc) rc = dc_sync(ctx);
@@ -1718,8 +1909,8 @@ extern "C" int dc_stage_synth(dc_stage* S, uint64_t model_seed, double factor) {
     if (!rc) rc = mat_load(S, ly.qkv, S->qDim, src(l, 4, S->C, S->kvDim), S->kvDim);
     if (!rc) rc = mat_load(S, ly.qkv, S->qDim + S->kvDim, src(l, 5, S->C, S->kvDim), S->kvDim);
     if (!rc) rc = mat_load(S, ly.o, 0, src(l, 6, S->qDim, S->C), S->C);
-    if (!rc) rc = mat_load(S, ly.gu, 0, src(l, 7, S->C, S->I), S->I);
-    if (!rc) rc = mat_load(S, ly.gu, S->I, src(l, 8, S->C, S->I), S->I);
+    if (!rc) rc = mat_load(S, ly.gu, 0, src(l, 7, S->C, S->I), S->I, 2);  // gate_j in column 2j
+    if (!rc) rc = mat_load(S, ly.gu, 1, src(l, 8, S->C, S->I), S->I, 2);  // up_j in column 2j + 1
     if (!rc) rc = mat_load(S, ly.down, 0, src(l, 9, S->I, S->C), S->C);
   }
   if (!rc && S->head) {
@@ -1795,6 +1986,41 @@ static cudaError_t launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// The fused one-row GEMV fits on chip when its norm row does (16 bytes per
+// column plus the int8 row, below the 227 KB a block may have).
+static bool fg_fits(const dc_stage* S) {
+  return fg_smem(FG_NORM, S->C) + 24 * 1024 <= 232448 && fg_smem(FG_ROWQ, S->I) + 24 * 1024 <= 232448;
+}
+
+// k_gemv_fused<mode> over the weight m (out = epilogue of m's n columns; with
+// FG_SWIGLU the n/2 SwiGLU values), launched as a programmatic dependent.
+static cudaError_t launch_fused(dc_stage* S, int mode, const float* x, int K, const float* nw, const uint32_t* rmax,
+                                const dc_mat& m, unsigned flags, float* out, uint32_t* rmax_out, uint32_t* zero2) {
+  dc_ctx* ctx = S->ctx;
+  const int blocks = std::max(1, std::min(ctx->sm_count, (m.n + 31) / 32));
+  const size_t smem = fg_smem(mode, K);
+  cudaError_t e;
+  switch (mode) {
+    case FG_NORM:
+      e = launch_dep(k_gemv_fused<FG_NORM>, dim3(blocks), dim3(FG_THREADS), smem, ctx->stream, x, K, nw,
+                     S->spec.norm_eps, rmax, (const int8_t*)m.qt, m.ldk, (const float*)m.cs, m.n, flags, out, rmax_out,
+                     zero2, ctx->d_status);
+      break;
+    case FG_NORM | FG_SWIGLU:
+      e = launch_dep(k_gemv_fused<FG_NORM | FG_SWIGLU>, dim3(blocks), dim3(FG_THREADS), smem, ctx->stream, x, K, nw,
+                     S->spec.norm_eps, rmax, (const int8_t*)m.qt, m.ldk, (const float*)m.cs, m.n, flags, out, rmax_out,
+                     zero2, ctx->d_status);
+      break;
+    default:
+      e = launch_dep(k_gemv_fused<FG_ROWQ>, dim3(blocks), dim3(FG_THREADS), smem, ctx->stream, x, K, nw,
+                     S->spec.norm_eps, rmax, (const int8_t*)m.qt, m.ldk, (const float*)m.cs, m.n, flags, out, rmax_out,
+                     zero2, ctx->d_status);
+      break;
+  }
+  dc_count_launch();
+  return e;
+}
+
 // The layer loop of one stage on T rows of x (in place).  Every position the
 // kernels need is read from *n0p (the cached tokens before this call; 0 for the
 // full window), so the same launches can be captured once in a CUDA graph and
@@ -1833,14 +2059,26 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   const size_t nrm_smem = rms_smem(S->C);
   // always raised: the kernel's static shared memory counts against the 48 KB default too
   if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
+  // a decode row: GEMVs with the norms, the SwiGLU and the row quantisation fused
+  const bool fuse = T == 1 && use_kv && dec_ch && S->row_fused && fg_fits(S);
+  if (fuse) {
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM>, (int)fg_smem(FG_NORM, S->C))) return rc0;
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM | FG_SWIGLU>, (int)fg_smem(FG_NORM, S->C)))
+      return rc0;
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_ROWQ>, (int)fg_smem(FG_ROWQ, S->I))) return rc0;
+  }
   int rc;
   for (auto& ly : S->L) {
     dc_kv& kv = ly.kv;
     // attention block
-    DC_CUDA(ctx, launch_dep(k_rmsnorm_quant, dim3(T), dim3(NORM_THREADS), nrm_smem, st, x, S->C, ly.nrm1,
-                            S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
-    dc_count_launch();
-    if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
+    if (fuse) {  // RMSNorm + QKV; zeroes the row maxima the attention and the SwiGLU collect
+      DC_CUDA(ctx, launch_fused(S, FG_NORM, x, S->C, ly.nrm1, nullptr, ly.qkv, 0, S->hbuf, nullptr, S->rowmax));
+    } else {
+      DC_CUDA(ctx, launch_dep(k_rmsnorm_quant, dim3(T), dim3(NORM_THREADS), nrm_smem, st, x, S->C, ly.nrm1,
+                              S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
+      dc_count_launch();
+      if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
+    }
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
     const int vblocks = (S->kvDim + 63) / 64;
     DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
@@ -1909,14 +2147,21 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, x, DC_F_ADDTO))) return rc;  // x2 = x + attn
     // MLP block
+    if (fuse) {  // RMSNorm + gate/up + SwiGLU; then the down projection quantises its own input
+      DC_CUDA(ctx, launch_fused(S, FG_NORM | FG_SWIGLU, x, S->C, ly.nrm2, nullptr, ly.gu, 0, S->hmid, S->rowmax + 1,
+                                nullptr));
+      DC_CUDA(ctx, launch_fused(S, FG_ROWQ, S->hmid, S->I, nullptr, S->rowmax + 1, ly.down, DC_F_ADDTO, x, nullptr,
+                                nullptr));
+      continue;
+    }
     DC_CUDA(ctx, launch_dep(k_rmsnorm_quant, dim3(T), dim3(NORM_THREADS), nrm_smem, st, x, S->C, ly.nrm2,
                             S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
     dc_count_launch();
     if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
-    DC_CUDA(ctx, launch_dep(k_swiglu, dim3((S->I + 255) / 256, T), dim3(256), 0, st, S->hbuf, S->I, S->rowmax,
+    DC_CUDA(ctx, launch_dep(k_swiglu, dim3((S->I + 255) / 256, T), dim3(256), 0, st, S->hbuf, S->I, S->hmid, S->rowmax,
                             ctx->d_status));
     dc_count_launch();
-    DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldI + 255) / 256, T), dim3(256), 0, st, S->hbuf, 2 * (int64_t)S->I,
+    DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldI + 255) / 256, T), dim3(256), 0, st, S->hmid, (int64_t)S->I,
                             S->I, S->rowmax, S->xq, S->ldI, S->rs));
     dc_count_launch();
     if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, x, DC_F_ADDTO))) return rc;  // out = x2 + down
@@ -1994,6 +2239,19 @@ extern "C" int dc_stage_set_row_graph(dc_stage* S, int on) {
   return DC_OK;
 }
 
+extern "C" int dc_stage_set_row_fusion(dc_stage* S, int on) {
+  if (!S) return DC_E_INVAL;
+  if ((on != 0) != S->row_fused) {  // captured graphs hold the other kernel sequence
+    if (S->row_exec) cudaGraphExecDestroy(S->row_exec);
+    S->row_exec = nullptr;
+    if (S->lap_exec) cudaGraphExecDestroy(S->lap_exec);
+    S->lap_exec = nullptr;
+    S->lap_key.clear();
+  }
+  S->row_fused = on != 0;
+  return DC_OK;
+}
+
 extern "C" int dc_stage_forward(dc_stage* S, float* x, int T, int pos0, int use_kv) {
   if (!S || !x || T < 1 || T > S->max_rows) return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_forward: bad T");
   dc_ctx* ctx = S->ctx;
@@ -2030,15 +2288,21 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
   dc_stage* H = st[0];
   dc_ctx* ctx = H->ctx;
   cudaStream_t s = ctx->stream;
-  const size_t nrm_smem = rms_smem(H->C);
-  // always raised: the kernel's static shared memory counts against the 48 KB default too
-  if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
-  k_rmsnorm_quant<<<1, NORM_THREADS, nrm_smem, s>>>(H->xlap, H->C, H->nrmF, H->spec.norm_eps, H->xq, H->ldC, H->rs,
-                                                     ctx->d_status);
-  dc_count_launch();
-  int rc = dc_gemm_dispatch(ctx, H->xq, H->ldC, H->lm.qt, H->lm.ldk, H->rs, H->lm.cs, 1, H->C, H->V, 1, 0, H->logits1,
-                            s, 0);
-  if (rc) return rc;
+  int rc = DC_OK;
+  if (H->row_fused && fg_fits(H)) {  // final RMSNorm fused into the lm_head GEMV
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM>, (int)fg_smem(FG_NORM, H->C))) return rc0;
+    DC_CUDA(ctx, launch_fused(H, FG_NORM, H->xlap, H->C, H->nrmF, nullptr, H->lm, 0, H->logits1, nullptr, nullptr));
+  } else {
+    const size_t nrm_smem = rms_smem(H->C);
+    // always raised: the kernel's static shared memory counts against the 48 KB default too
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
+    k_rmsnorm_quant<<<1, NORM_THREADS, nrm_smem, s>>>(H->xlap, H->C, H->nrmF, H->spec.norm_eps, H->xq, H->ldC, H->rs,
+                                                       ctx->d_status);
+    dc_count_launch();
+    rc = dc_gemm_dispatch(ctx, H->xq, H->ldC, H->lm.qt, H->lm.ldk, H->rs, H->lm.cs, 1, H->C, H->V, 1, 0, H->logits1, s,
+                          0);
+    if (rc) return rc;
+  }
   if ((rc = launch_argmax(H, H->logits1, 1, picks, H->d_step))) return rc;
   k_embed_at<<<1, 256, 0, s>>>(picks, H->d_step, H->emb, H->C, H->V, H->xlap, ctx->d_status);
   dc_count_launch();

@@ -224,6 +224,11 @@ class Stage:
         """One-row cached forwards (decode steps) as a CUDA graph (default) or kernel by kernel."""
         self._check(self.L.dc_stage_set_row_graph(self.h, 1 if on else 0), "set_row_graph")
 
+    def set_row_fusion(self, on: bool) -> None:
+        """Decode rows with the norm / SwiGLU / row quantisation fused into their
+        GEMVs (default) or as separate kernels; the results are identical."""
+        self._check(self.L.dc_stage_set_row_fusion(self.h, 1 if on else 0), "set_row_fusion")
+
     def kv_len(self) -> int:
         return self.L.dc_stage_kv_len(self.h)
 

@@ -224,6 +224,13 @@ int dc_stage_forward(dc_stage* stage, float* x, int T, int pos0, int use_kv);
  * (the default).  on = 0 launches the kernels one by one instead; the results
  * are identical. */
 int dc_stage_set_row_graph(dc_stage* stage, int on);
+/* One-row cached forwards (decode steps, and the head's logits in
+ * dc_decode_run) run their GEMVs with the neighbouring row operations fused
+ * into them (the default): the RMSNorm before the QKV and gate/up projections
+ * and before lm_head, the SwiGLU after gate/up, the down projection's row
+ * quantisation.  on = 0 runs those as separate kernels; the results are
+ * identical (the same arithmetic, infer.js:30-39, 59, 199-219). */
+int dc_stage_set_row_fusion(dc_stage* stage, int on);
 /* logitsAt (infer.js:324-334) for rows[0..nrows) (host ints, nrows <= 8):
  * logits (device, nrows x vocab) and the greedy pick of each row (device int32,
  * may be NULL), first maximum wins (infer.js:393-395). */

@@ -218,5 +218,11 @@ def test_synthetic_model_device_generator_matches_oracle(comp, O, P, cfg):
         assert x.cpu().numpy().tobytes() == want.tobytes(), f"synth={synth}"
         picks, logits = st[0].logits_at(x, [len(ids) - 1])
         assert logits.cpu().numpy().tobytes() == om.logits_rows(want, [len(ids) - 1]).tobytes()
-    got = P.infer.generate_chunked(st, ids, 6, 16)
-    assert got == O.generate_chunked(om, [(0, cfg["layers"])], ids, 6, 16)
+    want = O.generate_chunked(om, [(0, cfg["layers"])], ids, 6, 16)
+    for fused in (True, False):  # decode rows with the norm/SwiGLU/row quantisation fused into the GEMVs, or not
+        for S in st:
+            S.set_row_fusion(fused)
+        got = P.infer.generate_chunked(st, ids, 6, 16)
+        assert got == want, f"fused={fused}"
+        got = P.infer.generate_chunked(st, ids, 6, 16, use_device_loop=False)  # one-row graphs per stage
+        assert got == want, f"fused={fused}, host loop"
