@@ -161,8 +161,10 @@ int gate_one(dc_ctx* c, const GateShape& g, int kind, bool poison, uint32_t seed
   cudaMemsetAsync(dXp, 0, nxp, st);
   cudaMemcpy2DAsync(dXp, ld, dX, k, k, (size_t)B * m, cudaMemcpyDeviceToDevice, st);
   rc = dc_launch_transpose_i8(c, dW, k, n, dWt, ld, B, st);
-  const unsigned modes[2] = {DC_ACC, (unsigned)(g.relu ? DC_RELU : 0)};
-  for (int mi = 0; mi < 2 && rc == DC_OK; mi++) {
+  // accumulators, the f32 epilogue, and the requant unit (int8 out; the kernels
+  // evaluate the units' definition, the LUT kernel reads the tables)
+  const unsigned modes[3] = {DC_ACC, (unsigned)(g.relu ? DC_RELU : 0), (unsigned)(DC_REQUANT | (g.relu ? DC_RELU : 0))};
+  for (int mi = 0; mi < 3 && rc == DC_OK; mi++) {
     cudaMemsetAsync(o1, poison ? 0x7F : 0, 4 * no, st);
     cudaMemsetAsync(o2, poison ? 0x7F : 0, 4 * no, st);
     rc = dc_gemm_lut(c, dX, dW, drs, dcs, m, k, n, B, modes[mi], o1, st);
@@ -181,7 +183,8 @@ int gate_one(dc_ctx* c, const GateShape& g, int kind, bool poison, uint32_t seed
         if (h1[i] != h2[i]) {
           char b[256];
           snprintf(b, sizeof b, "%s mismatch @%zu (%dx%dx%d b%d, kernel %d%s): 0x%08x vs LUT 0x%08x",
-                   mi == 0 ? "accumulator" : "epilogue", i, m, k, n, B, kind, poison ? ", poisoned" : "",
+                   mi == 0 ? "accumulator" : (mi == 1 ? "epilogue" : "requant"), i, m, k, n, B, kind,
+                   poison ? ", poisoned" : "",
                    (unsigned)h2[i], (unsigned)h1[i]);
           why = b;
           rc = DC_E_GATE;

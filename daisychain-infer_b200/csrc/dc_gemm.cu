@@ -35,7 +35,7 @@ __global__ void k_lut_gemm(const int8_t* __restrict__ X, const int8_t* __restric
   const int8_t* wc = W + (int64_t)bz * k * n + col;
   uint32_t s = 0;
   for (int p = 0; p < k; p++) s += (uint32_t)(int32_t)__ldg(mul + ((uint8_t)xr[p]) * 256 + (uint8_t)wc[(int64_t)p * n]);
-  dc_store_out(out, ((int64_t)bz * m + row) * n + col, (int32_t)s, rs[bz * m + row], cs[bz * n + col], flags, requant,
+  dc_store_out_lut(out, ((int64_t)bz * m + row) * n + col, (int32_t)s, rs[bz * m + row], cs[bz * n + col], flags, requant,
                relu);
 }
 
@@ -178,6 +178,26 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
     const int j1 = min(j0 + 1, n - 1);
     const int4* w0 = (const int4*)(Wt + (int64_t)j0 * ldw);
     const int4* w1 = (const int4*)(Wt + (int64_t)j1 * ldw);
+    // L2 requests ahead of the register loads: the rest of these two rows past
+    // the first segment, and the warp's next two rows, so each later round
+    // trip of the warp starts from L2 instead of DRAM
+    {
+      const int jn = j0 + nw * 2;
+      const char* p0 = (const char*)w0;
+      const char* p1 = (const char*)w1;
+      for (int b = 32 * GV_SEG * 16 + lane * 128; b < k; b += 32 * 128) {
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p0 + b));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p1 + b));
+      }
+      if (jn < n) {
+        const char* q0 = (const char*)(Wt + (int64_t)jn * ldw);
+        const char* q1 = (const char*)(Wt + (int64_t)min(jn + 1, n - 1) * ldw);
+        for (int b = lane * 128; b < k; b += 32 * 128) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(q0 + b));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(q1 + b));
+        }
+      }
+    }
     const float csv = cs[lane == 1 ? j1 : j0];  // the epilogue's column scale, loaded with the weights
     int a0 = 0, a1 = 0;
 #pragma unroll 1

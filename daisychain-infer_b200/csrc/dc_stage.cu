@@ -262,7 +262,8 @@ __device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, cons
   // When every y_j is the same at both ends of the bracket, it is the serial
   // sum's y_j; otherwise (rare: some y_j within ~1e-13 of an f32 rounding
   // boundary) the block computes the serial-order sum itself.
-  double inv;
+  float mx = 0.0f;
+  bool any = false;
   {
     double part = 0.0, wpart = 0.0;
     for (int j = threadIdx.x; j < C; j += blockDim.x) {
@@ -272,46 +273,64 @@ __device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, cons
     const double2 sw = block_sum_d2(part, wpart, redd2);
     const double h = serial_sum_radius(sw.x, sw.y, (C + (int)blockDim.x - 1) / (int)blockDim.x + 10);
     const double inv_hi = rms_inv(sw.x - h, C, eps), inv_lo = rms_inv(sw.x + h, C, eps);
+    // Both ends of the bracket in one pass: the value at the lower end is kept
+    // (the serial sum's whenever no output is ambiguous), with its |y| maximum.
     bool amb = exact_sum != 0;
-    for (int j = threadIdx.x; j < C && !amb; j += blockDim.x) {
-      const double xw = (double)ys[j], wj = (double)wr[j];
-      amb |= __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_lo), wj)) !=
-             __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_hi), wj));
-    }
-    const bool wamb = __any_sync(0xffffffffu, amb);
-    if ((threadIdx.x & 31) == 0) vote[threadIdx.x >> 5] = wamb ? 1 : 0;
-    __syncthreads();
-    bool any = false;
-    for (int wv = 0; wv < (int)(blockDim.x >> 5); wv++) any |= vote[wv] != 0;
-    inv = inv_lo;
-    if (any) inv = rms_inv(OsumCold<NW>::sum(sq, C, osm), C, eps);
-  }
-  float mx = 0.0f;
-  if (vec) {
+    if (vec) {
 #pragma unroll 2
-    for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
-      const float4 wv = reinterpret_cast<const float4*>(wr)[i];
-      float4 y = reinterpret_cast<const float4*>(ys)[i];
-      y.x = __double2float_rn(__dmul_rn(__dmul_rn((double)y.x, inv), (double)wv.x));
-      y.y = __double2float_rn(__dmul_rn(__dmul_rn((double)y.y, inv), (double)wv.y));
-      y.z = __double2float_rn(__dmul_rn(__dmul_rn((double)y.z, inv), (double)wv.z));
-      y.w = __double2float_rn(__dmul_rn(__dmul_rn((double)y.w, inv), (double)wv.w));
-      reinterpret_cast<float4*>(ys)[i] = y;
-      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+      for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x) {
+        const float4 wv = reinterpret_cast<const float4*>(wr)[i];
+        float4 y = reinterpret_cast<const float4*>(ys)[i];
+        const float4 x = y;
+        y.x = __double2float_rn(__dmul_rn(__dmul_rn((double)x.x, inv_lo), (double)wv.x));
+        y.y = __double2float_rn(__dmul_rn(__dmul_rn((double)x.y, inv_lo), (double)wv.y));
+        y.z = __double2float_rn(__dmul_rn(__dmul_rn((double)x.z, inv_lo), (double)wv.z));
+        y.w = __double2float_rn(__dmul_rn(__dmul_rn((double)x.w, inv_lo), (double)wv.w));
+        amb |= y.x != __double2float_rn(__dmul_rn(__dmul_rn((double)x.x, inv_hi), (double)wv.x)) ||
+               y.y != __double2float_rn(__dmul_rn(__dmul_rn((double)x.y, inv_hi), (double)wv.y)) ||
+               y.z != __double2float_rn(__dmul_rn(__dmul_rn((double)x.z, inv_hi), (double)wv.z)) ||
+               y.w != __double2float_rn(__dmul_rn(__dmul_rn((double)x.w, inv_hi), (double)wv.w));
+        reinterpret_cast<float4*>(ys)[i] = y;
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+      }
+    } else {
+      for (int j = threadIdx.x; j < C; j += blockDim.x) {
+        const double xw = (double)ys[j], wj = (double)wr[j];
+        const float y = __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_lo), wj));
+        amb |= y != __double2float_rn(__dmul_rn(__dmul_rn(xw, inv_hi), wj));
+        ys[j] = y;
+        mx = fmaxf(mx, fabsf(y));
+      }
     }
-  } else {
+    // one exchange carries the ambiguity vote and the row maximum
+    const bool wamb = __any_sync(0xffffffffu, amb);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) {
+      vote[threadIdx.x >> 5] = wamb ? 1 : 0;
+      red[threadIdx.x >> 5] = mx;
+    }
+    __syncthreads();
+    for (int wv = 0; wv < (int)(blockDim.x >> 5); wv++) {
+      any |= vote[wv] != 0;
+      mx = fmaxf(mx, red[wv]);
+    }
+  }
+  if (any) {  // rare: the serial-order sum, then the outputs again from the input row
+    const double inv = rms_inv(OsumCold<NW>::sum(sq, C, osm), C, eps);
+    mx = 0.0f;
     for (int j = threadIdx.x; j < C; j += blockDim.x) {
-      float y = __double2float_rn(__dmul_rn(__dmul_rn((double)ys[j], inv), (double)wr[j]));
+      const float y = __double2float_rn(__dmul_rn(__dmul_rn((double)xr[j], inv), (double)wr[j]));
       ys[j] = y;
       mx = fmaxf(mx, fabsf(y));
     }
+    mx = block_max_f(mx, red);  // (its barriers also publish ys)
   }
   if (yo) {  // the normalised row itself (infer.js rmsnorm), no quantisation
     __syncthreads();
     for (int j = threadIdx.x; j < C; j += blockDim.x) yo[j] = ys[j];
     return;
   }
-  mx = block_max_f(mx, red);
   const double sc = quant_scale(mx), rsc = __drcp_rn(sc);
   if (threadIdx.x == 0) s[0] = __double2float_rn(sc);
   if (vec && (ldq & 3) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
@@ -333,9 +352,13 @@ __device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, cons
   }
 }
 
-// RMSNorm of one row fused with quantizeRows of its output, one block per row.
+// RMSNorm of one row fused with quantizeRows of its output, one block of NT
+// threads per row (NORM_WIDE for rows that run alone or in a single wave: a
+// one-row norm is a chain of dependent phases, and wider blocks shorten each).
 // x rows x C f32 -> q rows x ldq int8 (+ s[row]); the f32 norm output is not kept.
-__global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, int C,
+constexpr int NORM_WIDE = 512;
+template <int NT>
+__global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* x, int C,
                                                                const float* w, double eps,
                                                                int8_t* q, int ldq,
                                                                float* s, int* status,
@@ -349,7 +372,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
   __shared__ float red[32];
   __shared__ double2 redd2[32];
   __shared__ int vote[32];
-  __shared__ dco::Smem osm;
+  __shared__ dco::SmemT<NT / 32> osm;
   // the GEMV that consumes q may launch now: it streams its weights meanwhile
   asm volatile("griddepcontrol.launch_dependents;");
   const int row = blockIdx.x;
@@ -371,7 +394,7 @@ __global__ void __launch_bounds__(NORM_THREADS) k_rmsnorm_quant(const float* x, 
   if (zrow && threadIdx.x == 0) zrow[row] = 0;  // the row maximum the next row quantisation collects
   if (!vec && wsm)
     for (int j = threadIdx.x; j < C; j += blockDim.x) wsm[j] = w[j];  // published by the block's first barrier
-  rmsnorm_quant_block<NORM_THREADS / 32>(xr, C, wsm ? wsm : w, wpend, vec, eps, sq, ys, q + (int64_t)row * ldq, ldq,
+  rmsnorm_quant_block<NT / 32>(xr, C, wsm ? wsm : w, wpend, vec, eps, sq, ys, q + (int64_t)row * ldq, ldq,
                                           s + row, status, yo ? yo + (int64_t)row * C : nullptr, exact_sum, osm, red,
                                           redd2, vote);
 }
@@ -1036,17 +1059,16 @@ __device__ __noinline__ double dcl_exact_z(double* xs, float* af, int N, int S, 
 // Every CTA takes every cluster barrier on every path.
 __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv, int nH, int nKV, int hd,
                                                        const int8_t* k8, const float* ks,
-                                                       const int8_t* v8t, const float* vs,
+                                                       int8_t* v8t, const float* vs,
                                                        const int* n0p, int max_pos, int ldp, int CH,
                                                        double scale, float* out,
                                                        uint32_t* rowmax, int* done,
                                                        int8_t* xq, int ldq, float* rsq,
-                                                       int* status) {
+                                                       int* status, const float* vcache, const int* vchg) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   extern __shared__ __align__(16) uint8_t sm[];
   asm volatile("griddepcontrol.launch_dependents;");  // the O projection may start streaming its weights
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int ldpv = ldp;
   int8_t* sK = (int8_t*)sm;                                    // ATTD_NS slots x ATTD_KB x hd
   int8_t* sV = sK + ATTD_NS * ATTD_KB * hd;                    // CH x ldpv
@@ -1068,6 +1090,12 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const int hq = blockIdx.x, c0 = r * CH;
   const int g = hq / (nH / nKV);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The position counter is set before the step's first kernel runs, and the
+  // keys, key scales and int8 values of positions below n0 were written by
+  // earlier steps: they are read before the grid-dependency wait, so their
+  // copies overlap the kernels in front of this one.  Position n0 (this
+  // step's key and value) and the value channels whose scale moved this step
+  // come after it.
   const int n0 = *n0p, N = n0 + 1;
   const int ldpN = (N + 15) & ~15;
   const int nb = (N + ATTD_KB - 1) / ATTD_KB;
@@ -1082,24 +1110,38 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   __syncthreads();
   int issued[ATTD_NS];
   for (int i = 0; i < ATTD_NS; i++) issued[i] = -1;
+  const uint32_t s_old = (uint32_t)((n0 & ~3) * 4);      // key scales below n0, before the wait
+  const uint32_t s_all = (uint32_t)(((N + 3) & ~3) * 4);  // all of them
+  auto key_block = [&](int i) {  // lane 0 of warp 0: the CTA's i-th key block into ring slot i
+    issued[i] = i;
+    const int b = r + i * S;
+    const int kn = min(ATTD_KB, N - b * ATTD_KB);
+    const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
+    dcp::mbar_expect_tx(&full[i], bytes + (i == 0 ? s_all : 0u));  // the key scales ride with the first block
+    dcp::bulk_load(sK + (size_t)i * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[i]);
+  };
   if (warp == 0) {
     if (lane == 0) dcp::mbar_expect_tx(&vbar, (uint32_t)(CH * ldpN));
     __syncwarp();
     #pragma unroll 1
     for (int c = lane; c < CH; c += 32)
       dcp::bulk_load(sV + (size_t)c * ldpv, v8t + ((int64_t)g * hd + c0 + c) * ldp, (uint32_t)ldpN, &vbar);
-    if (lane == 0)
+    if (lane == 0) {
       #pragma unroll 1
-      for (int i = 0; i < ATTD_NS && i < nmine; i++) {
-        issued[i] = i;
-        const int b = r + i * S;
-        const int kn = min(ATTD_KB, N - b * ATTD_KB);
-        const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
-        const uint32_t sbytes = i == 0 ? (uint32_t)(((N + 3) & ~3) * 4) : 0u;  // key scales with the first block
-        dcp::mbar_expect_tx(&full[i], bytes + sbytes);
-        dcp::bulk_load(sK + (size_t)i * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[i]);
-        if (sbytes) dcp::bulk_load(af, ks + (int64_t)g * max_pos, sbytes, &full[i]);
-      }
+      for (int i = 0; i < ATTD_NS && i < nmine; i++)
+        if ((r + i * S + 1) * ATTD_KB <= n0) key_block(i);  // every key of the block is older than n0
+      // the older key scales, once the first block's barrier expects them
+      if (issued[0] >= 0 && s_old) dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_old, &full[0]);
+    }
+  }
+  const bool scales_early = issued[0] >= 0;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  if (warp == 0 && lane == 0 && nmine > 0) {
+    #pragma unroll 1
+    for (int i = 0; i < ATTD_NS && i < nmine; i++)
+      if (issued[i] < 0) key_block(i);
+    const uint32_t from = scales_early ? s_old : 0u;
+    dcp::bulk_load(af + (from >> 2), ks + (int64_t)g * max_pos + (from >> 2), s_all - from, &full[0]);
   }
   // 1. the query row, quantised
   const float* qrow = h + hq * hd;
@@ -1245,6 +1287,37 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const bool vok = dcp::mbar_wait(&vbar, 0, status);
   if (!vok) abort_flag = 1;
   __syncthreads();
+  if (!abort_flag && vcache) {
+    // The value rows came in before the grid-dependency wait.  This step's
+    // column n0 (appended under the channel's new scale) is taken now, and a
+    // channel whose scale moved this step is re-quantised here from the f32
+    // cache (k_vquant_dev's arithmetic); the first head of the KV group writes
+    // those rows back for the next steps (another head reading them meanwhile
+    // re-quantises the same channel itself).
+    const int kvDim = nKV * hd;
+    const bool writer = hq % (nH / nKV) == 0;
+    // the CTA's moved channels (CH <= 32), gathered in one warp vote
+    __shared__ unsigned chg_mask;
+    if (warp == 0) {
+      const unsigned m = __ballot_sync(0xffffffffu, lane < CH && vchg[g * hd + c0 + lane] != 0);
+      if (lane == 0) chg_mask = m;
+    }
+    __syncthreads();
+    #pragma unroll 1
+    for (unsigned mask = chg_mask; mask; mask &= mask - 1) {
+      const int c = __ffs(mask) - 1;
+      const int gc = g * hd + c0 + c;
+      const double sc = (double)vs[gc], rsc = __drcp_rn(sc);
+      #pragma unroll 1
+      for (int j = tid; j < n0; j += 256) {
+        const int8_t q = dc_quant_div((double)vcache[(int64_t)j * kvDim + gc], sc, rsc);
+        sV[(size_t)c * ldpv + j] = q;
+        if (writer) v8t[(int64_t)gc * ldp + j] = q;
+      }
+    }
+    for (int c = tid; c < CH; c += 256) sV[(size_t)c * ldpv + n0] = v8t[((int64_t)g * hd + c0 + c) * ldp + n0];
+    __syncthreads();
+  }
   if (!abort_flag) {
     const int nch = ldpN >> 4;
     const int4* a4 = (const int4*)a8;
@@ -2058,7 +2131,11 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     if (int rc0 = dc_set_smem(ctx, (const void*)k_attn_ctx, (int)ctx_smem)) return rc0;
   const size_t nrm_smem = rms_smem(S->C);
   // always raised: the kernel's static shared memory counts against the 48 KB default too
-  if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
+  // rows that fit in one wave get the wide norm block
+  const bool nwide = T <= ctx->sm_count;
+  auto norm_k = nwide ? k_rmsnorm_quant<NORM_WIDE> : k_rmsnorm_quant<NORM_THREADS>;
+  const int norm_nt = nwide ? NORM_WIDE : NORM_THREADS;
+  if (int rc0 = dc_set_smem(ctx, (const void*)norm_k, (int)nrm_smem)) return rc0;
   // a decode row: GEMVs with the norms, the SwiGLU and the row quantisation fused
   const bool fuse = T == 1 && use_kv && dec_ch && S->row_fused && fg_fits(S);
   if (fuse) {
@@ -2074,7 +2151,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     if (fuse) {  // RMSNorm + QKV; zeroes the row maxima the attention and the SwiGLU collect
       DC_CUDA(ctx, launch_fused(S, FG_NORM, x, S->C, ly.nrm1, nullptr, ly.qkv, 0, S->hbuf, nullptr, S->rowmax));
     } else {
-      DC_CUDA(ctx, launch_dep(k_rmsnorm_quant, dim3(T), dim3(NORM_THREADS), nrm_smem, st, x, S->C, ly.nrm1,
+      DC_CUDA(ctx, launch_dep(norm_k, dim3(T), dim3(norm_nt), nrm_smem, st, x, S->C, ly.nrm1,
                               S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
       dc_count_launch();
       if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
@@ -2090,15 +2167,18 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                               S->kvDim, n0p));
       dc_count_launch();
     }
-    if (T <= 8) {
+    // the decode row's cluster attention re-quantises moved value channels itself
+    const bool dcl = T == 1 && use_kv && dec_ch && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8;
+    if (dcl) {
+    } else if (T <= 8) {
       DC_CUDA(ctx, launch_dep(k_vquant_dev, dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), dim3(256), 0, st,
                               kv.v, kv.vs, kv.vchg, kv.v8t, T, n0p, S->kvDim, S->hd, S->ldp, T == 1 ? 1 : 0));
     } else {
       DC_CUDA(ctx, launch_dep(k_vquant, dim3((N + 63) / 64, (S->kvDim + 31) / 32), dim3(256), 0, st, kv.v, kv.vs,
                               kv.vchg, kv.v8t, N, n0, S->kvDim, S->hd, S->ldp));
     }
-    dc_count_launch();
-    if (T == 1 && use_kv && dec_ch && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8) {
+    if (!dcl) dc_count_launch();
+    if (dcl) {
       // the channel-group CTAs of a head as one cluster: the key work is split among them
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(S->nH, S->hd / dec_ch);
@@ -2115,9 +2195,9 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       cfg.attrs = attr;
       cfg.numAttrs = 2;
       DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_attention_dcl, (const float*)S->hbuf, S->nqkv, S->nH, S->nKV, S->hd,
-                                      (const int8_t*)kv.k8, (const float*)kv.ks, (const int8_t*)kv.v8t,
-                                      (const float*)kv.vs, n0p, S->max_pos, S->ldp, dec_ch, scale, S->ctxo,
-                                      S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status));
+                                      (const int8_t*)kv.k8, (const float*)kv.ks, kv.v8t, (const float*)kv.vs, n0p,
+                                      S->max_pos, S->ldp, dec_ch, scale, S->ctxo, S->rowmax, S->att_done, S->xq,
+                                      S->ldQ, S->rs, ctx->d_status, (const float*)kv.v, (const int*)kv.vchg));
       dc_count_launch();
     } else if (T == 1 && use_kv && dec_ch) {
       DC_CUDA(ctx, launch_dep(k_attention_dec, dim3(S->nH, S->hd / dec_ch), dim3(256), dec_smem, st, S->hbuf, S->nqkv,
@@ -2154,7 +2234,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                                 nullptr));
       continue;
     }
-    DC_CUDA(ctx, launch_dep(k_rmsnorm_quant, dim3(T), dim3(NORM_THREADS), nrm_smem, st, x, S->C, ly.nrm2,
+    DC_CUDA(ctx, launch_dep(norm_k, dim3(T), dim3(norm_nt), nrm_smem, st, x, S->C, ly.nrm2,
                             S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
     dc_count_launch();
     if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
@@ -2295,8 +2375,8 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
   } else {
     const size_t nrm_smem = rms_smem(H->C);
     // always raised: the kernel's static shared memory counts against the 48 KB default too
-    if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
-    k_rmsnorm_quant<<<1, NORM_THREADS, nrm_smem, s>>>(H->xlap, H->C, H->nrmF, H->spec.norm_eps, H->xq, H->ldC, H->rs,
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant<NORM_WIDE>, (int)nrm_smem)) return rc0;
+    k_rmsnorm_quant<NORM_WIDE><<<1, NORM_WIDE, nrm_smem, s>>>(H->xlap, H->C, H->nrmF, H->spec.norm_eps, H->xq, H->ldC, H->rs,
                                                        ctx->d_status);
     dc_count_launch();
     rc = dc_gemm_dispatch(ctx, H->xq, H->ldC, H->lm.qt, H->lm.ldk, H->rs, H->lm.cs, 1, H->C, H->V, 1, 0, H->logits1, s,
@@ -2408,8 +2488,8 @@ extern "C" int dc_stage_logits(dc_stage* S, const float* x, int T, const int32_t
                                  cudaMemcpyDeviceToDevice, st));
   const size_t nrm_smem = rms_smem(S->C);
   // always raised: the kernel's static shared memory counts against the 48 KB default too
-  if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, (int)nrm_smem)) return rc0;
-  k_rmsnorm_quant<<<nrows, NORM_THREADS, nrm_smem, st>>>(S->lx, S->C, S->nrmF, S->spec.norm_eps, S->xq, S->ldC, S->rs,
+  if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant<NORM_WIDE>, (int)nrm_smem)) return rc0;
+  k_rmsnorm_quant<NORM_WIDE><<<nrows, NORM_WIDE, nrm_smem, st>>>(S->lx, S->C, S->nrmF, S->spec.norm_eps, S->xq, S->ldC, S->rs,
                                                           ctx->d_status); dc_count_launch();
   int rc = dc_gemm_dispatch(ctx, S->xq, S->ldC, S->lm.qt, S->lm.ldk, S->rs, S->lm.cs, nrows, S->C, S->V, 1, 0,
                             logits, st, 0);
@@ -2458,8 +2538,10 @@ extern "C" int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, c
   if ((size_t)cols * 12 > 200 * 1024) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: row of %d does not fit on chip", cols);
   if (!rows) return DC_OK;
   const int smem = (int)rms_smem(cols);
-  if (int rc = dc_set_smem(ctx, (const void*)k_rmsnorm_quant, smem)) return rc;
-  k_rmsnorm_quant<<<rows, NORM_THREADS, smem, ctx->stream>>>(x, cols, w, eps, nullptr, 0, nullptr, ctx->d_status, y,
+  const bool wide = rows <= ctx->sm_count;
+  auto norm_k = wide ? k_rmsnorm_quant<NORM_WIDE> : k_rmsnorm_quant<NORM_THREADS>;
+  if (int rc = dc_set_smem(ctx, (const void*)norm_k, smem)) return rc;
+  norm_k<<<rows, wide ? NORM_WIDE : NORM_THREADS, smem, ctx->stream>>>(x, cols, w, eps, nullptr, 0, nullptr, ctx->d_status, y,
                                                            nullptr, exact_sum);
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
