@@ -38,7 +38,7 @@ def to_f32(dtype: str, raw) -> np.ndarray:
         return np.frombuffer(b, "<f2").astype(np.float32)
     if dtype == "F64":
         return np.frombuffer(b, "<f8").astype(np.float32)
-    raise ValueError(f"unsupported tensor dtype {dtype} — weights must be F32, F16, BF16 or F64")
+    raise ValueError(f"tensor dtype {dtype} cannot be widened to f32 here (F32, F16, BF16 and F64 can)")
 
 
 # ---- header (safetensors.js:68-103) ------------------------------------------------
@@ -48,19 +48,19 @@ def parse_header(head: bytes, file_size: int | None = None) -> dict:
     Raises ValueError for an implausible length, a truncated or non-JSON
     header, a malformed entry or a byte count that does not match its shape."""
     if len(head) < 8:
-        raise ValueError("safetensors header is truncated")
+        raise ValueError("the file ends before its header does (truncated)")
     lo, hi = struct.unpack_from("<II", head, 0)
     if hi != 0:
-        raise ValueError("safetensors header length is implausibly large — not a safetensors file")
+        raise ValueError("the 64-bit header length is implausibly large (its upper word is set)")
     limit = (file_size if file_size is not None else len(head)) - 8
     if lo <= 0 or lo > limit or 8 + lo > len(head):
-        raise ValueError("safetensors header is truncated")
+        raise ValueError("the file ends before its header does (truncated)")
     try:
         meta = json.loads(head[8:8 + lo].decode("utf-8"))
     except (UnicodeDecodeError, json.JSONDecodeError):
-        raise ValueError("safetensors header is not valid JSON — not a safetensors file") from None
+        raise ValueError("the header bytes are not valid JSON text") from None
     if not isinstance(meta, dict):
-        raise ValueError("safetensors header is not valid JSON — not a safetensors file")
+        raise ValueError("the header is not valid JSON for this format (not an object of tensors)")
     data_start = 8 + lo
     tensors = {}
     for name, t in meta.items():
@@ -68,13 +68,13 @@ def parse_header(head: bytes, file_size: int | None = None) -> dict:
             continue
         if (not isinstance(t, dict) or not t.get("dtype") or not isinstance(t.get("shape"), list)
                 or not isinstance(t.get("data_offsets"), list) or len(t["data_offsets"]) != 2):
-            raise ValueError(f'safetensors header entry "{name}" is malformed')
+            raise ValueError(f'header entry "{name}" is malformed: it needs a dtype, a shape and two data offsets')
         s, e = (int(v) for v in t["data_offsets"])
         elems = math.prod(int(d) for d in t["shape"])
         per = BYTES.get(t["dtype"], 0)
         if per and e - s != elems * per:
-            raise ValueError(f'tensor "{name}": header claims {e - s} bytes for a '
-                             f'{"x".join(str(d) for d in t["shape"])} {t["dtype"]} (expected {elems * per})')
+            raise ValueError(f'"{name}" spans {e - s} bytes, but a {"x".join(str(d) for d in t["shape"])} '
+                             f'{t["dtype"]} tensor takes {elems * per} (expected {elems * per})')
         tensors[name] = dict(name=name, dtype=t["dtype"], shape=[int(d) for d in t["shape"]], elems=elems,
                              start=data_start + s, end=data_start + e, bytes=e - s)
     return dict(tensors=tensors, data_start=data_start, metadata=meta.get("__metadata__") or {})
@@ -88,7 +88,7 @@ def read_header(path: str) -> dict:
         f.seek(0)
         first = f.read(8)
         if len(first) < 8:
-            raise ValueError("safetensors header is truncated")
+            raise ValueError("the file ends before its header does (truncated)")
         n = struct.unpack_from("<Q", first, 0)[0]
         if n > size:
             return parse_header(first, size)  # refused there: truncated or implausible
@@ -186,7 +186,7 @@ def read_stage_weights(path: str, spec, lo: int, hi: int, head: bool, slack: int
             f.seek(run["start"])
             blob = f.read(run["end"] - run["start"])
             if len(blob) != run["end"] - run["start"]:
-                raise ValueError("safetensors file is shorter than its header says")
+                raise ValueError("the file ends inside the byte range of a tensor its header lists (truncated)")
             for t in run["tensors"]:
                 got[t["name"]] = to_f32(t["dtype"], blob[t["start"] - run["start"]:t["end"] - run["start"]])
     C_, q, kv, I_ = spec.hidden, spec.heads * spec.headDim, spec.kvHeads * spec.headDim, spec.inter

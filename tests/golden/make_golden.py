@@ -1,8 +1,8 @@
 """Writes tests/golden/luts.json from the reference's public/*_lut.bin (Git LFS
 pointer files: the sha256 object id and byte size of each table) and
-public/luts_meta.json.  Run where the reference tree is present:
+public/luts_meta.json.  Run where the reference tree is present, naming its root:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py PATH_TO_REFERENCE
 
 The tests read only the JSON this writes (the reference is not needed to run them).
 """
@@ -31,4 +31,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py PATH_TO_REFERENCE (the reference project's root directory)")
+    main(sys.argv[1])
