@@ -217,7 +217,13 @@ int run_gates(dc_ctx* c) {
       int rc = gate_one(c, g, 2, poison, seed++, why);
       if (rc) return rc == DC_E_GATE ? dc_fail(c, DC_E_GATE, "init gate: %s", why.c_str()) : rc;
       if (c->tc_enabled) {
-        rc = gate_one(c, g, 3, poison, seed++, why);
+        rc = gate_one(c, g, 3, poison, seed, why);
+        if ((rc == DC_E_GATE || rc == DC_E_INVAL) && g.m > 128 && c->tc2_enabled) {
+          c->tc2_enabled = false;  // the 2-SM variant off; the one-SM kernel takes M > 128
+          fprintf(stderr, "dcinfer: tcgen05 2-SM GEMM gate failed, variant disabled: %s\n", why.c_str());
+          rc = gate_one(c, g, 3, poison, seed, why);
+        }
+        seed++;
         if (rc == DC_E_GATE || rc == DC_E_INVAL) {
           c->tc_enabled = false;  // tensor-core path off; SIMT kernel takes its shapes
           fprintf(stderr, "dcinfer: tcgen05 GEMM gate failed, path disabled: %s\n", why.c_str());
@@ -297,7 +303,8 @@ extern "C" int dc_init(int device, dc_ctx** out) {
   }
   if (!rc) {
     c->sm_count = prop.multiProcessorCount;
-    snprintf(c->label, sizeof c->label, "%s (sm_100a): tcgen05 i8 GEMM + dp4a GEMV, verified", prop.name);
+    snprintf(c->label, sizeof c->label, "%s (sm_100a): tcgen05 i8 GEMM (1- and 2-SM tiles) + dp4a GEMV, verified",
+             prop.name);
     build_luts(c);
     rc = check_luts(c);
   }
@@ -305,6 +312,7 @@ extern "C" int dc_init(int device, dc_ctx** out) {
     e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_hop, cudaEventDisableTiming);
     c->stream = c->own_stream;
     if (e == cudaSuccess) e = cudaMalloc(&c->d_mul, sizeof c->h_mul);
     if (e == cudaSuccess) e = cudaMalloc(&c->d_requant, sizeof c->h_requant);
@@ -319,6 +327,9 @@ extern "C" int dc_init(int device, dc_ctx** out) {
   if (!rc) rc = run_gates(c);
   if (!rc && !c->tc_enabled)
     snprintf(c->label, sizeof c->label, "%s (sm_100a): dp4a GEMM + GEMV, verified (tcgen05 gate failed)", prop.name);
+  else if (!rc && !c->tc2_enabled)
+    snprintf(c->label, sizeof c->label, "%s (sm_100a): tcgen05 i8 GEMM (one SM per tile; 2-SM gate failed) + dp4a GEMV, "
+             "verified", prop.name);
   if (rc) {
     g_init_error = c->err;
     fprintf(stderr, "dc_init failed: %s\n", c->err.c_str());
@@ -347,6 +358,7 @@ extern "C" void dc_destroy(dc_ctx* c) {
   for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
   if (c->ev_fork) cudaEventDestroy(c->ev_fork);
   if (c->ev_join) cudaEventDestroy(c->ev_join);
+  if (c->ev_hop) cudaEventDestroy(c->ev_hop);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
 }

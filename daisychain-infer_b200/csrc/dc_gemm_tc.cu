@@ -172,6 +172,99 @@ struct TcArgs {
   int* status;
 };
 
+// The epilogue of one CTA's 128 output columns j0.. x BN activation rows i0..:
+// every warp reads TMEM lanes 32(w%4).. (its 32 columns) and COLS activation
+// rows, applies the verified epilogue (or, split over K, adds its int32
+// partial sums into the scratch and the last split to arrive finishes the
+// tile, `tile` indexing its counter).  rs_s holds the BN row scales.
+template <int BN, int COLS>
+__device__ __forceinline__ void tc_epilogue(const TcArgs& a, uint32_t tmem, bool good, int bz, int j0, int i0,
+                                            int tile, const float* rs_s) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quarter = warp & 3;                          // TMEM lanes 32*quarter .. +31
+  const int cb0 = (warp >> 2) * COLS;        // this warp's activation rows
+  const int cb1 = cb0 + COLS;
+  const int j = j0 + quarter * 32 + lane;
+  const bool jv = j < a.n;
+  const float csv = jv ? __ldg(a.cs + bz * a.n + j) : 0.0f;
+  // 16 accumulators of one column j: residual values loaded first, then stored
+  auto store16 = [&](int cbase, const int32_t (&v)[16]) {
+    float old[16];
+    if (a.flags & DC_F_ADDTO) {
+#pragma unroll
+      for (int c = 0; c < 16; c++) {
+        const int i = i0 + cbase + c;
+        old[c] = (jv && i < a.m) ? ((const float*)a.out)[((int64_t)bz * a.m + i) * a.n + j] : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 16; c++) {
+      const int i = i0 + cbase + c;
+      if (!(jv && i < a.m)) continue;
+      const int64_t idx = ((int64_t)bz * a.m + i) * a.n + j;
+      if (a.flags & (DC_ACC | DC_REQUANT)) {
+        dc_store_out(a.out, idx, v[c], rs_s[cbase + c], csv, a.flags, a.requant, a.relu);
+      } else {
+        float o = dc_epi(v[c], rs_s[cbase + c], csv);
+        if ((a.flags & DC_RELU) && o < 0.0f) o = 0.0f;
+        if (a.flags & DC_F_ADDTO) o = __fadd_rn(old[c], o);
+        ((float*)a.out)[idx] = o;
+      }
+    }
+  };
+  if (a.splits == 1) {
+    if (good) {
+#pragma unroll 1
+      for (int c0 = cb0; c0 < cb1; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, r);
+        int32_t v[16];
+#pragma unroll
+        for (int c = 0; c < 16; c++) v[c] = (int32_t)r[c];
+        store16(c0, v);
+      }
+    }
+  } else {
+    if (good) {
+#pragma unroll 1
+      for (int c0 = cb0; c0 < cb1; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, r);
+#pragma unroll
+        for (int c = 0; c < 16; c++) {
+          const int i = i0 + c0 + c;
+          if (jv && i < a.m) atomicAdd(a.partial + ((int64_t)bz * a.m + i) * a.n + j, (int32_t)r[c]);
+        }
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) last = (atomicAdd(a.counters + tile, 1) == a.splits - 1);
+    __syncthreads();
+    if (last) {
+      __threadfence();
+#pragma unroll 1
+      for (int c0 = cb0; c0 < cb1; c0 += 16) {
+        int32_t v[16];
+#pragma unroll
+        for (int c = 0; c < 16; c++) {  // all 16 partial sums in flight together
+          const int i = i0 + c0 + c;
+          v[c] = (jv && i < a.m) ? __ldcg(a.partial + ((int64_t)bz * a.m + i) * a.n + j) : 0;
+        }
+        store16(c0, v);
+#pragma unroll
+        for (int c = 0; c < 16; c++) {
+          const int i = i0 + c0 + c;
+          if (jv && i < a.m) a.partial[((int64_t)bz * a.m + i) * a.n + j] = 0;
+        }
+      }
+      if (threadIdx.x == 0) a.counters[tile] = 0;
+    }
+  }
+
+}
+
 template <int BN>
 __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
@@ -281,88 +374,7 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();
   const bool good = have && (*(volatile int*)flag == 0) && nkb > 0;
-  const int quarter = warp & 3;                          // TMEM lanes 32*quarter .. +31
-  const int cb0 = (warp >> 2) * C::COLS_PER_WARP;        // this warp's activation rows
-  const int cb1 = cb0 + C::COLS_PER_WARP;
-  const int j = j0 + quarter * 32 + lane;
-  const bool jv = j < a.n;
-  const float csv = jv ? __ldg(a.cs + bz * a.n + j) : 0.0f;
-  // 16 accumulators of one column j: residual values loaded first, then stored
-  auto store16 = [&](int cbase, const int32_t (&v)[16]) {
-    float old[16];
-    if (a.flags & DC_F_ADDTO) {
-#pragma unroll
-      for (int c = 0; c < 16; c++) {
-        const int i = i0 + cbase + c;
-        old[c] = (jv && i < a.m) ? ((const float*)a.out)[((int64_t)bz * a.m + i) * a.n + j] : 0.0f;
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < 16; c++) {
-      const int i = i0 + cbase + c;
-      if (!(jv && i < a.m)) continue;
-      const int64_t idx = ((int64_t)bz * a.m + i) * a.n + j;
-      if (a.flags & (DC_ACC | DC_REQUANT)) {
-        dc_store_out(a.out, idx, v[c], rs_s[cbase + c], csv, a.flags, a.requant, a.relu);
-      } else {
-        float o = dc_epi(v[c], rs_s[cbase + c], csv);
-        if ((a.flags & DC_RELU) && o < 0.0f) o = 0.0f;
-        if (a.flags & DC_F_ADDTO) o = __fadd_rn(old[c], o);
-        ((float*)a.out)[idx] = o;
-      }
-    }
-  };
-  if (a.splits == 1) {
-    if (good) {
-#pragma unroll 1
-      for (int c0 = cb0; c0 < cb1; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, r);
-        int32_t v[16];
-#pragma unroll
-        for (int c = 0; c < 16; c++) v[c] = (int32_t)r[c];
-        store16(c0, v);
-      }
-    }
-  } else {
-    if (good) {
-#pragma unroll 1
-      for (int c0 = cb0; c0 < cb1; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, r);
-#pragma unroll
-        for (int c = 0; c < 16; c++) {
-          const int i = i0 + c0 + c;
-          if (jv && i < a.m) atomicAdd(a.partial + ((int64_t)bz * a.m + i) * a.n + j, (int32_t)r[c]);
-        }
-      }
-    }
-    __threadfence();
-    __syncthreads();
-    __shared__ int last;
-    const int tile = (bz * a.m_tiles + tile_m) * a.n_tiles + tile_n;
-    if (threadIdx.x == 0) last = (atomicAdd(a.counters + tile, 1) == a.splits - 1);
-    __syncthreads();
-    if (last) {
-      __threadfence();
-#pragma unroll 1
-      for (int c0 = cb0; c0 < cb1; c0 += 16) {
-        int32_t v[16];
-#pragma unroll
-        for (int c = 0; c < 16; c++) {  // all 16 partial sums in flight together
-          const int i = i0 + c0 + c;
-          v[c] = (jv && i < a.m) ? __ldcg(a.partial + ((int64_t)bz * a.m + i) * a.n + j) : 0;
-        }
-        store16(c0, v);
-#pragma unroll
-        for (int c = 0; c < 16; c++) {
-          const int i = i0 + c0 + c;
-          if (jv && i < a.m) a.partial[((int64_t)bz * a.m + i) * a.n + j] = 0;
-        }
-      }
-      if (threadIdx.x == 0) a.counters[tile] = 0;
-    }
-  }
+  tc_epilogue<BN, C::COLS_PER_WARP>(a, tmem, good, bz, j0, i0, (bz * a.m_tiles + tile_m) * a.n_tiles + tile_n, rs_s);
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -370,6 +382,192 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS)
                  : "memory");
+  }
+}
+
+// ---- the 2-SM variant for M > 128 -------------------------------------------
+// A CTA pair (a cluster of two along x) computes one 256 x 256 tile: 256
+// weight rows (this CTA's 128 at j0) against 256 activation rows (i0..), with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256) issued by the pair's even CTA.
+// Each CTA brings its own 128 weight rows and 128 of the 256 activation rows
+// of every K block into its shared memory (TMA with .cta_group::2, no
+// multicast; the copies of both CTAs complete on the even CTA's `full`
+// barrier); the MMA reads the two halves from the two CTAs, and its commits
+// are multicast to both CTAs' `empty` and `accum` barriers.  A stage is then
+// 32 KB per CTA instead of 48, so six stages fit where one CTA held four:
+// about 2.5 us of MMA work in flight against the TMA round trip.  Each CTA's
+// TMEM holds its 128 weight rows x 256 activation rows; the epilogue is
+// tc_epilogue's.  Every wait is bounded; every path of both CTAs reaches the
+// closing cluster barrier before the pair frees its TMEM.
+constexpr int TC2_STAGES = 6;
+constexpr int TC2_HALF = 128 * TILE_K;  // 16 KB: 128 rows of one operand
+constexpr int TC2_STAGE = 2 * TC2_HALF;
+constexpr int TC2_SMEM = TC2_STAGES * TC2_STAGE + 1024 + 256;
+constexpr int TC2_THREADS = 512;
+constexpr int TC2_COLS = 256 / (TC2_THREADS / 128);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(const void* p, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 2-D tile load into this CTA's shared memory, completing on the barrier at
+// cluster address `bar` (the even CTA's), as one half of a pair's operand.
+__device__ __forceinline__ void tma_load_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrive on `bar` in both CTAs of the pair once the MMAs issued so far are done.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(TC2_THREADS, 1)
+    k_gemm_tc2(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;                            // STAGES x 16 KB: this CTA's 128 weight rows
+  uint8_t* sB = smem + TC2_STAGES * TC2_HALF;    // STAGES x 16 KB: this CTA's 128 activation rows
+  uint64_t* full = (uint64_t*)(smem + TC2_STAGES * TC2_STAGE);
+  uint64_t* empty = full + TC2_STAGES;
+  uint64_t* accum = empty + TC2_STAGES;
+  uint32_t* tmem_slot = (uint32_t*)(accum + 1);
+  int* flag = (int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int tile_n = blockIdx.x >> 1, tile_m = blockIdx.y;
+  const int bz = blockIdx.z / a.splits, split = blockIdx.z - bz * a.splits;
+  const int j0 = tile_n * 256 + 128 * (int)rank;  // this CTA's weight rows = output columns
+  const int i0 = tile_m * 256;                    // the pair's activation rows
+  const int kb0 = split * a.kb_per_split;
+  const int kb1 = min(a.kb_total, kb0 + a.kb_per_split);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC2_STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    *flag = 0;
+  }
+  if (warp == 1) {  // the same warp in both CTAs allocates the pair's TMEM
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(256u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync_all();  // both CTAs' barriers exist before any copy or commit reaches them
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer, both CTAs.  Weights (constant) first, before the
+    // grid-dependency wait; activations after it.
+    const uint32_t full_l = map_rank(&full[0], 0);  // the even CTA's barriers
+    bool ok = true;
+    const int pre = min(nkb, TC2_STAGES);
+    for (int it = 0; it < pre; it++) {
+      if (leader) mbar_expect_tx(&full[it], 2 * TC2_STAGE);  // both CTAs' halves of both operands
+      tma_load_pair(sA + it * TC2_HALF, &tmW, (kb0 + it) * TILE_K, bz * a.n + j0, full_l + 8 * it);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int it = 0; it < pre; it++)
+      tma_load_pair(sB + it * TC2_HALF, &tmX, (kb0 + it) * TILE_K, bz * a.m + i0 + 128 * (int)rank, full_l + 8 * it);
+    for (int it = pre; it < nkb && ok; it++) {
+      const int s = it % TC2_STAGES;
+      const uint32_t ph = (uint32_t)(it / TC2_STAGES) & 1u;
+      ok = mbar_wait(&empty[s], ph ^ 1u, a.status);
+      if (!ok) break;
+      if (leader) mbar_expect_tx(&full[s], 2 * TC2_STAGE);
+      const int kx = (kb0 + it) * TILE_K;
+      tma_load_pair(sA + s * TC2_HALF, &tmW, kx, bz * a.n + j0, full_l + 8 * s);
+      tma_load_pair(sB + s * TC2_HALF, &tmX, kx, bz * a.m + i0 + 128 * (int)rank, full_l + 8 * s);
+    }
+    if (!ok) atomicExch(flag, 1);
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---- MMA issuer (the even CTA only)
+    const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                           ((uint32_t)(256 >> 4) << 24);  // s8 x s8 -> s32, K-major, M = 256, N = 256
+    int done = 0;
+    for (int it = 0; it < nkb; it++) {
+      const int s = it % TC2_STAGES;
+      const uint32_t ph = (uint32_t)(it / TC2_STAGES) & 1u;
+      if (!mbar_wait(&full[s], ph, a.status)) {
+        atomicExch(flag, 1);
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint8_t* ta = sA + s * TC2_HALF;
+      const uint8_t* tb = sB + s * TC2_HALF;
+#pragma unroll
+      for (int kk = 0; kk < TILE_K / MMA_K; kk++)
+        mma_i8_pair(tmem, umma_desc(ta + kk * MMA_K), umma_desc(tb + kk * MMA_K), idesc,
+                    (it > 0 || kk > 0) ? 1u : 0u);
+      mma_commit_pair(&empty[s]);
+      done = it + 1;
+    }
+    mma_commit_pair(accum);
+    // after an abort: every stage issued but not consumed lands before the pair goes away
+    for (int it = done; it < min(nkb, done + TC2_STAGES); it++)
+      mbar_wait(&full[it % TC2_STAGES], (uint32_t)(it / TC2_STAGES) & 1u, a.status);
+  }
+  __syncwarp();
+
+  // ---- epilogue (both CTAs, all warps)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float rs_s[256];
+  for (int c = threadIdx.x; c < 256; c += blockDim.x) rs_s[c] = (i0 + c < a.m) ? __ldg(a.rs + bz * a.m + i0 + c) : 0.0f;
+  const bool have = mbar_wait(accum, 0, a.status);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  __syncthreads();
+  // either CTA's failure spoils the pair's tile: read the other CTA's flag too
+  cluster_sync_all();
+  int bad = *(volatile int*)flag;
+  {
+    uint32_t other;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(other) : "r"(map_rank(flag, rank ^ 1u)));
+    bad |= (int)other;
+  }
+  const bool good = have && bad == 0 && nkb > 0;
+  tc_epilogue<256, TC2_COLS>(a, tmem, good, bz, j0, i0, (bz * a.m_tiles + tile_m) * a.n_tiles + 2 * tile_n + rank,
+                             rs_s);
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees the pair's TMEM or leaves while the other still uses it
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u) : "memory");
   }
 }
 
@@ -495,6 +693,68 @@ int launch_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw,
   return DC_OK;
 }
 
+// k_gemm_tc2 over pairs of SMs: grid (2 * ceil(n/256), ceil(m/256), batch * splits), clusters of two.
+int launch_tc2(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+               int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st, int32_t* partial,
+               int* counters, size_t partial_cap, size_t counter_cap, int clear) {
+  CUtensorMap mW, mX;
+  if (!make_map(&mW, Wt, ldw, (long)batch * n, TILE_N) || !make_map(&mX, Xq, ldx, (long)batch * m, 128))
+    return dc_fail(ctx, DC_E_INVAL, "tcgen05: tensor map encode failed");
+  TcArgs a;
+  a.rs = rs;
+  a.cs = cs;
+  a.m = m;
+  a.k = k;
+  a.n = n;
+  a.kb_total = (k + TILE_K - 1) / TILE_K;
+  const int pairs_n = (n + 255) / 256;
+  a.n_tiles = 2 * pairs_n;  // 128-column slots (the split-K counters' index)
+  a.m_tiles = (m + 255) / 256;
+  const int ctas = 2 * pairs_n * a.m_tiles * batch;
+  int splits = 1;
+  if (ctas < ctx->sm_count && a.kb_total > 1) {
+    splits = std::max(1, ctx->sm_count / ctas);
+    splits = std::min(splits, std::max(1, a.kb_total / 4));
+  }
+  a.kb_per_split = (a.kb_total + splits - 1) / splits;
+  splits = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
+  const size_t tiles = (size_t)a.n_tiles * a.m_tiles * batch;
+  if (splits > 1 && (!partial || (size_t)batch * m * n > partial_cap || tiles > counter_cap)) {
+    splits = 1;
+    a.kb_per_split = a.kb_total;
+  }
+  a.splits = splits;
+  if (splits > 1 && clear) {
+    DC_CUDA(ctx, cudaMemsetAsync(partial, 0, 4 * (size_t)batch * m * n, st));
+    DC_CUDA(ctx, cudaMemsetAsync(counters, 0, 4 * tiles, st));
+  }
+  a.flags = flags;
+  a.requant = ctx->d_requant;
+  a.relu = ctx->d_relu;
+  a.out = out;
+  a.partial = partial;
+  a.counters = counters;
+  a.status = ctx->d_status;
+  if (int rc = dc_set_smem(ctx, (const void*)k_gemm_tc2, TC2_SMEM)) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs_n, a.m_tiles, batch * splits);
+  cfg.blockDim = dim3(TC2_THREADS);
+  cfg.dynamicSmemBytes = TC2_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemm_tc2, mW, mX, a));
+  dc_count_launch();
+  return DC_OK;
+}
+
 }  // namespace
 
 // Split-K scratch of a context: int32 partial sums and tile counters, both kept
@@ -540,6 +800,9 @@ int dc_gemm_tc_with(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, in
   if (m <= 128)
     return launch_tc<128>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
                           partial_cap, counter_cap, clear);
+  if (ctx->tc2_enabled)
+    return launch_tc2(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters, partial_cap,
+                      counter_cap, clear);
   return launch_tc<256>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
                         partial_cap, counter_cap, clear);
 }

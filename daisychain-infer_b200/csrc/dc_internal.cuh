@@ -32,6 +32,7 @@ struct dc_ctx {
   cudaStream_t stream = nullptr;      // where work is launched
   cudaStream_t own_stream = nullptr;  // created by dc_init
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;  // ordering between `stream` and `own_stream`
+  cudaEvent_t ev_hop = nullptr;  // dc_stage_handoff: the source stage's work is done
   std::string err;
   char label[160] = {0};
   // LUT units: host copies (checked by sha256) and device copies.
@@ -46,6 +47,7 @@ struct dc_ctx {
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   bool tc_enabled = true;  // tcgen05 GEMM passed its gate
+  bool tc2_enabled = true;  // its 2-SM variant (M > 128) passed its gate
   // split-K scratch of the tcgen05 GEMM (kept zero between calls by the kernel)
   int32_t* tc_partial = nullptr;
   int* tc_counters = nullptr;

@@ -2013,6 +2013,31 @@ extern "C" int dc_stage_kv_reset(dc_stage* S) {
 
 extern "C" int dc_stage_kv_len(const dc_stage* S) { return S ? S->kv_len : -1; }
 
+// The activation hop from one stage to the next (app.js:705-765, wire.js
+// :106-138): T rows of hidden floats from x_src (on the source stage's
+// device) to x_dst (on the destination's), after the source stage's work and
+// before any later work of the destination: the copy runs on the source
+// context's stream, and the destination's stream waits for it through an
+// event.  Stages on different devices copy peer to peer; on one device it is
+// a device copy.
+extern "C" int dc_stage_handoff(dc_stage* src, dc_stage* dst, const float* x_src, float* x_dst, int T) {
+  if (!src || !dst) return DC_E_INVAL;
+  if (!x_src || !x_dst || T < 1 || T > dst->max_rows || src->C != dst->C)
+    return dc_fail(src->ctx, DC_E_INVAL, "stage_handoff: bad arguments");
+  dc_ctx* a = src->ctx;
+  dc_ctx* b = dst->ctx;
+  const size_t bytes = 4 * (size_t)T * src->C;
+  if (a->device == b->device)
+    DC_CUDA(a, cudaMemcpyAsync(x_dst, x_src, bytes, cudaMemcpyDeviceToDevice, a->stream));
+  else
+    DC_CUDA(a, cudaMemcpyPeerAsync(x_dst, b->device, x_src, a->device, bytes, a->stream));
+  if (a != b) {
+    DC_CUDA(a, cudaEventRecord(a->ev_hop, a->stream));
+    DC_CUDA(b, cudaStreamWaitEvent(b->stream, a->ev_hop, 0));
+  }
+  return DC_OK;
+}
+
 extern "C" int dc_stage_embed(dc_stage* S, const int32_t* ids, int T, float* x) {
   if (!S || !S->head || T < 1 || T > S->max_rows || !ids || !x)
     return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_embed: bad arguments");

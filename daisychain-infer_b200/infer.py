@@ -224,6 +224,13 @@ class Stage:
         """One-row cached forwards (decode steps) as a CUDA graph (default) or kernel by kernel."""
         self._check(self.L.dc_stage_set_row_graph(self.h, 1 if on else 0), "set_row_graph")
 
+    def handoff(self, dst: "Stage", x, out) -> "torch.Tensor":
+        """Hand this stage's output rows x to stage dst's buffer out (its device):
+        the stage-to-stage hop, ordered after this stage's work and before dst's."""
+        T = x.numel() // self.spec.hidden
+        self._check(self.L.dc_stage_handoff(self.h, dst.h, _ptr(x), _ptr(out), T), "stage_handoff")
+        return out
+
     def set_row_fusion(self, on: bool) -> None:
         """Decode rows with the norm / SwiGLU / row quantisation fused into their
         GEMVs (default) or as separate kernels; the results are identical."""

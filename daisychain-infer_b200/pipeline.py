@@ -60,6 +60,34 @@ class TorchP2P:
         return self.dist.irecv(t, src)
 
 
+class HopBuffers:
+    """A ring of hop buffers (up to ``cap`` floats each), so a lap allocates
+    nothing per hop: a buffer is handed out again only after the transfer last
+    posted on it has completed (``hold`` records that transfer)."""
+
+    def __init__(self, new_buffer, n: int, cap: int):
+        self.bufs = [new_buffer(cap) for _ in range(n)]
+        self.pending = [None] * n
+        self.i = 0
+
+    def take(self, floats: int):
+        i = self.i
+        self.i = (i + 1) % len(self.bufs)
+        if self.pending[i] is not None:
+            self.pending[i].wait()
+            self.pending[i] = None
+        return i, self.bufs[i][:floats]
+
+    def hold(self, i: int, work) -> None:
+        self.pending[i] = work
+
+    def drain(self) -> None:
+        for i, p in enumerate(self.pending):
+            if p is not None:
+                p.wait()
+                self.pending[i] = None
+
+
 class Ring:
     """One rank's part of the lap.  ``stage`` holds this rank's layers; rank 0
     is the head.  Every rank runs the same schedule (same chunk list, same
@@ -72,6 +100,14 @@ class Ring:
         self.prv = (rank - 1) % world
         self.new_buffer = new_buffer  # new_buffer(n_floats) -> tensor on this rank's device
         self.use_graph = True
+        self._rings = {}
+
+    def _ring(self, key: str, n: int, cap: int) -> HopBuffers:
+        """The hop buffers of one kind of transfer, made once per size."""
+        r = self._rings.get(key)
+        if r is None or r.bufs[0].numel() < cap or len(r.bufs) < n:
+            r = self._rings[key] = HopBuffers(self.new_buffer, n, cap)
+        return r
 
     # ---- chunked prefill + decode --------------------------------------------------
     def generate_chunked(self, ids0: list, n_new: int, chunk_size: int = 16, window: int = 2, on_prefill=None):
@@ -88,12 +124,14 @@ class Ring:
             if on_prefill:
                 on_prefill()
             return self._decode_local(last, len(ids0), n_new)
+        cap = chunks["chunkSize"] * H
         if self.rank == 0:
             flights = []
+            backs = self._ring("prefill-return", chunks["window"] + 1, cap)
             for ch in chunks["chunks"]:
                 x = S.run_layers_chunk(S.embed_rows(ids0[ch["lo"]:ch["hi"]]), ch["lo"])
                 sent = self.tp.send(x, self.nxt, token_idx=ch["lo"])  # the handle keeps the send (and x) alive
-                back = self.new_buffer((ch["hi"] - ch["lo"]) * H)
+                _, back = backs.take((ch["hi"] - ch["lo"]) * H)
                 flights.append((sent, self.tp.recv(back, self.prv, token_idx=ch["lo"]), back))
                 if len(flights) >= chunks["window"]:
                     sent_, req, buf = flights.pop(0)
@@ -109,21 +147,22 @@ class Ring:
                 on_prefill()
             return self._decode_head(last, len(ids0), n_new)
         # a middle or last stage: chunks arrive in order (the inbox of app.js:719-749)
-        pending = []
+        hops = self._ring("prefill-hop", chunks["window"] + 1, cap)
         for ch in chunks["chunks"]:
-            buf = self.new_buffer((ch["hi"] - ch["lo"]) * H)
+            i, buf = hops.take((ch["hi"] - ch["lo"]) * H)
             self.tp.recv(buf, self.prv, token_idx=ch["lo"]).wait()
             S.run_layers_chunk(buf, ch["lo"])
-            pending.append(self.tp.send(buf, self.nxt, token_idx=ch["lo"]))
+            hops.hold(i, self.tp.send(buf, self.nxt, token_idx=ch["lo"]))
         if on_prefill:
             on_prefill()
+        rows = self._ring("decode-hop", 2, H)
         for n in range(n_new):
-            buf = self.new_buffer(H)
+            i, buf = rows.take(H)
             self.tp.recv(buf, self.prv, token_idx=len(ids0) + n).wait()
             S.run_layers_chunk(buf, len(ids0) + n)
-            pending.append(self.tp.send(buf, self.nxt, token_idx=len(ids0) + n))
-        for p in pending:
-            p.wait()
+            rows.hold(i, self.tp.send(buf, self.nxt, token_idx=len(ids0) + n))
+        hops.drain()
+        rows.drain()
         return None
 
     def _decode_local(self, last, n_prompt: int, n_new: int):
@@ -140,12 +179,13 @@ class Ring:
     def _decode_head(self, last, n_prompt: int, n_new: int):
         S = self.stage
         picks = S.new_ids(n_new)
+        backs = self._ring("decode-return", 2, self.hidden)
         for n in range(n_new):
             rows = last.numel() // self.hidden
             S.pick_into(last, rows - 1, picks, n)
             x = S.run_layers_chunk(S.embed_device(picks, n), n_prompt + n)
             sent = self.tp.send(x, self.nxt, token_idx=n_prompt + n)
-            back = self.new_buffer(self.hidden)
+            _, back = backs.take(self.hidden)
             self.tp.recv(back, self.prv, token_idx=n_prompt + n).wait()
             sent.wait()
             last = back
@@ -160,14 +200,15 @@ class Ring:
             if self.world == 1:
                 return x
             sent = self.tp.send(x, self.nxt)
-            back = self.new_buffer(T * H)
+            _, back = self._ring("window-return", 2, T * H).take(T * H)
             self.tp.recv(back, self.prv).wait()
             sent.wait()
             return back
-        buf = self.new_buffer(T * H)
+        hops = self._ring("window-hop", 2, T * H)
+        i, buf = hops.take(T * H)
         self.tp.recv(buf, self.prv).wait()
         S.run_layers(buf)
-        self.tp.send(buf, self.nxt).wait()
+        hops.hold(i, self.tp.send(buf, self.nxt))
         return None
 
     def generate_lookahead(self, ids0: list, n_new: int, T: int, max_draft: int = 4):

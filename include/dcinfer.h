@@ -244,6 +244,12 @@ int dc_stage_logits(dc_stage* stage, const float* x, int T, const int32_t* rows,
  * never leave the device between laps.  use_graph = 1 captures one lap as a
  * CUDA graph (kernel positions live in device memory) and replays it. */
 int dc_decode_run(dc_stage** stages, int ns, const float* x_last, int n_new, int32_t* picks, int use_graph);
+/* The activation hop between pipeline stages (app.js:705-765, the act message
+ * of wire.js:106-138): T rows of hidden floats from x_src (device memory of
+ * src's GPU) to x_dst (device memory of dst's GPU), ordered after the work
+ * already issued for src and before any later work issued for dst (a peer
+ * copy over NVLink between devices, a device copy on one).  Asynchronous. */
+int dc_stage_handoff(dc_stage* src, dc_stage* dst, const float* x_src, float* x_dst, int T);
 /* The chunk path's cache: reset, and the number of cached tokens. */
 int dc_stage_kv_reset(dc_stage* stage);
 int dc_stage_kv_len(const dc_stage* stage);

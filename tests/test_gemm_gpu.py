@@ -59,6 +59,13 @@ def test_bgemm_empty_and_refusals(comp, P):
     assert (out == 0).all() and out.size == 6
 
 
+def test_tensor_core_paths_passed_their_gates(comp):
+    """dc_init gates the one-SM tcgen05 kernel and its 2-SM variant (M > 128)
+    against the LUT kernel; both must be in use on a B200."""
+    assert comp.tc_enabled
+    assert "gate failed" not in comp.label, comp.label
+
+
 def test_kernel_probe_matches_oracle(comp, O):
     assert comp.kernel_probe() == O.probe_hash_int32()
 

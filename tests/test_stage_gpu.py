@@ -103,6 +103,22 @@ def test_stages_load_their_slice_of_a_safetensors_file(comp, O, P, fixture, tmp_
         assert P.infer.generate_local(stages, PROMPT, 8, T) == ref
 
 
+def test_stage_handoff_carries_the_lap(comp, O, P, fixture):
+    """dc_stage_handoff (the stage-to-stage hop) between two stages: layers
+    0-2 on one stage, the hop into the next stage's buffer, layers 3-5 there;
+    the hidden state equals the one-stage run and the oracle bit for bit."""
+    import torch
+    ospec, spec, w, om = fixture
+    a, b = make_stages(P, comp, spec, w, [3, 3])
+    x = a.run_layers(a.embed_rows(win_of(PROMPT)))
+    y = torch.full_like(x, float("nan"))
+    a.handoff(b, x, y)
+    b.run_layers(y)
+    comp.sync()
+    want = om.run_layers(om.embed_rows(np.array(win_of(PROMPT), np.int32)), 0, 6)
+    assert y.cpu().numpy().tobytes() == want.tobytes()
+
+
 def test_mutations_are_caught_on_device(comp, O, P, fixture):
     ospec, spec, w, om = fixture
     ref = O.generate_local(om, [(0, 6)], PROMPT, 8, T)
