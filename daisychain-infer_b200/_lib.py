@@ -87,6 +87,8 @@ SIGNATURES = [
     ("dc_stage_forward", _i, [_p, _p, _i, _i, _i]),
     ("dc_stage_set_row_graph", _i, [_p, _i]),
     ("dc_stage_handoff", _i, [_p, _p, _p, _p, _i]),
+    ("dc_stage_set_timeline", _i, [_p, _p, _i, _i]),
+    ("dc_stage_timeline_info", _i, [_p, _p, _p, _i]),
     ("dc_stage_set_row_fusion", _i, [_p, _i]),
     ("dc_stage_logits", _i, [_p, _p, _i, _p, _i, _p, _p]),
     ("dc_decode_run", _i, [C.POINTER(_p), _i, _p, _i, _p, _i]),

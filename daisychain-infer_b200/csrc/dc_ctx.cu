@@ -233,6 +233,20 @@ int run_gates(dc_ctx* c) {
       }
     }
   }
+  // the persistent 2-SM form takes M > 128 shapes with a pair tile for every
+  // two SMs: ragged M (two activation tiles) and N (38 weight-pair tiles), K of two blocks
+  if (c->tc_enabled && c->tc2_enabled) {
+    const GateShape g = {300, 200, 9549, 1, true};
+    for (int poison = 0; poison < 2 && c->tp2_enabled; poison++) {
+      const int rc = gate_one(c, g, 3, poison, seed++, why);
+      if (rc == DC_E_GATE || rc == DC_E_INVAL) {
+        c->tp2_enabled = false;
+        fprintf(stderr, "dcinfer: persistent 2-SM GEMM gate failed, form disabled: %s\n", why.c_str());
+      } else if (rc) {
+        return rc;
+      }
+    }
+  }
   return DC_OK;
 }
 
@@ -259,7 +273,61 @@ int dc_set_smem(dc_ctx* ctx, const void* func, int bytes) {
 }
 
 static std::atomic<unsigned long long> g_launches{0};
-void dc_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// ---- decode-lap timeline ---------------------------------------------------
+// One thread writes %globaltimer once the kernel before it (on the stream) has
+// completed: launched as a programmatic dependent, it waits on the grid
+// dependency first.  Slot = lap counter * per_lap + index of the launch.
+__global__ void k_timeline_stamp(unsigned long long* buf, const int* step, int per_lap, int laps, int idx) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lap = *step;
+  if (threadIdx.x != 0 || lap < 0 || lap >= laps) return;  // laps past the buffer are not stamped
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  buf[(long long)lap * per_lap + idx] = t;
+}
+static thread_local dc_ctx* g_tl_ctx = nullptr;  // the context whose lap is being stamped
+
+static void timeline_stamp(dc_ctx* ctx) {
+  if (ctx->tl_idx >= ctx->tl_per_lap) return;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k_timeline_stamp, ctx->tl_buf, ctx->tl_step, ctx->tl_per_lap, ctx->tl_laps, ctx->tl_idx);
+  if ((int)ctx->tl_kind.size() <= ctx->tl_idx) {
+    ctx->tl_kind.resize(ctx->tl_idx + 1, 0);
+    ctx->tl_bytes.resize(ctx->tl_idx + 1, 0.0);
+  }
+  ctx->tl_kind[ctx->tl_idx] = 0;
+  ctx->tl_bytes[ctx->tl_idx] = 0.0;
+  ctx->tl_idx++;
+}
+void dc_timeline_begin(dc_ctx* ctx, const int* step) {
+  if (!ctx->tl_buf) return;
+  ctx->tl_idx = 0;
+  ctx->tl_step = step;
+  g_tl_ctx = ctx;
+  timeline_stamp(ctx);  // the lap's start
+}
+void dc_timeline_end(dc_ctx* ctx) {
+  if (g_tl_ctx == ctx) g_tl_ctx = nullptr;
+}
+void dc_timeline_tag(dc_ctx* ctx, int kind, double bytes) {
+  if (g_tl_ctx != ctx || ctx->tl_idx < 1) return;
+  ctx->tl_kind[ctx->tl_idx - 1] = kind;  // the stamp after the GEMM closes its interval
+  ctx->tl_bytes[ctx->tl_idx - 1] = bytes;
+}
+void dc_count_launch() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (dc_ctx* c = g_tl_ctx) timeline_stamp(c);
+}
 void dc_count_launches(long long n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 extern "C" unsigned long long dc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
@@ -327,6 +395,9 @@ extern "C" int dc_init(int device, dc_ctx** out) {
   if (!rc) rc = run_gates(c);
   if (!rc && !c->tc_enabled)
     snprintf(c->label, sizeof c->label, "%s (sm_100a): dp4a GEMM + GEMV, verified (tcgen05 gate failed)", prop.name);
+  else if (!rc && !c->tp2_enabled)
+    snprintf(c->label, sizeof c->label, "%s (sm_100a): tcgen05 i8 GEMM (1- and 2-SM tiles; persistent 2-SM gate failed) "
+             "+ dp4a GEMV, verified", prop.name);
   else if (!rc && !c->tc2_enabled)
     snprintf(c->label, sizeof c->label, "%s (sm_100a): tcgen05 i8 GEMM (one SM per tile; 2-SM gate failed) + dp4a GEMV, "
              "verified", prop.name);

@@ -630,7 +630,13 @@ int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, i
                      const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
                      int kind) {
   if (m == 0 || n == 0 || batch == 0) return DC_OK;
-  if (!ctx->timing) return gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind);
+  if (!ctx->timing) {
+    const int rc = gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind);
+    const double ob = (flags & DC_ACC) ? 4 : (flags & DC_REQUANT) ? 1 : 4;
+    dc_timeline_tag(ctx, (kind == 0) ? (m <= 8 ? 1 : 3) : kind,
+                    (double)batch * ((double)m * k + (double)k * n + 4.0 * m + 4.0 * n + ob * m * n));
+    return rc;
+  }
   dc_timed t;
   t.a = timing_event(ctx);
   t.b = timing_event(ctx);

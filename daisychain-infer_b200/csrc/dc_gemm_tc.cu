@@ -170,6 +170,7 @@ struct TcArgs {
   int32_t* partial;   // split-K int32 scratch (zero between calls), or null
   int* counters;      // split-K tile counters (zero between calls), or null
   int* status;
+  int batch;          // k_gemm_tp2: batches its pairs loop over (its grid has one z slice)
 };
 
 // The epilogue of one CTA's 128 output columns j0.. x BN activation rows i0..:
@@ -571,6 +572,199 @@ __global__ void __launch_bounds__(TC2_THREADS, 1)
   }
 }
 
+// ---- the persistent 2-SM variant ---------------------------------------------
+// k_gemm_tc2's tiles and operand split, with each CTA pair looping over pair
+// tiles t = pair, pair + pairs, ... (the activation-tile index fastest, so the
+// pairs running together share weight tiles through L2) and a double-buffered
+// accumulator: the pair's TMEM holds two 256-column accumulators, the even
+// CTA's MMA thread fills one while the epilogue warps of both CTAs drain the
+// other.  The epilogue warps hand a buffer back with a remote arrive on the
+// even CTA's `tempty` barrier.  Warps: 0 TMA producer, 1 MMA issuer (even CTA)
+// and TMEM owner, 2-3 idle, 4-11 epilogue (two per TMEM lane quarter, 128
+// activation rows each).  No split-K: used when the pair tiles fill the SMs.
+constexpr int TP2_THREADS = 384;
+constexpr int TP2_EPI_WARPS = 8;
+constexpr int TP2_SMEM = TC2_STAGES * TC2_STAGE + 1024 + 512;
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__global__ void __launch_bounds__(TP2_THREADS, 1)
+    k_gemm_tp2(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + TC2_STAGES * TC2_HALF;
+  uint64_t* full = (uint64_t*)(smem + TC2_STAGES * TC2_STAGE);
+  uint64_t* empty = full + TC2_STAGES;
+  uint64_t* tfull = empty + TC2_STAGES;  // [2]: an accumulator is complete
+  uint64_t* tempty = tfull + 2;          // [2]: an accumulator is drained (the even CTA's count both CTAs)
+  uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
+  int* flag = (int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int pairs_n = a.n_tiles >> 1;
+  const int tiles = pairs_n * a.m_tiles * a.batch;
+  const int nkb = a.kb_total;
+  // pair tile t -> (bz, tile_m, tile_n), tile_m fastest
+  auto decode = [&](int t, int& bz, int& tm, int& tn) {
+    tm = t % a.m_tiles;
+    tn = (t / a.m_tiles) % pairs_n;
+    bz = t / (a.m_tiles * pairs_n);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC2_STAGES; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * TP2_EPI_WARPS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    *flag = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync_all();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer, both CTAs, one K-block stream across all its tiles
+    const uint32_t full_l = map_rank(&full[0], 0);
+    int it = 0;
+    bool waited = false;
+    for (int t = pair; t < tiles && !*(volatile int*)flag; t += pairs) {
+      int bz, tm, tn;
+      decode(t, bz, tm, tn);
+      const int j0 = tn * 256 + 128 * (int)rank, i0 = tm * 256 + 128 * (int)rank;
+      for (int kb = 0; kb < nkb; kb++, it++) {
+        const int s = it % TC2_STAGES;
+        if (it >= TC2_STAGES && !mbar_wait(&empty[s], ((uint32_t)(it / TC2_STAGES) & 1u) ^ 1u, a.status)) {
+          atomicExch(flag, 1);
+          break;
+        }
+        if (leader) mbar_expect_tx(&full[s], 2 * TC2_STAGE);
+        tma_load_pair(sA + s * TC2_HALF, &tmW, kb * TILE_K, bz * a.n + j0, full_l + 8 * s);
+        if (!waited) {  // activations come from the kernel before this one
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          waited = true;
+        }
+        tma_load_pair(sB + s * TC2_HALF, &tmX, kb * TILE_K, bz * a.m + i0, full_l + 8 * s);
+      }
+    }
+    if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---- MMA issuer (the even CTA)
+    const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                           ((uint32_t)(256 >> 4) << 24);
+    int it = 0, lt = 0;
+    bool ok = true;
+    for (int t = pair; t < tiles && ok; t += pairs, lt++) {
+      const int b = lt & 1, use = lt >> 1;
+      if (use > 0 && !mbar_wait(&tempty[b], (uint32_t)(use - 1) & 1u, a.status)) {
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t acc = tmem + (uint32_t)(b * 256);
+      for (int kb = 0; kb < nkb; kb++, it++) {
+        const int s = it % TC2_STAGES;
+        if (!mbar_wait(&full[s], (uint32_t)(it / TC2_STAGES) & 1u, a.status)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint8_t* ta = sA + s * TC2_HALF;
+        const uint8_t* tb = sB + s * TC2_HALF;
+#pragma unroll
+        for (int kk = 0; kk < TILE_K / MMA_K; kk++)
+          mma_i8_pair(acc, umma_desc(ta + kk * MMA_K), umma_desc(tb + kk * MMA_K), idesc,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+        mma_commit_pair(&empty[s]);
+      }
+      mma_commit_pair(&tfull[b]);  // (after an abort too: the epilogues wake and see the flag)
+    }
+    if (!ok) {
+      atomicExch(flag, 1);
+      // every stage issued but not consumed lands before the pair goes away
+      for (int k = it; k < it + TC2_STAGES; k++) mbar_wait(&full[k % TC2_STAGES], (uint32_t)(k / TC2_STAGES) & 1u, a.status);
+    }
+  } else if (warp >= 4) {
+    // ---- epilogue warps, both CTAs
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // rs and a residual `out` come from earlier kernels
+    const int quarter = warp & 3, part = (warp - 4) >> 2;  // TMEM lanes 32*quarter.., activation rows part*128..
+    const uint32_t tempty_l = map_rank(&tempty[0], 0);
+    int lt = 0;
+    for (int t = pair; t < tiles; t += pairs, lt++) {
+      const int b = lt & 1, use = lt >> 1;
+      const bool have = mbar_wait(&tfull[b], (uint32_t)use & 1u, a.status);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (!have) atomicExch(flag, 1);
+      if (have && !*(volatile int*)flag) {
+        int bz, tm, tn;
+        decode(t, bz, tm, tn);
+        const int j = tn * 256 + 128 * (int)rank + quarter * 32 + lane;
+        const int i0 = tm * 256 + part * 128;
+        const bool jv = j < a.n;
+        const float csv = jv ? __ldg(a.cs + bz * a.n + j) : 0.0f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 256 + part * 128 + c0), r);
+          float old[16];
+          if (a.flags & DC_F_ADDTO) {
+#pragma unroll
+            for (int c = 0; c < 16; c++) {
+              const int i = i0 + c0 + c;
+              old[c] = (jv && i < a.m) ? ((const float*)a.out)[((int64_t)bz * a.m + i) * a.n + j] : 0.0f;
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 16; c++) {
+            const int i = i0 + c0 + c;
+            if (!(jv && i < a.m)) continue;
+            const int64_t idx = ((int64_t)bz * a.m + i) * a.n + j;
+            const float rsv = __ldg(a.rs + bz * a.m + i);
+            if (a.flags & (DC_ACC | DC_REQUANT)) {
+              dc_store_out(a.out, idx, (int32_t)r[c], rsv, csv, a.flags, a.requant, a.relu);
+            } else {
+              float o = dc_epi((int32_t)r[c], rsv, csv);
+              if ((a.flags & DC_RELU) && o < 0.0f) o = 0.0f;
+              if (a.flags & DC_F_ADDTO) o = __fadd_rn(old[c], o);
+              ((float*)a.out)[idx] = o;
+            }
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_l + 8 * b);  // this warp is done with buffer b
+      if (!have) break;
+    }
+  }
+  __syncwarp();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees the pair's TMEM or leaves while the other still uses it
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -755,6 +949,52 @@ int launch_tc2(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw
   return DC_OK;
 }
 
+// k_gemm_tp2: as many CTA pairs as fit beside each other (at most one per two
+// SMs), each looping over its share of the pair tiles.
+int launch_tp2(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+               int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st) {
+  CUtensorMap mW, mX;
+  if (!make_map(&mW, Wt, ldw, (long)batch * n, TILE_N) || !make_map(&mX, Xq, ldx, (long)batch * m, 128))
+    return dc_fail(ctx, DC_E_INVAL, "tcgen05: tensor map encode failed");
+  TcArgs a = {};
+  a.rs = rs;
+  a.cs = cs;
+  a.m = m;
+  a.k = k;
+  a.n = n;
+  a.kb_total = (k + TILE_K - 1) / TILE_K;
+  a.kb_per_split = a.kb_total;
+  a.splits = 1;
+  a.n_tiles = 2 * ((n + 255) / 256);
+  a.m_tiles = (m + 255) / 256;
+  a.batch = batch;
+  a.flags = flags;
+  a.requant = ctx->d_requant;
+  a.relu = ctx->d_relu;
+  a.out = out;
+  a.status = ctx->d_status;
+  const int tiles = (a.n_tiles / 2) * a.m_tiles * batch;
+  const int pairs = std::max(1, std::min(ctx->sm_count / 2, tiles));
+  if (int rc = dc_set_smem(ctx, (const void*)k_gemm_tp2, TP2_SMEM)) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(TP2_THREADS);
+  cfg.dynamicSmemBytes = TP2_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemm_tp2, mW, mX, a));
+  dc_count_launch();
+  return DC_OK;
+}
+
 }  // namespace
 
 // Split-K scratch of a context: int32 partial sums and tile counters, both kept
@@ -800,6 +1040,10 @@ int dc_gemm_tc_with(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, in
   if (m <= 128)
     return launch_tc<128>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
                           partial_cap, counter_cap, clear);
+  // enough pair tiles to give every SM pair one: the persistent kernel
+  if (ctx->tc2_enabled && ctx->tp2_enabled &&
+      (size_t)((n + 255) / 256) * ((m + 255) / 256) * batch >= (size_t)ctx->sm_count / 2)
+    return launch_tp2(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
   if (ctx->tc2_enabled)
     return launch_tc2(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters, partial_cap,
                       counter_cap, clear);

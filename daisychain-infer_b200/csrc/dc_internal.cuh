@@ -48,6 +48,7 @@ struct dc_ctx {
   size_t scratch_bytes = 0;
   bool tc_enabled = true;  // tcgen05 GEMM passed its gate
   bool tc2_enabled = true;  // its 2-SM variant (M > 128) passed its gate
+  bool tp2_enabled = true;  // its persistent 2-SM form (M > 128, many tiles) passed its gate
   // split-K scratch of the tcgen05 GEMM (kept zero between calls by the kernel)
   int32_t* tc_partial = nullptr;
   int* tc_counters = nullptr;
@@ -55,6 +56,13 @@ struct dc_ctx {
   // dc_bgemm_dev_noalloc: device address of the library's fixed scratch array,
   // looked up by the first call on this context
   int32_t* noalloc_scratch = nullptr;
+  // decode-lap timeline (dc_stage_set_timeline): a %globaltimer stamp after
+  // every launch of a lap, and what each launch was
+  unsigned long long* tl_buf = nullptr;
+  int tl_per_lap = 0, tl_idx = 0, tl_laps = 0;
+  const int* tl_step = nullptr;        // the lap counter (device)
+  std::vector<int> tl_kind;            // per launch of the lap: 1 one-row GEMV, 3 tcgen05, 0 other
+  std::vector<double> tl_bytes;        // and its algorithmic bytes (GEMMs)
   // live GEMM timing (dc_timing / dc_timing_read)
   bool timing = false;
   std::vector<dc_timed> timed;
@@ -92,6 +100,12 @@ int dc_set_smem(dc_ctx* ctx, const void* func, int bytes);
 
 // Kernels launched by this library in this process (reported by dc_launch_count).
 void dc_count_launch();
+// Decode-lap timeline: start stamping the launches of one lap on ctx (a stamp
+// now, then one after every launch until dc_timeline_end); tag the latest
+// launch as a GEMM of the given kind and algorithmic bytes.
+void dc_timeline_begin(dc_ctx* ctx, const int* step);
+void dc_timeline_end(dc_ctx* ctx);
+void dc_timeline_tag(dc_ctx* ctx, int kind, double bytes);
 void dc_count_launches(long long n);  // e.g. the kernels of one CUDA-graph replay
 
 // ---- launchers shared between translation units ----------------------------

@@ -2344,6 +2344,33 @@ extern "C" int dc_stage_set_row_graph(dc_stage* S, int on) {
   return DC_OK;
 }
 
+extern "C" int dc_stage_set_timeline(dc_stage* S, unsigned long long* buf, int per_lap, int laps) {
+  if (!S || per_lap < 0 || laps < 0 || (per_lap && laps && !buf))
+    return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_set_timeline: bad arguments");
+  dc_ctx* ctx = S->ctx;
+  const bool on = per_lap > 0 && laps > 0;
+  ctx->tl_buf = on ? buf : nullptr;
+  ctx->tl_per_lap = on ? per_lap : 0;
+  ctx->tl_laps = on ? laps : 0;
+  ctx->tl_kind.clear();
+  ctx->tl_bytes.clear();
+  if (S->lap_exec) cudaGraphExecDestroy(S->lap_exec);  // a captured lap holds the other kernel sequence
+  S->lap_exec = nullptr;
+  S->lap_key.clear();
+  return DC_OK;
+}
+
+extern "C" int dc_stage_timeline_info(const dc_stage* S, int* kinds, double* bytes, int cap) {
+  if (!S) return -1;
+  const dc_ctx* ctx = S->ctx;
+  const int n = (int)ctx->tl_kind.size();
+  for (int i = 0; i < n && i < cap; i++) {
+    if (kinds) kinds[i] = ctx->tl_kind[i];
+    if (bytes) bytes[i] = ctx->tl_bytes[i];
+  }
+  return n;
+}
+
 extern "C" int dc_stage_set_row_fusion(dc_stage* S, int on) {
   if (!S) return DC_E_INVAL;
   if ((on != 0) != S->row_fused) {  // captured graphs hold the other kernel sequence
@@ -2394,6 +2421,7 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
   dc_ctx* ctx = H->ctx;
   cudaStream_t s = ctx->stream;
   int rc = DC_OK;
+  dc_timeline_begin(ctx, H->d_step);
   if (H->row_fused && fg_fits(H)) {  // final RMSNorm fused into the lm_head GEMV
     if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM>, (int)fg_smem(FG_NORM, H->C))) return rc0;
     DC_CUDA(ctx, launch_fused(H, FG_NORM, H->xlap, H->C, H->nrmF, nullptr, H->lm, 0, H->logits1, nullptr, nullptr));
@@ -2418,6 +2446,7 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
     k_addpos<<<1, 1, 0, s>>>(S->d_pos, 1);
     dc_count_launch();
   }
+  dc_timeline_end(ctx);  // (the stamps of a lap end before its counter moves)
   k_addpos<<<1, 1, 0, s>>>(H->d_step, 1);
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());

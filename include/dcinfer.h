@@ -244,6 +244,18 @@ int dc_stage_logits(dc_stage* stage, const float* x, int T, const int32_t* rows,
  * never leave the device between laps.  use_graph = 1 captures one lap as a
  * CUDA graph (kernel positions live in device memory) and replays it. */
 int dc_decode_run(dc_stage** stages, int ns, const float* x_last, int n_new, int32_t* picks, int use_graph);
+/* Decode-lap timeline (a measurement aid; no counterpart in the reference).
+ * With buf set (device memory, laps x per_lap uint64) on the head stage,
+ * dc_decode_run stamps %globaltimer at the start of each lap and after every
+ * launch of it, into buf[lap * per_lap + i] (lap = index within the call; the
+ * first per_lap launches and the first laps laps only), with a one-thread
+ * kernel after each launch, which lengthens a lap by one or two microseconds
+ * per launch; per_lap = 0 turns it off.  dc_stage_timeline_info copies out,
+ * for stamp i, the kind of the launch it closes (1 one-row GEMV, 3 tcgen05
+ * GEMM, 0 other) and that GEMM's algorithmic bytes, and returns the stamps
+ * per lap of the last lap enqueued. */
+int dc_stage_set_timeline(dc_stage* head, unsigned long long* buf, int per_lap, int laps);
+int dc_stage_timeline_info(const dc_stage* head, int* kinds, double* bytes, int cap);
 /* The activation hop between pipeline stages (app.js:705-765, the act message
  * of wire.js:106-138): T rows of hidden floats from x_src (device memory of
  * src's GPU) to x_dst (device memory of dst's GPU), ordered after the work
