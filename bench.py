@@ -283,12 +283,8 @@ def bench_model(args, rank, world, peaks):
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
-    # chunked workloads run their decode rows as CUDA graphs, which carry no
-    # per-GEMM events: their GEMMs are timed in a pass right after the timed
-    # region; the window / lookahead workloads time them live
-    live = w["mode"] != "chunked"
-    if live:
-        comp.L.dc_timing(comp.h, 1)
+    # (the GEMMs are timed in passes right after the timed region, which runs
+    # with no per-GEMM events or stamps)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     t0.record()
@@ -319,31 +315,43 @@ def bench_model(args, rank, world, peaks):
             out[kind] = (ms.value, n.value, by.value, op.value)
         return out
 
-    if live:
-        kinds = read_kinds()
-        comp.L.dc_timing(comp.h, 0)
-        gemv_method = tc_method = "CUDA events around every launch in the timed region"
-    else:
-        # every rank: one more generation (the same prompt, 16 decode tokens)
-        # with events around each GEMM; its laps run kernel by kernel
+    # one more generation with CUDA events around every GEMM launch (a chunked
+    # workload: the same prompt and 16 decode tokens, decode laps launched
+    # kernel by kernel; a lookahead workload: one more step)
+    comp.L.dc_timing(comp.h, 1)
+    if w["mode"] == "chunked":
         use_graph = getattr(ring, "use_graph", False)
         ring.use_graph = False
-        comp.L.dc_timing(comp.h, 1)
         ring.generate_chunked(ids, 16, w["chunk"], w["window"])
-        got = read_kinds()
-        comp.L.dc_timing(comp.h, 0)
         ring.use_graph = use_graph
+        ev_scale = w["new"] * args.steps / 16.0
+    else:
+        one_step()
+        ev_scale = args.steps
+    got = read_kinds()
+    comp.L.dc_timing(comp.h, 0)
+    tc_method = ("CUDA events around every tcgen05 launch of the same prompt's prefill, run right after the timed "
+                 "region (launched one by one, as in the timed steps), times the timed steps")
+    tl = None
+    if w["mode"] == "chunked" and world == 1:
+        # the timed decode laps are CUDA-graph replays: time their GEMVs inside
+        # replays, from %globaltimer stamps between the launches of each lap
+        tl = decode_timeline(S, ring, ids, w)
         laps = w["new"] * args.steps
+        ops_per_byte = got[1][3] / got[1][2] if got[1][2] else 0.0
+        gemv = (tl["gemv_ms_per_lap"] * laps, tl["gemv_launches_per_lap"] * laps,
+                tl["gemv_bytes_per_lap"] * laps, tl["gemv_bytes_per_lap"] * laps * ops_per_byte)
+        gemv_method = ("%%globaltimer stamps between the launches of %d CUDA-graph-replayed decode laps run right "
+                       "after the timed region (dc_stage_set_timeline; same stages and shapes): a GEMV's time is "
+                       "the gap from the stamp after the launch before it to the stamp after it, median over the "
+                       "laps, times the timed region's laps; each gap includes one stamp launch (%.2f us, the "
+                       "lap's growth per stamp)" % (tl["laps"], tl["stamp_cost_us"]))
+    else:
         ms_, n_, by_, op_ = got[1]
-        scale = laps / 16.0
-        kinds = {1: (ms_ * scale, int(round(n_ * scale)), by_ * scale, op_ * scale),
-                 3: (got[3][0] * args.steps, int(got[3][1] * args.steps), got[3][2] * args.steps,
-                     got[3][3] * args.steps)}
-        gemv_method = ("CUDA events around every GEMV launch of 16 decode steps run kernel by kernel right after "
-                       "the timed region (same stages, same shapes; the timed decode steps are CUDA-graph "
-                       "replays), scaled to the timed region's steps")
-        tc_method = ("CUDA events around every tcgen05 launch of the same prompt's prefill, run right after the "
-                     "timed region, times the timed steps")
+        gemv = (ms_ * ev_scale, int(round(n_ * ev_scale)), by_ * ev_scale, op_ * ev_scale)
+        gemv_method = ("CUDA events around every GEMV launch of the pass above (kernel by kernel), scaled to the "
+                       "timed region's decode steps")
+    kinds = {1: gemv, 3: tuple(v * args.steps for v in got[3])}
     ms_step, pre, dec = max_over_ranks([ms_step, pre, dec], world)
     launches = int(sum_over_ranks([launches], world)[0])
     n_new = w["new"]
@@ -379,6 +387,8 @@ def bench_model(args, rank, world, peaks):
                     roofline=roof, kernels=other, gpu_launches=launches, clocks=clk, backend=comp.label,
                     generated_ids_fnv=P_fnv(gen_ids), generated_head=gen_ids[:8],
                     weights_gb=weight_bytes(spec, 0, spec.layers, True) / 1e9)
+        if tl is not None:
+            line["decode_timeline"] = tl
     if not args.no_e2e:  # every rank takes part in the ring; rank 0 reports
         e2e = e2e_model(comp, ring, w, ids, args, world)
         if rank == 0:
@@ -390,6 +400,72 @@ def bench_model(args, rank, world, peaks):
         dist.barrier()
     S.close()
     return line
+
+
+def decode_timeline(S, ring, ids, w, laps: int = 17, per_lap: int = 2048):
+    """Time the GEMVs of graph-replayed decode laps from the inside: one more
+    generation of the same prompt with `laps` decode tokens, the head stage
+    stamping %globaltimer after every launch of each lap (dc_stage_set_timeline).
+    Lap 0 runs kernel by kernel (it is captured into the graph the others
+    replay) and is dropped.  A GEMV's time is the gap between the stamp after it
+    and the stamp after the launch before it; the figures are medians over the
+    replayed laps.  The same generation without stamps gives the lap time the
+    stamps are charged against."""
+    import numpy as np
+    import torch
+
+    def decode_ms(stamped):
+        buf = None
+        if stamped:
+            buf = torch.zeros(laps * per_lap, dtype=torch.int64, device="cuda")
+            S.set_timeline(buf, per_lap, laps)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        try:
+            e[0].record()
+            ring.generate_chunked(ids, laps, w["chunk"], w["window"], on_prefill=e[1].record)
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            torch.cuda.synchronize()
+            info = S.timeline_info() if stamped else None
+        finally:
+            if stamped:
+                S.set_timeline()
+        return e[1].elapsed_time(end), buf, info
+
+    plain_ms, _, _ = decode_ms(False)
+    stamped_ms, buf, (kinds, by) = decode_ms(True)
+    n = len(kinds)
+    if n < 2 or n > per_lap:
+        raise RuntimeError(f"decode timeline: {n} stamps per lap (buffer holds {per_lap})")
+    t = buf.view(laps, per_lap)[1:, :n].cpu().numpy().astype(np.float64)
+    if not (t > 0).all():
+        raise RuntimeError("decode timeline: a replayed lap left stamps unwritten")
+    gaps = np.diff(t, axis=1) / 1e6  # ms; gaps[:, i - 1] is closed by stamp i
+    k = np.asarray(kinds[1:])
+    b = np.asarray(by[1:])
+    gemv = k == 1
+    lap_ms = np.median(t[:, -1] - t[:, 0]) / 1e6
+    gemv_ms = float(np.median(gaps[:, gemv].sum(axis=1)))
+    tc_ms = float(np.median(gaps[:, k == 3].sum(axis=1)))
+    gemv_bytes = float(b[gemv].sum())
+    per = gaps[:, gemv]
+    # per GEMV shape: (bytes) -> median in-graph GB/s
+    shapes = {}
+    for col, bb in zip(range(per.shape[1]), b[gemv]):
+        shapes.setdefault(round(bb), []).append(np.median(per[:, col]))
+    stamp_cost_us = (stamped_ms - plain_ms) / laps / n * 1e3
+    med = np.median(gaps, axis=0) * 1e3  # us, per launch of the lap
+    return dict(laps=laps - 1, stamps_per_lap=n, gemv_launches_per_lap=int(gemv.sum()),
+                gemv_bytes_per_lap=gemv_bytes, gemv_ms_per_lap=gemv_ms,
+                gemv_gbs=gemv_bytes / (gemv_ms / 1e3) / 1e9, tcgen05_ms_per_lap=tc_ms,
+                stamped_lap_ms=float(lap_ms), plain_decode_ms_per_lap=plain_ms / laps,
+                stamp_cost_us=stamp_cost_us,
+                launch_us_first=[round(float(v), 2) for v in med[:21]],
+                launch_us_last=[round(float(v), 2) for v in med[-8:]],
+                launch_kinds_first=[int(v) for v in k[:21]], launch_kinds_last=[int(v) for v in k[-8:]],
+                gemv_by_bytes_per_launch={str(kb): dict(launches_per_lap=len(v), us=float(np.median(v) * 1e3),
+                                                        gbs=kb / (np.median(v) / 1e3) / 1e9)
+                                          for kb, v in sorted(shapes.items())})
 
 
 def e2e_model(comp, ring, w, ids, args, world=1):
@@ -730,15 +806,15 @@ def bench_gemm_sweep(args, rank, world, peaks):
 
 def profile_gemm(args):
     """One GEMM of the sweep inside an NVTX range "profile", for an ncu capture
-    of exactly that launch (M = --gemm-m, K = 4096, N = 14336, requant int8
-    out), after three warm-up calls of the same shape:
+    of exactly that launch (M = --gemm-m, K = --gemm-k, N = --gemm-n, requant
+    int8 out), after three warm-up calls of the same shape:
 
         ncu --set full --nvtx --nvtx-include "profile/" -k regex:k_gemm ... python bench.py --profile gemm"""
     import torch
     import __graft_entry__ as G
     P = G.package()
     comp = P.init_compute(0, stream=torch.cuda.current_stream())
-    m, k, n = args.gemm_m, 4096, 14336
+    m, k, n = args.gemm_m, args.gemm_k, args.gemm_n
     g = torch.Generator(device="cuda").manual_seed(1)
     W = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
     cs = torch.rand(n, generator=g, device="cuda") * 9e-3 + 1e-3
@@ -813,7 +889,9 @@ def main():
     ap.add_argument("--profile", choices=["prefill", "decode", "gemm"], default=None,
                     help="run one prefill chunk, one decode lap or one sweep GEMM inside an NVTX range 'profile' "
                          "(for ncu); prints no benchmark line")
-    ap.add_argument("--gemm-m", type=int, default=512, help="M of the --profile gemm launch (K 4096, N 14336)")
+    ap.add_argument("--gemm-m", type=int, default=512, help="M of the --profile gemm launch")
+    ap.add_argument("--gemm-k", type=int, default=4096, help="K of the --profile gemm launch")
+    ap.add_argument("--gemm-n", type=int, default=14336, help="N of the --profile gemm launch")
     args = ap.parse_args()
     if args.workload in WORKLOADS:
         w = WORKLOADS[args.workload]

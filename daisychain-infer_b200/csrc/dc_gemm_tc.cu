@@ -188,28 +188,39 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, uint32_t tmem, bool
   const int j = j0 + quarter * 32 + lane;
   const bool jv = j < a.n;
   const float csv = jv ? __ldg(a.cs + bz * a.n + j) : 0.0f;
-  // 16 accumulators of one column j: residual values loaded first, then stored
+  // 16 accumulators of one column j (activation rows i0 + cbase ..): one
+  // loop per output mode, walking the rows at a stride of n through a
+  // pointer; residual values are all loaded before the first store
+  const int64_t n64 = a.n;
+  const bool relu = (a.flags & DC_RELU) != 0;
   auto store16 = [&](int cbase, const int32_t (&v)[16]) {
-    float old[16];
-    if (a.flags & DC_F_ADDTO) {
+    const int cn = min(16, a.m - (i0 + cbase));
+    if (!jv || cn <= 0) return;
+    const int64_t base = ((int64_t)bz * a.m + i0 + cbase) * n64 + j;
+    if (a.flags & DC_ACC) {  // (DC_ACC before DC_REQUANT, as dc_store_out)
+      int32_t* o = (int32_t*)a.out + base;
+#pragma unroll
+      for (int c = 0; c < 16; c++)
+        if (c < cn) o[(int64_t)c * n64] = v[c];
+    } else if (a.flags & DC_REQUANT) {
+      int8_t* o = (int8_t*)a.out + base;
+#pragma unroll
+      for (int c = 0; c < 16; c++)
+        if (c < cn) o[(int64_t)c * n64] = dc_requant_unit(v[c], relu);
+    } else {
+      float* o = (float*)a.out + base;
+      float old[16];
+      if (a.flags & DC_F_ADDTO) {
+#pragma unroll
+        for (int c = 0; c < 16; c++) old[c] = c < cn ? o[(int64_t)c * n64] : 0.0f;
+      }
 #pragma unroll
       for (int c = 0; c < 16; c++) {
-        const int i = i0 + cbase + c;
-        old[c] = (jv && i < a.m) ? ((const float*)a.out)[((int64_t)bz * a.m + i) * a.n + j] : 0.0f;
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < 16; c++) {
-      const int i = i0 + cbase + c;
-      if (!(jv && i < a.m)) continue;
-      const int64_t idx = ((int64_t)bz * a.m + i) * a.n + j;
-      if (a.flags & (DC_ACC | DC_REQUANT)) {
-        dc_store_out(a.out, idx, v[c], rs_s[cbase + c], csv, a.flags, a.requant, a.relu);
-      } else {
-        float o = dc_epi(v[c], rs_s[cbase + c], csv);
-        if ((a.flags & DC_RELU) && o < 0.0f) o = 0.0f;
-        if (a.flags & DC_F_ADDTO) o = __fadd_rn(old[c], o);
-        ((float*)a.out)[idx] = o;
+        if (c >= cn) continue;
+        float x = dc_epi(v[c], rs_s[cbase + c], csv);
+        if (relu && x < 0.0f) x = 0.0f;
+        if (a.flags & DC_F_ADDTO) x = __fadd_rn(old[c], x);
+        o[(int64_t)c * n64] = x;
       }
     }
   };
@@ -584,7 +595,7 @@ __global__ void __launch_bounds__(TC2_THREADS, 1)
 // activation rows each).  No split-K: used when the pair tiles fill the SMs.
 constexpr int TP2_THREADS = 384;
 constexpr int TP2_EPI_WARPS = 8;
-constexpr int TP2_SMEM = TC2_STAGES * TC2_STAGE + 1024 + 512;
+constexpr int TP2_SMEM = TC2_STAGES * TC2_STAGE + 1024 + 512 + 2 * 256 * 4;
 
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
@@ -602,11 +613,16 @@ __global__ void __launch_bounds__(TP2_THREADS, 1)
   uint64_t* tempty = tfull + 2;          // [2]: an accumulator is drained (the even CTA's count both CTAs)
   uint32_t* tmem_slot = (uint32_t*)(tempty + 2);
   int* flag = (int*)(tmem_slot + 1);
+  float* rs_s = (float*)(smem + TC2_STAGES * TC2_STAGE + 512);  // [2][256]: a tile's row scales (f32 output)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  if (warp == 0 && lane == 0) {  // the descriptors' first fetch overlaps the set-up
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmW) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmX) : "memory");
+  }
   const int pairs_n = a.n_tiles >> 1;
   const int tiles = pairs_n * a.m_tiles * a.batch;
   const int nkb = a.kb_total;
@@ -703,48 +719,73 @@ __global__ void __launch_bounds__(TP2_THREADS, 1)
       for (int k = it; k < it + TC2_STAGES; k++) mbar_wait(&full[k % TC2_STAGES], (uint32_t)(k / TC2_STAGES) & 1u, a.status);
     }
   } else if (warp >= 4) {
-    // ---- epilogue warps, both CTAs
+    // ---- epilogue warps, both CTAs.  Each thread owns one output column j and
+    // walks 128 activation rows at a stride of n through a pointer; the modes
+    // are separate loops, so the int8 / int32 outputs read nothing but TMEM and
+    // the f32 output reads its row scales from shared memory (staged once per
+    // tile), never a global load between two stores.
     asm volatile("griddepcontrol.wait;" ::: "memory");  // rs and a residual `out` come from earlier kernels
     const int quarter = warp & 3, part = (warp - 4) >> 2;  // TMEM lanes 32*quarter.., activation rows part*128..
+    const int et = threadIdx.x - 128;                      // 0..255 over the epilogue warps
     const uint32_t tempty_l = map_rank(&tempty[0], 0);
+    const bool f32_out = !(a.flags & (DC_ACC | DC_REQUANT));
+    const bool relu = (a.flags & DC_RELU) != 0, addto = (a.flags & DC_F_ADDTO) != 0;
+    const int64_t n64 = a.n;
     int lt = 0;
     for (int t = pair; t < tiles; t += pairs, lt++) {
       const int b = lt & 1, use = lt >> 1;
-      const bool have = mbar_wait(&tfull[b], (uint32_t)use & 1u, a.status);
+      int bz, tm, tn;
+      decode(t, bz, tm, tn);
+      float* rsb = rs_s + b * 256;
+      if (f32_out) {  // (double-buffered: a warp cannot pass the next tile's barrier before all leave this one)
+        const int i = tm * 256 + et;
+        rsb[et] = i < a.m ? __ldg(a.rs + (int64_t)bz * a.m + i) : 0.0f;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
+      // every epilogue warp takes every tile of the loop (so all meet at each
+      // barrier above); after a failure they only hand the buffers back
+      const bool have = !*(volatile int*)flag && mbar_wait(&tfull[b], (uint32_t)use & 1u, a.status);
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       if (!have) atomicExch(flag, 1);
       if (have && !*(volatile int*)flag) {
-        int bz, tm, tn;
-        decode(t, bz, tm, tn);
         const int j = tn * 256 + 128 * (int)rank + quarter * 32 + lane;
         const int i0 = tm * 256 + part * 128;
+        const int rows = min(128, a.m - i0);  // activation rows of this warp in range (<= 0: none)
         const bool jv = j < a.n;
-        const float csv = jv ? __ldg(a.cs + bz * a.n + j) : 0.0f;
+        const float csv = (f32_out && jv) ? __ldg(a.cs + (int64_t)bz * a.n + j) : 0.0f;
+        const int64_t base = ((int64_t)bz * a.m + i0) * n64 + j;
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 256 + part * 128);
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 16) {
+        for (int c0 = 0; c0 < 128 && c0 < rows; c0 += 16) {
           uint32_t r[16];
-          tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 256 + part * 128 + c0), r);
-          float old[16];
-          if (a.flags & DC_F_ADDTO) {
+          tmem_ld16(taddr + (uint32_t)c0, r);
+          if (!jv) continue;
+          const int cn = min(16, rows - c0);
+          if (a.flags & DC_ACC) {  // (DC_ACC before DC_REQUANT, as dc_store_out)
+            int32_t* o = (int32_t*)a.out + base + (int64_t)c0 * n64;
+#pragma unroll
+            for (int c = 0; c < 16; c++)
+              if (c < cn) o[(int64_t)c * n64] = (int32_t)r[c];
+          } else if (a.flags & DC_REQUANT) {
+            int8_t* o = (int8_t*)a.out + base + (int64_t)c0 * n64;
+#pragma unroll
+            for (int c = 0; c < 16; c++)
+              if (c < cn) o[(int64_t)c * n64] = dc_requant_unit((int32_t)r[c], relu);
+          } else {
+            float* o = (float*)a.out + base + (int64_t)c0 * n64;
+            const float* rsv = rsb + part * 128 + c0;
+            float old[16];
+            if (addto) {  // all 16 residual loads in flight before the first store
+#pragma unroll
+              for (int c = 0; c < 16; c++) old[c] = c < cn ? o[(int64_t)c * n64] : 0.0f;
+            }
 #pragma unroll
             for (int c = 0; c < 16; c++) {
-              const int i = i0 + c0 + c;
-              old[c] = (jv && i < a.m) ? ((const float*)a.out)[((int64_t)bz * a.m + i) * a.n + j] : 0.0f;
-            }
-          }
-#pragma unroll
-          for (int c = 0; c < 16; c++) {
-            const int i = i0 + c0 + c;
-            if (!(jv && i < a.m)) continue;
-            const int64_t idx = ((int64_t)bz * a.m + i) * a.n + j;
-            const float rsv = __ldg(a.rs + bz * a.m + i);
-            if (a.flags & (DC_ACC | DC_REQUANT)) {
-              dc_store_out(a.out, idx, (int32_t)r[c], rsv, csv, a.flags, a.requant, a.relu);
-            } else {
-              float o = dc_epi((int32_t)r[c], rsv, csv);
-              if ((a.flags & DC_RELU) && o < 0.0f) o = 0.0f;
-              if (a.flags & DC_F_ADDTO) o = __fadd_rn(old[c], o);
-              ((float*)a.out)[idx] = o;
+              if (c >= cn) continue;
+              float v = dc_epi((int32_t)r[c], rsv[c], csv);
+              if (relu && v < 0.0f) v = 0.0f;
+              if (addto) v = __fadd_rn(old[c], v);
+              o[(int64_t)c * n64] = v;
             }
           }
         }
@@ -752,7 +793,6 @@ __global__ void __launch_bounds__(TP2_THREADS, 1)
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(tempty_l + 8 * b);  // this warp is done with buffer b
-      if (!have) break;
     }
   }
   __syncwarp();

@@ -2422,6 +2422,10 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
   cudaStream_t s = ctx->stream;
   int rc = DC_OK;
   dc_timeline_begin(ctx, H->d_step);
+  struct TimelineEnd {  // (an early error return ends the lap's stamping too)
+    dc_ctx* c;
+    ~TimelineEnd() { dc_timeline_end(c); }
+  } tl_end{ctx};
   if (H->row_fused && fg_fits(H)) {  // final RMSNorm fused into the lm_head GEMV
     if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM>, (int)fg_smem(FG_NORM, H->C))) return rc0;
     DC_CUDA(ctx, launch_fused(H, FG_NORM, H->xlap, H->C, H->nrmF, nullptr, H->lm, 0, H->logits1, nullptr, nullptr));

@@ -233,8 +233,27 @@ class Stage:
 
     def set_row_fusion(self, on: bool) -> None:
         """Decode rows with the norm / SwiGLU / row quantisation fused into their
-        GEMVs (default) or as separate kernels; the results are identical."""
+        GEMVs, or as separate kernels (default); the results are identical."""
         self._check(self.L.dc_stage_set_row_fusion(self.h, 1 if on else 0), "set_row_fusion")
+
+    def set_timeline(self, buf=None, per_lap: int = 0, laps: int = 0) -> None:
+        """Stamp %globaltimer after every launch of each decode lap this (head)
+        stage runs through decode_many, into buf (device int64, laps x per_lap);
+        set_timeline() turns it off.  A measurement aid: each stamp adds a
+        one-thread launch to the lap."""
+        self._check(self.L.dc_stage_set_timeline(self.h, _ptr(buf) if buf is not None else None,
+                                                 per_lap if buf is not None else 0,
+                                                 laps if buf is not None else 0), "stage_set_timeline")
+
+    def timeline_info(self):
+        """(kinds, bytes) of the stamps of one lap: for stamp i, the kind of the
+        launch it closes (1 one-row GEMV, 3 tcgen05 GEMM, 0 other) and that
+        GEMM's algorithmic bytes."""
+        n = self.L.dc_stage_timeline_info(self.h, None, None, 0)
+        kinds = (C.c_int * max(n, 1))()
+        by = (C.c_double * max(n, 1))()
+        self.L.dc_stage_timeline_info(self.h, kinds, by, n)
+        return list(kinds)[:n], list(by)[:n]
 
     def kv_len(self) -> int:
         return self.L.dc_stage_kv_len(self.h)

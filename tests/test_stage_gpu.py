@@ -154,6 +154,41 @@ def test_decode_loop_modes_agree(comp, O, P, fixture):
     assert P.infer.generate_chunked(st, prompt, 12, 5, use_device_loop=False) == ref
 
 
+def test_decode_timeline_stamps_every_lap(comp, O, P, fixture):
+    """dc_stage_set_timeline: the stamped decode (graph replays) still equals
+    the oracle; every lap within the buffer has all its stamps, in time order;
+    laps past the buffer write nothing; one stamp per lap closes each GEMV (six
+    layers x four projections, and the lm_head), tagged with its bytes."""
+    import torch
+    ospec, spec, w, om = fixture
+    prompt = [9, 8, 7, 6, 5, 4, 3, 2, 1, 0, 11, 12, 13]
+    ref = O.generate_chunked(om, [(0, 6)], prompt, 12, 5)
+    laps, per = 8, 256
+    for splits in ([6], [0, 3, 3]):
+        st = make_stages(P, comp, spec, w, splits)
+        buf = torch.zeros(laps * per + 64, dtype=torch.int64, device="cuda")
+        st[0].set_timeline(buf[:laps * per], per, laps)
+        got = P.infer.generate_chunked(st, prompt, 12, 5)
+        comp.sync()
+        kinds, by = st[0].timeline_info()
+        st[0].set_timeline()
+        assert got == ref, splits
+        n = len(kinds)
+        assert 25 < n <= per
+        assert kinds.count(1) == 6 * 4 + 1
+        assert all(b > 0 for k, b in zip(kinds, by) if k == 1)
+        t = buf.cpu().numpy()
+        lapt = t[:laps * per].reshape(laps, per)
+        assert (lapt[:, :n] > 0).all()
+        assert (np.diff(lapt[:, :n].astype(np.int64), axis=1) >= 0).all()
+        assert (lapt[:, n:] == 0).all() and (t[laps * per:] == 0).all()
+        # and off again: the next generation runs (and replays) without stamps
+        buf.zero_()
+        assert P.infer.generate_chunked(st, prompt, 12, 5) == ref
+        comp.sync()
+        assert int(buf.abs().sum()) == 0
+
+
 def test_kv_cache_contents_match_oracle(comp, O, P, fixture):
     ospec, spec, w, om = fixture
     ids = [1, 2, 3, 4, 5]
