@@ -18,6 +18,7 @@
 #include <algorithm>
 
 #include "dc_internal.cuh"
+#include "dc_math.cuh"
 #include "dc_ptx.cuh"
 
 namespace {
@@ -156,7 +157,13 @@ __global__ void k_l2_prefetch(const int8_t* __restrict__ p, size_t bytes) {
 // reads the same row) are issued back to back, then consumed by dp4a.  No
 // shared memory, no prologue: a CTA starts pulling weights at its first
 // instruction, and 4-warp CTAs at 4 per SM keep ~128 KB of loads in flight on
-// each SM.  Grid-stride over row pairs; the epilogue is dc_store_out.
+// each SM.  Grid-stride over row pairs; the epilogue is dc_store_out, or with
+// DC_F_SWIGLU (interleaved gate/up rows: a warp's pair is gate_j, up_j) the
+// SwiGLU of the pair's two f32 epilogue values, stored at j, with the CTA's
+// |h| maximum folded into *rowmax by one atomic per CTA.  The SwiGLU (a chain
+// of double-precision exp and division) is deferred: lane t % 32 keeps the
+// accumulators of the warp's t-th pair, and every 32 pairs (and at the end)
+// the lanes evaluate theirs side by side, off the weight stream's path.
 constexpr int GV_SEG = 8;
 // X and rs are written by the kernel before this one on the stream: they carry
 // no __restrict__, so that no load of them is moved above griddepcontrol.wait.
@@ -164,17 +171,33 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
                                                      int ldw, const float* rs,
                                                      const float* __restrict__ cs, int k, int n, unsigned flags,
                                                      const int8_t* __restrict__ requant,
-                                                     const int8_t* __restrict__ relu, void* out) {
+                                                     const int8_t* __restrict__ relu, void* out,
+                                                     uint32_t* rowmax, int* status) {
   // the next kernel (launched as a programmatic dependent) may be scheduled
   // now; it waits for this grid's completion before reading its output
   asm volatile("griddepcontrol.launch_dependents;");
+  __shared__ float wmax[4];
+  // (DC_F_SWIGLU) the pair this lane keeps, and its |h| maximum
+  int sa0 = 0, sa1 = 0, sj = -1;
+  float sc0 = 0.0f, sc1 = 0.0f, hmax = 0.0f;
+  auto swiglu_flush = [&]() {
+    if (sj >= 0) {
+      const float r0 = rs[0];
+      const float h = dcm::swiglu_f32(dc_epi(sa0, r0, sc0), dc_epi(sa1, r0, sc1));
+      ((float*)out)[sj] = h;
+      if (!isfinite(h)) atomicOr(status, DC_ST_NONFINITE);
+      hmax = fmaxf(hmax, fabsf(h));
+      sj = -1;
+    }
+  };
+  int t = 0;  // pairs this warp has taken
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * 4 + (threadIdx.x >> 5), nw = gridDim.x * 4;
   const int nch = (k + 15) >> 4;
   const int4* X4 = (const int4*)X;
   const uint64_t pol = dcp::l2_evict_first();
   bool waited = false;
-  for (int j0 = gw * 2; j0 < n; j0 += nw * 2) {
+  for (int j0 = gw * 2; j0 < n; j0 += nw * 2, t++) {
     const int j1 = min(j0 + 1, n - 1);
     const int4* w0 = (const int4*)(Wt + (int64_t)j0 * ldw);
     const int4* w1 = (const int4*)(Wt + (int64_t)j1 * ldw);
@@ -232,10 +255,31 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
       a0 += __shfl_xor_sync(0xffffffffu, a0, o);
       a1 += __shfl_xor_sync(0xffffffffu, a1, o);
     }
-    if (lane == 0) dc_store_out(out, j0, a0, rs[0], csv, flags, requant, relu);
-    if (lane == 1 && j0 + 1 < n) dc_store_out(out, j0 + 1, a1, rs[0], csv, flags, requant, relu);
+    if (flags & DC_F_SWIGLU) {
+      const float c0 = __shfl_sync(0xffffffffu, csv, 0), c1 = __shfl_sync(0xffffffffu, csv, 1);
+      if (lane == (t & 31)) {
+        sa0 = a0;
+        sa1 = a1;
+        sc0 = c0;
+        sc1 = c1;
+        sj = j0 >> 1;
+      }
+      if ((t & 31) == 31) swiglu_flush();
+    } else {
+      if (lane == 0) dc_store_out(out, j0, a0, rs[0], csv, flags, requant, relu);
+      if (lane == 1 && j0 + 1 < n) dc_store_out(out, j0 + 1, a1, rs[0], csv, flags, requant, relu);
+    }
   }
   if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (flags & DC_F_SWIGLU) {
+    swiglu_flush();
+#pragma unroll
+    for (int o = 16; o; o >>= 1) hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, o));
+    if (lane == 0) wmax[threadIdx.x >> 5] = hmax;
+    __syncthreads();
+    if (threadIdx.x == 0)
+      atomicMax(rowmax, __float_as_uint(fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]))));
+  }
 }
 
 // ---- bulk-staged GEMV: M <= MR rows, the decode path -----------------------
@@ -520,7 +564,8 @@ int launch_gemv_bulk(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, i
 // programmatic dependent: the CTAs may start, and issue their weight loads,
 // while the previous kernel on the stream finishes.
 static int launch_gemv_row(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wt, int ldw, const float* rs,
-                           const float* cs, int k, int n, unsigned flags, void* out, cudaStream_t st) {
+                           const float* cs, int k, int n, unsigned flags, void* out, cudaStream_t st,
+                           uint32_t* rowmax = nullptr) {
   if (int rc = dc_set_smem(ctx, (const void*)k_gemv_row, 0)) return rc;
   const int pairs = (n + 1) / 2;
   const int blocks = std::max(1, std::min((pairs + 3) / 4, ctx->sm_count * 4));
@@ -535,7 +580,7 @@ static int launch_gemv_row(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wt, int 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_gemv_row, Xq, Wt, ldw, rs, cs, k, n, flags, (const int8_t*)ctx->d_requant,
-                                  (const int8_t*)ctx->d_relu, out));
+                                  (const int8_t*)ctx->d_relu, out, rowmax, ctx->d_status));
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;
@@ -626,29 +671,45 @@ static cudaEvent_t timing_event(dc_ctx* ctx) {
 
 // With timing on (dc_timing), every GEMM launch is bracketed by CUDA events on
 // its own stream and its algorithmic bytes and ops are recorded.
-int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
-                     const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
-                     int kind) {
-  if (m == 0 || n == 0 || batch == 0) return DC_OK;
+// One GEMM's launches with its accounting: the timeline tag (kind, algorithmic
+// bytes) and, with timing on, CUDA events around it on its stream.
+template <typename F>
+static int accounted(dc_ctx* ctx, int kind, double bytes, double ops, cudaStream_t st, F&& launch) {
   if (!ctx->timing) {
-    const int rc = gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind);
-    const double ob = (flags & DC_ACC) ? 4 : (flags & DC_REQUANT) ? 1 : 4;
-    dc_timeline_tag(ctx, (kind == 0) ? (m <= 8 ? 1 : 3) : kind,
-                    (double)batch * ((double)m * k + (double)k * n + 4.0 * m + 4.0 * n + ob * m * n));
+    const int rc = launch();
+    dc_timeline_tag(ctx, kind, bytes);
     return rc;
   }
   dc_timed t;
   t.a = timing_event(ctx);
   t.b = timing_event(ctx);
-  t.kind = (kind == 0) ? (m <= 8 ? 1 : 3) : kind;
-  const double ob = (flags & DC_ACC) ? 4 : (flags & DC_REQUANT) ? 1 : 4;
-  t.bytes = (double)batch * ((double)m * k + (double)k * n + 4.0 * m + 4.0 * n + ob * m * n);
-  t.ops = 2.0 * batch * (double)m * n * k;
+  t.kind = kind;
+  t.bytes = bytes;
+  t.ops = ops;
   if (t.a) cudaEventRecord(t.a, st);
-  int rc = gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind);
+  const int rc = launch();
   if (t.b) cudaEventRecord(t.b, st);
   if (t.a && t.b) ctx->timed.push_back(t);
   return rc;
+}
+
+int dc_gemm_dispatch(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
+                     const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
+                     int kind) {
+  if (m == 0 || n == 0 || batch == 0) return DC_OK;
+  const double ob = (flags & DC_ACC) ? 4 : (flags & DC_REQUANT) ? 1 : 4;
+  const double bytes = (double)batch * ((double)m * k + (double)k * n + 4.0 * m + 4.0 * n + ob * m * n);
+  return accounted(ctx, (kind == 0) ? (m <= 8 ? 1 : 3) : kind, bytes, 2.0 * batch * (double)m * n * k, st,
+                   [&] { return gemm_dispatch_impl(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, kind); });
+}
+
+int dc_gemv_swiglu(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+                   int k, int n2, float* hout, uint32_t* rowmax, cudaStream_t st) {
+  if (n2 < 2 || (n2 & 1) || !rowmax || (((uintptr_t)Wt | (uintptr_t)Xq) & 15) || (ldw & 15)) return DC_E_INVAL;
+  if (k > DC_MAX_INT32_K) return dc_fail(ctx, DC_E_ACCBOUND, "gemv_swiglu: k=%d", k);
+  const double bytes = (double)k + (double)k * n2 + 4.0 + 4.0 * n2 + 4.0 * (n2 / 2);
+  return accounted(ctx, 1, bytes, 2.0 * (double)n2 * k, st,
+                   [&] { return launch_gemv_row(ctx, Xq, Wt, ldw, rs, cs, k, n2, DC_F_SWIGLU, hout, st, rowmax); });
 }
 
 extern "C" int dc_timing(dc_ctx* ctx, int on) {

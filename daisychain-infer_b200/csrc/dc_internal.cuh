@@ -12,6 +12,10 @@
 // Internal GEMM flag (beside the public DC_RELU / DC_ACC / DC_REQUANT): add the
 // f32 epilogue value to what `out` already holds (the residual connection).
 #define DC_F_ADDTO 0x100u
+// Internal: the one-row GEMV over interleaved gate/up weight rows (gate_j at
+// row 2j, up_j at 2j + 1) stores h_j = f32(silu(g_j) * u_j) instead of the two
+// outputs, and folds |h_j| into a row maximum (dc_gemv_swiglu).
+#define DC_F_SWIGLU 0x200u
 
 // Device status word bits (atomicOr'd by kernels, read and cleared by dc_sync).
 #define DC_ST_NONFINITE 1
@@ -132,6 +136,12 @@ int dc_gemm_tc(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw
 int dc_gemm_tc_with(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,
                     const float* cs, int m, int k, int n, int batch, unsigned flags, void* out, cudaStream_t st,
                     int32_t* partial, int* counters, size_t partial_cap, size_t counter_cap, int clear);
+// The decode row's gate/up GEMV with SwiGLU in its epilogue: Wt holds n2 = 2I
+// interleaved rows (gate_j, up_j); hout (I floats) = f32(silu(g_j) * u_j) of
+// the f32 epilogue values; |hout| folded into *rowmax (zeroed by an earlier
+// kernel).  DC_E_INVAL when the operands do not suit the one-row GEMV.
+int dc_gemv_swiglu(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wt, int ldw, const float* rs, const float* cs,
+                   int k, int n2, float* hout, uint32_t* rowmax, cudaStream_t st);
 // dc_gemm_dispatch without the timing events: kind 1 GEMV (m <= 8), 2 SIMT dp4a,
 // 3 tcgen05 (falls back to 2 for shapes it does not take), 0 by m.
 int dc_gemm_untimed(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, int ldw, const float* rs,

@@ -75,4 +75,13 @@ __device__ inline double fdlibm_exp(double x) {
   return __dmul_rn(__longlong_as_double(by + (long long)(k + 1000) * 4503599627370496LL), twom1000);
 }
 
+
+// infer.js:59 + :212: f32(silu(g) * u) with silu(v) = v / (1 + exp(-v)) in
+// double and the exp above.
+__device__ __forceinline__ float swiglu_f32(float gf, float uf) {
+  const double v = gf;
+  const double sl = __ddiv_rn(v, __dadd_rn(1.0, fdlibm_exp(-v)));
+  return __double2float_rn(__dmul_rn(sl, (double)uf));
+}
+
 }  // namespace dcm

@@ -97,6 +97,8 @@ struct dc_stage {
   int* att_done = nullptr;  // decode attention: CTAs finished (kept at zero between launches)
   int8_t* a8g = nullptr;    // chunk attention: probability rows [head][row][ldp] (rows <= 16)
   float* asg = nullptr;     // and their scales [head][row]
+  int8_t* q8d = nullptr;    // decode row: the rotated query heads quantised [head][hd] (k_rope_append)
+  float* qsd = nullptr;     // and their scales [head]
   cudaGraphExec_t lap_exec = nullptr;
   unsigned long long lap_nk = 0;  // kernels in one replay of lap_exec
   float* xrow = nullptr;              // one-row graph: the row, in place
@@ -148,7 +150,7 @@ __device__ __forceinline__ double block_max_d(double v, double* red) {
 
 // max(mx/127, 1e-8) in double (verified_core.js:114, :128).
 __device__ __forceinline__ double quant_scale(float mx) {
-  double sc = dc_ddiv_slow((double)mx, 127.0);  // out of line: once per row
+  double sc = __ddiv_rn((double)mx, 127.0);  // (inline: an out-of-line call is an instruction fetch away)
   return sc > 1e-8 ? sc : 1e-8;
 }
 
@@ -272,7 +274,9 @@ __device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, cons
     }
     const double2 sw = block_sum_d2(part, wpart, redd2);
     const double h = serial_sum_radius(sw.x, sw.y, (C + (int)blockDim.x - 1) / (int)blockDim.x + 10);
-    const double inv_hi = rms_inv(sw.x - h, C, eps), inv_lo = rms_inv(sw.x + h, C, eps);
+    // (both ends inline, so their division and square-root chains overlap)
+    const double inv_hi = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sw.x - h, (double)C), eps)));
+    const double inv_lo = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sw.x + h, (double)C), eps)));
     // Both ends of the bracket in one pass: the value at the lower end is kept
     // (the serial sum's whenever no output is ambiguous), with its |y| maximum.
     bool amb = exact_sum != 0;
@@ -399,6 +403,56 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* x, int C,
                                           redd2, vote);
 }
 
+// quantizeRows of the f32 row x (n values; zero past n up to ldq) by one
+// block with the scale sc (rsc = 1/sc), x read through L2 (another CTA wrote
+// it): each thread's 16 loads are in flight before its first conversion.
+__device__ __forceinline__ void quant_row_block(const float* x, int n, int ldq, double sc, double rsc, int8_t* q) {
+  constexpr int U = 16;
+#pragma unroll 1
+  for (int j0 = threadIdx.x; j0 < ldq; j0 += U * (int)blockDim.x) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + u * (int)blockDim.x;
+      v[u] = j < n ? __ldcg(x + j) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + u * (int)blockDim.x;
+      if (j < ldq) q[j] = j < n ? dc_quant_div((double)v[u], sc, rsc) : (int8_t)0;
+    }
+  }
+}
+
+// quant_row_block with the scale from the row maximum *rowmax (float bits,
+// written by other CTAs): the maximum is loaded together with the row's first
+// values, and thread 0 stores the scale f32(sc) in *s.
+__device__ __forceinline__ void quant_row_block_max(const float* x, int n, int ldq, const uint32_t* rowmax,
+                                                    int8_t* q, float* s) {
+  constexpr int U = 16;
+  const uint32_t mb = __ldcg(rowmax);
+  double sc = 1.0, rsc = 1.0;
+#pragma unroll 1
+  for (int j0 = threadIdx.x, it = 0; j0 < ldq; j0 += U * (int)blockDim.x, it++) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + u * (int)blockDim.x;
+      v[u] = j < n ? __ldcg(x + j) : 0.0f;
+    }
+    if (it == 0) {
+      sc = quant_scale(__uint_as_float(mb));
+      rsc = __drcp_rn(sc);
+      if (threadIdx.x == 0) s[0] = __double2float_rn(sc);
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + u * (int)blockDim.x;
+      if (j < ldq) q[j] = j < n ? dc_quant_div((double)v[u], sc, rsc) : (int8_t)0;
+    }
+  }
+}
+
 // The softmax denominator z (infer.js:100-104: z += e_j in key order, each
 // add rounded) as far as the probabilities a_j = f32(f32(e_j) / z) can tell:
 // an any-order sum and serial_sum_radius bracket the serial z (non-negative
@@ -440,7 +494,8 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
                                                     int8_t* k8, float* ks,
                                                     float* vcache, uint32_t* vmax,
                                                     float* vs, int* vchg,
-                                                    int8_t* v8t, int ldp, int* status) {
+                                                    int8_t* v8t, int ldp, int* status,
+                                                    int8_t* q8, float* qs) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   __shared__ float kr[128];
@@ -487,13 +542,31 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
     if (isq) {
       o[i] = na;
       o[half + i] = nb;
-    } else {
+    }
+    if (!isq || q8) {
       kr[i] = na;
       kr[half + i] = nb;
     }
   }
-  if (isq) return;
+  if (isq && !q8) return;
   __syncthreads();
+  if (isq) {
+    // one decode row: the rotated query head quantised here (quantizeRows of the
+    // head's hd values, the scale kept in double for the quotients), so the
+    // attention reads it ready (infer.js:177-180)
+    float mx = 0.0f;
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+      const float v = kr[c];
+      bad |= !isfinite(v);
+      mx = fmaxf(mx, fabsf(v));
+    }
+    mx = block_max_f(mx, red);
+    const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
+    if (threadIdx.x == 0) qs[hh] = __double2float_rn(qsc);
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) q8[hh * hd + c] = dc_quant_div((double)kr[c], qsc, rqsc);
+    if (bad) atomicOr(status, DC_ST_NONFINITE);
+    return;
+  }
   // the rotated key: absmax over hd, f32 scale (quantizeCols rule), int8 row
   float mx = 0.0f;
   for (int c = threadIdx.x; c < hd; c += blockDim.x) {
@@ -1014,7 +1087,7 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* h, int nqkv,
       rsq[0] = __double2float_rn(sc);
       *done = 0;
     }
-    for (int j = tid; j < ldq; j += 256) xq[j] = j < qDim ? dc_quant_div((double)__ldcg(out + j), sc, rsc) : (int8_t)0;
+    quant_row_block(out, qDim, ldq, sc, rsc, xq);
   }
 }
 
@@ -1064,7 +1137,8 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
                                                        double scale, float* out,
                                                        uint32_t* rowmax, int* done,
                                                        int8_t* xq, int ldq, float* rsq,
-                                                       int* status, const float* vcache, const int* vchg) {
+                                                       int* status, const float* vcache, const int* vchg,
+                                                       const int8_t* q8g, const float* qsg) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   extern __shared__ __align__(16) uint8_t sm[];
@@ -1075,16 +1149,24 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   double* xs = (double*)(sV + (size_t)CH * ldpv);              // ldp doubles: s*scale, then e
   float* af = (float*)(xs + ldp);                              // ldp floats: key scales, then f32(e), then a
   int8_t* a8 = (int8_t*)(af + ldp);                            // ldp bytes
-  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar;
+  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar, sbar;
   __shared__ __align__(16) int8_t q8[256];
   __shared__ float red[32];
   __shared__ double2 redd2[32];  // also the 32 doubles of block_max_d / block_sum_d
   double* redd = reinterpret_cast<double*>(redd2);
   __shared__ int vote[32];
   __shared__ int abort_flag;
-  __shared__ double xd[3];  // published to the cluster: score maximum, sum of e, sum of (N - j) e_j
-  __shared__ float xf;      // probability maximum
-  __shared__ int xi;        // 1: some probability is ambiguous under the bracket of z
+  // The cluster's exchanges: every warp stores its partial result into slot
+  // [rank * 8 + warp] of every CTA of the cluster (remote stores, ordered by
+  // the cluster barrier that follows), and each thread then reduces the S * 8
+  // slots from its own shared memory, in slot order (the same value in every
+  // CTA).
+  __shared__ double x_max[64];    // score maxima
+  __shared__ double2 x_sum[64];   // (sum of e, sum of (N - j) e_j)
+  __shared__ float x_amx[64];     // probability maxima at the lower end of z's bracket
+  __shared__ int x_amb[64];       // 1: some probability is ambiguous under the bracket
+  __shared__ float x_cmax[8];     // the context maxima of this CTA's warps
+  __shared__ float xf;            // (the exact path) this CTA's probability maximum
   __shared__ dco::Smem osm;
   const int S = (int)gridDim.y, r = (int)blockIdx.y;
   const int hq = blockIdx.x, c0 = r * CH;
@@ -1104,6 +1186,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   if (tid == 0) {
     for (int i = 0; i < ATTD_NS; i++) dcp::mbar_init(&full[i], 1);
     dcp::mbar_init(&vbar, 1);
+    dcp::mbar_init(&sbar, 1);
     abort_flag = 0;
     dcp::mbar_fence_init();
   }
@@ -1112,14 +1195,19 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   for (int i = 0; i < ATTD_NS; i++) issued[i] = -1;
   const uint32_t s_old = (uint32_t)((n0 & ~3) * 4);      // key scales below n0, before the wait
   const uint32_t s_all = (uint32_t)(((N + 3) & ~3) * 4);  // all of them
-  auto key_block = [&](int i) {  // lane 0 of warp 0: the CTA's i-th key block into ring slot i
+  // The key scales ride with the first block: the older ones (below n0 & ~3)
+  // when that block is copied before the grid-dependency wait, all of them
+  // otherwise.  The newer ones (this step's key among them) all belong to the
+  // last block, whose owner alone copies them, after the wait, on `sbar`.
+  auto key_block = [&](int i, uint32_t sc_bytes) {  // lane 0 of warp 0: key block i into ring slot i
     issued[i] = i;
     const int b = r + i * S;
     const int kn = min(ATTD_KB, N - b * ATTD_KB);
     const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
-    dcp::mbar_expect_tx(&full[i], bytes + (i == 0 ? s_all : 0u));  // the key scales ride with the first block
+    dcp::mbar_expect_tx(&full[i], bytes + sc_bytes);
     dcp::bulk_load(sK + (size_t)i * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[i]);
   };
+  const bool last_mine = (nb - 1) % S == r;  // this CTA owns the block with position n0
   if (warp == 0) {
     if (lane == 0) dcp::mbar_expect_tx(&vbar, (uint32_t)(CH * ldpN));
     __syncwarp();
@@ -1129,7 +1217,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     if (lane == 0) {
       #pragma unroll 1
       for (int i = 0; i < ATTD_NS && i < nmine; i++)
-        if ((r + i * S + 1) * ATTD_KB <= n0) key_block(i);  // every key of the block is older than n0
+        if ((r + i * S + 1) * ATTD_KB <= n0) key_block(i, i == 0 ? s_old : 0u);  // all its keys older than n0
       // the older key scales, once the first block's barrier expects them
       if (issued[0] >= 0 && s_old) dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_old, &full[0]);
     }
@@ -1139,25 +1227,20 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   if (warp == 0 && lane == 0 && nmine > 0) {
     #pragma unroll 1
     for (int i = 0; i < ATTD_NS && i < nmine; i++)
-      if (issued[i] < 0) key_block(i);
-    const uint32_t from = scales_early ? s_old : 0u;
-    dcp::bulk_load(af + (from >> 2), ks + (int64_t)g * max_pos + (from >> 2), s_all - from, &full[0]);
+      if (issued[i] < 0) key_block(i, i == 0 ? s_all : 0u);
+    if (!scales_early) {
+      dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_all, &full[0]);
+    } else if (last_mine && s_all > s_old) {
+      dcp::mbar_expect_tx(&sbar, s_all - s_old);
+      dcp::bulk_load(af + (s_old >> 2), ks + (int64_t)g * max_pos + (s_old >> 2), s_all - s_old, &sbar);
+    }
   }
-  // 1. the query row, quantised
-  const float* qrow = h + hq * hd;
-  float mx = 0.0f;
+  const bool late_scales = nmine > 0 && scales_early && last_mine && s_all > s_old;
+  // 1. the query row, quantised by k_rope_append (its non-finite check too)
+  (void)h;
   bool bad = false;
-  #pragma unroll 1
-  for (int c = tid; c < hd; c += 256) {
-    const float v = qrow[c];
-    bad |= !isfinite(v);
-    mx = fmaxf(mx, fabsf(v));
-  }
-  mx = block_max_f(mx, red);
-  const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
-  const float qs = __double2float_rn(qsc);
-  #pragma unroll 1
-  for (int c = tid; c < hd; c += 256) q8[c] = dc_quant_div((double)qrow[c], qsc, rqsc);
+  if (tid < (hd >> 4)) ((int4*)q8)[tid] = ((const int4*)(q8g + hq * hd))[tid];
+  const float qs = qsg[hq];
   __syncthreads();
   // 2. scores of this CTA's key blocks (one key per thread)
   const int nchk = hd >> 4;
@@ -1166,6 +1249,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
     const int slot = i % ATTD_NS, b = r + i * S;
     if (!dcp::mbar_wait(&full[slot], (uint32_t)(i / ATTD_NS) & 1u, status)) abort_flag = 1;
+    if (late_scales && b == nb - 1 && !dcp::mbar_wait(&sbar, 0, status)) abort_flag = 1;
     __syncthreads();
     if (abort_flag) break;
     const int kb = b * ATTD_KB, kn = min(ATTD_KB, N - kb);
@@ -1193,16 +1277,18 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     }
   }
   // 3. the exact maximum over the cluster
-  m = block_max_d(m, redd);
-  if (tid == 0) xd[0] = m;
+  for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane < S) *cl.map_shared_rank(&x_max[r * 8 + warp], lane) = m;
   cl.sync();
   m = -INFINITY;
-#pragma unroll
-  for (int q = 0; q < 8; q++)  // S <= 8: every remote load in flight at once
-    if (q < S) m = fmax(m, *cl.map_shared_rank(&xd[0], q));
+#pragma unroll 8
+  for (int i = 0; i < S * 8; i++) m = fmax(m, x_max[i]);
   // 4. e_j of this CTA's keys; the cluster's any-order sum brackets z
   double part = 0.0, wpart = 0.0;
-  _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
+  // (the loops over this CTA's keys are unrolled: a thread's keys are independent
+  // chains of double-precision work, so their latencies overlap)
+#pragma unroll 4
+  for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < N) {
       const double e = dcm::fdlibm_exp(__dsub_rn(xs[j], m));
@@ -1212,29 +1298,28 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       wpart += (double)(N - j) * e;
     }
   }
-  {
-    const double2 pw = block_sum_d2(part, wpart, redd2);
-    if (tid == 0) {
-      xd[1] = pw.x;
-      xd[2] = pw.y;
-    }
+  for (int o = 16; o; o >>= 1) {
+    part += __shfl_xor_sync(0xffffffffu, part, o);
+    wpart += __shfl_xor_sync(0xffffffffu, wpart, o);
   }
+  if (lane < S) *cl.map_shared_rank(&x_sum[r * 8 + warp], lane) = make_double2(part, wpart);
   cl.sync();
   double zp = 0.0, zw = 0.0;
-#pragma unroll
-  for (int q = 0; q < 8; q++) {
-    if (q < S) {
-      zp += *cl.map_shared_rank(&xd[1], q);
-      zw += *cl.map_shared_rank(&xd[2], q);
-    }
+#pragma unroll 8
+  for (int i = 0; i < S * 8; i++) {
+    const double2 v = x_sum[i];
+    zp += v.x;
+    zw += v.y;
   }
-  // a term passes through at most nmine + 10 adds in its CTA and S - 1 across the cluster
-  const double zr = serial_sum_radius(zp, zw, (N + ATTD_KB - 1) / ATTD_KB + 24);
+  // a term passes through at most nmine adds in its thread, 5 in its warp and
+  // S * 8 - 1 <= 63 over the warps of the cluster
+  const double zr = serial_sum_radius(zp, zw, (N + ATTD_KB - 1) / ATTD_KB + 72);
   const double zlo = zp - zr, zhi = zp + zr;
   const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
   bool amb = false;
   float amx = 0.0f;
-  _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
+#pragma unroll 4
+  for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < N) {
       const float alo = dc_div_to_f32((double)af[j], zhi, rhi), ahi = dc_div_to_f32((double)af[j], zlo, rlo);
@@ -1243,46 +1328,55 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     }
   }
   {
-    const bool wamb = __any_sync(0xffffffffu, amb);
-    if (lane == 0) vote[warp] = wamb ? 1 : 0;
-    amx = block_max_f(amx, red);  // (its barriers also publish the votes)
-    int any = 0;
-    for (int w = 0; w < 8; w++) any |= vote[w];
-    if (tid == 0) {
-      xi = any;
-      xf = amx;
+    const int wamb = __any_sync(0xffffffffu, amb) ? 1 : 0;
+    for (int o = 16; o; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
+    if (lane < S) {
+      *cl.map_shared_rank(&x_amb[r * 8 + warp], lane) = wamb;
+      *cl.map_shared_rank(&x_amx[r * 8 + warp], lane) = amx;
     }
   }
   cl.sync();
   int any_amb = 0;
-#pragma unroll
-  for (int q = 0; q < 8; q++)
-    if (q < S) any_amb |= *cl.map_shared_rank(&xi, q);
-  const double z = any_amb ? dcl_exact_z(xs, af, N, S, r, nmine, osm, red, &xf) : zlo;
-  cl.sync();
   amx = 0.0f;
+#pragma unroll 8
+  for (int i = 0; i < S * 8; i++) {
+    any_amb |= x_amb[i];
+    amx = fmaxf(amx, x_amx[i]);
+  }
+  // the rare exact path: every CTA publishes its maximum under the serial z
+  const double z = any_amb ? dcl_exact_z(xs, af, N, S, r, nmine, osm, red, &xf) : zlo;
+  if (any_amb) {
+    cl.sync();
+    amx = 0.0f;
 #pragma unroll
-  for (int q = 0; q < 8; q++)
-    if (q < S) amx = fmaxf(amx, *cl.map_shared_rank(&xf, q));
+    for (int q = 0; q < 8; q++)
+      if (q < S) amx = fmaxf(amx, *cl.map_shared_rank(&xf, q));
+  }
   // 6-7. a_j = f32(f32(e_j) / z) of this CTA's keys, quantised with the row's scale
   const double asc = quant_scale(amx), rasc = __drcp_rn(asc);
   const float as = __double2float_rn(asc);
   {
     const double rz = __drcp_rn(z);
-    _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
+#pragma unroll 4
+    for (int i = 0; i < nmine; i++) {
       const int kb = (r + i * S) * ATTD_KB;
       const int j = kb + tid;
       if (j < ldpN) a8[j] = j < N ? dc_quant_div((double)dc_div_to_f32((double)af[j], z, rz), asc, rasc) : (int8_t)0;
     }
   }
-  cl.sync();
-  // the other CTAs' probability bytes, 16 at a time
+  __syncthreads();
+  // this CTA's probability bytes to the other CTAs, 16 at a time (remote
+  // stores, ordered by the barrier below); no CTA touches another's shared
+  // memory after it, so none has to wait for the others before it exits
   #pragma unroll 1
   for (int q16 = tid; q16 < (ldpN >> 4); q16 += 256) {
-    const int owner = ((q16 << 4) / ATTD_KB) % S;
-    if (owner != r) ((int4*)a8)[q16] = *cl.map_shared_rank(&((int4*)a8)[q16], owner);
+    if (((q16 << 4) / ATTD_KB) % S != r) continue;
+    const int4 v = ((const int4*)a8)[q16];
+#pragma unroll 1
+    for (int p = 0; p < S; p++)
+      if (p != r) *cl.map_shared_rank(&((int4*)a8)[q16], p) = v;
   }
-  __syncthreads();
+  cl.sync();
   // 8. the context of this CTA's CH channels over all keys
   const bool vok = dcp::mbar_wait(&vbar, 0, status);
   if (!vok) abort_flag = 1;
@@ -1318,6 +1412,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     for (int c = tid; c < CH; c += 256) sV[(size_t)c * ldpv + n0] = v8t[((int64_t)g * hd + c0 + c) * ldp + n0];
     __syncthreads();
   }
+  float cmx = 0.0f;  // this thread's |context| maximum
   if (!abort_flag) {
     const int nch = ldpN >> 4;
     const int4* a4 = (const int4*)a8;
@@ -1339,17 +1434,28 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
         const float o = dc_epi(acc, as, vs[g * hd + c]);
         out[hq * hd + c] = o;
         bad |= !isfinite(o);
-        atomicMax(rowmax, __float_as_uint(fabsf(o)));
+        cmx = fmaxf(cmx, fabsf(o));
       }
     }
   }
   if (abort_flag && tid == 0) {
     dcp::mbar_wait(&vbar, 0, status);
+    if (late_scales) dcp::mbar_wait(&sbar, 0, status);
     for (int sl = 0; sl < ATTD_NS; sl++)
       if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] / ATTD_NS) & 1u, status);
   }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
-  cl.sync();  // no CTA leaves while another may still read its shared memory
+  // one |context| maximum per CTA into the row maximum
+  for (int o = 16; o; o >>= 1) cmx = fmaxf(cmx, __shfl_xor_sync(0xffffffffu, cmx, o));
+  if (lane == 0) x_cmax[warp] = cmx;
+  __syncthreads();
+  if (tid == 0) {
+    float v = x_cmax[0];
+    for (int w = 1; w < 8; w++) v = fmaxf(v, x_cmax[w]);
+    atomicMax(rowmax, __float_as_uint(v));
+  }
+  // the last CTA to finish quantises the whole context row (quantizeRows) for
+  // the O projection, then re-arms the counter
   __shared__ int is_last;
   __threadfence();
   __syncthreads();
@@ -1357,23 +1463,13 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   __syncthreads();
   if (is_last) {
     __threadfence();
-    const double sc = quant_scale(__uint_as_float(__ldcg(rowmax))), rsc = __drcp_rn(sc);
     const int qDim = nH * hd;
-    if (tid == 0) {
-      rsq[0] = __double2float_rn(sc);
-      *done = 0;
-    }
-    for (int j = tid; j < ldq; j += 256) xq[j] = j < qDim ? dc_quant_div((double)__ldcg(out + j), sc, rsc) : (int8_t)0;
+    if (tid == 0) *done = 0;
+    quant_row_block_max(out, qDim, ldq, rowmax, xq, rsq);
   }
 }
 
-// infer.js:59 + :212: f32(silu(g) * u), silu(v) = v / (1 + exp(-v)) in double
-// with the fdlibm exp.
-__device__ __forceinline__ float swiglu_f32(float gf, float uf) {
-  const double v = gf;
-  const double sl = __ddiv_rn(v, __dadd_rn(1.0, dcm::fdlibm_exp(-v)));
-  return __double2float_rn(__dmul_rn(sl, (double)uf));
-}
+using dcm::swiglu_f32;
 
 // SwiGLU, element-parallel over grid (ceil(I/256), rows): hid = f32(silu(g)*u)
 // with silu(v) = v / (1 + exp(-v)) in double, from the fused gate/up GEMM's
@@ -1830,6 +1926,8 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->att_done, 16)) ||
       (rc = st_alloc(S, (void**)&S->xrow, 4 * (size_t)S->C)) ||
       (rc = st_alloc(S, (void**)&S->a8g, (size_t)std::min(S->max_rows, 16) * S->nH * S->ldp)) ||
+      (rc = st_alloc(S, (void**)&S->q8d, (size_t)round_up(S->qDim, 16))) ||
+      (rc = st_alloc(S, (void**)&S->qsd, 4 * (size_t)S->nH)) ||
       (rc = st_alloc(S, (void**)&S->asg, 4 * (size_t)std::min(S->max_rows, 16) * S->nH)) ||
       (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
     return fail(rc);
@@ -2182,18 +2280,20 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
     }
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
+    // the decode row's cluster attention: it takes the query heads quantised by
+    // k_rope_append and re-quantises moved value channels itself
+    const bool dcl = T == 1 && use_kv && dec_ch && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8;
     const int vblocks = (S->kvDim + 63) / 64;
     DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
                             S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
-                            kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status));
+                            kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status,
+                            dcl ? S->q8d : nullptr, S->qsd));
     dc_count_launch();
     if (T > 1) {
       DC_CUDA(ctx, launch_dep(k_vscale, dim3((S->kvDim + 127) / 128), dim3(128), 0, st, kv.vmax, kv.vs, kv.vchg,
                               S->kvDim, n0p));
       dc_count_launch();
     }
-    // the decode row's cluster attention re-quantises moved value channels itself
-    const bool dcl = T == 1 && use_kv && dec_ch && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8;
     if (dcl) {
     } else if (T <= 8) {
       DC_CUDA(ctx, launch_dep(k_vquant_dev, dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), dim3(256), 0, st,
@@ -2222,7 +2322,8 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_attention_dcl, (const float*)S->hbuf, S->nqkv, S->nH, S->nKV, S->hd,
                                       (const int8_t*)kv.k8, (const float*)kv.ks, kv.v8t, (const float*)kv.vs, n0p,
                                       S->max_pos, S->ldp, dec_ch, scale, S->ctxo, S->rowmax, S->att_done, S->xq,
-                                      S->ldQ, S->rs, ctx->d_status, (const float*)kv.v, (const int*)kv.vchg));
+                                      S->ldQ, S->rs, ctx->d_status, (const float*)kv.v, (const int*)kv.vchg,
+                                      (const int8_t*)S->q8d, (const float*)S->qsd));
       dc_count_launch();
     } else if (T == 1 && use_kv && dec_ch) {
       DC_CUDA(ctx, launch_dep(k_attention_dec, dim3(S->nH, S->hd / dec_ch), dim3(256), dec_smem, st, S->hbuf, S->nqkv,
@@ -2262,10 +2363,19 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     DC_CUDA(ctx, launch_dep(norm_k, dim3(T), dim3(norm_nt), nrm_smem, st, x, S->C, ly.nrm2,
                             S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
     dc_count_launch();
-    if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
-    DC_CUDA(ctx, launch_dep(k_swiglu, dim3((S->I + 255) / 256, T), dim3(256), 0, st, S->hbuf, S->I, S->hmid, S->rowmax,
-                            ctx->d_status));
-    dc_count_launch();
+    // a decode row: SwiGLU in the gate/up GEMV's epilogue (the interleaved rows
+    // gate_j, up_j are one warp's pair); otherwise its own kernel
+    int swg = DC_E_INVAL;
+    if (T == 1) {
+      swg = dc_gemv_swiglu(ctx, S->xq, ly.gu.qt, ly.gu.ldk, S->rs, ly.gu.cs, ly.gu.k, ly.gu.n, S->hmid, S->rowmax, st);
+      if (swg != DC_OK && swg != DC_E_INVAL) return swg;
+    }
+    if (swg == DC_E_INVAL) {
+      if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
+      DC_CUDA(ctx, launch_dep(k_swiglu, dim3((S->I + 255) / 256, T), dim3(256), 0, st, S->hbuf, S->I, S->hmid,
+                              S->rowmax, ctx->d_status));
+      dc_count_launch();
+    }
     DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldI + 255) / 256, T), dim3(256), 0, st, S->hmid, (int64_t)S->I,
                             S->I, S->rowmax, S->xq, S->ldI, S->rs));
     dc_count_launch();
