@@ -52,11 +52,11 @@ L2_BYTES = 126 * 1024 * 1024
 WORKLOADS = {
     "llama3-8b-chunked": dict(spec=dict(hidden=4096, layers=32, heads=32, kvHeads=8, inter=14336, vocab=128256,
                                         ropeTheta=500000.0, tie=False),
-                              mode="chunked", prompt=2048, new=256, chunk=16, window=2,
+                              mode="chunked", prompt=2048, new=256, chunk=16, window=2, per_pass=16,
                               name="Llama-3-8B-shaped decoder"),
     "tinyllama-chunked": dict(spec=dict(hidden=2048, layers=22, heads=32, kvHeads=4, inter=5632, vocab=32000,
                                         ropeTheta=10000.0, tie=False),
-                              mode="chunked", prompt=512, new=128, chunk=16, window=2,
+                              mode="chunked", prompt=512, new=128, chunk=16, window=2, per_pass=16,
                               name="TinyLlama-1.1B-shaped decoder"),
     "smollm-135m-window": dict(spec=dict(hidden=576, layers=30, heads=9, kvHeads=3, inter=1536, vocab=49152,
                                          ropeTheta=10000.0, tie=True),
@@ -206,8 +206,9 @@ def workload_config(name: str, world: int) -> dict:
     sp = w["spec"]
     n_prompt = 256 if w["prompt"] == "ngram" else w["prompt"]
     plan = shard.plan_stages(sp["layers"], [dict(id=f"gpu{i}", capacity=1.0) for i in range(world)])
-    sched = (f"{n_prompt}-token prompt in chunks of {w['chunk']} ({w['window']} in flight), {w['new']} greedy decode "
-             f"tokens" if w["mode"] == "chunked" else
+    sched = (f"{n_prompt}-token prompt in chunks of {w['chunk']} ({w['window']} passes in flight, "
+             f"{w['per_pass']} chunks per pass over the weights; ids identical to one chunk per pass), "
+             f"{w['new']} greedy decode tokens" if w["mode"] == "chunked" else
              f"full-window lookahead T={w['T']}, {n_prompt}-token prompt, {w['new']} new tokens")
     return dict(workload=name, model=(f"{w['name']}: hidden {sp['hidden']}, {sp['layers']} layers, "
                                       f"{sp['heads']}/{sp['kvHeads']} heads, inter {sp['inter']}, vocab {sp['vocab']}"),
@@ -223,7 +224,7 @@ def build_rank(P, comp, w: dict, rank: int, world: int):
     assert len(plan) == world
     st = plan[rank]
     if w["mode"] == "chunked":
-        max_rows, max_pos = max(w["chunk"], 8), w["prompt"] + w["new"] + 1
+        max_rows, max_pos = max(w["chunk"] * w["per_pass"], 8), w["prompt"] + w["new"] + 1
     else:
         max_rows, max_pos = w["T"], w["T"]
     S = P.infer.Stage(comp, spec, st["lo"], st["hi"], head=(rank == 0), max_rows=max_rows, max_pos=max_pos)
@@ -263,7 +264,8 @@ def bench_model(args, rank, world, peaks):
         if w["mode"] == "chunked":
             e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             e0.record()
-            out = ring.generate_chunked(ids, w["new"], w["chunk"], w["window"], on_prefill=e1.record)
+            out = ring.generate_chunked(ids, w["new"], w["chunk"], w["window"], on_prefill=e1.record,
+                                        per_pass=w["per_pass"])
             e2.record()
             marks.setdefault("ev", []).append((e0, e1, e2))
             return out
@@ -322,7 +324,7 @@ def bench_model(args, rank, world, peaks):
     if w["mode"] == "chunked":
         use_graph = getattr(ring, "use_graph", False)
         ring.use_graph = False
-        ring.generate_chunked(ids, 16, w["chunk"], w["window"])
+        ring.generate_chunked(ids, 16, w["chunk"], w["window"], per_pass=w["per_pass"])
         ring.use_graph = use_graph
         ev_scale = w["new"] * args.steps / 16.0
     else:
@@ -330,6 +332,15 @@ def bench_model(args, rank, world, peaks):
         ev_scale = args.steps
     got = read_kinds()
     comp.L.dc_timing(comp.h, 0)
+    pre1 = None
+    if w["mode"] == "chunked" and w["per_pass"] > 1:
+        # for comparison: the same prefill one chunk per pass over the weights
+        pe = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        for _ in range(2):  # (the first run warms the one-chunk path)
+            pe[0].record()
+            ring.generate_chunked(ids, 1, w["chunk"], w["window"], on_prefill=pe[1].record, per_pass=1)
+        comp.sync()
+        pre1 = max_over_ranks([pe[0].elapsed_time(pe[1])], world)[0]
     tc_method = ("CUDA events around every tcgen05 launch of the same prompt's prefill, run right after the timed "
                  "region (launched one by one, as in the timed steps), times the timed steps")
     tl = None
@@ -384,6 +395,7 @@ def bench_model(args, rank, world, peaks):
                     config=workload_config(args.workload, world),
                     prefill_tok_s=(len(ids) / (pre / 1e3)) if w["mode"] == "chunked" else None,
                     prefill_ms=pre if w["mode"] == "chunked" else None, decode_ms=dec,
+                    prefill_tok_s_one_chunk_per_pass=(len(ids) / (pre1 / 1e3)) if pre1 else None,
                     roofline=roof, kernels=other, gpu_launches=launches, clocks=clk, backend=comp.label,
                     generated_ids_fnv=P_fnv(gen_ids), generated_head=gen_ids[:8],
                     weights_gb=weight_bytes(spec, 0, spec.layers, True) / 1e9)
@@ -422,7 +434,8 @@ def decode_timeline(S, ring, ids, w, laps: int = 17, per_lap: int = 2048):
         e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         try:
             e[0].record()
-            ring.generate_chunked(ids, laps, w["chunk"], w["window"], on_prefill=e[1].record)
+            ring.generate_chunked(ids, laps, w["chunk"], w["window"], on_prefill=e[1].record,
+                                  per_pass=w["per_pass"])
             end = torch.cuda.Event(enable_timing=True)
             end.record()
             torch.cuda.synchronize()
@@ -484,7 +497,7 @@ def e2e_model(comp, ring, w, ids, args, world=1):
     for _ in range(steps):
         prompt = host_ids.tolist()
         if w["mode"] == "chunked":
-            picks = ring.generate_chunked(prompt, w["new"], w["chunk"], w["window"])
+            picks = ring.generate_chunked(prompt, w["new"], w["chunk"], w["window"], per_pass=w["per_pass"])
             out = picks.cpu() if picks is not None else None
         else:
             out = ring.generate_lookahead(prompt, w["new"], w["T"], 4)
@@ -834,7 +847,7 @@ def profile_gemm(args):
 
 
 def profile_model(args):
-    """One prefill chunk or one decode lap of the workload, inside an NVTX range
+    """One prefill pass or one decode lap of the workload, inside an NVTX range
     named "profile", for an ncu launch list of exactly that unit of work:
 
         ncu --nvtx --nvtx-include "profile/" --metrics gpu__time_duration.sum ...
@@ -851,14 +864,15 @@ def profile_model(args):
     spec, plan, S, ring = build_rank(P, comp, w, 0, 1)
     ids = prompt_ids(w, spec.vocab)
     chunks = P.shard.prefill_chunks(len(ids), w["chunk"], w["window"])["chunks"]
+    passes = P.shard.chunk_passes(chunks, w["per_pass"])
     S.kv_reset()
     last = None
-    for i, ch in enumerate(chunks):
-        inside = args.profile == "prefill" and i == len(chunks) - 1
+    for i, (lo, hi, rows) in enumerate(passes):
+        inside = args.profile == "prefill" and i == len(passes) - 1
         if inside:
             torch.cuda.synchronize()
             torch.cuda.nvtx.range_push("profile")
-        last = S.run_layers_chunk(S.embed_rows(ids[ch["lo"]:ch["hi"]]), ch["lo"])
+        last = P.infer.run_ring([S], S.embed_rows(ids[lo:hi]), lo, rows)
         if inside:
             torch.cuda.synchronize()
             torch.cuda.nvtx.range_pop()
@@ -871,7 +885,8 @@ def profile_model(args):
     comp.sync()
     S.close()
     return dict(profiled=args.profile, workload=args.workload, prompt=len(ids),
-                unit=("the last prefill chunk (rows %d..%d)" % (chunks[-1]["lo"], chunks[-1]["hi"])
+                unit=("the last prefill pass (rows %d..%d, %d chunks)" % (passes[-1][0], passes[-1][1],
+                                                                         len(passes[-1][2]))
                       if args.profile == "prefill" else "one decode lap at KV length %d" % len(ids)))
 
 
@@ -886,6 +901,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--prompt-len", type=int, default=0, help="override the prompt length (profiling runs)")
     ap.add_argument("--new-tokens", type=int, default=0, help="override the generated tokens (profiling runs)")
+    ap.add_argument("--per-pass", type=int, default=0, help="override the chunks per pass over the weights")
     ap.add_argument("--profile", choices=["prefill", "decode", "gemm"], default=None,
                     help="run one prefill chunk, one decode lap or one sweep GEMM inside an NVTX range 'profile' "
                          "(for ncu); prints no benchmark line")
@@ -899,6 +915,8 @@ def main():
             w["prompt"] = args.prompt_len
         if args.new_tokens:
             w["new"] = args.new_tokens
+        if args.per_pass and w["mode"] == "chunked":
+            w["per_pass"] = args.per_pass
     args.warmup = max(args.warmup, 3)
     peaks = load_peaks()
     if args.profile:

@@ -85,6 +85,7 @@ SIGNATURES = [
     ("dc_stage_synth", _i, [_p, _u64, _d]),
     ("dc_stage_embed", _i, [_p, _p, _i, _p]),
     ("dc_stage_forward", _i, [_p, _p, _i, _i, _i]),
+    ("dc_stage_forward_chunks", _i, [_p, _p, _i, _i, _p, _i]),
     ("dc_stage_set_row_graph", _i, [_p, _i]),
     ("dc_stage_handoff", _i, [_p, _p, _p, _p, _i]),
     ("dc_stage_set_timeline", _i, [_p, _p, _i, _i]),

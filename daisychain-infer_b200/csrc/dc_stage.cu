@@ -95,8 +95,15 @@ struct dc_stage {
   float* logits1 = nullptr; // head: logits of the lap's row
   unsigned long long* amax_keys = nullptr;  // head: greedy-pick keys (8 rows), kept at zero between uses
   int* att_done = nullptr;  // decode attention: CTAs finished (kept at zero between launches)
-  int8_t* a8g = nullptr;    // chunk attention: probability rows [head][row][ldp] (rows <= 16)
+  int8_t* a8g = nullptr;    // chunk attention: probability rows [head][row][ldp] (max_rows rows)
   float* asg = nullptr;     // and their scales [head][row]
+  // a pass of several chunks (dc_stage_forward_chunks): chunk g's value channel
+  // scales, their change flags, and (every chunk but the last, whose values go
+  // to the cache) its int8 values [g][kv head][channel][ldp]
+  float* vsg = nullptr;     // [DC_MAX_CHUNKS][kvDim]
+  int* vchgg = nullptr;     // [DC_MAX_CHUNKS][kvDim]
+  int8_t* v8s = nullptr;    // [max_chunks - 1][kvDim][ldp]
+  int max_chunks = 1;       // chunks one pass may hold (min(max_rows, DC_MAX_CHUNKS))
   int8_t* q8d = nullptr;    // decode row: the rotated query heads quantised [head][hd] (k_rope_append)
   float* qsd = nullptr;     // and their scales [head]
   cudaGraphExec_t lap_exec = nullptr;
@@ -487,7 +494,8 @@ __device__ __forceinline__ double softmax_z(const double* e, const float* af, in
 // the cache at row n0 + t, and the running per-channel |v| maximum.
 // grid (T, nH + nKV + 1), block 64: block y < nH rotates query head y in place;
 // nH <= y < nH + nKV rotates key head y - nH, quantises it and appends it;
-// the last block appends the value row and folds |v| into the channel maxima.
+// the last block appends the value row and folds |v| into the channel maxima
+// (vmax null: only appends).
 __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, int nKV, int hd,
                                                     const float* rc, const float* rsn,
                                                     const int* n0p, int max_pos,
@@ -525,7 +533,7 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
         // the new row's int8 value (channel-major); older rows move only when
         // the channel's scale did (k_vquant_dev)
         v8t[(int64_t)c * ldp + n0] = dc_clamp8(dc_js_round(dc_ddiv_slow((double)v, (double)ns)));
-      } else {
+      } else if (vmax) {  // (a pass of several chunks: k_vscale_chunks folds them per chunk)
         atomicMax(vmax + c, __float_as_uint(fabsf(v)));
       }
     }
@@ -599,15 +607,12 @@ __global__ void k_vscale(const uint32_t* vmax, float* vs, int* vchg,
 
 // int8 V under the channel scales, stored channel-major ([kv head][channel][ldp]
 // so a context dot product streams contiguous bytes): rows >= n0 always, older
-// rows only in channels whose scale moved.  grid (ceil(N/64), ceil(kvDim/32)),
-// block 256 (32 channels x 8 rows); the tile is transposed through shared memory.
-__global__ void __launch_bounds__(256) k_vquant(const float* vcache, const float* vs,
-                                                const int* vchg, int8_t* v8t, int N, int n0,
-                                                int kvDim, int hd, int ldp) {
-  asm volatile("griddepcontrol.launch_dependents;");
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+// rows only in channels whose scale moved.  One tile of 64 rows (from jb) x 32
+// channels (from cb) on 256 threads (32 channels x 8 rows), transposed through
+// shared memory.
+__device__ __forceinline__ void vquant_tile(const float* vcache, const float* vs, const int* vchg, int8_t* v8t,
+                                            int N, int n0, int kvDim, int hd, int ldp, int jb, int cb) {
   __shared__ int8_t tile[32][65];
-  const int cb = blockIdx.y * 32, jb = blockIdx.x * 64;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = cb + tx;
   const bool cval = c < kvDim;
@@ -627,6 +632,79 @@ __global__ void __launch_bounds__(256) k_vquant(const float* vcache, const float
     if (j < n0 && !vchg[cc]) continue;  // an unchanged channel keeps its int8 rows
     const int g = cc / hd, ch = cc - g * hd;
     v8t[((int64_t)g * hd + ch) * ldp + j] = tile[cl][r];
+  }
+}
+
+// grid (ceil(N/64), ceil(kvDim/32)), block 256: vquant_tile over rows 0..N-1.
+__global__ void __launch_bounds__(256) k_vquant(const float* vcache, const float* vs,
+                                                const int* vchg, int8_t* v8t, int N, int n0,
+                                                int kvDim, int hd, int ldp) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  vquant_tile(vcache, vs, vchg, v8t, N, n0, kvDim, hd, ldp, blockIdx.x * 64, blockIdx.y * 32);
+}
+
+// A pass of several consecutive chunks (dc_stage_forward_chunks): G chunks,
+// chunk g holding rows [end[g-1], end[g]) of the pass (end[-1] = 0).
+struct ChunkSet {
+  int G;
+  int end[DC_MAX_CHUNKS];
+};
+
+// The value channel scales as of each chunk's last row (the per-column scales
+// of vh in infer.js:186-196 are taken over the cache as it stands after that
+// chunk's append): per channel, the running |v| maximum folded over the pass's
+// rows one chunk at a time; chunk g's scale and its change flag against the
+// cache's current scale go to vsg/vchgg[g], and the last chunk's become the
+// cache's (vmax, vs, vchg).  grid ceil(kvDim/128), block 128.
+__global__ void __launch_bounds__(128) k_vscale_chunks(const float* vcache, uint32_t* vmax, float* vs, int* vchg,
+                                                       int kvDim, const int* n0p, ChunkSet cks, float* vsg,
+                                                       int* vchgg) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= kvDim) return;
+  const int n0 = *n0p;
+  const int fresh = n0 == 0;
+  const float prior = vs[c];
+  uint32_t m = vmax[c];
+  const float* vc = vcache + (int64_t)n0 * kvDim + c;
+  float ns = prior;
+  int chg = 0;
+  int r = 0;
+  for (int g = 0; g < cks.G; g++) {
+    const int e = cks.end[g];
+#pragma unroll 8
+    for (; r < e; r++) m = max(m, __float_as_uint(fabsf(vc[(int64_t)r * kvDim])));
+    ns = __double2float_rn(quant_scale(__uint_as_float(m)));
+    chg = fresh || ns != prior;
+    vsg[g * kvDim + c] = ns;
+    vchgg[g * kvDim + c] = chg;
+  }
+  vmax[c] = m;
+  vs[c] = ns;
+  vchg[c] = chg;
+}
+
+// The int8 values each chunk of a pass attends with: chunk g < G-1 into the
+// pass buffer v8s[g] (every row up to the chunk's end, under its scales), the
+// last chunk into the cache (its new rows, and older rows in channels whose
+// scale moved), as k_vquant.  grid (ceil(N/64), ceil(kvDim/32), G), block 256.
+__global__ void __launch_bounds__(256) k_vquant_chunks(const float* vcache, const float* vs, const int* vchg,
+                                                       int8_t* v8t, int n0, int kvDim, int hd, int ldp,
+                                                       ChunkSet cks, const float* vsg, int8_t* v8s) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  const int g = blockIdx.z;
+  const int N = n0 + cks.end[g];
+  const int jb = blockIdx.x * 64;
+  if (jb >= N) return;
+  if (g == cks.G - 1) {
+    vquant_tile(vcache, vs, vchg, v8t, N, n0, kvDim, hd, ldp, jb, blockIdx.y * 32);
+  } else {
+    // n0 = 0: every row is written (vchg is then never read)
+    vquant_tile(vcache, vsg + (int64_t)g * kvDim, vchg, v8s + (int64_t)g * kvDim * ldp, N, 0, kvDim, hd, ldp, jb,
+                blockIdx.y * 32);
   }
 }
 
@@ -828,47 +906,62 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* h, in
 }
 
 // The context of a chunk's T rows for 32 channels of one head, from the
-// probability rows k_attention wrote (split form): grid (nH, hd / 32), 256
+// probability rows k_attention wrote (split form): grid (nH, hd / 32, G), 256
 // threads; ctx[t][c] = sum_j a8[t][j] * v8[c][j] (exact int32), verified
 // epilogue with the row's probability scale and the channel's value scale.
-// The 32 value rows and the T probability rows land in shared memory by 1-D
-// bulk copies.  Dynamic shared memory: (32 + T) * ldp.
+// The 32 value rows and the chunk's probability rows land in shared memory by
+// 1-D bulk copies.  Dynamic shared memory: (32 + 16) * ldp.  In a pass of
+// several chunks (cks.G > 1) CTA z forms chunk z's rows (at most 16) with the
+// values and scales of that chunk (v8s/vsg, the cache's for the last chunk).
 __global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* a8g, const float* asg,
                                                   const int8_t* v8t, const float* vs,
                                                   int nH, int nKV, int hd, int T, const int* n0p,
                                                   int ldp, float* out, int qDim,
-                                                  uint32_t* rowmax, int* status) {
+                                                  uint32_t* rowmax, int* status,
+                                                  ChunkSet cks, const int8_t* v8s, const float* vsg) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   extern __shared__ __align__(16) uint8_t sm[];
   int8_t* sV = (int8_t*)sm;              // 32 x ldp
-  int8_t* sA = sV + (size_t)32 * ldp;     // T x ldp
+  int8_t* sA = sV + (size_t)32 * ldp;     // Tc x ldp
   __shared__ __align__(8) uint64_t bar;
   __shared__ float sas[16];
   const int hq = blockIdx.x, c0 = blockIdx.y * 32;
   const int g = hq / (nH / nKV);
   const int tid = threadIdx.x;
-  const int nfill = (*n0p + T + 15) & ~15;  // bytes of each row in use
+  int r0 = 0, r1 = T;  // this CTA's rows
+  if (cks.G > 1) {
+    const int z = blockIdx.z;
+    r0 = z ? cks.end[z - 1] : 0;
+    r1 = cks.end[z];
+    if (z < cks.G - 1) {
+      v8t = v8s + (int64_t)z * nKV * hd * ldp;
+      vs = vsg + (int64_t)z * nKV * hd;
+    }
+  }
+  const int Tc = r1 - r0;
+  const int nfill = (*n0p + r1 + 15) & ~15;  // bytes of each row in use
   if (tid == 0) {
     dcp::mbar_init(&bar, 1);
     dcp::mbar_fence_init();
   }
   __syncthreads();
   if (tid < 32) {
-    if (tid == 0) dcp::mbar_expect_tx(&bar, (uint32_t)((32 + T) * nfill));
+    if (tid == 0) dcp::mbar_expect_tx(&bar, (uint32_t)((32 + Tc) * nfill));
     __syncwarp();
     dcp::bulk_load(sV + (size_t)tid * ldp, v8t + ((int64_t)g * hd + c0 + tid) * ldp, (uint32_t)nfill, &bar);
-    if (tid < T) dcp::bulk_load(sA + (size_t)tid * ldp, a8g + ((int64_t)hq * T + tid) * ldp, (uint32_t)nfill, &bar);
+    if (tid < Tc)
+      dcp::bulk_load(sA + (size_t)tid * ldp, a8g + ((int64_t)hq * T + r0 + tid) * ldp, (uint32_t)nfill, &bar);
   }
-  if (tid < T) sas[tid] = asg[hq * T + tid];
+  if (tid < Tc) sas[tid] = asg[hq * T + r0 + tid];
   const bool ok = dcp::mbar_wait(&bar, 0, status);
   __syncthreads();
   if (!ok) return;
-  const int cl = tid >> 3, tg = tid & 7;  // channel c0 + cl; rows tg and tg + 8
+  const int cl = tid >> 3, tg = tid & 7;  // channel c0 + cl; rows tg and tg + 8 of the chunk
   const int t0 = tg, t1 = tg + 8;
   const int4* vr = (const int4*)(sV + (size_t)cl * ldp);
-  const int4* ar0 = (const int4*)(sA + (size_t)t0 * ldp);
-  const int4* ar1 = (const int4*)(sA + (size_t)(t1 < T ? t1 : t0) * ldp);
+  const int4* ar0 = (const int4*)(sA + (size_t)(t0 < Tc ? t0 : 0) * ldp);
+  const int4* ar1 = (const int4*)(sA + (size_t)(t1 < Tc ? t1 : 0) * ldp);
   int s0 = 0, s1 = 0;
   for (int q = 0; q < (nfill >> 4); q++) {
     const int4 v = vr[q];
@@ -878,17 +971,17 @@ __global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* a8g, const float
   const int c = c0 + cl;
   const float vsc = vs[g * hd + c];
   bool bad = false;
-  if (t0 < T) {
+  if (t0 < Tc) {
     const float o = dc_epi(s0, sas[t0], vsc);
-    out[(int64_t)t0 * qDim + hq * hd + c] = o;
+    out[(int64_t)(r0 + t0) * qDim + hq * hd + c] = o;
     bad |= !isfinite(o);
-    atomicMax(rowmax + t0, __float_as_uint(fabsf(o)));
+    atomicMax(rowmax + r0 + t0, __float_as_uint(fabsf(o)));
   }
-  if (t1 < T) {
+  if (t1 < Tc) {
     const float o = dc_epi(s1, sas[t1], vsc);
-    out[(int64_t)t1 * qDim + hq * hd + c] = o;
+    out[(int64_t)(r0 + t1) * qDim + hq * hd + c] = o;
     bad |= !isfinite(o);
-    atomicMax(rowmax + t1, __float_as_uint(fabsf(o)));
+    atomicMax(rowmax + r0 + t1, __float_as_uint(fabsf(o)));
   }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
@@ -1871,6 +1964,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
   S->hi = hi;
   S->head = head;
   S->max_rows = max_rows;
+  S->max_chunks = std::min(max_rows, DC_MAX_CHUNKS);
   S->max_pos = max_pos;
   S->C = s.hidden;
   S->hd = s.head_dim;
@@ -1925,10 +2019,14 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->amax_keys, 64)) ||
       (rc = st_alloc(S, (void**)&S->att_done, 16)) ||
       (rc = st_alloc(S, (void**)&S->xrow, 4 * (size_t)S->C)) ||
-      (rc = st_alloc(S, (void**)&S->a8g, (size_t)std::min(S->max_rows, 16) * S->nH * S->ldp)) ||
+      (rc = st_alloc(S, (void**)&S->a8g, (size_t)S->max_rows * S->nH * S->ldp)) ||
       (rc = st_alloc(S, (void**)&S->q8d, (size_t)round_up(S->qDim, 16))) ||
       (rc = st_alloc(S, (void**)&S->qsd, 4 * (size_t)S->nH)) ||
-      (rc = st_alloc(S, (void**)&S->asg, 4 * (size_t)std::min(S->max_rows, 16) * S->nH)) ||
+      (rc = st_alloc(S, (void**)&S->asg, 4 * (size_t)S->max_rows * S->nH)) ||
+      (rc = st_alloc(S, (void**)&S->vsg, 4 * (size_t)DC_MAX_CHUNKS * S->kvDim)) ||
+      (rc = st_alloc(S, (void**)&S->vchgg, 4 * (size_t)DC_MAX_CHUNKS * S->kvDim)) ||
+      (S->max_chunks > 1 &&
+       (rc = st_alloc(S, (void**)&S->v8s, (size_t)(S->max_chunks - 1) * S->kvDim * S->ldp))) ||
       (rc = st_alloc(S, (void**)&S->lx, 4 * (size_t)8 * S->C)))
     return fail(rc);
   // RoPE tables (infer.js:71-81), positions 0 .. max_pos-1, with the fdlibm
@@ -2222,8 +2320,17 @@ static cudaError_t launch_fused(dc_stage* S, int mode, const float* x, int K, co
 // full window), so the same launches can be captured once in a CUDA graph and
 // replayed lap after lap.  n0 is the host's copy, used only to size the tiled
 // V quantisation of chunk/window calls (T > 8), which are never captured.
-static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, const int* n0p) {
+// The chunk attention's split form (k_attention, then k_attn_ctx per 32
+// channels) fits this stage's geometry.
+static bool split_ctx_ok(const dc_stage* S) {
+  return S->a8g && S->hd % 32 == 0 && (size_t)(32 + 16) * S->ldp + 1024 <= 232448;
+}
+
+static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, const int* n0p,
+                          const ChunkSet* cks = nullptr) {
   dc_ctx* ctx = S->ctx;
+  const bool multi = cks && cks->G > 1;  // several chunks in this pass (split context path, checked by the caller)
+  const ChunkSet one = {0, {}};
   cudaStream_t st = ctx->stream;
   const int N = n0 + T;
   const double scale = 1.0 / sqrt((double)S->hd);
@@ -2249,7 +2356,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   // chunk rows (T <= 16): probabilities per (head, row), then the context per
   // (head, 32 channels) from shared-memory copies of the value and probability rows
   const size_t ctx_smem = (size_t)(32 + 16) * S->ldp;
-  const bool split_ctx = S->a8g && S->hd % 32 == 0 && ctx_smem + 1024 <= 232448;
+  const bool split_ctx = split_ctx_ok(S);
   if (split_ctx)
     if (int rc0 = dc_set_smem(ctx, (const void*)k_attn_ctx, (int)ctx_smem)) return rc0;
   const size_t nrm_smem = rms_smem(S->C);
@@ -2286,15 +2393,23 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     const int vblocks = (S->kvDim + 63) / 64;
     DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
                             S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
-                            kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status,
+                            multi ? nullptr : kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status,
                             dcl ? S->q8d : nullptr, S->qsd));
     dc_count_launch();
-    if (T > 1) {
+    if (multi) {
+      DC_CUDA(ctx, launch_dep(k_vscale_chunks, dim3((S->kvDim + 127) / 128), dim3(128), 0, st, (const float*)kv.v,
+                              kv.vmax, kv.vs, kv.vchg, S->kvDim, n0p, *cks, S->vsg, S->vchgg));
+      dc_count_launch();
+    } else if (T > 1) {
       DC_CUDA(ctx, launch_dep(k_vscale, dim3((S->kvDim + 127) / 128), dim3(128), 0, st, kv.vmax, kv.vs, kv.vchg,
                               S->kvDim, n0p));
       dc_count_launch();
     }
     if (dcl) {
+    } else if (multi) {
+      DC_CUDA(ctx, launch_dep(k_vquant_chunks, dim3((N + 63) / 64, (S->kvDim + 31) / 32, cks->G), dim3(256), 0, st,
+                              (const float*)kv.v, (const float*)kv.vs, (const int*)kv.vchg, kv.v8t, n0, S->kvDim, S->hd,
+                              S->ldp, *cks, (const float*)S->vsg, S->v8s));
     } else if (T <= 8) {
       DC_CUDA(ctx, launch_dep(k_vquant_dev, dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), dim3(256), 0, st,
                               kv.v, kv.vs, kv.vchg, kv.v8t, T, n0p, S->kvDim, S->hd, S->ldp, T == 1 ? 1 : 0));
@@ -2330,14 +2445,16 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                               S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch,
                               scale, S->ctxo, S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status));
       dc_count_launch();
-    } else if (split_ctx && T <= 16) {
+    } else if (split_ctx && (T <= 16 || multi)) {
       DC_CUDA(ctx, launch_dep(k_attention, dim3(S->nH, T), dim3(ATT_THREADS), att_smem, st, S->hbuf, S->nqkv, S->nH,
                               S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale, S->ctxo,
                               S->rowmax, S->qDim, ctx->d_status, S->a8g, S->asg));
       dc_count_launch();
-      DC_CUDA(ctx, launch_dep(k_attn_ctx, dim3(S->nH, S->hd / 32), dim3(256), ctx_smem, st, S->a8g, S->asg, kv.v8t,
-                              kv.vs, S->nH, S->nKV, S->hd, T, n0p, S->ldp, S->ctxo, S->qDim, S->rowmax,
-                              ctx->d_status));
+      DC_CUDA(ctx, launch_dep(k_attn_ctx, dim3(S->nH, S->hd / 32, multi ? cks->G : 1), dim3(256), ctx_smem, st,
+                              (const int8_t*)S->a8g, (const float*)S->asg, (const int8_t*)kv.v8t,
+                              (const float*)kv.vs, S->nH, S->nKV, S->hd, T, n0p, S->ldp, S->ctxo, S->qDim,
+                              S->rowmax, ctx->d_status, multi ? *cks : one, (const int8_t*)S->v8s,
+                              (const float*)S->vsg));
       dc_count_launch();
       DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldQ + 255) / 256, T), dim3(256), 0, st, S->ctxo,
                               (int64_t)S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ, S->rs));
@@ -2518,6 +2635,48 @@ extern "C" int dc_stage_forward(dc_stage* S, float* x, int T, int pos0, int use_
   int rc = forward_layers(S, x, T, n0, use_kv, n0p);
   if (rc) return rc;
   if (use_kv) S->kv_len = N;
+  return DC_OK;
+}
+
+// runLayersChunk on several consecutive chunks in one pass over the weights
+// (infer.js:288-296 called once per chunk, as generateChunked does, :339-367):
+// every row-wise step is the same at any row count, and the only quantity that
+// depends on where a chunk ends -- the value channel scales its context is
+// formed with (the per-column scales of vh over the cache as it stands after
+// the chunk's append, :154-165, :186-196) -- is computed per chunk
+// (k_vscale_chunks, k_vquant_chunks, k_attn_ctx per chunk).  So the rows and
+// the cache come out bit-identical to one dc_stage_forward per chunk.  Where
+// the split context path does not fit (head_dim not a multiple of 32, or a
+// chunk of more than 16 rows), the chunks run one by one.
+extern "C" int dc_stage_forward_chunks(dc_stage* S, float* x, int T, int pos0, const int* rows, int nchunks) {
+  if (!S || !x || !rows || nchunks < 1 || nchunks > DC_MAX_CHUNKS || T < 1 || T > S->max_rows)
+    return dc_fail(S ? S->ctx : nullptr, DC_E_INVAL, "stage_forward_chunks: bad arguments");
+  dc_ctx* ctx = S->ctx;
+  ChunkSet cks = {nchunks, {}};
+  int sum = 0, widest = 0;
+  for (int g = 0; g < nchunks; g++) {
+    if (rows[g] < 1) return dc_fail(ctx, DC_E_INVAL, "stage_forward_chunks: chunk %d has %d rows", g, rows[g]);
+    sum += rows[g];
+    widest = std::max(widest, rows[g]);
+    cks.end[g] = sum;
+  }
+  if (sum != T) return dc_fail(ctx, DC_E_INVAL, "stage_forward_chunks: chunks hold %d rows, not %d", sum, T);
+  if (nchunks == 1) return dc_stage_forward(S, x, T, pos0, 1);
+  const int n0 = S->kv_len;
+  if (pos0 != n0)
+    return dc_fail(ctx, DC_E_INVAL, "stage_forward_chunks: position %d does not follow the cached %d tokens", pos0, n0);
+  if (n0 + T > S->max_pos)
+    return dc_fail(ctx, DC_E_INVAL, "stage_forward_chunks: %d positions exceed max_pos %d", n0 + T, S->max_pos);
+  if (S->L.empty()) return DC_OK;
+  if (!split_ctx_ok(S) || widest > 16 || nchunks > S->max_chunks) {
+    for (int g = 0, r = 0; g < nchunks; r += rows[g], g++)
+      if (int rc = dc_stage_forward(S, x + (size_t)r * S->C, rows[g], pos0 + r, 1)) return rc;
+    return DC_OK;
+  }
+  k_setpos<<<1, 1, 0, ctx->stream>>>(S->d_pos, n0);
+  dc_count_launch();
+  if (int rc = forward_layers(S, x, T, n0, 1, S->d_pos, &cks)) return rc;
+  S->kv_len = n0 + T;
   return DC_OK;
 }
 

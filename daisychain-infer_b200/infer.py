@@ -173,6 +173,17 @@ class Stage:
         self._check(self.L.dc_stage_forward(self.h, _ptr(x), T, pos0, 1), "runLayersChunk")
         return x
 
+    def run_layers_chunks(self, x, pos0: int, rows) -> "torch.Tensor":
+        """Consecutive chunks (lengths ``rows``) at positions pos0.. in one pass
+        over this stage's weights, appending to the KV cache; bit-identical to
+        run_layers_chunk on each chunk in turn."""
+        T = x.numel() // self.spec.hidden
+        r = np.ascontiguousarray(rows, np.int32)
+        if r.size == 1:
+            return self.run_layers_chunk(x, pos0)
+        self._check(self.L.dc_stage_forward_chunks(self.h, _ptr(x), T, pos0, _ptr(r), r.size), "runLayersChunk")
+        return x
+
     def logits_at(self, x, rows):
         """Greedy picks (host list) and device logits of the given rows."""
         T = x.numel() // self.spec.hidden
@@ -272,11 +283,17 @@ def _sync_check(stages):
     stages[0].comp.sync()
 
 
-def run_ring(stages, x, chunk_pos=None):
-    """One lap through every stage in plan order (the hop is a device buffer)."""
+def run_ring(stages, x, chunk_pos=None, rows=None):
+    """One lap through every stage in plan order (the hop is a device buffer);
+    ``rows`` (chunk lengths) runs several chunks in one pass of each stage."""
     for S in stages:
         if S.hi > S.lo:
-            x = S.run_layers(x) if chunk_pos is None else S.run_layers_chunk(x, chunk_pos)
+            if chunk_pos is None:
+                x = S.run_layers(x)
+            elif rows is not None and len(rows) > 1:
+                x = S.run_layers_chunks(x, chunk_pos, rows)
+            else:
+                x = S.run_layers_chunk(x, chunk_pos)
     return x
 
 
@@ -317,17 +334,20 @@ def generate_lookahead(stages, ids0, n_new: int, T: int, max_draft: int = 4) -> 
 
 
 def generate_chunked(stages, ids0, n_new: int, chunk_size: int, use_device_loop: bool = True,
-                     use_graph: bool = True) -> list:
+                     use_graph: bool = True, per_pass: int = 1) -> list:
     """infer.js:339-367, greedy: chunked prefill on per-stage KV, then one token per lap.
     The decode laps run on the device (dc_decode_run, optionally one CUDA graph
-    replayed per lap); use_device_loop=False runs them from the host instead."""
+    replayed per lap); use_device_loop=False runs them from the host instead.
+    per_pass > 1 runs that many consecutive chunks per pass over the weights
+    (the same ids)."""
     head = stages[0]
     ids = list(ids0)
     for S in stages:
         S.kv_reset()
     last = None
-    for ch in shard.prefill_chunks(len(ids), chunk_size, 1)["chunks"]:
-        last = run_ring(stages, head.embed_rows(ids[ch["lo"]:ch["hi"]]), ch["lo"])
+    chunks = shard.prefill_chunks(len(ids), chunk_size, 1)["chunks"]
+    for lo, hi, rows in shard.chunk_passes(chunks, per_pass):
+        last = run_ring(stages, head.embed_rows(ids[lo:hi]), lo, rows)
     if use_device_loop:
         picks = head.decode_many(stages, last, n_new, use_graph)
         return ids + picks[:n_new].cpu().tolist()

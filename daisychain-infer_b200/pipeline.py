@@ -110,29 +110,37 @@ class Ring:
         return r
 
     # ---- chunked prefill + decode --------------------------------------------------
-    def generate_chunked(self, ids0: list, n_new: int, chunk_size: int = 16, window: int = 2, on_prefill=None):
+    def _run_pass(self, x, lo: int, rows: list):
+        S = self.stage
+        return S.run_layers_chunks(x, lo, rows) if len(rows) > 1 else S.run_layers_chunk(x, lo)
+
+    def generate_chunked(self, ids0: list, n_new: int, chunk_size: int = 16, window: int = 2, on_prefill=None,
+                         per_pass: int = 1):
         """Returns the device tensor of picked ids on the head (n_new int32), None elsewhere.
         ``on_prefill`` (optional) is called on every rank once its prefill part is issued
-        (on the head: when the prefill lap has returned)."""
+        (on the head: when the prefill lap has returned).  ``per_pass`` consecutive
+        chunks travel and run together (one pass over each stage's weights; the
+        same ids); ``window`` counts such passes in flight."""
         S, H = self.stage, self.hidden
         S.kv_reset()
         chunks = shard.prefill_chunks(len(ids0), chunk_size, window)
+        passes = shard.chunk_passes(chunks["chunks"], per_pass)
         last = None
         if self.world == 1:
-            for ch in chunks["chunks"]:
-                last = S.run_layers_chunk(S.embed_rows(ids0[ch["lo"]:ch["hi"]]), ch["lo"])
+            for lo, hi, rows in passes:
+                last = self._run_pass(S.embed_rows(ids0[lo:hi]), lo, rows)
             if on_prefill:
                 on_prefill()
             return self._decode_local(last, len(ids0), n_new)
-        cap = chunks["chunkSize"] * H
+        cap = chunks["chunkSize"] * max(1, int(per_pass)) * H
         if self.rank == 0:
             flights = []
             backs = self._ring("prefill-return", chunks["window"] + 1, cap)
-            for ch in chunks["chunks"]:
-                x = S.run_layers_chunk(S.embed_rows(ids0[ch["lo"]:ch["hi"]]), ch["lo"])
-                sent = self.tp.send(x, self.nxt, token_idx=ch["lo"])  # the handle keeps the send (and x) alive
-                _, back = backs.take((ch["hi"] - ch["lo"]) * H)
-                flights.append((sent, self.tp.recv(back, self.prv, token_idx=ch["lo"]), back))
+            for lo, hi, rows in passes:
+                x = self._run_pass(S.embed_rows(ids0[lo:hi]), lo, rows)
+                sent = self.tp.send(x, self.nxt, token_idx=lo)  # the handle keeps the send (and x) alive
+                _, back = backs.take((hi - lo) * H)
+                flights.append((sent, self.tp.recv(back, self.prv, token_idx=lo), back))
                 if len(flights) >= chunks["window"]:
                     sent_, req, buf = flights.pop(0)
                     sent_.wait()
@@ -148,11 +156,11 @@ class Ring:
             return self._decode_head(last, len(ids0), n_new)
         # a middle or last stage: chunks arrive in order (the inbox of app.js:719-749)
         hops = self._ring("prefill-hop", chunks["window"] + 1, cap)
-        for ch in chunks["chunks"]:
-            i, buf = hops.take((ch["hi"] - ch["lo"]) * H)
-            self.tp.recv(buf, self.prv, token_idx=ch["lo"]).wait()
-            S.run_layers_chunk(buf, ch["lo"])
-            hops.hold(i, self.tp.send(buf, self.nxt, token_idx=ch["lo"]))
+        for lo, hi, rows in passes:
+            i, buf = hops.take((hi - lo) * H)
+            self.tp.recv(buf, self.prv, token_idx=lo).wait()
+            self._run_pass(buf, lo, rows)
+            hops.hold(i, self.tp.send(buf, self.nxt, token_idx=lo))
         if on_prefill:
             on_prefill()
         rows = self._ring("decode-hop", 2, H)

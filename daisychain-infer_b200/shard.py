@@ -59,6 +59,19 @@ def prefill_chunks(n_tokens: int, chunk_size: int, in_flight: int) -> dict:
     return dict(chunks=chunks, window=window, chunkSize=size)
 
 
+def chunk_passes(chunks: list, per_pass: int) -> list:
+    """Consecutive prefillChunks chunks, ``per_pass`` at a time, as the passes
+    a stage runs them in (one pass over its weights each, the same ids as one
+    chunk per pass): [(lo, hi, [chunk lengths])].  Every rank derives the same
+    list from the same chunks."""
+    n = max(1, int(per_pass))
+    out = []
+    for i in range(0, len(chunks), n):
+        g = chunks[i:i + n]
+        out.append((g[0]["lo"], g[-1]["hi"], [c["hi"] - c["lo"] for c in g]))
+    return out
+
+
 def prompt_lookup_draft(ids: list, max_draft: int) -> list:
     cap = max(0, int(max_draft))
     n = len(ids)

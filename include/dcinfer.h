@@ -219,6 +219,18 @@ int dc_stage_embed(dc_stage* stage, const int32_t* ids, int T, float* x);
  * stage's cache, infer.js:288-296); x (device, T x hidden) is updated in place.
  * Asynchronous: a non-finite activation is reported by dc_sync as DC_E_NONFINITE. */
 int dc_stage_forward(dc_stage* stage, float* x, int T, int pos0, int use_kv);
+/* runLayersChunk (infer.js:288-296) on nchunks consecutive chunks in one pass
+ * over the stage's weights, as generateChunked calls it once per chunk
+ * (infer.js:339-367; app.js:877-923 keeps two chunks in flight per ring).
+ * rows (host ints) holds the chunks' lengths, summing to T <= max_rows, in
+ * position order from pos0 (the cached length); x (device, T x hidden) is
+ * updated in place.  The result and the cache are bit-identical to one
+ * dc_stage_forward(use_kv = 1) per chunk: each chunk's attention context uses
+ * the value channel scales as of its own last row.  Chunks of up to 16 rows,
+ * nchunks <= min(DC_MAX_CHUNKS, max_rows) share the weight pass; otherwise the
+ * chunks run one by one. */
+#define DC_MAX_CHUNKS 16
+int dc_stage_forward_chunks(dc_stage* stage, float* x, int T, int pos0, const int* rows, int nchunks);
 /* A cached one-row forward (use_kv = 1, T = 1: a decode step of a pipeline
  * stage) runs as a CUDA graph of the stage's layers, captured on first use
  * (the default).  on = 0 launches the kernels one by one instead; the results

@@ -54,12 +54,12 @@ def load(path):
         return json.load(f)
 
 
-def build(P, comp, g, splits):
+def build(P, comp, g, splits, per_pass=1):
     s = g["spec"]
     spec = P.infer.Spec(hidden=s["hidden"], layers=s["layers"], heads=s["heads"], kvHeads=s["kvHeads"],
                         inter=s["inter"], vocab=s["vocab"], ropeTheta=s["ropeTheta"], tie=s["tie"])
     if g["mode"] == "chunked":
-        max_rows, max_pos = max(g["chunk"], 8), len(g["prompt"]) + g["new"] + 1
+        max_rows, max_pos = max(g["chunk"] * per_pass, 8), len(g["prompt"]) + g["new"] + 1
     else:
         max_rows, max_pos = g["T"], g["T"]
     stages = []
@@ -75,11 +75,11 @@ def close(stages):
         S.close()
 
 
-def check_chunked(P, comp, g, splits):
-    spec, stages = build(P, comp, g, splits)
+def check_chunked(P, comp, g, splits, per_pass=1):
+    spec, stages = build(P, comp, g, splits, per_pass)
     try:
         prompt = g["prompt"]
-        got = P.infer.generate_chunked(stages, prompt, g["new"], g["chunk"])[len(prompt):]
+        got = P.infer.generate_chunked(stages, prompt, g["new"], g["chunk"], per_pass=per_pass)[len(prompt):]
         assert got == g["generated"], f"ids differ from index {first_diff(got, g['generated'])}"
         kv = g["kv_last_layer"]
         k8, ks, v = stages[-1].kv_read(spec.layers - 1)
@@ -91,8 +91,9 @@ def check_chunked(P, comp, g, splits):
         for S in stages:
             S.kv_reset()
         last = None
-        for ch in P.shard.prefill_chunks(len(prompt), g["chunk"], 1)["chunks"]:
-            last = P.infer.run_ring(stages, stages[0].embed_rows(prompt[ch["lo"]:ch["hi"]]), ch["lo"])
+        chunks = P.shard.prefill_chunks(len(prompt), g["chunk"], 1)["chunks"]
+        for lo, hi, rows in P.shard.chunk_passes(chunks, per_pass):
+            last = P.infer.run_ring(stages, stages[0].embed_rows(prompt[lo:hi]), lo, rows)
         rows = last.numel() // spec.hidden
         picks, logits = stages[0].logits_at(last, [rows - 1])
         assert sha(last[(rows - 1) * spec.hidden:]) == g["prefill_last_row_sha256"], "prefill hidden row differs"
@@ -141,15 +142,29 @@ def test_config_generation_matches_oracle(comp, P, path, split):
         check_lookahead(P, comp, g, splits)
 
 
+CHUNKED = [p for p in FILES if load(p)["mode"] == "chunked"]
+
+
+@pytest.mark.parametrize("path", CHUNKED, ids=[os.path.basename(p)[:-5] for p in CHUNKED])
+@pytest.mark.parametrize("per_pass,split", [(8, "one-stage"), (16, "config-stages")])
+def test_chunk_passes_generation_matches_oracle(comp, P, path, per_pass, split):
+    """The chunked configurations with several 16-token chunks per pass over
+    the weights (dc_stage_forward_chunks) give the oracle's ids, prefill row,
+    first logits and last-layer cache, which it computes one chunk at a time."""
+    g = load(path)
+    splits = [(0, g["spec"]["layers"])] if split == "one-stage" else [tuple(s) for s in g["stages"]]
+    check_chunked(P, comp, g, splits, per_pass)
+
+
 def test_bench_ring_matches_oracle(comp, P):
     """The benchmark's own call (pipeline.Ring, one GPU, two chunks in flight,
     decode laps as CUDA graphs) on the Llama-3-8B model gives the oracle's ids."""
     g = load(os.path.join(GOLDEN, "llama3-8b-chunked.json"))
-    spec, stages = build(P, comp, g, [(0, g["spec"]["layers"])])
+    spec, stages = build(P, comp, g, [(0, g["spec"]["layers"])], per_pass=16)
     try:
         ring = P.pipeline.Ring(stages[0], 0, 1, spec.hidden)
-        for _ in range(2):  # twice: the second run reuses the captured graphs
-            picks = ring.generate_chunked(g["prompt"], g["new"], g["chunk"], 2)
-            assert picks[:g["new"]].cpu().tolist() == g["generated"]
+        for per_pass in (1, 16, 16):  # the last run reuses the captured graphs
+            picks = ring.generate_chunked(g["prompt"], g["new"], g["chunk"], 2, per_pass=per_pass)
+            assert picks[:g["new"]].cpu().tolist() == g["generated"], per_pass
     finally:
         close(stages)

@@ -31,9 +31,12 @@ class FakeStage:
     def kv_reset(self):
         self.kv = {l: np.zeros(H) for l in range(self.lo, self.hi)}
 
-    def _layers(self, x, pos0, cached):
+    def _layers(self, x, pos0, cached, rows=None):
         T = x.numel() // H
         a = x.view(T, H).double().numpy().copy()
+        # the cache also moves at every chunk's end (as the value scales do),
+        # so the result depends on where the chunks of a pass end
+        ends = set(np.cumsum(rows).tolist()) if rows else {T}
         for l in range(self.lo, self.hi):
             for t in range(T):
                 if cached:
@@ -42,6 +45,8 @@ class FakeStage:
                 else:
                     ctx = a[: t + 1].sum(0)
                 a[t] = np.sin(3.0 * a[t] * self.w[l] + 0.5 * ctx + 0.37 * (pos0 + t))
+                if cached and t + 1 in ends:
+                    self.kv[l] = self.kv[l] * 0.9 + 0.01
         x.copy_(torch.from_numpy(a.astype(np.float32)).view(-1))
         return x
 
@@ -50,6 +55,10 @@ class FakeStage:
 
     def run_layers_chunk(self, x, pos0):
         return self._layers(x, pos0, True)
+
+    def run_layers_chunks(self, x, pos0, rows):
+        assert sum(rows) == x.numel() // H and len(rows) > 1
+        return self._layers(x, pos0, True, rows)
 
     def embed_rows(self, ids):
         return torch.from_numpy(self.emb[np.asarray(ids)].astype(np.float32).reshape(-1)).clone()
@@ -83,7 +92,7 @@ def plan_for(world):
     return {1: [(0, 6)], 2: [(0, 2), (2, 6)], 3: [(0, 1), (1, 4), (4, 6)]}[world]
 
 
-def run_rank(rank, world, port, prompt, q, wire=False):
+def run_rank(rank, world, port, prompt, q, wire=False, per_pass=1):
     import torch.distributed as dist
     import __graft_entry__ as G
     P = G.package()
@@ -100,7 +109,8 @@ def run_rank(rank, world, port, prompt, q, wire=False):
         tp = P.wire.WireTransport(tp, plan, rank, model_hash=0x5EED1234, seq=7)
     ring = P.pipeline.Ring(st, rank, world, H, tp, new_buffer=lambda n: torch.empty(n, dtype=torch.float32))
     marks = []
-    picks = ring.generate_chunked(prompt, 5, chunk_size=3, window=2, on_prefill=lambda: marks.append(rank))
+    picks = ring.generate_chunked(prompt, 5, chunk_size=3, window=2, on_prefill=lambda: marks.append(rank),
+                                  per_pass=per_pass)
     assert marks == [rank]  # every rank marks the end of its prefill part once (the bench's timer)
     look = ring.generate_lookahead([4, 4, 4, 7, 4, 4, 4], 4, 12, 4)
     if world > 1:
@@ -117,11 +127,11 @@ def _free_port():
     return p
 
 
-def run_world(world, prompt, wire=False):
+def run_world(world, prompt, wire=False, per_pass=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=run_rank, args=(r, world, port, prompt, q, wire)) for r in range(world)]
+    procs = [ctx.Process(target=run_rank, args=(r, world, port, prompt, q, wire, per_pass)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -178,3 +188,24 @@ def test_return_leg_is_not_stage_zero(P):
     assert last["to"] == "p0" and last["isReturn"] and last["address"] != 0
     assert P.pipeline.classify_act(last["address"], 0) == "return"
     assert P.pipeline.classify_act(0, 0) == "mine"
+
+
+@pytest.mark.parametrize("world,per_pass", [(1, 3), (2, 2), (3, 4)])
+def test_chunk_passes_match_one_chunk_per_pass(P, world, per_pass):
+    """Several chunks per pass travel the ring together (pipeline.Ring with
+    per_pass > 1, ragged chunks of 3 and 2 rows, the last pass short): the
+    stand-in stage sees the chunk ends inside each pass, and the ids equal one
+    chunk per pass on one rank."""
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7]
+    assert run_world(world, prompt, per_pass=per_pass) == run_world(1, prompt)
+
+
+def test_chunk_passes_grouping(P):
+    chunks = P.shard.prefill_chunks(40, 16, 2)["chunks"]  # 14, 13, 13
+    assert P.shard.chunk_passes(chunks, 2) == [(0, 27, [14, 13]), (27, 40, [13])]
+    assert P.shard.chunk_passes(chunks, 1) == [(0, 14, [14]), (14, 27, [13]), (27, 40, [13])]
+    assert P.shard.chunk_passes(chunks, 8) == [(0, 40, [14, 13, 13])]
+    big = P.shard.prefill_chunks(2048, 16, 2)["chunks"]
+    passes = P.shard.chunk_passes(big, 8)
+    assert len(passes) == 16 and all(r == [16] * 8 for _, _, r in passes)
+    assert [p[0] for p in passes] == list(range(0, 2048, 128))

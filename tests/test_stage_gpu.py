@@ -277,3 +277,58 @@ def test_synthetic_model_device_generator_matches_oracle(comp, O, P, cfg):
         assert got == want, f"fused={fused}"
         got = P.infer.generate_chunked(st, ids, 6, 16, use_device_loop=False)  # one-row graphs per stage
         assert got == want, f"fused={fused}, host loop"
+
+
+@pytest.mark.parametrize("cfg", [dict(hidden=256, layers=2, heads=4, kv=2, inter=512, vocab=1000, tie=True),
+                                 dict(hidden=512, layers=2, heads=4, kv=1, inter=1024, vocab=777, tie=False,
+                                      theta=500000.0)],
+                         ids=["hd64", "hd128"])
+def test_chunk_passes_match_oracle(comp, O, P, cfg):
+    """dc_stage_forward_chunks: consecutive chunks in one pass over the weights
+    give the oracle's rows (one chunk at a time, infer.js:339-367) bit for bit,
+    each chunk's context under the value scales as of its own last row; the
+    cache (f32 values, int8 keys and their scales) and the decode ids that
+    follow agree too.  Ragged chunks (prefillChunks of 45 in 16s: 15, 15, 15;
+    of 45 in 4s: twelve chunks of 3 and 4), passes of 2, 3, 5 and 16 chunks, a
+    pass split over two stages, and chunks wider than 16 rows (one by one)."""
+    ospec, spec, w = synth_model(O, P, **cfg)
+    om = O.Model(ospec, w)
+    L = cfg["layers"]
+    ids = [int(v) for v in np.random.default_rng(11).integers(0, cfg["vocab"], 45)]
+    for chunk, per_pass, splits in ((16, 3, [L]), (4, 5, [L]), (4, 16, [L]), (4, 2, [1, 1]), (23, 2, [L])):
+        chunks = P.shard.prefill_chunks(len(ids), chunk, 1)["chunks"]
+        kv = [O.KV(om, 0, L, 96)]
+        want_rows = []
+        for ch in chunks:
+            x = om.run_layers(om.embed_rows(ids[ch["lo"]:ch["hi"]]), 0, L, kv[0], ch["lo"])
+            want_rows.append(x)
+        want = np.concatenate(want_rows)
+        st = make_stages(P, comp, spec, w, splits, max_rows=64, max_pos=96)
+        got = []
+        for lo, hi, rows in P.shard.chunk_passes(chunks, per_pass):
+            got.append(P.infer.run_ring(st, st[0].embed_rows(ids[lo:hi]), lo, rows).cpu().numpy())
+        comp.sync()
+        case = (chunk, per_pass, splits)
+        assert np.concatenate(got).tobytes() == want.tobytes(), case
+        k8, ks, v = st[-1].kv_read(L - 1)
+        _, vf = kv[0].read(L - 1)
+        assert v.tobytes() == vf.tobytes(), case
+        assert st[-1].kv_len() == len(ids), case
+        ref = O.generate_chunked(om, [(0, L)], ids, 6, chunk)
+        assert P.infer.generate_chunked(st, ids, 6, chunk, per_pass=per_pass) == ref, case
+
+
+def test_chunk_pass_argument_checks(comp, P, fixture):
+    ospec, spec, w, om = fixture
+    st = make_stages(P, comp, spec, w, [6], max_rows=16)
+    x = st[0].embed_rows(list(range(12)))
+    with pytest.raises(P.DeviceError):
+        st[0].run_layers_chunks(x, 0, [5, 5])      # rows do not sum to T
+    with pytest.raises(P.DeviceError):
+        st[0].run_layers_chunks(x, 3, [6, 6])      # not at the cached length
+    with pytest.raises(P.DeviceError):
+        st[0].run_layers_chunks(x, 0, [6, 0, 6])   # an empty chunk
+    assert st[0].kv_len() == 0
+    # head_dim 16 (the reference's fixture): the chunks run one by one, same rows
+    st[0].run_layers_chunks(x, 0, [4, 4, 4])
+    assert st[0].kv_len() == 12
