@@ -902,6 +902,7 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=0, help="override the prompt length (profiling runs)")
     ap.add_argument("--new-tokens", type=int, default=0, help="override the generated tokens (profiling runs)")
     ap.add_argument("--per-pass", type=int, default=0, help="override the chunks per pass over the weights")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling runs)")
     ap.add_argument("--profile", choices=["prefill", "decode", "gemm"], default=None,
                     help="run one prefill chunk, one decode lap or one sweep GEMM inside an NVTX range 'profile' "
                          "(for ncu); prints no benchmark line")
@@ -917,6 +918,8 @@ def main():
             w["new"] = args.new_tokens
         if args.per_pass and w["mode"] == "chunked":
             w["per_pass"] = args.per_pass
+        if args.layers:
+            w["spec"] = dict(w["spec"], layers=args.layers)
     args.warmup = max(args.warmup, 3)
     peaks = load_peaks()
     if args.profile:

@@ -74,6 +74,7 @@ SIGNATURES = [
     ("dc_weight_info", _i, [_p, C.POINTER(_p), C.POINTER(_i), C.POINTER(_p), C.POINTER(_i), C.POINTER(_i)]),
     ("dc_vgemm", _i, [_p, _p, _i, _p, _u, _p]),
     ("dc_ordered_sum_dev", _i, [_p, _p, _i, _i, _p]),
+    ("dc_exp_dev", _i, [_p, _p, _i, _p, _i]),
     ("dc_rmsnorm_dev", _i, [_p, _p, _i, _i, _p, _d, _p, _i]),
     ("dc_l2_prefetch", _i, [_p, _p, C.c_size_t]),
     ("dc_kernel_probe", _i, [_p, C.POINTER(_u32)]),
@@ -91,6 +92,7 @@ SIGNATURES = [
     ("dc_stage_set_timeline", _i, [_p, _p, _i, _i]),
     ("dc_stage_timeline_info", _i, [_p, _p, _p, _i]),
     ("dc_stage_set_row_fusion", _i, [_p, _i]),
+    ("dc_stage_set_pass_attention", _i, [_p, _i]),
     ("dc_stage_logits", _i, [_p, _p, _i, _p, _i, _p, _p]),
     ("dc_decode_run", _i, [C.POINTER(_p), _i, _p, _i, _p, _i]),
     ("dc_stage_kv_reset", _i, [_p]),

@@ -190,6 +190,32 @@ __device__ __forceinline__ float dc_div_to_f32(double a, double z, double rz) {
   return f;
 }
 
+// f32(a / zlo) for the lower end of a bracket [zlo, zhi] that holds a serial
+// sum z (a >= 0, rlo = 1/zlo and rhi = 1/zhi in any rounding), and in *amb
+// whether f32(a / z) may differ across the bracket.  `narrow` says the bracket
+// is below 5e-13 relative: then a quotient a * rlo that dc_div_to_f32 finds
+// clear of every f32 rounding boundary (by its 2^-40 relative margin, beyond
+// the bracket's width and the product's rounding) rounds the same way for
+// every z in the bracket, and only the quotients near a boundary take both
+// ends.  The result is dc_div_to_f32(a, zlo, rlo) in every case.
+__device__ __forceinline__ float dc_div_bracket(double a, double zlo, double rlo, double zhi, double rhi,
+                                                bool narrow, bool* amb) {
+  const double q = __dmul_rn(a, rlo);
+  const float f = __double2float_rn(q);
+  const unsigned fb = __float_as_uint(f);
+  const int fe = (int)((fb >> 23) & 0xff);
+  bool slow = fe <= 1 || fe >= 254 || (fb & 0x7fffff) == 0;
+  if (!slow) {
+    const double hu = __longlong_as_double((long long)(fe - 151 + 1023) << 52);  // half a float ulp at f
+    const double d = fabs(__dsub_rn(q, (double)f));
+    slow = fabs(__dsub_rn(d, hu)) < q * 9.094947017729282e-13;
+  }
+  if (!slow && narrow) return f;
+  const float flo = slow ? __double2float_rn(dc_ddiv_slow(a, zlo)) : f;
+  *amb |= flo != dc_div_to_f32(a, zhi, rhi);
+  return flo;
+}
+
 // verified_core.js:227-228: f32(f32(f32(s) * a) * b), each step rounded.
 __device__ __forceinline__ float dc_epi(int32_t s, float a, float b) {
   return __fmul_rn(__fmul_rn(__int2float_rn(s), a), b);

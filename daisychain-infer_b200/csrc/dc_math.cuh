@@ -75,6 +75,47 @@ __device__ inline double fdlibm_exp(double x) {
   return __dmul_rn(__longlong_as_double(by + (long long)(k + 1000) * 4503599627370496LL), twom1000);
 }
 
+// fdlibm_exp for x <= 0 (finite), without branches: the reduction
+// k = (int)(x / ln2 - 1/2), hi = x - k ln2hi, lo = k ln2lo is fdlibm's general
+// one, and for 0.5 ln2 < |x| < 1.5 ln2 it yields exactly the k = -1, hi =
+// x + ln2hi, lo = -ln2lo of fdlibm's special case (k*ln2hi and k*ln2lo are
+// exact); for |x| up to fdlibm's k = 0 bound (high word 0x3fd62e42) k is set
+// to 0, where hi = x, lo = 0 and the rebuilt 1 - ((0 - xc/(2-c)) - x) equals
+// fdlibm's 1 - (xc/(c-2) - x) bit for bit (negation is exact).  Tiny |x|
+// (1 + x), results below the underflow threshold (+0) and the subnormal
+// scaling are selected, not branched to.  Equal to fdlibm_exp for every
+// finite x <= 0 (checked on the device against it).
+__device__ __forceinline__ double fdlibm_exp_nonpos(double x) {
+  const double one = 1.0;
+  const double twom1000 = b2d(0x0170000000000000ULL);
+  const double u_threshold = b2d(0xC0874910D52D3051ULL);
+  const double ln2HI0 = b2d(0x3FE62E42FEE00000ULL);
+  const double ln2LO0 = b2d(0x3DEA39EF35793C76ULL);
+  const double invln2 = b2d(0x3FF71547652B82FEULL);
+  const double P1 = b2d(0x3FC555555555553EULL), P2 = b2d(0xBF66C16C16BEBD93ULL),
+               P3 = b2d(0x3F11566AAF25DE2CULL), P4 = b2d(0xBEBBBD41C5D26BF1ULL),
+               P5 = b2d(0x3E66376972BEA4D0ULL);
+  const uint32_t hx = (uint32_t)((uint64_t)__double_as_longlong(x) >> 32) & 0x7fffffffu;
+  const int kg = (int)__dadd_rn(__dmul_rn(invln2, x), -0.5);  // truncation toward zero, as (int) in C
+  const int k = hx > 0x3fd62e42u ? kg : 0;
+  const double t = (double)k;
+  const double hi = __dsub_rn(x, __dmul_rn(t, ln2HI0));
+  const double lo = __dmul_rn(t, ln2LO0);
+  const double r = __dsub_rn(hi, lo);
+  const double tt = __dmul_rn(r, r);
+  double p = __dadd_rn(P4, __dmul_rn(tt, P5));
+  p = __dadd_rn(P3, __dmul_rn(tt, p));
+  p = __dadd_rn(P2, __dmul_rn(tt, p));
+  p = __dadd_rn(P1, __dmul_rn(tt, p));
+  const double c = __dsub_rn(r, __dmul_rn(tt, p));
+  const double y = __dsub_rn(one, __dsub_rn(__dsub_rn(lo, __ddiv_rn(__dmul_rn(r, c), __dsub_rn(2.0, c))), hi));
+  const long long by = __double_as_longlong(y);
+  const double yn = __longlong_as_double(by + (long long)k * 4503599627370496LL);
+  const double ys = __dmul_rn(__longlong_as_double(by + (long long)(k + 1000) * 4503599627370496LL), twom1000);
+  double res = k >= -1021 ? yn : ys;
+  res = hx < 0x3e300000u ? __dadd_rn(one, x) : res;
+  return x < u_threshold ? 0.0 : res;
+}
 
 // infer.js:59 + :212: f32(silu(g) * u) with silu(v) = v / (1 + exp(-v)) in
 // double and the exp above.

@@ -113,6 +113,7 @@ struct dc_stage {
   unsigned long long row_nk = 0;
   bool row_graph = true;
   bool row_fused = false;  // decode rows: GEMVs with the norm / SwiGLU / row quantisation fused
+  int pass_attn = 0;       // a pass's attention: 0 k_attn_chunk when the CTAs fill the SMs, 1 always, 2 never
   std::vector<dc_stage*> lap_key;
   int32_t* lap_picks = nullptr;
   std::vector<void*> allocs;
@@ -611,17 +612,21 @@ __global__ void k_vscale(const uint32_t* vmax, float* vs, int* vchg,
 // channels (from cb) on 256 threads (32 channels x 8 rows), transposed through
 // shared memory.
 __device__ __forceinline__ void vquant_tile(const float* vcache, const float* vs, const int* vchg, int8_t* v8t,
-                                            int N, int n0, int kvDim, int hd, int ldp, int jb, int cb) {
+                                            int N, int n0, int kvDim, int hd, int ldp, int jb, int cb,
+                                            const float* vfin = nullptr) {
   __shared__ int8_t tile[32][65];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = cb + tx;
   const bool cval = c < kvDim;
-  const bool chg = cval && vchg[c] != 0;
+  // vfin (a pass buffer): only the channels whose scale differs from vfin's,
+  // every row; otherwise new rows always and older rows in moved channels
+  const bool chg = cval && (vfin ? vs[c] != vfin[c] : vchg[c] != 0);
+  if (vfin && !__any_sync(0xffffffffu, chg)) return;  // (every warp holds the same channels)
   const double sc = cval ? (double)vs[c] : 1.0, rsc = __drcp_rn(sc);
   for (int r = ty; r < 64; r += 8) {
     const int j = jb + r;
     int8_t v = 0;
-    if (cval && j < N && (j >= n0 || chg)) v = dc_quant_div((double)vcache[(int64_t)j * kvDim + c], sc, rsc);
+    if (cval && j < N && (vfin ? chg : (j >= n0 || chg))) v = dc_quant_div((double)vcache[(int64_t)j * kvDim + c], sc, rsc);
     tile[tx][r] = v;
   }
   __syncthreads();
@@ -629,7 +634,7 @@ __device__ __forceinline__ void vquant_tile(const float* vcache, const float* vs
     const int cl = idx >> 6, r = idx & 63;
     const int cc = cb + cl, j = jb + r;
     if (cc >= kvDim || j >= N) continue;
-    if (j < n0 && !vchg[cc]) continue;  // an unchanged channel keeps its int8 rows
+    if (vfin ? vs[cc] == vfin[cc] : (j < n0 && !vchg[cc])) continue;  // rows that keep their int8 values
     const int g = cc / hd, ch = cc - g * hd;
     v8t[((int64_t)g * hd + ch) * ldp + j] = tile[cl][r];
   }
@@ -656,26 +661,37 @@ struct ChunkSet {
 // chunk's append): per channel, the running |v| maximum folded over the pass's
 // rows one chunk at a time; chunk g's scale and its change flag against the
 // cache's current scale go to vsg/vchgg[g], and the last chunk's become the
-// cache's (vmax, vs, vchg).  grid ceil(kvDim/128), block 128.
-__global__ void __launch_bounds__(128) k_vscale_chunks(const float* vcache, uint32_t* vmax, float* vs, int* vchg,
-                                                       int kvDim, const int* n0p, ChunkSet cks, float* vsg,
-                                                       int* vchgg) {
+// cache's (vmax, vs, vchg).  grid ceil(kvDim/32), block 32 x DC_MAX_CHUNKS:
+// warp g takes chunk g's rows for the block's 32 channels (lane = channel).
+__global__ void __launch_bounds__(32 * DC_MAX_CHUNKS) k_vscale_chunks(const float* vcache, uint32_t* vmax,
+                                                                     float* vs, int* vchg, int kvDim,
+                                                                     const int* n0p, ChunkSet cks, float* vsg,
+                                                                     int* vchgg) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= kvDim) return;
+  __shared__ uint32_t cm[DC_MAX_CHUNKS][32];  // [chunk][channel]: |v| maxima of the chunk's rows
+  const int lane = threadIdx.x & 31, gw = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
   const int n0 = *n0p;
+  if (gw < cks.G) {
+    uint32_t m = 0;
+    const int rb = gw ? cks.end[gw - 1] : 0, re = cks.end[gw];
+    if (c < kvDim) {
+      const float* vc = vcache + (int64_t)(n0 + rb) * kvDim + c;
+#pragma unroll 4
+      for (int r = 0; r < re - rb; r++) m = max(m, __float_as_uint(fabsf(__ldcg(vc + (int64_t)r * kvDim))));
+    }
+    cm[gw][lane] = m;
+  }
+  __syncthreads();
+  if (gw != 0 || c >= kvDim) return;
   const int fresh = n0 == 0;
   const float prior = vs[c];
   uint32_t m = vmax[c];
-  const float* vc = vcache + (int64_t)n0 * kvDim + c;
   float ns = prior;
   int chg = 0;
-  int r = 0;
   for (int g = 0; g < cks.G; g++) {
-    const int e = cks.end[g];
-#pragma unroll 8
-    for (; r < e; r++) m = max(m, __float_as_uint(fabsf(vc[(int64_t)r * kvDim])));
+    m = max(m, cm[g][lane]);
     ns = __double2float_rn(quant_scale(__uint_as_float(m)));
     chg = fresh || ns != prior;
     vsg[g * kvDim + c] = ns;
@@ -686,25 +702,61 @@ __global__ void __launch_bounds__(128) k_vscale_chunks(const float* vcache, uint
   vchg[c] = chg;
 }
 
-// The int8 values each chunk of a pass attends with: chunk g < G-1 into the
-// pass buffer v8s[g] (every row up to the chunk's end, under its scales), the
-// last chunk into the cache (its new rows, and older rows in channels whose
-// scale moved), as k_vquant.  grid (ceil(N/64), ceil(kvDim/32), G), block 256.
+// The int8 values each chunk of a pass attends with: the last chunk's into the
+// cache (its new rows, and older rows in channels whose scale moved), as
+// k_vquant; for chunk g < G-1, the channels whose scale at the chunk's end is
+// not the final one into the pass buffer v8s[g] (every row up to the chunk's
+// end) -- in every other channel the cache's int8 rows are chunk g's.  grid
+// (ceil(N/64), ceil(kvDim/32)), block 256 (32 channels x 8 rows): each block
+// reads its 64 x 32 tile of values once and writes it for every chunk that
+// needs it (transposed through shared memory).
 __global__ void __launch_bounds__(256) k_vquant_chunks(const float* vcache, const float* vs, const int* vchg,
                                                        int8_t* v8t, int n0, int kvDim, int hd, int ldp,
                                                        ChunkSet cks, const float* vsg, int8_t* v8s) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
-  const int g = blockIdx.z;
-  const int N = n0 + cks.end[g];
-  const int jb = blockIdx.x * 64;
-  if (jb >= N) return;
-  if (g == cks.G - 1) {
-    vquant_tile(vcache, vs, vchg, v8t, N, n0, kvDim, hd, ldp, jb, blockIdx.y * 32);
-  } else {
-    // n0 = 0: every row is written (vchg is then never read)
-    vquant_tile(vcache, vsg + (int64_t)g * kvDim, vchg, v8s + (int64_t)g * kvDim * ldp, N, 0, kvDim, hd, ldp, jb,
-                blockIdx.y * 32);
+  __shared__ int8_t tile[32][65];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int cb = blockIdx.y * 32, jb = blockIdx.x * 64;
+  const int c = cb + tx;
+  const bool cval = c < kvDim;
+  const int N = n0 + cks.end[cks.G - 1];
+  float v[8];
+#pragma unroll
+  for (int u = 0; u < 8; u++) {
+    const int j = jb + ty + 8 * u;
+    v[u] = cval && j < N ? __ldcg(vcache + (int64_t)j * kvDim + c) : 0.0f;
+  }
+  const float fin = cval ? vs[c] : 1.0f;
+#pragma unroll 1
+  for (int g = 0; g < cks.G; g++) {
+    const bool last = g == cks.G - 1;
+    const int Ng = n0 + cks.end[g];
+    if (jb >= Ng) continue;  // (block-uniform)
+    const float sg = last ? fin : (cval ? vsg[(int64_t)g * kvDim + c] : fin);
+    // the channels this chunk writes: all (new rows) and moved ones (older rows)
+    // for the cache; those whose scale is not the final one for a pass buffer
+    const bool chg = cval && (last ? vchg[c] != 0 : sg != fin);
+    const bool any_new = last && jb + 64 > n0;
+    if (!any_new && !__any_sync(0xffffffffu, chg)) continue;  // (every warp holds the same channels)
+    const double sc = (double)sg, rsc = __drcp_rn(sc);
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int j = jb + ty + 8 * u;
+      int8_t q = 0;
+      if (cval && j < Ng && (chg || (last && j >= n0))) q = dc_quant_div((double)v[u], sc, rsc);
+      tile[tx][ty + 8 * u] = q;
+    }
+    __syncthreads();
+    int8_t* dst = last ? v8t : v8s + (int64_t)g * kvDim * ldp;
+    for (int idx = threadIdx.x; idx < 32 * 64; idx += blockDim.x) {
+      const int cl = idx >> 6, r = idx & 63;
+      const int cc = cb + cl, j = jb + r;
+      if (cc >= kvDim || j >= Ng) continue;
+      const bool wr = last ? (j >= n0 || vchg[cc] != 0) : (vsg[(int64_t)g * kvDim + cc] != vs[cc]);
+      if (wr) dst[(int64_t)cc * ldp + j] = tile[cl][r];
+    }
+    __syncthreads();
   }
 }
 
@@ -829,7 +881,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* h, in
   m = block_max_d(m, redd);
   // 4. e_j and its f32 copy
   for (int j = threadIdx.x; j <= see; j += blockDim.x) {
-    const double e = dcm::fdlibm_exp(__dsub_rn(__dmul_rn((double)af[j], scale), m));
+    const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(__dmul_rn((double)af[j], scale), m));
     ed[j] = e;
     af[j] = __double2float_rn(e);
   }
@@ -905,6 +957,320 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* h, in
   if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
 
+// The attention of one chunk's query rows (at most 16) for one head, the
+// whole of infer.js:174-196 for those rows in one CTA: grid (nH, G) (G chunks
+// of a pass, 1 otherwise), AR_THREADS threads, HD the head dim (64, 128 or
+// 256).  The rows share every key and value load, and the per-row reductions
+// are warp-level:
+//  1. warp w quantises query row w (quantizeRows of the head's HD values);
+//  2. scores s_ij = epi(q_i . k_j, qs_i, ks_j) by 16-row x 8-key int8
+//     tensor-core tiles (mma.sync m16n8k32, int32 accumulators: the dot
+//     products are exact), each warp taking every 16th tile, keys read
+//     straight from the cache (16 bytes per thread; the bytes a thread gives
+//     the A and B fragments are the same physical head-dim positions, so the
+//     sum over them is the dot product); s into shared memory, the exact row
+//     maximum of s * scale (double) on the way;
+//  3. warp w: e_j = exp(s_j * scale - m) (fdlibm method, double) for keys
+//     0..see, f32(e_j) kept in place, the bracket of the serial sum z;
+//     a_j = f32(f32(e_j) / z) at the lower end of the bracket, checked
+//     against the upper end; the row's |a| maximum;
+//  4. a row whose a_j depend on where z falls in the bracket (rare) gets the
+//     serial key-order z from the whole block (dco::ordered_sum over e_j
+//     recomputed in double);
+//  5. warp w quantises its a row (quantizeRows over the row's keys; zero past
+//     `see`) into shared memory;
+//  6. the context ctx_ic = sum_j a8_ij v8_cj by 16-row x 8-channel int8 tiles
+//     over the keys (value rows channel-major from the cache, or for a chunk
+//     before a pass's last, from the pass buffer in channels whose scale moved
+//     after it), verified epilogue with the row's probability scale and the
+//     channel's value scale; |ctx| folded into the row maxima.
+// Dynamic shared memory: 16 * ldp floats (scores / e / a) + 16 * ldp bytes
+// (the int8 probability rows; before them, one row of doubles for step 4).
+constexpr int AR_THREADS = 512;
+__device__ __forceinline__ void mma_s8_16832(int& c0, int& c1, int& c2, int& c3, unsigned a0, unsigned a1,
+                                             unsigned a2, unsigned a3, unsigned b0, unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c0), "+r"(c1), "+r"(c2), "+r"(c3)
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Two m16n8k32 steps over 64 k positions: A rows gi / gi + 8 and the B column
+// each give the same 16 physical bytes (64p + 16 ti ..) of their rows.
+__device__ __forceinline__ void mma_s8_pair(int* c, const int4& ra, const int4& rb, const int4& kb) {
+  mma_s8_16832(c[0], c[1], c[2], c[3], ra.x, rb.x, ra.y, rb.y, kb.x, kb.y);
+  mma_s8_16832(c[0], c[1], c[2], c[3], ra.z, rb.z, ra.w, rb.w, kb.z, kb.w);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, int nqkv, int nH, int nKV,
+                                                             const int8_t* k8, const float* ks,
+                                                             const int8_t* v8t, const float* vs, int T,
+                                                             const int* n0p, int max_pos, int ldp, double scale,
+                                                             float* out, int qDim, uint32_t* rowmax, int* status,
+                                                             ChunkSet cks, const int8_t* v8s, const float* vsg) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  constexpr int NP = HD / 64;  // pairs of 32-byte k-steps
+  constexpr int QLD = HD + 16;
+  extern __shared__ __align__(16) uint8_t sm[];
+  float* S = (float*)sm;                                  // [16][ldp]
+  int8_t* A8 = (int8_t*)(S + (size_t)16 * ldp);           // [16][ldp]
+  double* eb = (double*)A8;                               // [ldp] (step 4, before A8 is written)
+  __shared__ __align__(16) int8_t q8s[16 * QLD];
+  __shared__ float qsf[16], asf[16];
+  __shared__ double wm[16][16];  // [warp][row] maxima
+  __shared__ float amxs[16];
+  __shared__ int ambs[16];
+  __shared__ dco::Smem16 osm;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hq = blockIdx.x, g = hq / (nH / nKV);
+  int r0 = 0, r1 = T;
+  const int8_t* vz = nullptr;  // chunk z < G-1 of a pass: its buffer, and its value scales
+  const float* vsz = vs;
+  if (cks.G > 1) {
+    const int z = blockIdx.y;
+    r0 = z ? cks.end[z - 1] : 0;
+    r1 = cks.end[z];
+    if (z < cks.G - 1) {
+      vz = v8s + (int64_t)z * nKV * HD * ldp;
+      vsz = vsg + (int64_t)z * nKV * HD;
+    }
+  }
+  const int Tc = r1 - r0, n0 = *n0p;
+  const int Nc = n0 + r1;  // keys the chunk's last row sees
+  // 1. the query rows, quantised (warp w: row w); rows past the chunk are zero
+  {
+    bool bad = false;
+    float v[HD / 32];
+    float mx = 0.0f;
+    if (warp < Tc) {
+      const float* qrow = h + (int64_t)(r0 + warp) * nqkv + hq * HD;
+#pragma unroll
+      for (int u = 0; u < HD / 32; u++) {
+        v[u] = qrow[lane + 32 * u];
+        bad |= !isfinite(v[u]);
+        mx = fmaxf(mx, fabsf(v[u]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
+#pragma unroll
+    for (int u = 0; u < HD / 32; u++)
+      q8s[warp * QLD + lane + 32 * u] = warp < Tc ? dc_quant_div((double)v[u], qsc, rqsc) : (int8_t)0;
+    if (lane == 0) qsf[warp] = __double2float_rn(qsc);
+    if (bad) atomicOr(status, DC_ST_NONFINITE);
+  }
+  __syncthreads();
+  // 2. scores by 16 x 8 tiles
+  const int gi = lane >> 2, ti = lane & 3;
+  const int see0 = n0 + r0 + gi, see1 = see0 + 8;  // rows gi and gi + 8 see keys 0..see
+  int4 QA[NP], QB[NP];
+#pragma unroll
+  for (int p = 0; p < NP; p++) {
+    QA[p] = *(const int4*)(q8s + gi * QLD + 64 * p + 16 * ti);
+    QB[p] = *(const int4*)(q8s + (gi + 8) * QLD + 64 * p + 16 * ti);
+  }
+  const float qs0 = gi < Tc ? qsf[gi] : 0.0f, qs1 = gi + 8 < Tc ? qsf[gi + 8] : 0.0f;
+  double m0 = -INFINITY, m1 = -INFINITY;
+  const int8_t* kb = k8 + (int64_t)g * max_pos * HD;
+  const float* ksg = ks + (int64_t)g * max_pos;
+  const int ntile = (Nc + 7) >> 3;
+#pragma unroll 2
+  for (int tile = warp; tile < ntile; tile += AR_THREADS / 32) {
+    const int key = min(tile * 8 + gi, max_pos - 1);
+    const int4* kr = (const int4*)(kb + (int64_t)key * HD) + ti;
+    int4 kv[NP];
+#pragma unroll
+    for (int p = 0; p < NP; p++) kv[p] = __ldcg(kr + 4 * p);
+    const int j0 = tile * 8 + 2 * ti;
+    const float ks0 = ksg[min(j0, max_pos - 1)], ks1 = ksg[min(j0 + 1, max_pos - 1)];
+    int c[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < NP; p++) mma_s8_pair(c, QA[p], QB[p], kv[p]);
+    const float s00 = dc_epi(c[0], qs0, ks0), s01 = dc_epi(c[1], qs0, ks1);
+    const float s10 = dc_epi(c[2], qs1, ks0), s11 = dc_epi(c[3], qs1, ks1);
+    *(float2*)(S + (size_t)gi * ldp + j0) = make_float2(s00, s01);
+    *(float2*)(S + (size_t)(gi + 8) * ldp + j0) = make_float2(s10, s11);
+    if (j0 <= see0) m0 = fmax(m0, __dmul_rn((double)s00, scale));
+    if (j0 + 1 <= see0) m0 = fmax(m0, __dmul_rn((double)s01, scale));
+    if (j0 <= see1) m1 = fmax(m1, __dmul_rn((double)s10, scale));
+    if (j0 + 1 <= see1) m1 = fmax(m1, __dmul_rn((double)s11, scale));
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    m0 = fmax(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    m1 = fmax(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+  }
+  if (ti == 0) {
+    wm[warp][gi] = m0;
+    wm[warp][gi + 8] = m1;
+  }
+  __syncthreads();
+  // 3. warp w: row w's softmax over keys 0..see
+  const int row = warp, see = n0 + r0 + row, n = see + 1;
+  float* Sr = S + (size_t)row * ldp;
+  if (row < Tc) {
+    double m = wm[0][row];
+#pragma unroll
+    for (int w = 1; w < 16; w++) m = fmax(m, wm[w][row]);
+    double part = 0.0, wpart = 0.0;
+#pragma unroll 4
+    for (int j = lane; j < n; j += 32) {
+      const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(__dmul_rn((double)Sr[j], scale), m));
+      Sr[j] = __double2float_rn(e);
+      part += e;
+      wpart += (double)(n - j) * e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      part += __shfl_xor_sync(0xffffffffu, part, o);
+      wpart += __shfl_xor_sync(0xffffffffu, wpart, o);
+    }
+    // a term passes through at most ceil(n / 32) adds in its lane and 5 in the warp
+    const double hr = serial_sum_radius(part, wpart, (n + 31) / 32 + 10);
+    const double zlo = part - hr, zhi = part + hr;
+    const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
+    const bool narrow = __dsub_rn(zhi, zlo) < 5e-13 * zlo;
+    bool amb = false;
+    float amx = 0.0f;
+#pragma unroll 4
+    for (int j = lane; j < n; j += 32) {
+      const float a = dc_div_bracket((double)Sr[j], zlo, rlo, zhi, rhi, narrow, &amb);
+      Sr[j] = a;
+      amx = fmaxf(amx, a);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
+    const bool wamb = __any_sync(0xffffffffu, amb);
+    if (lane == 0) {
+      amxs[row] = amx;
+      ambs[row] = wamb ? 1 : 0;
+      wm[0][row] = m;  // (kept for the exact path)
+    }
+  } else if (lane == 0) {
+    ambs[row] = 0;
+  }
+  __syncthreads();
+  // 4. rows whose probabilities the bracket cannot settle: the serial z
+#pragma unroll 1
+  for (int i = 0; i < Tc; i++) {
+    if (!ambs[i]) continue;  // (block-uniform)
+    const int ni = n0 + r0 + i + 1;
+    const double m = wm[0][i];
+    const int4* q4 = (const int4*)(q8s + i * QLD);
+    for (int j = tid; j < ni; j += AR_THREADS) {
+      const int4* kr = (const int4*)(kb + (int64_t)j * HD);
+      int acc = 0;
+#pragma unroll
+      for (int cc = 0; cc < HD / 16; cc++) acc = dp4a16(kr[cc], q4[cc], acc);
+      eb[j] = dcm::fdlibm_exp_nonpos(__dsub_rn(__dmul_rn((double)dc_epi(acc, qsf[i], ksg[j]), scale), m));
+    }
+    __syncthreads();
+    const double z = ordered_sum_cold16(eb, ni, osm);
+    const double rz = __drcp_rn(z);
+    float amx = 0.0f;
+    float* Si = S + (size_t)i * ldp;
+    for (int j = tid; j < ni; j += AR_THREADS) {
+      const float a = dc_div_to_f32((double)__double2float_rn(eb[j]), z, rz);
+      Si[j] = a;
+      amx = fmaxf(amx, fabsf(a));
+    }
+    amx = block_max_f(amx, (float*)wm[1]);  // (32 floats of scratch)
+    if (tid == 0) amxs[i] = amx;
+    __syncthreads();
+  }
+  // 5. each probability row quantised into A8 (zero past `see`, up to Kc)
+  const int Kc = (Nc + 63) & ~63;  // keys of the context's k-steps (ldp is a multiple of 64)
+  if (row < Tc) {
+    const double asc = quant_scale(amxs[row]), rasc = __drcp_rn(asc);
+    uint32_t* dst = (uint32_t*)(A8 + (size_t)row * ldp);
+    for (int j4 = lane; j4 < (Kc >> 2); j4 += 32) {
+      const float4 a = *(const float4*)(Sr + 4 * j4);
+      const int j = 4 * j4;
+      const uint32_t b0 = j <= see ? (uint8_t)dc_quant_div((double)a.x, asc, rasc) : 0u;
+      const uint32_t b1 = j + 1 <= see ? (uint8_t)dc_quant_div((double)a.y, asc, rasc) : 0u;
+      const uint32_t b2 = j + 2 <= see ? (uint8_t)dc_quant_div((double)a.z, asc, rasc) : 0u;
+      const uint32_t b3 = j + 3 <= see ? (uint8_t)dc_quant_div((double)a.w, asc, rasc) : 0u;
+      dst[j4] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+    if (lane == 0) asf[row] = __double2float_rn(asc);
+  } else {
+    uint32_t* dst = (uint32_t*)(A8 + (size_t)row * ldp);
+    for (int j4 = lane; j4 < (Kc >> 2); j4 += 32) dst[j4] = 0u;
+  }
+  __syncthreads();
+  // 6. the context by 16 x 8 tiles over the keys (64 per step pair)
+  constexpr int NT = HD / 8;                     // channel tiles
+  constexpr int TPW = NT > 16 ? NT / 16 : 1;      // tiles per warp
+  constexpr int KS = NT < 16 ? 16 / NT : 1;       // key splits (warps sharing a tile)
+  const int tile0 = warp % (16 / KS), sp = warp / (16 / KS);
+  const int npair = Kc >> 6, per = (npair + KS - 1) / KS;
+  const int p0 = sp * per, p1 = min(npair, p0 + per);
+  int acc[TPW][4];
+  const int4* vrow[TPW];
+#pragma unroll
+  for (int u = 0; u < TPW; u++) {
+    acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0;
+    const int cc = g * HD + (tile0 + 16 * u) * 8 + gi;  // this lane's B channel
+    const int8_t* src = (vz && vsz[cc] != vs[cc]) ? vz : v8t;
+    vrow[u] = (const int4*)(src + (int64_t)cc * ldp) + ti;
+  }
+  const int4* ar = (const int4*)(A8 + (size_t)gi * ldp) + ti;
+  const int4* br = (const int4*)(A8 + (size_t)(gi + 8) * ldp) + ti;
+#pragma unroll 2
+  for (int p = p0; p < p1; p++) {
+    const int4 ra = ar[4 * p], rb = br[4 * p];
+#pragma unroll
+    for (int u = 0; u < TPW; u++) mma_s8_pair(acc[u], ra, rb, __ldcg(vrow[u] + 4 * p));
+  }
+  if (KS > 1) {  // the other key splits' partial sums into split 0 (exact int32)
+    int* red = (int*)S;  // [split][tile][lane][4] (the score rows are free now)
+    if (sp > 0)
+      *(int4*)(red + (((sp - 1) * 16 + tile0) * 32 + lane) * 4) = make_int4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+    __syncthreads();
+    if (sp == 0) {
+      for (int q = 1; q < KS; q++) {
+        const int4 o = *(const int4*)(red + (((q - 1) * 16 + tile0) * 32 + lane) * 4);
+        acc[0][0] += o.x;
+        acc[0][1] += o.y;
+        acc[0][2] += o.z;
+        acc[0][3] += o.w;
+      }
+    }
+  }
+  if (sp == 0) {
+    bool bad = false;
+    float x0 = 0.0f, x1 = 0.0f;  // |ctx| maxima of rows gi, gi + 8
+    const float as0 = gi < Tc ? asf[gi] : 0.0f, as1 = gi + 8 < Tc ? asf[gi + 8] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < TPW; u++) {
+      const int c = (tile0 + 16 * u) * 8 + 2 * ti;
+      const float vc0 = vsz[g * HD + c], vc1 = vsz[g * HD + c + 1];
+      if (gi < Tc) {
+        const float o0 = dc_epi(acc[u][0], as0, vc0), o1 = dc_epi(acc[u][1], as0, vc1);
+        *(float2*)(out + (int64_t)(r0 + gi) * qDim + hq * HD + c) = make_float2(o0, o1);
+        bad |= !isfinite(o0) || !isfinite(o1);
+        x0 = fmaxf(x0, fmaxf(fabsf(o0), fabsf(o1)));
+      }
+      if (gi + 8 < Tc) {
+        const float o0 = dc_epi(acc[u][2], as1, vc0), o1 = dc_epi(acc[u][3], as1, vc1);
+        *(float2*)(out + (int64_t)(r0 + gi + 8) * qDim + hq * HD + c) = make_float2(o0, o1);
+        bad |= !isfinite(o0) || !isfinite(o1);
+        x1 = fmaxf(x1, fmaxf(fabsf(o0), fabsf(o1)));
+      }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, o));
+      x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, o));
+    }
+    if (ti == 0 && gi < Tc) atomicMax(rowmax + r0 + gi, __float_as_uint(x0));
+    if (ti == 0 && gi + 8 < Tc) atomicMax(rowmax + r0 + gi + 8, __float_as_uint(x1));
+    if (bad) atomicOr(status, DC_ST_NONFINITE);
+  }
+}
+
 // The context of a chunk's T rows for 32 channels of one head, from the
 // probability rows k_attention wrote (split form): grid (nH, hd / 32, G), 256
 // threads; ctx[t][c] = sum_j a8[t][j] * v8[c][j] (exact int32), verified
@@ -930,13 +1296,16 @@ __global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* a8g, const float
   const int g = hq / (nH / nKV);
   const int tid = threadIdx.x;
   int r0 = 0, r1 = T;  // this CTA's rows
+  const int8_t* vsrc = v8t;  // this thread's value row (tid < 32: channel c0 + tid)
   if (cks.G > 1) {
     const int z = blockIdx.z;
     r0 = z ? cks.end[z - 1] : 0;
     r1 = cks.end[z];
     if (z < cks.G - 1) {
-      v8t = v8s + (int64_t)z * nKV * hd * ldp;
-      vs = vsg + (int64_t)z * nKV * hd;
+      const float* vz = vsg + (int64_t)z * nKV * hd;
+      const int cc = g * hd + c0 + (tid & 31);
+      if (vz[cc] != vs[cc]) vsrc = v8s + (int64_t)z * nKV * hd * ldp;  // a channel whose scale moved later
+      vs = vz;
     }
   }
   const int Tc = r1 - r0;
@@ -949,7 +1318,7 @@ __global__ void __launch_bounds__(256) k_attn_ctx(const int8_t* a8g, const float
   if (tid < 32) {
     if (tid == 0) dcp::mbar_expect_tx(&bar, (uint32_t)((32 + Tc) * nfill));
     __syncwarp();
-    dcp::bulk_load(sV + (size_t)tid * ldp, v8t + ((int64_t)g * hd + c0 + tid) * ldp, (uint32_t)nfill, &bar);
+    dcp::bulk_load(sV + (size_t)tid * ldp, vsrc + ((int64_t)g * hd + c0 + tid) * ldp, (uint32_t)nfill, &bar);
     if (tid < Tc)
       dcp::bulk_load(sA + (size_t)tid * ldp, a8g + ((int64_t)hq * T + r0 + tid) * ldp, (uint32_t)nfill, &bar);
   }
@@ -1112,7 +1481,7 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* h, int nqkv,
     m = block_max_d(m, redd);
 #pragma unroll 1
     for (int j = tid; j < N; j += 256) {
-      const double e = dcm::fdlibm_exp(__dsub_rn(xs[j], m));
+      const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(xs[j], m));
       xs[j] = e;
       af[j] = __double2float_rn(e);
     }
@@ -1384,7 +1753,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < N) {
-      const double e = dcm::fdlibm_exp(__dsub_rn(xs[j], m));
+      const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(xs[j], m));
       xs[j] = e;
       af[j] = __double2float_rn(e);
       part += e;
@@ -1409,16 +1778,13 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const double zr = serial_sum_radius(zp, zw, (N + ATTD_KB - 1) / ATTD_KB + 72);
   const double zlo = zp - zr, zhi = zp + zr;
   const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
+  const bool narrow = __dsub_rn(zhi, zlo) < 5e-13 * zlo;
   bool amb = false;
   float amx = 0.0f;
 #pragma unroll 4
   for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
-    if (j < N) {
-      const float alo = dc_div_to_f32((double)af[j], zhi, rhi), ahi = dc_div_to_f32((double)af[j], zlo, rlo);
-      amb |= alo != ahi;
-      amx = fmaxf(amx, ahi);
-    }
+    if (j < N) amx = fmaxf(amx, dc_div_bracket((double)af[j], zlo, rlo, zhi, rhi, narrow, &amb));
   }
   {
     const int wamb = __any_sync(0xffffffffu, amb) ? 1 : 0;
@@ -1564,7 +1930,14 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
 
 using dcm::swiglu_f32;
 
-// SwiGLU, element-parallel over grid (ceil(I/256), rows): hid = f32(silu(g)*u)
+// Blocks per row of an element-parallel row kernel (256 threads, grid-stride
+// over the row): enough for about four blocks per SM over all rows.
+static int ew_blocks(const dc_ctx* ctx, int cols, int rows) {
+  const int need = (4 * ctx->sm_count + rows - 1) / rows;
+  return std::max(1, std::min((cols + 255) / 256, need));
+}
+
+// SwiGLU, element-parallel over grid (ew_blocks, rows): hid = f32(silu(g)*u)
 // with silu(v) = v / (1 + exp(-v)) in double, from the fused gate/up GEMM's
 // interleaved output row (g_j at 2j, u_j at 2j + 1) into hout (I per row), and
 // |hid| folded into the row maximum (rowmax must start at 0).  The row's
@@ -1575,15 +1948,16 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* ho
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   __shared__ float red[32];
   const int row = blockIdx.y;
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  const float* g = h + (int64_t)row * 2 * I;
+  const float2* g = (const float2*)(h + (int64_t)row * 2 * I);
   float mx = 0.0f;
   bool bad = false;
-  if (j < I) {
-    const float y = swiglu_f32(g[2 * j], g[2 * j + 1]);
-    bad = !isfinite(y);
+#pragma unroll 4
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < I; j += gridDim.x * blockDim.x) {
+    const float2 gu = g[j];
+    const float y = swiglu_f32(gu.x, gu.y);
+    bad |= !isfinite(y);
     hout[(int64_t)row * I + j] = y;
-    mx = fabsf(y);
+    mx = fmaxf(mx, fabsf(y));
   }
   mx = block_max_f(mx, red);
   if (threadIdx.x == 0) atomicMax(rowmax + row, __float_as_uint(mx));
@@ -1591,17 +1965,18 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* ho
 }
 
 // quantizeRows from a finished row maximum, element-parallel over grid
-// (ceil(ldq/256), rows): s[row] = f32(max(mx/127, 1e-8)) in double, q = clamp(round(x/sc)).
+// (ew_blocks, rows): s[row] = f32(max(mx/127, 1e-8)) in double, q = clamp(round(x/sc)).
 __global__ void __launch_bounds__(256) k_rowquant(const float* x, int64_t ldx, int cols,
                                                  const uint32_t* rowmax, int8_t* q,
                                                  int ldq, float* s) {
   asm volatile("griddepcontrol.launch_dependents;");  // the next GEMV may start streaming weights
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int row = blockIdx.y;
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  const double sc = quant_scale(__uint_as_float(rowmax[row]));
+  const double sc = quant_scale(__uint_as_float(rowmax[row])), rsc = __drcp_rn(sc);
   if (blockIdx.x == 0 && threadIdx.x == 0) s[row] = __double2float_rn(sc);
-  if (j < ldq) q[(int64_t)row * ldq + j] = j < cols ? dc_quant_div((double)x[row * ldx + j], sc, __drcp_rn(sc)) : (int8_t)0;
+#pragma unroll 4
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < ldq; j += gridDim.x * blockDim.x)
+    q[(int64_t)row * ldq + j] = j < cols ? dc_quant_div((double)x[row * ldx + j], sc, rsc) : (int8_t)0;
 }
 
 
@@ -1978,7 +2353,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
   S->ldC = round_up(S->C, 16);
   S->ldQ = round_up(S->qDim, 16);
   S->ldI = round_up(S->I, 16);
-  S->ldp = round_up(max_pos, 16);
+  S->ldp = round_up(max_pos, 64);
   int rc = DC_OK;
   auto fail = [&](int r) {
     dc_stage_free(S);
@@ -2357,6 +2732,17 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   // (head, 32 channels) from shared-memory copies of the value and probability rows
   const size_t ctx_smem = (size_t)(32 + 16) * S->ldp;
   const bool split_ctx = split_ctx_ok(S);
+  // a pass of several chunks: each chunk's attention by k_attn_chunk (a chunk's
+  // rows of one head per CTA) when there are CTAs enough for the SMs and its
+  // shared memory fits (16 score rows and 16 probability rows, beside ~24 KB of
+  // static shared memory)
+  auto ar_kernel = S->hd == 64 ? k_attn_chunk<64> : S->hd == 128 ? k_attn_chunk<128> : k_attn_chunk<256>;
+  const size_t ar_smem = 80 * (size_t)S->ldp;
+  const bool use_ar = multi && split_ctx && (S->hd == 64 || S->hd == 128 || S->hd == 256) &&
+                      ar_smem + 24 * 1024 <= 232448 && S->pass_attn != 2 &&
+                      (S->pass_attn == 1 || S->nH * cks->G >= ctx->sm_count / 2);
+  if (use_ar)
+    if (int rc0 = dc_set_smem(ctx, (const void*)ar_kernel, (int)ar_smem)) return rc0;
   if (split_ctx)
     if (int rc0 = dc_set_smem(ctx, (const void*)k_attn_ctx, (int)ctx_smem)) return rc0;
   const size_t nrm_smem = rms_smem(S->C);
@@ -2397,7 +2783,8 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                             dcl ? S->q8d : nullptr, S->qsd));
     dc_count_launch();
     if (multi) {
-      DC_CUDA(ctx, launch_dep(k_vscale_chunks, dim3((S->kvDim + 127) / 128), dim3(128), 0, st, (const float*)kv.v,
+      DC_CUDA(ctx, launch_dep(k_vscale_chunks, dim3((S->kvDim + 31) / 32), dim3(32 * DC_MAX_CHUNKS), 0, st,
+                              (const float*)kv.v,
                               kv.vmax, kv.vs, kv.vchg, S->kvDim, n0p, *cks, S->vsg, S->vchgg));
       dc_count_launch();
     } else if (T > 1) {
@@ -2407,7 +2794,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     if (dcl) {
     } else if (multi) {
-      DC_CUDA(ctx, launch_dep(k_vquant_chunks, dim3((N + 63) / 64, (S->kvDim + 31) / 32, cks->G), dim3(256), 0, st,
+      DC_CUDA(ctx, launch_dep(k_vquant_chunks, dim3((N + 63) / 64, (S->kvDim + 31) / 32), dim3(256), 0, st,
                               (const float*)kv.v, (const float*)kv.vs, (const int*)kv.vchg, kv.v8t, n0, S->kvDim, S->hd,
                               S->ldp, *cks, (const float*)S->vsg, S->v8s));
     } else if (T <= 8) {
@@ -2445,10 +2832,20 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                               S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, n0p, S->max_pos, S->ldp, dec_ch,
                               scale, S->ctxo, S->rowmax, S->att_done, S->xq, S->ldQ, S->rs, ctx->d_status));
       dc_count_launch();
+    } else if (use_ar) {
+      DC_CUDA(ctx, launch_dep(ar_kernel, dim3(S->nH, cks->G), dim3(AR_THREADS), ar_smem, st, (const float*)S->hbuf,
+                              S->nqkv, S->nH, S->nKV, (const int8_t*)kv.k8, (const float*)kv.ks,
+                              (const int8_t*)kv.v8t, (const float*)kv.vs, T, n0p, S->max_pos, S->ldp, scale,
+                              S->ctxo, S->qDim, S->rowmax, ctx->d_status, *cks, (const int8_t*)S->v8s,
+                              (const float*)S->vsg));
+      dc_count_launch();
+      DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, S->ldQ, T), T), dim3(256), 0, st, S->ctxo,
+                              (int64_t)S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ, S->rs));
+      dc_count_launch();
     } else if (split_ctx && (T <= 16 || multi)) {
-      DC_CUDA(ctx, launch_dep(k_attention, dim3(S->nH, T), dim3(ATT_THREADS), att_smem, st, S->hbuf, S->nqkv, S->nH,
-                              S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale, S->ctxo,
-                              S->rowmax, S->qDim, ctx->d_status, S->a8g, S->asg));
+      DC_CUDA(ctx, launch_dep(k_attention, dim3(S->nH, T), dim3(ATT_THREADS), att_smem, st, S->hbuf, S->nqkv,
+                              S->nH, S->nKV, S->hd, kv.k8, kv.ks, kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
+                              S->ctxo, S->rowmax, S->qDim, ctx->d_status, S->a8g, S->asg));
       dc_count_launch();
       DC_CUDA(ctx, launch_dep(k_attn_ctx, dim3(S->nH, S->hd / 32, multi ? cks->G : 1), dim3(256), ctx_smem, st,
                               (const int8_t*)S->a8g, (const float*)S->asg, (const int8_t*)kv.v8t,
@@ -2456,7 +2853,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                               S->rowmax, ctx->d_status, multi ? *cks : one, (const int8_t*)S->v8s,
                               (const float*)S->vsg));
       dc_count_launch();
-      DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldQ + 255) / 256, T), dim3(256), 0, st, S->ctxo,
+      DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, S->ldQ, T), T), dim3(256), 0, st, S->ctxo,
                               (int64_t)S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ, S->rs));
       dc_count_launch();
     } else {
@@ -2464,7 +2861,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                                                                 kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
                                                                 S->ctxo, S->rowmax, S->qDim, ctx->d_status);
       dc_count_launch();
-      k_rowquant<<<dim3((S->ldQ + 255) / 256, T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
+      k_rowquant<<<dim3(ew_blocks(ctx, S->ldQ, T), T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
                                                                 S->rs);
       dc_count_launch();
     }
@@ -2489,11 +2886,11 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     if (swg == DC_E_INVAL) {
       if ((rc = gemm(S, ly.gu, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
-      DC_CUDA(ctx, launch_dep(k_swiglu, dim3((S->I + 255) / 256, T), dim3(256), 0, st, S->hbuf, S->I, S->hmid,
+      DC_CUDA(ctx, launch_dep(k_swiglu, dim3(ew_blocks(ctx, S->I, T), T), dim3(256), 0, st, S->hbuf, S->I, S->hmid,
                               S->rowmax, ctx->d_status));
       dc_count_launch();
     }
-    DC_CUDA(ctx, launch_dep(k_rowquant, dim3((S->ldI + 255) / 256, T), dim3(256), 0, st, S->hmid, (int64_t)S->I,
+    DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, S->ldI, T), T), dim3(256), 0, st, S->hmid, (int64_t)S->I,
                             S->I, S->rowmax, S->xq, S->ldI, S->rs));
     dc_count_launch();
     if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, x, DC_F_ADDTO))) return rc;  // out = x2 + down
@@ -2596,6 +2993,12 @@ extern "C" int dc_stage_timeline_info(const dc_stage* S, int* kinds, double* byt
     if (bytes) bytes[i] = ctx->tl_bytes[i];
   }
   return n;
+}
+
+extern "C" int dc_stage_set_pass_attention(dc_stage* S, int mode) {
+  if (!S || mode < 0 || mode > 2) return DC_E_INVAL;
+  S->pass_attn = mode;
+  return DC_OK;
 }
 
 extern "C" int dc_stage_set_row_fusion(dc_stage* S, int on) {
@@ -2854,6 +3257,20 @@ extern "C" int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, in
   if (!ctx || rows < 0 || n < 0 || (rows && (!out || (n && !terms)))) return dc_fail(ctx, DC_E_INVAL, "ordered_sum: bad arguments");
   if (!rows) return DC_OK;
   k_ordered_sum<<<rows, 256, 0, ctx->stream>>>(terms, n, out);
+  dc_count_launch();
+  DC_CUDA(ctx, cudaGetLastError());
+  return DC_OK;
+}
+
+__global__ void k_exp(const double* __restrict__ x, int n, double* __restrict__ y, int nonpos) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = nonpos ? dcm::fdlibm_exp_nonpos(x[i]) : dcm::fdlibm_exp(x[i]);
+}
+
+extern "C" int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int nonpos) {
+  if (!ctx || n < 0 || (n && (!x || !y))) return dc_fail(ctx, DC_E_INVAL, "exp: bad arguments");
+  if (!n) return DC_OK;
+  k_exp<<<(n + 255) / 256, 256, 0, ctx->stream>>>(x, n, y, nonpos ? 1 : 0);
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;

@@ -242,6 +242,10 @@ class Stage:
         self._check(self.L.dc_stage_handoff(self.h, dst.h, _ptr(x), _ptr(out), T), "stage_handoff")
         return out
 
+    def set_pass_attention(self, mode: int) -> None:
+        """0: by size (default); 1: one CTA per (head, chunk) whenever it fits; 2: never."""
+        self._check(self.L.dc_stage_set_pass_attention(self.h, int(mode)), "set_pass_attention")
+
     def set_row_fusion(self, on: bool) -> None:
         """Decode rows with the norm / SwiGLU / row quantisation fused into their
         GEMVs, or as separate kernels (default); the results are identical."""

@@ -166,6 +166,10 @@ int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned fl
  *   its error bound); exact_sum = 1 always computes the serial-order sum
  *   instead -- both give the same bits. */
 int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double* out);
+/* dc_exp_dev: y[i] = Math.exp(x[i]) by the fdlibm method (infer.js:59, :192),
+ *   as the softmax and SiLU kernels compute it; nonpos = 1 takes the
+ *   branch-free form the attention kernels use for their arguments (x <= 0). */
+int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int nonpos);
 int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y,
                    int exact_sum);
 
@@ -231,6 +235,11 @@ int dc_stage_forward(dc_stage* stage, float* x, int T, int pos0, int use_kv);
  * chunks run one by one. */
 #define DC_MAX_CHUNKS 16
 int dc_stage_forward_chunks(dc_stage* stage, float* x, int T, int pos0, const int* rows, int nchunks);
+/* The attention kernel of a pass of several chunks: mode 0 (the default) one
+ * CTA per (head, chunk) for the chunk's rows when those CTAs fill half the SMs
+ * or more, else one CTA per (head, row) and one per (head, 32 channels);
+ * 1 the former whenever it fits, 2 never.  The results are identical. */
+int dc_stage_set_pass_attention(dc_stage* stage, int mode);
 /* A cached one-row forward (use_kv = 1, T = 1: a decode step of a pipeline
  * stage) runs as a CUDA graph of the stage's layers, captured on first use
  * (the default).  on = 0 launches the kernels one by one instead; the results

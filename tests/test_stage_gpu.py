@@ -303,19 +303,22 @@ def test_chunk_passes_match_oracle(comp, O, P, cfg):
             x = om.run_layers(om.embed_rows(ids[ch["lo"]:ch["hi"]]), 0, L, kv[0], ch["lo"])
             want_rows.append(x)
         want = np.concatenate(want_rows)
-        st = make_stages(P, comp, spec, w, splits, max_rows=64, max_pos=96)
-        got = []
-        for lo, hi, rows in P.shard.chunk_passes(chunks, per_pass):
-            got.append(P.infer.run_ring(st, st[0].embed_rows(ids[lo:hi]), lo, rows).cpu().numpy())
-        comp.sync()
-        case = (chunk, per_pass, splits)
-        assert np.concatenate(got).tobytes() == want.tobytes(), case
-        k8, ks, v = st[-1].kv_read(L - 1)
-        _, vf = kv[0].read(L - 1)
-        assert v.tobytes() == vf.tobytes(), case
-        assert st[-1].kv_len() == len(ids), case
         ref = O.generate_chunked(om, [(0, L)], ids, 6, chunk)
-        assert P.infer.generate_chunked(st, ids, 6, chunk, per_pass=per_pass) == ref, case
+        for mode in (1, 2):  # the pass's attention by (head, chunk) CTAs, or by (head, row) CTAs
+            st = make_stages(P, comp, spec, w, splits, max_rows=64, max_pos=96)
+            for S in st:
+                S.set_pass_attention(mode)
+            got = []
+            for lo, hi, rows in P.shard.chunk_passes(chunks, per_pass):
+                got.append(P.infer.run_ring(st, st[0].embed_rows(ids[lo:hi]), lo, rows).cpu().numpy())
+            comp.sync()
+            case = (chunk, per_pass, splits, mode)
+            assert np.concatenate(got).tobytes() == want.tobytes(), case
+            k8, ks, v = st[-1].kv_read(L - 1)
+            _, vf = kv[0].read(L - 1)
+            assert v.tobytes() == vf.tobytes(), case
+            assert st[-1].kv_len() == len(ids), case
+            assert P.infer.generate_chunked(st, ids, 6, chunk, per_pass=per_pass) == ref, case
 
 
 def test_chunk_pass_argument_checks(comp, P, fixture):
