@@ -75,19 +75,20 @@ __device__ inline double fdlibm_exp(double x) {
   return __dmul_rn(__longlong_as_double(by + (long long)(k + 1000) * 4503599627370496LL), twom1000);
 }
 
-// fdlibm_exp for x <= 0 (finite), without branches: the reduction
-// k = (int)(x / ln2 - 1/2), hi = x - k ln2hi, lo = k ln2lo is fdlibm's general
-// one, and for 0.5 ln2 < |x| < 1.5 ln2 it yields exactly the k = -1, hi =
-// x + ln2hi, lo = -ln2lo of fdlibm's special case (k*ln2hi and k*ln2lo are
-// exact); for |x| up to fdlibm's k = 0 bound (high word 0x3fd62e42) k is set
-// to 0, where hi = x, lo = 0 and the rebuilt 1 - ((0 - xc/(2-c)) - x) equals
-// fdlibm's 1 - (xc/(c-2) - x) bit for bit (negation is exact).  Tiny |x|
-// (1 + x), results below the underflow threshold (+0) and the subnormal
-// scaling are selected, not branched to.  Equal to fdlibm_exp for every
-// finite x <= 0 (checked on the device against it).
-__device__ __forceinline__ double fdlibm_exp_nonpos(double x) {
+// fdlibm_exp without branches (selects only), for the kernels that evaluate
+// it over many arguments side by side.  The reduction k = (int)(x/ln2 +- 1/2),
+// hi = x - k ln2hi, lo = k ln2lo is fdlibm's general one; for 0.5 ln2 < |x| <
+// 1.5 ln2 it yields exactly the k = +-1, hi = x -+ ln2hi, lo = +-ln2lo of
+// fdlibm's special case (k*ln2hi and k*ln2lo are exact); up to fdlibm's k = 0
+// bound (high word 0x3fd62e42) k is set to 0, where hi = x, lo = 0 and the
+// rebuilt 1 - ((0 - xc/(2-c)) - x) equals fdlibm's 1 - (xc/(c-2) - x) bit for
+// bit (negation is exact).  Tiny |x| (1 + x), overflow (+inf), underflow (+0),
+// the subnormal scaling and non-finite arguments are selected.  Equal to
+// fdlibm_exp for every argument (checked on the device against it).
+__device__ __forceinline__ double fdlibm_exp_sel(double x) {
   const double one = 1.0;
   const double twom1000 = b2d(0x0170000000000000ULL);
+  const double o_threshold = b2d(0x40862E42FEFA39EFULL);
   const double u_threshold = b2d(0xC0874910D52D3051ULL);
   const double ln2HI0 = b2d(0x3FE62E42FEE00000ULL);
   const double ln2LO0 = b2d(0x3DEA39EF35793C76ULL);
@@ -95,9 +96,12 @@ __device__ __forceinline__ double fdlibm_exp_nonpos(double x) {
   const double P1 = b2d(0x3FC555555555553EULL), P2 = b2d(0xBF66C16C16BEBD93ULL),
                P3 = b2d(0x3F11566AAF25DE2CULL), P4 = b2d(0xBEBBBD41C5D26BF1ULL),
                P5 = b2d(0x3E66376972BEA4D0ULL);
-  const uint32_t hx = (uint32_t)((uint64_t)__double_as_longlong(x) >> 32) & 0x7fffffffu;
-  const int kg = (int)__dadd_rn(__dmul_rn(invln2, x), -0.5);  // truncation toward zero, as (int) in C
-  const int k = hx > 0x3fd62e42u ? kg : 0;
+  const uint64_t bx = (uint64_t)__double_as_longlong(x);
+  const uint32_t hx = (uint32_t)(bx >> 32) & 0x7fffffffu;
+  const bool neg = (bx >> 63) != 0;
+  // (clamped so that the conversion is defined for every argument)
+  const double kd = __dadd_rn(__dmul_rn(invln2, fmin(fmax(x, -800.0), 800.0)), neg ? -0.5 : 0.5);
+  const int k = hx > 0x3fd62e42u ? (int)kd : 0;  // truncation toward zero, as (int) in C
   const double t = (double)k;
   const double hi = __dsub_rn(x, __dmul_rn(t, ln2HI0));
   const double lo = __dmul_rn(t, ln2LO0);
@@ -114,14 +118,16 @@ __device__ __forceinline__ double fdlibm_exp_nonpos(double x) {
   const double ys = __dmul_rn(__longlong_as_double(by + (long long)(k + 1000) * 4503599627370496LL), twom1000);
   double res = k >= -1021 ? yn : ys;
   res = hx < 0x3e300000u ? __dadd_rn(one, x) : res;
-  return x < u_threshold ? 0.0 : res;
+  res = x < u_threshold ? 0.0 : res;
+  res = x > o_threshold ? __longlong_as_double(0x7ff0000000000000LL) : res;
+  return hx >= 0x7ff00000u ? (isnan(x) ? __dadd_rn(x, x) : (neg ? 0.0 : x)) : res;
 }
 
 // infer.js:59 + :212: f32(silu(g) * u) with silu(v) = v / (1 + exp(-v)) in
 // double and the exp above.
 __device__ __forceinline__ float swiglu_f32(float gf, float uf) {
   const double v = gf;
-  const double sl = __ddiv_rn(v, __dadd_rn(1.0, fdlibm_exp(-v)));
+  const double sl = __ddiv_rn(v, __dadd_rn(1.0, fdlibm_exp_sel(-v)));
   return __double2float_rn(__dmul_rn(sl, (double)uf));
 }
 

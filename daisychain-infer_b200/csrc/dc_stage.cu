@@ -612,21 +612,17 @@ __global__ void k_vscale(const uint32_t* vmax, float* vs, int* vchg,
 // channels (from cb) on 256 threads (32 channels x 8 rows), transposed through
 // shared memory.
 __device__ __forceinline__ void vquant_tile(const float* vcache, const float* vs, const int* vchg, int8_t* v8t,
-                                            int N, int n0, int kvDim, int hd, int ldp, int jb, int cb,
-                                            const float* vfin = nullptr) {
+                                            int N, int n0, int kvDim, int hd, int ldp, int jb, int cb) {
   __shared__ int8_t tile[32][65];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int c = cb + tx;
   const bool cval = c < kvDim;
-  // vfin (a pass buffer): only the channels whose scale differs from vfin's,
-  // every row; otherwise new rows always and older rows in moved channels
-  const bool chg = cval && (vfin ? vs[c] != vfin[c] : vchg[c] != 0);
-  if (vfin && !__any_sync(0xffffffffu, chg)) return;  // (every warp holds the same channels)
+  const bool chg = cval && vchg[c] != 0;
   const double sc = cval ? (double)vs[c] : 1.0, rsc = __drcp_rn(sc);
   for (int r = ty; r < 64; r += 8) {
     const int j = jb + r;
     int8_t v = 0;
-    if (cval && j < N && (vfin ? chg : (j >= n0 || chg))) v = dc_quant_div((double)vcache[(int64_t)j * kvDim + c], sc, rsc);
+    if (cval && j < N && (j >= n0 || chg)) v = dc_quant_div((double)vcache[(int64_t)j * kvDim + c], sc, rsc);
     tile[tx][r] = v;
   }
   __syncthreads();
@@ -634,7 +630,7 @@ __device__ __forceinline__ void vquant_tile(const float* vcache, const float* vs
     const int cl = idx >> 6, r = idx & 63;
     const int cc = cb + cl, j = jb + r;
     if (cc >= kvDim || j >= N) continue;
-    if (vfin ? vs[cc] == vfin[cc] : (j < n0 && !vchg[cc])) continue;  // rows that keep their int8 values
+    if (j < n0 && !vchg[cc]) continue;  // an unchanged channel keeps its int8 rows
     const int g = cc / hd, ch = cc - g * hd;
     v8t[((int64_t)g * hd + ch) * ldp + j] = tile[cl][r];
   }
@@ -702,62 +698,38 @@ __global__ void __launch_bounds__(32 * DC_MAX_CHUNKS) k_vscale_chunks(const floa
   vchg[c] = chg;
 }
 
-// The int8 values each chunk of a pass attends with: the last chunk's into the
-// cache (its new rows, and older rows in channels whose scale moved), as
-// k_vquant; for chunk g < G-1, the channels whose scale at the chunk's end is
-// not the final one into the pass buffer v8s[g] (every row up to the chunk's
-// end) -- in every other channel the cache's int8 rows are chunk g's.  grid
-// (ceil(N/64), ceil(kvDim/32)), block 256 (32 channels x 8 rows): each block
-// reads its 64 x 32 tile of values once and writes it for every chunk that
-// needs it (transposed through shared memory).
+// The int8 values each chunk of a pass attends with.  Blocks below `ntiles`:
+// the last chunk's into the cache (its new rows, and older rows in channels
+// whose scale moved), one 64-row x 32-channel tile each, as k_vquant.  The
+// blocks after them: chunk g < G-1 (blockIdx / 8 ... ) for 8 channels, one
+// warp per channel: a channel whose scale at chunk g's end is not the final
+// one gets chunk g's int8 row (every position up to the chunk's end) in the
+// pass buffer v8s[g]; every other channel of chunk g reads the cache's rows,
+// so its warp returns at once.  grid ntiles + (G - 1) * ceil(kvDim / 8), 256
+// threads.
 __global__ void __launch_bounds__(256) k_vquant_chunks(const float* vcache, const float* vs, const int* vchg,
                                                        int8_t* v8t, int n0, int kvDim, int hd, int ldp,
-                                                       ChunkSet cks, const float* vsg, int8_t* v8s) {
+                                                       ChunkSet cks, const float* vsg, int8_t* v8s, int ntiles) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
-  __shared__ int8_t tile[32][65];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int cb = blockIdx.y * 32, jb = blockIdx.x * 64;
-  const int c = cb + tx;
-  const bool cval = c < kvDim;
   const int N = n0 + cks.end[cks.G - 1];
-  float v[8];
-#pragma unroll
-  for (int u = 0; u < 8; u++) {
-    const int j = jb + ty + 8 * u;
-    v[u] = cval && j < N ? __ldcg(vcache + (int64_t)j * kvDim + c) : 0.0f;
+  const int b = blockIdx.x;
+  if (b < ntiles) {
+    const int nrt = (N + 63) / 64;
+    vquant_tile(vcache, vs, vchg, v8t, N, n0, kvDim, hd, ldp, (b % nrt) * 64, (b / nrt) * 32);
+    return;
   }
-  const float fin = cval ? vs[c] : 1.0f;
-#pragma unroll 1
-  for (int g = 0; g < cks.G; g++) {
-    const bool last = g == cks.G - 1;
-    const int Ng = n0 + cks.end[g];
-    if (jb >= Ng) continue;  // (block-uniform)
-    const float sg = last ? fin : (cval ? vsg[(int64_t)g * kvDim + c] : fin);
-    // the channels this chunk writes: all (new rows) and moved ones (older rows)
-    // for the cache; those whose scale is not the final one for a pass buffer
-    const bool chg = cval && (last ? vchg[c] != 0 : sg != fin);
-    const bool any_new = last && jb + 64 > n0;
-    if (!any_new && !__any_sync(0xffffffffu, chg)) continue;  // (every warp holds the same channels)
-    const double sc = (double)sg, rsc = __drcp_rn(sc);
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const int j = jb + ty + 8 * u;
-      int8_t q = 0;
-      if (cval && j < Ng && (chg || (last && j >= n0))) q = dc_quant_div((double)v[u], sc, rsc);
-      tile[tx][ty + 8 * u] = q;
-    }
-    __syncthreads();
-    int8_t* dst = last ? v8t : v8s + (int64_t)g * kvDim * ldp;
-    for (int idx = threadIdx.x; idx < 32 * 64; idx += blockDim.x) {
-      const int cl = idx >> 6, r = idx & 63;
-      const int cc = cb + cl, j = jb + r;
-      if (cc >= kvDim || j >= Ng) continue;
-      const bool wr = last ? (j >= n0 || vchg[cc] != 0) : (vsg[(int64_t)g * kvDim + cc] != vs[cc]);
-      if (wr) dst[(int64_t)cc * ldp + j] = tile[cl][r];
-    }
-    __syncthreads();
-  }
+  const int cgroups = (kvDim + 7) / 8;
+  const int g = (b - ntiles) / cgroups;
+  const int c = ((b - ntiles) % cgroups) * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (c >= kvDim) return;
+  const float sg = vsg[(int64_t)g * kvDim + c];
+  if (sg == vs[c]) return;  // (warp-uniform)
+  const int Ng = n0 + cks.end[g];
+  const double sc = (double)sg, rsc = __drcp_rn(sc);
+  int8_t* dst = v8s + ((int64_t)g * kvDim + c) * ldp;
+#pragma unroll 4
+  for (int j = lane; j < Ng; j += 32) dst[j] = dc_quant_div((double)__ldcg(vcache + (int64_t)j * kvDim + c), sc, rsc);
 }
 
 // The tiled quantisation for short chunks and decode steps, reading the cache
@@ -881,7 +853,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 4) k_attention(const float* h, in
   m = block_max_d(m, redd);
   // 4. e_j and its f32 copy
   for (int j = threadIdx.x; j <= see; j += blockDim.x) {
-    const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(__dmul_rn((double)af[j], scale), m));
+    const double e = dcm::fdlibm_exp_sel(__dsub_rn(__dmul_rn((double)af[j], scale), m));
     ed[j] = e;
     af[j] = __double2float_rn(e);
   }
@@ -1117,7 +1089,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
     double part = 0.0, wpart = 0.0;
 #pragma unroll 4
     for (int j = lane; j < n; j += 32) {
-      const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(__dmul_rn((double)Sr[j], scale), m));
+      const double e = dcm::fdlibm_exp_sel(__dsub_rn(__dmul_rn((double)Sr[j], scale), m));
       Sr[j] = __double2float_rn(e);
       part += e;
       wpart += (double)(n - j) * e;
@@ -1164,7 +1136,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
       int acc = 0;
 #pragma unroll
       for (int cc = 0; cc < HD / 16; cc++) acc = dp4a16(kr[cc], q4[cc], acc);
-      eb[j] = dcm::fdlibm_exp_nonpos(__dsub_rn(__dmul_rn((double)dc_epi(acc, qsf[i], ksg[j]), scale), m));
+      eb[j] = dcm::fdlibm_exp_sel(__dsub_rn(__dmul_rn((double)dc_epi(acc, qsf[i], ksg[j]), scale), m));
     }
     __syncthreads();
     const double z = ordered_sum_cold16(eb, ni, osm);
@@ -1481,7 +1453,7 @@ __global__ void __launch_bounds__(256) k_attention_dec(const float* h, int nqkv,
     m = block_max_d(m, redd);
 #pragma unroll 1
     for (int j = tid; j < N; j += 256) {
-      const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(xs[j], m));
+      const double e = dcm::fdlibm_exp_sel(__dsub_rn(xs[j], m));
       xs[j] = e;
       af[j] = __double2float_rn(e);
     }
@@ -1753,7 +1725,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < N) {
-      const double e = dcm::fdlibm_exp_nonpos(__dsub_rn(xs[j], m));
+      const double e = dcm::fdlibm_exp_sel(__dsub_rn(xs[j], m));
       xs[j] = e;
       af[j] = __double2float_rn(e);
       part += e;
@@ -1951,13 +1923,23 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* ho
   const float2* g = (const float2*)(h + (int64_t)row * 2 * I);
   float mx = 0.0f;
   bool bad = false;
-#pragma unroll 4
-  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < I; j += gridDim.x * blockDim.x) {
-    const float2 gu = g[j];
-    const float y = swiglu_f32(gu.x, gu.y);
-    bad |= !isfinite(y);
-    hout[(int64_t)row * I + j] = y;
-    mx = fmaxf(mx, fabsf(y));
+  // eight elements per thread at a time: their loads in flight together, then
+  // their (independent) double-precision chains side by side
+  const int stride = gridDim.x * blockDim.x;
+  for (int j0 = blockIdx.x * blockDim.x + threadIdx.x; j0 < I; j0 += 8 * stride) {
+    float2 gu[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) gu[u] = j0 + u * stride < I ? g[j0 + u * stride] : make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int j = j0 + u * stride;
+      if (j < I) {
+        const float y = swiglu_f32(gu[u].x, gu[u].y);
+        bad |= !isfinite(y);
+        hout[(int64_t)row * I + j] = y;
+        mx = fmaxf(mx, fabsf(y));
+      }
+    }
   }
   mx = block_max_f(mx, red);
   if (threadIdx.x == 0) atomicMax(rowmax + row, __float_as_uint(mx));
@@ -2794,9 +2776,10 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     if (dcl) {
     } else if (multi) {
-      DC_CUDA(ctx, launch_dep(k_vquant_chunks, dim3((N + 63) / 64, (S->kvDim + 31) / 32), dim3(256), 0, st,
+      const int ntiles = ((N + 63) / 64) * ((S->kvDim + 31) / 32);
+      DC_CUDA(ctx, launch_dep(k_vquant_chunks, dim3(ntiles + (cks->G - 1) * ((S->kvDim + 7) / 8)), dim3(256), 0, st,
                               (const float*)kv.v, (const float*)kv.vs, (const int*)kv.vchg, kv.v8t, n0, S->kvDim, S->hd,
-                              S->ldp, *cks, (const float*)S->vsg, S->v8s));
+                              S->ldp, *cks, (const float*)S->vsg, S->v8s, ntiles));
     } else if (T <= 8) {
       DC_CUDA(ctx, launch_dep(k_vquant_dev, dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), dim3(256), 0, st,
                               kv.v, kv.vs, kv.vchg, kv.v8t, T, n0p, S->kvDim, S->hd, S->ldp, T == 1 ? 1 : 0));
@@ -3262,15 +3245,15 @@ extern "C" int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, in
   return DC_OK;
 }
 
-__global__ void k_exp(const double* __restrict__ x, int n, double* __restrict__ y, int nonpos) {
+__global__ void k_exp(const double* __restrict__ x, int n, double* __restrict__ y, int sel) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = nonpos ? dcm::fdlibm_exp_nonpos(x[i]) : dcm::fdlibm_exp(x[i]);
+  if (i < n) y[i] = sel ? dcm::fdlibm_exp_sel(x[i]) : dcm::fdlibm_exp(x[i]);
 }
 
-extern "C" int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int nonpos) {
+extern "C" int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int sel) {
   if (!ctx || n < 0 || (n && (!x || !y))) return dc_fail(ctx, DC_E_INVAL, "exp: bad arguments");
   if (!n) return DC_OK;
-  k_exp<<<(n + 255) / 256, 256, 0, ctx->stream>>>(x, n, y, nonpos ? 1 : 0);
+  k_exp<<<(n + 255) / 256, 256, 0, ctx->stream>>>(x, n, y, sel ? 1 : 0);
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;

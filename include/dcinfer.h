@@ -166,10 +166,10 @@ int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned fl
  *   its error bound); exact_sum = 1 always computes the serial-order sum
  *   instead -- both give the same bits. */
 int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double* out);
-/* dc_exp_dev: y[i] = Math.exp(x[i]) by the fdlibm method (infer.js:59, :192),
- *   as the softmax and SiLU kernels compute it; nonpos = 1 takes the
- *   branch-free form the attention kernels use for their arguments (x <= 0). */
-int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int nonpos);
+/* dc_exp_dev: y[i] = Math.exp(x[i]) by the fdlibm method (infer.js:59, :192):
+ *   sel = 0 its branching form, sel = 1 the branch-free form the softmax and
+ *   SiLU kernels evaluate (the same bits for every argument). */
+int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int sel);
 int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y,
                    int exact_sum);
 

@@ -121,46 +121,48 @@ def test_rmsnorm_many_rows_matches_oracle(comp, O):
 
 
 def exp_inputs():
-    """Arguments of the softmax's exp (x <= 0) across every branch of the
-    fdlibm method: tiny, the k = 0 and k = -1 ranges and their high-word
-    bounds (0x3fd62e42, 0x3ff0a2b2) from both sides, the general reduction,
-    the subnormal results (k < -1021) and the underflow threshold."""
+    """Arguments across every branch of the fdlibm method, both signs: tiny,
+    the k = 0 and k = +-1 ranges and their high-word bounds (0x3fd62e42,
+    0x3ff0a2b2) from both sides, the general reduction, subnormal results
+    (k < -1021), the underflow and overflow thresholds, and non-finite
+    values; plus the ranges the softmax (x <= 0) and SiLU (exp(-v)) take."""
     import struct
     rng = np.random.default_rng(5)
 
     def hw(h, lo=0):
         return struct.unpack("<d", struct.pack("<Q", (h << 32) | lo))[0]
 
-    edges = [0.0, -0.0, -1e-300, -2.0 ** -30, -2.0 ** -28, -hw(0x3e300000), -hw(0x3e2fffff, 0xffffffff),
-             -hw(0x3fd62e42), -hw(0x3fd62e42, 0xffffffff), -hw(0x3fd62e43), -hw(0x3fd62e42, 0xfefa39ef),
-             -hw(0x3ff0a2b1, 0xffffffff), -hw(0x3ff0a2b2), -hw(0x3ff0a2b2, 0x3f3bab73), -0.5 * np.log(2),
-             -1.5 * np.log(2), -np.log(2), -700.0, -707.7, -708.39, -708.4, -709.78, -709.79, -730.0, -745.13,
-             -745.1332191019411, -745.1332191019412, -745.14, -800.0, -1e300]
+    mag = [1e-300, 2.0 ** -30, 2.0 ** -28, hw(0x3e300000), hw(0x3e2fffff, 0xffffffff), hw(0x3fd62e42),
+           hw(0x3fd62e42, 0xffffffff), hw(0x3fd62e43), hw(0x3fd62e42, 0xfefa39ef), hw(0x3ff0a2b1, 0xffffffff),
+           hw(0x3ff0a2b2), hw(0x3ff0a2b2, 0x3f3bab73), 0.5 * np.log(2), 1.5 * np.log(2), np.log(2), 700.0,
+           707.7, 708.39, 708.4, 709.78, hw(0x40862E42, 0xFEFA39EF), 709.79, 730.0, 745.13,
+           745.1332191019411, 745.1332191019412, 745.14, 800.0, 1e300]
+    edges = [0.0, -0.0] + [m * s for m in mag for s in (1.0, -1.0)]
     near = []
-    for e in edges[3:]:
-        for k in range(-3, 4):
-            near.append(np.nextafter(e, 0.0) if k > 0 else e)
-            e = np.nextafter(e, -np.inf) if k < 0 else e
-    xs = np.concatenate([np.array(edges + near, np.float64), -rng.exponential(3.0, 20000),
-                         rng.uniform(-750, 0, 20000), -rng.uniform(0, 0.4, 5000), -rng.uniform(0.3, 1.1, 5000),
-                         -np.abs(rng.standard_normal(5000)) * 1e-9])
+    for e in edges[2:]:
+        for d in range(1, 4):
+            near += [e + d * np.spacing(e), e - d * np.spacing(e)]
+    special = [np.inf, -np.inf, np.nan]
+    xs = np.concatenate([np.array(edges + near + special, np.float64), -rng.exponential(3.0, 20000),
+                         rng.uniform(-750, 750, 20000), rng.uniform(-1.1, 1.1, 10000),
+                         rng.standard_normal(10000) * 1e-9, rng.standard_normal(10000) * 4])
     return xs
 
 
 def test_exp_branch_free_equals_fdlibm_and_oracle(comp, O):
-    """The attention kernels' branch-free exp (arguments <= 0) gives the bits
-    of the fdlibm-method exp on the device, and both the oracle's exp."""
+    """The kernels' branch-free exp gives the bits of the branching fdlibm
+    method on the device for every argument, and both the oracle's exp."""
     import torch
     xs = exp_inputs()
     x = torch.tensor(xs, dtype=torch.float64, device="cuda")
     y0 = torch.empty_like(x)
     y1 = torch.empty_like(x)
-    comp.exp_dev(x, xs.size, y0, nonpos=False)
-    comp.exp_dev(x, xs.size, y1, nonpos=True)
+    comp.exp_dev(x, xs.size, y0, sel=False)
+    comp.exp_dev(x, xs.size, y1, sel=True)
     comp.sync()
     a, b = y0.cpu().numpy(), y1.cpu().numpy()
-    bad = np.nonzero(a.view(np.uint64) != b.view(np.uint64))[0]
+    bad = np.nonzero((a.view(np.uint64) != b.view(np.uint64)) & ~(np.isnan(a) & np.isnan(b)))[0]
     assert bad.size == 0, [(xs[i], a[i], b[i]) for i in bad[:5]]
     want = np.array([O.exp(float(v)) for v in xs])
-    bad = np.nonzero(a.view(np.uint64) != want.view(np.uint64))[0]
+    bad = np.nonzero((a.view(np.uint64) != want.view(np.uint64)) & ~(np.isnan(a) & np.isnan(want)))[0]
     assert bad.size == 0, [(xs[i], a[i], want[i]) for i in bad[:5]]
