@@ -52,11 +52,11 @@ L2_BYTES = 126 * 1024 * 1024
 WORKLOADS = {
     "llama3-8b-chunked": dict(spec=dict(hidden=4096, layers=32, heads=32, kvHeads=8, inter=14336, vocab=128256,
                                         ropeTheta=500000.0, tie=False),
-                              mode="chunked", prompt=2048, new=256, chunk=16, window=2, per_pass=16,
+                              mode="chunked", prompt=2048, new=256, chunk=16, window=2, per_pass=32,
                               name="Llama-3-8B-shaped decoder"),
     "tinyllama-chunked": dict(spec=dict(hidden=2048, layers=22, heads=32, kvHeads=4, inter=5632, vocab=32000,
                                         ropeTheta=10000.0, tie=False),
-                              mode="chunked", prompt=512, new=128, chunk=16, window=2, per_pass=16,
+                              mode="chunked", prompt=512, new=128, chunk=16, window=2, per_pass=32,
                               name="TinyLlama-1.1B-shaped decoder"),
     "smollm-135m-window": dict(spec=dict(hidden=576, layers=30, heads=9, kvHeads=3, inter=1536, vocab=49152,
                                          ropeTheta=10000.0, tie=True),

@@ -174,6 +174,19 @@ __device__ __forceinline__ int8_t dc_quant_div(double v, double s, double rs) {
   return dc_clamp8(dc_js_round(q));
 }
 
+// dc_quant_div for an f32 value v with |v / s| <= 128, mostly in f32: the
+// product v * rsf (rsf = f32(1/s)) is within 2^-16 of v / s, so when it lies
+// more than 2^-13 from a half-integer it rounds as the quotient does; nearer,
+// the double path decides.
+__device__ __forceinline__ int8_t dc_quant_div_f(float v, double s, double rs, float rsf) {
+  const float q = __fmul_rn(v, rsf);
+  const float fl = floorf(q);
+  const float fr = __fsub_rn(q, fl);
+  if (fabsf(__fsub_rn(fr, 0.5f)) < 1.220703125e-4f) return dc_quant_div((double)v, s, rs);
+  const float r = fr > 0.5f ? __fadd_rn(fl, 1.0f) : fl;
+  return r < -128.0f ? (int8_t)-128 : r > 127.0f ? (int8_t)127 : (int8_t)(int)r;
+}
+
 // f32(a / z) for a >= 0, z > 0 (the double quotient rounded to float): from
 // a * rz (rz = 1/z, any rounding) unless that lies within 2^-40 (relative) of
 // a midpoint between two floats, or at a power of two or below the normal
@@ -193,23 +206,23 @@ __device__ __forceinline__ float dc_div_to_f32(double a, double z, double rz) {
 // f32(a / zlo) for the lower end of a bracket [zlo, zhi] that holds a serial
 // sum z (a >= 0, rlo = 1/zlo and rhi = 1/zhi in any rounding), and in *amb
 // whether f32(a / z) may differ across the bracket.  `narrow` says the bracket
-// is below 5e-13 relative: then a quotient a * rlo that dc_div_to_f32 finds
-// clear of every f32 rounding boundary (by its 2^-40 relative margin, beyond
-// the bracket's width and the product's rounding) rounds the same way for
-// every z in the bracket, and only the quotients near a boundary take both
-// ends.  The result is dc_div_to_f32(a, zlo, rlo) in every case.
+// is below 5e-13 relative: then a quotient a * rlo clear of every f32
+// rounding boundary (by a margin beyond the bracket's width and the product's
+// rounding) rounds the same way for every z in the bracket, and only the
+// quotients near a boundary take both ends.  The result is
+// dc_div_to_f32(a, zlo, rlo) in every case.
 __device__ __forceinline__ float dc_div_bracket(double a, double zlo, double rlo, double zhi, double rhi,
                                                 bool narrow, bool* amb) {
   const double q = __dmul_rn(a, rlo);
   const float f = __double2float_rn(q);
   const unsigned fb = __float_as_uint(f);
   const int fe = (int)((fb >> 23) & 0xff);
-  bool slow = fe <= 1 || fe >= 254 || (fb & 0x7fffff) == 0;
-  if (!slow) {
-    const double hu = __longlong_as_double((long long)(fe - 151 + 1023) << 52);  // half a float ulp at f
-    const double d = fabs(__dsub_rn(q, (double)f));
-    slow = fabs(__dsub_rn(d, hu)) < q * 9.094947017729282e-13;
-  }
+  // the 29 mantissa bits of q that the f32 rounding drops, against the
+  // midpoint 2^28: within 2^13 double ulps of it (a superset of within 2^-40
+  // relative) the quotient is near a rounding boundary; a bracket below 5e-13
+  // relative moves the quotient by under 2^12.2 ulps
+  const int low = (int)(__double_as_longlong(q) & 0x1fffffffLL);
+  const bool slow = fe <= 1 || fe >= 254 || (fb & 0x7fffff) == 0 || abs(low - 0x10000000) < 0x2000;
   if (!slow && narrow) return f;
   const float flo = slow ? __double2float_rn(dc_ddiv_slow(a, zlo)) : f;
   *amb |= flo != dc_div_to_f32(a, zhi, rhi);

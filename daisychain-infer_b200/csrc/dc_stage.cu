@@ -1086,13 +1086,15 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
     double m = wm[0][row];
 #pragma unroll
     for (int w = 1; w < 16; w++) m = fmax(m, wm[w][row]);
-    double part = 0.0, wpart = 0.0;
+    double part = 0.0;
+    float wpart = 0.0f;  // sum of (n - j) e_j: only the radius needs it, to well within its 1e-3 slack
 #pragma unroll 4
     for (int j = lane; j < n; j += 32) {
       const double e = dcm::fdlibm_exp_sel(__dsub_rn(__dmul_rn((double)Sr[j], scale), m));
-      Sr[j] = __double2float_rn(e);
+      const float ef = __double2float_rn(e);
+      Sr[j] = ef;
       part += e;
-      wpart += (double)(n - j) * e;
+      wpart = __fadd_rn(wpart, __fmul_rn((float)(n - j), ef));
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
@@ -1100,7 +1102,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
       wpart += __shfl_xor_sync(0xffffffffu, wpart, o);
     }
     // a term passes through at most ceil(n / 32) adds in its lane and 5 in the warp
-    const double hr = serial_sum_radius(part, wpart, (n + 31) / 32 + 10);
+    const double hr = serial_sum_radius(part, (double)wpart, (n + 31) / 32 + 10);
     const double zlo = part - hr, zhi = part + hr;
     const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
     const bool narrow = __dsub_rn(zhi, zlo) < 5e-13 * zlo;
@@ -1156,14 +1158,15 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
   const int Kc = (Nc + 63) & ~63;  // keys of the context's k-steps (ldp is a multiple of 64)
   if (row < Tc) {
     const double asc = quant_scale(amxs[row]), rasc = __drcp_rn(asc);
+    const float rascf = __double2float_rn(rasc);
     uint32_t* dst = (uint32_t*)(A8 + (size_t)row * ldp);
     for (int j4 = lane; j4 < (Kc >> 2); j4 += 32) {
       const float4 a = *(const float4*)(Sr + 4 * j4);
       const int j = 4 * j4;
-      const uint32_t b0 = j <= see ? (uint8_t)dc_quant_div((double)a.x, asc, rasc) : 0u;
-      const uint32_t b1 = j + 1 <= see ? (uint8_t)dc_quant_div((double)a.y, asc, rasc) : 0u;
-      const uint32_t b2 = j + 2 <= see ? (uint8_t)dc_quant_div((double)a.z, asc, rasc) : 0u;
-      const uint32_t b3 = j + 3 <= see ? (uint8_t)dc_quant_div((double)a.w, asc, rasc) : 0u;
+      const uint32_t b0 = j <= see ? (uint8_t)dc_quant_div_f(a.x, asc, rasc, rascf) : 0u;
+      const uint32_t b1 = j + 1 <= see ? (uint8_t)dc_quant_div_f(a.y, asc, rasc, rascf) : 0u;
+      const uint32_t b2 = j + 2 <= see ? (uint8_t)dc_quant_div_f(a.z, asc, rasc, rascf) : 0u;
+      const uint32_t b3 = j + 3 <= see ? (uint8_t)dc_quant_div_f(a.w, asc, rasc, rascf) : 0u;
       dst[j4] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
     }
     if (lane == 0) asf[row] = __double2float_rn(asc);

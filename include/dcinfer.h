@@ -233,7 +233,7 @@ int dc_stage_forward(dc_stage* stage, float* x, int T, int pos0, int use_kv);
  * the value channel scales as of its own last row.  Chunks of up to 16 rows,
  * nchunks <= min(DC_MAX_CHUNKS, max_rows) share the weight pass; otherwise the
  * chunks run one by one. */
-#define DC_MAX_CHUNKS 16
+#define DC_MAX_CHUNKS 32
 int dc_stage_forward_chunks(dc_stage* stage, float* x, int T, int pos0, const int* rows, int nchunks);
 /* The attention kernel of a pass of several chunks: mode 0 (the default) one
  * CTA per (head, chunk) for the chunk's rows when those CTAs fill half the SMs

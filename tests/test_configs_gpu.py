@@ -160,10 +160,10 @@ def test_bench_ring_matches_oracle(comp, P):
     """The benchmark's own call (pipeline.Ring, one GPU, two chunks in flight,
     decode laps as CUDA graphs) on the Llama-3-8B model gives the oracle's ids."""
     g = load(os.path.join(GOLDEN, "llama3-8b-chunked.json"))
-    spec, stages = build(P, comp, g, [(0, g["spec"]["layers"])], per_pass=16)
+    spec, stages = build(P, comp, g, [(0, g["spec"]["layers"])], per_pass=32)
     try:
         ring = P.pipeline.Ring(stages[0], 0, 1, spec.hidden)
-        for per_pass in (1, 16, 16):  # the last run reuses the captured graphs
+        for per_pass in (1, 32, 32):  # the last run reuses the captured graphs
             picks = ring.generate_chunked(g["prompt"], g["new"], g["chunk"], 2, per_pass=per_pass)
             assert picks[:g["new"]].cpu().tolist() == g["generated"], per_pass
     finally:
