@@ -114,6 +114,7 @@ struct dc_stage {
   bool row_graph = true;
   bool row_fused = false;  // decode rows: GEMVs with the norm / SwiGLU / row quantisation fused
   int pass_attn = 0;       // a pass's attention: 0 k_attn_chunk when the CTAs fill the SMs, 1 always, 2 never
+  bool o_rowq = true;      // decode rows: the O projection quantises the context row itself (not the attention's last CTA)
   std::vector<dc_stage*> lap_key;
   int32_t* lap_picks = nullptr;
   std::vector<void*> allocs;
@@ -1836,11 +1837,21 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       const int c = __ffs(mask) - 1;
       const int gc = g * hd + c0 + c;
       const double sc = (double)vs[gc], rsc = __drcp_rn(sc);
+      // (eight strided loads of the column in flight per thread, then their quotients)
       #pragma unroll 1
-      for (int j = tid; j < n0; j += 256) {
-        const int8_t q = dc_quant_div((double)vcache[(int64_t)j * kvDim + gc], sc, rsc);
-        sV[(size_t)c * ldpv + j] = q;
-        if (writer) v8t[(int64_t)gc * ldp + j] = q;
+      for (int j0 = tid; j0 < n0; j0 += 8 * 256) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = j0 + 256 * u < n0 ? __ldcg(vcache + (int64_t)(j0 + 256 * u) * kvDim + gc) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const int j = j0 + 256 * u;
+          if (j < n0) {
+            const int8_t q = dc_quant_div((double)v[u], sc, rsc);
+            sV[(size_t)c * ldpv + j] = q;
+            if (writer) v8t[(int64_t)gc * ldp + j] = q;
+          }
+        }
       }
     }
     for (int c = tid; c < CH; c += 256) sV[(size_t)c * ldpv + n0] = v8t[((int64_t)g * hd + c0 + c) * ldp + n0];
@@ -1888,8 +1899,10 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     for (int w = 1; w < 8; w++) v = fmaxf(v, x_cmax[w]);
     atomicMax(rowmax, __float_as_uint(v));
   }
-  // the last CTA to finish quantises the whole context row (quantizeRows) for
-  // the O projection, then re-arms the counter
+  // without xq the O projection quantises the context row from the row
+  // maximum itself; otherwise the last CTA to finish quantises it
+  // (quantizeRows), then re-arms the counter
+  if (!xq) return;
   __shared__ int is_last;
   __threadfence();
   __syncthreads();
@@ -2739,6 +2752,10 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
   if (int rc0 = dc_set_smem(ctx, (const void*)norm_k, (int)nrm_smem)) return rc0;
   // a decode row: GEMVs with the norms, the SwiGLU and the row quantisation fused
   const bool fuse = T == 1 && use_kv && dec_ch && S->row_fused && fg_fits(S);
+  // a decode row's O projection through the fused GEMV that quantises its input row
+  const bool o_rowq = T == 1 && use_kv && dec_ch && S->o_rowq && fg_smem(FG_ROWQ, S->qDim) + 24 * 1024 <= 232448;
+  if (o_rowq)
+    if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_ROWQ>, (int)fg_smem(FG_ROWQ, S->qDim))) return rc0;
   if (fuse) {
     if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM>, (int)fg_smem(FG_NORM, S->C))) return rc0;
     if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM | FG_SWIGLU>, (int)fg_smem(FG_NORM, S->C)))
@@ -2809,8 +2826,9 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       cfg.numAttrs = 2;
       DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_attention_dcl, (const float*)S->hbuf, S->nqkv, S->nH, S->nKV, S->hd,
                                       (const int8_t*)kv.k8, (const float*)kv.ks, kv.v8t, (const float*)kv.vs, n0p,
-                                      S->max_pos, S->ldp, dec_ch, scale, S->ctxo, S->rowmax, S->att_done, S->xq,
-                                      S->ldQ, S->rs, ctx->d_status, (const float*)kv.v, (const int*)kv.vchg,
+                                      S->max_pos, S->ldp, dec_ch, scale, S->ctxo, S->rowmax, S->att_done,
+                                      o_rowq ? nullptr : S->xq, S->ldQ, S->rs, ctx->d_status, (const float*)kv.v,
+                                      (const int*)kv.vchg,
                                       (const int8_t*)S->q8d, (const float*)S->qsd));
       dc_count_launch();
     } else if (T == 1 && use_kv && dec_ch) {
@@ -2851,7 +2869,12 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                                                                 S->rs);
       dc_count_launch();
     }
-    if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, x, DC_F_ADDTO))) return rc;  // x2 = x + attn
+    if (dcl && o_rowq) {  // x2 = x + attn, the context row quantised by the GEMV's blocks
+      DC_CUDA(ctx, launch_fused(S, FG_ROWQ, S->ctxo, S->qDim, nullptr, S->rowmax, ly.o, DC_F_ADDTO, x, nullptr,
+                                nullptr));
+    } else if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, x, DC_F_ADDTO))) {  // x2 = x + attn
+      return rc;
+    }
     // MLP block
     if (fuse) {  // RMSNorm + gate/up + SwiGLU; then the down projection quantises its own input
       DC_CUDA(ctx, launch_fused(S, FG_NORM | FG_SWIGLU, x, S->C, ly.nrm2, nullptr, ly.gu, 0, S->hmid, S->rowmax + 1,
