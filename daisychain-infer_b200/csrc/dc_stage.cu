@@ -53,6 +53,7 @@ struct dc_kv {
   int8_t* k8 = nullptr;   // [kvh][max_pos][hd] int8 keys (rotated)
   float* ks = nullptr;    // [kvh][max_pos] key scales (f32, quantizeCols rule)
   float* v = nullptr;     // [max_pos][kvDim] f32 values
+  float* vt = nullptr;    // [kvDim][ldvt] the same values channel-major (a channel's column re-quantises from it)
   int8_t* v8t = nullptr;  // [kvh][hd][ldp] int8 values (channel-major) under the current channel scales
   float* vs = nullptr;    // [kvDim] channel scales
   uint32_t* vmax = nullptr;  // [kvDim] running |v| maximum (float bits)
@@ -72,6 +73,7 @@ struct dc_stage {
   int lo = 0, hi = 0, head = 0, max_rows = 0, max_pos = 0;
   int C = 0, hd = 0, nH = 0, nKV = 0, qDim = 0, kvDim = 0, I = 0, V = 0, nqkv = 0;
   int ldC = 0, ldQ = 0, ldI = 0, ldp = 0;  // ldp: positions per channel row of the int8 V cache
+  int ldvt = 0;  // positions per channel row of the f32 channel-major V copy (ldp + 8: no power-of-two stride)
   std::vector<dc_layer> L;
   float* emb = nullptr;  // V x C
   float* nrmF = nullptr;
@@ -505,9 +507,15 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
                                                     float* vcache, uint32_t* vmax,
                                                     float* vs, int* vchg,
                                                     int8_t* v8t, int ldp, int* status,
-                                                    int8_t* q8, float* qs) {
-  asm volatile("griddepcontrol.launch_dependents;");
+                                                    int8_t* q8, float* qs, float* vt, int ldvt) {
+  // The decode attention after this kernel reads the cache's older keys and
+  // int8 values before its own grid-dependency wait.  Its launch is released
+  // only once this kernel has passed its wait, so every earlier kernel -- the
+  // previous step's attention, which rewrites the rows of moved value channels,
+  // among them -- has completed by then (each kernel of the chain waits for its
+  // predecessor before it completes).
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  asm volatile("griddepcontrol.launch_dependents;");
   __shared__ float kr[128];
   __shared__ float red[32];
   const int n0 = *n0p;  // cached tokens before this chunk = its first position
@@ -526,6 +534,7 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
       const float v = row[qDim + kvDim + c];
       bad |= !isfinite(v);
       vcache[(int64_t)(n0 + t) * kvDim + c] = v;
+      vt[(int64_t)c * ldvt + n0 + t] = v;
       if (vs) {
         const uint32_t m = max(vmax[c], __float_as_uint(fabsf(v)));
         vmax[c] = m;
@@ -707,10 +716,11 @@ __global__ void __launch_bounds__(32 * DC_MAX_CHUNKS) k_vscale_chunks(const floa
 // one gets chunk g's int8 row (every position up to the chunk's end) in the
 // pass buffer v8s[g]; every other channel of chunk g reads the cache's rows,
 // so its warp returns at once.  grid ntiles + (G - 1) * ceil(kvDim / 8), 256
-// threads.
+// threads.  The moved rows read the channel-major f32 copy (contiguous).
 __global__ void __launch_bounds__(256) k_vquant_chunks(const float* vcache, const float* vs, const int* vchg,
                                                        int8_t* v8t, int n0, int kvDim, int hd, int ldp,
-                                                       ChunkSet cks, const float* vsg, int8_t* v8s, int ntiles) {
+                                                       ChunkSet cks, const float* vsg, int8_t* v8s, int ntiles,
+                                                       const float* vt, int ldvt) {
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int N = n0 + cks.end[cks.G - 1];
@@ -730,7 +740,7 @@ __global__ void __launch_bounds__(256) k_vquant_chunks(const float* vcache, cons
   const double sc = (double)sg, rsc = __drcp_rn(sc);
   int8_t* dst = v8s + ((int64_t)g * kvDim + c) * ldp;
 #pragma unroll 4
-  for (int j = lane; j < Ng; j += 32) dst[j] = dc_quant_div((double)__ldcg(vcache + (int64_t)j * kvDim + c), sc, rsc);
+  for (int j = lane; j < Ng; j += 32) dst[j] = dc_quant_div((double)__ldcg(vt + (int64_t)c * ldvt + j), sc, rsc);
 }
 
 // The tiled quantisation for short chunks and decode steps, reading the cache
@@ -1575,7 +1585,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
                                                        double scale, float* out,
                                                        uint32_t* rowmax, int* done,
                                                        int8_t* xq, int ldq, float* rsq,
-                                                       int* status, const float* vcache, const int* vchg,
+                                                       int* status, const float* vt, int ldvt, const int* vchg,
                                                        const int8_t* q8g, const float* qsg) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
@@ -1816,14 +1826,13 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const bool vok = dcp::mbar_wait(&vbar, 0, status);
   if (!vok) abort_flag = 1;
   __syncthreads();
-  if (!abort_flag && vcache) {
+  if (!abort_flag && vt) {
     // The value rows came in before the grid-dependency wait.  This step's
     // column n0 (appended under the channel's new scale) is taken now, and a
     // channel whose scale moved this step is re-quantised here from the f32
     // cache (k_vquant_dev's arithmetic); the first head of the KV group writes
     // those rows back for the next steps (another head reading them meanwhile
     // re-quantises the same channel itself).
-    const int kvDim = nKV * hd;
     const bool writer = hq % (nH / nKV) == 0;
     // the CTA's moved channels (CH <= 32), gathered in one warp vote
     __shared__ unsigned chg_mask;
@@ -1832,25 +1841,36 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       if (lane == 0) chg_mask = m;
     }
     __syncthreads();
+    // every moved channel's rows at once: (channel, row) pairs flattened over
+    // the block, eight loads in flight per thread, read along the channel-major
+    // f32 copy (contiguous per channel)
+    __shared__ int mlist[32];
+    __shared__ double msc[32], mrs[32];
+    const int nm = __popc(chg_mask);
+    if (tid < 32 && ((chg_mask >> tid) & 1u)) {
+      const int slot = __popc(chg_mask & ((1u << tid) - 1u));
+      mlist[slot] = tid;
+      msc[slot] = (double)vs[g * hd + c0 + tid];
+      mrs[slot] = __drcp_rn(msc[slot]);
+    }
+    __syncthreads();
+    const int total = nm * n0;
     #pragma unroll 1
-    for (unsigned mask = chg_mask; mask; mask &= mask - 1) {
-      const int c = __ffs(mask) - 1;
-      const int gc = g * hd + c0 + c;
-      const double sc = (double)vs[gc], rsc = __drcp_rn(sc);
-      // (eight strided loads of the column in flight per thread, then their quotients)
-      #pragma unroll 1
-      for (int j0 = tid; j0 < n0; j0 += 8 * 256) {
-        float v[8];
+    for (int i0 = tid; i0 < total; i0 += 8 * 256) {
+      float v[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) v[u] = j0 + 256 * u < n0 ? __ldcg(vcache + (int64_t)(j0 + 256 * u) * kvDim + gc) : 0.0f;
+      for (int u = 0; u < 8; u++) {
+        const int i = i0 + 256 * u;
+        v[u] = i < total ? __ldcg(vt + (int64_t)(g * hd + c0 + mlist[i / n0]) * ldvt + i % n0) : 0.0f;
+      }
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const int j = j0 + 256 * u;
-          if (j < n0) {
-            const int8_t q = dc_quant_div((double)v[u], sc, rsc);
-            sV[(size_t)c * ldpv + j] = q;
-            if (writer) v8t[(int64_t)gc * ldp + j] = q;
-          }
+      for (int u = 0; u < 8; u++) {
+        const int i = i0 + 256 * u;
+        if (i < total) {
+          const int m = i / n0, j = i - m * n0, c = mlist[m];
+          const int8_t q = dc_quant_div((double)v[u], msc[m], mrs[m]);
+          sV[(size_t)c * ldpv + j] = q;
+          if (writer) v8t[(int64_t)(g * hd + c0 + c) * ldp + j] = q;
         }
       }
     }
@@ -2352,6 +2372,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
   S->ldQ = round_up(S->qDim, 16);
   S->ldI = round_up(S->I, 16);
   S->ldp = round_up(max_pos, 64);
+  S->ldvt = S->ldp + 8;
   int rc = DC_OK;
   auto fail = [&](int r) {
     dc_stage_free(S);
@@ -2368,6 +2389,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
     if ((rc = st_alloc(S, (void**)&kv.k8, (size_t)S->nKV * max_pos * S->hd)) ||
         (rc = st_alloc(S, (void**)&kv.ks, 4 * (size_t)S->nKV * max_pos)) ||
         (rc = st_alloc(S, (void**)&kv.v, 4 * (size_t)max_pos * S->kvDim)) ||
+        (rc = st_alloc(S, (void**)&kv.vt, 4 * (size_t)S->ldvt * S->kvDim)) ||
         (rc = st_alloc(S, (void**)&kv.v8t, (size_t)S->kvDim * S->ldp)) ||
         (rc = st_alloc(S, (void**)&kv.vs, 4 * (size_t)S->kvDim)) ||
         (rc = st_alloc(S, (void**)&kv.vmax, 4 * (size_t)S->kvDim)) ||
@@ -2782,7 +2804,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
                             S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
                             multi ? nullptr : kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status,
-                            dcl ? S->q8d : nullptr, S->qsd));
+                            dcl ? S->q8d : nullptr, S->qsd, kv.vt, S->ldvt));
     dc_count_launch();
     if (multi) {
       DC_CUDA(ctx, launch_dep(k_vscale_chunks, dim3((S->kvDim + 31) / 32), dim3(32 * DC_MAX_CHUNKS), 0, st,
@@ -2799,7 +2821,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       const int ntiles = ((N + 63) / 64) * ((S->kvDim + 31) / 32);
       DC_CUDA(ctx, launch_dep(k_vquant_chunks, dim3(ntiles + (cks->G - 1) * ((S->kvDim + 7) / 8)), dim3(256), 0, st,
                               (const float*)kv.v, (const float*)kv.vs, (const int*)kv.vchg, kv.v8t, n0, S->kvDim, S->hd,
-                              S->ldp, *cks, (const float*)S->vsg, S->v8s, ntiles));
+                              S->ldp, *cks, (const float*)S->vsg, S->v8s, ntiles, (const float*)kv.vt, S->ldvt));
     } else if (T <= 8) {
       DC_CUDA(ctx, launch_dep(k_vquant_dev, dim3((S->max_pos + 127) / 128, (S->kvDim + 31) / 32), dim3(256), 0, st,
                               kv.v, kv.vs, kv.vchg, kv.v8t, T, n0p, S->kvDim, S->hd, S->ldp, T == 1 ? 1 : 0));
@@ -2827,8 +2849,8 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_attention_dcl, (const float*)S->hbuf, S->nqkv, S->nH, S->nKV, S->hd,
                                       (const int8_t*)kv.k8, (const float*)kv.ks, kv.v8t, (const float*)kv.vs, n0p,
                                       S->max_pos, S->ldp, dec_ch, scale, S->ctxo, S->rowmax, S->att_done,
-                                      o_rowq ? nullptr : S->xq, S->ldQ, S->rs, ctx->d_status, (const float*)kv.v,
-                                      (const int*)kv.vchg,
+                                      o_rowq ? nullptr : S->xq, S->ldQ, S->rs, ctx->d_status, (const float*)kv.vt,
+                                      S->ldvt, (const int*)kv.vchg,
                                       (const int8_t*)S->q8d, (const float*)S->qsd));
       dc_count_launch();
     } else if (T == 1 && use_kv && dec_ch) {
