@@ -468,6 +468,17 @@ def decode_timeline(S, ring, ids, w, laps: int = 17, per_lap: int = 2048):
         shapes.setdefault(round(bb), []).append(np.median(per[:, col]))
     stamp_cost_us = (stamped_ms - plain_ms) / laps / n * 1e3
     med = np.median(gaps, axis=0) * 1e3  # us, per launch of the lap
+    # the layers' launch pattern: four GEMVs per layer after the lap's first
+    # GEMV (lm_head of the previous row); period = launches per layer
+    gp = [i for i, kk in enumerate(k) if kk == 1]
+    layer_us, layer_kinds = None, None
+    if len(gp) >= 6:
+        per_layer, start = gp[5] - gp[1], gp[1] - 1
+        nl = (len(med) - start) // per_layer
+        if nl > 0:
+            m = np.array([med[start + l * per_layer:start + (l + 1) * per_layer] for l in range(nl)])
+            layer_us = [round(float(v), 2) for v in m.mean(axis=0)]
+            layer_kinds = [int(v) for v in k[start:start + per_layer]]
     return dict(laps=laps - 1, stamps_per_lap=n, gemv_launches_per_lap=int(gemv.sum()),
                 gemv_bytes_per_lap=gemv_bytes, gemv_ms_per_lap=gemv_ms,
                 gemv_gbs=gemv_bytes / (gemv_ms / 1e3) / 1e9, tcgen05_ms_per_lap=tc_ms,
@@ -476,6 +487,7 @@ def decode_timeline(S, ring, ids, w, laps: int = 17, per_lap: int = 2048):
                 launch_us_first=[round(float(v), 2) for v in med[:21]],
                 launch_us_last=[round(float(v), 2) for v in med[-8:]],
                 launch_kinds_first=[int(v) for v in k[:21]], launch_kinds_last=[int(v) for v in k[-8:]],
+                layer_us=layer_us, layer_kinds=layer_kinds,
                 gemv_by_bytes_per_launch={str(kb): dict(launches_per_lap=len(v), us=float(np.median(v) * 1e3),
                                                         gbs=kb / (np.median(v) / 1e3) / 1e9)
                                           for kb, v in sorted(shapes.items())})
