@@ -1611,7 +1611,6 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   // CTA).
   __shared__ double x_max[64];    // score maxima
   __shared__ double2 x_sum[64];   // (sum of e, sum of (N - j) e_j)
-  __shared__ float x_amx[64];     // probability maxima at the lower end of z's bracket
   __shared__ int x_amb[64];       // 1: some probability is ambiguous under the bracket
   __shared__ float x_cmax[8];     // the context maxima of this CTA's warps
   __shared__ float xf;            // (the exact path) this CTA's probability maximum
@@ -1765,63 +1764,61 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const double zlo = zp - zr, zhi = zp + zr;
   const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
   const bool narrow = __dsub_rn(zhi, zlo) < 5e-13 * zlo;
+  // 6-7. a_j = f32(f32(e_j) / z) of this CTA's keys at the lower end of z's
+  // bracket, quantised with the row's scale.  The row's largest probability is
+  // that of its largest score (e = 1 there, and f32(f32(e) / z) grows with e),
+  // so the scale needs no exchange: only the ambiguity flags travel, with the
+  // probability bytes, before one cluster barrier.
+  float amx = dc_div_to_f32(1.0, zlo, rlo);
+  double asc = quant_scale(amx), rasc = __drcp_rn(asc);
   bool amb = false;
-  float amx = 0.0f;
 #pragma unroll 4
   for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
-    if (j < N) amx = fmaxf(amx, dc_div_bracket((double)af[j], zlo, rlo, zhi, rhi, narrow, &amb));
+    if (j < ldpN)
+      a8[j] = j < N ? dc_quant_div((double)dc_div_bracket((double)af[j], zlo, rlo, zhi, rhi, narrow, &amb), asc, rasc)
+                    : (int8_t)0;
   }
+  // this CTA's probability bytes to the other CTAs, 16 at a time (remote
+  // stores, ordered by the barrier after them); no CTA touches another's
+  // shared memory after the last one, so none has to wait before it exits
+  auto send_a8 = [&]() {
+    __syncthreads();
+    #pragma unroll 1
+    for (int q16 = tid; q16 < (ldpN >> 4); q16 += 256) {
+      if (((q16 << 4) / ATTD_KB) % S != r) continue;
+      const int4 v = ((const int4*)a8)[q16];
+#pragma unroll 1
+      for (int p = 0; p < S; p++)
+        if (p != r) *cl.map_shared_rank(&((int4*)a8)[q16], p) = v;
+    }
+  };
   {
     const int wamb = __any_sync(0xffffffffu, amb) ? 1 : 0;
-    for (int o = 16; o; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
-    if (lane < S) {
-      *cl.map_shared_rank(&x_amb[r * 8 + warp], lane) = wamb;
-      *cl.map_shared_rank(&x_amx[r * 8 + warp], lane) = amx;
-    }
+    if (lane < S) *cl.map_shared_rank(&x_amb[r * 8 + warp], lane) = wamb;
   }
+  send_a8();
   cl.sync();
   int any_amb = 0;
-  amx = 0.0f;
 #pragma unroll 8
-  for (int i = 0; i < S * 8; i++) {
-    any_amb |= x_amb[i];
-    amx = fmaxf(amx, x_amx[i]);
-  }
-  // the rare exact path: every CTA publishes its maximum under the serial z
-  const double z = any_amb ? dcl_exact_z(xs, af, N, S, r, nmine, osm, red, &xf) : zlo;
+  for (int i = 0; i < S * 8; i++) any_amb |= x_amb[i];
   if (any_amb) {
-    cl.sync();
-    amx = 0.0f;
-#pragma unroll
-    for (int q = 0; q < 8; q++)
-      if (q < S) amx = fmaxf(amx, *cl.map_shared_rank(&xf, q));
-  }
-  // 6-7. a_j = f32(f32(e_j) / z) of this CTA's keys, quantised with the row's scale
-  const double asc = quant_scale(amx), rasc = __drcp_rn(asc);
-  const float as = __double2float_rn(asc);
-  {
+    // the rare exact path (cluster-uniform): the serial z, then every CTA's
+    // probability bytes again under it
+    const double z = dcl_exact_z(xs, af, N, S, r, nmine, osm, red, &xf);
     const double rz = __drcp_rn(z);
+    amx = dc_div_to_f32(1.0, z, rz);
+    asc = quant_scale(amx);
+    rasc = __drcp_rn(asc);
 #pragma unroll 4
     for (int i = 0; i < nmine; i++) {
-      const int kb = (r + i * S) * ATTD_KB;
-      const int j = kb + tid;
+      const int j = (r + i * S) * ATTD_KB + tid;
       if (j < ldpN) a8[j] = j < N ? dc_quant_div((double)dc_div_to_f32((double)af[j], z, rz), asc, rasc) : (int8_t)0;
     }
+    send_a8();
+    cl.sync();
   }
-  __syncthreads();
-  // this CTA's probability bytes to the other CTAs, 16 at a time (remote
-  // stores, ordered by the barrier below); no CTA touches another's shared
-  // memory after it, so none has to wait for the others before it exits
-  #pragma unroll 1
-  for (int q16 = tid; q16 < (ldpN >> 4); q16 += 256) {
-    if (((q16 << 4) / ATTD_KB) % S != r) continue;
-    const int4 v = ((const int4*)a8)[q16];
-#pragma unroll 1
-    for (int p = 0; p < S; p++)
-      if (p != r) *cl.map_shared_rank(&((int4*)a8)[q16], p) = v;
-  }
-  cl.sync();
+  const float as = __double2float_rn(asc);
   // 8. the context of this CTA's CH channels over all keys
   const bool vok = dcp::mbar_wait(&vbar, 0, status);
   if (!vok) abort_flag = 1;
@@ -2144,6 +2141,25 @@ __global__ void __launch_bounds__(FG_THREADS, 1) k_gemv_fused(const float* x, in
   }
 }
 
+// One embedding row (C floats) copied by the block with every load in flight
+// before the first store (the table is cold in HBM).
+__device__ __forceinline__ void embed_row(const float* __restrict__ src, int C, float* __restrict__ dst) {
+  constexpr int U = 8;
+  for (int j0 = threadIdx.x; j0 < C; j0 += U * (int)blockDim.x) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + u * (int)blockDim.x;
+      v[u] = j < C ? src[j] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int j = j0 + u * (int)blockDim.x;
+      if (j < C) dst[j] = v[u];
+    }
+  }
+}
+
 __global__ void k_embed(const int32_t* __restrict__ ids, int T, const float* __restrict__ emb, int C, int V,
                         float* __restrict__ x, int* status) {
   const int t = blockIdx.x;
@@ -2152,7 +2168,7 @@ __global__ void k_embed(const int32_t* __restrict__ ids, int T, const float* __r
     if (threadIdx.x == 0) atomicOr(status, DC_ST_BOUNDS);
     return;
   }
-  for (int j = threadIdx.x; j < C; j += blockDim.x) x[(int64_t)t * C + j] = emb[(int64_t)id * C + j];
+  embed_row(emb + (int64_t)id * C, C, x + (int64_t)t * C);
 }
 
 // One id per decode lap: ids[*stepp] (the previous lap's greedy pick).
@@ -2163,7 +2179,7 @@ __global__ void k_embed_at(const int32_t* __restrict__ ids, const int* __restric
     if (threadIdx.x == 0) atomicOr(status, DC_ST_BOUNDS);
     return;
   }
-  for (int j = threadIdx.x; j < C; j += blockDim.x) x[j] = emb[(int64_t)id * C + j];
+  embed_row(emb + (int64_t)id * C, C, x);
 }
 
 __global__ void k_gather_rows(const float* __restrict__ x, int C, const int32_t* __restrict__ rows, int nrows,
@@ -3144,7 +3160,7 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
     if (rc) return rc;
   }
   if ((rc = launch_argmax(H, H->logits1, 1, picks, H->d_step))) return rc;
-  k_embed_at<<<1, 256, 0, s>>>(picks, H->d_step, H->emb, H->C, H->V, H->xlap, ctx->d_status);
+  k_embed_at<<<1, 512, 0, s>>>(picks, H->d_step, H->emb, H->C, H->V, H->xlap, ctx->d_status);
   dc_count_launch();
   for (int i = 0; i < ns; i++) {
     dc_stage* S = st[i];
