@@ -514,14 +514,20 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
   // previous step's attention, which rewrites the rows of moved value channels,
   // among them -- has completed by then (each kernel of the chain waits for its
   // predecessor before it completes).
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
-  asm volatile("griddepcontrol.launch_dependents;");
-  __shared__ float kr[128];
-  __shared__ float red[32];
+  // The position counter is set before the step's first kernel and the RoPE
+  // tables are constant: this thread's first table entries are read before
+  // the wait, so their round trip overlaps the kernel in front.
   const int n0 = *n0p;  // cached tokens before this chunk = its first position
   const int t = blockIdx.x, hh = blockIdx.y;
   const int p = n0 + t;
   const int half = hd >> 1, qDim = nH * hd, kvDim = nKV * hd;
+  const bool rot = hh < nH + nKV && (int)threadIdx.x < half;
+  const double c_first = rot ? (double)rc[(int64_t)p * half + threadIdx.x] : 0.0;
+  const double s_first = rot ? (double)rsn[(int64_t)p * half + threadIdx.x] : 0.0;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  asm volatile("griddepcontrol.launch_dependents;");
+  __shared__ float kr[128];
+  __shared__ float red[32];
   float* row = h + (int64_t)t * nqkv;
   bool bad = false;
   if (hh >= nH + nKV) {
@@ -554,7 +560,9 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
   const bool isq = hh < nH;
   float* o = isq ? row + hh * hd : row + qDim + (hh - nH) * hd;
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const double c = rc[(int64_t)p * half + i], s = rsn[(int64_t)p * half + i];
+    const bool first = i == (int)threadIdx.x;
+    const double c = first ? c_first : (double)rc[(int64_t)p * half + i];
+    const double s = first ? s_first : (double)rsn[(int64_t)p * half + i];
     const double a = o[i], b = o[half + i];
     const float na = __double2float_rn(__dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s)));
     const float nb = __double2float_rn(__dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s)));
