@@ -468,12 +468,15 @@ def decode_timeline(S, ring, ids, w, laps: int = 17, per_lap: int = 2048):
         shapes.setdefault(round(bb), []).append(np.median(per[:, col]))
     stamp_cost_us = (stamped_ms - plain_ms) / laps / n * 1e3
     med = np.median(gaps, axis=0) * 1e3  # us, per launch of the lap
-    # the layers' launch pattern: four GEMVs per layer after the lap's first
-    # GEMV (lm_head of the previous row); period = launches per layer
+    # the layers' launch pattern: after the lap's first GEMV (lm_head of the
+    # previous row) each layer has the same number of tagged GEMVs; the period
+    # is the launches from one layer's first GEMV to the next layer's
     gp = [i for i, kk in enumerate(k) if kk == 1]
+    nlay = max(1, S.hi - S.lo)
     layer_us, layer_kinds = None, None
-    if len(gp) >= 6:
-        per_layer, start = gp[5] - gp[1], gp[1] - 1
+    g_l = (len(gp) - 1) // nlay
+    if g_l >= 1 and len(gp) > 1 + g_l:
+        per_layer, start = gp[1 + g_l] - gp[1], gp[1] - 1
         nl = (len(med) - start) // per_layer
         if nl > 0:
             m = np.array([med[start + l * per_layer:start + (l + 1) * per_layer] for l in range(nl)])
