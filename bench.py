@@ -332,6 +332,15 @@ def bench_model(args, rank, world, peaks):
         ev_scale = args.steps
     got = read_kinds()
     comp.L.dc_timing(comp.h, 0)
+    pre_wn = None
+    if w["mode"] == "chunked" and world > 2:
+        # labelled variant: as many passes in flight as there are stages (the
+        # reference keeps two); the same ids
+        pe = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        pe[0].record()
+        ring.generate_chunked(ids, 1, w["chunk"], world, on_prefill=pe[1].record, per_pass=w["per_pass"])
+        comp.sync()
+        pre_wn = max_over_ranks([pe[0].elapsed_time(pe[1])], world)[0]
     pre1 = None
     if w["mode"] == "chunked" and w["per_pass"] > 1:
         # for comparison: the same prefill one chunk per pass over the weights
@@ -396,6 +405,7 @@ def bench_model(args, rank, world, peaks):
                     prefill_tok_s=(len(ids) / (pre / 1e3)) if w["mode"] == "chunked" else None,
                     prefill_ms=pre if w["mode"] == "chunked" else None, decode_ms=dec,
                     prefill_tok_s_one_chunk_per_pass=(len(ids) / (pre1 / 1e3)) if pre1 else None,
+                    prefill_tok_s_window_n=(len(ids) / (pre_wn / 1e3)) if pre_wn else None,
                     roofline=roof, kernels=other, gpu_launches=launches, clocks=clk, backend=comp.label,
                     generated_ids_fnv=P_fnv(gen_ids), generated_head=gen_ids[:8],
                     weights_gb=weight_bytes(spec, 0, spec.layers, True) / 1e9)
