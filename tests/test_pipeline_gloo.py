@@ -92,7 +92,7 @@ def plan_for(world):
     return {1: [(0, 6)], 2: [(0, 2), (2, 6)], 3: [(0, 1), (1, 4), (4, 6)]}[world]
 
 
-def run_rank(rank, world, port, prompt, q, wire=False, per_pass=1):
+def run_rank(rank, world, port, prompt, q, wire=False, per_pass=1, window=2):
     import torch.distributed as dist
     import __graft_entry__ as G
     P = G.package()
@@ -109,7 +109,7 @@ def run_rank(rank, world, port, prompt, q, wire=False, per_pass=1):
         tp = P.wire.WireTransport(tp, plan, rank, model_hash=0x5EED1234, seq=7)
     ring = P.pipeline.Ring(st, rank, world, H, tp, new_buffer=lambda n: torch.empty(n, dtype=torch.float32))
     marks = []
-    picks = ring.generate_chunked(prompt, 5, chunk_size=3, window=2, on_prefill=lambda: marks.append(rank),
+    picks = ring.generate_chunked(prompt, 5, chunk_size=3, window=window, on_prefill=lambda: marks.append(rank),
                                   per_pass=per_pass)
     assert marks == [rank]  # every rank marks the end of its prefill part once (the bench's timer)
     look = ring.generate_lookahead([4, 4, 4, 7, 4, 4, 4], 4, 12, 4)
@@ -127,11 +127,12 @@ def _free_port():
     return p
 
 
-def run_world(world, prompt, wire=False, per_pass=1):
+def run_world(world, prompt, wire=False, per_pass=1, window=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=run_rank, args=(r, world, port, prompt, q, wire, per_pass)) for r in range(world)]
+    procs = [ctx.Process(target=run_rank, args=(r, world, port, prompt, q, wire, per_pass, window))
+             for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -209,3 +210,10 @@ def test_chunk_passes_grouping(P):
     passes = P.shard.chunk_passes(big, 8)
     assert len(passes) == 16 and all(r == [16] * 8 for _, _, r in passes)
     assert [p[0] for p in passes] == list(range(0, 2048, 128))
+
+
+def test_more_passes_in_flight_match(P):
+    """As many passes in flight as stages (the benchmark's labelled variant;
+    the reference keeps two): the same ids."""
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8, 9, 7]
+    assert run_world(3, prompt, per_pass=2, window=3) == run_world(1, prompt)
