@@ -230,7 +230,8 @@ def build_rank(P, comp, w: dict, rank: int, world: int):
     S = P.infer.Stage(comp, spec, st["lo"], st["hi"], head=(rank == 0), max_rows=max_rows, max_pos=max_pos)
     S.synth(MODEL_SEED, P.infer.SYNTH_FACTOR)
     dev = torch.device("cuda", comp.device)
-    ring = P.pipeline.Ring(S, rank, world, spec.hidden, P.pipeline.TorchP2P() if world > 1 else None,
+    tp = P.pipeline.TorchP2P(P.pipeline.ring_edge_groups(world)) if world > 1 else None
+    ring = P.pipeline.Ring(S, rank, world, spec.hidden, tp,
                            new_buffer=lambda n: torch.empty(n, dtype=torch.float32, device=dev))
     return spec, plan, S, ring
 

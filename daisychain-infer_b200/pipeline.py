@@ -46,18 +46,36 @@ def classify_act(next_index: int, my_index: int) -> str:
     return "other"
 
 
-class TorchP2P:
-    """Point-to-point transport over torch.distributed (NCCL on GPUs, gloo on CPU)."""
+def ring_edge_groups(world: int) -> dict:
+    """One process group per directed ring edge i -> (i + 1) % world, so that a
+    rank's send to its successor and receive from its predecessor run on
+    separate communicators: NCCL orders the point-to-point operations of one
+    communicator, and on a single group a pass's return hop would have to
+    finish before the next pass could be sent.  Every rank calls this, in the
+    same order (group creation is collective).  Returns {(src, dst): group}."""
+    import torch.distributed as dist
+    edges = {}
+    for i in range(world):
+        j = (i + 1) % world
+        edges[(i, j)] = dist.new_group([i, j])
+    return edges
 
-    def __init__(self):
+
+class TorchP2P:
+    """Point-to-point transport over torch.distributed (NCCL on GPUs, gloo on CPU);
+    with ``edges`` (``ring_edge_groups``) each hop uses its edge's group."""
+
+    def __init__(self, edges: dict | None = None):
         import torch.distributed as dist
         self.dist = dist
+        self.edges = edges or {}
+        self.me = dist.get_rank() if dist.is_initialized() else 0
 
     def send(self, t, dst: int, token_idx: int = 0):
-        return self.dist.isend(t, dst)
+        return self.dist.isend(t, dst, group=self.edges.get((self.me, dst)))
 
     def recv(self, t, src: int, token_idx: int | None = None):
-        return self.dist.irecv(t, src)
+        return self.dist.irecv(t, src, group=self.edges.get((src, self.me)))
 
 
 class HopBuffers:

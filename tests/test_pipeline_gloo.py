@@ -102,7 +102,7 @@ def run_rank(rank, world, port, prompt, q, wire=False, per_pass=1, window=2):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     lo, hi = plan_for(world)[rank]
     st = FakeStage(lo, hi, rank == 0)
-    tp = P.pipeline.TorchP2P() if world > 1 else None
+    tp = P.pipeline.TorchP2P(P.pipeline.ring_edge_groups(world)) if world > 1 else None
     if tp is not None and wire:
         # every hop as a wire.js activation frame, checked on arrival
         plan = [dict(id=f"rank{i}", index=i) for i in range(world)]
