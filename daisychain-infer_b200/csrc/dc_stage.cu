@@ -347,6 +347,7 @@ __device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, cons
     return;
   }
   const double sc = quant_scale(mx), rsc = __drcp_rn(sc);
+  const float rscf = __double2float_rn(rsc);
   if (threadIdx.x == 0) s[0] = __double2float_rn(sc);
   if (vec && (ldq & 3) == 0 && (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
 #pragma unroll 1
@@ -354,16 +355,16 @@ __device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, cons
       char4 o = make_char4(0, 0, 0, 0);
       if (4 * i < C) {
         const float4 y = reinterpret_cast<const float4*>(ys)[i];
-        o.x = dc_quant_div((double)y.x, sc, rsc);
-        o.y = dc_quant_div((double)y.y, sc, rsc);
-        o.z = dc_quant_div((double)y.z, sc, rsc);
-        o.w = dc_quant_div((double)y.w, sc, rsc);
+        o.x = dc_quant_div_f(y.x, sc, rsc, rscf);
+        o.y = dc_quant_div_f(y.y, sc, rsc, rscf);
+        o.z = dc_quant_div_f(y.z, sc, rsc, rscf);
+        o.w = dc_quant_div_f(y.w, sc, rsc, rscf);
       }
       reinterpret_cast<char4*>(q)[i] = o;
     }
   } else {
 #pragma unroll 1
-    for (int j = threadIdx.x; j < ldq; j += blockDim.x) q[j] = j < C ? dc_quant_div((double)ys[j], sc, rsc) : (int8_t)0;
+    for (int j = threadIdx.x; j < ldq; j += blockDim.x) q[j] = j < C ? dc_quant_div_f(ys[j], sc, rsc, rscf) : (int8_t)0;
   }
 }
 
@@ -419,6 +420,7 @@ __global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* x, int C,
 // it): each thread's 16 loads are in flight before its first conversion.
 __device__ __forceinline__ void quant_row_block(const float* x, int n, int ldq, double sc, double rsc, int8_t* q) {
   constexpr int U = 16;
+  const float rscf = __double2float_rn(rsc);
 #pragma unroll 1
   for (int j0 = threadIdx.x; j0 < ldq; j0 += U * (int)blockDim.x) {
     float v[U];
@@ -430,7 +432,7 @@ __device__ __forceinline__ void quant_row_block(const float* x, int n, int ldq, 
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const int j = j0 + u * (int)blockDim.x;
-      if (j < ldq) q[j] = j < n ? dc_quant_div((double)v[u], sc, rsc) : (int8_t)0;
+      if (j < ldq) q[j] = j < n ? dc_quant_div_f(v[u], sc, rsc, rscf) : (int8_t)0;
     }
   }
 }
@@ -443,6 +445,7 @@ __device__ __forceinline__ void quant_row_block_max(const float* x, int n, int l
   constexpr int U = 16;
   const uint32_t mb = __ldcg(rowmax);
   double sc = 1.0, rsc = 1.0;
+  float rscf = 1.0f;
 #pragma unroll 1
   for (int j0 = threadIdx.x, it = 0; j0 < ldq; j0 += U * (int)blockDim.x, it++) {
     float v[U];
@@ -454,12 +457,13 @@ __device__ __forceinline__ void quant_row_block_max(const float* x, int n, int l
     if (it == 0) {
       sc = quant_scale(__uint_as_float(mb));
       rsc = __drcp_rn(sc);
+      rscf = __double2float_rn(rsc);
       if (threadIdx.x == 0) s[0] = __double2float_rn(sc);
     }
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const int j = j0 + u * (int)blockDim.x;
-      if (j < ldq) q[j] = j < n ? dc_quant_div((double)v[u], sc, rsc) : (int8_t)0;
+      if (j < ldq) q[j] = j < n ? dc_quant_div_f(v[u], sc, rsc, rscf) : (int8_t)0;
     }
   }
 }
@@ -637,10 +641,11 @@ __device__ __forceinline__ void vquant_tile(const float* vcache, const float* vs
   const bool cval = c < kvDim;
   const bool chg = cval && vchg[c] != 0;
   const double sc = cval ? (double)vs[c] : 1.0, rsc = __drcp_rn(sc);
+  const float rscf = __double2float_rn(rsc);
   for (int r = ty; r < 64; r += 8) {
     const int j = jb + r;
     int8_t v = 0;
-    if (cval && j < N && (j >= n0 || chg)) v = dc_quant_div((double)vcache[(int64_t)j * kvDim + c], sc, rsc);
+    if (cval && j < N && (j >= n0 || chg)) v = dc_quant_div_f(vcache[(int64_t)j * kvDim + c], sc, rsc, rscf);
     tile[tx][r] = v;
   }
   __syncthreads();
@@ -746,9 +751,10 @@ __global__ void __launch_bounds__(256) k_vquant_chunks(const float* vcache, cons
   if (sg == vs[c]) return;  // (warp-uniform)
   const int Ng = n0 + cks.end[g];
   const double sc = (double)sg, rsc = __drcp_rn(sc);
+  const float rscf = __double2float_rn(rsc);
   int8_t* dst = v8s + ((int64_t)g * kvDim + c) * ldp;
 #pragma unroll 4
-  for (int j = lane; j < Ng; j += 32) dst[j] = dc_quant_div((double)__ldcg(vt + (int64_t)c * ldvt + j), sc, rsc);
+  for (int j = lane; j < Ng; j += 32) dst[j] = dc_quant_div_f(__ldcg(vt + (int64_t)c * ldvt + j), sc, rsc, rscf);
 }
 
 // The tiled quantisation for short chunks and decode steps, reading the cache
@@ -1873,7 +1879,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
         const int i = i0 + 256 * u;
         if (i < total) {
           const int m = i / n0, j = i - m * n0, c = mlist[m];
-          const int8_t q = dc_quant_div((double)v[u], msc[m], mrs[m]);
+          const int8_t q = dc_quant_div_f(v[u], msc[m], mrs[m], (float)mrs[m]);
           sV[(size_t)c * ldpv + j] = q;
           if (writer) v8t[(int64_t)(g * hd + c0 + c) * ldp + j] = q;
         }
@@ -1996,10 +2002,11 @@ __global__ void __launch_bounds__(256) k_rowquant(const float* x, int64_t ldx, i
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   const int row = blockIdx.y;
   const double sc = quant_scale(__uint_as_float(rowmax[row])), rsc = __drcp_rn(sc);
+  const float rscf = __double2float_rn(rsc);
   if (blockIdx.x == 0 && threadIdx.x == 0) s[row] = __double2float_rn(sc);
 #pragma unroll 4
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < ldq; j += gridDim.x * blockDim.x)
-    q[(int64_t)row * ldq + j] = j < cols ? dc_quant_div((double)x[row * ldx + j], sc, rsc) : (int8_t)0;
+    q[(int64_t)row * ldq + j] = j < cols ? dc_quant_div_f(x[row * ldx + j], sc, rsc, rscf) : (int8_t)0;
 }
 
 
