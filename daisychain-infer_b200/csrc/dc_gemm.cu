@@ -175,7 +175,8 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
                                                      uint32_t* rowmax, int* status) {
   // the next kernel (launched as a programmatic dependent) may be scheduled
   // now; it waits for this grid's completion before reading its output
-  asm volatile("griddepcontrol.launch_dependents;");
+  // (DC_F_LATE_RELEASE: once this grid has passed its own wait)
+  if (!(flags & DC_F_LATE_RELEASE)) asm volatile("griddepcontrol.launch_dependents;");
   __shared__ float wmax[4];
   // (DC_F_SWIGLU) the pair this lane keeps, and its |h| maximum
   int sa0 = 0, sa1 = 0, sj = -1;
@@ -238,6 +239,7 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
         // kernel that writes it has completed
         asm volatile("griddepcontrol.wait;" ::: "memory");
         waited = true;
+        if (flags & DC_F_LATE_RELEASE) asm volatile("griddepcontrol.launch_dependents;");
       }
 #pragma unroll
       for (int u = 0; u < GV_SEG; u++) {
@@ -270,7 +272,10 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
       if (lane == 1 && j0 + 1 < n) dc_store_out(out, j0 + 1, a1, rs[0], csv, flags, requant, relu);
     }
   }
-  if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (!waited) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (flags & DC_F_LATE_RELEASE) asm volatile("griddepcontrol.launch_dependents;");
+  }
   if (flags & DC_F_SWIGLU) {
     swiglu_flush();
 #pragma unroll
@@ -315,7 +320,8 @@ __global__ void __launch_bounds__(288, 1) k_gemv_bulk(const int8_t* X, int ldx,
   int4* xs = (int4*)(smraw + (size_t)stages * stage_bytes);
   uint64_t* full = (uint64_t*)(xs + MR * nch);
   uint64_t* empty = full + stages;
-  asm volatile("griddepcontrol.launch_dependents;");
+  // DC_F_LATE_RELEASE: the dependent launches when this grid completes
+  if (!(flags & DC_F_LATE_RELEASE)) asm volatile("griddepcontrol.launch_dependents;");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bz = blockIdx.y;
   const int rb = blockIdx.x * rows_per_cta;

@@ -16,6 +16,10 @@
 // row 2j, up_j at 2j + 1) stores h_j = f32(silu(g_j) * u_j) instead of the two
 // outputs, and folds |h_j| into a row maximum (dc_gemv_swiglu).
 #define DC_F_SWIGLU 0x200u
+// Internal: the one-row GEMV releases its programmatic dependent only after
+// its own grid-dependency wait (the decode attention after the QKV projection
+// reads older cache rows before its wait; they must follow the previous step).
+#define DC_F_LATE_RELEASE 0x400u
 
 // Device status word bits (atomicOr'd by kernels, read and cleared by dc_sync).
 #define DC_ST_NONFINITE 1

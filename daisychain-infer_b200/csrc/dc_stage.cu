@@ -106,8 +106,8 @@ struct dc_stage {
   int* vchgg = nullptr;     // [DC_MAX_CHUNKS][kvDim]
   int8_t* v8s = nullptr;    // [max_chunks - 1][kvDim][ldp]
   int max_chunks = 1;       // chunks one pass may hold (min(max_rows, DC_MAX_CHUNKS))
-  int8_t* q8d = nullptr;    // decode row: the rotated query heads quantised [head][hd] (k_rope_append)
-  float* qsd = nullptr;     // and their scales [head]
+  uint32_t* vstage = nullptr;  // [2][kvDim] decode row: the attention's new value channel maxima, then scales
+                               // (float bits), committed to the layer's cache by the O projection
   cudaGraphExec_t lap_exec = nullptr;
   unsigned long long lap_nk = 0;  // kernels in one replay of lap_exec
   float* xrow = nullptr;              // one-row graph: the row, in place
@@ -510,8 +510,7 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
                                                     int8_t* k8, float* ks,
                                                     float* vcache, uint32_t* vmax,
                                                     float* vs, int* vchg,
-                                                    int8_t* v8t, int ldp, int* status,
-                                                    int8_t* q8, float* qs, float* vt, int ldvt) {
+                                                    int8_t* v8t, int ldp, int* status, float* vt, int ldvt) {
   // The decode attention after this kernel reads the cache's older keys and
   // int8 values before its own grid-dependency wait.  Its launch is released
   // only once this kernel has passed its wait, so every earlier kernel -- the
@@ -573,31 +572,13 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
     if (isq) {
       o[i] = na;
       o[half + i] = nb;
-    }
-    if (!isq || q8) {
+    } else {
       kr[i] = na;
       kr[half + i] = nb;
     }
   }
-  if (isq && !q8) return;
+  if (isq) return;
   __syncthreads();
-  if (isq) {
-    // one decode row: the rotated query head quantised here (quantizeRows of the
-    // head's hd values, the scale kept in double for the quotients), so the
-    // attention reads it ready (infer.js:177-180)
-    float mx = 0.0f;
-    for (int c = threadIdx.x; c < hd; c += blockDim.x) {
-      const float v = kr[c];
-      bad |= !isfinite(v);
-      mx = fmaxf(mx, fabsf(v));
-    }
-    mx = block_max_f(mx, red);
-    const double qsc = quant_scale(mx), rqsc = __drcp_rn(qsc);
-    if (threadIdx.x == 0) qs[hh] = __double2float_rn(qsc);
-    for (int c = threadIdx.x; c < hd; c += blockDim.x) q8[hh * hd + c] = dc_quant_div((double)kr[c], qsc, rqsc);
-    if (bad) atomicOr(status, DC_ST_NONFINITE);
-    return;
-  }
   // the rotated key: absmax over hd, f32 scale (quantizeCols rule), int8 row
   float mx = 0.0f;
   for (int c = threadIdx.x; c < hd; c += blockDim.x) {
@@ -1590,17 +1571,20 @@ __device__ __noinline__ double dcl_exact_z(double* xs, float* af, int N, int S, 
 // exchange through distributed shared memory what the softmax needs across
 // blocks (the maximum, the partial sums of e, the probability maximum, and
 // finally the int8 probability rows for the context).  Each CTA then forms the
-// context of its CH channels over all keys.  The numbers are k_attention_dec's.
-// Every CTA takes every cluster barrier on every path.
+// context of its CH channels over all keys.  The numbers are k_attention_dec's
+// after k_rope_append, whose one-row work (RoPE, the query and key
+// quantisation, the value append and channel scales) each CTA does itself for
+// its head and channels.  Every CTA takes every cluster barrier on every path.
 __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv, int nH, int nKV, int hd,
-                                                       const int8_t* k8, const float* ks,
+                                                       int8_t* k8, float* ks,
                                                        int8_t* v8t, const float* vs,
                                                        const int* n0p, int max_pos, int ldp, int CH,
                                                        double scale, float* out,
                                                        uint32_t* rowmax, int* done,
                                                        int8_t* xq, int ldq, float* rsq,
-                                                       int* status, const float* vt, int ldvt, const int* vchg,
-                                                       const int8_t* q8g, const float* qsg) {
+                                                       int* status, float* vt, int ldvt, const float* rc,
+                                                       const float* rsn, float* vcache, const uint32_t* vmax,
+                                                       uint32_t* vmax_next, float* vs_next) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   extern __shared__ __align__(16) uint8_t sm[];
@@ -1613,6 +1597,10 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   int8_t* a8 = (int8_t*)(af + ldp);                            // ldp bytes
   __shared__ __align__(8) uint64_t full[ATTD_NS], vbar, sbar;
   __shared__ __align__(16) int8_t q8[256];
+  __shared__ __align__(16) int8_t knew[256];  // this step's key, rotated and quantised
+  __shared__ float ch_ns[32];                 // this CTA's value channels: their scales after this step,
+  __shared__ int8_t ch_q[32];                 //   their int8 values at position n0
+  __shared__ unsigned chg_mask;               //   and which of them moved (bit per channel)
   __shared__ float red[32];
   __shared__ double2 redd2[32];  // also the 32 doubles of block_max_d / block_sum_d
   double* redd = reinterpret_cast<double*>(redd2);
@@ -1637,8 +1625,8 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   // keys, key scales and int8 values of positions below n0 were written by
   // earlier steps: they are read before the grid-dependency wait, so their
   // copies overlap the kernels in front of this one.  Position n0 (this
-  // step's key and value) and the value channels whose scale moved this step
-  // come after it.
+  // step's key and value, formed here in step 1) and the value channels whose
+  // scale moved this step come after it.
   const int n0 = *n0p, N = n0 + 1;
   const int ldpN = (N + 15) & ~15;
   const int nb = (N + ATTD_KB - 1) / ATTD_KB;
@@ -1684,25 +1672,111 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     }
   }
   const bool scales_early = issued[0] >= 0;
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
-  if (warp == 0 && lane == 0 && nmine > 0) {
-    #pragma unroll 1
-    for (int i = 0; i < ATTD_NS && i < nmine; i++)
-      if (issued[i] < 0) key_block(i, i == 0 ? s_all : 0u);
-    if (!scales_early) {
-      dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_all, &full[0]);
-    } else if (last_mine && s_all > s_old) {
-      dcp::mbar_expect_tx(&sbar, s_all - s_old);
-      dcp::bulk_load(af + (s_old >> 2), ks + (int64_t)g * max_pos + (s_old >> 2), s_all - s_old, &sbar);
+  // 1. this step's row (infer.js:139-165), computed alike by every head of the
+  // KV group; the group's first head writes the key and this CTA's value
+  // channels to the cache (no CTA reads them there during this step):
+  //  - the query head and the kv head's new key rotated (f32(a c - b s),
+  //    f32(b c + a s) in double) and quantised (the query per row, double
+  //    scale; the key by the quantizeCols rule, f32 scale);
+  //  - this CTA's value channels: appended, their running |v| maximum and the
+  //    scale it gives, the change flag against the current scale, and the
+  //    int8 value of the new position.  The new maxima and scales go to
+  //    vmax_next / vs_next: every cluster of the KV group reads the current
+  //    ones during this kernel, and the O projection commits them.
+  // The rotation tables, the channel maxima and scales are read before the
+  // grid-dependency wait (the kernel before this one releases it only after its
+  // own wait, so every earlier kernel has completed); the row after it.
+  const int qDim = nH * hd, kvDim = nKV * hd, half = hd >> 1;
+  const bool writer = hq % (nH / nKV) == 0;
+  bool bad = false;
+  // thread i < hd / 2 rotates the pairs (i, i + hd/2) of the query head and the
+  // key; warp 0's lanes < CH hold this CTA's value channels
+  const bool rt = tid < half;
+  float qa = 0.0f, qb = 0.0f, ka = 0.0f, kb = 0.0f;
+  {
+    const double c = rt ? (double)rc[(int64_t)n0 * half + tid] : 0.0;
+    const double s = rt ? (double)rsn[(int64_t)n0 * half + tid] : 0.0;
+    const int cc = g * hd + c0 + lane;
+    const bool vl = warp == 0 && lane < CH;
+    const uint32_t vm0 = vl ? vmax[cc] : 0u;
+    const float vs0 = vl ? vs[cc] : 0.0f;
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+    if (warp == 0 && lane == 0 && nmine > 0) {
+      #pragma unroll 1
+      for (int i = 0; i < ATTD_NS && i < nmine; i++)
+        if (issued[i] < 0) key_block(i, i == 0 ? s_all : 0u);
+      if (!scales_early) {
+        dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_all, &full[0]);
+      } else if (last_mine && s_all > s_old) {
+        dcp::mbar_expect_tx(&sbar, s_all - s_old);
+        dcp::bulk_load(af + (s_old >> 2), ks + (int64_t)g * max_pos + (s_old >> 2), s_all - s_old, &sbar);
+      }
+    }
+    if (rt) {
+      const double a = h[hq * hd + tid], b = h[hq * hd + half + tid];
+      const double e = h[qDim + g * hd + tid], f = h[qDim + g * hd + half + tid];
+      qa = __double2float_rn(__dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s)));
+      qb = __double2float_rn(__dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s)));
+      ka = __double2float_rn(__dsub_rn(__dmul_rn(e, c), __dmul_rn(f, s)));
+      kb = __double2float_rn(__dadd_rn(__dmul_rn(f, c), __dmul_rn(e, s)));
+      bad |= !isfinite(qa) || !isfinite(qb) || !isfinite(ka) || !isfinite(kb);
+    }
+    if (warp == 0) {
+      bool mv = false;
+      if (vl) {
+        const float v = h[qDim + kvDim + cc];
+        bad |= !isfinite(v);
+        const uint32_t mx = max(vm0, __float_as_uint(fabsf(v)));
+        const float ns = __double2float_rn(quant_scale(__uint_as_float(mx)));
+        mv = n0 == 0 || ns != vs0;
+        const int8_t qv = dc_clamp8(dc_js_round(dc_ddiv_slow((double)v, (double)ns)));
+        ch_ns[lane] = ns;
+        ch_q[lane] = qv;
+        if (writer) {
+          vcache[(int64_t)n0 * kvDim + cc] = v;
+          vt[(int64_t)cc * ldvt + n0] = v;
+          v8t[(int64_t)cc * ldp + n0] = qv;
+          vmax_next[cc] = mx;
+          vs_next[cc] = ns;
+        }
+      }
+      const unsigned vm = __ballot_sync(0xffffffffu, mv);
+      if (lane == 0) chg_mask = vm;
     }
   }
-  const bool late_scales = nmine > 0 && scales_early && last_mine && s_all > s_old;
-  // 1. the query row, quantised by k_rope_append (its non-finite check too)
-  (void)h;
-  bool bad = false;
-  if (tid < (hd >> 4)) ((int4*)q8)[tid] = ((const int4*)(q8g + hq * hd))[tid];
-  const float qs = qsg[hq];
+  {
+    float mq = fmaxf(fabsf(qa), fabsf(qb)), mk = fmaxf(fabsf(ka), fabsf(kb));
+    for (int o = 16; o; o >>= 1) {
+      mq = fmaxf(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+      mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+    }
+    if (lane == 0) {
+      red[warp] = mq;
+      red[8 + warp] = mk;
+    }
+  }
   __syncthreads();
+  float mq = red[0], mk = red[8];
+  for (int w = 1; w < 8; w++) {
+    mq = fmaxf(mq, red[w]);
+    mk = fmaxf(mk, red[8 + w]);
+  }
+  const double qsc = quant_scale(mq);
+  const float qs = __double2float_rn(qsc);
+  const float ksc = __double2float_rn(quant_scale(mk));
+  if (rt) {
+    const double rqsc = __drcp_rn(qsc), rksc = __drcp_rn((double)ksc);
+    q8[tid] = dc_quant_div((double)qa, qsc, rqsc);
+    q8[half + tid] = dc_quant_div((double)qb, qsc, rqsc);
+    knew[tid] = dc_quant_div((double)ka, (double)ksc, rksc);
+    knew[half + tid] = dc_quant_div((double)kb, (double)ksc, rksc);
+  }
+  __syncthreads();
+  const bool late_scales = nmine > 0 && scales_early && last_mine && s_all > s_old;
+  if (writer && last_mine) {  // the group's copy of the new key
+    if (tid < (hd >> 4)) ((int4*)(k8 + ((int64_t)g * max_pos + n0) * hd))[tid] = ((const int4*)knew)[tid];
+    if (tid == 0) ks[(int64_t)g * max_pos + n0] = ksc;
+  }
   // 2. scores of this CTA's key blocks (one key per thread)
   const int nchk = hd >> 4;
   const int rot = lane >> 2;
@@ -1711,6 +1785,11 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     const int slot = i % ATTD_NS, b = r + i * S;
     if (!dcp::mbar_wait(&full[slot], (uint32_t)(i / ATTD_NS) & 1u, status)) abort_flag = 1;
     if (late_scales && b == nb - 1 && !dcp::mbar_wait(&sbar, 0, status)) abort_flag = 1;
+    if (b == nb - 1) {  // the block holding position n0: its key and scale from step 1
+      if (tid < (hd >> 4))
+        ((int4*)(sK + (size_t)slot * ATTD_KB * hd + (size_t)(n0 - b * ATTD_KB) * hd))[tid] = ((const int4*)knew)[tid];
+      if (tid == 0) af[n0] = ksc;
+    }
     __syncthreads();
     if (abort_flag) break;
     const int kb = b * ATTD_KB, kn = min(ATTD_KB, N - kb);
@@ -1837,21 +1916,13 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const bool vok = dcp::mbar_wait(&vbar, 0, status);
   if (!vok) abort_flag = 1;
   __syncthreads();
-  if (!abort_flag && vt) {
+  if (!abort_flag) {
     // The value rows came in before the grid-dependency wait.  This step's
-    // column n0 (appended under the channel's new scale) is taken now, and a
-    // channel whose scale moved this step is re-quantised here from the f32
-    // cache (k_vquant_dev's arithmetic); the first head of the KV group writes
-    // those rows back for the next steps (another head reading them meanwhile
-    // re-quantises the same channel itself).
-    const bool writer = hq % (nH / nKV) == 0;
-    // the CTA's moved channels (CH <= 32), gathered in one warp vote
-    __shared__ unsigned chg_mask;
-    if (warp == 0) {
-      const unsigned m = __ballot_sync(0xffffffffu, lane < CH && vchg[g * hd + c0 + lane] != 0);
-      if (lane == 0) chg_mask = m;
-    }
-    __syncthreads();
+    // column n0 is taken from step 1, and a channel whose scale moved this step
+    // is re-quantised here from the f32 cache (k_vquant_dev's arithmetic); the
+    // first head of the KV group writes those rows back for the next steps
+    // (another head reading them meanwhile re-quantises the same channel
+    // itself).
     // every moved channel's rows at once: (channel, row) pairs flattened over
     // the block, eight loads in flight per thread, read along the channel-major
     // f32 copy (contiguous per channel)
@@ -1861,7 +1932,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     if (tid < 32 && ((chg_mask >> tid) & 1u)) {
       const int slot = __popc(chg_mask & ((1u << tid) - 1u));
       mlist[slot] = tid;
-      msc[slot] = (double)vs[g * hd + c0 + tid];
+      msc[slot] = (double)ch_ns[tid];
       mrs[slot] = __drcp_rn(msc[slot]);
     }
     __syncthreads();
@@ -1885,7 +1956,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
         }
       }
     }
-    for (int c = tid; c < CH; c += 256) sV[(size_t)c * ldpv + n0] = v8t[((int64_t)g * hd + c0 + c) * ldp + n0];
+    for (int c = tid; c < CH; c += 256) sV[(size_t)c * ldpv + n0] = ch_q[c];
     __syncthreads();
   }
   float cmx = 0.0f;  // this thread's |context| maximum
@@ -1907,7 +1978,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       if (lane < 4) {
         const int c = c0 + cl4 + lane;
         const int acc = lane == 0 ? sacc[0] : lane == 1 ? sacc[1] : lane == 2 ? sacc[2] : sacc[3];
-        const float o = dc_epi(acc, as, vs[g * hd + c]);
+        const float o = dc_epi(acc, as, ch_ns[c - c0]);
         out[hq * hd + c] = o;
         bad |= !isfinite(o);
         cmx = fmaxf(cmx, fabsf(o));
@@ -2034,6 +2105,14 @@ __global__ void __launch_bounds__(256) k_rowquant(const float* x, int64_t ldx, i
 // ldK; FG_ROWQ: ldK (the int8 row).
 constexpr int FG_THREADS = 512;
 constexpr int FG_SEG = 8;
+// A copy the fused GEMV makes after its wait (n 0: none): src[i] -> vmax[i] and
+// the float bits src[n + i] -> vs[i], i < n.
+struct VCommit {
+  const uint32_t* src;
+  uint32_t* vmax;
+  float* vs;
+  int n;
+};
 enum { FG_NORM = 1, FG_ROWQ = 2, FG_SWIGLU = 4 };
 static size_t fg_smem(int mode, int K) {
   return ((mode & FG_NORM) ? 16 * (size_t)K : 0) + (size_t)round_up(K, 16) + 16;
@@ -2050,14 +2129,14 @@ __global__ void __launch_bounds__(FG_THREADS, 1) k_gemv_fused(const float* x, in
                                                               const uint32_t* rmax, const int8_t* __restrict__ Wt,
                                                               int ldw, const float* __restrict__ cs, int n,
                                                               unsigned flags, float* out, uint32_t* rmax_out,
-                                                              uint32_t* zero2, int* status) {
+                                                              uint32_t* zero2, int* status, VCommit vc) {
   extern __shared__ __align__(16) uint8_t fsm[];
   __shared__ float red[32];
   __shared__ double2 redd2[32];
   __shared__ int vote[32];
   __shared__ float s_row;
   __shared__ dco::Smem16 osm;
-  asm volatile("griddepcontrol.launch_dependents;");
+  if (!(flags & DC_F_LATE_RELEASE)) asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gw = blockIdx.x * (FG_THREADS / 32) + warp, nwarps = gridDim.x * (FG_THREADS / 32);
   const int ldK = (K + 15) & ~15;
@@ -2085,9 +2164,15 @@ __global__ void __launch_bounds__(FG_THREADS, 1) k_gemv_fused(const float* x, in
     wpend = true;
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (flags & DC_F_LATE_RELEASE) asm volatile("griddepcontrol.launch_dependents;");
   if (zero2 && blockIdx.x == 0 && threadIdx.x == 0) {
     zero2[0] = 0;
     zero2[1] = 0;
+  }
+  // the decode attention's new value channel maxima and scales into the cache's
+  for (int i = blockIdx.x * FG_THREADS + threadIdx.x; i < vc.n; i += gridDim.x * FG_THREADS) {
+    vc.vmax[i] = vc.src[i];
+    vc.vs[i] = __uint_as_float(vc.src[vc.n + i]);
   }
   // ---- prologue: the int8 activation row in shared memory
   if (MODE & FG_NORM) {
@@ -2446,8 +2531,7 @@ extern "C" int dc_stage_create(dc_ctx* ctx, const dc_spec* spec, int lo, int hi,
       (rc = st_alloc(S, (void**)&S->att_done, 16)) ||
       (rc = st_alloc(S, (void**)&S->xrow, 4 * (size_t)S->C)) ||
       (rc = st_alloc(S, (void**)&S->a8g, (size_t)S->max_rows * S->nH * S->ldp)) ||
-      (rc = st_alloc(S, (void**)&S->q8d, (size_t)round_up(S->qDim, 16))) ||
-      (rc = st_alloc(S, (void**)&S->qsd, 4 * (size_t)S->nH)) ||
+      (rc = st_alloc(S, (void**)&S->vstage, 8 * (size_t)S->kvDim)) ||
       (rc = st_alloc(S, (void**)&S->asg, 4 * (size_t)S->max_rows * S->nH)) ||
       (rc = st_alloc(S, (void**)&S->vsg, 4 * (size_t)DC_MAX_CHUNKS * S->kvDim)) ||
       (rc = st_alloc(S, (void**)&S->vchgg, 4 * (size_t)DC_MAX_CHUNKS * S->kvDim)) ||
@@ -2715,7 +2799,8 @@ static bool fg_fits(const dc_stage* S) {
 // k_gemv_fused<mode> over the weight m (out = epilogue of m's n columns; with
 // FG_SWIGLU the n/2 SwiGLU values), launched as a programmatic dependent.
 static cudaError_t launch_fused(dc_stage* S, int mode, const float* x, int K, const float* nw, const uint32_t* rmax,
-                                const dc_mat& m, unsigned flags, float* out, uint32_t* rmax_out, uint32_t* zero2) {
+                                const dc_mat& m, unsigned flags, float* out, uint32_t* rmax_out, uint32_t* zero2,
+                                VCommit vc = {nullptr, nullptr, nullptr, 0}) {
   dc_ctx* ctx = S->ctx;
   const int blocks = std::max(1, std::min(ctx->sm_count, (m.n + 31) / 32));
   const size_t smem = fg_smem(mode, K);
@@ -2724,17 +2809,17 @@ static cudaError_t launch_fused(dc_stage* S, int mode, const float* x, int K, co
     case FG_NORM:
       e = launch_dep(k_gemv_fused<FG_NORM>, dim3(blocks), dim3(FG_THREADS), smem, ctx->stream, x, K, nw,
                      S->spec.norm_eps, rmax, (const int8_t*)m.qt, m.ldk, (const float*)m.cs, m.n, flags, out, rmax_out,
-                     zero2, ctx->d_status);
+                     zero2, ctx->d_status, vc);
       break;
     case FG_NORM | FG_SWIGLU:
       e = launch_dep(k_gemv_fused<FG_NORM | FG_SWIGLU>, dim3(blocks), dim3(FG_THREADS), smem, ctx->stream, x, K, nw,
                      S->spec.norm_eps, rmax, (const int8_t*)m.qt, m.ldk, (const float*)m.cs, m.n, flags, out, rmax_out,
-                     zero2, ctx->d_status);
+                     zero2, ctx->d_status, vc);
       break;
     default:
       e = launch_dep(k_gemv_fused<FG_ROWQ>, dim3(blocks), dim3(FG_THREADS), smem, ctx->stream, x, K, nw,
                      S->spec.norm_eps, rmax, (const int8_t*)m.qt, m.ldk, (const float*)m.cs, m.n, flags, out, rmax_out,
-                     zero2, ctx->d_status);
+                     zero2, ctx->d_status, vc);
       break;
   }
   dc_count_launch();
@@ -2815,28 +2900,34 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       return rc0;
     if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_ROWQ>, (int)fg_smem(FG_ROWQ, S->I))) return rc0;
   }
+  // the decode row's cluster attention: it rotates, quantises and appends the
+  // step's row itself (no k_rope_append), re-quantises moved value channels,
+  // and leaves the new channel maxima and scales for the O projection to commit
+  const bool dcl = T == 1 && use_kv && dec_ch && o_rowq && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8;
+  // its kernel before releases it only after that kernel's own wait
+  const unsigned qkv_flags = dcl ? DC_F_LATE_RELEASE : 0u;
   int rc;
   for (auto& ly : S->L) {
     dc_kv& kv = ly.kv;
     // attention block
     if (fuse) {  // RMSNorm + QKV; zeroes the row maxima the attention and the SwiGLU collect
-      DC_CUDA(ctx, launch_fused(S, FG_NORM, x, S->C, ly.nrm1, nullptr, ly.qkv, 0, S->hbuf, nullptr, S->rowmax));
+      DC_CUDA(ctx, launch_fused(S, FG_NORM, x, S->C, ly.nrm1, nullptr, ly.qkv, qkv_flags, S->hbuf, nullptr,
+                                S->rowmax));
     } else {
       DC_CUDA(ctx, launch_dep(norm_k, dim3(T), dim3(norm_nt), nrm_smem, st, x, S->C, ly.nrm1,
                               S->spec.norm_eps, S->xq, S->ldC, S->rs, ctx->d_status, nullptr, S->rowmax, 0));
       dc_count_launch();
-      if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, 0))) return rc;
+      if ((rc = gemm(S, ly.qkv, T, S->xq, S->ldC, S->hbuf, qkv_flags))) return rc;
     }
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
-    // the decode row's cluster attention: it takes the query heads quantised by
-    // k_rope_append and re-quantises moved value channels itself
-    const bool dcl = T == 1 && use_kv && dec_ch && S->hd / dec_ch > 1 && S->hd / dec_ch <= 8;
-    const int vblocks = (S->kvDim + 63) / 64;
-    DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
-                            S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
-                            multi ? nullptr : kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp, ctx->d_status,
-                            dcl ? S->q8d : nullptr, S->qsd, kv.vt, S->ldvt));
-    dc_count_launch();
+    if (!dcl) {
+      const int vblocks = (S->kvDim + 63) / 64;
+      DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
+                              S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
+                              multi ? nullptr : kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp,
+                              ctx->d_status, kv.vt, S->ldvt));
+      dc_count_launch();
+    }
     if (multi) {
       DC_CUDA(ctx, launch_dep(k_vscale_chunks, dim3((S->kvDim + 31) / 32), dim3(32 * DC_MAX_CHUNKS), 0, st,
                               (const float*)kv.v,
@@ -2878,11 +2969,11 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
       cfg.attrs = attr;
       cfg.numAttrs = 2;
       DC_CUDA(ctx, cudaLaunchKernelEx(&cfg, k_attention_dcl, (const float*)S->hbuf, S->nqkv, S->nH, S->nKV, S->hd,
-                                      (const int8_t*)kv.k8, (const float*)kv.ks, kv.v8t, (const float*)kv.vs, n0p,
-                                      S->max_pos, S->ldp, dec_ch, scale, S->ctxo, S->rowmax, S->att_done,
-                                      o_rowq ? nullptr : S->xq, S->ldQ, S->rs, ctx->d_status, (const float*)kv.vt,
-                                      S->ldvt, (const int*)kv.vchg,
-                                      (const int8_t*)S->q8d, (const float*)S->qsd));
+                                      kv.k8, kv.ks, kv.v8t, (const float*)kv.vs, n0p, S->max_pos, S->ldp, dec_ch,
+                                      scale, S->ctxo, S->rowmax, S->att_done, (int8_t*)nullptr, S->ldQ, S->rs,
+                                      ctx->d_status, kv.vt, S->ldvt, (const float*)S->rope_cos,
+                                      (const float*)S->rope_sin, kv.v, (const uint32_t*)kv.vmax, S->vstage,
+                                      (float*)(S->vstage + S->kvDim)));
       dc_count_launch();
     } else if (T == 1 && use_kv && dec_ch) {
       DC_CUDA(ctx, launch_dep(k_attention_dec, dim3(S->nH, S->hd / dec_ch), dim3(256), dec_smem, st, S->hbuf, S->nqkv,
@@ -2922,9 +3013,9 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                                                                 S->rs);
       dc_count_launch();
     }
-    if (dcl && o_rowq) {  // x2 = x + attn, the context row quantised by the GEMV's blocks
+    if (dcl) {  // x2 = x + attn, the context row quantised by the GEMV's blocks; the value scales committed
       DC_CUDA(ctx, launch_fused(S, FG_ROWQ, S->ctxo, S->qDim, nullptr, S->rowmax, ly.o, DC_F_ADDTO, x, nullptr,
-                                nullptr));
+                                nullptr, VCommit{S->vstage, kv.vmax, kv.vs, S->kvDim}));
     } else if ((rc = gemm(S, ly.o, T, S->xq, S->ldQ, x, DC_F_ADDTO))) {  // x2 = x + attn
       return rc;
     }
