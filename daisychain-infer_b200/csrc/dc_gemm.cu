@@ -198,6 +198,11 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
   const int4* X4 = (const int4*)X;
   const uint64_t pol = dcp::l2_evict_first();
   bool waited = false;
+  // loaded right after the wait, so that their round trips overlap the
+  // weight stream: the row scale, and (f32 residual adds) this lane's output
+  // value of the warp's first pair
+  const bool addto = (flags & DC_F_ADDTO) && !(flags & (DC_ACC | DC_REQUANT | DC_F_SWIGLU));
+  float rs0 = 0.0f, res0 = 0.0f;
   for (int j0 = gw * 2; j0 < n; j0 += nw * 2, t++) {
     const int j1 = min(j0 + 1, n - 1);
     const int4* w0 = (const int4*)(Wt + (int64_t)j0 * ldw);
@@ -240,6 +245,8 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
         asm volatile("griddepcontrol.wait;" ::: "memory");
         waited = true;
         if (flags & DC_F_LATE_RELEASE) asm volatile("griddepcontrol.launch_dependents;");
+        rs0 = rs[0];
+        if (addto && lane < 2 && j0 + lane < n) res0 = ((const float*)out)[j0 + lane];
       }
 #pragma unroll
       for (int u = 0; u < GV_SEG; u++) {
@@ -267,9 +274,15 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
         sj = j0 >> 1;
       }
       if ((t & 31) == 31) swiglu_flush();
+    } else if (addto && t == 0) {  // the first pair: its residuals are in res0
+      if (lane < 2 && j0 + lane < n) {
+        float v = dc_epi(lane == 0 ? a0 : a1, rs0, csv);
+        if ((flags & DC_RELU) && v < 0.0f) v = 0.0f;
+        ((float*)out)[j0 + lane] = __fadd_rn(res0, v);  // residual: out = out + v (f32 add)
+      }
     } else {
-      if (lane == 0) dc_store_out(out, j0, a0, rs[0], csv, flags, requant, relu);
-      if (lane == 1 && j0 + 1 < n) dc_store_out(out, j0 + 1, a1, rs[0], csv, flags, requant, relu);
+      if (lane == 0) dc_store_out(out, j0, a0, rs0, csv, flags, requant, relu);
+      if (lane == 1 && j0 + 1 < n) dc_store_out(out, j0 + 1, a1, rs0, csv, flags, requant, relu);
     }
   }
   if (!waited) {

@@ -1595,12 +1595,14 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   double* xs = (double*)(sV + (size_t)CH * ldpv);              // ldp doubles: s*scale, then e
   float* af = (float*)(xs + ldp);                              // ldp floats: key scales, then f32(e), then a
   int8_t* a8 = (int8_t*)(af + ldp);                            // ldp bytes
-  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar, sbar;
+  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar, sbar, mvbar;
   __shared__ __align__(16) int8_t q8[256];
   __shared__ __align__(16) int8_t knew[256];  // this step's key, rotated and quantised
   __shared__ float ch_ns[32];                 // this CTA's value channels: their scales after this step,
   __shared__ int8_t ch_q[32];                 //   their int8 values at position n0
-  __shared__ unsigned chg_mask;               //   and which of them moved (bit per channel)
+  __shared__ unsigned chg_mask;               //   and which of them moved (bit per channel):
+  __shared__ int mlist[32];                   //   the moved ones in order, their new scales
+  __shared__ double msc[32], mrs[32];         //   and the scales' reciprocals
   __shared__ float red[32];
   __shared__ double2 redd2[32];  // also the 32 doubles of block_max_d / block_sum_d
   double* redd = reinterpret_cast<double*>(redd2);
@@ -1636,6 +1638,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     for (int i = 0; i < ATTD_NS; i++) dcp::mbar_init(&full[i], 1);
     dcp::mbar_init(&vbar, 1);
     dcp::mbar_init(&sbar, 1);
+    dcp::mbar_init(&mvbar, 1);
     abort_flag = 0;
     dcp::mbar_fence_init();
   }
@@ -1742,6 +1745,12 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       }
       const unsigned vm = __ballot_sync(0xffffffffu, mv);
       if (lane == 0) chg_mask = vm;
+      if (mv) {  // the moved channels in order, with their new scales
+        const int slot = __popc(vm & ((1u << lane) - 1u));
+        mlist[slot] = lane;
+        msc[slot] = (double)ch_ns[lane];
+        mrs[slot] = __drcp_rn(msc[slot]);
+      }
     }
   }
   {
@@ -1772,6 +1781,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     knew[half + tid] = dc_quant_div((double)kb, (double)ksc, rksc);
   }
   __syncthreads();
+  const int nmv = __popc(chg_mask);  // moved value channels of this CTA
   const bool late_scales = nmine > 0 && scales_early && last_mine && s_all > s_old;
   if (writer && last_mine) {  // the group's copy of the new key
     if (tid < (hd >> 4)) ((int4*)(k8 + ((int64_t)g * max_pos + n0) * hd))[tid] = ((const int4*)knew)[tid];
@@ -1815,6 +1825,19 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       dcp::mbar_expect_tx(&full[slot], bytes);
       dcp::bulk_load(sK + (size_t)slot * ATTD_KB * hd, kg + (int64_t)b2 * ATTD_KB * hd, bytes, &full[slot]);
     }
+  }
+  // The key ring is free from here on: the moved channels' f32 rows (as many
+  // as it holds) are copied into it now, so that the copies overlap the
+  // softmax; step 8 re-quantises them from shared memory.
+  const uint32_t mrow = (uint32_t)((n0 * 4 + 15) & ~15);
+  const int ring_rows = mrow ? min(nmv, (int)((size_t)ATTD_NS * ATTD_KB * hd / mrow)) : 0;
+  bool mv_issued = false;  // (thread 0)
+  if (tid == 0 && ring_rows > 0 && !abort_flag) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the scores' reads of the ring
+    dcp::mbar_expect_tx(&mvbar, (uint32_t)ring_rows * mrow);
+    for (int m = 0; m < ring_rows; m++)
+      dcp::bulk_load(sK + (size_t)m * mrow, vt + (int64_t)(g * hd + c0 + mlist[m]) * ldvt, mrow, &mvbar);
+    mv_issued = true;
   }
   // 3. the exact maximum over the cluster
   for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -1913,7 +1936,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   }
   const float as = __double2float_rn(asc);
   // 8. the context of this CTA's CH channels over all keys
-  const bool vok = dcp::mbar_wait(&vbar, 0, status);
+  const bool vok = dcp::mbar_wait(&vbar, 0, status) && (ring_rows == 0 || abort_flag || dcp::mbar_wait(&mvbar, 0, status));
   if (!vok) abort_flag = 1;
   __syncthreads();
   if (!abort_flag) {
@@ -1923,36 +1946,37 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     // first head of the KV group writes those rows back for the next steps
     // (another head reading them meanwhile re-quantises the same channel
     // itself).
-    // every moved channel's rows at once: (channel, row) pairs flattened over
-    // the block, eight loads in flight per thread, read along the channel-major
-    // f32 copy (contiguous per channel)
-    __shared__ int mlist[32];
-    __shared__ double msc[32], mrs[32];
-    const int nm = __popc(chg_mask);
-    if (tid < 32 && ((chg_mask >> tid) & 1u)) {
-      const int slot = __popc(chg_mask & ((1u << tid) - 1u));
-      mlist[slot] = tid;
-      msc[slot] = (double)ch_ns[tid];
-      mrs[slot] = __drcp_rn(msc[slot]);
-    }
-    __syncthreads();
-    const int total = nm * n0;
-    #pragma unroll 1
-    for (int i0 = tid; i0 < total; i0 += 8 * 256) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int i = i0 + 256 * u;
-        v[u] = i < total ? __ldcg(vt + (int64_t)(g * hd + c0 + mlist[i / n0]) * ldvt + i % n0) : 0.0f;
+    // the moved channels' rows: from the ring, then any rest from global
+    // memory (eight loads in flight per thread)
+    for (int m = 0; m < nmv; m++) {
+      const int c = mlist[m];
+      const double sc = msc[m], rsc = mrs[m];
+      const float rscf = (float)rsc;
+      int8_t* dq = sV + (size_t)c * ldpv;
+      int8_t* gq = v8t + (int64_t)(g * hd + c0 + c) * ldp;
+      if (m < ring_rows) {
+        const float* src = (const float*)(sK + (size_t)m * mrow);
+        for (int j = tid; j < n0; j += 256) {
+          const int8_t q = dc_quant_div_f(src[j], sc, rsc, rscf);
+          dq[j] = q;
+          if (writer) gq[j] = q;
+        }
+        continue;
       }
+      const float* src = vt + (int64_t)(g * hd + c0 + c) * ldvt;
+      #pragma unroll 1
+      for (int j0 = tid; j0 < n0; j0 += 8 * 256) {
+        float v[8];
 #pragma unroll
-      for (int u = 0; u < 8; u++) {
-        const int i = i0 + 256 * u;
-        if (i < total) {
-          const int m = i / n0, j = i - m * n0, c = mlist[m];
-          const int8_t q = dc_quant_div_f(v[u], msc[m], mrs[m], (float)mrs[m]);
-          sV[(size_t)c * ldpv + j] = q;
-          if (writer) v8t[(int64_t)(g * hd + c0 + c) * ldp + j] = q;
+        for (int u = 0; u < 8; u++) v[u] = j0 + 256 * u < n0 ? __ldcg(src + j0 + 256 * u) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const int j = j0 + 256 * u;
+          if (j < n0) {
+            const int8_t q = dc_quant_div_f(v[u], sc, rsc, rscf);
+            dq[j] = q;
+            if (writer) gq[j] = q;
+          }
         }
       }
     }
@@ -1987,6 +2011,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   }
   if (abort_flag && tid == 0) {
     dcp::mbar_wait(&vbar, 0, status);
+    if (mv_issued) dcp::mbar_wait(&mvbar, 0, status);
     if (late_scales) dcp::mbar_wait(&sbar, 0, status);
     for (int sl = 0; sl < ATTD_NS; sl++)
       if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] / ATTD_NS) & 1u, status);
@@ -2165,6 +2190,10 @@ __global__ void __launch_bounds__(FG_THREADS, 1) k_gemv_fused(const float* x, in
   }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (flags & DC_F_LATE_RELEASE) asm volatile("griddepcontrol.launch_dependents;");
+  // (residual adds) this lane's output value of the warp's first pair, loaded
+  // now so that its round trip overlaps the prologue
+  const bool addto = (flags & DC_F_ADDTO) && !(MODE & FG_SWIGLU);
+  const float res0 = addto && lane < 2 && gw * 2 + lane < n ? out[gw * 2 + lane] : 0.0f;
   if (zero2 && blockIdx.x == 0 && threadIdx.x == 0) {
     zero2[0] = 0;
     zero2[1] = 0;
@@ -2181,10 +2210,25 @@ __global__ void __launch_bounds__(FG_THREADS, 1) k_gemv_fused(const float* x, in
     rmsnorm_quant_block<FG_THREADS / 32>(x, K, wsm, wpend, vec, eps, sq, ys, x8, ldK, &s_row, status, nullptr, 0, osm,
                                          red, redd2, vote);
   } else {
+    // the row's loads eight at a time in flight, then their quotients
+    constexpr int U = 8;
     const double sc = quant_scale(__uint_as_float(*rmax)), rsc = __drcp_rn(sc);
+    const float rscf = __double2float_rn(rsc);
     if (threadIdx.x == 0) s_row = __double2float_rn(sc);
-    for (int j = threadIdx.x; j < ldK; j += blockDim.x)
-      x8[j] = j < K ? dc_quant_div((double)x[j], sc, rsc) : (int8_t)0;
+#pragma unroll 1
+    for (int j0 = threadIdx.x; j0 < ldK; j0 += U * FG_THREADS) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int j = j0 + u * FG_THREADS;
+        v[u] = j < K ? __ldcg(x + j) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int j = j0 + u * FG_THREADS;
+        if (j < ldK) x8[j] = j < K ? dc_quant_div_f(v[u], sc, rsc, rscf) : (int8_t)0;
+      }
+    }
   }
   __syncthreads();
   const float rsv = s_row;
@@ -2231,7 +2275,7 @@ __global__ void __launch_bounds__(FG_THREADS, 1) k_gemv_fused(const float* x, in
     } else if (lane < 2 && (lane == 0 || j0 + 1 < n)) {
       const int j = lane == 0 ? j0 : j1;
       float v = dc_epi(lane == 0 ? a0 : a1, rsv, cs[j]);
-      if (flags & DC_F_ADDTO) v = __fadd_rn(out[j], v);  // residual: out = out + v (f32 add)
+      if (flags & DC_F_ADDTO) v = __fadd_rn(j0 == gw * 2 ? res0 : out[j], v);  // residual: out = out + v (f32 add)
       out[j] = v;
     }
   }
