@@ -1700,7 +1700,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     const double c = rt ? (double)rc[(int64_t)n0 * half + tid] : 0.0;
     const double s = rt ? (double)rsn[(int64_t)n0 * half + tid] : 0.0;
     const int cc = g * hd + c0 + lane;
-    const bool vl = warp == 0 && lane < CH;
+    const bool vl = warp == 7 && lane < CH;  // (the rotation takes threads below hd / 2 <= 128)
     const uint32_t vm0 = vl ? vmax[cc] : 0u;
     const float vs0 = vl ? vs[cc] : 0.0f;
     asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
@@ -1724,7 +1724,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       kb = __double2float_rn(__dadd_rn(__dmul_rn(f, c), __dmul_rn(e, s)));
       bad |= !isfinite(qa) || !isfinite(qb) || !isfinite(ka) || !isfinite(kb);
     }
-    if (warp == 0) {
+    if (warp == 7) {
       bool mv = false;
       if (vl) {
         const float v = h[qDim + kvDim + cc];
@@ -1775,10 +1775,11 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const float ksc = __double2float_rn(quant_scale(mk));
   if (rt) {
     const double rqsc = __drcp_rn(qsc), rksc = __drcp_rn((double)ksc);
-    q8[tid] = dc_quant_div((double)qa, qsc, rqsc);
-    q8[half + tid] = dc_quant_div((double)qb, qsc, rqsc);
-    knew[tid] = dc_quant_div((double)ka, (double)ksc, rksc);
-    knew[half + tid] = dc_quant_div((double)kb, (double)ksc, rksc);
+    const float rqf = __double2float_rn(rqsc), rkf = __double2float_rn(rksc);
+    q8[tid] = dc_quant_div_f(qa, qsc, rqsc, rqf);
+    q8[half + tid] = dc_quant_div_f(qb, qsc, rqsc, rqf);
+    knew[tid] = dc_quant_div_f(ka, (double)ksc, rksc, rkf);
+    knew[half + tid] = dc_quant_div_f(kb, (double)ksc, rksc, rkf);
   }
   __syncthreads();
   const int nmv = __popc(chg_mask);  // moved value channels of this CTA
@@ -1791,18 +1792,8 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const int nchk = hd >> 4;
   const int rot = lane >> 2;
   double m = -INFINITY;
-  _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
-    const int slot = i % ATTD_NS, b = r + i * S;
-    if (!dcp::mbar_wait(&full[slot], (uint32_t)(i / ATTD_NS) & 1u, status)) abort_flag = 1;
-    if (late_scales && b == nb - 1 && !dcp::mbar_wait(&sbar, 0, status)) abort_flag = 1;
-    if (b == nb - 1) {  // the block holding position n0: its key and scale from step 1
-      if (tid < (hd >> 4))
-        ((int4*)(sK + (size_t)slot * ATTD_KB * hd + (size_t)(n0 - b * ATTD_KB) * hd))[tid] = ((const int4*)knew)[tid];
-      if (tid == 0) af[n0] = ksc;
-    }
-    __syncthreads();
-    if (abort_flag) break;
-    const int kb = b * ATTD_KB, kn = min(ATTD_KB, N - kb);
+  auto score_block = [&](int i, int slot) {
+    const int kb = (r + i * S) * ATTD_KB, kn = min(ATTD_KB, N - kb);
     const int k = tid;
     if (k < kn) {
       const int8_t* kr = sK + (size_t)slot * ATTD_KB * hd + (size_t)k * hd;
@@ -1816,14 +1807,47 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
       xs[kb + k] = x;
       m = fmax(m, x);
     }
+  };
+  if (nmine <= ATTD_NS) {
+    // every key block of this CTA has a ring slot of its own: one barrier for all
+    bool ok = true;
+    for (int i = 0; i < nmine; i++) ok &= dcp::mbar_wait(&full[i], 0u, status);
+    if (late_scales) ok &= dcp::mbar_wait(&sbar, 0, status);
+    if (!ok) abort_flag = 1;
+    if (last_mine) {  // the block holding position n0: its key and scale from step 1
+      const int i = (nb - 1 - r) / S;
+      if (tid < (hd >> 4))
+        ((int4*)(sK + (size_t)i * ATTD_KB * hd + (size_t)(n0 - (nb - 1) * ATTD_KB) * hd))[tid] = ((const int4*)knew)[tid];
+      if (tid == 0) af[n0] = ksc;
+    }
     __syncthreads();
-    if (tid == 0 && i + ATTD_NS < nmine) {
-      issued[slot] = i + ATTD_NS;
-      const int b2 = r + (i + ATTD_NS) * S;
-      const int kn2 = min(ATTD_KB, N - b2 * ATTD_KB);
-      const uint32_t bytes = (uint32_t)(((kn2 * hd) + 15) & ~15);
-      dcp::mbar_expect_tx(&full[slot], bytes);
-      dcp::bulk_load(sK + (size_t)slot * ATTD_KB * hd, kg + (int64_t)b2 * ATTD_KB * hd, bytes, &full[slot]);
+    if (!abort_flag) {
+#pragma unroll
+      for (int i = 0; i < ATTD_NS; i++)
+        if (i < nmine) score_block(i, i);
+    }
+  } else {
+    _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
+      const int slot = i % ATTD_NS, b = r + i * S;
+      if (!dcp::mbar_wait(&full[slot], (uint32_t)(i / ATTD_NS) & 1u, status)) abort_flag = 1;
+      if (late_scales && b == nb - 1 && !dcp::mbar_wait(&sbar, 0, status)) abort_flag = 1;
+      if (b == nb - 1) {  // the block holding position n0: its key and scale from step 1
+        if (tid < (hd >> 4))
+          ((int4*)(sK + (size_t)slot * ATTD_KB * hd + (size_t)(n0 - b * ATTD_KB) * hd))[tid] = ((const int4*)knew)[tid];
+        if (tid == 0) af[n0] = ksc;
+      }
+      __syncthreads();
+      if (abort_flag) break;
+      score_block(i, slot);
+      __syncthreads();
+      if (tid == 0 && i + ATTD_NS < nmine) {
+        issued[slot] = i + ATTD_NS;
+        const int b2 = r + (i + ATTD_NS) * S;
+        const int kn2 = min(ATTD_KB, N - b2 * ATTD_KB);
+        const uint32_t bytes = (uint32_t)(((kn2 * hd) + 15) & ~15);
+        dcp::mbar_expect_tx(&full[slot], bytes);
+        dcp::bulk_load(sK + (size_t)slot * ATTD_KB * hd, kg + (int64_t)b2 * ATTD_KB * hd, bytes, &full[slot]);
+      }
     }
   }
   // The key ring is free from here on: the moved channels' f32 rows (as many
@@ -1832,6 +1856,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   const uint32_t mrow = (uint32_t)((n0 * 4 + 15) & ~15);
   const int ring_rows = mrow ? min(nmv, (int)((size_t)ATTD_NS * ATTD_KB * hd / mrow)) : 0;
   bool mv_issued = false;  // (thread 0)
+  if (ring_rows > 0) __syncthreads();  // every thread's reads of the ring are done
   if (tid == 0 && ring_rows > 0 && !abort_flag) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the scores' reads of the ring
     dcp::mbar_expect_tx(&mvbar, (uint32_t)ring_rows * mrow);
@@ -1887,12 +1912,13 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   // probability bytes, before one cluster barrier.
   float amx = dc_div_to_f32(1.0, zlo, rlo);
   double asc = quant_scale(amx), rasc = __drcp_rn(asc);
+  float rascf = __double2float_rn(rasc);
   bool amb = false;
 #pragma unroll 4
   for (int i = 0; i < nmine; i++) {
     const int j = (r + i * S) * ATTD_KB + tid;
     if (j < ldpN)
-      a8[j] = j < N ? dc_quant_div((double)dc_div_bracket((double)af[j], zlo, rlo, zhi, rhi, narrow, &amb), asc, rasc)
+      a8[j] = j < N ? dc_quant_div_f(dc_div_bracket((double)af[j], zlo, rlo, zhi, rhi, narrow, &amb), asc, rasc, rascf)
                     : (int8_t)0;
   }
   // this CTA's probability bytes to the other CTAs, 16 at a time (remote
@@ -1926,10 +1952,11 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     amx = dc_div_to_f32(1.0, z, rz);
     asc = quant_scale(amx);
     rasc = __drcp_rn(asc);
+    rascf = __double2float_rn(rasc);
 #pragma unroll 4
     for (int i = 0; i < nmine; i++) {
       const int j = (r + i * S) * ATTD_KB + tid;
-      if (j < ldpN) a8[j] = j < N ? dc_quant_div((double)dc_div_to_f32((double)af[j], z, rz), asc, rasc) : (int8_t)0;
+      if (j < ldpN) a8[j] = j < N ? dc_quant_div_f(dc_div_to_f32((double)af[j], z, rz), asc, rasc, rascf) : (int8_t)0;
     }
     send_a8();
     cl.sync();
