@@ -1595,7 +1595,7 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   double* xs = (double*)(sV + (size_t)CH * ldpv);              // ldp doubles: s*scale, then e
   float* af = (float*)(xs + ldp);                              // ldp floats: key scales, then f32(e), then a
   int8_t* a8 = (int8_t*)(af + ldp);                            // ldp bytes
-  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar, sbar, mvbar;
+  __shared__ __align__(8) uint64_t full[ATTD_NS], vbar, mvbar;
   __shared__ __align__(16) int8_t q8[256];
   __shared__ __align__(16) int8_t knew[256];  // this step's key, rotated and quantised
   __shared__ float ch_ns[32];                 // this CTA's value channels: their scales after this step,
@@ -1637,7 +1637,6 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   if (tid == 0) {
     for (int i = 0; i < ATTD_NS; i++) dcp::mbar_init(&full[i], 1);
     dcp::mbar_init(&vbar, 1);
-    dcp::mbar_init(&sbar, 1);
     dcp::mbar_init(&mvbar, 1);
     abort_flag = 0;
     dcp::mbar_fence_init();
@@ -1645,19 +1644,18 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   __syncthreads();
   int issued[ATTD_NS];
   for (int i = 0; i < ATTD_NS; i++) issued[i] = -1;
-  const uint32_t s_old = (uint32_t)((n0 & ~3) * 4);      // key scales below n0, before the wait
-  const uint32_t s_all = (uint32_t)(((N + 3) & ~3) * 4);  // all of them
-  // The key scales ride with the first block: the older ones (below n0 & ~3)
-  // when that block is copied before the grid-dependency wait, all of them
-  // otherwise.  The newer ones (this step's key among them) all belong to the
-  // last block, whose owner alone copies them, after the wait, on `sbar`.
-  auto key_block = [&](int i, uint32_t sc_bytes) {  // lane 0 of warp 0: key block i into ring slot i
+  // Every key and key scale this CTA reads from the cache is older than n0:
+  // the CTA's first ATTD_NS key blocks (without position n0, which step 1
+  // forms) and the scales below n0 are copied before the grid-dependency wait,
+  // the scales on the first block's barrier (all but the last n0 % 4, which
+  // lanes 1-3 load).  Blocks past the ring's slots follow as slots free up.
+  const uint32_t s_old = (uint32_t)((n0 & ~3) * 4);
+  auto key_block = [&](int i, int rows, uint32_t sc_bytes) {  // lane 0 of warp 0: key block i into ring slot i
     issued[i] = i;
     const int b = r + i * S;
-    const int kn = min(ATTD_KB, N - b * ATTD_KB);
-    const uint32_t bytes = (uint32_t)(((kn * hd) + 15) & ~15);
+    const uint32_t bytes = (uint32_t)(rows * hd);  // (hd is a multiple of 16)
     dcp::mbar_expect_tx(&full[i], bytes + sc_bytes);
-    dcp::bulk_load(sK + (size_t)i * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[i]);
+    if (bytes) dcp::bulk_load(sK + (size_t)i * ATTD_KB * hd, kg + (int64_t)b * ATTD_KB * hd, bytes, &full[i]);
   };
   const bool last_mine = (nb - 1) % S == r;  // this CTA owns the block with position n0
   if (warp == 0) {
@@ -1666,15 +1664,17 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     #pragma unroll 1
     for (int c = lane; c < CH; c += 32)
       dcp::bulk_load(sV + (size_t)c * ldpv, v8t + ((int64_t)g * hd + c0 + c) * ldp, (uint32_t)ldpN, &vbar);
-    if (lane == 0) {
+    if (lane == 0 && nmine > 0) {
       #pragma unroll 1
       for (int i = 0; i < ATTD_NS && i < nmine; i++)
-        if ((r + i * S + 1) * ATTD_KB <= n0) key_block(i, i == 0 ? s_old : 0u);  // all its keys older than n0
-      // the older key scales, once the first block's barrier expects them
-      if (issued[0] >= 0 && s_old) dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_old, &full[0]);
+        key_block(i, min(ATTD_KB, n0 - (r + i * S) * ATTD_KB), i == 0 ? s_old : 0u);
+      if (s_old) dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_old, &full[0]);
+    }
+    if (nmine > 0 && lane >= 1 && lane <= (n0 & 3)) {
+      const int j = (n0 & ~3) + lane - 1;
+      af[j] = ks[(int64_t)g * max_pos + j];
     }
   }
-  const bool scales_early = issued[0] >= 0;
   // 1. this step's row (infer.js:139-165), computed alike by every head of the
   // KV group; the group's first head writes the key and this CTA's value
   // channels to the cache (no CTA reads them there during this step):
@@ -1704,17 +1704,6 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     const uint32_t vm0 = vl ? vmax[cc] : 0u;
     const float vs0 = vl ? vs[cc] : 0.0f;
     asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
-    if (warp == 0 && lane == 0 && nmine > 0) {
-      #pragma unroll 1
-      for (int i = 0; i < ATTD_NS && i < nmine; i++)
-        if (issued[i] < 0) key_block(i, i == 0 ? s_all : 0u);
-      if (!scales_early) {
-        dcp::bulk_load(af, ks + (int64_t)g * max_pos, s_all, &full[0]);
-      } else if (last_mine && s_all > s_old) {
-        dcp::mbar_expect_tx(&sbar, s_all - s_old);
-        dcp::bulk_load(af + (s_old >> 2), ks + (int64_t)g * max_pos + (s_old >> 2), s_all - s_old, &sbar);
-      }
-    }
     if (rt) {
       const double a = h[hq * hd + tid], b = h[hq * hd + half + tid];
       const double e = h[qDim + g * hd + tid], f = h[qDim + g * hd + half + tid];
@@ -1732,7 +1721,8 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
         const uint32_t mx = max(vm0, __float_as_uint(fabsf(v)));
         const float ns = __double2float_rn(quant_scale(__uint_as_float(mx)));
         mv = n0 == 0 || ns != vs0;
-        const int8_t qv = dc_clamp8(dc_js_round(dc_ddiv_slow((double)v, (double)ns)));
+        const double rns = __drcp_rn((double)ns);
+        const int8_t qv = dc_quant_div_f(v, (double)ns, rns, __double2float_rn(rns));
         ch_ns[lane] = ns;
         ch_q[lane] = qv;
         if (writer) {
@@ -1783,7 +1773,6 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   }
   __syncthreads();
   const int nmv = __popc(chg_mask);  // moved value channels of this CTA
-  const bool late_scales = nmine > 0 && scales_early && last_mine && s_all > s_old;
   if (writer && last_mine) {  // the group's copy of the new key
     if (tid < (hd >> 4)) ((int4*)(k8 + ((int64_t)g * max_pos + n0) * hd))[tid] = ((const int4*)knew)[tid];
     if (tid == 0) ks[(int64_t)g * max_pos + n0] = ksc;
@@ -1812,7 +1801,6 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     // every key block of this CTA has a ring slot of its own: one barrier for all
     bool ok = true;
     for (int i = 0; i < nmine; i++) ok &= dcp::mbar_wait(&full[i], 0u, status);
-    if (late_scales) ok &= dcp::mbar_wait(&sbar, 0, status);
     if (!ok) abort_flag = 1;
     if (last_mine) {  // the block holding position n0: its key and scale from step 1
       const int i = (nb - 1 - r) / S;
@@ -1830,7 +1818,6 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
     _Pragma("unroll 1") for (int i = 0; i < nmine; i++) {
       const int slot = i % ATTD_NS, b = r + i * S;
       if (!dcp::mbar_wait(&full[slot], (uint32_t)(i / ATTD_NS) & 1u, status)) abort_flag = 1;
-      if (late_scales && b == nb - 1 && !dcp::mbar_wait(&sbar, 0, status)) abort_flag = 1;
       if (b == nb - 1) {  // the block holding position n0: its key and scale from step 1
         if (tid < (hd >> 4))
           ((int4*)(sK + (size_t)slot * ATTD_KB * hd + (size_t)(n0 - b * ATTD_KB) * hd))[tid] = ((const int4*)knew)[tid];
@@ -2039,7 +2026,6 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
   if (abort_flag && tid == 0) {
     dcp::mbar_wait(&vbar, 0, status);
     if (mv_issued) dcp::mbar_wait(&mvbar, 0, status);
-    if (late_scales) dcp::mbar_wait(&sbar, 0, status);
     for (int sl = 0; sl < ATTD_NS; sl++)
       if (issued[sl] >= 0) dcp::mbar_wait(&full[sl], (uint32_t)(issued[sl] / ATTD_NS) & 1u, status);
   }
