@@ -193,7 +193,9 @@ __global__ void __launch_bounds__(128, 4) k_gemv_row(const int8_t* X, const int8
   };
   int t = 0;  // pairs this warp has taken
   const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * 4 + (threadIdx.x >> 5), nw = gridDim.x * 4;
+  // warps numbered across blocks first: the last, partial round of row pairs
+  // falls on one warp in each of many blocks (SMs), not on whole blocks
+  const int gw = (threadIdx.x >> 5) * gridDim.x + blockIdx.x, nw = gridDim.x * 4;
   const int nch = (k + 15) >> 4;
   const int4* X4 = (const int4*)X;
   const uint64_t pol = dcp::l2_evict_first();
@@ -587,7 +589,7 @@ static int launch_gemv_row(dc_ctx* ctx, const int8_t* Xq, const int8_t* Wt, int 
                            uint32_t* rowmax = nullptr) {
   if (int rc = dc_set_smem(ctx, (const void*)k_gemv_row, 0)) return rc;
   const int pairs = (n + 1) / 2;
-  const int blocks = std::max(1, std::min((pairs + 3) / 4, ctx->sm_count * 4));
+  const int blocks = std::max(1, std::min(pairs, ctx->sm_count * 4));  // four per SM when there are pairs enough
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks);
   cfg.blockDim = dim3(128);
