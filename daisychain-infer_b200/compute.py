@@ -151,9 +151,11 @@ class Compute:
         """out[r] = serial double sum of terms[r] in index order (infer.js:73-76, :100-104)."""
         self._check(self.L.dc_ordered_sum_dev(self.h, _ptr(terms), rows, n, _ptr(out)), "ordered_sum")
 
-    def exp_dev(self, x, n, y, sel: bool = False) -> None:
-        """y = Math.exp(x) by the fdlibm method (sel: the branch-free form the kernels use)."""
-        self._check(self.L.dc_exp_dev(self.h, _ptr(x), n, _ptr(y), 1 if sel else 0), "exp")
+    def exp_dev(self, x, n, y, sel=False) -> None:
+        """y = Math.exp(x) by the fdlibm method (sel True or 1: the branch-free form the kernels
+        use; 2: the table-driven exp of the chunk softmax; 3: f32(Math.exp(x)) as that softmax
+        settles it)."""
+        self._check(self.L.dc_exp_dev(self.h, _ptr(x), n, _ptr(y), int(sel)), "exp")
 
     def rmsnorm_dev(self, x, rows, cols, w, eps, y, exact_sum: bool = False) -> None:
         """infer.js rmsnorm (:70-80) of rows x cols f32 (exact_sum: always the serial-order sum)."""

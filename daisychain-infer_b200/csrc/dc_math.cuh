@@ -15,6 +15,8 @@
 #pragma once
 #include <stdint.h>
 
+#include "dc_exp2_table.cuh"
+
 namespace dcm {
 
 __device__ __forceinline__ double b2d(uint64_t u) { return __longlong_as_double((long long)u); }
@@ -121,6 +123,54 @@ __device__ __forceinline__ double fdlibm_exp_sel(double x) {
   res = x < u_threshold ? 0.0 : res;
   res = x > o_threshold ? __longlong_as_double(0x7ff0000000000000LL) : res;
   return hx >= 0x7ff00000u ? (isnan(x) ? __dadd_rn(x, x) : (neg ? 0.0 : x)) : res;
+}
+
+// ---- a faster exp whose error bound settles the softmax's f32 values -------
+// Tang's table-driven method (P. T. P. Tang, "Table-driven implementation of
+// the exponential function in IEEE floating-point arithmetic", ACM TOMS 15(2),
+// 1989), written here from the mathematics: x = (64 K + j) ln2/64 + r with
+// |r| <= ln2/128 (ln2/64 split hi + lo, k * hi exact), e^r - 1 by its Taylor
+// polynomial to degree 5 (truncation below 3.6e-17 relative), and
+// exp(x) = 2^K * 2^(j/64) * e^r with 2^(j/64) a double-double from
+// dc_exp2_table.cuh.  For -700 <= x <= 0.35 the result is normal and within
+// 0.9 ulp of e^x; fdlibm's is within 1 ulp, so the two differ by less than
+// 2^-51 relative.  It is not fdlibm's value bit for bit: exp_settle uses it
+// only where that bound decides the f32 rounding.
+// tab: the 64 pairs in shared memory (exp2_tab_load).
+__device__ __forceinline__ void exp2_tab_load(double2* tab) {
+  for (int i = threadIdx.x; i < 64; i += blockDim.x) tab[i] = make_double2(b2d(kExp2Tab[i][0]), b2d(kExp2Tab[i][1]));
+}
+__device__ __forceinline__ double exp_tang(double x, const double2* tab) {
+  const int k = __double2int_rn(__dmul_rn(x, b2d(kInvLn2Times64)));
+  const double kd = (double)k;
+  const double r = __dsub_rn(__dsub_rn(x, __dmul_rn(kd, b2d(kLn2Over64Hi))), __dmul_rn(kd, b2d(kLn2Over64Lo)));
+  double p = __dadd_rn(1.0 / 24.0, __dmul_rn(r, 1.0 / 120.0));
+  p = __dadd_rn(1.0 / 6.0, __dmul_rn(r, p));
+  p = __dadd_rn(0.5, __dmul_rn(r, p));
+  p = __dadd_rn(1.0, __dmul_rn(r, p));
+  p = __dmul_rn(r, p);  // e^r - 1
+  const double2 t = tab[k & 63];
+  const double y = __dadd_rn(t.x, __dadd_rn(__dmul_rn(t.x, p), t.y));  // 2^(j/64) e^r, in [0.99, 2.02)
+  return __longlong_as_double(__double_as_longlong(y) + ((long long)(k >> 6) << 52));
+}
+
+// f32(fdlibm_exp(x)) -- the rounding the softmax keeps -- and in *e a double
+// within 2^-49 relative of fdlibm_exp(x) (for the sums that are bracketed):
+// from exp_tang when both ends of that interval round to the same float,
+// otherwise (rarely, and for x < -700) from fdlibm_exp_sel itself.
+__device__ __forceinline__ float exp_settle(double x, const double2* tab, double* e) {
+  if (x >= -700.0 && x <= 0.0) {
+    const double t = exp_tang(x, tab);
+    const float lo = __double2float_rn(__dmul_rn(t, 1.0 - 0x1p-49));
+    const float hi = __double2float_rn(__dmul_rn(t, 1.0 + 0x1p-49));
+    if (lo == hi) {
+      *e = t;
+      return lo;
+    }
+  }
+  const double f = fdlibm_exp_sel(x);
+  *e = f;
+  return __double2float_rn(f);
 }
 
 // infer.js:59 + :212: f32(silu(g) * u) with silu(v) = v / (1 + exp(-v)) in

@@ -1000,8 +1000,10 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
   __shared__ float amxs[16];
   __shared__ int ambs[16];
   __shared__ dco::Smem16 osm;
+  __shared__ double2 etab[64];  // 2^(j/64) for the table-driven exp (published by the first barrier)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hq = blockIdx.x, g = hq / (nH / nKV);
+  dcm::exp2_tab_load(etab);
   int r0 = 0, r1 = T;
   const int8_t* vz = nullptr;  // chunk z < G-1 of a pass: its buffer, and its value scales
   const float* vsz = vs;
@@ -1094,10 +1096,12 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
     for (int w = 1; w < 16; w++) m = fmax(m, wm[w][row]);
     double part = 0.0;
     float wpart = 0.0f;  // sum of (n - j) e_j: only the radius needs it, to well within its 1e-3 slack
+    // f32(e_j) exactly as the fdlibm exp rounds, with e_j itself within 2^-51
+    // relative of fdlibm's for the sum (exp_settle)
 #pragma unroll 4
     for (int j = lane; j < n; j += 32) {
-      const double e = dcm::fdlibm_exp_sel(__dsub_rn(__dmul_rn((double)Sr[j], scale), m));
-      const float ef = __double2float_rn(e);
+      double e;
+      const float ef = dcm::exp_settle(__dsub_rn(__dmul_rn((double)Sr[j], scale), m), etab, &e);
       Sr[j] = ef;
       part += e;
       wpart = __fadd_rn(wpart, __fmul_rn((float)(n - j), ef));
@@ -1107,8 +1111,10 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
       part += __shfl_xor_sync(0xffffffffu, part, o);
       wpart += __shfl_xor_sync(0xffffffffu, wpart, o);
     }
-    // a term passes through at most ceil(n / 32) adds in its lane and 5 in the warp
-    const double hr = serial_sum_radius(part, (double)wpart, (n + 31) / 32 + 10);
+    // a term passes through at most ceil(n / 32) adds in its lane and 5 in the
+    // warp; the radius also covers the terms' distance from fdlibm's (2^-51
+    // relative each, taken as 2^-48 of the sum)
+    const double hr = __dadd_rn(serial_sum_radius(part, (double)wpart, (n + 31) / 32 + 10), __dmul_rn(0x1p-48, part));
     const double zlo = part - hr, zhi = part + hr;
     const double rlo = __drcp_rn(zlo), rhi = __drcp_rn(zhi);
     const bool narrow = __dsub_rn(zhi, zlo) < 5e-13 * zlo;
@@ -3473,14 +3479,25 @@ extern "C" int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, in
 }
 
 __global__ void k_exp(const double* __restrict__ x, int n, double* __restrict__ y, int sel) {
+  __shared__ double2 tab[64];
+  dcm::exp2_tab_load(tab);
+  __syncthreads();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = sel ? dcm::fdlibm_exp_sel(x[i]) : dcm::fdlibm_exp(x[i]);
+  if (i >= n) return;
+  double e = 0.0;
+  switch (sel) {
+    case 0: y[i] = dcm::fdlibm_exp(x[i]); break;
+    case 1: y[i] = dcm::fdlibm_exp_sel(x[i]); break;
+    case 2: y[i] = dcm::exp_tang(x[i], tab); break;
+    default: y[i] = (double)dcm::exp_settle(x[i], tab, &e); break;
+  }
 }
 
 extern "C" int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int sel) {
   if (!ctx || n < 0 || (n && (!x || !y))) return dc_fail(ctx, DC_E_INVAL, "exp: bad arguments");
   if (!n) return DC_OK;
-  k_exp<<<(n + 255) / 256, 256, 0, ctx->stream>>>(x, n, y, sel ? 1 : 0);
+  if (sel < 0 || sel > 3) return dc_fail(ctx, DC_E_INVAL, "exp: sel %d not in 0..3", sel);
+  k_exp<<<(n + 255) / 256, 256, 0, ctx->stream>>>(x, n, y, sel);
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());
   return DC_OK;

@@ -168,7 +168,10 @@ int dc_vgemm(dc_ctx* ctx, const float* X, int m, const dc_weight* w, unsigned fl
 int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double* out);
 /* dc_exp_dev: y[i] = Math.exp(x[i]) by the fdlibm method (infer.js:59, :192):
  *   sel = 0 its branching form, sel = 1 the branch-free form the softmax and
- *   SiLU kernels evaluate (the same bits for every argument). */
+ *   SiLU kernels evaluate (the same bits for every argument); sel = 2 the
+ *   table-driven exp the chunk softmax evaluates first (not fdlibm's bits:
+ *   within 2^-51 relative of them for -700 <= x <= 0), sel = 3 the f32
+ *   rounding of fdlibm's value as the chunk softmax settles it (as a double). */
 int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int sel);
 int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y,
                    int exact_sum);

@@ -149,6 +149,32 @@ def exp_inputs():
     return xs
 
 
+def test_exp_table_driven_within_bound_and_settles_f32(comp):
+    """The table-driven exp of the chunk softmax stays within 2^-51 relative of
+    the fdlibm value on -700 <= x <= 0, and the f32 value the softmax settles
+    from it is f32 of the fdlibm value for every argument (including those it
+    hands back to the fdlibm path: x < -700, x > 0, non-finite)."""
+    import torch
+    rng = np.random.default_rng(11)
+    xs = np.concatenate([exp_inputs(), -rng.exponential(2.0, 200000), rng.uniform(-700, 0, 100000),
+                         -np.abs(rng.standard_normal(50000)) * 1e-3, np.array([-700.0, -699.999, -0.0])])
+    x = torch.tensor(xs, dtype=torch.float64, device="cuda")
+    ys = {}
+    for sel in (1, 2, 3):
+        y = torch.empty_like(x)
+        comp.exp_dev(x, xs.size, y, sel=sel)
+        ys[sel] = y
+    comp.sync()
+    fd, tg, st = (ys[k].cpu().numpy() for k in (1, 2, 3))
+    dom = (xs >= -700.0) & (xs <= 0.0)
+    rel = np.abs(tg[dom] - fd[dom]) / fd[dom]
+    assert rel.max() <= 2.0 ** -51, (rel.max(), xs[dom][np.argmax(rel)])
+    with np.errstate(over="ignore"):  # (results above the float range round to infinity)
+        want = fd.astype(np.float32).astype(np.float64)
+    bad = np.nonzero((want.view(np.uint64) != st.view(np.uint64)) & ~(np.isnan(want) & np.isnan(st)))[0]
+    assert bad.size == 0, [(xs[i], want[i], st[i]) for i in bad[:5]]
+
+
 def test_exp_branch_free_equals_fdlibm_and_oracle(comp, O):
     """The kernels' branch-free exp gives the bits of the branching fdlibm
     method on the device for every argument, and both the oracle's exp."""
