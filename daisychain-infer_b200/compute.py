@@ -154,7 +154,7 @@ class Compute:
     def exp_dev(self, x, n, y, sel=False) -> None:
         """y = Math.exp(x) by the fdlibm method (sel True or 1: the branch-free form the kernels
         use; 2: the table-driven exp of the chunk softmax; 3: f32(Math.exp(x)) as that softmax
-        settles it)."""
+        settles it; 4, 5: the SwiGLU value of g = f32(x), u = f32(x/2 + 1/4), settled and exact)."""
         self._check(self.L.dc_exp_dev(self.h, _ptr(x), n, _ptr(y), int(sel)), "exp")
 
     def rmsnorm_dev(self, x, rows, cols, w, eps, y, exact_sum: bool = False) -> None:

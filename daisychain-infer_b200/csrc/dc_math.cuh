@@ -181,4 +181,25 @@ __device__ __forceinline__ float swiglu_f32(float gf, float uf) {
   return __double2float_rn(__dmul_rn(sl, (double)uf));
 }
 
+// swiglu_f32's value, settled from exp_tang: e = exp(-v) within 2^-51 of
+// fdlibm's, 1/(1 + e) from an f32 reciprocal refined by two Newton steps
+// (within 2^-51), so the double product lies within 2^-49.4 relative of the
+// exact chain's; unless both ends of a 2^-46 interval around it round to the
+// same float (and for v outside [-80, 700], where f32(1 + e) could overflow),
+// the exact chain decides.  tab: exp2_tab_load's table.
+__device__ __forceinline__ float swiglu_settle(float gf, float uf, const double2* tab) {
+  const double v = gf;
+  if (v >= -80.0 && v <= 700.0) {
+    const double d = __dadd_rn(1.0, exp_tang(-v, tab));
+    const double r0 = (double)__frcp_rn(__double2float_rn(d));
+    double r = __fma_rn(r0, __fma_rn(-d, r0, 1.0), r0);
+    r = __fma_rn(r, __fma_rn(-d, r, 1.0), r);
+    const double y = __dmul_rn(__dmul_rn(v, r), (double)uf);
+    const float lo = __double2float_rn(__dmul_rn(y, 1.0 - 0x1p-46));
+    const float hi = __double2float_rn(__dmul_rn(y, 1.0 + 0x1p-46));
+    if (lo == hi) return lo;
+  }
+  return swiglu_f32(gf, uf);
+}
+
 }  // namespace dcm

@@ -2079,7 +2079,10 @@ static int ew_blocks(const dc_ctx* ctx, int cols, int rows) {
 __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* hout, uint32_t* rowmax,
                                                int* status) {
   asm volatile("griddepcontrol.launch_dependents;");
+  __shared__ double2 etab[64];
+  dcm::exp2_tab_load(etab);  // (constant: before the wait)
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
+  __syncthreads();
   __shared__ float red[32];
   const int row = blockIdx.y;
   const float2* g = (const float2*)(h + (int64_t)row * 2 * I);
@@ -2096,7 +2099,7 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* ho
     for (int u = 0; u < 8; u++) {
       const int j = j0 + u * stride;
       if (j < I) {
-        const float y = swiglu_f32(gu[u].x, gu[u].y);
+        const float y = dcm::swiglu_settle(gu[u].x, gu[u].y, etab);
         bad |= !isfinite(y);
         hout[(int64_t)row * I + j] = y;
         mx = fmaxf(mx, fabsf(y));
@@ -3485,18 +3488,22 @@ __global__ void k_exp(const double* __restrict__ x, int n, double* __restrict__ 
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   double e = 0.0;
+  // (sel 4, 5: the SwiGLU value of g = f32(x), u = f32(x / 2 + 1/4), settled and exact)
+  const float g = (float)x[i], u = (float)__dadd_rn(__dmul_rn(x[i], 0.5), 0.25);
   switch (sel) {
     case 0: y[i] = dcm::fdlibm_exp(x[i]); break;
     case 1: y[i] = dcm::fdlibm_exp_sel(x[i]); break;
     case 2: y[i] = dcm::exp_tang(x[i], tab); break;
-    default: y[i] = (double)dcm::exp_settle(x[i], tab, &e); break;
+    case 3: y[i] = (double)dcm::exp_settle(x[i], tab, &e); break;
+    case 4: y[i] = (double)dcm::swiglu_settle(g, u, tab); break;
+    default: y[i] = (double)dcm::swiglu_f32(g, u); break;
   }
 }
 
 extern "C" int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int sel) {
   if (!ctx || n < 0 || (n && (!x || !y))) return dc_fail(ctx, DC_E_INVAL, "exp: bad arguments");
   if (!n) return DC_OK;
-  if (sel < 0 || sel > 3) return dc_fail(ctx, DC_E_INVAL, "exp: sel %d not in 0..3", sel);
+  if (sel < 0 || sel > 5) return dc_fail(ctx, DC_E_INVAL, "exp: sel %d not in 0..5", sel);
   k_exp<<<(n + 255) / 256, 256, 0, ctx->stream>>>(x, n, y, sel);
   dc_count_launch();
   DC_CUDA(ctx, cudaGetLastError());

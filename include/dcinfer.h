@@ -171,7 +171,10 @@ int dc_ordered_sum_dev(dc_ctx* ctx, const double* terms, int rows, int n, double
  *   SiLU kernels evaluate (the same bits for every argument); sel = 2 the
  *   table-driven exp the chunk softmax evaluates first (not fdlibm's bits:
  *   within 2^-51 relative of them for -700 <= x <= 0), sel = 3 the f32
- *   rounding of fdlibm's value as the chunk softmax settles it (as a double). */
+ *   rounding of fdlibm's value as the chunk softmax settles it (as a double);
+ *   sel = 4, 5 the SwiGLU value f32(silu(g) * u) (infer.js:59, :212) of
+ *   g = f32(x), u = f32(x / 2 + 1/4), as the SwiGLU kernel settles it and by
+ *   the exact chain. */
 int dc_exp_dev(dc_ctx* ctx, const double* x, int n, double* y, int sel);
 int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, const float* w, double eps, float* y,
                    int exact_sum);

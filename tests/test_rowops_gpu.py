@@ -175,6 +175,27 @@ def test_exp_table_driven_within_bound_and_settles_f32(comp):
     assert bad.size == 0, [(xs[i], want[i], st[i]) for i in bad[:5]]
 
 
+def test_swiglu_settled_equals_exact(comp):
+    """The SwiGLU value settled from the table-driven exp is the exact chain's
+    f32 (infer.js:59, :212) for every argument: g = f32(x), u = f32(x/2 + 1/4)
+    over the fast range, its edges (-80, 700), zeros, tiny, huge and
+    non-finite values."""
+    import torch
+    rng = np.random.default_rng(13)
+    edges = np.array([-80.0, -80.00001, -79.99999, 700.0, 700.001, 699.999, 0.0, -0.0, 1e-30, -1e-30, 1e-8,
+                      88.7, -88.7, 1e30, -1e30, 3e38, -3e38, np.inf, -np.inf, np.nan])
+    xs = np.concatenate([edges, rng.standard_normal(200000) * 3, rng.uniform(-90, 720, 100000),
+                         rng.standard_normal(50000) * 1e-3]).astype(np.float32).astype(np.float64)
+    x = torch.tensor(xs, dtype=torch.float64, device="cuda")
+    fast, exact = torch.empty_like(x), torch.empty_like(x)
+    comp.exp_dev(x, xs.size, fast, sel=4)
+    comp.exp_dev(x, xs.size, exact, sel=5)
+    comp.sync()
+    a, b = fast.cpu().numpy(), exact.cpu().numpy()
+    bad = np.nonzero((a.view(np.uint64) != b.view(np.uint64)) & ~(np.isnan(a) & np.isnan(b)))[0]
+    assert bad.size == 0, [(xs[i], a[i], b[i]) for i in bad[:5]]
+
+
 def test_exp_branch_free_equals_fdlibm_and_oracle(comp, O):
     """The kernels' branch-free exp gives the bits of the branching fdlibm
     method on the device for every argument, and both the oracle's exp."""
