@@ -2112,7 +2112,8 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* ho
 }
 
 // quantizeRows from a finished row maximum, element-parallel over grid
-// (ew_blocks, rows): s[row] = f32(max(mx/127, 1e-8)) in double, q = clamp(round(x/sc)).
+// (ew_blocks of a quarter of the row, rows): s[row] = f32(max(mx/127, 1e-8)) in
+// double, q = clamp(round(x/sc)); any grid covers the row (grid-stride).
 __global__ void __launch_bounds__(256) k_rowquant(const float* x, int64_t ldx, int cols,
                                                  const uint32_t* rowmax, int8_t* q,
                                                  int ldq, float* s) {
@@ -2122,9 +2123,28 @@ __global__ void __launch_bounds__(256) k_rowquant(const float* x, int64_t ldx, i
   const double sc = quant_scale(__uint_as_float(rowmax[row])), rsc = __drcp_rn(sc);
   const float rscf = __double2float_rn(rsc);
   if (blockIdx.x == 0 && threadIdx.x == 0) s[row] = __double2float_rn(sc);
+  const float* xr = x + row * ldx;
+  int8_t* qr = q + (int64_t)row * ldq;
+  if (((reinterpret_cast<uintptr_t>(xr) & 15) | (cols & 3) | (ldq & 3)) == 0) {
+    // four values per thread and step (16-byte loads, 4-byte stores), four steps in flight
+    const int n4 = ldq >> 2, c4 = cols >> 2;
+#pragma unroll 4
+    for (int j4 = blockIdx.x * blockDim.x + threadIdx.x; j4 < n4; j4 += gridDim.x * blockDim.x) {
+      char4 o = make_char4(0, 0, 0, 0);
+      if (j4 < c4) {
+        const float4 v = reinterpret_cast<const float4*>(xr)[j4];
+        o.x = dc_quant_div_f(v.x, sc, rsc, rscf);
+        o.y = dc_quant_div_f(v.y, sc, rsc, rscf);
+        o.z = dc_quant_div_f(v.z, sc, rsc, rscf);
+        o.w = dc_quant_div_f(v.w, sc, rsc, rscf);
+      }
+      reinterpret_cast<char4*>(qr)[j4] = o;
+    }
+    return;
+  }
 #pragma unroll 4
   for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < ldq; j += gridDim.x * blockDim.x)
-    q[(int64_t)row * ldq + j] = j < cols ? dc_quant_div_f(x[row * ldx + j], sc, rsc, rscf) : (int8_t)0;
+    qr[j] = j < cols ? dc_quant_div_f(xr[j], sc, rsc, rscf) : (int8_t)0;
 }
 
 
@@ -3053,7 +3073,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                               S->ctxo, S->qDim, S->rowmax, ctx->d_status, *cks, (const int8_t*)S->v8s,
                               (const float*)S->vsg));
       dc_count_launch();
-      DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, S->ldQ, T), T), dim3(256), 0, st, S->ctxo,
+      DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, (S->ldQ + 3) / 4, T), T), dim3(256), 0, st, S->ctxo,
                               (int64_t)S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ, S->rs));
       dc_count_launch();
     } else if (split_ctx && (T <= 16 || multi)) {
@@ -3067,7 +3087,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                               S->rowmax, ctx->d_status, multi ? *cks : one, (const int8_t*)S->v8s,
                               (const float*)S->vsg));
       dc_count_launch();
-      DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, S->ldQ, T), T), dim3(256), 0, st, S->ctxo,
+      DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, (S->ldQ + 3) / 4, T), T), dim3(256), 0, st, S->ctxo,
                               (int64_t)S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ, S->rs));
       dc_count_launch();
     } else {
@@ -3075,7 +3095,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                                                                 kv.v8t, kv.vs, T, n0p, S->max_pos, S->ldp, scale,
                                                                 S->ctxo, S->rowmax, S->qDim, ctx->d_status);
       dc_count_launch();
-      k_rowquant<<<dim3(ew_blocks(ctx, S->ldQ, T), T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
+      k_rowquant<<<dim3(ew_blocks(ctx, (S->ldQ + 3) / 4, T), T), 256, 0, st>>>(S->ctxo, S->qDim, S->qDim, S->rowmax, S->xq, S->ldQ,
                                                                 S->rs);
       dc_count_launch();
     }
@@ -3109,7 +3129,7 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
                               S->rowmax, ctx->d_status));
       dc_count_launch();
     }
-    DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, S->ldI, T), T), dim3(256), 0, st, S->hmid, (int64_t)S->I,
+    DC_CUDA(ctx, launch_dep(k_rowquant, dim3(ew_blocks(ctx, (S->ldI + 3) / 4, T), T), dim3(256), 0, st, S->hmid, (int64_t)S->I,
                             S->I, S->rowmax, S->xq, S->ldI, S->rs));
     dc_count_launch();
     if ((rc = gemm(S, ly.down, T, S->xq, S->ldI, x, DC_F_ADDTO))) return rc;  // out = x2 + down
