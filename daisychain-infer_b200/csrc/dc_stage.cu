@@ -186,9 +186,6 @@ template <> struct OsumCold<16> {
 
 // Dynamic shared memory of k_rmsnorm_quant: squares (double) and the row
 // (float), plus the weight row (float) when that still fits.
-static size_t rms_smem(int C) {
-  return 16 * (size_t)C + 20 * 1024 <= 232448 ? 16 * (size_t)C : 12 * (size_t)C;
-}
 
 // 1 / sqrt(s / C + eps) with every step correctly rounded (infer.js:77-78);
 // monotone non-increasing in s.
@@ -372,23 +369,49 @@ __device__ __forceinline__ void rmsnorm_quant_block(const float* xr, int C, cons
 // threads per row (NORM_WIDE for rows that run alone or in a single wave: a
 // one-row norm is a chain of dependent phases, and wider blocks shorten each).
 // x rows x C f32 -> q rows x ldq int8 (+ s[row]); the f32 norm output is not kept.
+// Dynamic shared memory: C doubles (v*v) and C floats (x, then y); then,
+// when the launch leaves room for it, C floats (the weight row); then the
+// exact ordered sum's scratch, unless it fits over the y row (which that rare
+// path rewrites afterwards).  Without the weight row a 256-thread block takes
+// about 12 bytes per column, so four blocks share an SM at C = 4096.
 constexpr int NORM_WIDE = 512;
 template <int NT>
-__global__ void __launch_bounds__(NT) k_rmsnorm_quant(const float* x, int C,
+__host__ __device__ constexpr bool rms_osm_alias(int C) {
+  return 4 * (size_t)C >= sizeof(dco::SmemT<NT / 32>);
+}
+__host__ __device__ constexpr size_t rms_osm_at(int C, bool with_w) {  // byte offset of the scratch
+  return ((with_w ? 16 : 12) * (size_t)C + 15) & ~(size_t)15;
+}
+template <int NT>
+static size_t rms_smem_t(int C, bool with_w) {
+  return rms_osm_at(C, with_w) + (rms_osm_alias<NT>(C) ? 0 : sizeof(dco::SmemT<NT / 32>));
+}
+// with_w: keep the weight row on chip when that still leaves 20 KB of the SM
+static size_t rms_smem(int C, int nt, bool with_w = true) {
+  const bool w = with_w && (nt == NORM_WIDE ? rms_smem_t<NORM_WIDE>(C, true) : rms_smem_t<NORM_THREADS>(C, true)) +
+                                   20 * 1024 <= 232448;
+  return nt == NORM_WIDE ? rms_smem_t<NORM_WIDE>(C, w) : rms_smem_t<NORM_THREADS>(C, w);
+}
+template <int NT>
+__global__ void __launch_bounds__(NT, NT == NORM_THREADS ? 4 : 1) k_rmsnorm_quant(const float* x, int C,
                                                                const float* w, double eps,
                                                                int8_t* q, int ldq,
                                                                float* s, int* status,
                                                                float* yo = nullptr,
                                                                uint32_t* zrow = nullptr,
                                                                int exact_sum = 0) {
-  extern __shared__ __align__(16) double sq[];  // C doubles (v*v), C floats (x, then y), C floats (w)
+  extern __shared__ __align__(16) double sq[];
   float* ys = (float*)(sq + C);
-  // the weight row rides along in shared memory when it fits (16 bytes per column)
-  float* wsm = 16 * (size_t)C + 20 * 1024 <= 232448 ? ys + C : nullptr;
+  uint32_t dsm;
+  asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsm));
+  using Osm = dco::SmemT<NT / 32>;
+  const bool alias = rms_osm_alias<NT>(C);
+  const bool with_w = dsm >= rms_osm_at(C, true) + (alias ? 0 : sizeof(Osm));
+  float* wsm = with_w ? ys + C : nullptr;
+  Osm& osm = alias ? *reinterpret_cast<Osm*>(ys) : *reinterpret_cast<Osm*>((uint8_t*)sq + rms_osm_at(C, with_w));
   __shared__ float red[32];
   __shared__ double2 redd2[32];
   __shared__ int vote[32];
-  __shared__ dco::SmemT<NT / 32> osm;
   // the GEMV that consumes q may launch now: it streams its weights meanwhile
   asm volatile("griddepcontrol.launch_dependents;");
   const int row = blockIdx.x;
@@ -2967,12 +2990,13 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     if (int rc0 = dc_set_smem(ctx, (const void*)ar_kernel, (int)ar_smem)) return rc0;
   if (split_ctx)
     if (int rc0 = dc_set_smem(ctx, (const void*)k_attn_ctx, (int)ctx_smem)) return rc0;
-  const size_t nrm_smem = rms_smem(S->C);
-  // always raised: the kernel's static shared memory counts against the 48 KB default too
-  // rows that fit in one wave get the wide norm block
+  // rows that fit in one wave get the wide norm block; more than three waves'
+  // worth of rows leave the weight row in L2 (four blocks per SM)
   const bool nwide = T <= ctx->sm_count;
   auto norm_k = nwide ? k_rmsnorm_quant<NORM_WIDE> : k_rmsnorm_quant<NORM_THREADS>;
   const int norm_nt = nwide ? NORM_WIDE : NORM_THREADS;
+  // always raised: the kernel's static shared memory counts against the 48 KB default too
+  const size_t nrm_smem = rms_smem(S->C, norm_nt, T <= 3 * ctx->sm_count);
   if (int rc0 = dc_set_smem(ctx, (const void*)norm_k, (int)nrm_smem)) return rc0;
   // a decode row: GEMVs with the norms, the SwiGLU and the row quantisation fused
   const bool fuse = T == 1 && use_kv && dec_ch && S->row_fused && fg_fits(S);
@@ -3341,7 +3365,7 @@ static int decode_lap(dc_stage** st, int ns, int32_t* picks) {
     if (int rc0 = dc_set_smem(ctx, (const void*)k_gemv_fused<FG_NORM>, (int)fg_smem(FG_NORM, H->C))) return rc0;
     DC_CUDA(ctx, launch_fused(H, FG_NORM, H->xlap, H->C, H->nrmF, nullptr, H->lm, 0, H->logits1, nullptr, nullptr));
   } else {
-    const size_t nrm_smem = rms_smem(H->C);
+    const size_t nrm_smem = rms_smem(H->C, NORM_WIDE);
     // always raised: the kernel's static shared memory counts against the 48 KB default too
     if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant<NORM_WIDE>, (int)nrm_smem)) return rc0;
     k_rmsnorm_quant<NORM_WIDE><<<1, NORM_WIDE, nrm_smem, s>>>(H->xlap, H->C, H->nrmF, H->spec.norm_eps, H->xq, H->ldC, H->rs,
@@ -3455,7 +3479,7 @@ extern "C" int dc_stage_logits(dc_stage* S, const float* x, int T, const int32_t
   for (int r = 0; r < nrows; r++)
     DC_CUDA(ctx, cudaMemcpyAsync(S->lx + (size_t)r * S->C, x + (size_t)rows[r] * S->C, 4 * (size_t)S->C,
                                  cudaMemcpyDeviceToDevice, st));
-  const size_t nrm_smem = rms_smem(S->C);
+  const size_t nrm_smem = rms_smem(S->C, NORM_WIDE);
   // always raised: the kernel's static shared memory counts against the 48 KB default too
   if (int rc0 = dc_set_smem(ctx, (const void*)k_rmsnorm_quant<NORM_WIDE>, (int)nrm_smem)) return rc0;
   k_rmsnorm_quant<NORM_WIDE><<<nrows, NORM_WIDE, nrm_smem, st>>>(S->lx, S->C, S->nrmF, S->spec.norm_eps, S->xq, S->ldC, S->rs,
@@ -3535,8 +3559,8 @@ extern "C" int dc_rmsnorm_dev(dc_ctx* ctx, const float* x, int rows, int cols, c
   if (!ctx || rows < 0 || cols < 1 || (rows && (!x || !w || !y))) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: bad arguments");
   if ((size_t)cols * 12 > 200 * 1024) return dc_fail(ctx, DC_E_INVAL, "rmsnorm: row of %d does not fit on chip", cols);
   if (!rows) return DC_OK;
-  const int smem = (int)rms_smem(cols);
   const bool wide = rows <= ctx->sm_count;
+  const int smem = (int)rms_smem(cols, wide ? NORM_WIDE : NORM_THREADS);
   auto norm_k = wide ? k_rmsnorm_quant<NORM_WIDE> : k_rmsnorm_quant<NORM_THREADS>;
   if (int rc = dc_set_smem(ctx, (const void*)norm_k, smem)) return rc;
   norm_k<<<rows, wide ? NORM_WIDE : NORM_THREADS, smem, ctx->stream>>>(x, cols, w, eps, nullptr, 0, nullptr, ctx->d_status, y,
