@@ -1119,14 +1119,21 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
     for (int w = 1; w < 16; w++) m = fmax(m, wm[w][row]);
     double part = 0.0;
     float wpart = 0.0f;  // sum of (n - j) e_j: only the radius needs it, to well within its 1e-3 slack
-    // f32(e_j) exactly as the fdlibm exp rounds, with e_j itself within 2^-51
-    // relative of fdlibm's for the sum (exp_settle)
+    // f32(e_j) as the fdlibm exp rounds it, and e_j within 2^-51 relative of
+    // fdlibm's for the sum, from the table-driven exp with no branch in the
+    // loop (exp_settle's test, inline).  Below x = -700 both are zero to far
+    // within the bracket's radius.  A key whose f32 rounding the bound cannot
+    // settle (about one in 2^24) sends its row to the exact path below, which
+    // recomputes the whole row with fdlibm.
+    bool unsettled = false;
 #pragma unroll 4
     for (int j = lane; j < n; j += 32) {
-      double e;
-      const float ef = dcm::exp_settle(__dsub_rn(__dmul_rn((double)Sr[j], scale), m), etab, &e);
+      const double x = __dsub_rn(__dmul_rn((double)Sr[j], scale), m);
+      const double t = x >= -700.0 ? dcm::exp_tang(x, etab) : 0.0;
+      const float ef = __double2float_rn(__dmul_rn(t, 1.0 - 0x1p-49));
+      unsettled |= ef != __double2float_rn(__dmul_rn(t, 1.0 + 0x1p-49));
       Sr[j] = ef;
-      part += e;
+      part += t;
       wpart = __fadd_rn(wpart, __fmul_rn((float)(n - j), ef));
     }
 #pragma unroll
@@ -1151,7 +1158,7 @@ __global__ void __launch_bounds__(AR_THREADS, 1) k_attn_chunk(const float* h, in
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) amx = fmaxf(amx, __shfl_xor_sync(0xffffffffu, amx, o));
-    const bool wamb = __any_sync(0xffffffffu, amb);
+    const bool wamb = __any_sync(0xffffffffu, amb || unsettled);
     if (lane == 0) {
       amxs[row] = amx;
       ambs[row] = wamb ? 1 : 0;
