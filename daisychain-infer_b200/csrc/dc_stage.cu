@@ -523,17 +523,20 @@ __device__ __forceinline__ double softmax_z(const double* e, const float* af, in
 // RoPE on the q and k parts of the fused QKV output row, quantisation of each
 // rotated key (per kv head, quantizeCols rule), append of keys and values to
 // the cache at row n0 + t, and the running per-channel |v| maximum.
-// grid (T, nH + nKV + 1), block 64: block y < nH rotates query head y in place;
+// grid (ceil(T / R), nH + nKV + kvDim / 64), block 64, R rows per block:
+// block y < nH rotates query head y in place;
 // nH <= y < nH + nKV rotates key head y - nH, quantises it and appends it;
 // the last block appends the value row and folds |v| into the channel maxima
 // (vmax null: only appends).
+template <int R>
 __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, int nKV, int hd,
                                                     const float* rc, const float* rsn,
                                                     const int* n0p, int max_pos,
                                                     int8_t* k8, float* ks,
                                                     float* vcache, uint32_t* vmax,
                                                     float* vs, int* vchg,
-                                                    int8_t* v8t, int ldp, int* status, float* vt, int ldvt) {
+                                                    int8_t* v8t, int ldp, int* status, float* vt, int ldvt,
+                                                    int T) {
   // The decode attention after this kernel reads the cache's older keys and
   // int8 values before its own grid-dependency wait.  Its launch is released
   // only once this kernel has passed its wait, so every earlier kernel -- the
@@ -541,81 +544,113 @@ __global__ void __launch_bounds__(64) k_rope_append(float* h, int nqkv, int nH, 
   // among them -- has completed by then (each kernel of the chain waits for its
   // predecessor before it completes).
   // The position counter is set before the step's first kernel and the RoPE
-  // tables are constant: this thread's first table entries are read before
-  // the wait, so their round trip overlaps the kernel in front.
+  // tables are constant: this thread's first table entries (one per row of
+  // the block) are read before the wait, so their round trips overlap the
+  // kernel in front.  A block takes rows t0 .. t0 + R - 1 (below T).
   const int n0 = *n0p;  // cached tokens before this chunk = its first position
-  const int t = blockIdx.x, hh = blockIdx.y;
-  const int p = n0 + t;
+  const int t0 = blockIdx.x * R, hh = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int half = hd >> 1, qDim = nH * hd, kvDim = nKV * hd;
-  const bool rot = hh < nH + nKV && (int)threadIdx.x < half;
-  const double c_first = rot ? (double)rc[(int64_t)p * half + threadIdx.x] : 0.0;
-  const double s_first = rot ? (double)rsn[(int64_t)p * half + threadIdx.x] : 0.0;
+  const bool rot = hh < nH + nKV && tid < half;
+  double c_first[R], s_first[R];
+#pragma unroll
+  for (int rr = 0; rr < R; rr++) {
+    const bool ok = rot && t0 + rr < T;
+    const int64_t p = n0 + t0 + rr;
+    c_first[rr] = ok ? (double)rc[p * half + tid] : 0.0;
+    s_first[rr] = ok ? (double)rsn[p * half + tid] : 0.0;
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");  // launched as a programmatic dependent
   asm volatile("griddepcontrol.launch_dependents;");
-  __shared__ float kr[128];
-  __shared__ float red[32];
-  float* row = h + (int64_t)t * nqkv;
+  __shared__ float kr[R][128];
+  __shared__ float red[R][2];
   bool bad = false;
   if (hh >= nH + nKV) {
     // values, 64 channels per block: copy and fold into the running channel
     // maximum; with one row (vs != null) also the channel scales, their change
     // flags and the row's int8 values, which otherwise k_vscale and k_vquant*
     // compute once every row is in
-    const int c = (hh - nH - nKV) * 64 + threadIdx.x;
+    const int c = (hh - nH - nKV) * 64 + tid;
     if (c < kvDim) {
-      const float v = row[qDim + kvDim + c];
-      bad |= !isfinite(v);
-      vcache[(int64_t)(n0 + t) * kvDim + c] = v;
-      vt[(int64_t)c * ldvt + n0 + t] = v;
-      if (vs) {
-        const uint32_t m = max(vmax[c], __float_as_uint(fabsf(v)));
-        vmax[c] = m;
-        const float ns = __double2float_rn(quant_scale(__uint_as_float(m)));
-        vchg[c] = n0 == 0 || ns != vs[c];
-        vs[c] = ns;
-        // the new row's int8 value (channel-major); older rows move only when
-        // the channel's scale did (k_vquant_dev)
-        v8t[(int64_t)c * ldp + n0] = dc_clamp8(dc_js_round(dc_ddiv_slow((double)v, (double)ns)));
-      } else if (vmax) {  // (a pass of several chunks: k_vscale_chunks folds them per chunk)
-        atomicMax(vmax + c, __float_as_uint(fabsf(v)));
+#pragma unroll
+      for (int rr = 0; rr < R; rr++) {
+        const int t = t0 + rr;
+        if (t >= T) break;
+        const float v = h[(int64_t)t * nqkv + qDim + kvDim + c];
+        bad |= !isfinite(v);
+        vcache[(int64_t)(n0 + t) * kvDim + c] = v;
+        vt[(int64_t)c * ldvt + n0 + t] = v;
+        if (vs) {  // (one row)
+          const uint32_t m = max(vmax[c], __float_as_uint(fabsf(v)));
+          vmax[c] = m;
+          const float ns = __double2float_rn(quant_scale(__uint_as_float(m)));
+          vchg[c] = n0 == 0 || ns != vs[c];
+          vs[c] = ns;
+          // the new row's int8 value (channel-major); older rows move only when
+          // the channel's scale did (k_vquant_dev)
+          v8t[(int64_t)c * ldp + n0] = dc_clamp8(dc_js_round(dc_ddiv_slow((double)v, (double)ns)));
+        } else if (vmax) {  // (a pass of several chunks: k_vscale_chunks folds them per chunk)
+          atomicMax(vmax + c, __float_as_uint(fabsf(v)));
+        }
       }
     }
     if (bad) atomicOr(status, DC_ST_NONFINITE);
     return;
   }
   const bool isq = hh < nH;
-  float* o = isq ? row + hh * hd : row + qDim + (hh - nH) * hd;
-  for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const bool first = i == (int)threadIdx.x;
-    const double c = first ? c_first : (double)rc[(int64_t)p * half + i];
-    const double s = first ? s_first : (double)rsn[(int64_t)p * half + i];
-    const double a = o[i], b = o[half + i];
-    const float na = __double2float_rn(__dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s)));
-    const float nb = __double2float_rn(__dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s)));
-    if (isq) {
-      o[i] = na;
-      o[half + i] = nb;
-    } else {
-      kr[i] = na;
-      kr[half + i] = nb;
+#pragma unroll
+  for (int rr = 0; rr < R; rr++) {
+    const int t = t0 + rr;
+    if (t >= T) break;
+    const int64_t p = n0 + t;
+    float* row = h + (int64_t)t * nqkv;
+    float* o = isq ? row + hh * hd : row + qDim + (hh - nH) * hd;
+    for (int i = tid; i < half; i += 64) {
+      const bool first = i == tid;
+      const double c = first ? c_first[rr] : (double)rc[p * half + i];
+      const double s = first ? s_first[rr] : (double)rsn[p * half + i];
+      const double a = o[i], b = o[half + i];
+      const float na = __double2float_rn(__dsub_rn(__dmul_rn(a, c), __dmul_rn(b, s)));
+      const float nb = __double2float_rn(__dadd_rn(__dmul_rn(b, c), __dmul_rn(a, s)));
+      if (isq) {
+        o[i] = na;
+        o[half + i] = nb;
+      } else {
+        kr[rr][i] = na;
+        kr[rr][half + i] = nb;
+      }
     }
   }
   if (isq) return;
   __syncthreads();
-  // the rotated key: absmax over hd, f32 scale (quantizeCols rule), int8 row
-  float mx = 0.0f;
-  for (int c = threadIdx.x; c < hd; c += blockDim.x) {
-    const float v = kr[c];
-    bad |= !isfinite(v);
-    mx = fmaxf(mx, fabsf(v));
+  // each rotated key: absmax over hd (all the block's rows in one exchange), f32
+  // scale (quantizeCols rule), int8 row
+  float mx[R];
+#pragma unroll
+  for (int rr = 0; rr < R; rr++) {
+    mx[rr] = 0.0f;
+    if (t0 + rr < T)
+      for (int c = tid; c < hd; c += 64) {
+        const float v = kr[rr][c];
+        bad |= !isfinite(v);
+        mx[rr] = fmaxf(mx[rr], fabsf(v));
+      }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], o));
+    if (lane == 0) red[rr][warp] = mx[rr];
   }
-  mx = block_max_f(mx, red);
-  const float sc = __double2float_rn(quant_scale(mx));
+  __syncthreads();
   const int g = hh - nH;
-  const int64_t slot = (int64_t)g * max_pos + n0 + t;
-  if (threadIdx.x == 0) ks[slot] = sc;
-  const double rsc = __drcp_rn((double)sc);
-  for (int c = threadIdx.x; c < hd; c += blockDim.x) k8[slot * hd + c] = dc_quant_div((double)kr[c], (double)sc, rsc);
+#pragma unroll
+  for (int rr = 0; rr < R; rr++) {
+    const int t = t0 + rr;
+    if (t >= T) break;
+    const float sc = __double2float_rn(quant_scale(fmaxf(red[rr][0], red[rr][1])));
+    const int64_t slot = (int64_t)g * max_pos + n0 + t;
+    if (tid == 0) ks[slot] = sc;
+    const double rsc = __drcp_rn((double)sc);
+    for (int c = tid; c < hd; c += 64) k8[slot * hd + c] = dc_quant_div((double)kr[rr][c], (double)sc, rsc);
+  }
   if (bad) atomicOr(status, DC_ST_NONFINITE);
 }
 
@@ -2560,7 +2595,8 @@ static int upload(dc_stage* S, const float* h, size_t n, float** d) {
 
 // The shared-memory carve-out of every kernel a layer launches (dc_set_smem).
 static int stage_kernel_attrs(dc_ctx* ctx) {
-  const void* fns[] = {(const void*)k_rope_append, (const void*)k_vscale,      (const void*)k_vquant,
+  const void* fns[] = {(const void*)k_rope_append<1>, (const void*)k_rope_append<4>, (const void*)k_vscale,
+                       (const void*)k_vquant,
                        (const void*)k_vquant_dev,  (const void*)k_setpos,      (const void*)k_addpos,
                        (const void*)k_swiglu,      (const void*)k_rowquant,    (const void*)k_embed,
                        (const void*)k_embed_at,    (const void*)k_argmax_part, (const void*)k_argmax_fin};
@@ -3038,11 +3074,19 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
     if (!dcl) {
+      // four rows per block once there are several (one row: the scale path of a decode row)
       const int vblocks = (S->kvDim + 63) / 64;
-      DC_CUDA(ctx, launch_dep(k_rope_append, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf, S->nqkv,
-                              S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8, kv.ks, kv.v,
-                              multi ? nullptr : kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t, S->ldp,
-                              ctx->d_status, kv.vt, S->ldvt));
+      if (T >= 4) {
+        DC_CUDA(ctx, launch_dep(k_rope_append<4>, dim3((T + 3) / 4, S->nH + S->nKV + vblocks), dim3(64), 0, st,
+                                S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos,
+                                kv.k8, kv.ks, kv.v, multi ? nullptr : kv.vmax, (float*)nullptr, kv.vchg, kv.v8t,
+                                S->ldp, ctx->d_status, kv.vt, S->ldvt, T));
+      } else {
+        DC_CUDA(ctx, launch_dep(k_rope_append<1>, dim3(T, S->nH + S->nKV + vblocks), dim3(64), 0, st, S->hbuf,
+                                S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos, kv.k8,
+                                kv.ks, kv.v, multi ? nullptr : kv.vmax, T == 1 ? kv.vs : nullptr, kv.vchg, kv.v8t,
+                                S->ldp, ctx->d_status, kv.vt, S->ldvt, T));
+      }
       dc_count_launch();
     }
     if (multi) {
