@@ -187,19 +187,27 @@ __device__ __forceinline__ float swiglu_f32(float gf, float uf) {
 // exact chain's; unless both ends of a 2^-46 interval around it round to the
 // same float (and for v outside [-80, 700], where f32(1 + e) could overflow),
 // the exact chain decides.  tab: exp2_tab_load's table.
-__device__ __forceinline__ float swiglu_settle(float gf, float uf, const double2* tab) {
+// swiglu_fast: the same value with no branch, *ok false where only the exact
+// chain may decide (the caller then calls swiglu_f32).
+__device__ __forceinline__ float swiglu_fast(float gf, float uf, const double2* tab, bool* ok) {
   const double v = gf;
-  if (v >= -80.0 && v <= 700.0) {
-    const double d = __dadd_rn(1.0, exp_tang(-v, tab));
-    const double r0 = (double)__frcp_rn(__double2float_rn(d));
-    double r = __fma_rn(r0, __fma_rn(-d, r0, 1.0), r0);
-    r = __fma_rn(r, __fma_rn(-d, r, 1.0), r);
-    const double y = __dmul_rn(__dmul_rn(v, r), (double)uf);
-    const float lo = __double2float_rn(__dmul_rn(y, 1.0 - 0x1p-46));
-    const float hi = __double2float_rn(__dmul_rn(y, 1.0 + 0x1p-46));
-    if (lo == hi) return lo;
-  }
-  return swiglu_f32(gf, uf);
+  const bool inr = v >= -80.0 && v <= 700.0;
+  const double d = __dadd_rn(1.0, exp_tang(inr ? -v : 0.0, tab));
+  const double r0 = (double)__frcp_rn(__double2float_rn(d));
+  double r = __fma_rn(r0, __fma_rn(-d, r0, 1.0), r0);
+  r = __fma_rn(r, __fma_rn(-d, r, 1.0), r);
+  const double y = __dmul_rn(__dmul_rn(v, r), (double)uf);
+  const float lo = __double2float_rn(__dmul_rn(y, 1.0 - 0x1p-46));
+  const float hi = __double2float_rn(__dmul_rn(y, 1.0 + 0x1p-46));
+  *ok = inr && lo == hi;
+  return lo;
+}
+// the exact chain out of line, for the rare calls of a branch-free loop
+static __device__ __noinline__ float swiglu_f32_cold(float gf, float uf) { return swiglu_f32(gf, uf); }
+__device__ __forceinline__ float swiglu_settle(float gf, float uf, const double2* tab) {
+  bool ok;
+  const float y = swiglu_fast(gf, uf, tab, &ok);
+  return ok ? y : swiglu_f32(gf, uf);
 }
 
 }  // namespace dcm

@@ -2160,14 +2160,27 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* ho
     float2 gu[8];
 #pragma unroll
     for (int u = 0; u < 8; u++) gu[u] = j0 + u * stride < I ? g[j0 + u * stride] : make_float2(0.0f, 0.0f);
+    // the eight values with no branch, then (rarely) the exact chain for those
+    // the error bound cannot settle
+    float y[8];
+    bool ok[8], all = true;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      y[u] = dcm::swiglu_fast(gu[u].x, gu[u].y, etab, &ok[u]);
+      all &= ok[u] || j0 + u * stride >= I;
+    }
+    if (!__all_sync(__activemask(), all)) {
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (!ok[u] && j0 + u * stride < I) y[u] = dcm::swiglu_f32_cold(gu[u].x, gu[u].y);
+    }
 #pragma unroll
     for (int u = 0; u < 8; u++) {
       const int j = j0 + u * stride;
       if (j < I) {
-        const float y = dcm::swiglu_settle(gu[u].x, gu[u].y, etab);
-        bad |= !isfinite(y);
-        hout[(int64_t)row * I + j] = y;
-        mx = fmaxf(mx, fabsf(y));
+        bad |= !isfinite(y[u]);
+        hout[(int64_t)row * I + j] = y[u];
+        mx = fmaxf(mx, fabsf(y[u]));
       }
     }
   }
