@@ -202,8 +202,6 @@ __device__ __forceinline__ float swiglu_fast(float gf, float uf, const double2* 
   *ok = inr && lo == hi;
   return lo;
 }
-// the exact chain out of line, for the rare calls of a branch-free loop
-static __device__ __noinline__ float swiglu_f32_cold(float gf, float uf) { return swiglu_f32(gf, uf); }
 __device__ __forceinline__ float swiglu_settle(float gf, float uf, const double2* tab) {
   bool ok;
   const float y = swiglu_fast(gf, uf, tab, &ok);

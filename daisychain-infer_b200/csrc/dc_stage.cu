@@ -2129,6 +2129,9 @@ __global__ void __launch_bounds__(256) k_attention_dcl(const float* h, int nqkv,
 
 using dcm::swiglu_f32;
 
+// the exact SwiGLU chain out of line, for the rare calls of a branch-free loop
+static __device__ __noinline__ float swiglu_f32_cold(float gf, float uf) { return swiglu_f32(gf, uf); }
+
 // Blocks per row of an element-parallel row kernel (256 threads, grid-stride
 // over the row): enough for about four blocks per SM over all rows.
 static int ew_blocks(const dc_ctx* ctx, int cols, int rows) {
@@ -2172,7 +2175,7 @@ __global__ void __launch_bounds__(256) k_swiglu(const float* h, int I, float* ho
     if (!__all_sync(__activemask(), all)) {
 #pragma unroll
       for (int u = 0; u < 8; u++)
-        if (!ok[u] && j0 + u * stride < I) y[u] = dcm::swiglu_f32_cold(gu[u].x, gu[u].y);
+        if (!ok[u] && j0 + u * stride < I) y[u] = swiglu_f32_cold(gu[u].x, gu[u].y);
     }
 #pragma unroll
     for (int u = 0; u < 8; u++) {
