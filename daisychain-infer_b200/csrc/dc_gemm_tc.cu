@@ -1081,6 +1081,11 @@ int dc_gemm_tc_with(dc_ctx* ctx, const int8_t* Xq, int ldx, const int8_t* Wt, in
     return launch_tc<128>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
                           partial_cap, counter_cap, clear);
   // enough pair tiles to give every SM pair one: the persistent kernel
+  // up to 512 rows with too few 256 x 256 tile pairs to fill half the SMs: 1-SM
+  // tiles of 128 rows (four times the CTAs, split-K over the rest)
+  if (m <= 512 && (size_t)((n + 255) / 256) * ((m + 255) / 256) * batch < (size_t)ctx->sm_count / 2)
+    return launch_tc<128>(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st, partial, counters,
+                          partial_cap, counter_cap, clear);
   if (ctx->tc2_enabled && ctx->tp2_enabled &&
       (size_t)((n + 255) / 256) * ((m + 255) / 256) * batch >= (size_t)ctx->sm_count / 2)
     return launch_tp2(ctx, Xq, ldx, Wt, ldw, rs, cs, m, k, n, batch, flags, out, st);
