@@ -3090,9 +3090,10 @@ static int forward_layers(dc_stage* S, float* x, int T, int n0, int use_kv, cons
     }
     if (!use_kv) DC_CUDA(ctx, cudaMemsetAsync(kv.vmax, 0, 4 * (size_t)S->kvDim, st));
     if (!dcl) {
-      // four rows per block once there are several (one row: the scale path of a decode row)
+      // four rows per block for long chunk passes (short ones keep a block per
+      // row, so that they still fill the SMs; one row: the scale path of a decode row)
       const int vblocks = (S->kvDim + 63) / 64;
-      if (T >= 4) {
+      if (T >= 128) {
         DC_CUDA(ctx, launch_dep(k_rope_append<4>, dim3((T + 3) / 4, S->nH + S->nKV + vblocks), dim3(64), 0, st,
                                 S->hbuf, S->nqkv, S->nH, S->nKV, S->hd, S->rope_cos, S->rope_sin, n0p, S->max_pos,
                                 kv.k8, kv.ks, kv.v, multi ? nullptr : kv.vmax, (float*)nullptr, kv.vchg, kv.v8t,
